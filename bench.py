@@ -1,0 +1,452 @@
+"""Benchmark: dynamic block-shape block-sparse attention, forward + backward of
+one video self-attention layer (720p: B=1, 40 heads,
+head_dim 128, grid 21x45x80 = 75,600 tokens + 125 audio tokens, zone-structured
+q/k/v, top-k 8% + cumulative mass 0.9) on 1..N B200s of one node.
+
+A step = audio token norms + zone statistics + shape choice + permutation +
+pooled selection + sparse attention forward + scatter, then the backward
+(gather dO, sparse attention backward, scatter dQ/dK/dV).  With N > 1 GPUs the
+layer runs under Ulysses sequence parallelism (each rank holds S/N tokens of
+all 40 heads; all-to-all to 40/N heads of the full sequence and back), so the
+total work is fixed: "scaling": "strong".
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+value = whole-job effective TFLOPS = FLOPs of the selected 64x64 tile pairs
+(4*D*64*64 per pair for the forward, 2.5x that for the backward) / time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = dict(workload="720p dynamic BSA layer fwd+bwd (BASELINE config 1)", model="prism-video-self-attn",
+              grid=(21, 45, 80), heads=40, head_dim=128, audio_tokens=125, hidden=5120,
+              sparsity=0.92, cdf_threshold=0.9, method="ivpq")
+FWD_BWD_FACTOR = 3.5  # 1 (forward) + 2.5 (backward), SURVEY 8(d)
+
+
+# ------------------------------------------------------------------ inputs
+def make_layer_inputs(device, rank=0, world=1, seed=0):
+    """Config-1 synthetic layer, generated on the device from a seeded CPU generator
+    per zone (zone mean + 0.3 noise, both N(0, 0.5^2))."""
+    import torch
+    T, H, W = CONFIG["grid"]
+    h, D = CONFIG["heads"], CONFIG["head_dim"]
+    Tp, Hp, Wp = (math.ceil(x / 8) * 8 for x in (T, H, W))
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def zoned():
+        mean = torch.randn(h, Tp // 8, Hp // 8, Wp // 8, D, generator=g, device=device) * 0.5
+        m = mean.repeat_interleave(8, 1).repeat_interleave(8, 2).repeat_interleave(8, 3)
+        x = m + 0.3 * 0.5 * torch.randn(h, Tp, Hp, Wp, D, generator=g, device=device)
+        return x[:, :T, :H, :W].reshape(h, T * H * W, D).transpose(0, 1).to(torch.bfloat16)
+
+    S = T * H * W
+    q, k, v = zoned(), zoned(), zoned()          # [S, h, D]  (sequence-major, like the projections)
+    do = torch.randn(S, h, D, generator=g, device=device).to(torch.bfloat16)
+    a2v = torch.randn(S, CONFIG["hidden"], generator=g, device=device).to(torch.bfloat16)
+    from prism_b200.communications import sp_chunk_sizes
+    sizes = sp_chunk_sizes(S, world)
+    s0 = sum(sizes[:rank])
+    sl = slice(s0, s0 + sizes[rank])
+    out = {}
+    for name, t in (("q", q), ("k", k), ("v", v), ("do", do)):
+        out[name] = t[sl].reshape(1, sizes[rank], h * D).contiguous()
+    out["a2v"] = a2v[sl].unsqueeze(0).contiguous()
+    return out, S
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        def run():
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            while not self._stop.is_set():
+                try:
+                    r = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                        "--format=csv,noheader,nounits"], capture_output=True,
+                                       text=True, timeout=5)
+                    self.samples.append([x.strip() for x in r.stdout.strip().split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        sm = [float(s[0]) for s in self.samples if len(s) >= 7 and s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if len(s) >= 7 and s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples if len(s) >= 7 for i in range(4)
+                          if s[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ step
+def make_step(inp, S, world, capture=None):
+    import torch
+    from prism_b200.attention import dynamic_self_attention
+
+    T, H, W = CONFIG["grid"]
+    h = CONFIG["heads"]
+
+    def step(q, k, v, do, a2v):
+        x, _ = dynamic_self_attention(q, k, v, (T, H, W), h, a2v_bridge_residual=a2v,
+                                      full_seq_len=S, method=CONFIG["method"],
+                                      sparsity=CONFIG["sparsity"],
+                                      cdf_threshold=CONFIG["cdf_threshold"],
+                                      return_shape_ids=True)
+        x.backward(do)
+        return x
+    return step
+
+
+def selected_pairs(q, k, v, a2v, S, world):
+    """Count selected (q tile, k tile) pairs over all heads of this rank."""
+    import torch
+    from prism_b200.attention import audio_token_norms
+    from prism_b200.communications import all_to_all_4D
+    from prism_b200.dynamic_block_attention import run_bsa_dynamic
+    from prism_b200.parallel_states import get_sequence_parallel_state, nccl_info
+    h, D = CONFIG["heads"], CONFIG["head_dim"]
+    with torch.no_grad():
+        norms = audio_token_norms(a2v, S)
+        q4, k4, v4 = (t.view(1, t.shape[1], h, D) for t in (q, k, v))
+        if get_sequence_parallel_state():
+            g = nccl_info.sp_group
+            q4, k4, v4 = (all_to_all_4D(t, g, 2, 1, S) for t in (q4, k4, v4))
+        _, plan = run_bsa_dynamic(q4, k4, v4, CONFIG["grid"], layout="bshd", method=CONFIG["method"],
+                                  sparsity=CONFIG["sparsity"], cdf_threshold=CONFIG["cdf_threshold"],
+                                  audio_token_norms=norms, return_plan=True)
+        pc = torch.zeros(1, dtype=torch.int64, device=q.device)
+        bq = plan.bits_q.view(torch.int32)
+        # popcount over int32 words
+        x = bq.to(torch.int64) & 0xFFFFFFFF
+        cnt = torch.zeros_like(x)
+        for _ in range(32):
+            cnt += x & 1
+            x = x >> 1
+        pc += cnt.sum()
+    return int(pc.item()), plan, (q4, k4, v4, norms)
+
+
+def kernel_times(plan, q4, k4, v4, reps=3):
+    """CUDA-event timing of each attention kernel launch on its own stream."""
+    import torch
+    from prism_b200 import ops, _lib
+    from prism_b200.dynamic_block_attention import _hsd
+    qh, kh, vh = (_hsd(t, "bshd") for t in (q4, k4, v4))
+    q_re = ops.gather_rows(qh, plan.grid, plan.grid_padded, plan.src_idx)
+    k_re = ops.gather_rows(kh, plan.grid, plan.grid_padded, plan.src_idx)
+    v_re = ops.gather_rows(vh, plan.grid, plan.grid_padded, plan.src_idx)
+    heads, Sp, D = q_re.shape
+    stream = torch.cuda.current_stream()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    res = {}
+    o, lse = ops.bsa_fwd(q_re, k_re, v_re, plan.bits_q, plan.tile_bits, plan.sm_scale)
+    do = torch.randn_like(o)
+    delta = torch.empty(heads, Sp, dtype=torch.float32, device=o.device)
+    dq, dk, dv = torch.empty_like(o), torch.empty_like(o), torch.empty_like(o)
+    P = ops._p
+    st = ops._stream(o)
+    calls = {
+        "bsa_fwd": lambda: ops.bsa_fwd(q_re, k_re, v_re, plan.bits_q, plan.tile_bits, plan.sm_scale),
+        "bsa_bwd_delta": lambda: _lib.call("prism_bsa_bwd_delta", P(o), P(do), heads, Sp, D, P(delta), st),
+        "bsa_bwd_dkdv": lambda: _lib.call("prism_bsa_bwd_dkdv", P(q_re), P(k_re), P(v_re), P(do), P(lse),
+                                          P(delta), heads, Sp, D, float(plan.sm_scale), P(plan.bits_k),
+                                          P(plan.tile_bits), P(dk), P(dv), st),
+        "bsa_bwd_dq": lambda: _lib.call("prism_bsa_bwd_dq", P(q_re), P(k_re), P(v_re), P(do), P(lse),
+                                        P(delta), heads, Sp, D, float(plan.sm_scale), P(plan.bits_q),
+                                        P(plan.tile_bits), P(dq), st),
+    }
+    for name, fn in calls.items():
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / reps
+    return res
+
+
+# ------------------------------------------------------------------ CPU leg
+def cpu_baseline(seconds=15.0, threads=None):
+    """The CPU oracle (numpy float32 block-gather attention + the C selection
+    restatement) timed on the host on a bounded sample of the config-1 layer:
+    one head, a random subset of q tiles, forward + backward."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    from oracle import oracle as O  # CPU checker / baseline only
+    threads = threads or os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    T, H, W = CONFIG["grid"]
+    D = CONFIG["head_dim"]
+    Tp, Hp, Wp = (math.ceil(x / 8) * 8 for x in (T, H, W))
+    rng = np.random.default_rng(0)
+    Nz = (Tp // 8) * (Hp // 8) * (Wp // 8)
+    S = Tp * Hp * Wp
+    nt = S // 64
+
+    def zoned():
+        mean = rng.standard_normal((Nz, D), dtype=np.float32) * 0.5
+        x = np.repeat(mean, 512, axis=0) + 0.15 * rng.standard_normal((S, D), dtype=np.float32)
+        return x
+
+    q, k, v = zoned(), zoned(), zoned()
+    do = rng.standard_normal((S, D), dtype=np.float32)
+    valid = np.ones(S, np.uint8)
+    # selection (C oracle, one head) -- all 64-token shape-0 layout of the bench grid
+    t0 = time.perf_counter()
+    ids = np.zeros(Nz, np.int64)
+    src, inv, bot, bt, nb = O.layout(ids, (Tp, Hp, Wp))
+    qb = O.f32_to_bf16_bits(q)[None]
+    kb = O.f32_to_bf16_bits(k)[None]
+    bq, bk, _ = O.block_select(qb, kb, valid, bt, nb, CONFIG["sparsity"], CONFIG["cdf_threshold"])
+    t_sel = time.perf_counter() - t0
+    dense = O.bits_to_dense(bq, nt)[0]
+    # attention: as many q tiles as fit the time budget
+    sc = 1.0 / math.sqrt(D)
+    flops = 0.0
+    n_done = 0
+    t1 = time.perf_counter()
+    order = rng.permutation(nt)
+    for qt in order:
+        cols = np.nonzero(dense[qt])[0]
+        keys = (cols[:, None] * 64 + np.arange(64)).reshape(-1)
+        rows = slice(qt * 64, qt * 64 + 64)
+        Q, K, V, dO = q[rows], k[keys], v[keys], do[rows]
+        s = Q @ K.T * sc
+        p = np.exp(s - s.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        o = p @ V
+        dv = p.T @ dO
+        dp = dO @ V.T
+        ds = p * (dp - (o * dO).sum(1, keepdims=True))
+        dq = ds @ K * sc
+        dk = ds.T @ Q * sc
+        flops += FWD_BWD_FACTOR * 4 * D * 64 * 64 * cols.size
+        n_done += 1
+        if time.perf_counter() - t1 > seconds:
+            break
+    t_attn = time.perf_counter() - t1
+    tflops = flops / t_attn / 1e12
+    return {"value": tflops, "unit": "TFLOPS", "cores": threads, "kind": "port",
+            "sample": f"1 of 40 heads, {n_done} of {nt} q tiles fwd+bwd in numpy float32 "
+                      f"block-gather form ({t_attn:.1f} s); selection of that head by the C "
+                      f"oracle took {t_sel:.1f} s",
+            "ms_per_layer_extrapolated": (t_attn / max(n_done, 1) * nt * CONFIG["heads"] + t_sel * CONFIG["heads"]) * 1e3}
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="prism", choices=["prism", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = []
+        cpu = None
+        for i in range(args.warmup + args.steps):
+            r = cpu_baseline(seconds=8.0)
+            if i >= args.warmup:
+                steps.append(r)
+            cpu = r
+        val = statistics.mean(s["value"] for s in steps)
+        line = {"impl": "reference", "metric": "bsa_fwd_bwd_effective_tflops", "value": val,
+                "unit": "TFLOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": statistics.mean(s["ms_per_layer_extrapolated"] for s in steps),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic",
+                "config": dict(CONFIG, grid=list(CONFIG["grid"])),
+                "cpu_baseline": {k: cpu[k] for k in ("kind", "cores", "sample")} | {"value": val, "unit": "TFLOPS"},
+                "e2e": {"value": val, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    from prism_b200 import _lib
+    from prism_b200.parallel_states import initialize_sequence_parallel
+    _lib.load(build_if_missing=False)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        initialize_sequence_parallel()
+
+    inp, S = make_layer_inputs(dev, rank, world)
+    q = inp["q"].requires_grad_(True)
+    k = inp["k"].requires_grad_(True)
+    v = inp["v"].requires_grad_(True)
+    do, a2v = inp["do"], inp["a2v"]
+    step = make_step(inp, S, world)
+
+    def run_step():
+        q.grad = k.grad = v.grad = None
+        step(q, k, v, do, a2v)
+
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    l0 = _lib.launch_count
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record()
+    for _ in range(args.steps):
+        run_step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clk.stop()
+    launches = (_lib.launch_count - l0) // args.steps
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+
+    # FLOPs actually computed (selected tile pairs, all ranks)
+    pairs, plan, (q4, k4, v4, norms) = selected_pairs(q.detach(), k.detach(), v.detach(), a2v, S, world)
+    pt = torch.tensor([pairs], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(pt)
+    total_pairs = float(pt.item())
+    D = CONFIG["head_dim"]
+    flops = FWD_BWD_FACTOR * 4 * D * 64 * 64 * total_pairs
+    tflops = flops / (ms * 1e-3) / 1e12
+    Tp, Hp, Wp = (math.ceil(x / 8) * 8 for x in CONFIG["grid"])
+    n_tiles = Tp * Hp * Wp // 64
+    density = total_pairs / (CONFIG["heads"] * n_tiles * n_tiles)
+
+    # per-kernel times (rank 0's local heads) for the roofline of the dominant kernel
+    kt = kernel_times(plan, q4, k4, v4)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    local_pairs = pairs
+    # per (q tile, k tile) pair one 64x64xD product is 2*64*64*D FLOPs; the forward
+    # computes 2 of them (QK^T, PV), dK/dV 4 (S^T, dP^T, dV, dK), dQ 3 (S, dP, dQ)
+    mm = 2 * 64 * 64 * D * local_pairs
+    algo = {"bsa_fwd": 2 * mm, "bsa_bwd_dkdv": 4 * mm, "bsa_bwd_dq": 3 * mm}
+    dom = max(("bsa_fwd", "bsa_bwd_dkdv", "bsa_bwd_dq"), key=lambda n: kt[n])
+    achieved = algo[dom] / (kt[dom] * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if peaks else "fallback",
+                "kernel_ms": kt}
+
+    # end-to-end through host buffers (pinned), H2D inputs + D2H output and grads
+    e2e = None
+    if not args.no_e2e:
+        host = {n: inp[n].detach().cpu().pin_memory() for n in ("q", "k", "v", "do", "a2v")}
+        outs = {n: torch.empty(inp["q"].shape, dtype=torch.bfloat16).pin_memory() for n in ("o", "dq", "dk", "dv")}
+        h2d = sum(x.numel() * x.element_size() for x in host.values())
+        d2h = sum(x.numel() * x.element_size() for x in outs.values())
+        from prism_b200.attention import dynamic_self_attention
+
+        def e2e_step():
+            dq_, dk_, dv_ = (host[n].to(dev, non_blocking=True).requires_grad_(True) for n in ("q", "k", "v"))
+            dd = host["do"].to(dev, non_blocking=True)
+            aa = host["a2v"].to(dev, non_blocking=True)
+            x = dynamic_self_attention(dq_, dk_, dv_, CONFIG["grid"], CONFIG["heads"], a2v_bridge_residual=aa,
+                                       full_seq_len=S, method=CONFIG["method"], sparsity=CONFIG["sparsity"],
+                                       cdf_threshold=CONFIG["cdf_threshold"])
+            x.backward(dd)
+            outs["o"].copy_(x.detach(), non_blocking=True)
+            outs["dq"].copy_(dq_.grad, non_blocking=True)
+            outs["dk"].copy_(dk_.grad, non_blocking=True)
+            outs["dv"].copy_(dv_.grad, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        f1.record()
+        torch.cuda.synchronize()
+        ms_e = f0.elapsed_time(f1) / args.steps
+        te = torch.tensor([ms_e], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        ms_e = float(te.item())
+        e2e = {"value": flops / (ms_e * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": ms_e,
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(seconds=12.0)
+
+    if rank == 0:
+        line = {"metric": "bsa_fwd_bwd_effective_tflops", "value": tflops, "unit": "TFLOPS",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded zone-structured q/k/v, N(0,1) a2v residual)",
+                "config": dict(CONFIG, grid=list(CONFIG["grid"]), parallelism=f"ulysses_sp{world}",
+                               global_batch=1, seq_len=S, selected_tile_pairs=int(total_pairs),
+                               pair_density=density, l2="inputs larger than L2 (q/k/v 774 MB each)"),
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

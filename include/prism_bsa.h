@@ -1,0 +1,176 @@
+/*
+ * prism_bsa.h -- C ABI of the B200 (sm_100a) dynamic block-shape block-sparse
+ * attention path of Tencent-Hunyuan/Prism.
+ *
+ * All tensors are raw DEVICE pointers owned by the caller; every entry point
+ * enqueues work on `stream` and returns immediately.  No entry point allocates
+ * device memory, synchronises the host or exits the process; workspaces are
+ * caller-provided and sized by the matching *_workspace_bytes() query.
+ * Errors come back as a prism_status_t; prism_last_error() gives a
+ * thread-local message.
+ *
+ * Layout conventions
+ *   THW order   token s = (t*H + h)*W + w over a (T, H, W) latent grid.
+ *   padded grid (Tp, Hp, Wp) = (T, H, W) rounded up to multiples of 8 (the
+ *               8x8x8 macro-zone, dynamic_block_shape.py:31).
+ *   tile order  the per-zone anisotropic rearrangement: zone z holds tokens
+ *               [512 z, 512 z + 512), split into 64-token tiles; built by
+ *               prism_build_layout (src_idx[r] = padded THW index of row r).
+ *   bitmaps     bits_q[h][q_tile][w] bit b set <=> q tile attends key tile
+ *               32 w + b; bits_k is its transpose (key tile -> q tiles).
+ *               Row length WQ = ceil(N_tiles / 32) 32-bit words.
+ *   bf16        tensors are passed as void* holding __nv_bfloat16.
+ *
+ * Reference paths below are relative to the reference project root.
+ */
+#ifndef PRISM_BSA_H_
+#define PRISM_BSA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  PRISM_OK = 0,
+  PRISM_ERR_INVALID_ARG = 1,
+  PRISM_ERR_CUDA = 2,
+  PRISM_ERR_UNSUPPORTED = 3,
+} prism_status_t;
+
+/* Thread-local text of the last error raised on this host thread. */
+const char* prism_last_error(void);
+/* ABI version (incremented on any signature change). */
+int prism_abi_version(void);
+
+/* Per-token L2 norm of the audio->video bridge residual, bf16 in/out, fp32
+ * accumulation.  Replaces `a2v_bridge_residual.norm(dim=-1)`
+ * (hymm/models/modules/wan_video_dit.py:742-744).  dim % 8 == 0. */
+prism_status_t prism_token_norms(const void* x, int64_t n_tokens, int dim, void* out,
+                                 cudaStream_t stream);
+
+/* Zone statistics: head average of V (bf16, dynamic_block_attention.py:236) and
+ * the masked per-zone means packed as [Nz, 25*D] fp32 = channel | per-t[8] |
+ * per-h[8] | per-w[8] (compute_zone_aggregates, dynamic_block_shape.py:68-129),
+ * axis validity [Nz, 24] u8, and the same means of the audio norms [Nz, 25] fp32
+ * (compute_audio_directional's masked means, dynamic_block_shape.py:216-229).
+ * v [heads, T*H*W, D] bf16 on the source grid (T, H, W) <= (Tp, Hp, Wp) with
+ * head stride v_stride_h and token stride v_stride_s (elements); norms [T*H*W]
+ * bf16 on the same grid or NULL.  A token of the padded grid is valid iff it
+ * lies inside (T, H, W) and valid[padded index] (valid NULL = no extra mask):
+ * passing the unpadded tensors fuses the zero padding of
+ * wan_video_dit.py:364-395.  workspace: prism_zone_stats_workspace_bytes(). */
+size_t prism_zone_stats_workspace_bytes(int Tp, int Hp, int Wp, int D);
+prism_status_t prism_zone_stats(const void* v, int heads, int64_t v_stride_h, int64_t v_stride_s,
+                                int T, int H, int W, int Tp, int Hp, int Wp, int D,
+                                const uint8_t* valid, const void* norms, void* workspace,
+                                float* packed, uint8_t* axis_valid, float* audio,
+                                cudaStream_t stream);
+
+/* Shape choice per zone from the (SP-averaged) packed statistics:
+ * compute_effective_gradient + select_shapes_ivpq (method 0) or
+ * select_shapes_penalty (method 1) (dynamic_block_shape.py:248-391).
+ * shape_ids [Nz] int64 in [0, 13).  g_out [Nz,3] / rho_out [Nz] optional. */
+prism_status_t prism_shape_select(const float* packed, const uint8_t* axis_valid,
+                                  const float* audio, int has_audio, int Nz, int D, int method,
+                                  float lambda_a, float tau_128, float lambda_128,
+                                  int64_t* shape_ids, float* g_out, float* rho_out,
+                                  cudaStream_t stream);
+
+/* Permutation and tile/block maps (_precompute_local_orders,
+ * _build_rearrange_index, _build_block_tile_maps:
+ * dynamic_block_attention.py:21-63, 107-170).
+ * src_idx/inv_idx [S] int32; block_of_tile [N_tiles] int32;
+ * block_tiles [(N_tiles+1)*2] int32 (rows >= n_blocks hold the sentinel
+ * N_tiles); n_blocks [1] int32 (device).  N_tiles = 8 * Nz. */
+prism_status_t prism_build_layout(const int64_t* shape_ids, int Tp, int Hp, int Wp,
+                                  int32_t* src_idx, int32_t* inv_idx, int32_t* block_of_tile,
+                                  int32_t* block_tiles, int32_t* n_blocks, cudaStream_t stream);
+
+/* Key validity of each 64-token tile in tile order: bit i of tile_bits[j] is
+ * set iff padded token src_idx[64 j + i] lies inside the source grid
+ * (T, H, W) and (valid == NULL or valid[src_idx[64 j + i]]); tile_count[j] is
+ * its popcount (the reference's valid_re / tile_counts,
+ * dynamic_block_attention.py:253, 260). */
+prism_status_t prism_tile_valid(const int32_t* src_idx, const uint8_t* valid, int T, int H, int W,
+                                int Tp, int Hp, int Wp, uint64_t* tile_bits, int32_t* tile_count,
+                                cudaStream_t stream);
+
+/* Gather rows into tile order: out[h][r] = x[h][thw(src_idx[r])], where
+ * src_idx holds padded-grid THW indices and x is laid out on the grid
+ * (T, H, W) <= (Tp, Hp, Wp); rows outside (T, H, W) are written as zeros
+ * (the F.pad of wan_video_dit.py:382-389 fused with
+ * q.index_select(2, src_idx), dynamic_block_attention.py:250-252).
+ * Strides in elements; rows are D contiguous bf16, D % 8 == 0. */
+prism_status_t prism_gather_rows(const void* x, int64_t x_stride_h, int64_t x_stride_s, int heads,
+                                 int D, int T, int H, int W, int Tp, int Hp, int Wp,
+                                 const int32_t* src_idx, void* out, int64_t out_stride_h,
+                                 cudaStream_t stream);
+
+/* Inverse of prism_gather_rows for the tokens inside (T, H, W):
+ * out[h][thw] = x_re[h][inv_idx[padded thw]] (o_re.index_select(2, inv_idx)
+ * + unpad, dynamic_block_attention.py:329, wan_video_dit.py:429-431). */
+prism_status_t prism_scatter_rows(const void* x_re, int64_t x_stride_h, int heads, int D, int T,
+                                  int H, int W, int Tp, int Hp, int Wp, const int32_t* inv_idx,
+                                  void* out, int64_t out_stride_h, int64_t out_stride_s,
+                                  cudaStream_t stream);
+
+/* Pooled logical-block scores and hybrid selection, per head
+ * (masked_mean_pooling_compression bsa_interface.py:177-201,
+ * _logical_block_means dynamic_block_attention.py:173-188, cal_score
+ * bsa_interface.py:203-207, get_select_indices_{cdf_topk,cdf,topk}_from_score
+ * bsa_interface.py:235-304, tile expansion dynamic_block_attention.py:297-319).
+ * mode 0 = top-k + cumulative mass, 1 = cumulative mass only, 2 = top-k only.
+ * tile_bits from prism_tile_valid.  Writes every word of bits_q
+ * [heads, N_tiles, WQ] and of its transpose bits_k.  Ties in the top-k /
+ * cumulative-mass order are broken by lower block index.
+ * workspace: prism_block_select_workspace_bytes(). */
+size_t prism_block_select_workspace_bytes(int heads, int64_t S, int D);
+prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads, int64_t S, int D,
+                                  const int32_t* block_tiles, const int32_t* n_blocks,
+                                  const uint64_t* tile_bits, int mode, double sparsity,
+                                  double cdf_threshold, void* workspace, uint32_t* bits_q,
+                                  uint32_t* bits_k, cudaStream_t stream);
+
+/* Block-sparse attention forward over tile-ordered q/k/v [heads, S, D] bf16
+ * (attn_fwd_bsa_varlen_triton + _attn_fwd_bsa_varlen_align,
+ * bsa_interface.py:328-385, flash_attn_bsa_varlen_mask.py:193-319).
+ * o [heads, S, D] bf16; lse [heads, S] fp32 natural log.  D in {64, 128}. */
+prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
+                             int D, float sm_scale, const uint32_t* bits_q,
+                             const uint64_t* tile_bits, void* o, float* lse,
+                             cudaStream_t stream);
+
+/* Block-sparse attention backward (attn_bwd_bsa_varlen_triton,
+ * bsa_interface.py:387-523): delta, then dK/dV over bits_k, then dQ over
+ * bits_q.  workspace: prism_bsa_bwd_workspace_bytes() (holds delta). */
+size_t prism_bsa_bwd_workspace_bytes(int heads, int64_t S);
+prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const void* o,
+                             const void* dout, const float* lse, int heads, int64_t S, int D,
+                             float sm_scale, const uint32_t* bits_q, const uint32_t* bits_k,
+                             const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
+                             void* dv, cudaStream_t stream);
+
+/* The three stages of prism_bsa_bwd, callable one by one:
+ * delta[h][s] = sum_d O * dO (_attn_bwd_preprocess, common.py:94-111);
+ * dK, dV per key-tile pair over the transposed selection
+ * (_attn_bwd_dkdv_bsa_varlen_wrapper, flash_attn_bsa_varlen_mask.py:564-704);
+ * dQ per query-tile pair (_attn_bwd_dq_bsa_varlen_align_wrapper, :881-1014). */
+prism_status_t prism_bsa_bwd_delta(const void* o, const void* dout, int heads, int64_t S, int D,
+                                   float* delta, cudaStream_t stream);
+prism_status_t prism_bsa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout,
+                                  const float* lse, const float* delta, int heads, int64_t S, int D,
+                                  float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
+                                  void* dk, void* dv, cudaStream_t stream);
+prism_status_t prism_bsa_bwd_dq(const void* q, const void* k, const void* v, const void* dout,
+                                const float* lse, const float* delta, int heads, int64_t S, int D,
+                                float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
+                                void* dq, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PRISM_BSA_H_ */

@@ -1,0 +1,286 @@
+"""CPU oracle for Prism's dynamic block-sparse attention path.
+
+TEST INFRASTRUCTURE ONLY.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import this
+module, and only as the checker or the timed CPU baseline.  The product
+(``prism_b200``) never imports it.
+
+Two parts:
+
+* ``libprism_oracle.so`` (``prism_oracle.c``): bit-exact restatement of the
+  integer / selection side (zone statistics, shape choice, permutation,
+  pooled-block scoring and hybrid top-k + cumulative-mass selection).
+* numpy float64 block-sparse attention forward/backward, restating the Triton
+  kernels ``_attn_fwd_bsa_varlen_align`` (flash_attn_bsa_varlen_mask.py:193-319),
+  ``_attn_bwd_preprocess`` (common.py:94-111), ``_attn_bwd_dkdv_bsa_varlen_wrapper``
+  (flash_attn_bsa_varlen_mask.py:564-704) and ``_attn_bwd_dq_bsa_varlen_align_wrapper``
+  (:881-1014) as dense masked softmax attention over the selected 64-token tiles.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libprism_oracle.so")
+_lib = None
+
+SHAPES = [
+    (4, 4, 4), (8, 2, 4), (8, 4, 2), (2, 4, 8), (2, 8, 4), (4, 2, 8), (4, 8, 2),
+    (2, 8, 8), (8, 2, 8), (8, 8, 2), (4, 4, 8), (4, 8, 4), (8, 4, 4),
+]  # dynamic_block_shape.py:6-23
+
+
+def build() -> str:
+    """Compile prism_oracle.c with the committed Makefile."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH) or (
+            os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "prism_oracle.c"))
+        ):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        P = ctypes.c_void_p
+        i64, i32, f32, f64 = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_double
+        L.oracle_det_expf.argtypes = [f32]
+        L.oracle_det_expf.restype = f32
+        L.oracle_det_log2f.argtypes = [f32]
+        L.oracle_det_log2f.restype = f32
+        L.oracle_token_norms.argtypes = [P, i64, i32, P]
+        L.oracle_zone_stats.argtypes = [P, i32, i32, i32, i32, i32, P, P, P, P, P]
+        L.oracle_shape_select.argtypes = [P, P, P, i32, i32, i32, i32, f32, f32, f32, P, P, P]
+        L.oracle_layout.argtypes = [P, i32, i32, i32, P, P, P, P]
+        L.oracle_layout.restype = i64
+        L.oracle_block_select.argtypes = [P, P, i32, i64, i32, P, i64, P, i32, f64, f64, P, P, P]
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ---------------------------------------------------------------- bf16 helpers
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ------------------------------------------------------------ selection side
+def token_norms(x_bits: np.ndarray) -> np.ndarray:
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    n, dim = x_bits.shape
+    out = np.empty(n, dtype=np.uint16)
+    lib().oracle_token_norms(_p(x_bits), n, dim, _p(out))
+    return out
+
+
+def zone_stats(v_bits, grid, valid=None, norms_bits=None):
+    """v_bits [heads, S, D] uint16 (bf16 bits).  Returns packed, axis_valid, audio."""
+    v_bits = np.ascontiguousarray(v_bits, dtype=np.uint16)
+    heads, S, D = v_bits.shape
+    T, H, W = grid
+    Nz = (T // 8) * (H // 8) * (W // 8)
+    packed = np.empty((Nz, 25 * D), np.float32)
+    axis_valid = np.empty((Nz, 24), np.uint8)
+    audio = np.empty((Nz, 25), np.float32)
+    valid = None if valid is None else np.ascontiguousarray(valid, dtype=np.uint8)
+    norms_bits = None if norms_bits is None else np.ascontiguousarray(norms_bits, dtype=np.uint16)
+    lib().oracle_zone_stats(_p(v_bits), heads, T, H, W, D, _p(valid), _p(norms_bits),
+                            _p(packed), _p(axis_valid), _p(audio))
+    return packed, axis_valid, audio
+
+
+def shape_select(packed, axis_valid, audio, has_audio, method="ivpq", lambda_a=0.5,
+                 tau_128=0.15, lambda_128=1.0):
+    packed = np.ascontiguousarray(packed, np.float32)
+    axis_valid = np.ascontiguousarray(axis_valid, np.uint8)
+    audio = np.ascontiguousarray(audio, np.float32)
+    Nz = packed.shape[0]
+    D = packed.shape[1] // 25
+    ids = np.empty(Nz, np.int64)
+    g = np.empty((Nz, 3), np.float32)
+    rho = np.empty(Nz, np.float32)
+    m = {"ivpq": 0, "penalty": 1}[method]
+    lib().oracle_shape_select(_p(packed), _p(axis_valid), _p(audio), int(bool(has_audio)), Nz, D,
+                              m, lambda_a, tau_128, lambda_128, _p(ids), _p(g), _p(rho))
+    return ids, g, rho
+
+
+def layout(shape_ids, grid):
+    shape_ids = np.ascontiguousarray(shape_ids, np.int64)
+    T, H, W = grid
+    S = T * H * W
+    Nz = shape_ids.shape[0]
+    src = np.empty(S, np.int64)
+    inv = np.empty(S, np.int64)
+    bot = np.empty(Nz * 8, np.int64)
+    bt = np.empty((Nz * 8 + 1) * 2, np.int64)
+    nb = lib().oracle_layout(_p(shape_ids), T, H, W, _p(src), _p(inv), _p(bot), _p(bt))
+    return src, inv, bot, bt[: (nb + 1) * 2].reshape(nb + 1, 2), int(nb)
+
+
+def selection_mode(sparsity, cdf_threshold):
+    if sparsity is not None and cdf_threshold is not None:
+        return 0
+    if sparsity is None and cdf_threshold is not None:
+        return 1
+    if sparsity is not None and cdf_threshold is None:
+        return 2
+    raise ValueError("Either sparsity or cdf_threshold must be provided")
+
+
+def block_select(q_re_bits, k_re_bits, valid_re, block_tiles, nb, sparsity, cdf_threshold,
+                 want_blocks=False):
+    """Returns (bits_q [h, N_tiles, WQ] u32, bits_k [h, N_tiles, WQ] u32, sel_blocks or None)."""
+    q_re_bits = np.ascontiguousarray(q_re_bits, np.uint16)
+    k_re_bits = np.ascontiguousarray(k_re_bits, np.uint16)
+    heads, S, D = q_re_bits.shape
+    n_tiles = S // 64
+    wq = (n_tiles + 31) // 32
+    bits_q = np.zeros((heads, n_tiles, wq), np.uint32)
+    bits_k = np.zeros((heads, n_tiles, wq), np.uint32)
+    sel = np.zeros((heads, nb, nb), np.uint8) if want_blocks else None
+    valid_re = None if valid_re is None else np.ascontiguousarray(valid_re, np.uint8)
+    bt = np.ascontiguousarray(block_tiles, np.int64)
+    mode = selection_mode(sparsity, cdf_threshold)
+    lib().oracle_block_select(_p(q_re_bits), _p(k_re_bits), heads, S, D, _p(valid_re), nb, _p(bt),
+                              mode, float(sparsity if sparsity is not None else 0.0),
+                              float(cdf_threshold if cdf_threshold is not None else 0.0),
+                              _p(bits_q), _p(bits_k), _p(sel))
+    return bits_q, bits_k, sel
+
+
+def bits_to_dense(bits: np.ndarray, n_cols: int) -> np.ndarray:
+    """[..., rows, WQ] u32 -> [..., rows, n_cols] bool."""
+    b = bits.view(np.uint8).reshape(*bits.shape[:-1], bits.shape[-1] * 4)
+    d = np.unpackbits(b, axis=-1, bitorder="little").astype(bool)
+    return d[..., :n_cols]
+
+
+def dense_to_bits(dense: np.ndarray) -> np.ndarray:
+    n_cols = dense.shape[-1]
+    wq = (n_cols + 31) // 32
+    pad = np.zeros((*dense.shape[:-1], wq * 32), bool)
+    pad[..., :n_cols] = dense
+    return np.packbits(pad, axis=-1, bitorder="little").view(np.uint32)
+
+
+def tile_lists_to_dense(tile_block_indices, lens, n_tiles):
+    """Reference selection (tile_block_indices [B,h,Nt,W], lens [B,h,Nt]) -> [h, Nt, Nt] bool."""
+    tbi = np.asarray(tile_block_indices)[0]
+    ln = np.asarray(lens)[0]
+    h, nt, w = tbi.shape
+    dense = np.zeros((h, nt, n_tiles), bool)
+    pos = np.arange(w)[None, None, :]
+    keep = pos < ln[..., None]
+    hh, rr, cc = np.nonzero(keep)
+    dense[hh, rr, tbi[hh, rr, cc]] = True
+    return dense
+
+
+# ------------------------------------------------------------ attention side
+def token_mask(bits_q: np.ndarray, valid_re, S: int) -> np.ndarray:
+    """[h, S, S] bool: query token i may attend key token j."""
+    n_tiles = S // 64
+    dense = bits_to_dense(bits_q, n_tiles)  # [h, Nt, Nt]
+    m = np.repeat(np.repeat(dense, 64, axis=1), 64, axis=2)
+    if valid_re is not None:
+        m = m & np.asarray(valid_re, bool)[None, None, :]
+    return m
+
+
+def bsa_forward(q, k, v, bits_q, valid_re, sm_scale=None):
+    """Float64 restatement of the sparse forward.  q,k,v [h, S, D] float.
+
+    Returns (o [h,S,D], lse [h,S]) with lse natural-log (bsa_interface.py:382-383);
+    rows with no selected valid key give o = 0 and lse = -inf, as the
+    reference's l_i = 1 initialisation does (flash_attn_bsa_varlen_mask.py:264)."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    h, S, D = q.shape
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    m = token_mask(bits_q, valid_re, S)
+    s = np.einsum("hid,hjd->hij", q, k) * sm_scale
+    s = np.where(m, s, -np.inf)
+    mx = s.max(-1, keepdims=True)
+    empty = ~np.isfinite(mx)
+    mx = np.where(empty, 0.0, mx)
+    p = np.exp(s - mx)
+    l = p.sum(-1, keepdims=True)
+    lsafe = np.where(l > 0, l, 1.0)
+    o = np.einsum("hij,hjd->hid", p / lsafe, v)
+    lse = np.where(empty[..., 0], -np.inf, (mx + np.log(lsafe))[..., 0])
+    return o, lse
+
+
+def bsa_backward(q, k, v, o, do, bits_q, valid_re, sm_scale=None):
+    """Float64 gradient of bsa_forward given the (possibly rounded) output o.
+
+    Delta = rowsum(o * do) uses the stored output, as _attn_bwd_preprocess does."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    o = np.asarray(o, np.float64)
+    do = np.asarray(do, np.float64)
+    h, S, D = q.shape
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    m = token_mask(bits_q, valid_re, S)
+    s = np.einsum("hid,hjd->hij", q, k) * sm_scale
+    s = np.where(m, s, -np.inf)
+    mx = s.max(-1, keepdims=True)
+    mx = np.where(np.isfinite(mx), mx, 0.0)
+    p = np.exp(s - mx)
+    l = p.sum(-1, keepdims=True)
+    p = p / np.where(l > 0, l, 1.0)
+    delta = (o * do).sum(-1, keepdims=True)
+    dp = np.einsum("hid,hjd->hij", do, v)
+    ds = p * (dp - delta)
+    dq = np.einsum("hij,hjd->hid", ds, k) * sm_scale
+    dk = np.einsum("hij,hid->hjd", ds, q) * sm_scale
+    dv = np.einsum("hij,hid->hjd", p, do)
+    return dq, dk, dv
+
+
+# -------------------------------------------------------------- full path
+def dynamic_forward_selection(q_bits, k_bits, v_bits, grid, *, method, sparsity, cdf_threshold,
+                              norms_bits=None, valid=None, lambda_a=0.5, tau_128=0.15,
+                              lambda_128=1.0, shape_ids=None):
+    """Oracle for steps (1)-(5) of flash_attn_bsa_3d_dynamic
+    (dynamic_block_attention.py:233-319).  Inputs are bf16 bit arrays [h,S,D].
+
+    Returns a dict with shape_ids, src_idx, inv_idx, block_tiles, nb, valid_re,
+    q_re/k_re/v_re (bits), bits_q, bits_k."""
+    T, H, W = grid
+    if shape_ids is None:
+        packed, av, audio = zone_stats(v_bits, grid, valid, norms_bits)
+        shape_ids, g, rho = shape_select(packed, av, audio, norms_bits is not None, method,
+                                         lambda_a, tau_128, lambda_128)
+    src, inv, bot, bt, nb = layout(shape_ids, grid)
+    q_re = np.ascontiguousarray(q_bits[:, src])
+    k_re = np.ascontiguousarray(k_bits[:, src])
+    v_re = np.ascontiguousarray(v_bits[:, src])
+    valid_re = None if valid is None else np.ascontiguousarray(np.asarray(valid, np.uint8)[src])
+    bq, bk, _ = block_select(q_re, k_re, valid_re, bt, nb, sparsity, cdf_threshold)
+    return dict(shape_ids=np.asarray(shape_ids, np.int64), src_idx=src, inv_idx=inv,
+                block_of_tile=bot, block_tiles=bt, nb=nb, valid_re=valid_re, q_re=q_re,
+                k_re=k_re, v_re=v_re, bits_q=bq, bits_k=bk)

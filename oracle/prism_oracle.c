@@ -1,0 +1,635 @@
+/*
+ * prism_oracle.c -- CPU restatement of Prism's dynamic block-shape block-sparse
+ * attention path (selection side).  TEST INFRASTRUCTURE ONLY: this file is the
+ * checker that the CUDA kernels in prism_b200/csrc are compared against.  The
+ * product never links, loads or calls it.
+ *
+ * Every function follows one step of the reference and cites it
+ * (paths are relative to the reference project root):
+ *
+ *   oracle_token_norms   hymm/models/modules/wan_video_dit.py:742-744
+ *   oracle_zone_stats    block_sparse_attention/dynamic_block_attention.py:236,
+ *                        block_sparse_attention/dynamic_block_shape.py:68-129,
+ *                        dynamic_block_shape.py:189-245 (audio part)
+ *   oracle_shape_select  dynamic_block_shape.py:248-391
+ *   oracle_layout        dynamic_block_attention.py:21-63, 107-170
+ *   oracle_block_select  bsa_interface.py:177-201, 203-207, 235-304,
+ *                        dynamic_block_attention.py:173-188, 256-319
+ *
+ * Floating-point order.  The reference leaves summation order to torch; this
+ * restatement fixes one order (the one the CUDA kernels use) so that GPU and
+ * CPU agree bit for bit.  Build with -ffp-contract=off: every a*b+c below is
+ * two roundings unless fmaf() is written out.
+ *
+ * Parity against the reference itself is pinned by tests/golden (fixtures
+ * produced by running the reference's own Python code on CPU).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ bf16 */
+static float bf16_to_f32(uint16_t b) {
+  uint32_t u = ((uint32_t)b) << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+static uint16_t f32_to_bf16_rn(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u); /* NaN */
+  uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7fffu + lsb;
+  return (uint16_t)(u >> 16);
+}
+
+/* ------------------------------------------------- deterministic math
+ * exp and log2 evaluated in double with only + - * / (each correctly rounded)
+ * and exact scalings, then rounded once to float.  Same algorithm as the
+ * device code; results are bit-identical on CPU and GPU.
+ *
+ * exp:  Cody-Waite argument reduction x = k*ln2 + r, |r| <= ln2/2, then the
+ *       Taylor series of e^r to degree 13 (Horner), then scaling by 2^k.
+ * log2: x = 2^e * m with m in [sqrt(1/2), sqrt(2)), ln m = 2*atanh(z),
+ *       z = (m-1)/(m+1), atanh series to z^23, then log2 x = e + ln m / ln 2.
+ */
+static double pow2_int(int k) { /* 2^k for -1022 <= k <= 1023 */
+  uint64_t bits = (uint64_t)(k + 1023) << 52;
+  double d;
+  memcpy(&d, &bits, 8);
+  return d;
+}
+
+float oracle_det_expf(float xf) {
+  if (xf == -INFINITY) return 0.0f;
+  if (xf < -120.0f) return 0.0f;
+  if (xf > 88.0f) return INFINITY;
+  const double LN2_HI = 6.93147180369123816490e-01; /* ln2 split: hi has 32 bits */
+  const double LN2_LO = 1.90821492927058770002e-10;
+  const double INV_LN2 = 1.44269504088896338700e+00;
+  double x = (double)xf;
+  double kd = nearbyint(x * INV_LN2);
+  int k = (int)kd;
+  double r = (x - kd * LN2_HI) - kd * LN2_LO;
+  /* Taylor: sum_{n=0}^{13} r^n / n!  (Horner) */
+  double p = 1.0 / 6227020800.0; /* 1/13! */
+  p = p * r + 1.0 / 479001600.0;
+  p = p * r + 1.0 / 39916800.0;
+  p = p * r + 1.0 / 3628800.0;
+  p = p * r + 1.0 / 362880.0;
+  p = p * r + 1.0 / 40320.0;
+  p = p * r + 1.0 / 5040.0;
+  p = p * r + 1.0 / 720.0;
+  p = p * r + 1.0 / 120.0;
+  p = p * r + 1.0 / 24.0;
+  p = p * r + 1.0 / 6.0;
+  p = p * r + 0.5;
+  p = p * r + 1.0;
+  p = p * r + 1.0;
+  return (float)(p * pow2_int(k));
+}
+
+float oracle_det_log2f(float xf) {
+  /* xf > 0 and normal (callers clamp to >= 1e-4) */
+  uint32_t u;
+  memcpy(&u, &xf, 4);
+  int e = (int)((u >> 23) & 0xff) - 127;
+  uint32_t mb = (u & 0x007fffffu) | 0x3f800000u;
+  float mf;
+  memcpy(&mf, &mb, 4);
+  double m = (double)mf;
+  if (m > 1.4142135623730951) { m = m * 0.5; e += 1; }
+  double z = (m - 1.0) / (m + 1.0);
+  double z2 = z * z;
+  double s = 1.0 / 23.0;
+  s = s * z2 + 1.0 / 21.0;
+  s = s * z2 + 1.0 / 19.0;
+  s = s * z2 + 1.0 / 17.0;
+  s = s * z2 + 1.0 / 15.0;
+  s = s * z2 + 1.0 / 13.0;
+  s = s * z2 + 1.0 / 11.0;
+  s = s * z2 + 1.0 / 9.0;
+  s = s * z2 + 1.0 / 7.0;
+  s = s * z2 + 1.0 / 5.0;
+  s = s * z2 + 1.0 / 3.0;
+  s = s * z2 + 1.0;
+  double lnm = 2.0 * z * s;
+  const double INV_LN2 = 1.44269504088896338700e+00;
+  return (float)((double)e + lnm * INV_LN2);
+}
+
+/* -------------------------------------------------------- token norms
+ * ||x[n]||_2 over `dim` channels, bf16 in / bf16 out.
+ * Order (one 32-lane warp per token): lane l owns 8-element chunks
+ * c = l, l+32, ...; within a chunk acc = fmaf(x, x, acc) sequentially;
+ * then a butterfly over lanes (xor 16, 8, 4, 2, 1) of plain adds.
+ * Reference: wan_video_dit.py:742-744 (a2v_bridge_residual.norm(dim=-1)).
+ */
+void oracle_token_norms(const uint16_t* x, int64_t n, int dim, uint16_t* out) {
+  for (int64_t t = 0; t < n; ++t) {
+    const uint16_t* row = x + t * (int64_t)dim;
+    float acc[32];
+    for (int l = 0; l < 32; ++l) {
+      float a = 0.0f;
+      for (int c = l; c * 8 < dim; c += 32)
+        for (int j = 0; j < 8; ++j) {
+          float v = bf16_to_f32(row[c * 8 + j]);
+          a = fmaf(v, v, a);
+        }
+      acc[l] = a;
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+      float nxt[32];
+      for (int l = 0; l < 32; ++l) nxt[l] = acc[l] + acc[l ^ off];
+      memcpy(acc, nxt, sizeof(acc));
+    }
+    out[t] = f32_to_bf16_rn(sqrtf(acc[0]));
+  }
+}
+
+/* ---------------------------------------------------------- zone stats
+ * v [heads, S, D] bf16 (THW order, padded), valid [S] (NULL = all valid),
+ * norms [S] bf16 (NULL = no audio).
+ * Outputs:
+ *   packed      [Nz, 25*D] f32 : channel mean | T means [8,D] | H [8,D] | W [8,D]
+ *   axis_valid  [Nz, 24] u8    : t_valid[8] | h_valid[8] | w_valid[8]
+ *   audio       [Nz, 25]  f32  : a_bar | aT[8] | aH[8] | aW[8]  (masked means)
+ * Head average: vavg = bf16( (sum_h v_h, sequential) / heads )
+ *   (dynamic_block_attention.py:236 -- torch bf16 mean = fp32 sum / n, rounded).
+ * Per (zone, local frame lt), per channel: rowH[lh] = sum_lw x (sequential lw),
+ * frame = sum_lh rowH[lh], colW[lw] = sum_lh x (sequential lh); then the
+ * zone sums combine the eight frames in order lt = 0..7.
+ * Masked means as dynamic_block_shape.py:96-111 (count clamped to >= 1).
+ */
+void oracle_zone_stats(const uint16_t* v, int heads, int T, int H, int W, int D,
+                       const uint8_t* valid, const uint16_t* norms,
+                       float* packed, uint8_t* axis_valid, float* audio) {
+  const int ZT = T / 8, ZH = H / 8, ZW = W / 8;
+  const int Nz = ZT * ZH * ZW;
+  const int64_t S = (int64_t)T * H * W;
+  const int PK = 25 * D;
+  float* rowH = (float*)malloc(sizeof(float) * 8 * 8 * D); /* [lt][lh][D] */
+  float* colW = (float*)malloc(sizeof(float) * 8 * 8 * D); /* [lt][lw][D] */
+  float* frame = (float*)malloc(sizeof(float) * 8 * D);    /* [lt][D] */
+  for (int z = 0; z < Nz; ++z) {
+    const int zt = z / (ZH * ZW), zh = (z / ZW) % ZH, zw = z % ZW;
+    int cT[8] = {0}, cH[8] = {0}, cW[8] = {0}, call = 0;
+    float arow[8][8], acol[8][8], aframe[8];
+    for (int lt = 0; lt < 8; ++lt) {
+      for (int d = 0; d < D; ++d) {
+        float cw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float fr = 0.0f;
+        for (int lh = 0; lh < 8; ++lh) {
+          float rh = 0.0f;
+          for (int lw = 0; lw < 8; ++lw) {
+            int64_t s = ((int64_t)(zt * 8 + lt) * H + (zh * 8 + lh)) * W + (zw * 8 + lw);
+            if (valid && !valid[s]) continue;
+            float acc = 0.0f;
+            for (int h = 0; h < heads; ++h) acc += bf16_to_f32(v[((int64_t)h * S + s) * D + d]);
+            float x = bf16_to_f32(f32_to_bf16_rn(acc / (float)heads));
+            rh += x;
+            cw[lw] += x;
+          }
+          rowH[(lt * 8 + lh) * D + d] = rh;
+          fr += rh;
+        }
+        for (int lw = 0; lw < 8; ++lw) colW[(lt * 8 + lw) * D + d] = cw[lw];
+        frame[lt * D + d] = fr;
+      }
+      /* audio: one scalar per token, same structure */
+      {
+        float cw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float fr = 0.0f;
+        for (int lh = 0; lh < 8; ++lh) {
+          float rh = 0.0f;
+          for (int lw = 0; lw < 8; ++lw) {
+            int64_t s = ((int64_t)(zt * 8 + lt) * H + (zh * 8 + lh)) * W + (zw * 8 + lw);
+            if (valid && !valid[s]) continue;
+            cT[lt]++; cH[lh]++; cW[lw]++; call++;
+            float x = norms ? bf16_to_f32(norms[s]) : 0.0f;
+            rh += x;
+            cw[lw] += x;
+          }
+          arow[lt][lh] = rh;
+          fr += rh;
+        }
+        for (int lw = 0; lw < 8; ++lw) acol[lt][lw] = cw[lw];
+        aframe[lt] = fr;
+      }
+    }
+    float* pk = packed + (int64_t)z * PK;
+    const float fall = (float)(call > 0 ? call : 1);
+    for (int d = 0; d < D; ++d) {
+      float cs = 0.0f;
+      for (int lt = 0; lt < 8; ++lt) cs += frame[lt * D + d];
+      pk[d] = cs / fall;
+      for (int lt = 0; lt < 8; ++lt)
+        pk[D + lt * D + d] = frame[lt * D + d] / (float)(cT[lt] > 0 ? cT[lt] : 1);
+      for (int p = 0; p < 8; ++p) {
+        float sh = 0.0f, sw = 0.0f;
+        for (int lt = 0; lt < 8; ++lt) {
+          sh += rowH[(lt * 8 + p) * D + d];
+          sw += colW[(lt * 8 + p) * D + d];
+        }
+        pk[D + 8 * D + p * D + d] = sh / (float)(cH[p] > 0 ? cH[p] : 1);
+        pk[D + 16 * D + p * D + d] = sw / (float)(cW[p] > 0 ? cW[p] : 1);
+      }
+    }
+    uint8_t* av = axis_valid + (int64_t)z * 24;
+    for (int p = 0; p < 8; ++p) {
+      av[p] = cT[p] > 0;
+      av[8 + p] = cH[p] > 0;
+      av[16 + p] = cW[p] > 0;
+    }
+    float* au = audio + (int64_t)z * 25;
+    {
+      float cs = 0.0f;
+      for (int lt = 0; lt < 8; ++lt) cs += aframe[lt];
+      au[0] = cs / fall;
+      for (int lt = 0; lt < 8; ++lt) au[1 + lt] = aframe[lt] / (float)(cT[lt] > 0 ? cT[lt] : 1);
+      for (int p = 0; p < 8; ++p) {
+        float sh = 0.0f, sw = 0.0f;
+        for (int lt = 0; lt < 8; ++lt) {
+          sh += arow[lt][p];
+          sw += acol[lt][p];
+        }
+        au[9 + p] = sh / (float)(cH[p] > 0 ? cH[p] : 1);
+        au[17 + p] = sw / (float)(cW[p] > 0 ? cW[p] : 1);
+      }
+    }
+  }
+  free(rowH);
+  free(colW);
+  free(frame);
+}
+
+/* -------------------------------------------------------- shape select */
+static const int SHAPES[13][3] = {
+    {4, 4, 4}, {8, 2, 4}, {8, 4, 2}, {2, 4, 8}, {2, 8, 4}, {4, 2, 8}, {4, 8, 2},
+    {2, 8, 8}, {8, 2, 8}, {8, 8, 2}, {4, 4, 8}, {4, 8, 4}, {8, 4, 4}};
+
+static int ilog2i(int x) { int r = 0; while (x > 1) { x >>= 1; ++r; } return r; }
+
+/* _axis_var, dynamic_block_shape.py:165-178 (masked branch) */
+static float axis_var(const float* A, const uint8_t* valid, int D) {
+  float n = 0.0f;
+  for (int p = 0; p < 8; ++p) n += valid[p] ? 1.0f : 0.0f;
+  if (n < 1.0f) n = 1.0f;
+  float tot = 0.0f;
+  for (int d = 0; d < D; ++d) {
+    float s = 0.0f;
+    for (int p = 0; p < 8; ++p) if (valid[p]) s += A[p * D + d];
+    float mean = s / n;
+    float q = 0.0f;
+    for (int p = 0; p < 8; ++p) if (valid[p]) { float t = A[p * D + d] - mean; q += t * t; }
+    tot += q / n;
+  }
+  return tot / (float)D;
+}
+
+/* _masked_var_1d, dynamic_block_shape.py:181-186 */
+static float masked_var8(const float* a, const uint8_t* valid) {
+  float n = 0.0f;
+  for (int p = 0; p < 8; ++p) n += valid[p] ? 1.0f : 0.0f;
+  if (n < 1.0f) n = 1.0f;
+  float s = 0.0f;
+  for (int p = 0; p < 8; ++p) if (valid[p]) s += a[p];
+  float mean = s / n;
+  float q = 0.0f;
+  for (int p = 0; p < 8; ++p) if (valid[p]) { float t = a[p] - mean; q += t * t; }
+  return q / n;
+}
+
+/* compute_effective_gradient + select_shapes_{ivpq,penalty},
+ * dynamic_block_shape.py:248-355.  method 0 = ivpq, 1 = penalty.
+ * has_audio = 0 reproduces audio_norms_thw=None (a_bar = v_hat = 0).
+ * g_out [Nz,3] and rho_out [Nz] are optional diagnostics. */
+void oracle_shape_select(const float* packed, const uint8_t* axis_valid, const float* audio,
+                         int has_audio, int Nz, int D, int method, float lambda_a,
+                         float tau_128, float lambda_128, int64_t* shape_ids,
+                         float* g_out, float* rho_out) {
+  const float EPS = 1e-6f;
+  float* rho_raw = (float*)malloc(sizeof(float) * Nz);
+  float* aniso = (float*)malloc(sizeof(float) * Nz * 3);
+  float* vhat = (float*)malloc(sizeof(float) * Nz * 3);
+  float* abar = (float*)malloc(sizeof(float) * Nz);
+  for (int z = 0; z < Nz; ++z) {
+    const float* pk = packed + (int64_t)z * 25 * D;
+    const uint8_t* av = axis_valid + (int64_t)z * 24;
+    float s = 0.0f;
+    for (int d = 0; d < D; ++d) s += pk[d];
+    float gcm = s / (float)D;
+    float sv = 0.0f;
+    for (int d = 0; d < D; ++d) { float t = pk[d] - gcm; sv += t * t; }
+    float spatial = sv / (float)D;
+    float npairs = 0.0f;
+    uint8_t both[7];
+    for (int p = 0; p < 7; ++p) { both[p] = av[p + 1] && av[p]; npairs += both[p] ? 1.0f : 0.0f; }
+    if (npairs < 1.0f) npairs = 1.0f;
+    float tv = 0.0f;
+    for (int d = 0; d < D; ++d) {
+      float a = 0.0f;
+      for (int p = 0; p < 7; ++p)
+        if (both[p]) { float t = pk[D + (p + 1) * D + d] - pk[D + p * D + d]; a += t * t; }
+      tv += a / npairs;
+    }
+    float temporal = tv / (float)D;
+    rho_raw[z] = spatial + temporal;
+    float vT = axis_var(pk + D, av, D);
+    float vH = axis_var(pk + D + 8 * D, av + 8, D);
+    float vW = axis_var(pk + D + 16 * D, av + 16, D);
+    float asum = (vT + vH) + vW;
+    if (asum < EPS) asum = EPS;
+    aniso[z * 3 + 0] = vT / asum;
+    aniso[z * 3 + 1] = vH / asum;
+    aniso[z * 3 + 2] = vW / asum;
+    if (has_audio) {
+      const float* au = audio + (int64_t)z * 25;
+      abar[z] = au[0];
+      float aT = masked_var8(au + 1, av);
+      float aH = masked_var8(au + 9, av + 8);
+      float aW = masked_var8(au + 17, av + 16);
+      float den = (aT + aH) + aW;
+      if (den < EPS) den = EPS;
+      vhat[z * 3 + 0] = aT / den;
+      vhat[z * 3 + 1] = aH / den;
+      vhat[z * 3 + 2] = aW / den;
+    } else {
+      abar[z] = 0.0f;
+      vhat[z * 3 + 0] = vhat[z * 3 + 1] = vhat[z * 3 + 2] = 0.0f;
+    }
+  }
+  float rmax = rho_raw[0], amax = abar[0];
+  for (int z = 1; z < Nz; ++z) {
+    if (rho_raw[z] > rmax) rmax = rho_raw[z];
+    if (abar[z] > amax) amax = abar[z];
+  }
+  if (rmax < EPS) rmax = EPS;
+  if (amax < EPS) amax = EPS;
+  for (int z = 0; z < Nz; ++z) {
+    float rho = rho_raw[z] / rmax;
+    float an = has_audio ? abar[z] / amax : 0.0f;
+    float la = lambda_a * an;
+    float g[3];
+    for (int d = 0; d < 3; ++d) {
+      g[d] = aniso[z * 3 + d] + la * vhat[z * 3 + d];
+      if (g[d] < 1e-4f) g[d] = 1e-4f;
+    }
+    if (g_out) { g_out[z * 3] = g[0]; g_out[z * 3 + 1] = g[1]; g_out[z * 3 + 2] = g[2]; }
+    if (rho_out) rho_out[z] = rho;
+    const int forbid128 = rho >= tau_128;
+    int best = 0;
+    float bestv = INFINITY;
+    if (method == 0) {
+      const float c23 = (float)(-2.0 / 3.0);
+      float lr[3];
+      for (int d = 0; d < 3; ++d) lr[d] = c23 * oracle_det_log2f(g[d]);
+      float sum = (lr[0] + lr[1]) + lr[2];
+      float add = (6.0f - sum) / 3.0f;
+      float li[3] = {lr[0] + add, lr[1] + add, lr[2] + add};
+      for (int c = 0; c < 13; ++c) {
+        float dist;
+        if (forbid128 && c >= 7) dist = INFINITY;
+        else {
+          float a0 = (float)ilog2i(SHAPES[c][0]) - li[0];
+          float a1 = (float)ilog2i(SHAPES[c][1]) - li[1];
+          float a2 = (float)ilog2i(SHAPES[c][2]) - li[2];
+          dist = (a0 * a0 + a1 * a1) + a2 * a2;
+        }
+        if (dist < bestv) { bestv = dist; best = c; }
+      }
+    } else {
+      float bonus = lambda_128 * (1.0f - rho);
+      for (int c = 0; c < 13; ++c) {
+        float pen;
+        if (forbid128 && c >= 7) pen = INFINITY;
+        else {
+          pen = (g[0] * (float)SHAPES[c][0] + g[1] * (float)SHAPES[c][1]) + g[2] * (float)SHAPES[c][2];
+          pen = pen - bonus * (c >= 7 ? 1.0f : 0.0f);
+        }
+        if (pen < bestv) { bestv = pen; best = c; }
+      }
+    }
+    shape_ids[z] = best;
+  }
+  free(rho_raw);
+  free(aniso);
+  free(vhat);
+  free(abar);
+}
+
+/* -------------------------------------------------------------- layout
+ * _precompute_local_orders / _build_rearrange_index / _build_block_tile_maps
+ * (dynamic_block_attention.py:21-63, 107-170).
+ * src_idx[S], inv_idx[S] (int64), block_of_tile[N_tiles], block_tiles[(N_b+1)*2]
+ * (sentinel N_tiles); returns N_b. */
+int64_t oracle_layout(const int64_t* shape_ids, int T, int H, int W, int64_t* src_idx,
+                      int64_t* inv_idx, int64_t* block_of_tile, int64_t* block_tiles) {
+  const int ZT = T / 8, ZH = H / 8, ZW = W / 8;
+  const int Nz = ZT * ZH * ZW;
+  const int64_t S = (int64_t)T * H * W;
+  const int64_t N_tiles = (int64_t)Nz * 8;
+  int order[13][512];
+  for (int c = 0; c < 13; ++c) {
+    const int bt = SHAPES[c][0], bh = SHAPES[c][1], bw = SHAPES[c][2];
+    const int bsz = bt * bh * bw, Nh = 8 / bh, Nw = 8 / bw;
+    for (int lf = 0; lf < 512; ++lf) {
+      int lt = lf / 64, lh = (lf / 8) % 8, lw = lf % 8;
+      int blk = ((lt / bt) * Nh + lh / bh) * Nw + lw / bw;
+      int off = ((lt % bt) * bh + lh % bh) * bw + lw % bw;
+      order[c][blk * bsz + off] = lf;
+    }
+  }
+  int64_t nb = 0;
+  for (int z = 0; z < Nz; ++z) {
+    const int c = (int)shape_ids[z];
+    const int zt = z / (ZH * ZW), zh = (z / ZW) % ZH, zw = z % ZW;
+    for (int r = 0; r < 512; ++r) {
+      int lf = order[c][r];
+      int lt = lf / 64, lh = (lf / 8) % 8, lw = lf % 8;
+      int64_t g = ((int64_t)(zt * 8 + lt) * H + (zh * 8 + lh)) * W + (zw * 8 + lw);
+      src_idx[(int64_t)z * 512 + r] = g;
+    }
+    const int bsz = SHAPES[c][0] * SHAPES[c][1] * SHAPES[c][2];
+    const int tpb = bsz / 64;
+    for (int tl = 0; tl < 8; ++tl) block_of_tile[(int64_t)z * 8 + tl] = nb + tl / tpb;
+    nb += 512 / bsz;
+  }
+  for (int64_t r = 0; r < S; ++r) inv_idx[src_idx[r]] = r;
+  for (int64_t b = 0; b < (nb + 1) * 2; ++b) block_tiles[b] = N_tiles;
+  for (int64_t j = 0; j < N_tiles; ++j) {
+    const int c = (int)shape_ids[j / 8];
+    const int tpb = SHAPES[c][0] * SHAPES[c][1] * SHAPES[c][2] / 64;
+    block_tiles[block_of_tile[j] * 2 + (j % 8) % tpb] = j;
+  }
+  return nb;
+}
+
+/* ---------------------------------------------------------- selection */
+typedef struct { float w; int32_t idx; } wi_t;
+static int cmp_wdesc(const void* a, const void* b) {
+  const wi_t* x = (const wi_t*)a;
+  const wi_t* y = (const wi_t*)b;
+  if (x->w > y->w) return -1;
+  if (x->w < y->w) return 1;
+  return (x->idx < y->idx) ? -1 : (x->idx > y->idx);
+}
+
+/* Pooled tile/block means (bsa_interface.py:177-201 masked branch;
+ * dynamic_block_attention.py:173-188).  x_re [heads, S, D] bf16 in tile order.
+ * tile_mean[j] = (sum_{i valid, sequential} x) / max(count, 1);
+ * block_mean[b] = ((0 + m0*c0) + m1*c1) / max(c0 + c1, 1). */
+static void pool_blocks(const uint16_t* x_re, int64_t S, int D, const uint8_t* valid_re,
+                        int64_t nb, const int64_t* block_tiles, float* out /* [nb, D] */) {
+  const int64_t N_tiles = S / 64;
+  float* tm = (float*)malloc(sizeof(float) * D);
+  for (int64_t b = 0; b < nb; ++b) {
+    float cnt = 0.0f;
+    for (int d = 0; d < D; ++d) out[b * D + d] = 0.0f;
+    for (int p = 0; p < 2; ++p) {
+      const int64_t j = block_tiles[b * 2 + p];
+      if (j >= N_tiles) continue;
+      int c = 0;
+      for (int d = 0; d < D; ++d) tm[d] = 0.0f;
+      for (int i = 0; i < 64; ++i) {
+        const int64_t s = j * 64 + i;
+        if (valid_re && !valid_re[s]) continue;
+        ++c;
+        for (int d = 0; d < D; ++d) tm[d] += bf16_to_f32(x_re[s * D + d]);
+      }
+      const float fc = (float)c;
+      const float den = c > 0 ? fc : 1.0f;
+      for (int d = 0; d < D; ++d) out[b * D + d] += (tm[d] / den) * fc;
+      cnt += fc;
+    }
+    const float den = cnt < 1.0f ? 1.0f : cnt;
+    for (int d = 0; d < D; ++d) out[b * D + d] = out[b * D + d] / den;
+  }
+  free(tm);
+}
+
+/* Block selection for one head, writing q-tile-major and k-tile-major
+ * bitmaps.  mode: 0 = top-k + cdf (get_select_indices_cdf_topk_from_score,
+ * bsa_interface.py:284-304), 1 = cdf only (:257-275), 2 = top-k only
+ * (:235-248).  Ties are broken by lower block index.
+ *
+ * Cumulative mass: cdf_m = round_f32(sum of the top-m weights) where the sum
+ * is exact in 2^-63 fixed point (torch's CPU cumsum accumulates in double and
+ * rounds each partial sum to float).  Softmax denominator: exact in 2^-50
+ * fixed point, rounded once to float.
+ *
+ * bits_q [N_tiles, WQ] u32, bits_k [N_tiles, WQ] u32 with WQ = ceil(N_tiles/32);
+ * callers zero them first.  The kept logical-block set per q block is written
+ * to sel_blocks [nb, nb] u8 if non-NULL. */
+void oracle_block_select(const uint16_t* q_re, const uint16_t* k_re, int heads, int64_t S, int D,
+                         const uint8_t* valid_re, int64_t nb, const int64_t* block_tiles,
+                         int mode, double sparsity, double cdf, uint32_t* bits_q,
+                         uint32_t* bits_k, uint8_t* sel_blocks) {
+  const int64_t N_tiles = S / 64;
+  const int64_t WQ = (N_tiles + 31) / 32;
+  const float scale = (float)(1.0 / sqrt((double)D));
+  const float pf = (float)cdf;
+  float* qc = (float*)malloc(sizeof(float) * nb * D);
+  float* kc = (float*)malloc(sizeof(float) * nb * D);
+  float* score = (float*)malloc(sizeof(float) * nb);
+  wi_t* arr = (wi_t*)malloc(sizeof(wi_t) * nb);
+  int* tile_cnt = (int*)malloc(sizeof(int) * N_tiles);
+  uint8_t* bvalid = (uint8_t*)malloc(nb);
+  for (int64_t j = 0; j < N_tiles; ++j) {
+    int c = 0;
+    for (int i = 0; i < 64; ++i) c += valid_re ? (valid_re[j * 64 + i] != 0) : 1;
+    tile_cnt[j] = c;
+  }
+  for (int64_t b = 0; b < nb; ++b) {
+    int c = 0;
+    for (int p = 0; p < 2; ++p) {
+      int64_t j = block_tiles[b * 2 + p];
+      if (j < N_tiles) c += tile_cnt[j];
+    }
+    bvalid[b] = c > 0;
+  }
+  int64_t k_topk = 0, ub = nb;
+  if (mode == 0) {
+    k_topk = (int64_t)((1.0 - sparsity) * (double)nb);
+    if (k_topk < 1) k_topk = 1;
+    int64_t u = (int64_t)(cdf * (double)nb) + 1;
+    ub = k_topk > u ? k_topk : u;
+    if (ub > nb) ub = nb;
+  } else if (mode == 1) {
+    k_topk = 1;
+    ub = (int64_t)(cdf * (double)nb) + 1;
+    if (ub > nb) ub = nb;
+  } else {
+    k_topk = (int64_t)((1.0 - sparsity) * (double)nb);
+  }
+  for (int h = 0; h < heads; ++h) {
+    pool_blocks(q_re + (int64_t)h * S * D, S, D, valid_re, nb, block_tiles, qc);
+    pool_blocks(k_re + (int64_t)h * S * D, S, D, valid_re, nb, block_tiles, kc);
+    uint32_t* bq = bits_q + (int64_t)h * N_tiles * WQ;
+    uint32_t* bk = bits_k + (int64_t)h * N_tiles * WQ;
+    for (int64_t a = 0; a < nb; ++a) {
+      for (int64_t b = 0; b < nb; ++b) {
+        if (!bvalid[b]) { score[b] = -INFINITY; continue; }
+        float acc = 0.0f;
+        for (int d = 0; d < D; ++d) acc = fmaf(qc[a * D + d], kc[b * D + d], acc);
+        score[b] = acc;
+      }
+      int64_t n_eff;
+      if (mode == 2) {
+        for (int64_t b = 0; b < nb; ++b) { arr[b].w = score[b]; arr[b].idx = (int32_t)b; }
+        qsort(arr, nb, sizeof(wi_t), cmp_wdesc);
+        n_eff = k_topk;
+      } else {
+        float mx = -INFINITY;
+        for (int64_t b = 0; b < nb; ++b) {
+          float x = score[b] * scale;
+          score[b] = x;
+          if (x > mx) mx = x;
+        }
+        uint64_t Z = 0;
+        for (int64_t b = 0; b < nb; ++b) {
+          float e = oracle_det_expf(score[b] - mx);
+          score[b] = e;
+          Z += (uint64_t)(e * 0x1p50f);
+        }
+        const float Zf = (float)Z * 0x1p-50f;
+        for (int64_t b = 0; b < nb; ++b) { arr[b].w = score[b] / Zf; arr[b].idx = (int32_t)b; }
+        qsort(arr, nb, sizeof(wi_t), cmp_wdesc);
+        uint64_t run = 0;
+        int64_t cnt_lt = 0;
+        for (int64_t m = 0; m < ub; ++m) {
+          run += (uint64_t)(arr[m].w * 0x1p63f);
+          float cf = (float)run * 0x1p-63f;
+          if (cf < pf) ++cnt_lt;
+        }
+        int64_t n = cnt_lt + 1;
+        if (n < k_topk) n = k_topk;
+        if (n > nb) n = nb;
+        n_eff = n < ub ? n : ub;
+      }
+      if (sel_blocks) memset(sel_blocks + ((int64_t)h * nb + a) * nb, 0, nb);
+      for (int64_t m = 0; m < n_eff; ++m) {
+        const int64_t b = arr[m].idx;
+        if (sel_blocks) sel_blocks[((int64_t)h * nb + a) * nb + b] = 1;
+        for (int p = 0; p < 2; ++p) {
+          const int64_t kt = block_tiles[b * 2 + p];
+          if (kt >= N_tiles || tile_cnt[kt] == 0) continue;
+          for (int pq = 0; pq < 2; ++pq) {
+            const int64_t qt = block_tiles[a * 2 + pq];
+            if (qt >= N_tiles) continue;
+            bq[qt * WQ + kt / 32] |= 1u << (kt % 32);
+            bk[kt * WQ + qt / 32] |= 1u << (qt % 32);
+          }
+        }
+      }
+    }
+  }
+  free(qc);
+  free(kc);
+  free(score);
+  free(arr);
+  free(tile_cnt);
+  free(bvalid);
+}

@@ -1,0 +1,18 @@
+"""prism_b200 -- B200-native (sm_100a) dynamic block-shape block-sparse
+attention for Tencent-Hunyuan/Prism's video self-attention.
+
+Public entry points mirror the reference names:
+  flash_attn_bsa_3d_dynamic   hymm/models/modules/block_sparse_attention/dynamic_block_attention.py:194
+  run_bsa_dynamic             SelfAttention._run_bsa_dynamic, wan_video_dit.py:342
+  select_zone_shapes          block_sparse_attention/dynamic_block_shape.py:358
+  all_to_all_4D / all_gather  hymm/utils/communications.py:277, 401
+The kernels live in libprism_bsa.so (C ABI: include/prism_bsa.h).
+"""
+from .dynamic_block_attention import build_plan, flash_attn_bsa_3d_dynamic, run_bsa_dynamic  # noqa: F401
+from .dynamic_block_shape import (  # noqa: F401
+    ALL_CANDIDATE_SHAPES, CANDIDATE_SHAPES_64, CANDIDATE_SHAPES_128, NUM_CANDIDATES,
+    NUM_CANDIDATES_64, ZONE_SIZE, compute_effective_gradient, select_zone_shapes,
+)
+from .ops import token_norms  # noqa: F401
+
+__version__ = "0.1.0"

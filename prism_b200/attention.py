@@ -1,0 +1,103 @@
+"""Video self-attention core with Ulysses sequence parallelism.
+
+``dynamic_self_attention`` is the part of ``SelfAttention.forward``
+(hymm/models/modules/wan_video_dit.py:689-841) between the q/k/v projections
+(+ RMSNorm + RoPE, done by the caller) and the output projection ``self.o``,
+for the dynamic block-shape path:
+
+* audio token norms from the a2v bridge residual, all-gathered over SP
+  (:739-757);
+* head padding + sequence->heads all-to-all of q, k, v (:764-787);
+* dynamic block-sparse attention on the local heads (:795-812 ->
+  ``_run_bsa_dynamic``), reading the all-to-all output in its [B, S, H, D]
+  layout directly (the reference's permute().contiguous() copies are fused
+  into the gather kernel);
+* padding-only ranks stay connected to the graph (:814-823);
+* heads->sequence all-to-all of the output and head truncation (:824-828).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import ops
+from .communications import (all_gather, all_to_all_4D, sp_num_local_real_heads,
+                             sp_pad_heads, sp_pad_num_heads)
+from .dynamic_block_attention import run_bsa_dynamic
+from .parallel_states import get_sequence_parallel_state, nccl_info
+
+
+def audio_token_norms(a2v_bridge_residual: Optional[torch.Tensor], full_seq_len: Optional[int] = None):
+    """||a2v[m]||_2 per token (bf16), all-gathered over SP (wan_video_dit.py:739-752)."""
+    if a2v_bridge_residual is None:
+        return None
+    with torch.no_grad():
+        local = ops.token_norms(a2v_bridge_residual)  # [B, S_local]
+        if get_sequence_parallel_state():
+            full = all_gather(local.unsqueeze(-1), dim=1, group=nccl_info.sp_group,
+                              full_seq_len=full_seq_len)
+            return full.squeeze(-1)[0]
+        return local[0]
+
+
+def dynamic_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           grid_size: Tuple[int, int, int], num_heads: int, *,
+                           a2v_bridge_residual: Optional[torch.Tensor] = None,
+                           full_seq_len: Optional[int] = None, method: str = "ivpq",
+                           sparsity: Optional[float] = 0.9375,
+                           cdf_threshold: Optional[float] = None, lambda_a: float = 0.5,
+                           tau_128: float = 0.15, lambda_128: float = 1.0,
+                           shape_ids: Optional[torch.Tensor] = None,
+                           return_shape_ids: bool = False):
+    """q, k, v: [B=1, S_local, num_heads*D] (projected, normed, rotated).
+    Returns x [B, S_local, num_heads*D] (input of the output projection)."""
+    b, s_local, hd = q.shape
+    D = hd // num_heads
+    norms = audio_token_norms(a2v_bridge_residual, full_seq_len)
+    kw = dict(method=method, sparsity=sparsity, cdf_threshold=cdf_threshold, lambda_a=lambda_a,
+              tau_128=tau_128, lambda_128=lambda_128, shape_ids=shape_ids, return_shape_ids=True,
+              audio_token_norms=norms, layout="bshd")
+    q4, k4, v4 = (t.view(b, s_local, num_heads, D) for t in (q, k, v))
+    used = shape_ids
+    if get_sequence_parallel_state():
+        P = nccl_info.sp_size
+        rank = nccl_info.rank_within_spgroup
+        padded = sp_pad_num_heads(num_heads, P)
+        if padded != num_heads:
+            q4, k4, v4 = (sp_pad_heads(t, padded) for t in (q4, k4, v4))
+        group = nccl_info.sp_group
+        q4 = all_to_all_4D(q4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
+        k4 = all_to_all_4D(k4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
+        v4 = all_to_all_4D(v4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
+        hpr = q4.shape[2]
+        local = sp_num_local_real_heads(num_heads, padded, P, rank)
+        if local > 0:
+            if local != hpr:
+                q4, k4, v4 = q4[:, :, :local], k4[:, :, :local], v4[:, :, :local]
+            x, used = run_bsa_dynamic(q4, k4, v4, grid_size, **kw)
+            if x.shape[2] != hpr:
+                x = sp_pad_heads(x, hpr)
+        else:
+            # padding-only rank: keep the graph connected so the backward
+            # all-to-alls fire symmetrically on every rank (wan_video_dit.py:814-823).
+            # The zone statistics all-reduce must still be joined.
+            from .dynamic_block_shape import _maybe_sp_average
+            Tp, Hp, Wp = ops.padded_grid(grid_size)
+            Nz = (Tp // 8) * (Hp // 8) * (Wp // 8)
+            if shape_ids is None:
+                _maybe_sp_average(torch.zeros(Nz, 25 * D, device=q.device))
+            x = (q4 + k4 + v4) * 0.0
+        x = all_to_all_4D(x, group, scatter_dim=1, gather_dim=2, full_seq_len=full_seq_len)
+        if padded != num_heads:
+            x = x[:, :, :num_heads]
+        x = x.flatten(2)
+    else:
+        x, used = run_bsa_dynamic(q4, k4, v4, grid_size, **kw)
+        x = x.flatten(2)
+    if return_shape_ids:
+        return x, used
+    return x
+
+
+__all__ = ["dynamic_self_attention", "audio_token_norms"]

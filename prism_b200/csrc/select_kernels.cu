@@ -1,0 +1,1166 @@
+// Selection side of the dynamic block-sparse attention path: audio token norms,
+// zone statistics, per-zone shape choice, permutation / tile maps, row gather
+// and scatter, pooled block scoring and hybrid top-k + cumulative-mass
+// selection into q-major / k-major tile bitmaps.
+//
+// Compiled with -fmad=false: every floating-point step is one IEEE operation in
+// a fixed order, so results are bit-identical to the CPU restatement in
+// oracle/prism_oracle.c and to themselves run after run (the reference
+// recomputes the selection under activation checkpointing,
+// dynamic_block_attention.py:256-319, so it must be deterministic).
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdarg.h>
+#include <stdint.h>
+
+#include "prism_common.cuh"
+
+namespace prism {
+
+static thread_local char g_err[512] = "";
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+const char* last_error() { return g_err; }
+
+// ===================================================================== a2
+// One warp per token.  Lane l owns 8-element chunks l, l+32, ...; within a
+// chunk acc = fma(x, x, acc) in element order; then an xor butterfly.
+__global__ void token_norms_kernel(const uint16_t* __restrict__ x, int64_t n, int dim,
+                                   __nv_bfloat16* __restrict__ out) {
+  const int64_t tok = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (tok >= n) return;
+  const uint4* row = reinterpret_cast<const uint4*>(x + tok * (int64_t)dim);
+  const int nchunks = dim >> 3;
+  float acc = 0.0f;
+  for (int c = lane; c < nchunks; c += 32) {
+    uint4 u = __ldg(row + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float lo = __uint_as_float(w[j] << 16);
+      float hi = __uint_as_float(w[j] & 0xffff0000u);
+      acc = __fmaf_rn(lo, lo, acc);
+      acc = __fmaf_rn(hi, hi, acc);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  if (lane == 0) out[tok] = __float2bfloat16_rn(__fsqrt_rn(acc));
+}
+
+// ============================================================ a4/a5/a6
+// Stage 1: one CTA per (zone, local frame lt); thread i owns channels 2i, 2i+1.
+// Partial layout per (zone, lt): [17][D] = frame | rowH[8] | colW[8]; audio
+// partial [17] the same for the scalar norm.
+constexpr int kPart = 17;
+
+__device__ __forceinline__ bool token_valid(int t, int h, int w, int T, int H, int W, int Hp,
+                                            int Wp, const uint8_t* __restrict__ valid,
+                                            int64_t& src) {
+  if (t >= T || h >= H || w >= W) return false;
+  if (valid != nullptr && !valid[((int64_t)t * Hp + h) * Wp + w]) return false;
+  src = ((int64_t)t * H + h) * W + w;
+  return true;
+}
+
+__global__ void zone_partial_kernel(const uint16_t* __restrict__ v, int heads, int64_t sh,
+                                    int64_t ss, int T, int H, int W, int Hp, int Wp, int D,
+                                    const uint8_t* __restrict__ valid,
+                                    const uint16_t* __restrict__ norms, float* __restrict__ part,
+                                    float* __restrict__ apart) {
+  const int ZH = Hp / 8, ZW = Wp / 8;
+  const int z = blockIdx.x >> 3, lt = blockIdx.x & 7;
+  const int zt = z / (ZH * ZW), zh = (z / ZW) % ZH, zw = z % ZW;
+  const int t = zt * 8 + lt;
+  const int c0 = 2 * threadIdx.x;
+  float* P = part + (int64_t)blockIdx.x * kPart * D;
+  const float fheads = (float)heads;
+  float cw0[8], cw1[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) cw0[i] = cw1[i] = 0.0f;
+  float fr0 = 0.0f, fr1 = 0.0f;
+  for (int lh = 0; lh < 8; ++lh) {
+    float rh0 = 0.0f, rh1 = 0.0f;
+#pragma unroll
+    for (int lw = 0; lw < 8; ++lw) {
+      int64_t s;
+      if (!token_valid(t, zh * 8 + lh, zw * 8 + lw, T, H, W, Hp, Wp, valid, s)) continue;
+      const uint16_t* base = v + s * ss + c0;
+      float a0 = 0.0f, a1 = 0.0f;
+      int hh = 0;
+      for (; hh + 4 <= heads; hh += 4) {
+        uint32_t u0 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 0) * sh));
+        uint32_t u1 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 1) * sh));
+        uint32_t u2 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 2) * sh));
+        uint32_t u3 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 3) * sh));
+        a0 = __fadd_rn(a0, __uint_as_float(u0 << 16));
+        a1 = __fadd_rn(a1, __uint_as_float(u0 & 0xffff0000u));
+        a0 = __fadd_rn(a0, __uint_as_float(u1 << 16));
+        a1 = __fadd_rn(a1, __uint_as_float(u1 & 0xffff0000u));
+        a0 = __fadd_rn(a0, __uint_as_float(u2 << 16));
+        a1 = __fadd_rn(a1, __uint_as_float(u2 & 0xffff0000u));
+        a0 = __fadd_rn(a0, __uint_as_float(u3 << 16));
+        a1 = __fadd_rn(a1, __uint_as_float(u3 & 0xffff0000u));
+      }
+      for (; hh < heads; ++hh) {
+        uint32_t u0 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)hh * sh));
+        a0 = __fadd_rn(a0, __uint_as_float(u0 << 16));
+        a1 = __fadd_rn(a1, __uint_as_float(u0 & 0xffff0000u));
+      }
+      const float x0 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a0, fheads)));
+      const float x1 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a1, fheads)));
+      rh0 = __fadd_rn(rh0, x0);
+      rh1 = __fadd_rn(rh1, x1);
+      cw0[lw] = __fadd_rn(cw0[lw], x0);
+      cw1[lw] = __fadd_rn(cw1[lw], x1);
+    }
+    P[(1 + lh) * D + c0] = rh0;
+    P[(1 + lh) * D + c0 + 1] = rh1;
+    fr0 = __fadd_rn(fr0, rh0);
+    fr1 = __fadd_rn(fr1, rh1);
+  }
+  P[c0] = fr0;
+  P[c0 + 1] = fr1;
+#pragma unroll
+  for (int lw = 0; lw < 8; ++lw) {
+    P[(9 + lw) * D + c0] = cw0[lw];
+    P[(9 + lw) * D + c0 + 1] = cw1[lw];
+  }
+  if (threadIdx.x == 0) {
+    float* A = apart + (int64_t)blockIdx.x * kPart;
+    float cw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float fr = 0.0f;
+    for (int lh = 0; lh < 8; ++lh) {
+      float rh = 0.0f;
+      for (int lw = 0; lw < 8; ++lw) {
+        int64_t s;
+        if (!token_valid(t, zh * 8 + lh, zw * 8 + lw, T, H, W, Hp, Wp, valid, s)) continue;
+        const float x = norms != nullptr ? bfbits2f(norms[s]) : 0.0f;
+        rh = __fadd_rn(rh, x);
+        cw[lw] = __fadd_rn(cw[lw], x);
+      }
+      A[1 + lh] = rh;
+      fr = __fadd_rn(fr, rh);
+    }
+    A[0] = fr;
+    for (int lw = 0; lw < 8; ++lw) A[9 + lw] = cw[lw];
+  }
+}
+
+// Stage 2: one CTA per zone; combine the eight frames in order lt = 0..7.
+__global__ void zone_combine_kernel(const float* __restrict__ part, const float* __restrict__ apart,
+                                    int T, int H, int W, int Hp, int Wp, int D,
+                                    const uint8_t* __restrict__ valid,
+                                    float* __restrict__ packed, uint8_t* __restrict__ axis_valid,
+                                    float* __restrict__ audio) {
+  const int ZH = Hp / 8, ZW = Wp / 8;
+  const int z = blockIdx.x;
+  const int zt = z / (ZH * ZW), zh = (z / ZW) % ZH, zw = z % ZW;
+  __shared__ int cT[8], cH[8], cW[8], call;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) cT[i] = cH[i] = cW[i] = 0;
+    call = 0;
+    for (int lt = 0; lt < 8; ++lt)
+      for (int lh = 0; lh < 8; ++lh)
+        for (int lw = 0; lw < 8; ++lw) {
+          int64_t s;
+          if (!token_valid(zt * 8 + lt, zh * 8 + lh, zw * 8 + lw, T, H, W, Hp, Wp, valid, s)) continue;
+          cT[lt]++;
+          cH[lh]++;
+          cW[lw]++;
+          call++;
+        }
+  }
+  __syncthreads();
+  const float* Pz = part + (int64_t)z * 8 * kPart * D;
+  float* pk = packed + (int64_t)z * 25 * D;
+  const float fall = (float)(call > 0 ? call : 1);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float cs = 0.0f;
+    for (int lt = 0; lt < 8; ++lt) cs = __fadd_rn(cs, Pz[(lt * kPart) * D + d]);
+    pk[d] = __fdiv_rn(cs, fall);
+    for (int lt = 0; lt < 8; ++lt)
+      pk[D + lt * D + d] = __fdiv_rn(Pz[(lt * kPart) * D + d], (float)(cT[lt] > 0 ? cT[lt] : 1));
+    for (int p = 0; p < 8; ++p) {
+      float sh = 0.0f, sw = 0.0f;
+      for (int lt = 0; lt < 8; ++lt) {
+        sh = __fadd_rn(sh, Pz[(lt * kPart + 1 + p) * D + d]);
+        sw = __fadd_rn(sw, Pz[(lt * kPart + 9 + p) * D + d]);
+      }
+      pk[D + 8 * D + p * D + d] = __fdiv_rn(sh, (float)(cH[p] > 0 ? cH[p] : 1));
+      pk[D + 16 * D + p * D + d] = __fdiv_rn(sw, (float)(cW[p] > 0 ? cW[p] : 1));
+    }
+  }
+  if (threadIdx.x == 0) {
+    uint8_t* av = axis_valid + (int64_t)z * 24;
+    for (int p = 0; p < 8; ++p) {
+      av[p] = cT[p] > 0;
+      av[8 + p] = cH[p] > 0;
+      av[16 + p] = cW[p] > 0;
+    }
+    const float* Az = apart + (int64_t)z * 8 * kPart;
+    float* au = audio + (int64_t)z * 25;
+    float cs = 0.0f;
+    for (int lt = 0; lt < 8; ++lt) cs = __fadd_rn(cs, Az[lt * kPart]);
+    au[0] = __fdiv_rn(cs, fall);
+    for (int lt = 0; lt < 8; ++lt)
+      au[1 + lt] = __fdiv_rn(Az[lt * kPart], (float)(cT[lt] > 0 ? cT[lt] : 1));
+    for (int p = 0; p < 8; ++p) {
+      float sh = 0.0f, sw = 0.0f;
+      for (int lt = 0; lt < 8; ++lt) {
+        sh = __fadd_rn(sh, Az[lt * kPart + 1 + p]);
+        sw = __fadd_rn(sw, Az[lt * kPart + 9 + p]);
+      }
+      au[9 + p] = __fdiv_rn(sh, (float)(cH[p] > 0 ? cH[p] : 1));
+      au[17 + p] = __fdiv_rn(sw, (float)(cW[p] > 0 ? cW[p] : 1));
+    }
+  }
+}
+
+// ================================================================ a4/a6/a7
+__device__ float axis_var_dev(const float* A, const uint8_t* valid, int D) {
+  float n = 0.0f;
+  for (int p = 0; p < 8; ++p) n = __fadd_rn(n, valid[p] ? 1.0f : 0.0f);
+  if (n < 1.0f) n = 1.0f;
+  float tot = 0.0f;
+  for (int d = 0; d < D; ++d) {
+    float s = 0.0f;
+    for (int p = 0; p < 8; ++p)
+      if (valid[p]) s = __fadd_rn(s, A[p * D + d]);
+    const float mean = __fdiv_rn(s, n);
+    float q = 0.0f;
+    for (int p = 0; p < 8; ++p)
+      if (valid[p]) {
+        const float t = __fsub_rn(A[p * D + d], mean);
+        q = __fadd_rn(q, __fmul_rn(t, t));
+      }
+    tot = __fadd_rn(tot, __fdiv_rn(q, n));
+  }
+  return __fdiv_rn(tot, (float)D);
+}
+
+__device__ float masked_var8_dev(const float* a, const uint8_t* valid) {
+  float n = 0.0f;
+  for (int p = 0; p < 8; ++p) n = __fadd_rn(n, valid[p] ? 1.0f : 0.0f);
+  if (n < 1.0f) n = 1.0f;
+  float s = 0.0f;
+  for (int p = 0; p < 8; ++p)
+    if (valid[p]) s = __fadd_rn(s, a[p]);
+  const float mean = __fdiv_rn(s, n);
+  float q = 0.0f;
+  for (int p = 0; p < 8; ++p)
+    if (valid[p]) {
+      const float t = __fsub_rn(a[p], mean);
+      q = __fadd_rn(q, __fmul_rn(t, t));
+    }
+  return __fdiv_rn(q, n);
+}
+
+__device__ float block_max_f(float v, float* red) {
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < nw ? red[l] : -INFINITY;
+    for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  v = red[0];
+  __syncthreads();
+  return v;
+}
+
+// One CTA; one thread per zone (strided).  Per-zone intermediates in shared
+// memory: rho_raw, aniso[3], abar, vhat[3].
+__global__ void shape_select_kernel(const float* __restrict__ packed,
+                                    const uint8_t* __restrict__ axis_valid,
+                                    const float* __restrict__ audio, int has_audio, int Nz, int D,
+                                    int method, float lambda_a, float tau_128, float lambda_128,
+                                    int64_t* __restrict__ shape_ids, float* __restrict__ g_out,
+                                    float* __restrict__ rho_out) {
+  extern __shared__ float zsm[];
+  float* rho_raw = zsm;
+  float* aniso = zsm + Nz;
+  float* vhat = zsm + 4 * Nz;
+  float* abar = zsm + 7 * Nz;
+  __shared__ float red[32];
+  const float EPS = 1e-6f;
+  float lmax_r = -INFINITY, lmax_a = -INFINITY;
+  for (int z = threadIdx.x; z < Nz; z += blockDim.x) {
+    const float* pk = packed + (int64_t)z * 25 * D;
+    const uint8_t* av = axis_valid + (int64_t)z * 24;
+    float s = 0.0f;
+    for (int d = 0; d < D; ++d) s = __fadd_rn(s, pk[d]);
+    const float gcm = __fdiv_rn(s, (float)D);
+    float sv = 0.0f;
+    for (int d = 0; d < D; ++d) {
+      const float t = __fsub_rn(pk[d], gcm);
+      sv = __fadd_rn(sv, __fmul_rn(t, t));
+    }
+    const float spatial = __fdiv_rn(sv, (float)D);
+    float npairs = 0.0f;
+    uint8_t both[7];
+    for (int p = 0; p < 7; ++p) {
+      both[p] = av[p + 1] && av[p];
+      npairs = __fadd_rn(npairs, both[p] ? 1.0f : 0.0f);
+    }
+    if (npairs < 1.0f) npairs = 1.0f;
+    float tv = 0.0f;
+    for (int d = 0; d < D; ++d) {
+      float a = 0.0f;
+      for (int p = 0; p < 7; ++p)
+        if (both[p]) {
+          const float t = __fsub_rn(pk[D + (p + 1) * D + d], pk[D + p * D + d]);
+          a = __fadd_rn(a, __fmul_rn(t, t));
+        }
+      tv = __fadd_rn(tv, __fdiv_rn(a, npairs));
+    }
+    const float temporal = __fdiv_rn(tv, (float)D);
+    rho_raw[z] = __fadd_rn(spatial, temporal);
+    const float vT = axis_var_dev(pk + D, av, D);
+    const float vH = axis_var_dev(pk + D + 8 * D, av + 8, D);
+    const float vW = axis_var_dev(pk + D + 16 * D, av + 16, D);
+    float asum = __fadd_rn(__fadd_rn(vT, vH), vW);
+    if (asum < EPS) asum = EPS;
+    aniso[3 * z + 0] = __fdiv_rn(vT, asum);
+    aniso[3 * z + 1] = __fdiv_rn(vH, asum);
+    aniso[3 * z + 2] = __fdiv_rn(vW, asum);
+    if (has_audio) {
+      const float* au = audio + (int64_t)z * 25;
+      abar[z] = au[0];
+      const float aT = masked_var8_dev(au + 1, av);
+      const float aH = masked_var8_dev(au + 9, av + 8);
+      const float aW = masked_var8_dev(au + 17, av + 16);
+      float den = __fadd_rn(__fadd_rn(aT, aH), aW);
+      if (den < EPS) den = EPS;
+      vhat[3 * z + 0] = __fdiv_rn(aT, den);
+      vhat[3 * z + 1] = __fdiv_rn(aH, den);
+      vhat[3 * z + 2] = __fdiv_rn(aW, den);
+    } else {
+      abar[z] = 0.0f;
+      vhat[3 * z + 0] = vhat[3 * z + 1] = vhat[3 * z + 2] = 0.0f;
+    }
+    lmax_r = fmaxf(lmax_r, rho_raw[z]);
+    lmax_a = fmaxf(lmax_a, abar[z]);
+  }
+  float rmax = block_max_f(lmax_r, red);
+  float amax = block_max_f(lmax_a, red);
+  if (rmax < EPS) rmax = EPS;
+  if (amax < EPS) amax = EPS;
+  for (int z = threadIdx.x; z < Nz; z += blockDim.x) {
+    const float rho = __fdiv_rn(rho_raw[z], rmax);
+    const float an = has_audio ? __fdiv_rn(abar[z], amax) : 0.0f;
+    const float la = __fmul_rn(lambda_a, an);
+    float g[3];
+    for (int d = 0; d < 3; ++d) {
+      g[d] = __fadd_rn(aniso[3 * z + d], __fmul_rn(la, vhat[3 * z + d]));
+      if (g[d] < 1e-4f) g[d] = 1e-4f;
+    }
+    if (g_out) {
+      g_out[3 * z] = g[0];
+      g_out[3 * z + 1] = g[1];
+      g_out[3 * z + 2] = g[2];
+    }
+    if (rho_out) rho_out[z] = rho;
+    const bool forbid128 = rho >= tau_128;
+    int best = 0;
+    float bestv = INFINITY;
+    if (method == 0) {
+      const float c23 = (float)(-2.0 / 3.0);
+      float lr[3];
+      for (int d = 0; d < 3; ++d) lr[d] = __fmul_rn(c23, det_log2f(g[d]));
+      const float sum = __fadd_rn(__fadd_rn(lr[0], lr[1]), lr[2]);
+      const float add = __fdiv_rn(__fsub_rn(6.0f, sum), 3.0f);
+      const float li0 = __fadd_rn(lr[0], add), li1 = __fadd_rn(lr[1], add), li2 = __fadd_rn(lr[2], add);
+      for (int c = 0; c < kNumShapes; ++c) {
+        float dist;
+        if (forbid128 && c >= kNumShapes64) {
+          dist = INFINITY;
+        } else {
+          const float a0 = __fsub_rn((float)(31 - __clz(shape_dim(c, 0))), li0);
+          const float a1 = __fsub_rn((float)(31 - __clz(shape_dim(c, 1))), li1);
+          const float a2 = __fsub_rn((float)(31 - __clz(shape_dim(c, 2))), li2);
+          dist = __fadd_rn(__fadd_rn(__fmul_rn(a0, a0), __fmul_rn(a1, a1)), __fmul_rn(a2, a2));
+        }
+        if (dist < bestv) {
+          bestv = dist;
+          best = c;
+        }
+      }
+    } else {
+      const float bonus = __fmul_rn(lambda_128, __fsub_rn(1.0f, rho));
+      for (int c = 0; c < kNumShapes; ++c) {
+        float pen;
+        if (forbid128 && c >= kNumShapes64) {
+          pen = INFINITY;
+        } else {
+          pen = __fadd_rn(__fadd_rn(__fmul_rn(g[0], (float)shape_dim(c, 0)),
+                                    __fmul_rn(g[1], (float)shape_dim(c, 1))),
+                          __fmul_rn(g[2], (float)shape_dim(c, 2)));
+          pen = __fsub_rn(pen, __fmul_rn(bonus, c >= kNumShapes64 ? 1.0f : 0.0f));
+        }
+        if (pen < bestv) {
+          bestv = pen;
+          best = c;
+        }
+      }
+    }
+    shape_ids[z] = best;
+  }
+}
+
+// ================================================================ a8/a9
+// Rearranged row r of zone z (shape c) -> local flat lt*64 + lh*8 + lw.
+// Inverse of dynamic_block_attention.py:41-51: r = blk*bsz + off with
+// blk = (nt*Nh + nh)*Nw + nw, off = (it*bh + ih)*bw + iw.
+__device__ __forceinline__ void local_coords(int c, int r, int& lt, int& lh, int& lw) {
+  const int bt = shape_dim(c, 0), bh = shape_dim(c, 1), bw = shape_dim(c, 2);
+  const int bsz = bt * bh * bw;
+  const int Nh = 8 / bh, Nw = 8 / bw;
+  const int blk = r / bsz, off = r % bsz;
+  const int it = off / (bh * bw), ih = (off / bw) % bh, iw = off % bw;
+  const int nt = blk / (Nh * Nw), nh = (blk / Nw) % Nh, nw = blk % Nw;
+  lt = nt * bt + it;
+  lh = nh * bh + ih;
+  lw = nw * bw + iw;
+}
+
+// One CTA of 1024 threads: exclusive scan of blocks-per-zone, then tile maps.
+__global__ void block_map_kernel(const int64_t* __restrict__ shape_ids, int Nz,
+                                 int32_t* __restrict__ block_of_tile,
+                                 int32_t* __restrict__ block_tiles, int32_t* __restrict__ n_blocks) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  const int n_tiles = Nz * 8;
+  if (threadIdx.x == 0) carry = 0;
+  // sentinel fill of every block row first
+  for (int i = threadIdx.x; i < (n_tiles + 1) * 2; i += blockDim.x) block_tiles[i] = n_tiles;
+  __syncthreads();
+  for (int base = 0; base < Nz; base += blockDim.x) {
+    const int z = base + threadIdx.x;
+    int c = 0, nbz = 0;
+    if (z < Nz) {
+      c = (int)shape_ids[z];
+      nbz = 512 / shape_tokens(c);
+    }
+    // block-wide exclusive scan of nbz
+    int v = nbz;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int o = 1; o < 32; o <<= 1) {
+      int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_sums[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      int s = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        int n = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += n;
+      }
+      warp_sums[lane] = s;  // inclusive
+    }
+    __syncthreads();
+    const int excl = carry + (w > 0 ? warp_sums[w - 1] : 0) + v - nbz;
+    if (z < Nz) {
+      const int tpb = shape_tokens(c) / 64;
+      for (int tl = 0; tl < 8; ++tl) {
+        const int j = z * 8 + tl;
+        const int b = excl + tl / tpb;
+        block_of_tile[j] = b;
+        block_tiles[b * 2 + tl % tpb] = j;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) carry += warp_sums[(blockDim.x >> 5) - 1];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *n_blocks = carry;
+}
+
+__global__ void perm_kernel(const int64_t* __restrict__ shape_ids, int Hp, int Wp, int64_t S,
+                            int32_t* __restrict__ src_idx, int32_t* __restrict__ inv_idx) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= S) return;
+  const int ZH = Hp / 8, ZW = Wp / 8;
+  const int z = (int)(r >> 9), rr = (int)(r & 511);
+  const int zt = z / (ZH * ZW), zh = (z / ZW) % ZH, zw = z % ZW;
+  int lt, lh, lw;
+  local_coords((int)shape_ids[z], rr, lt, lh, lw);
+  const int64_t g = ((int64_t)(zt * 8 + lt) * Hp + (zh * 8 + lh)) * Wp + (zw * 8 + lw);
+  src_idx[r] = (int32_t)g;
+  inv_idx[g] = (int32_t)r;
+}
+
+// One warp per tile.
+__device__ __forceinline__ bool padded_valid(int64_t g, int T, int H, int W, int Hp, int Wp,
+                                             const uint8_t* __restrict__ valid) {
+  const int t = (int)(g / ((int64_t)Hp * Wp));
+  const int h = (int)((g / Wp) % Hp);
+  const int w = (int)(g % Wp);
+  if (t >= T || h >= H || w >= W) return false;
+  return valid == nullptr || valid[g] != 0;
+}
+
+__global__ void tile_valid_kernel(const int32_t* __restrict__ src_idx,
+                                  const uint8_t* __restrict__ valid, int64_t n_tiles, int T, int H,
+                                  int W, int Hp, int Wp, uint64_t* __restrict__ tile_bits,
+                                  int32_t* __restrict__ tile_count) {
+  const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (j >= n_tiles) return;
+  const bool v0 = padded_valid(src_idx[j * 64 + lane], T, H, W, Hp, Wp, valid);
+  const bool v1 = padded_valid(src_idx[j * 64 + 32 + lane], T, H, W, Hp, Wp, valid);
+  const uint32_t b0 = __ballot_sync(0xffffffffu, v0);
+  const uint32_t b1 = __ballot_sync(0xffffffffu, v1);
+  if (lane == 0) {
+    tile_bits[j] = (uint64_t)b0 | ((uint64_t)b1 << 32);
+    tile_count[j] = __popc(b0) + __popc(b1);
+  }
+}
+
+// ================================================================ a10/a17
+// 16-byte chunks; rows of D bf16.
+__global__ void gather_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int64_t xss, int heads,
+                                   int chunks, int T, int H, int W, int Hp, int Wp, int64_t Sp,
+                                   const int32_t* __restrict__ src_idx, uint4* __restrict__ out,
+                                   int64_t osh) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)heads * Sp * chunks;
+  if (i >= total) return;
+  const int c = (int)(i % chunks);
+  const int64_t r = (i / chunks) % Sp;
+  const int h = (int)(i / ((int64_t)chunks * Sp));
+  const int64_t g = src_idx[r];
+  const int t = (int)(g / ((int64_t)Hp * Wp));
+  const int hh = (int)((g / Wp) % Hp);
+  const int w = (int)(g % Wp);
+  uint4 val = make_uint4(0, 0, 0, 0);
+  if (t < T && hh < H && w < W) {
+    const int64_t s = ((int64_t)t * H + hh) * W + w;
+    val = __ldg(x + ((int64_t)h * xsh + s * xss) / 8 + c);
+  }
+  out[((int64_t)h * osh + r * chunks * 8) / 8 + c] = val;
+}
+
+__global__ void scatter_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int heads, int chunks,
+                                    int T, int H, int W, int Hp, int Wp,
+                                    const int32_t* __restrict__ inv_idx, uint4* __restrict__ out,
+                                    int64_t osh, int64_t oss) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t S = (int64_t)T * H * W;
+  const int64_t total = (int64_t)heads * S * chunks;
+  if (i >= total) return;
+  const int c = (int)(i % chunks);
+  const int64_t s = (i / chunks) % S;
+  const int h = (int)(i / ((int64_t)chunks * S));
+  const int t = (int)(s / ((int64_t)H * W));
+  const int hh = (int)((s / W) % H);
+  const int w = (int)(s % W);
+  const int64_t g = ((int64_t)t * Hp + hh) * Wp + w;
+  const int64_t r = inv_idx[g];
+  out[((int64_t)h * osh + s * oss) / 8 + c] = __ldg(x + ((int64_t)h * xsh + r * chunks * 8) / 8 + c);
+}
+
+// ================================================================ a11
+// One CTA per (block b, head h), D threads.  tile mean = sequential masked sum
+// over the 64 rows / max(count, 1); block mean = ((0 + m0*c0) + m1*c1) / max(c, 1).
+__global__ void pool_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, int64_t S,
+                            int D, const int32_t* __restrict__ block_tiles,
+                            const int32_t* __restrict__ n_blocks,
+                            const uint64_t* __restrict__ tile_bits, float* __restrict__ qc,
+                            float* __restrict__ kc, uint8_t* __restrict__ bvalid, int nb_max) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  if (b >= *n_blocks) return;
+  const int64_t n_tiles = S / 64;
+  const int d = threadIdx.x;
+  float oq = 0.0f, ok = 0.0f, cnt = 0.0f;
+  for (int p = 0; p < 2; ++p) {
+    const int j = block_tiles[2 * b + p];
+    if (j >= n_tiles) continue;
+    const uint64_t bits = tile_bits[j];
+    const int c = __popcll(bits);
+    const uint16_t* qr = q + ((int64_t)h * S + (int64_t)j * 64) * D + d;
+    const uint16_t* kr = k + ((int64_t)h * S + (int64_t)j * 64) * D + d;
+    float sq = 0.0f, sk = 0.0f;
+    for (int i = 0; i < 64; ++i) {
+      if (!((bits >> i) & 1ull)) continue;
+      sq = __fadd_rn(sq, bfbits2f(qr[(int64_t)i * D]));
+      sk = __fadd_rn(sk, bfbits2f(kr[(int64_t)i * D]));
+    }
+    const float fc = (float)c;
+    const float den = c > 0 ? fc : 1.0f;
+    oq = __fadd_rn(oq, __fmul_rn(__fdiv_rn(sq, den), fc));
+    ok = __fadd_rn(ok, __fmul_rn(__fdiv_rn(sk, den), fc));
+    cnt = __fadd_rn(cnt, fc);
+  }
+  const float den = cnt < 1.0f ? 1.0f : cnt;
+  qc[((int64_t)h * nb_max + b) * D + d] = __fdiv_rn(oq, den);
+  kc[((int64_t)h * nb_max + b) * D + d] = __fdiv_rn(ok, den);
+  if (h == 0 && d == 0) bvalid[b] = cnt > 0.0f;
+}
+
+// ================================================================ a12
+// Register-tiled fp32 GEMM: score[a][b] = fma-chain over d = 0..D-1 of
+// qc[a][d] * kc[b][d] (each accumulator updated once per d, in order).
+constexpr int kScoreTile = 64;
+__global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc,
+                                                    const float* __restrict__ kc, int D,
+                                                    const int32_t* __restrict__ n_blocks,
+                                                    int nb_max, float* __restrict__ score) {
+  extern __shared__ float ssm[];
+  const int nb = *n_blocks;
+  const int a0 = blockIdx.y * kScoreTile, b0 = blockIdx.x * kScoreTile, h = blockIdx.z;
+  if (a0 >= nb || b0 >= nb) return;
+  float* Qs = ssm;                       // [D][64+4]
+  float* Ks = ssm + D * (kScoreTile + 4);
+  const float* qh = qc + (int64_t)h * nb_max * D;
+  const float* kh = kc + (int64_t)h * nb_max * D;
+  for (int i = threadIdx.x; i < kScoreTile * D; i += blockDim.x) {
+    const int r = i / D, d = i % D;
+    Qs[d * (kScoreTile + 4) + r] = (a0 + r < nb) ? qh[(int64_t)(a0 + r) * D + d] : 0.0f;
+    Ks[d * (kScoreTile + 4) + r] = (b0 + r < nb) ? kh[(int64_t)(b0 + r) * D + d] : 0.0f;
+  }
+  __syncthreads();
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  for (int d = 0; d < D; ++d) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) av[i] = Qs[d * (kScoreTile + 4) + ty * 4 + i];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bv[j] = Ks[d * (kScoreTile + 4) + tx * 4 + j];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+  }
+  float* sh = score + (int64_t)h * nb_max * nb_max;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int a = a0 + ty * 4 + i;
+    if (a >= nb) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = b0 + tx * 4 + j;
+      if (b < nb) sh[(int64_t)a * nb_max + b] = acc[i][j];
+    }
+  }
+}
+
+// ================================================================ a13/a14
+// One CTA per (q block a, head h).  Keys are 32-bit patterns that order like
+// the values: non-negative softmax weights as raw float bits (modes 0/1), raw
+// scores mapped to an order-preserving unsigned integer (mode 2).
+constexpr int kSelThreads = 256;
+
+__device__ __forceinline__ uint32_t f2key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long fix63(uint32_t wbits) {
+  return __float2ull_rz(__fmul_rn(__uint_as_float(wbits), 0x1p63f));
+}
+__device__ __forceinline__ float round63(unsigned long long s) {
+  return __fmul_rn(__ull2float_rn(s), 0x1p-63f);
+}
+
+template <typename T>
+__device__ T block_sum_u64(T v, unsigned long long* red) {
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < nw ? (T)red[l] : (T)0;
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  v = (T)red[0];
+  __syncthreads();
+  return v;
+}
+
+// Warp 0 walks 256 buckets from high to low: lane l owns buckets 255-8l .. 248-8l.
+// Returns (via shared state) the bucket where the running count (mode_mass=0)
+// reaches `target_cnt`, or where the running mass rounds to >= pf (mode_mass=1).
+struct RadixState {
+  uint32_t prefix, pmask;
+  int cnt_above;
+  unsigned long long mass_above;
+  int found;       // bucket found in this pass
+  int bucket_cnt;  // count in the chosen bucket
+};
+
+__device__ void radix_walk(const uint32_t* hist_cnt, const unsigned long long* hist_mass, int shift,
+                           int mode_mass, int target_cnt, float pf, RadixState* st) {
+  const int lane = threadIdx.x & 31;
+  int c8[8];
+  unsigned long long m8[8];
+  int lc = 0;
+  unsigned long long lm = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int b = 255 - 8 * lane - i;
+    c8[i] = hist_cnt[b];
+    m8[i] = mode_mass ? hist_mass[b] : 0ull;
+    lc += c8[i];
+    lm += m8[i];
+  }
+  // inclusive scans across lanes (lane order == descending bucket order)
+  int ic = lc;
+  unsigned long long im = lm;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int nc = __shfl_up_sync(0xffffffffu, ic, o);
+    const unsigned long long nm = __shfl_up_sync(0xffffffffu, im, o);
+    if (lane >= o) {
+      ic += nc;
+      im += nm;
+    }
+  }
+  const int base_c = st->cnt_above;
+  const unsigned long long base_m = st->mass_above;
+  bool hit;
+  if (mode_mass) hit = round63(base_m + im) >= pf;
+  else hit = base_c + ic >= target_cnt;
+  const uint32_t ball = __ballot_sync(0xffffffffu, hit);
+  if (ball == 0) {
+    if (lane == 0) st->found = 0;
+    __syncwarp();
+    return;
+  }
+  const int L = __ffs(ball) - 1;
+  if (lane == L) {
+    int c = base_c + ic - lc;
+    unsigned long long m = base_m + im - lm;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const bool h2 = mode_mass ? (round63(m + m8[i]) >= pf) : (c + c8[i] >= target_cnt);
+      if (h2) {
+        const int b = 255 - 8 * lane - i;
+        st->prefix |= (uint32_t)b << shift;
+        st->pmask |= 0xffu << shift;
+        st->cnt_above = c;
+        st->mass_above = m;
+        st->bucket_cnt = c8[i];
+        st->found = 1;
+        break;
+      }
+      c += c8[i];
+      m += m8[i];
+    }
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_kernel(
+    const float* __restrict__ score, const uint8_t* __restrict__ bvalid,
+    const int32_t* __restrict__ n_blocks, int nb_max, const int32_t* __restrict__ block_tiles,
+    const uint64_t* __restrict__ tile_bits, int64_t n_tiles, int wq, int mode, double sparsity,
+    double cdf, float sm_scale, uint32_t* __restrict__ bits_q) {
+  extern __shared__ uint32_t keys[];  // [nb_max] then row bitmap [wq]
+  uint32_t* row = keys + nb_max;
+  __shared__ uint32_t hist_cnt[256];
+  __shared__ unsigned long long hist_mass[256];
+  __shared__ unsigned long long red[32];
+  __shared__ float redf[32];
+  __shared__ RadixState st;
+  __shared__ int tie_base[kSelThreads];
+  const int nb = *n_blocks;
+  const int a = blockIdx.x, h = blockIdx.y;
+  if (a >= nb) return;
+  const float* srow = score + ((int64_t)h * nb_max + a) * nb_max;
+  const int tid = threadIdx.x;
+
+  // selection sizes (computed in double exactly as Python does on the host)
+  long long k_topk, ub;
+  if (mode == 0) {
+    k_topk = (long long)((1.0 - sparsity) * (double)nb);
+    if (k_topk < 1) k_topk = 1;
+    long long u = (long long)(cdf * (double)nb) + 1;
+    ub = k_topk > u ? k_topk : u;
+    if (ub > nb) ub = nb;
+  } else if (mode == 1) {
+    k_topk = 1;
+    ub = (long long)(cdf * (double)nb) + 1;
+    if (ub > nb) ub = nb;
+  } else {
+    k_topk = (long long)((1.0 - sparsity) * (double)nb);
+    ub = nb;
+  }
+  const float pf = (float)cdf;
+  long long n_eff;
+
+  if (mode == 2) {
+    for (int i = tid; i < nb; i += blockDim.x) keys[i] = f2key(bvalid[i] ? srow[i] : -INFINITY);
+    n_eff = k_topk;
+    __syncthreads();
+  } else {
+    float lmax = -INFINITY;
+    for (int i = tid; i < nb; i += blockDim.x) {
+      const float x = bvalid[i] ? __fmul_rn(srow[i], sm_scale) : -INFINITY;
+      keys[i] = __float_as_uint(x);
+      lmax = fmaxf(lmax, x);
+    }
+    const float mx = block_max_f(lmax, redf);
+    unsigned long long lz = 0;
+    for (int i = tid; i < nb; i += blockDim.x) {
+      const float e = det_expf(__fsub_rn(__uint_as_float(keys[i]), mx));
+      keys[i] = __float_as_uint(e);
+      lz += __float2ull_rz(__fmul_rn(e, 0x1p50f));
+    }
+    const unsigned long long Z = block_sum_u64<unsigned long long>(lz, red);
+    const float Zf = __fmul_rn(__ull2float_rn(Z), 0x1p-50f);
+    for (int i = tid; i < nb; i += blockDim.x)
+      keys[i] = __float_as_uint(__fdiv_rn(__uint_as_float(keys[i]), Zf));
+    // crossing point m_c: smallest m with round(S(m)) >= pf, by mass radix descent
+    if (tid == 0) {
+      st.prefix = 0;
+      st.pmask = 0;
+      st.cnt_above = 0;
+      st.mass_above = 0;
+      st.found = 1;
+      st.bucket_cnt = 0;
+    }
+    __syncthreads();
+    bool crossed = true;
+    for (int pass = 0; pass < 4 && crossed; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int i = tid; i < 256; i += blockDim.x) {
+        hist_cnt[i] = 0;
+        hist_mass[i] = 0;
+      }
+      __syncthreads();
+      const uint32_t prefix = st.prefix, pmask = st.pmask;
+      for (int i = tid; i < nb; i += blockDim.x) {
+        const uint32_t kk = keys[i];
+        if ((kk & pmask) == prefix) {
+          const int bkt = (kk >> shift) & 0xff;
+          atomicAdd(&hist_cnt[bkt], 1u);
+          atomicAdd(&hist_mass[bkt], fix63(kk));
+        }
+      }
+      __syncthreads();
+      if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 1, 0, pf, &st);
+      __syncthreads();
+      crossed = st.found != 0;
+    }
+    long long cnt_lt;
+    if (!crossed) {
+      cnt_lt = ub;
+    } else {
+      // all remaining candidates share the value st.prefix; find j* in [1, bucket_cnt]
+      const unsigned long long fv = fix63(st.prefix);
+      long long lo = 1, hi = st.bucket_cnt;
+      while (lo < hi) {
+        const long long mid = (lo + hi) >> 1;
+        if (round63(st.mass_above + (unsigned long long)mid * fv) >= pf) hi = mid;
+        else lo = mid + 1;
+      }
+      const long long m_c = st.cnt_above + lo;
+      cnt_lt = m_c - 1 < ub ? m_c - 1 : ub;
+    }
+    long long n = cnt_lt + 1;
+    if (n < k_topk) n = k_topk;
+    if (n > nb) n = nb;
+    n_eff = n < ub ? n : ub;
+    __syncthreads();
+  }
+
+  // threshold element: the n_eff-th largest key (ties by lower index)
+  for (int i = tid; i < wq; i += blockDim.x) row[i] = 0;
+  uint32_t vstar = 0;
+  int need = 0;
+  if (n_eff > 0) {
+    if (tid == 0) {
+      st.prefix = 0;
+      st.pmask = 0;
+      st.cnt_above = 0;
+      st.mass_above = 0;
+      st.found = 1;
+    }
+    __syncthreads();
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int i = tid; i < 256; i += blockDim.x) hist_cnt[i] = 0;
+      __syncthreads();
+      const uint32_t prefix = st.prefix, pmask = st.pmask;
+      for (int i = tid; i < nb; i += blockDim.x) {
+        const uint32_t kk = keys[i];
+        if ((kk & pmask) == prefix) atomicAdd(&hist_cnt[(kk >> shift) & 0xff], 1u);
+      }
+      __syncthreads();
+      if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 0, (int)n_eff, pf, &st);
+      __syncthreads();
+    }
+    vstar = st.prefix;
+    need = (int)n_eff - st.cnt_above;
+  }
+  __syncthreads();
+  // compaction: key > v*, or key == v* among the first `need` ties in index order
+  if (n_eff > 0) {
+    const int chunk = (nb + blockDim.x - 1) / blockDim.x;
+    const int i0 = tid * chunk, i1 = min(nb, i0 + chunk);
+    int nt = 0;
+    for (int i = i0; i < i1; ++i) nt += keys[i] == vstar;
+    // exclusive scan of nt over threads
+    tie_base[tid] = nt;
+    __syncthreads();
+    if (tid == 0) {
+      int run = 0;
+      for (int i = 0; i < (int)blockDim.x; ++i) {
+        const int x = tie_base[i];
+        tie_base[i] = run;
+        run += x;
+      }
+    }
+    __syncthreads();
+    int rank = tie_base[tid];
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t kk = keys[i];
+      bool sel = kk > vstar;
+      if (kk == vstar) {
+        sel = rank < need;
+        ++rank;
+      }
+      if (!sel) continue;
+      for (int p = 0; p < 2; ++p) {
+        const int kt = block_tiles[2 * i + p];
+        if (kt >= n_tiles || tile_bits[kt] == 0ull) continue;
+        atomicOr(&row[kt >> 5], 1u << (kt & 31));
+      }
+    }
+  }
+  __syncthreads();
+  for (int p = 0; p < 2; ++p) {
+    const int qt = block_tiles[2 * a + p];
+    if (qt >= n_tiles) continue;
+    uint32_t* dst = bits_q + ((int64_t)h * n_tiles + qt) * wq;
+    for (int i = tid; i < wq; i += blockDim.x) dst[i] = row[i];
+  }
+}
+
+// bits_k = transpose of bits_q per head, by 32x32 bit blocks (warp ballots).
+__global__ void transpose_bits_kernel(const uint32_t* __restrict__ bq, int64_t n_tiles, int wq,
+                                      uint32_t* __restrict__ bk) {
+  const int bi = blockIdx.x;  // q-tile word block
+  const int bj = blockIdx.y;  // k-tile word block
+  const int h = blockIdx.z;
+  const int lane = threadIdx.x;
+  const int64_t qt = (int64_t)bi * 32 + lane;
+  const uint32_t w = qt < n_tiles ? bq[((int64_t)h * n_tiles + qt) * wq + bj] : 0u;
+  for (int b = 0; b < 32; ++b) {
+    const uint32_t col = __ballot_sync(0xffffffffu, (w >> b) & 1u);
+    const int64_t kt = (int64_t)bj * 32 + b;
+    if (lane == 0 && kt < n_tiles) bk[((int64_t)h * n_tiles + kt) * wq + bi] = col;
+  }
+}
+
+}  // namespace prism
+
+using namespace prism;
+
+// ===================================================================== C ABI
+extern "C" {
+
+const char* prism_last_error(void) { return prism::last_error(); }
+int prism_abi_version(void) { return 1; }
+
+prism_status_t prism_token_norms(const void* x, int64_t n_tokens, int dim, void* out,
+                                 cudaStream_t stream) {
+  PRISM_CHECK_ARG(x && out, "prism_token_norms: null pointer");
+  PRISM_CHECK_ARG(n_tokens >= 0 && dim > 0 && dim % 8 == 0, "prism_token_norms: dim %d must be a positive multiple of 8", dim);
+  PRISM_CHECK_ARG(aligned16(x), "prism_token_norms: x must be 16-byte aligned");
+  if (n_tokens == 0) return PRISM_OK;
+  const int threads = 256;
+  const int64_t blocks = (n_tokens * 32 + threads - 1) / threads;
+  token_norms_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+      (const uint16_t*)x, n_tokens, dim, (__nv_bfloat16*)out);
+  PRISM_CHECK_LAUNCH("prism_token_norms");
+  return PRISM_OK;
+}
+
+size_t prism_zone_stats_workspace_bytes(int Tp, int Hp, int Wp, int D) {
+  const size_t nz = (size_t)(Tp / 8) * (Hp / 8) * (Wp / 8);
+  return nz * 8 * (size_t)kPart * ((size_t)D + 1) * sizeof(float);
+}
+
+prism_status_t prism_zone_stats(const void* v, int heads, int64_t v_stride_h, int64_t v_stride_s,
+                                int T, int H, int W, int Tp, int Hp, int Wp, int D,
+                                const uint8_t* valid, const void* norms, void* workspace,
+                                float* packed, uint8_t* axis_valid, float* audio,
+                                cudaStream_t stream) {
+  PRISM_CHECK_ARG(v && workspace && packed && axis_valid && audio, "prism_zone_stats: null pointer");
+  PRISM_CHECK_ARG(Tp > 0 && Hp > 0 && Wp > 0 && Tp % 8 == 0 && Hp % 8 == 0 && Wp % 8 == 0,
+                  "prism_zone_stats: grid (%d,%d,%d) must be positive multiples of 8", Tp, Hp, Wp);
+  PRISM_CHECK_ARG(heads >= 1 && D >= 2 && D % 2 == 0 && D <= 2048, "prism_zone_stats: bad heads/D");
+  PRISM_CHECK_ARG(T >= 1 && H >= 1 && W >= 1 && T <= Tp && H <= Hp && W <= Wp && Tp - T < 8 &&
+                  Hp - H < 8 && Wp - W < 8, "prism_zone_stats: source grid (%d,%d,%d) does not pad to (%d,%d,%d)",
+                  T, H, W, Tp, Hp, Wp);
+  PRISM_CHECK_ARG(v_stride_s % 2 == 0 && v_stride_h % 2 == 0 && ((uintptr_t)v & 3) == 0,
+                  "prism_zone_stats: v must allow 4-byte channel-pair loads");
+  const int Nz = (Tp / 8) * (Hp / 8) * (Wp / 8);
+  float* part = (float*)workspace;
+  float* apart = part + (size_t)Nz * 8 * kPart * D;
+  zone_partial_kernel<<<Nz * 8, D / 2, 0, stream>>>((const uint16_t*)v, heads, v_stride_h, v_stride_s,
+                                                    T, H, W, Hp, Wp, D, valid, (const uint16_t*)norms, part,
+                                                    apart);
+  PRISM_CHECK_LAUNCH("prism_zone_stats/partial");
+  zone_combine_kernel<<<Nz, D < 1024 ? (D < 32 ? 32 : D) : 1024, 0, stream>>>(
+      part, apart, T, H, W, Hp, Wp, D, valid, packed, axis_valid, audio);
+  PRISM_CHECK_LAUNCH("prism_zone_stats/combine");
+  return PRISM_OK;
+}
+
+prism_status_t prism_shape_select(const float* packed, const uint8_t* axis_valid,
+                                  const float* audio, int has_audio, int Nz, int D, int method,
+                                  float lambda_a, float tau_128, float lambda_128,
+                                  int64_t* shape_ids, float* g_out, float* rho_out,
+                                  cudaStream_t stream) {
+  PRISM_CHECK_ARG(packed && axis_valid && shape_ids && (audio || !has_audio), "prism_shape_select: null pointer");
+  PRISM_CHECK_ARG(method == 0 || method == 1, "prism_shape_select: unknown dynamic-block method %d", method);
+  PRISM_CHECK_ARG(Nz >= 1 && Nz <= 6000, "prism_shape_select: Nz=%d outside [1, 6000]", Nz);
+  const size_t smem = (size_t)Nz * 8 * sizeof(float);
+  if (smem > 48 * 1024)
+    PRISM_CHECK_CUDA(cudaFuncSetAttribute(shape_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                     "prism_shape_select: smem attribute");
+  shape_select_kernel<<<1, 1024, smem, stream>>>(packed, axis_valid, audio, has_audio, Nz, D, method,
+                                                 lambda_a, tau_128, lambda_128, shape_ids, g_out,
+                                                 rho_out);
+  PRISM_CHECK_LAUNCH("prism_shape_select");
+  return PRISM_OK;
+}
+
+prism_status_t prism_build_layout(const int64_t* shape_ids, int Tp, int Hp, int Wp,
+                                  int32_t* src_idx, int32_t* inv_idx, int32_t* block_of_tile,
+                                  int32_t* block_tiles, int32_t* n_blocks, cudaStream_t stream) {
+  PRISM_CHECK_ARG(shape_ids && src_idx && inv_idx && block_of_tile && block_tiles && n_blocks,
+                  "prism_build_layout: null pointer");
+  PRISM_CHECK_ARG(Tp > 0 && Hp > 0 && Wp > 0 && Tp % 8 == 0 && Hp % 8 == 0 && Wp % 8 == 0,
+                  "prism_build_layout: grid (%d,%d,%d) must be positive multiples of 8", Tp, Hp, Wp);
+  const int64_t S = (int64_t)Tp * Hp * Wp;
+  PRISM_CHECK_ARG(S < (int64_t)1 << 31, "prism_build_layout: sequence too long for int32 indices");
+  const int Nz = (int)(S / 512);
+  block_map_kernel<<<1, 1024, 0, stream>>>(shape_ids, Nz, block_of_tile, block_tiles, n_blocks);
+  PRISM_CHECK_LAUNCH("prism_build_layout/blocks");
+  perm_kernel<<<(unsigned)((S + 255) / 256), 256, 0, stream>>>(shape_ids, Hp, Wp, S, src_idx, inv_idx);
+  PRISM_CHECK_LAUNCH("prism_build_layout/perm");
+  return PRISM_OK;
+}
+
+prism_status_t prism_tile_valid(const int32_t* src_idx, const uint8_t* valid, int T, int H, int W,
+                                int Tp, int Hp, int Wp, uint64_t* tile_bits, int32_t* tile_count,
+                                cudaStream_t stream) {
+  PRISM_CHECK_ARG(src_idx && tile_bits && tile_count, "prism_tile_valid: null pointer");
+  PRISM_CHECK_ARG(Tp % 8 == 0 && Hp % 8 == 0 && Wp % 8 == 0 && Tp > 0 && Hp > 0 && Wp > 0 &&
+                  T <= Tp && H <= Hp && W <= Wp, "prism_tile_valid: bad grids");
+  const int64_t nt = (int64_t)Tp * Hp * Wp / 64;
+  tile_valid_kernel<<<(unsigned)((nt * 32 + 255) / 256), 256, 0, stream>>>(src_idx, valid, nt, T, H, W, Hp, Wp,
+                                                                            tile_bits, tile_count);
+  PRISM_CHECK_LAUNCH("prism_tile_valid");
+  return PRISM_OK;
+}
+
+prism_status_t prism_gather_rows(const void* x, int64_t x_stride_h, int64_t x_stride_s, int heads,
+                                 int D, int T, int H, int W, int Tp, int Hp, int Wp,
+                                 const int32_t* src_idx, void* out, int64_t out_stride_h,
+                                 cudaStream_t stream) {
+  PRISM_CHECK_ARG(x && src_idx && out, "prism_gather_rows: null pointer");
+  PRISM_CHECK_ARG(D % 8 == 0 && x_stride_h % 8 == 0 && x_stride_s % 8 == 0 && out_stride_h % 8 == 0 &&
+                  aligned16(x) && aligned16(out), "prism_gather_rows: rows must be 16-byte aligned (D %% 8 == 0)");
+  PRISM_CHECK_ARG(T <= Tp && H <= Hp && W <= Wp && Tp % 8 == 0 && Hp % 8 == 0 && Wp % 8 == 0,
+                  "prism_gather_rows: bad grids");
+  const int64_t Sp = (int64_t)Tp * Hp * Wp;
+  const int chunks = D / 8;
+  const int64_t total = (int64_t)heads * Sp * chunks;
+  if (total == 0) return PRISM_OK;
+  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      (const uint4*)x, x_stride_h, x_stride_s, heads, chunks, T, H, W, Hp, Wp, Sp, src_idx,
+      (uint4*)out, out_stride_h);
+  PRISM_CHECK_LAUNCH("prism_gather_rows");
+  return PRISM_OK;
+}
+
+prism_status_t prism_scatter_rows(const void* x_re, int64_t x_stride_h, int heads, int D, int T,
+                                  int H, int W, int Tp, int Hp, int Wp, const int32_t* inv_idx,
+                                  void* out, int64_t out_stride_h, int64_t out_stride_s,
+                                  cudaStream_t stream) {
+  PRISM_CHECK_ARG(x_re && inv_idx && out, "prism_scatter_rows: null pointer");
+  PRISM_CHECK_ARG(D % 8 == 0 && x_stride_h % 8 == 0 && out_stride_h % 8 == 0 && out_stride_s % 8 == 0 &&
+                  aligned16(x_re) && aligned16(out), "prism_scatter_rows: rows must be 16-byte aligned (D %% 8 == 0)");
+  PRISM_CHECK_ARG(T <= Tp && H <= Hp && W <= Wp, "prism_scatter_rows: bad grids");
+  const int64_t S = (int64_t)T * H * W;
+  const int chunks = D / 8;
+  const int64_t total = (int64_t)heads * S * chunks;
+  if (total == 0) return PRISM_OK;
+  scatter_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      (const uint4*)x_re, x_stride_h, heads, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out,
+      out_stride_h, out_stride_s);
+  PRISM_CHECK_LAUNCH("prism_scatter_rows");
+  return PRISM_OK;
+}
+
+size_t prism_block_select_workspace_bytes(int heads, int64_t S, int D) {
+  const size_t nb_max = (size_t)(S / 64);
+  size_t b = 2 * (size_t)heads * nb_max * D * sizeof(float);  // pooled q, k
+  b += (size_t)heads * nb_max * nb_max * sizeof(float);       // scores
+  b += (nb_max + 255) / 256 * 256;                            // block valid
+  return b;
+}
+
+prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads, int64_t S, int D,
+                                  const int32_t* block_tiles, const int32_t* n_blocks,
+                                  const uint64_t* tile_bits, int mode, double sparsity,
+                                  double cdf_threshold, void* workspace, uint32_t* bits_q,
+                                  uint32_t* bits_k, cudaStream_t stream) {
+  PRISM_CHECK_ARG(q_re && k_re && block_tiles && n_blocks && tile_bits && workspace && bits_q && bits_k,
+                  "prism_block_select: null pointer");
+  PRISM_CHECK_ARG(mode >= 0 && mode <= 2, "prism_block_select: Either sparsity or cdf_threshold must be provided");
+  PRISM_CHECK_ARG(S > 0 && S % 512 == 0, "prism_block_select: S must be a positive multiple of 512");
+  PRISM_CHECK_ARG(D >= 16 && D <= 256, "prism_block_select: D=%d unsupported", D);
+  const int64_t n_tiles = S / 64;
+  const int nb_max = (int)n_tiles;
+  PRISM_CHECK_ARG(nb_max <= 40000, "prism_block_select: %d blocks exceed the per-row shared-memory limit", nb_max);
+  const int wq = (int)((n_tiles + 31) / 32);
+  float* qc = (float*)workspace;
+  float* kc = qc + (size_t)heads * nb_max * D;
+  float* sc = kc + (size_t)heads * nb_max * D;
+  uint8_t* bvalid = (uint8_t*)(sc + (size_t)heads * nb_max * nb_max);
+  pool_kernel<<<dim3(nb_max, heads), D, 0, stream>>>((const uint16_t*)q_re, (const uint16_t*)k_re, S, D,
+                                                    block_tiles, n_blocks, tile_bits, qc, kc, bvalid,
+                                                    nb_max);
+  PRISM_CHECK_LAUNCH("prism_block_select/pool");
+  const size_t ssm = 2 * (size_t)D * (kScoreTile + 4) * sizeof(float);
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),
+                   "prism_block_select: smem attribute");
+  const int nt = (nb_max + kScoreTile - 1) / kScoreTile;
+  score_kernel<<<dim3(nt, nt, heads), 256, ssm, stream>>>(qc, kc, D, n_blocks, nb_max, sc);
+  PRISM_CHECK_LAUNCH("prism_block_select/score");
+  const float sm_scale = (float)(1.0 / sqrt((double)D));
+  const size_t selsm = ((size_t)nb_max + wq) * sizeof(uint32_t);
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)selsm),
+                   "prism_block_select: smem attribute");
+  select_kernel<<<dim3(nb_max, heads), kSelThreads, selsm, stream>>>(
+      sc, bvalid, n_blocks, nb_max, block_tiles, tile_bits, n_tiles, wq, mode, sparsity,
+      cdf_threshold, sm_scale, bits_q);
+  PRISM_CHECK_LAUNCH("prism_block_select/select");
+  transpose_bits_kernel<<<dim3(wq, wq, heads), 32, 0, stream>>>(bits_q, n_tiles, wq, bits_k);
+  PRISM_CHECK_LAUNCH("prism_block_select/transpose");
+  return PRISM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,217 @@
+"""Dynamic block-shape block-sparse attention (drop-in for the reference's
+``hymm/models/modules/block_sparse_attention/dynamic_block_attention.py``).
+
+``flash_attn_bsa_3d_dynamic`` keeps the reference signature and contract
+(dynamic_block_attention.py:194-332): q, k, v [1, H, S, D] in THW order,
+already padded to the 8x8x8 macro-zone grid, optional audio token norms and
+valid mask, optional cached ``shape_ids`` (activation-checkpoint recompute),
+output [1, H, S, D] in THW order.
+
+``run_bsa_dynamic`` is the call the DiT makes one level up
+(``SelfAttention._run_bsa_dynamic``, wan_video_dit.py:342-432): it takes the
+UNPADDED tokens, in either [1, H, S, D] or [1, S, H, D] layout, and fuses the
+zero padding, the permutation into tile order and its inverse into the
+gather / scatter kernels.
+
+Pipeline per call (all on the current CUDA stream, no host synchronisation):
+  zone statistics -> [SP all-reduce] -> shape ids -> permutation / tile maps
+  -> gather q,k,v into tile order -> pooled block scores + hybrid selection
+  (bitmaps) -> sparse attention forward -> scatter back.
+The backward gathers dO, runs the sparse backward and scatters dQ, dK, dV.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import ops
+from .dynamic_block_shape import ZONE_SIZE, shapes_from_qkv
+
+_TILE = 64  # dynamic_block_attention.py:15
+
+
+class SparsePlan:
+    """Everything the kernels need for one attention call, built without grad."""
+
+    def __init__(self, grid, grid_padded, layout, tile_bits, sparsity, cdf_threshold, sm_scale):
+        self.grid = tuple(grid)
+        self.grid_padded = tuple(grid_padded)
+        self.layout = layout
+        self.src_idx = layout["src_idx"]
+        self.inv_idx = layout["inv_idx"]
+        self.tile_bits = tile_bits
+        self.sparsity = sparsity
+        self.cdf_threshold = cdf_threshold
+        self.sm_scale = sm_scale
+        self.bits_q = None
+        self.bits_k = None
+
+
+def _hsd(x: torch.Tensor, layout: str) -> torch.Tensor:
+    """[1,H,S,D] or [1,S,H,D] -> [H,S,D] view with contiguous rows."""
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    return x[0] if layout == "bhsd" else x[0].transpose(0, 1)
+
+
+def _new_like_layout(heads, S, D, layout, dtype, device):
+    if layout == "bhsd":
+        t = torch.empty(1, heads, S, D, dtype=dtype, device=device)
+        return t, t[0]
+    t = torch.empty(1, S, heads, D, dtype=dtype, device=device)
+    return t, t[0].transpose(0, 1)
+
+
+class _DynBsaFunction(torch.autograd.Function):
+    """Gather -> select -> sparse attention -> scatter, with the matching backward.
+    Gradients flow to q, k, v only (selection is non-differentiable, as in the
+    reference's no_grad blocks at dynamic_block_attention.py:234, 256)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, plan: SparsePlan, layout: str):
+        qh, kh, vh = _hsd(q, layout), _hsd(k, layout), _hsd(v, layout)
+        heads, S, D = qh.shape
+        q_re = ops.gather_rows(qh, plan.grid, plan.grid_padded, plan.src_idx)
+        k_re = ops.gather_rows(kh, plan.grid, plan.grid_padded, plan.src_idx)
+        v_re = ops.gather_rows(vh, plan.grid, plan.grid_padded, plan.src_idx)
+        bits_q, bits_k = ops.block_select(q_re, k_re, plan.layout, plan.tile_bits, plan.sparsity,
+                                          plan.cdf_threshold)
+        plan.bits_q, plan.bits_k = bits_q, bits_k
+        o_re, lse = ops.bsa_fwd(q_re, k_re, v_re, bits_q, plan.tile_bits, plan.sm_scale)
+        out, out_hsd = _new_like_layout(heads, S, D, layout, q.dtype, q.device)
+        ops.scatter_rows(o_re, plan.grid, plan.grid_padded, plan.inv_idx, out=out_hsd)
+        ctx.save_for_backward(q_re, k_re, v_re, o_re, lse, bits_q, bits_k)
+        ctx.plan = plan
+        ctx.layout = layout
+        ctx.shape = (heads, S, D)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q_re, k_re, v_re, o_re, lse, bits_q, bits_k = ctx.saved_tensors
+        plan = ctx.plan
+        layout = ctx.layout
+        heads, S, D = ctx.shape
+        do_re = ops.gather_rows(_hsd(dout, layout), plan.grid, plan.grid_padded, plan.src_idx)
+        dq_re, dk_re, dv_re = ops.bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k,
+                                          plan.tile_bits, plan.sm_scale)
+        grads = []
+        for g_re in (dq_re, dk_re, dv_re):
+            g, g_hsd = _new_like_layout(heads, S, D, layout, dout.dtype, dout.device)
+            ops.scatter_rows(g_re, plan.grid, plan.grid_padded, plan.inv_idx, out=g_hsd)
+            grads.append(g)
+        return grads[0], grads[1], grads[2], None, None
+
+
+def _check_head_dim(D: int):
+    assert D in {16, 32, 64, 128, 256}, "head dim must be one of 16, 32, 64, 128, 256"
+    if D not in (64, 128):
+        raise NotImplementedError(f"prism_b200 kernels support head_dim 64 and 128, got {D}")
+
+
+def build_plan(q_hsd, k_hsd, v_hsd, grid, grid_padded, *, method, sparsity, cdf_threshold,
+               audio_token_norms=None, valid_mask=None, lambda_a=0.5, tau_128=0.15,
+               lambda_128=1.0, shape_ids=None):
+    """Shape ids (unless given), permutation, tile maps and key validity; no grad."""
+    ops.selection_mode(sparsity, cdf_threshold)
+    D = q_hsd.shape[-1]
+    with torch.no_grad():
+        if shape_ids is None:
+            shape_ids = shapes_from_qkv(v_hsd, grid, grid_padded, method,
+                                        audio_norms=audio_token_norms, valid_mask=valid_mask,
+                                        lambda_a=lambda_a, tau_128=tau_128, lambda_128=lambda_128)
+        layout = ops.build_layout(shape_ids, grid_padded)
+        tile_bits, _ = ops.tile_valid(layout["src_idx"], valid_mask, grid, grid_padded)
+    plan = SparsePlan(grid, grid_padded, layout, tile_bits, sparsity, cdf_threshold,
+                      1.0 / (D ** 0.5))
+    return plan, shape_ids
+
+
+def flash_attn_bsa_3d_dynamic(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    grid_padded: Tuple[int, int, int],
+    *,
+    method: str,
+    sparsity: Optional[float] = 0.9375,
+    cdf_threshold: Optional[float] = None,
+    audio_token_norms: Optional[torch.Tensor] = None,
+    valid_mask: Optional[torch.Tensor] = None,
+    lambda_a: float = 0.5,
+    tau_128: float = 0.15,
+    lambda_128: float = 1.0,
+    shape_ids: Optional[torch.Tensor] = None,
+    return_shape_ids: bool = False,
+):
+    """Dynamic-block-shape BSA for video self-attention. Returns [B,H,S,D] THW order.
+
+    Same contract as the reference (dynamic_block_attention.py:194-332):
+    shape_ids, if given, skips the shape choice (checkpoint recompute);
+    return_shape_ids returns it as well."""
+    B, Hn, S, D = q.shape
+    T, H, W = grid_padded
+    assert T * H * W == S
+    assert T % ZONE_SIZE == 0 and H % ZONE_SIZE == 0 and W % ZONE_SIZE == 0
+    assert B == 1, "the dynamic path takes shape statistics from v[0] (batch 1)"
+    _check_head_dim(D)
+    if shape_ids is None and method not in ("ivpq", "penalty"):
+        raise ValueError(f"unknown dynamic-block method: {method!r}")
+    plan, shape_ids = build_plan(
+        _hsd(q, "bhsd"), _hsd(k, "bhsd"), _hsd(v, "bhsd"), grid_padded, grid_padded,
+        method=method, sparsity=sparsity, cdf_threshold=cdf_threshold,
+        audio_token_norms=audio_token_norms, valid_mask=valid_mask, lambda_a=lambda_a,
+        tau_128=tau_128, lambda_128=lambda_128, shape_ids=shape_ids)
+    out = _DynBsaFunction.apply(q, k, v, plan, "bhsd")
+    if return_shape_ids:
+        return out, shape_ids
+    return out
+
+
+def run_bsa_dynamic(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    grid_size: Tuple[int, int, int],
+    *,
+    method: str = "ivpq",
+    sparsity: Optional[float] = 0.9375,
+    cdf_threshold: Optional[float] = None,
+    audio_token_norms: Optional[torch.Tensor] = None,
+    lambda_a: float = 0.5,
+    tau_128: float = 0.15,
+    lambda_128: float = 1.0,
+    shape_ids: Optional[torch.Tensor] = None,
+    return_shape_ids: bool = False,
+    layout: str = "bhsd",
+    return_plan: bool = False,
+):
+    """``SelfAttention._run_bsa_dynamic`` (wan_video_dit.py:342-432) on unpadded
+    tokens: q, k, v [1, H, T*H*W, D] (layout="bhsd") or [1, T*H*W, H, D]
+    (layout="bshd"), audio_token_norms [T*H*W] or None.  Padding to the zone
+    grid, the valid mask and the unpad are implicit.  Output has q's layout."""
+    if layout not in ("bhsd", "bshd"):
+        raise ValueError("layout must be 'bhsd' or 'bshd'")
+    T, H, W = grid_size
+    qh = _hsd(q, layout)
+    heads, S, D = qh.shape
+    assert S == T * H * W, f"sequence {S} != grid {grid_size}"
+    assert q.shape[0] == 1, "batch 1"
+    _check_head_dim(D)
+    gp = ops.padded_grid(grid_size)
+    plan, shape_ids = build_plan(
+        qh, _hsd(k, layout), _hsd(v, layout), grid_size, gp, method=method, sparsity=sparsity,
+        cdf_threshold=cdf_threshold, audio_token_norms=audio_token_norms, valid_mask=None,
+        lambda_a=lambda_a, tau_128=tau_128, lambda_128=lambda_128, shape_ids=shape_ids)
+    out = _DynBsaFunction.apply(q, k, v, plan, layout)
+    res = [out]
+    if return_shape_ids:
+        res.append(shape_ids)
+    if return_plan:
+        res.append(plan)
+    return res[0] if len(res) == 1 else tuple(res)
+
+
+__all__ = ["flash_attn_bsa_3d_dynamic", "run_bsa_dynamic", "build_plan", "SparsePlan"]

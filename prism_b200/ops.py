@@ -1,0 +1,215 @@
+"""Torch-facing wrappers of the C ABI (include/prism_bsa.h).
+
+Every function takes CUDA tensors, allocates its outputs and workspaces with
+torch's caching allocator, and enqueues the kernels on the current stream.
+Nothing here computes on the CPU; a missing library or a non-CUDA tensor is an
+error.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+SELECT_MODES = {"topk_cdf": 0, "cdf": 1, "topk": 2}
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise _lib.PrismError("prism_b200 ops require CUDA tensors (no CPU fallback)")
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+def padded_grid(grid: Tuple[int, int, int]) -> Tuple[int, int, int]:
+    return tuple(int(math.ceil(int(x) / 8) * 8) for x in grid)
+
+
+def selection_mode(sparsity, cdf_threshold) -> int:
+    if sparsity is not None and cdf_threshold is None:
+        return SELECT_MODES["topk"]
+    if sparsity is None and cdf_threshold is not None:
+        return SELECT_MODES["cdf"]
+    if sparsity is not None and cdf_threshold is not None:
+        return SELECT_MODES["topk_cdf"]
+    raise ValueError("Either sparsity or cdf_threshold must be provided")
+
+
+# ------------------------------------------------------------------- a2
+def token_norms(x: torch.Tensor) -> torch.Tensor:
+    """||x||_2 over the last dim, bf16 in/out (wan_video_dit.py:742-744)."""
+    _check_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("token_norms expects bf16")
+    xc = x.contiguous()
+    dim = xc.shape[-1]
+    n = xc.numel() // dim
+    out = torch.empty(xc.shape[:-1], dtype=torch.bfloat16, device=x.device)
+    _lib.call("prism_token_norms", _p(xc), n, dim, _p(out), _stream(x))
+    return out
+
+
+# --------------------------------------------------------------- a4-a7
+def zone_stats(v_hsd: torch.Tensor, grid, grid_padded, valid: Optional[torch.Tensor] = None,
+               norms: Optional[torch.Tensor] = None):
+    """v_hsd: [heads, T*H*W, D] bf16 view (D contiguous) on the source grid.
+    Returns packed [Nz, 25*D] f32, axis_valid [Nz, 24] u8, audio [Nz, 25] f32."""
+    _check_cuda(v_hsd, valid, norms)
+    heads, S, D = v_hsd.shape
+    T, H, W = grid
+    Tp, Hp, Wp = grid_padded
+    if S != T * H * W:
+        raise ValueError(f"sequence {S} != grid {grid}")
+    if v_hsd.stride(2) != 1:
+        raise ValueError("v must be contiguous in the head dim")
+    Nz = (Tp // 8) * (Hp // 8) * (Wp // 8)
+    dev = v_hsd.device
+    packed = torch.empty(Nz, 25 * D, dtype=torch.float32, device=dev)
+    axis_valid = torch.empty(Nz, 24, dtype=torch.uint8, device=dev)
+    audio = torch.empty(Nz, 25, dtype=torch.float32, device=dev)
+    ws = _ws(_lib.query("prism_zone_stats_workspace_bytes", Tp, Hp, Wp, D), dev)
+    vm = None if valid is None else valid.to(torch.uint8).contiguous()
+    nm = None if norms is None else norms.to(torch.bfloat16).contiguous()
+    _lib.call("prism_zone_stats", _p(v_hsd), heads, v_hsd.stride(0), v_hsd.stride(1), T, H, W,
+              Tp, Hp, Wp, D, _p(vm), _p(nm), _p(ws), _p(packed), _p(axis_valid), _p(audio),
+              _stream(v_hsd))
+    return packed, axis_valid, audio
+
+
+def shape_select(packed, axis_valid, audio, has_audio: bool, method: str, lambda_a=0.5,
+                 tau_128=0.15, lambda_128=1.0, want_diag=False):
+    if method not in ("ivpq", "penalty"):
+        raise ValueError(f"unknown dynamic-block method: {method!r}")
+    _check_cuda(packed)
+    Nz = packed.shape[0]
+    D = packed.shape[1] // 25
+    dev = packed.device
+    ids = torch.empty(Nz, dtype=torch.int64, device=dev)
+    g = torch.empty(Nz, 3, dtype=torch.float32, device=dev) if want_diag else None
+    rho = torch.empty(Nz, dtype=torch.float32, device=dev) if want_diag else None
+    _lib.call("prism_shape_select", _p(packed), _p(axis_valid), _p(audio), int(bool(has_audio)),
+              Nz, D, 0 if method == "ivpq" else 1, float(lambda_a), float(tau_128),
+              float(lambda_128), _p(ids), _p(g), _p(rho), _stream(packed))
+    if want_diag:
+        return ids, g, rho
+    return ids
+
+
+# ---------------------------------------------------------------- a8/a9
+def build_layout(shape_ids: torch.Tensor, grid_padded):
+    _check_cuda(shape_ids)
+    Tp, Hp, Wp = grid_padded
+    S = Tp * Hp * Wp
+    n_tiles = S // 64
+    dev = shape_ids.device
+    ids = shape_ids.to(torch.int64).contiguous()
+    src = torch.empty(S, dtype=torch.int32, device=dev)
+    inv = torch.empty(S, dtype=torch.int32, device=dev)
+    bot = torch.empty(n_tiles, dtype=torch.int32, device=dev)
+    bt = torch.empty(n_tiles + 1, 2, dtype=torch.int32, device=dev)
+    nb = torch.empty(1, dtype=torch.int32, device=dev)
+    _lib.call("prism_build_layout", _p(ids), Tp, Hp, Wp, _p(src), _p(inv), _p(bot), _p(bt), _p(nb),
+              _stream(ids))
+    return dict(src_idx=src, inv_idx=inv, block_of_tile=bot, block_tiles=bt, n_blocks=nb)
+
+
+def tile_valid(src_idx, valid, grid, grid_padded):
+    _check_cuda(src_idx, valid)
+    T, H, W = grid
+    Tp, Hp, Wp = grid_padded
+    n_tiles = src_idx.numel() // 64
+    dev = src_idx.device
+    bits = torch.empty(n_tiles, dtype=torch.int64, device=dev)
+    cnt = torch.empty(n_tiles, dtype=torch.int32, device=dev)
+    vm = None if valid is None else valid.to(torch.uint8).contiguous()
+    _lib.call("prism_tile_valid", _p(src_idx), _p(vm), T, H, W, Tp, Hp, Wp, _p(bits), _p(cnt),
+              _stream(src_idx))
+    return bits, cnt
+
+
+# -------------------------------------------------------------- a10/a17
+def gather_rows(x_hsd: torch.Tensor, grid, grid_padded, src_idx: torch.Tensor) -> torch.Tensor:
+    """x_hsd [heads, T*H*W, D] (D contiguous) -> [heads, S_p, D] tile order, zero rows
+    for padded tokens."""
+    _check_cuda(x_hsd, src_idx)
+    heads, S, D = x_hsd.shape
+    T, H, W = grid
+    Tp, Hp, Wp = grid_padded
+    if x_hsd.stride(2) != 1:
+        raise ValueError("rows must be contiguous")
+    out = torch.empty(heads, Tp * Hp * Wp, D, dtype=x_hsd.dtype, device=x_hsd.device)
+    _lib.call("prism_gather_rows", _p(x_hsd), x_hsd.stride(0), x_hsd.stride(1), heads, D, T, H, W,
+              Tp, Hp, Wp, _p(src_idx), _p(out), out.stride(0), _stream(x_hsd))
+    return out
+
+
+def scatter_rows(x_re: torch.Tensor, grid, grid_padded, inv_idx: torch.Tensor,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[heads, S_p, D] tile order -> out [heads, T*H*W, D] (any head/token strides)."""
+    _check_cuda(x_re, inv_idx)
+    heads, Sp, D = x_re.shape
+    T, H, W = grid
+    Tp, Hp, Wp = grid_padded
+    if out is None:
+        out = torch.empty(heads, T * H * W, D, dtype=x_re.dtype, device=x_re.device)
+    _lib.call("prism_scatter_rows", _p(x_re), x_re.stride(0), heads, D, T, H, W, Tp, Hp, Wp,
+              _p(inv_idx), _p(out), out.stride(0), out.stride(1), _stream(x_re))
+    return out
+
+
+# -------------------------------------------------------------- a11-a14
+def block_select(q_re, k_re, layout, tile_bits, sparsity, cdf_threshold):
+    _check_cuda(q_re, k_re)
+    heads, S, D = q_re.shape
+    mode = selection_mode(sparsity, cdf_threshold)
+    n_tiles = S // 64
+    wq = (n_tiles + 31) // 32
+    dev = q_re.device
+    bits_q = torch.empty(heads, n_tiles, wq, dtype=torch.int32, device=dev)
+    bits_k = torch.empty(heads, n_tiles, wq, dtype=torch.int32, device=dev)
+    ws = _ws(_lib.query("prism_block_select_workspace_bytes", heads, S, D), dev)
+    _lib.call("prism_block_select", _p(q_re), _p(k_re), heads, S, D, _p(layout["block_tiles"]),
+              _p(layout["n_blocks"]), _p(tile_bits), mode,
+              float(sparsity if sparsity is not None else 0.0),
+              float(cdf_threshold if cdf_threshold is not None else 0.0), _p(ws), _p(bits_q),
+              _p(bits_k), _stream(q_re))
+    return bits_q, bits_k
+
+
+# -------------------------------------------------------------- a15/a16
+def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float):
+    _check_cuda(q_re, k_re, v_re)
+    heads, S, D = q_re.shape
+    o = torch.empty_like(q_re)
+    lse = torch.empty(heads, S, dtype=torch.float32, device=q_re.device)
+    _lib.call("prism_bsa_fwd", _p(q_re), _p(k_re), _p(v_re), heads, S, D, float(sm_scale),
+              _p(bits_q), _p(tile_bits), _p(o), _p(lse), _stream(q_re))
+    return o, lse
+
+
+def bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k, tile_bits, sm_scale: float):
+    _check_cuda(q_re, do_re)
+    heads, S, D = q_re.shape
+    dq = torch.empty_like(q_re)
+    dk = torch.empty_like(k_re)
+    dv = torch.empty_like(v_re)
+    ws = _ws(_lib.query("prism_bsa_bwd_workspace_bytes", heads, S), q_re.device)
+    _lib.call("prism_bsa_bwd", _p(q_re), _p(k_re), _p(v_re), _p(o_re), _p(do_re), _p(lse), heads, S,
+              D, float(sm_scale), _p(bits_q), _p(bits_k), _p(tile_bits), _p(ws), _p(dq), _p(dk),
+              _p(dv), _stream(q_re))
+    return dq, dk, dv

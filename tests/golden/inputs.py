@@ -1,0 +1,162 @@
+"""Seeded synthetic inputs for the parity fixtures.
+
+Generated with torch's CPU generator, so the same seeds give the same values on
+any machine with the same torch build; the fixtures therefore store seeds and
+reference outputs, not the input tensors.
+
+Value models:
+* ``normal``: q, k, v ~ N(0, 1) (config 0).
+* ``zoned``: each 8x8x8 macro-zone of the padded grid holds tokens
+  ``zone_mean + 0.3 * noise`` with zone_mean, noise ~ N(0, 0.5^2) (configs 1-2),
+  optionally times a per-zone amplitude U(lo, hi) so that zone densities differ.
+* ``aniso``: zone_mean + sum over the axes d of w_d(zone) * wave_d(zone, position
+  along d) + 0.1 * noise, with random per-zone axis weights, so zones are
+  anisotropic and every candidate shape family (64- and 128-token) occurs.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+
+@dataclass
+class Case:
+    name: str
+    grid: Tuple[int, int, int]          # unpadded T, H, W
+    heads: int
+    head_dim: int
+    values: str = "normal"              # "normal" | "zoned" | "aniso"
+    amp: Optional[Tuple[float, float]] = None
+    audio: bool = True
+    audio_tokens: int = 32
+    method: str = "ivpq"
+    sparsity: Optional[float] = 0.75
+    cdf_threshold: Optional[float] = 0.9
+    lambda_a: float = 0.5
+    tau_128: float = 0.15
+    lambda_128: float = 1.0
+    seed: int = 0
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def grid_padded(self):
+        return tuple(int(math.ceil(x / 8) * 8) for x in self.grid)
+
+    @property
+    def needs_pad(self):
+        return self.grid_padded != tuple(self.grid)
+
+
+CASES = {
+    # 4 heads, D=64, 4x8x8 grid (padded to 8x8x8), 32 audio tokens,
+    # top-k 2 of 8 blocks (sparsity 0.75) + cumulative mass 0.9.
+    "c0": Case("c0", (4, 8, 8), 4, 64),
+    "c0_tau25_penalty": Case("c0_tau25_penalty", (4, 8, 8), 4, 64, method="penalty", tau_128=0.25),
+    # anisotropic zones + penalty matching with a strong 128-token bonus: mixed 64/128 shapes
+    "mixed_d64": Case("mixed_d64", (13, 14, 21), 2, 64, values="aniso", amp=(0.02, 1.0),
+                      method="penalty", sparsity=0.9, cdf_threshold=0.5, tau_128=0.8,
+                      lambda_128=3.0, seed=10),
+    "mixed_d128_penalty": Case("mixed_d128_penalty", (5, 9, 16), 2, 128, values="aniso",
+                               amp=(0.02, 1.0), method="penalty", sparsity=0.92,
+                               cdf_threshold=0.9, tau_128=0.8, lambda_128=3.0, seed=33),
+    "topk_only": Case("topk_only", (6, 11, 13), 2, 64, values="aniso", amp=(0.02, 1.0),
+                      method="penalty", sparsity=0.8, cdf_threshold=None, tau_128=0.8,
+                      lambda_128=3.0, seed=30),
+    "cdf_only": Case("cdf_only", (6, 11, 13), 2, 64, values="aniso", amp=(0.02, 1.0),
+                     method="penalty", sparsity=None, cdf_threshold=0.6, tau_128=0.8,
+                     lambda_128=3.0, seed=40, audio=False),
+    # IVPQ on anisotropic zones (64-token shapes of every orientation)
+    "aniso_ivpq": Case("aniso_ivpq", (13, 14, 21), 2, 64, values="aniso", amp=(0.05, 1.0),
+                       sparsity=0.9, cdf_threshold=0.5, tau_128=0.5, seed=10),
+    "nopad_bf16": Case("nopad_bf16", (8, 8, 16), 2, 64, values="aniso", amp=(0.1, 1.0),
+                       sparsity=0.75, cdf_threshold=0.9, seed=50),
+}
+
+
+def _zoned(gen, heads, grid_p, D, amp):
+    T, H, W = grid_p
+    ZT, ZH, ZW = T // 8, H // 8, W // 8
+    mean = torch.randn(heads, ZT, ZH, ZW, D, generator=gen) * 0.5
+    noise = torch.randn(heads, T, H, W, D, generator=gen) * 0.5
+    if amp is not None:
+        a = torch.rand(ZT, ZH, ZW, generator=gen) * (amp[1] - amp[0]) + amp[0]
+        mean = mean * a[None, :, :, :, None]
+        scale = a.repeat_interleave(8, 0).repeat_interleave(8, 1).repeat_interleave(8, 2)
+        noise = noise * scale[None, :, :, :, None]
+    m = mean.repeat_interleave(8, 1).repeat_interleave(8, 2).repeat_interleave(8, 3)
+    return (m + 0.3 * noise).reshape(heads, T * H * W, D)
+
+
+def _aniso(gen, heads, grid_p, D, amp):
+    T, H, W = grid_p
+    ZT, ZH, ZW = T // 8, H // 8, W // 8
+    mean = torch.randn(heads, ZT, 1, ZH, 1, ZW, 1, D, generator=gen) * 0.5
+    wt = torch.randn(heads, ZT, 8, ZH, 1, ZW, 1, D, generator=gen) * 0.5
+    wh = torch.randn(heads, ZT, 1, ZH, 8, ZW, 1, D, generator=gen) * 0.5
+    ww = torch.randn(heads, ZT, 1, ZH, 1, ZW, 8, D, generator=gen) * 0.5
+    w = torch.rand(3, ZT, 1, ZH, 1, ZW, 1, 1, generator=gen) ** 3
+    w = w / w.sum(0, keepdim=True)
+    x = mean + w[0] * wt + w[1] * wh + w[2] * ww
+    noise = torch.randn(heads, ZT, 8, ZH, 8, ZW, 8, D, generator=gen) * 0.05
+    if amp is not None:
+        a = torch.rand(ZT, 1, ZH, 1, ZW, 1, 1, generator=gen) * (amp[1] - amp[0]) + amp[0]
+        x = mean + a * (x - mean + noise)
+    else:
+        x = x + noise
+    return x.reshape(heads, T * H * W, D)
+
+
+def make_inputs(case: Case):
+    """Returns dict of CPU tensors:
+    q, k, v  [1, h, S_p, D] bf16, THW order, zero-padded (F.pad semantics);
+    q_u, k_u, v_u [1, h, S, D] bf16 unpadded; do [1, h, S_p, D] bf16 (zero on padding);
+    valid [S_p] bool or None; a2v [S, Da] bf16 or None; norms [S_p] bf16 or None."""
+    T, H, W = case.grid
+    Tp, Hp, Wp = case.grid_padded
+    h, D = case.heads, case.head_dim
+    out = {}
+    for i, name in enumerate(("q", "k", "v", "do")):
+        gen = torch.Generator().manual_seed(case.seed + i)
+        if case.values in ("zoned", "aniso") and name != "do":
+            fn = _zoned if case.values == "zoned" else _aniso
+            full = fn(gen, h, (Tp, Hp, Wp), D, case.amp)
+            x = full.reshape(h, Tp, Hp, Wp, D)[:, :T, :H, :W].reshape(1, h, T * H * W, D)
+        else:
+            x = torch.randn(1, h, T * H * W, D, generator=gen)
+        out[name + "_u"] = x.to(torch.bfloat16)
+    for name in ("q", "k", "v", "do"):
+        x = out[name + "_u"].view(1, h, T, H, W, D)
+        xp = F.pad(x, (0, 0, 0, Wp - W, 0, Hp - H, 0, Tp - T))
+        out[name] = xp.reshape(1, h, Tp * Hp * Wp, D).contiguous()
+    if case.needs_pad:
+        it = torch.arange(Tp)[:, None, None] < T
+        ih = torch.arange(Hp)[None, :, None] < H
+        iw = torch.arange(Wp)[None, None, :] < W
+        out["valid"] = (it & ih & iw).reshape(-1).contiguous()
+    else:
+        out["valid"] = None
+    if case.audio:
+        gen = torch.Generator().manual_seed(case.seed + 4)
+        a2v = torch.randn(T * H * W, case.audio_tokens * 2, generator=gen)
+        gen = torch.Generator().manual_seed(case.seed + 5)
+        zscale = torch.rand((Tp // 8) * (Hp // 8) * (Wp // 8), generator=gen) * 1.8 + 0.2
+        # per-zone amplitude U(0.2, 2) on the cross-attention output
+        tt = torch.arange(T)[:, None, None] // 8
+        hh = torch.arange(H)[None, :, None] // 8
+        ww = torch.arange(W)[None, None, :] // 8
+        zid = ((tt * (Hp // 8) + hh) * (Wp // 8) + ww).reshape(-1)
+        a2v = (a2v * zscale[zid][:, None]).to(torch.bfloat16)
+        out["a2v"] = a2v
+        norms = a2v.norm(dim=-1)  # wan_video_dit.py:744, bf16 in -> bf16 out
+        n3 = norms.reshape(T, H, W)
+        out["norms_u"] = norms
+        out["norms"] = F.pad(n3, (0, Wp - W, 0, Hp - H, 0, Tp - T)).reshape(-1).contiguous()
+    else:
+        out["a2v"] = None
+        out["norms_u"] = None
+        out["norms"] = None
+    return out
