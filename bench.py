@@ -168,15 +168,15 @@ def kernel_times(plan, q4, k4, v4, reps=3):
     stream = torch.cuda.current_stream()
     ev = lambda: torch.cuda.Event(enable_timing=True)
     res = {}
-    o, lse = ops.bsa_fwd(q_re, k_re, v_re, plan.bits_q, plan.tile_bits, plan.sm_scale)
+    o, lse, o_lo = ops.bsa_fwd(q_re, k_re, v_re, plan.bits_q, plan.tile_bits, plan.sm_scale, want_lo=True)
     do = torch.randn_like(o)
     delta = torch.empty(heads, Sp, dtype=torch.float32, device=o.device)
     dq, dk, dv = torch.empty_like(o), torch.empty_like(o), torch.empty_like(o)
     P = ops._p
     st = ops._stream(o)
     calls = {
-        "bsa_fwd": lambda: ops.bsa_fwd(q_re, k_re, v_re, plan.bits_q, plan.tile_bits, plan.sm_scale),
-        "bsa_bwd_delta": lambda: _lib.call("prism_bsa_bwd_delta", P(o), P(do), heads, Sp, D, P(delta), st),
+        "bsa_fwd": lambda: ops.bsa_fwd(q_re, k_re, v_re, plan.bits_q, plan.tile_bits, plan.sm_scale, want_lo=True),
+        "bsa_bwd_delta": lambda: _lib.call("prism_bsa_bwd_delta", P(o), P(o_lo), P(do), heads, Sp, D, P(delta), st),
         "bsa_bwd_dkdv": lambda: _lib.call("prism_bsa_bwd_dkdv", P(q_re), P(k_re), P(v_re), P(do), P(lse),
                                           P(delta), heads, Sp, D, float(plan.sm_scale), P(plan.bits_k),
                                           P(plan.tile_bits), P(dk), P(dv), st),

@@ -138,18 +138,23 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
 /* Block-sparse attention forward over tile-ordered q/k/v [heads, S, D] bf16
  * (attn_fwd_bsa_varlen_triton + _attn_fwd_bsa_varlen_align,
  * bsa_interface.py:328-385, flash_attn_bsa_varlen_mask.py:193-319).
- * o [heads, S, D] bf16; lse [heads, S] fp32 natural log.  D in {64, 128}. */
+ * o [heads, S, D] bf16; lse [heads, S] fp32 natural log.  D in {64, 128}.
+ * o_lo (optional, same shape as o) receives the bf16 rounding residual of the
+ * output (o + o_lo = the fp32 result to ~16 bits); pass it to the backward so
+ * that delta = rowsum(O * dO) is not limited by O's bf16 rounding. */
 prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
                              int D, float sm_scale, const uint32_t* bits_q,
-                             const uint64_t* tile_bits, void* o, float* lse,
+                             const uint64_t* tile_bits, void* o, void* o_lo, float* lse,
                              cudaStream_t stream);
 
 /* Block-sparse attention backward (attn_bwd_bsa_varlen_triton,
  * bsa_interface.py:387-523): delta, then dK/dV over bits_k, then dQ over
- * bits_q.  workspace: prism_bsa_bwd_workspace_bytes() (holds delta). */
+ * bits_q.  o_lo: the forward's residual or NULL.
+ * workspace: prism_bsa_bwd_workspace_bytes() (holds delta). */
 size_t prism_bsa_bwd_workspace_bytes(int heads, int64_t S);
 prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const void* o,
-                             const void* dout, const float* lse, int heads, int64_t S, int D,
+                             const void* o_lo, const void* dout, const float* lse, int heads,
+                             int64_t S, int D,
                              float sm_scale, const uint32_t* bits_q, const uint32_t* bits_k,
                              const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
                              void* dv, cudaStream_t stream);
@@ -159,8 +164,8 @@ prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const 
  * dK, dV per key-tile pair over the transposed selection
  * (_attn_bwd_dkdv_bsa_varlen_wrapper, flash_attn_bsa_varlen_mask.py:564-704);
  * dQ per query-tile pair (_attn_bwd_dq_bsa_varlen_align_wrapper, :881-1014). */
-prism_status_t prism_bsa_bwd_delta(const void* o, const void* dout, int heads, int64_t S, int D,
-                                   float* delta, cudaStream_t stream);
+prism_status_t prism_bsa_bwd_delta(const void* o, const void* o_lo, const void* dout, int heads,
+                                   int64_t S, int D, float* delta, cudaStream_t stream);
 prism_status_t prism_bsa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout,
                                   const float* lse, const float* delta, int heads, int64_t S, int D,
                                   float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,

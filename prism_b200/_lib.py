@@ -32,10 +32,10 @@ SIGNATURES = {
     "prism_scatter_rows": (_I, [_P, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _I64, _P]),
     "prism_block_select_workspace_bytes": (_SZ, [_I, _I64, _I]),
     "prism_block_select": (_I, [_P, _P, _I, _I64, _I, _P, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
-    "prism_bsa_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P]),
+    "prism_bsa_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_workspace_bytes": (_SZ, [_I, _I64]),
-    "prism_bsa_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
-    "prism_bsa_bwd_delta": (_I, [_P, _P, _I, _I64, _I, _P, _P]),
+    "prism_bsa_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "prism_bsa_bwd_delta": (_I, [_P, _P, _P, _I, _I64, _I, _P, _P]),
     "prism_bsa_bwd_dkdv": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P]),
 }

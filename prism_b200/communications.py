@@ -162,13 +162,17 @@ class _AllGather(torch.autograd.Function):
             lst = [torch.empty_like(input_) for _ in range(world)]
             dist.all_gather(lst, input_, group=group)
             return torch.cat(lst, dim=dim)
-        lst = []
-        for s in sizes:
+        # ragged shards: pad to the largest shard, one uniform all-gather, slice
+        # (the reference issues a ragged dist.all_gather, i.e. one broadcast per rank)
+        mx = max(sizes)
+        pad = mx - input_.shape[dim]
+        if pad > 0:
             shape = list(input_.shape)
-            shape[dim] = s
-            lst.append(torch.empty(shape, dtype=input_.dtype, device=input_.device))
+            shape[dim] = pad
+            input_ = torch.cat([input_, input_.new_zeros(shape)], dim=dim)
+        lst = [torch.empty_like(input_) for _ in range(world)]
         dist.all_gather(lst, input_, group=group)
-        return torch.cat(lst, dim=dim)
+        return torch.cat([t.narrow(dim, 0, s) for t, s in zip(lst, sizes)], dim=dim)
 
     @staticmethod
     def backward(ctx, grad_output):

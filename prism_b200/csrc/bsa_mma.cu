@@ -116,7 +116,8 @@ __global__ void __launch_bounds__(256, 1)
     fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                const __nv_bfloat16* __restrict__ v, int64_t S, int wq, float qk_scale,
                const uint32_t* __restrict__ bits_q, const uint64_t* __restrict__ tile_bits,
-               __nv_bfloat16* __restrict__ o, float* __restrict__ lse) {
+               __nv_bfloat16* __restrict__ o, __nv_bfloat16* __restrict__ o_lo,
+               float* __restrict__ lse) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int pair = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -268,8 +269,20 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) {
     const int c = i * 8 + tq * 2;
-    *reinterpret_cast<uint32_t*>(o0 + c) = pack_bf16(acc[i][0] * inv0, acc[i][1] * inv0);
-    *reinterpret_cast<uint32_t*>(o1 + c) = pack_bf16(acc[i][2] * inv1, acc[i][3] * inv1);
+    const float x0 = acc[i][0] * inv0, x1 = acc[i][1] * inv0;
+    const float x2 = acc[i][2] * inv1, x3 = acc[i][3] * inv1;
+    const uint32_t h01 = pack_bf16(x0, x1), h23 = pack_bf16(x2, x3);
+    *reinterpret_cast<uint32_t*>(o0 + c) = h01;
+    *reinterpret_cast<uint32_t*>(o1 + c) = h23;
+    if (o_lo != nullptr) {
+      // bf16 rounding residual: O = hi + lo to ~16 mantissa bits, so that the
+      // backward's delta = rowsum(O * dO) does not inherit O's bf16 rounding
+      const int64_t off0 = (o0 - o) + c, off1 = (o1 - o) + c;
+      *reinterpret_cast<uint32_t*>(o_lo + off0) =
+          pack_bf16(x0 - __uint_as_float(h01 << 16), x1 - __uint_as_float(h01 & 0xffff0000u));
+      *reinterpret_cast<uint32_t*>(o_lo + off1) =
+          pack_bf16(x2 - __uint_as_float(h23 << 16), x3 - __uint_as_float(h23 & 0xffff0000u));
+    }
   }
   if (tq == 0) {
     lse[(int64_t)h * S + r0] = (m0 + __log2f(l0)) * kLn2;
@@ -279,9 +292,11 @@ __global__ void __launch_bounds__(256, 1)
 
 // ================================================================ preprocess
 // delta[h][s] = sum_d O * dO (fp32), one warp per row.
+// With o_lo (the forward's rounding residual) the row uses O = hi + lo.
 template <int D>
-__global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
-                             int64_t rows, float* __restrict__ delta) {
+__global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ o_lo,
+                             const __nv_bfloat16* __restrict__ dout, int64_t rows,
+                             float* __restrict__ delta) {
   const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -290,7 +305,13 @@ __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfl
   for (int c = lane * 2; c < D; c += 64) {
     const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(o + r * D + c);
     const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(dout + r * D + c);
-    acc += __low2float(a) * __low2float(b) + __high2float(a) * __high2float(b);
+    float a0 = __low2float(a), a1 = __high2float(a);
+    if (o_lo != nullptr) {
+      const __nv_bfloat162 l = *reinterpret_cast<const __nv_bfloat162*>(o_lo + r * D + c);
+      a0 += __low2float(l);
+      a1 += __high2float(l);
+    }
+    acc += a0 * __low2float(b) + a1 * __high2float(b);
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
@@ -613,7 +634,7 @@ size_t dq_smem(int wq) { return (size_t)(256 + 4 * 64) * D * 2 + 2 * wq * 4; }
 template <int D>
 prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
                           float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits, void* o,
-                          float* lse, cudaStream_t stream) {
+                          void* o_lo, float* lse, cudaStream_t stream) {
   const int64_t n_tiles = S / 64;
   const int wq = (int)((n_tiles + 31) / 32);
   const size_t sm = fwd_smem<D>(wq);
@@ -622,17 +643,17 @@ prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads
                    "prism_bsa_fwd: smem attribute");
   fwd_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), 256, sm, stream>>>(
       (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, S, wq,
-      sm_scale * kLog2e, bits_q, tile_bits, (__nv_bfloat16*)o, lse);
+      sm_scale * kLog2e, bits_q, tile_bits, (__nv_bfloat16*)o, (__nv_bfloat16*)o_lo, lse);
   PRISM_CHECK_LAUNCH("prism_bsa_fwd");
   return PRISM_OK;
 }
 
 template <int D>
-prism_status_t launch_delta(const void* o, const void* dout, int heads, int64_t S, float* delta,
-                            cudaStream_t stream) {
+prism_status_t launch_delta(const void* o, const void* o_lo, const void* dout, int heads, int64_t S,
+                            float* delta, cudaStream_t stream) {
   const int64_t rows = (int64_t)heads * S;
   delta_kernel<D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(
-      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, rows, delta);
+      (const __nv_bfloat16*)o, (const __nv_bfloat16*)o_lo, (const __nv_bfloat16*)dout, rows, delta);
   PRISM_CHECK_LAUNCH("prism_bsa_bwd_delta");
   return PRISM_OK;
 }
@@ -684,13 +705,14 @@ extern "C" {
 
 prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
                              int D, float sm_scale, const uint32_t* bits_q,
-                             const uint64_t* tile_bits, void* o, float* lse,
+                             const uint64_t* tile_bits, void* o, void* o_lo, float* lse,
                              cudaStream_t stream) {
   PRISM_CHECK_ARG(q && k && v && bits_q && tile_bits && o && lse, "prism_bsa_fwd: null pointer");
   PRISM_CHECK_ARG(S > 0 && S % 128 == 0 && heads >= 1, "prism_bsa_fwd: S must be a positive multiple of 128");
   PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o), "prism_bsa_fwd: tensors must be 16-byte aligned");
-  if (D == 128) return mma::launch_fwd<128>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, lse, stream);
-  if (D == 64) return mma::launch_fwd<64>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, lse, stream);
+  PRISM_CHECK_ARG(o_lo == nullptr || aligned16(o_lo), "prism_bsa_fwd: o_lo must be 16-byte aligned");
+  if (D == 128) return mma::launch_fwd<128>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
+  if (D == 64) return mma::launch_fwd<64>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
   set_error("prism_bsa_fwd: head dim %d not supported (64, 128)", D);
   return PRISM_ERR_UNSUPPORTED;
 }
@@ -703,12 +725,12 @@ size_t prism_bsa_bwd_workspace_bytes(int heads, int64_t S) {
   PRISM_CHECK_ARG(S > 0 && S % 128 == 0 && heads >= 1, name ": S must be a positive multiple of 128"); \
   PRISM_CHECK_ARG(D == 64 || D == 128, name ": head dim %d not supported (64, 128)", D)
 
-prism_status_t prism_bsa_bwd_delta(const void* o, const void* dout, int heads, int64_t S, int D,
-                                   float* delta, cudaStream_t stream) {
+prism_status_t prism_bsa_bwd_delta(const void* o, const void* o_lo, const void* dout, int heads,
+                                   int64_t S, int D, float* delta, cudaStream_t stream) {
   PRISM_CHECK_ARG(o && dout && delta, "prism_bsa_bwd_delta: null pointer");
   PRISM_BWD_COMMON_CHECKS("prism_bsa_bwd_delta");
-  return D == 128 ? mma::launch_delta<128>(o, dout, heads, S, delta, stream)
-                  : mma::launch_delta<64>(o, dout, heads, S, delta, stream);
+  return D == 128 ? mma::launch_delta<128>(o, o_lo, dout, heads, S, delta, stream)
+                  : mma::launch_delta<64>(o, o_lo, dout, heads, S, delta, stream);
 }
 
 prism_status_t prism_bsa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout,
@@ -737,13 +759,14 @@ prism_status_t prism_bsa_bwd_dq(const void* q, const void* k, const void* v, con
 }
 
 prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const void* o,
-                             const void* dout, const float* lse, int heads, int64_t S, int D,
+                             const void* o_lo, const void* dout, const float* lse, int heads,
+                             int64_t S, int D,
                              float sm_scale, const uint32_t* bits_q, const uint32_t* bits_k,
                              const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
                              void* dv, cudaStream_t stream) {
   PRISM_CHECK_ARG(workspace, "prism_bsa_bwd: null pointer");
   float* delta = (float*)workspace;
-  prism_status_t st = prism_bsa_bwd_delta(o, dout, heads, S, D, delta, stream);
+  prism_status_t st = prism_bsa_bwd_delta(o, o_lo, dout, heads, S, D, delta, stream);
   if (st != PRISM_OK) return st;
   st = prism_bsa_bwd_dkdv(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_k, tile_bits, dk, dv, stream);
   if (st != PRISM_OK) return st;

@@ -280,7 +280,7 @@ __device__ float block_max_f(float v, float* red) {
 
 // One CTA; one thread per zone (strided).  Per-zone intermediates in shared
 // memory: rho_raw, aniso[3], abar, vhat[3].
-__global__ void shape_select_kernel(const float* __restrict__ packed,
+__global__ void __launch_bounds__(512) shape_select_kernel(const float* __restrict__ packed,
                                     const uint8_t* __restrict__ axis_valid,
                                     const float* __restrict__ audio, int has_audio, int Nz, int D,
                                     int method, float lambda_a, float tau_128, float lambda_128,
@@ -434,7 +434,7 @@ __device__ __forceinline__ void local_coords(int c, int r, int& lt, int& lh, int
 }
 
 // One CTA of 1024 threads: exclusive scan of blocks-per-zone, then tile maps.
-__global__ void block_map_kernel(const int64_t* __restrict__ shape_ids, int Nz,
+__global__ void __launch_bounds__(1024) block_map_kernel(const int64_t* __restrict__ shape_ids, int Nz,
                                  int32_t* __restrict__ block_of_tile,
                                  int32_t* __restrict__ block_tiles, int32_t* __restrict__ n_blocks) {
   __shared__ int warp_sums[32];
@@ -1038,7 +1038,7 @@ prism_status_t prism_shape_select(const float* packed, const uint8_t* axis_valid
   if (smem > 48 * 1024)
     PRISM_CHECK_CUDA(cudaFuncSetAttribute(shape_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                      "prism_shape_select: smem attribute");
-  shape_select_kernel<<<1, 1024, smem, stream>>>(packed, axis_valid, audio, has_audio, Nz, D, method,
+  shape_select_kernel<<<1, 512, smem, stream>>>(packed, axis_valid, audio, has_audio, Nz, D, method,
                                                  lambda_a, tau_128, lambda_128, shape_ids, g_out,
                                                  rho_out);
   PRISM_CHECK_LAUNCH("prism_shape_select");

@@ -79,10 +79,11 @@ class _DynBsaFunction(torch.autograd.Function):
         bits_q, bits_k = ops.block_select(q_re, k_re, plan.layout, plan.tile_bits, plan.sparsity,
                                           plan.cdf_threshold)
         plan.bits_q, plan.bits_k = bits_q, bits_k
-        o_re, lse = ops.bsa_fwd(q_re, k_re, v_re, bits_q, plan.tile_bits, plan.sm_scale)
+        o_re, lse, o_lo = ops.bsa_fwd(q_re, k_re, v_re, bits_q, plan.tile_bits, plan.sm_scale,
+                                      want_lo=True)
         out, out_hsd = _new_like_layout(heads, S, D, layout, q.dtype, q.device)
         ops.scatter_rows(o_re, plan.grid, plan.grid_padded, plan.inv_idx, out=out_hsd)
-        ctx.save_for_backward(q_re, k_re, v_re, o_re, lse, bits_q, bits_k)
+        ctx.save_for_backward(q_re, k_re, v_re, o_re, o_lo, lse, bits_q, bits_k)
         ctx.plan = plan
         ctx.layout = layout
         ctx.shape = (heads, S, D)
@@ -90,13 +91,13 @@ class _DynBsaFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout):
-        q_re, k_re, v_re, o_re, lse, bits_q, bits_k = ctx.saved_tensors
+        q_re, k_re, v_re, o_re, o_lo, lse, bits_q, bits_k = ctx.saved_tensors
         plan = ctx.plan
         layout = ctx.layout
         heads, S, D = ctx.shape
         do_re = ops.gather_rows(_hsd(dout, layout), plan.grid, plan.grid_padded, plan.src_idx)
         dq_re, dk_re, dv_re = ops.bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k,
-                                          plan.tile_bits, plan.sm_scale)
+                                          plan.tile_bits, plan.sm_scale, o_lo=o_lo)
         grads = []
         for g_re in (dq_re, dk_re, dv_re):
             g, g_hsd = _new_like_layout(heads, S, D, layout, dout.dtype, dout.device)

@@ -192,24 +192,29 @@ def block_select(q_re, k_re, layout, tile_bits, sparsity, cdf_threshold):
 
 
 # -------------------------------------------------------------- a15/a16
-def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float):
+def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float, want_lo: bool = False):
+    """Returns (o, lse) or (o, lse, o_lo) with o_lo the bf16 rounding residual of o."""
     _check_cuda(q_re, k_re, v_re)
     heads, S, D = q_re.shape
     o = torch.empty_like(q_re)
+    o_lo = torch.empty_like(q_re) if want_lo else None
     lse = torch.empty(heads, S, dtype=torch.float32, device=q_re.device)
     _lib.call("prism_bsa_fwd", _p(q_re), _p(k_re), _p(v_re), heads, S, D, float(sm_scale),
-              _p(bits_q), _p(tile_bits), _p(o), _p(lse), _stream(q_re))
+              _p(bits_q), _p(tile_bits), _p(o), _p(o_lo), _p(lse), _stream(q_re))
+    if want_lo:
+        return o, lse, o_lo
     return o, lse
 
 
-def bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k, tile_bits, sm_scale: float):
+def bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k, tile_bits, sm_scale: float,
+            o_lo=None):
     _check_cuda(q_re, do_re)
     heads, S, D = q_re.shape
     dq = torch.empty_like(q_re)
     dk = torch.empty_like(k_re)
     dv = torch.empty_like(v_re)
     ws = _ws(_lib.query("prism_bsa_bwd_workspace_bytes", heads, S), q_re.device)
-    _lib.call("prism_bsa_bwd", _p(q_re), _p(k_re), _p(v_re), _p(o_re), _p(do_re), _p(lse), heads, S,
-              D, float(sm_scale), _p(bits_q), _p(bits_k), _p(tile_bits), _p(ws), _p(dq), _p(dk),
+    _lib.call("prism_bsa_bwd", _p(q_re), _p(k_re), _p(v_re), _p(o_re), _p(o_lo), _p(do_re), _p(lse),
+              heads, S, D, float(sm_scale), _p(bits_q), _p(bits_k), _p(tile_bits), _p(ws), _p(dq), _p(dk),
               _p(dv), _stream(q_re))
     return dq, dk, dv

@@ -39,7 +39,7 @@ def test_error_channel_without_gpu():
     assert L.prism_abi_version() >= 1
     # invalid arguments are rejected on the host before any CUDA call
     rc = L.prism_bsa_fwd(None, None, None, 1, 128, 128, ctypes.c_float(0.1), None, None, None,
-                         None, None)
+                         None, None, None)
     assert rc != 0
     assert b"null pointer" in L.prism_last_error()
     rc = L.prism_shape_select(None, None, None, 0, 1, 64, 7, ctypes.c_float(0.5),

@@ -88,7 +88,12 @@ def test_selection_pipeline_bit_exact(name, cuda):
     if name in CASES and valid is not None:
         nt = src.size // 64
         ref = O.bits_to_dense(load_fixture(name)["sel_bits"], nt)
-        assert np.array_equal(O.bits_to_dense(o_bq, nt), ref)
+        # rows of padding-only query blocks tie on every score; the reference's
+        # choice there is torch.topk's unspecified tie order (see test_oracle_golden)
+        tile_cnt = vre.reshape(-1, 64).sum(1)
+        blk_cnt = np.array([sum(tile_cnt[j] for j in bt[b] if j < nt) for b in range(nbk)])
+        real = blk_cnt[bot] > 0
+        assert np.array_equal(O.bits_to_dense(o_bq, nt)[:, real], ref[:, real])
     # determinism: a second run is bit-identical
     bq2, _ = ops.block_select(q_re, k_re, lay, tb, case.sparsity, case.cdf_threshold)
     assert torch.equal(bq, bq2)

@@ -2,7 +2,13 @@
 (tests/golden/make_golden.py ran the reference's Python/Triton code on CPU).
 
 * token norms, shape ids, permutation and the tile-level selection must be
-  identical to the reference's;
+  identical to the reference's.  One documented exception: a query block made
+  only of padding tokens has pooled q = 0, so every one of its block scores
+  ties and the reference's choice among them is torch.topk's unspecified tie
+  order (ours: lower block index first).  Such rows are sliced off by the
+  caller and carry zero gradient, so the comparison covers every query tile
+  of a block with at least one real token, and attention outputs are
+  compared on real tokens;
 * g / rho (zone statistics -> effective gradient) agree to float rounding;
 * the float64 attention restatement agrees with the reference's fp32 Triton
   kernels (run under TRITON_INTERPRET) to ~1e-5.
@@ -20,6 +26,16 @@ MASKED = [n for n, c in CASES.items() if c.needs_pad]
 def _b(t):
     import torch
     return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def real_q_tiles(r):
+    """q tiles whose logical block holds at least one real (non-padding) token."""
+    vre = np.ones(r["src_idx"].size, np.uint8) if r["valid_re"] is None else r["valid_re"]
+    tile_cnt = vre.reshape(-1, 64).sum(1)
+    bt = r["block_tiles"]
+    nt = tile_cnt.size
+    blk_cnt = np.array([sum(tile_cnt[j] for j in bt[b] if j < nt) for b in range(r["nb"])])
+    return blk_cnt[r["block_of_tile"]] > 0
 
 
 def _run(name):
@@ -69,7 +85,9 @@ def test_selection_exact(name):
     mine = O.bits_to_dense(r["bits_q"], nt)
     if valid is not None:
         ref = O.bits_to_dense(fx["sel_bits"], nt)
-        assert (mine == ref).all(), f"{(mine != ref).sum()} of {ref.sum()} tile pairs differ"
+        real = real_q_tiles(r)
+        assert (mine[:, real] == ref[:, real]).all(), \
+            f"{(mine[:, real] != ref[:, real]).sum()} of {ref[:, real].sum()} tile pairs differ"
     else:
         # unmasked grid: the oracle (and the CUDA path) pool and score in fp32, as the
         # reference does whenever padding exists; the reference's own unmasked branch
@@ -92,8 +110,11 @@ def test_attention_restatement(name):
     do_re = f(do)[:, r["src_idx"]]
     dq, dk, dv = O.bsa_backward(qr, kr, vr, o, do_re, r["bits_q"], r["valid_re"])
     inv, rows = r["inv_idx"], fx["rows"]
+    real_rows = valid[rows].astype(bool)
     for nm, x in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
         ref = fx[nm]
         got = x[:, inv][:, rows]
+        if nm == "o":
+            ref, got = ref[:, real_rows], got[:, real_rows]
         err = np.abs(got - ref).max()
         assert err <= 1e-5 * max(1.0, np.abs(ref).max()), (nm, err)
