@@ -175,6 +175,34 @@ prism_status_t prism_bsa_bwd_dq(const void* q, const void* k, const void* v, con
                                 float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
                                 void* dq, cudaStream_t stream);
 
+/* Backward without any device allocation -- no counterpart in the reference,
+ * which always runs inside PyTorch's allocator.
+ *
+ * Some callers cannot allocate device memory at the moment they run the
+ * backward: an inference or training engine that plans every byte up front
+ * and forbids allocation while a step executes, a plugin hosted by a runtime
+ * that owns the device pool, or code that must not call cudaMalloc because it
+ * would synchronise the device mid-step.  This entry point takes the same
+ * inputs and outputs as prism_bsa_bwd (minus `workspace`) and keeps its only
+ * scratch, the per-row delta, in a fixed array compiled into the library:
+ *   - limit: heads * S <= PRISM_BSA_BWD_NOALLOC_MAX_ROWS query rows (16 MiB of
+ *     scratch, reserved on every GPU that loads the library until exit);
+ *     larger calls return PRISM_ERR_INVALID_ARG;
+ *   - it calls no cudaMalloc / cudaFree and no allocating library routine;
+ *   - the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture;
+ *   - all calls share the one array: calls whose kernels overlap on the GPU
+ *     (different streams, or different host threads) race and must be
+ *     serialised by the caller.  The array keeps the last call's contents;
+ *     every value a call reads is first written by that same call. */
+#define PRISM_BSA_BWD_NOALLOC_MAX_ROWS (4u << 20)
+prism_status_t prism_bsa_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                     const void* o_lo, const void* dout, const float* lse,
+                                     int heads, int64_t S, int D, float sm_scale,
+                                     const uint32_t* bits_q, const uint32_t* bits_k,
+                                     const uint64_t* tile_bits, void* dq, void* dk, void* dv,
+                                     cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,7 @@ SIGNATURES = {
     "prism_bsa_bwd_delta": (_I, [_P, _P, _P, _I, _I64, _I, _P, _P]),
     "prism_bsa_bwd_dkdv": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P]),
+    "prism_bsa_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P]),
 }
 
 # kernels launched per entry point (the bench's gpu_launches count)
@@ -46,6 +47,7 @@ KERNELS = {
     "prism_build_layout": 2, "prism_tile_valid": 1, "prism_gather_rows": 1,
     "prism_scatter_rows": 1, "prism_block_select": 4, "prism_bsa_fwd": 1, "prism_bsa_bwd": 3,
     "prism_bsa_bwd_delta": 1, "prism_bsa_bwd_dkdv": 1, "prism_bsa_bwd_dq": 1,
+    "prism_bsa_bwd_noalloc": 3,
 }
 launch_count = 0
 

@@ -19,6 +19,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "prism_common.cuh"
 
 namespace prism {
@@ -774,3 +776,64 @@ prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const 
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------
+// Backward without any device allocation (prism_bsa_bwd_noalloc).
+//
+// The only scratch the backward needs is delta[h][s] (one float per query
+// row).  Here it lives in a file-scope device array of a fixed size, so the
+// caller passes inputs and outputs only.  The array is part of this library's
+// device image: every GPU that loads the library reserves it until the
+// process exits.  Host code cannot use the array's name as a device address
+// (on the host it names a stand-in object), so its real address is looked up
+// with cudaGetSymbolAddress, once per device, with that device current, on
+// the first call made on that device.
+namespace prism {
+namespace mma {
+static __device__ __align__(256) float g_noalloc_delta[PRISM_BSA_BWD_NOALLOC_MAX_ROWS];
+}  // namespace mma
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_addr[128] = {nullptr};
+
+static prism_status_t noalloc_scratch(float** out) {
+  int dev = -1;
+  PRISM_CHECK_CUDA(cudaGetDevice(&dev), "prism_bsa_bwd_noalloc: cudaGetDevice");
+  PRISM_CHECK_ARG(dev >= 0 && dev < 128, "prism_bsa_bwd_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, mma::g_noalloc_delta);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("prism_bsa_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      return PRISM_ERR_CUDA;
+    }
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return PRISM_OK;
+}
+}  // namespace prism
+
+extern "C" prism_status_t prism_bsa_bwd_noalloc(
+    const void* q, const void* k, const void* v, const void* o, const void* o_lo, const void* dout,
+    const float* lse, int heads, int64_t S, int D, float sm_scale, const uint32_t* bits_q,
+    const uint32_t* bits_k, const uint64_t* tile_bits, void* dq, void* dk, void* dv,
+    cudaStream_t stream) {
+  PRISM_CHECK_ARG(heads >= 1 && S > 0, "prism_bsa_bwd_noalloc: heads and S must be positive");
+  PRISM_CHECK_ARG((uint64_t)heads * (uint64_t)S <= (uint64_t)PRISM_BSA_BWD_NOALLOC_MAX_ROWS,
+                  "prism_bsa_bwd_noalloc: heads*S = %lld query rows exceed the built-in scratch "
+                  "of %u rows; use prism_bsa_bwd with a caller-provided workspace",
+                  (long long)heads * (long long)S, (unsigned)PRISM_BSA_BWD_NOALLOC_MAX_ROWS);
+  float* delta = nullptr;
+  const prism_status_t st0 = noalloc_scratch(&delta);
+  if (st0 != PRISM_OK) return st0;
+  // Every delta row is written by the first stage before the other two read
+  // it, so nothing left in the array by an earlier call is ever used.
+  prism_status_t st = prism_bsa_bwd_delta(o, o_lo, dout, heads, S, D, delta, stream);
+  if (st != PRISM_OK) return st;
+  st = prism_bsa_bwd_dkdv(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  if (st != PRISM_OK) return st;
+  return prism_bsa_bwd_dq(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_q, tile_bits, dq, stream);
+}
