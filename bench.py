@@ -274,7 +274,11 @@ def main():
     ap.add_argument("--impl", default="prism", choices=["prism", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heads", type=int, default=CONFIG["heads"],
+                    help="attention heads of the layer (40 in BASELINE config 1; smaller only "
+                         "for profiler captures)")
     args = ap.parse_args()
+    CONFIG["heads"] = args.heads
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
