@@ -45,6 +45,13 @@ typedef enum {
 const char* prism_last_error(void);
 /* ABI version (incremented on any signature change). */
 int prism_abi_version(void);
+/* Device-side status of the attention kernels: 0 when every bounded wait
+ * inside them completed, otherwise the code of the first wait that gave up
+ * (the kernel then drained its in-flight copies, released its tensor memory
+ * and returned without finishing its outputs).  Reading the status
+ * synchronises with the device and resets it to 0; -1 = the read failed.
+ * No counterpart in the reference (Triton kernels have no device-side waits). */
+int prism_device_status(void);
 
 /* Per-token L2 norm of the audio->video bridge residual, bf16 in/out, fp32
  * accumulation.  Replaces `a2v_bridge_residual.norm(dim=-1)`

@@ -219,7 +219,7 @@ def bsa_forward(q, k, v, bits_q, valid_re, sm_scale=None):
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     m = token_mask(bits_q, valid_re, S)
-    s = np.einsum("hid,hjd->hij", q, k) * sm_scale
+    s = np.matmul(q, k.transpose(0, 2, 1)) * sm_scale
     s = np.where(m, s, -np.inf)
     mx = s.max(-1, keepdims=True)
     empty = ~np.isfinite(mx)
@@ -227,7 +227,7 @@ def bsa_forward(q, k, v, bits_q, valid_re, sm_scale=None):
     p = np.exp(s - mx)
     l = p.sum(-1, keepdims=True)
     lsafe = np.where(l > 0, l, 1.0)
-    o = np.einsum("hij,hjd->hid", p / lsafe, v)
+    o = np.matmul(p / lsafe, v)
     lse = np.where(empty[..., 0], -np.inf, (mx + np.log(lsafe))[..., 0])
     return o, lse
 
@@ -245,7 +245,7 @@ def bsa_backward(q, k, v, o, do, bits_q, valid_re, sm_scale=None):
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     m = token_mask(bits_q, valid_re, S)
-    s = np.einsum("hid,hjd->hij", q, k) * sm_scale
+    s = np.matmul(q, k.transpose(0, 2, 1)) * sm_scale
     s = np.where(m, s, -np.inf)
     mx = s.max(-1, keepdims=True)
     mx = np.where(np.isfinite(mx), mx, 0.0)
@@ -253,11 +253,11 @@ def bsa_backward(q, k, v, o, do, bits_q, valid_re, sm_scale=None):
     l = p.sum(-1, keepdims=True)
     p = p / np.where(l > 0, l, 1.0)
     delta = (o * do).sum(-1, keepdims=True)
-    dp = np.einsum("hid,hjd->hij", do, v)
+    dp = np.matmul(do, v.transpose(0, 2, 1))
     ds = p * (dp - delta)
-    dq = np.einsum("hij,hjd->hid", ds, k) * sm_scale
-    dk = np.einsum("hij,hid->hjd", ds, q) * sm_scale
-    dv = np.einsum("hij,hid->hjd", p, do)
+    dq = np.matmul(ds, k) * sm_scale
+    dk = np.matmul(ds.transpose(0, 2, 1), q) * sm_scale
+    dv = np.matmul(p.transpose(0, 2, 1), do)
     return dq, dk, dv
 
 

@@ -23,7 +23,7 @@ COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path
           "--expt-relaxed-constexpr"]
 SOURCES = {
     "select_kernels.cu": ["-fmad=false"],
-    "bsa_mma.cu": [],
+    "bsa_tc.cu": [],
 }
 
 

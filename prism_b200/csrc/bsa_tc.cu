@@ -1,0 +1,1315 @@
+// Block-sparse attention forward / backward on the sm_100a tensor cores
+// (tcgen05.mma, accumulators in TMEM, operands staged by TMA in 128B-swizzled
+// shared memory).
+//
+// Work decomposition.  Tokens are in tile order (64-token tiles, zone by
+// zone).  A CTA owns 128 rows = the tile pair (2p, 2p+1) of one head and walks
+// the union of the two tiles' selection bitmap rows in increasing tile order;
+// rows of the half that did not select a tile get p = 0 for it, so the result
+// is exactly the per-tile sparse attention of the reference.
+//
+//   forward   CTA = 128 queries; per step two selected key tiles (N = 128):
+//             S = Q K^T -> TMEM, online softmax in registers (one thread per
+//             query row), P (bf16) -> smem, O += P V in TMEM.
+//   dK / dV   CTA = 128 keys; per step one query tile (N = 64) of the
+//             transposed selection: S^T = K Q^T, dP^T = V dO^T -> TMEM,
+//             P^T and dS^T = P^T (dP^T - delta) -> smem, dV += P^T dO,
+//             dK += dS^T Q in TMEM.
+//   dQ        CTA = 128 queries; per step one key tile: S = Q K^T,
+//             dP = dO V^T -> TMEM, dS -> smem, dQ += dS K in TMEM.
+//
+// Warp roles (192 threads): warps 0-3 = softmax / epilogue (thread i owns
+// TMEM lane i = row i of the CTA), warp 4 = TMA producer, warp 5 = MMA
+// issuer (one thread) and TMEM owner.  Producer, MMA issuer and softmax warps
+// all walk the same bitmap union, so they agree on the sequence of tiles
+// without exchanging it.
+//
+// Numerics follow the reference Triton kernels
+// (hymm/models/modules/block_sparse_attention/flash_attn_bsa_varlen_mask.py:
+// 193-319 forward, 564-704 dK/dV, 881-1014 dQ; common.py:94-111 delta):
+// scores in log2 units s * sm_scale * log2(e); initial state m = -inf, l = 1;
+// masked keys get p = 0; lse stored in natural-log units; dK and dQ scaled by
+// sm_scale.  The forward keeps a running maximum that is only raised when the
+// new block maximum exceeds it by more than 2^8 (the rescale of O in TMEM is
+// then rare); p = exp2(s - m) <= 256 stays exact in fp32 and is rounded to
+// bf16 for P V exactly as the reference rounds p.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "prism_common.cuh"
+#include "sm100.cuh"
+
+namespace prism {
+namespace tc {
+
+using namespace sm100;
+
+constexpr float kLn2 = 0.6931471824645996f;
+constexpr float kRcpLn2 = 1.4426950408889634f;
+constexpr int kThreads = 192;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+// Device error word: 0 = ok, otherwise the code of the first bounded wait that
+// gave up (see prism_device_status).
+__device__ int g_tc_error = 0;
+
+enum WaitCode : int {
+  kErrFwdProducer = 101, kErrFwdMma = 102, kErrFwdSoftmax = 103,
+  kErrDkdvProducer = 201, kErrDkdvMma = 202, kErrDkdvSoftmax = 203,
+  kErrDqProducer = 301, kErrDqMma = 302, kErrDqSoftmax = 303,
+};
+
+// Union iterator over two bitmap rows (global memory, read through the
+// read-only cache).  Every role of a CTA runs its own copy and sees the same
+// sequence: increasing tile index.
+struct UnionIter {
+  const uint32_t* ra;
+  const uint32_t* rb;
+  int wq, wi;
+  uint32_t a, b;
+  __device__ __forceinline__ void init(const uint32_t* row_a, const uint32_t* row_b, int n) {
+    ra = row_a;
+    rb = row_b;
+    wq = n;
+    wi = 0;
+    a = n > 0 ? __ldg(ra) : 0u;
+    b = n > 0 ? __ldg(rb) : 0u;
+  }
+  // next tile index, or -1; sel bit 0: first row selected it, bit 1: second row
+  __device__ __forceinline__ int next(int& sel) {
+    while ((a | b) == 0u) {
+      if (++wi >= wq) return -1;
+      a = __ldg(ra + wi);
+      b = __ldg(rb + wi);
+    }
+    const int bit = __ffs(a | b) - 1;
+    const uint32_t m = 1u << bit;
+    sel = ((a & m) ? 1 : 0) | ((b & m) ? 2 : 0);
+    a &= ~m;
+    b &= ~m;
+    return wi * 32 + bit;
+  }
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
+}
+
+// Warp-uniform bounded wait (every lane must agree before a .sync.aligned op).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int code) {
+  bool ok = mbar_wait(bar, parity, abort_flag, &g_tc_error, code);
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) *abort_flag = 1;
+  return ok;
+}
+
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+
+// 32 * N consecutive TMEM columns of this warp's 32 lanes -> registers (waited).
+template <int N>
+__device__ __forceinline__ void tmem_load(uint32_t taddr, float (&out)[32 * N]) {
+  uint32_t raw[N][32];
+#pragma unroll
+  for (int c = 0; c < N; ++c) tmem_ld32(taddr + c * 32, raw[c]);
+#pragma unroll
+  for (int c = 0; c < N; ++c) tmem_wait_ld_dep(raw[c]);
+#pragma unroll
+  for (int c = 0; c < N; ++c)
+#pragma unroll
+    for (int i = 0; i < 32; ++i) out[c * 32 + i] = u2f(raw[c][i]);
+}
+
+// Request at least this much dynamic shared memory so that a second CTA never
+// shares the SM (each CTA allocates 512 TMEM columns, the whole TMEM).
+constexpr size_t kMinSmem = 116 * 1024;
+
+// ===================================================================== forward
+template <int D>
+struct FwdLayout {
+  static constexpr int kRing = 4;                       // K tiles and V tiles in flight
+  static constexpr int kSub = D / 64;                   // 128-byte sub-buffers per row
+  static constexpr int Q = 0;                           // 128 rows
+  static constexpr int K = Q + kSub * 16384;            // kRing x 64 rows
+  static constexpr int V = K + kRing * kSub * 8192;
+  static constexpr int P = V + kRing * kSub * 8192;     // 128 rows x 128 keys bf16
+  static constexpr int BAR = P + 2 * 16384;
+  static constexpr int B_Q = 0, B_KF = 1, B_KE = B_KF + kRing, B_VF = B_KE + kRing,
+                       B_VE = B_VF + kRing, B_SF = B_VE + kRing, B_SE = B_SF + 2, B_PF = B_SE + 2,
+                       B_PV = B_PF + 1, B_DRAIN = B_PV + 1, NBAR = B_DRAIN + 1;
+  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
+  static constexpr int ABORT = TMEM_SLOT + 4;
+  static constexpr size_t kBytes = 1024 + ABORT + 4;
+  static constexpr int T_S = 0;      // S[b] at 128 b, 128 columns each
+  static constexpr int T_O = 256;    // O, D columns
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, int64_t S, int wq, float qk_scale,
+                  const uint32_t* __restrict__ bits_q, const uint64_t* __restrict__ tile_bits,
+                  __nv_bfloat16* __restrict__ o, __nv_bfloat16* __restrict__ o_lo,
+                  float* __restrict__ lse) {
+  using L = FwdLayout<D>;
+  constexpr int R = L::kRing;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const uint32_t sb = smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x, h = blockIdx.y;
+  const int64_t n_tiles = S / 64;
+  const int row_base = (int)((int64_t)h * S + (int64_t)pair * 128);  // row of [heads*S, D]
+  const int head_row = (int)((int64_t)h * S);
+  auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
+  const uint32_t* row_a = bits_q + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
+  const uint32_t* row_b = row_a + wq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::B_Q), 1);
+    for (int i = 0; i < R; ++i) {
+      mbar_init(bar(L::B_KF + i), 1);
+      mbar_init(bar(L::B_KE + i), 1);
+      mbar_init(bar(L::B_VF + i), 1);
+      mbar_init(bar(L::B_VE + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(L::B_SF + i), 1);
+      mbar_init(bar(L::B_SE + i), 4);
+    }
+    mbar_init(bar(L::B_PF), 4);
+    mbar_init(bar(L::B_PV), 1);
+    mbar_init(bar(L::B_DRAIN), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(sb + L::TMEM_SLOT, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_expect_tx(bar(L::B_Q), 128 * D * 2);
+#pragma unroll
+      for (int s = 0; s < L::kSub; ++s)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+          tma_load_2d(sb + L::Q + s * 16384 + r * 8192, &tm_q, s * 64, row_base + r * 64, bar(L::B_Q));
+      UnionIter it;
+      it.init(row_a, row_b, wq);
+      int nk = 0, nv = 0, sel = 0, t;
+      while ((t = it.next(sel)) >= 0) {
+        const int st = nk % R;
+        if (nk >= R && !mbar_wait(bar(L::B_KE + st), ((nk / R) - 1) & 1, abort_flag, &g_tc_error,
+                                  kErrFwdProducer))
+          break;
+        mbar_expect_tx(bar(L::B_KF + st), 64 * D * 2);
+#pragma unroll
+        for (int s = 0; s < L::kSub; ++s)
+          tma_load_2d(sb + L::K + st * L::kSub * 8192 + s * 8192, &tm_k, s * 64, head_row + t * 64,
+                      bar(L::B_KF + st));
+        ++nk;
+        if (nv >= R && !mbar_wait(bar(L::B_VE + st), ((nv / R) - 1) & 1, abort_flag, &g_tc_error,
+                                  kErrFwdProducer))
+          break;
+        mbar_expect_tx(bar(L::B_VF + st), 64 * D * 2);
+#pragma unroll
+        for (int s = 0; s < L::kSub; ++s)
+          tma_load_2d(sb + L::V + st * L::kSub * 8192 + s * 8192, &tm_v, s * 64, head_row + t * 64,
+                      bar(L::B_VF + st));
+        ++nv;
+      }
+      // drain: every issued load has landed before the CTA may exit
+      for (int m = (nk > R ? nk - R : 0); m < nk; ++m)
+        mbar_wait(bar(L::B_KF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrFwdProducer);
+      for (int m = (nv > R ? nv - R : 0); m < nv; ++m)
+        mbar_wait(bar(L::B_VF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrFwdProducer);
+      mbar_wait(bar(L::B_Q), 0, abort_flag, &g_tc_error, kErrFwdProducer);
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t IDESC_PV = idesc_bf16(128, D, false, true);
+      bool ok = mbar_wait(bar(L::B_Q), 0, abort_flag, &g_tc_error, kErrFwdMma);
+      tc_fence_after();
+      UnionIter it;
+      it.init(row_a, row_b, wq);
+      int n = 0, iter = 0, prev_cnt = 0, prev_n = 0;
+      auto issue_pv = [&](int j, int cnt, int n0) -> bool {
+        if (!mbar_wait(bar(L::B_PF), j & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
+        tc_fence_after();
+        for (int u = 0; u < cnt; ++u) {
+          const int st = (n0 + u) % R;
+          if (!mbar_wait(bar(L::B_VF + st), ((n0 + u) / R) & 1, abort_flag, &g_tc_error, kErrFwdMma))
+            return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k16 = 0; k16 < 4; ++k16) {
+            const uint64_t a = desc_k_sw128(sb + L::P + u * 16384 + k16 * 32);
+            const uint64_t b = desc_mn_sw128(sb + L::V + st * L::kSub * 8192 + k16 * 2048, 8192);
+            mma_bf16(tmem + L::T_O, a, b, IDESC_PV, (j > 0 || u > 0 || k16 > 0) ? 1u : 0u);
+          }
+          mma_commit(bar(L::B_VE + st));
+        }
+        mma_commit(bar(L::B_PV));
+        return true;
+      };
+      while (ok) {
+        int sel0 = 0, sel1 = 0;
+        const int t0 = it.next(sel0);
+        if (t0 < 0) break;
+        const int t1 = it.next(sel1);
+        const int cnt = t1 >= 0 ? 2 : 1;
+        const int b = iter & 1;
+        if (iter >= 2 && !mbar_wait(bar(L::B_SE + b), ((iter >> 1) - 1) & 1, abort_flag, &g_tc_error,
+                                    kErrFwdMma)) {
+          ok = false;
+          break;
+        }
+        for (int u = 0; u < cnt; ++u) {
+          const int st = (n + u) % R;
+          if (!mbar_wait(bar(L::B_KF + st), ((n + u) / R) & 1, abort_flag, &g_tc_error, kErrFwdMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t a = desc_k_sw128(sb + L::Q + (kk >> 2) * 16384 + (kk & 3) * 32);
+            const uint64_t bd =
+                desc_k_sw128(sb + L::K + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
+            mma_bf16(tmem + L::T_S + b * 128 + u * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar(L::B_KE + st));
+        }
+        if (!ok) break;
+        mma_commit(bar(L::B_SF + b));
+        if (iter >= 1 && !issue_pv(iter - 1, prev_cnt, prev_n)) {
+          ok = false;
+          break;
+        }
+        prev_cnt = cnt;
+        prev_n = n;
+        n += cnt;
+        ++iter;
+        if (t1 < 0) break;
+      }
+      if (ok && iter >= 1) issue_pv(iter - 1, prev_cnt, prev_n);
+      // drain: all issued MMAs complete before TMEM is released
+      mma_commit(bar(L::B_DRAIN));
+      mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrFwdMma);
+    }
+  } else {
+    // ------------------------------------------------------ softmax warps
+    const int r = threadIdx.x;  // row within the CTA == TMEM lane
+    const int half = r >> 6;
+    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+    float m = -INFINITY, l = 1.0f;
+    UnionIter it;
+    it.init(row_a, row_b, wq);
+    int iter = 0;
+    bool ok = true;
+    uint8_t* sP = sm + L::P;
+    for (;;) {
+      int sel0 = 0, sel1 = 0;
+      const int t0 = it.next(sel0);
+      if (t0 < 0) break;
+      const int t1 = it.next(sel1);
+      const int b = iter & 1;
+      if (!warp_wait(bar(L::B_SF + b), (iter >> 1) & 1, abort_flag, kErrFwdSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+      {
+        float* s0 = s;
+        tmem_load<2>(t_lane + L::T_S + b * 128, *reinterpret_cast<float(*)[64]>(s0));
+        if (t1 >= 0) tmem_load<2>(t_lane + L::T_S + b * 128 + 64, *reinterpret_cast<float(*)[64]>(s0 + 64));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_SE + b));
+      // masks: row did not select the tile -> all keys masked; else key validity
+      {
+        const uint64_t vb0 = ((sel0 >> half) & 1) ? tile_bits[t0] : 0ull;
+        if (vb0 != ~0ull) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (!((vb0 >> c) & 1ull)) s[c] = -INFINITY;
+        }
+        const uint64_t vb1 = (t1 >= 0 && ((sel1 >> half) & 1)) ? tile_bits[t1] : 0ull;
+        if (vb1 != ~0ull) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (!((vb1 >> c) & 1ull)) s[64 + c] = -INFINITY;
+        }
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int c = 4; c < 128; c += 4) {
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
+        mx2 = fmaxf(mx2, s[c + 2]);
+        mx3 = fmaxf(mx3, s[c + 3]);
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * qk_scale;
+      const bool need = mx > m + kRescaleThreshold;  // m = -inf: any valid key
+      bool waited_pv = false;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_new = need ? mx : m;
+        const float alpha = need ? ex2(m - m_new) : 1.0f;  // m = -inf -> 0
+        const bool o_live = __any_sync(0xffffffffu, need && m != -INFINITY);
+        l *= alpha;
+        m = m_new;
+        if (iter > 0 && o_live) {
+          if (!warp_wait(bar(L::B_PV), (iter - 1) & 1, abort_flag, kErrFwdSoftmax)) {
+            ok = false;
+            break;
+          }
+          waited_pv = true;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t raw[32];
+            tmem_ld32(t_lane + L::T_O + c * 32, raw);
+            tmem_wait_ld_dep(raw);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
+            tmem_st32(t_lane + L::T_O + c * 32, raw);
+          }
+          tmem_wait_st();
+        }
+      }
+      const float mb = (m == -INFINITY) ? 0.0f : m;
+      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 128; c += 4) {
+        const float p0 = ex2(fmaf(s[c], qk_scale, -mb));
+        const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mb));
+        const float p2 = ex2(fmaf(s[c + 2], qk_scale, -mb));
+        const float p3 = ex2(fmaf(s[c + 3], qk_scale, -mb));
+        sum0 += p0;
+        sum1 += p1;
+        sum2 += p2;
+        sum3 += p3;
+        pk[c / 2] = pack_bf16(p0, p1);
+        pk[c / 2 + 1] = pack_bf16(p2, p3);
+      }
+      l += (sum0 + sum1) + (sum2 + sum3);
+      if (iter > 0 && !waited_pv) {
+        if (!warp_wait(bar(L::B_PV), (iter - 1) & 1, abort_flag, kErrFwdSoftmax)) {
+          ok = false;
+          break;
+        }
+      }
+      // P row -> two 128B-swizzled sub-buffers (keys 0-63 and 64-127)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const uint4 v4 = make_uint4(pk[u * 32 + ch * 4], pk[u * 32 + ch * 4 + 1],
+                                      pk[u * 32 + ch * 4 + 2], pk[u * 32 + ch * 4 + 3]);
+          *reinterpret_cast<uint4*>(sP + u * 16384 + sw128_off(r, ch)) = v4;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_PF));
+      ++iter;
+      if (t1 < 0) break;
+    }
+    // epilogue
+    const int64_t grow = (int64_t)row_base + r;
+    if (ok && iter > 0 && warp_wait(bar(L::B_PV), (iter - 1) & 1, abort_flag, kErrFwdSoftmax)) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(t_lane + L::T_O + c * 32, raw);
+        tmem_wait_ld_dep(raw);
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = u2f(raw[2 * i]) * inv, x1 = u2f(raw[2 * i + 1]) * inv;
+          hi[i] = pack_bf16(x0, x1);
+          lo[i] = pack_bf16(x0 - u2f(hi[i] << 16), x1 - u2f(hi[i] & 0xffff0000u));
+        }
+        uint4* dst = reinterpret_cast<uint4*>(o + grow * D + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(hi[4 * i], hi[4 * i + 1], hi[4 * i + 2], hi[4 * i + 3]);
+        if (o_lo != nullptr) {
+          uint4* dl = reinterpret_cast<uint4*>(o_lo + grow * D + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dl[i] = make_uint4(lo[4 * i], lo[4 * i + 1], lo[4 * i + 2], lo[4 * i + 3]);
+        }
+      }
+      lse[grow] = (m + __log2f(l)) * kLn2;
+    } else if (ok && iter == 0) {
+      // no selected tile at all: O = 0, lse = -inf (m = -inf, l = 1)
+      uint4* dst = reinterpret_cast<uint4*>(o + grow * D);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+      if (o_lo != nullptr) {
+        uint4* dl = reinterpret_cast<uint4*>(o_lo + grow * D);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) dl[i] = make_uint4(0, 0, 0, 0);
+      }
+      lse[grow] = -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ================================================================== dK / dV
+template <int D>
+struct DkdvLayout {
+  static constexpr int kRing = 3;
+  static constexpr int kSub = D / 64;
+  static constexpr int K = 0;                              // 128 keys
+  static constexpr int V = K + kSub * 16384;
+  static constexpr int Q = V + kSub * 16384;               // kRing x 64 queries
+  static constexpr int DO = Q + kRing * kSub * 8192;
+  static constexpr int PT = DO + kRing * kSub * 8192;      // 2 x (128 keys x 64 queries)
+  static constexpr int DST = PT + 2 * 16384;
+  static constexpr int M = DST + 2 * 16384;                // kRing x 64 f32 (lse)
+  static constexpr int DL = M + kRing * 256;               // kRing x 64 f32 (delta)
+  static constexpr int BAR = DL + kRing * 256;
+  static constexpr int B_KV = 0, B_QF = 1, B_QE = 1 + kRing, B_SF = 1 + 2 * kRing, B_SE = B_SF + 2,
+                       B_DF = B_SE + 2, B_DE = B_DF + 2, B_FIN = B_DE + 2, B_DRAIN = B_FIN + 1,
+                       NBAR = B_DRAIN + 1;
+  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
+  static constexpr int ABORT = TMEM_SLOT + 4;
+  static constexpr size_t kBytes = 1024 + ABORT + 4;
+  static constexpr int T_DK = 0, T_DV = D, T_S = 2 * D, T_DP = 2 * D + 128;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                   const float* __restrict__ lse, const float* __restrict__ delta, int64_t S, int wq,
+                   float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_k,
+                   const uint64_t* __restrict__ tile_bits, __nv_bfloat16* __restrict__ dk,
+                   __nv_bfloat16* __restrict__ dv) {
+  using L = DkdvLayout<D>;
+  constexpr int R = L::kRing;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const uint32_t sb = smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x, h = blockIdx.y;
+  const int64_t n_tiles = S / 64;
+  const int row_base = (int)((int64_t)h * S + (int64_t)pair * 128);
+  const int head_row = (int)((int64_t)h * S);
+  auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
+  const uint32_t* row_a = bits_k + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
+  const uint32_t* row_b = row_a + wq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::B_KV), 1);
+    for (int i = 0; i < R; ++i) {
+      mbar_init(bar(L::B_QF + i), 1);
+      mbar_init(bar(L::B_QE + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(L::B_SF + i), 1);
+      mbar_init(bar(L::B_SE + i), 4);
+      mbar_init(bar(L::B_DF + i), 4);
+      mbar_init(bar(L::B_DE + i), 1);
+    }
+    mbar_init(bar(L::B_FIN), 1);
+    mbar_init(bar(L::B_DRAIN), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(sb + L::TMEM_SLOT, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      mbar_expect_tx(bar(L::B_KV), 2 * 128 * D * 2);
+#pragma unroll
+      for (int s = 0; s < L::kSub; ++s)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          tma_load_2d(sb + L::K + s * 16384 + r * 8192, &tm_k, s * 64, row_base + r * 64, bar(L::B_KV));
+          tma_load_2d(sb + L::V + s * 16384 + r * 8192, &tm_v, s * 64, row_base + r * 64, bar(L::B_KV));
+        }
+      UnionIter it;
+      it.init(row_a, row_b, wq);
+      int n = 0, sel = 0, t;
+      while ((t = it.next(sel)) >= 0) {
+        const int st = n % R;
+        if (n >= R && !mbar_wait(bar(L::B_QE + st), ((n / R) - 1) & 1, abort_flag, &g_tc_error,
+                                 kErrDkdvProducer))
+          break;
+        mbar_expect_tx(bar(L::B_QF + st), 2 * 64 * D * 2 + 2 * 256);
+#pragma unroll
+        for (int s = 0; s < L::kSub; ++s) {
+          tma_load_2d(sb + L::Q + st * L::kSub * 8192 + s * 8192, &tm_q, s * 64, head_row + t * 64,
+                      bar(L::B_QF + st));
+          tma_load_2d(sb + L::DO + st * L::kSub * 8192 + s * 8192, &tm_do, s * 64, head_row + t * 64,
+                      bar(L::B_QF + st));
+        }
+        bulk_load(sb + L::M + st * 256, lse + head_row + (int64_t)t * 64, 256, bar(L::B_QF + st));
+        bulk_load(sb + L::DL + st * 256, delta + head_row + (int64_t)t * 64, 256, bar(L::B_QF + st));
+        ++n;
+      }
+      for (int m = (n > R ? n - R : 0); m < n; ++m)
+        mbar_wait(bar(L::B_QF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
+      mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
+      bool ok = mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
+      tc_fence_after();
+      UnionIter it;
+      it.init(row_a, row_b, wq);
+      int n = 0;
+      auto grads = [&](int j) -> bool {
+        const int b = j & 1, st = j % R;
+        if (!mbar_wait(bar(L::B_DF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k16 = 0; k16 < 4; ++k16) {
+          const uint64_t a = desc_k_sw128(sb + L::PT + b * 16384 + k16 * 32);
+          const uint64_t bd = desc_mn_sw128(sb + L::DO + st * L::kSub * 8192 + k16 * 2048, 8192);
+          mma_bf16(tmem + L::T_DV, a, bd, IDESC_G, (j > 0 || k16 > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k16 = 0; k16 < 4; ++k16) {
+          const uint64_t a = desc_k_sw128(sb + L::DST + b * 16384 + k16 * 32);
+          const uint64_t bd = desc_mn_sw128(sb + L::Q + st * L::kSub * 8192 + k16 * 2048, 8192);
+          mma_bf16(tmem + L::T_DK, a, bd, IDESC_G, (j > 0 || k16 > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(L::B_QE + st));
+        mma_commit(bar(L::B_DE + b));
+        return true;
+      };
+      int sel = 0, t;
+      while (ok && (t = it.next(sel)) >= 0) {
+        const int st = n % R, b = n & 1;
+        if (!mbar_wait(bar(L::B_QF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) {
+          ok = false;
+          break;
+        }
+        if (n >= 2 && !mbar_wait(bar(L::B_SE + b), ((n >> 1) - 1) & 1, abort_flag, &g_tc_error,
+                                 kErrDkdvMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a = desc_k_sw128(sb + L::K + (kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t bd =
+              desc_k_sw128(sb + L::Q + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
+          mma_bf16(tmem + L::T_S + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a = desc_k_sw128(sb + L::V + (kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t bd =
+              desc_k_sw128(sb + L::DO + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
+          mma_bf16(tmem + L::T_DP + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(L::B_SF + b));
+        if (n >= 1 && !grads(n - 1)) {
+          ok = false;
+          break;
+        }
+        ++n;
+      }
+      if (ok && n >= 1) ok = grads(n - 1);
+      mma_commit(bar(L::B_FIN));
+      mma_commit(bar(L::B_DRAIN));
+      mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
+    }
+  } else {
+    const int r = threadIdx.x;  // key row within the CTA
+    const int half = r >> 6;
+    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool kvalid = (tile_bits[2 * pair + half] >> (r & 63)) & 1ull;
+    UnionIter it;
+    it.init(row_a, row_b, wq);
+    int n = 0, sel = 0, t;
+    bool ok = true;
+    const float* sM = reinterpret_cast<const float*>(sm + L::M);
+    const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
+    while ((t = it.next(sel)) >= 0) {
+      const int st = n % R, b = n & 1;
+      if (!warp_wait(bar(L::B_QF + st), (n / R) & 1, abort_flag, kErrDkdvSoftmax) ||
+          !warp_wait(bar(L::B_SF + b), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[64], dp[64];
+      tmem_load<2>(t_lane + L::T_S + b * 64, s);
+      tmem_load<2>(t_lane + L::T_DP + b * 64, dp);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_SE + b));
+      const bool on = kvalid && ((sel >> half) & 1);
+      uint32_t pp[32], pd[32];
+      const float* m_st = sM + st * 64;
+      const float* d_st = sDl + st * 64;
+      if (on) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = ex2(fmaf(s[c], qk_scale, -m_st[c] * kRcpLn2));
+          const float p1 = ex2(fmaf(s[c + 1], qk_scale, -m_st[c + 1] * kRcpLn2));
+          pp[c / 2] = pack_bf16(p0, p1);
+          pd[c / 2] = pack_bf16(p0 * (dp[c] - d_st[c]), p1 * (dp[c + 1] - d_st[c + 1]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pp[i] = pd[i] = 0u;
+      }
+      if (n >= 2 && !warp_wait(bar(L::B_DE + b), ((n >> 1) - 1) & 1, abort_flag, kErrDkdvSoftmax)) {
+        ok = false;
+        break;
+      }
+      uint8_t* sPT = sm + L::PT + b * 16384;
+      uint8_t* sDST = sm + L::DST + b * 16384;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        *reinterpret_cast<uint4*>(sPT + sw128_off(r, ch)) =
+            make_uint4(pp[ch * 4], pp[ch * 4 + 1], pp[ch * 4 + 2], pp[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(sDST + sw128_off(r, ch)) =
+            make_uint4(pd[ch * 4], pd[ch * 4 + 1], pd[ch * 4 + 2], pd[ch * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_DF + b));
+      ++n;
+    }
+    const int64_t grow = (int64_t)row_base + r;
+    if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDkdvSoftmax)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t raw[32], pk[16];
+        tmem_ld32(t_lane + L::T_DK + c * 32, raw);
+        tmem_wait_ld_dep(raw);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]) * sm_scale, u2f(raw[2 * i + 1]) * sm_scale);
+        uint4* dst = reinterpret_cast<uint4*>(dk + grow * D + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        tmem_ld32(t_lane + L::T_DV + c * 32, raw);
+        tmem_wait_ld_dep(raw);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]), u2f(raw[2 * i + 1]));
+        dst = reinterpret_cast<uint4*>(dv + grow * D + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+    } else if (ok && n == 0) {
+      uint4* a = reinterpret_cast<uint4*>(dk + grow * D);
+      uint4* c = reinterpret_cast<uint4*>(dv + grow * D);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) a[i] = c[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ======================================================================= dQ
+template <int D>
+struct DqLayout {
+  static constexpr int kRing = 4;
+  static constexpr int kSub = D / 64;
+  static constexpr int Q = 0;                              // 128 queries
+  static constexpr int DO = Q + kSub * 16384;
+  static constexpr int K = DO + kSub * 16384;              // kRing x 64 keys
+  static constexpr int V = K + kRing * kSub * 8192;
+  static constexpr int DS = V + kRing * kSub * 8192;       // 2 x (128 queries x 64 keys)
+  static constexpr int BAR = DS + 2 * 16384;
+  static constexpr int B_QD = 0, B_KF = 1, B_KE = B_KF + kRing, B_VF = B_KE + kRing,
+                       B_VE = B_VF + kRing, B_SF = B_VE + kRing, B_SE = B_SF + 2, B_DF = B_SE + 2,
+                       B_DE = B_DF + 2, B_FIN = B_DE + 2, B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
+  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
+  static constexpr int ABORT = TMEM_SLOT + 4;
+  static constexpr size_t kBytes = 1024 + ABORT + 4;
+  static constexpr int T_DQ = 0, T_S = D, T_DP = D + 128;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                 const float* __restrict__ lse, const float* __restrict__ delta, int64_t S, int wq,
+                 float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_q,
+                 const uint64_t* __restrict__ tile_bits, __nv_bfloat16* __restrict__ dq) {
+  using L = DqLayout<D>;
+  constexpr int R = L::kRing;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const uint32_t sb = smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x, h = blockIdx.y;
+  const int64_t n_tiles = S / 64;
+  const int row_base = (int)((int64_t)h * S + (int64_t)pair * 128);
+  const int head_row = (int)((int64_t)h * S);
+  auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
+  const uint32_t* row_a = bits_q + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
+  const uint32_t* row_b = row_a + wq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::B_QD), 1);
+    for (int i = 0; i < R; ++i) {
+      mbar_init(bar(L::B_KF + i), 1);
+      mbar_init(bar(L::B_KE + i), 1);
+      mbar_init(bar(L::B_VF + i), 1);
+      mbar_init(bar(L::B_VE + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(L::B_SF + i), 1);
+      mbar_init(bar(L::B_SE + i), 4);
+      mbar_init(bar(L::B_DF + i), 4);
+      mbar_init(bar(L::B_DE + i), 1);
+    }
+    mbar_init(bar(L::B_FIN), 1);
+    mbar_init(bar(L::B_DRAIN), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(sb + L::TMEM_SLOT, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      mbar_expect_tx(bar(L::B_QD), 2 * 128 * D * 2);
+#pragma unroll
+      for (int s = 0; s < L::kSub; ++s)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          tma_load_2d(sb + L::Q + s * 16384 + r * 8192, &tm_q, s * 64, row_base + r * 64, bar(L::B_QD));
+          tma_load_2d(sb + L::DO + s * 16384 + r * 8192, &tm_do, s * 64, row_base + r * 64, bar(L::B_QD));
+        }
+      UnionIter it;
+      it.init(row_a, row_b, wq);
+      int nk = 0, nv = 0, sel = 0, t;
+      while ((t = it.next(sel)) >= 0) {
+        const int st = nk % R;
+        if (nk >= R && !mbar_wait(bar(L::B_KE + st), ((nk / R) - 1) & 1, abort_flag, &g_tc_error,
+                                  kErrDqProducer))
+          break;
+        mbar_expect_tx(bar(L::B_KF + st), 64 * D * 2);
+#pragma unroll
+        for (int s = 0; s < L::kSub; ++s)
+          tma_load_2d(sb + L::K + st * L::kSub * 8192 + s * 8192, &tm_k, s * 64, head_row + t * 64,
+                      bar(L::B_KF + st));
+        ++nk;
+        if (nv >= R && !mbar_wait(bar(L::B_VE + st), ((nv / R) - 1) & 1, abort_flag, &g_tc_error,
+                                  kErrDqProducer))
+          break;
+        mbar_expect_tx(bar(L::B_VF + st), 64 * D * 2);
+#pragma unroll
+        for (int s = 0; s < L::kSub; ++s)
+          tma_load_2d(sb + L::V + st * L::kSub * 8192 + s * 8192, &tm_v, s * 64, head_row + t * 64,
+                      bar(L::B_VF + st));
+        ++nv;
+      }
+      for (int m = (nk > R ? nk - R : 0); m < nk; ++m)
+        mbar_wait(bar(L::B_KF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDqProducer);
+      for (int m = (nv > R ? nv - R : 0); m < nv; ++m)
+        mbar_wait(bar(L::B_VF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDqProducer);
+      mbar_wait(bar(L::B_QD), 0, abort_flag, &g_tc_error, kErrDqProducer);
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
+      bool ok = mbar_wait(bar(L::B_QD), 0, abort_flag, &g_tc_error, kErrDqMma);
+      tc_fence_after();
+      UnionIter it;
+      it.init(row_a, row_b, wq);
+      int n = 0;
+      auto grads = [&](int j) -> bool {
+        const int b = j & 1, st = j % R;
+        if (!mbar_wait(bar(L::B_DF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDqMma)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k16 = 0; k16 < 4; ++k16) {
+          const uint64_t a = desc_k_sw128(sb + L::DS + b * 16384 + k16 * 32);
+          const uint64_t bd = desc_mn_sw128(sb + L::K + st * L::kSub * 8192 + k16 * 2048, 8192);
+          mma_bf16(tmem + L::T_DQ, a, bd, IDESC_G, (j > 0 || k16 > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(L::B_KE + st));
+        mma_commit(bar(L::B_DE + b));
+        return true;
+      };
+      int sel = 0, t;
+      while (ok && (t = it.next(sel)) >= 0) {
+        const int st = n % R, b = n & 1;
+        if (!mbar_wait(bar(L::B_KF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDqMma)) {
+          ok = false;
+          break;
+        }
+        if (n >= 2 && !mbar_wait(bar(L::B_SE + b), ((n >> 1) - 1) & 1, abort_flag, &g_tc_error,
+                                 kErrDqMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a = desc_k_sw128(sb + L::Q + (kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t bd =
+              desc_k_sw128(sb + L::K + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
+          mma_bf16(tmem + L::T_S + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        if (!mbar_wait(bar(L::B_VF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDqMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a = desc_k_sw128(sb + L::DO + (kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t bd =
+              desc_k_sw128(sb + L::V + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
+          mma_bf16(tmem + L::T_DP + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(L::B_VE + st));
+        mma_commit(bar(L::B_SF + b));
+        if (n >= 1 && !grads(n - 1)) {
+          ok = false;
+          break;
+        }
+        ++n;
+      }
+      if (ok && n >= 1) ok = grads(n - 1);
+      mma_commit(bar(L::B_FIN));
+      mma_commit(bar(L::B_DRAIN));
+      mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDqMma);
+    }
+  } else {
+    const int r = threadIdx.x;
+    const int half = r >> 6;
+    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+    const int64_t grow = (int64_t)row_base + r;
+    const float mrow = lse[grow] * kRcpLn2;
+    const float drow = delta[grow];
+    UnionIter it;
+    it.init(row_a, row_b, wq);
+    int n = 0, sel = 0, t;
+    bool ok = true;
+    while ((t = it.next(sel)) >= 0) {
+      const int b = n & 1;
+      if (!warp_wait(bar(L::B_SF + b), (n >> 1) & 1, abort_flag, kErrDqSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[64], dp[64];
+      tmem_load<2>(t_lane + L::T_S + b * 64, s);
+      tmem_load<2>(t_lane + L::T_DP + b * 64, dp);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_SE + b));
+      const uint64_t vb = ((sel >> half) & 1) ? tile_bits[t] : 0ull;
+      uint32_t pd[32];
+      if (vb == ~0ull) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = ex2(fmaf(s[c], qk_scale, -mrow));
+          const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mrow));
+          pd[c / 2] = pack_bf16(p0 * (dp[c] - drow), p1 * (dp[c + 1] - drow));
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = ((vb >> c) & 1ull) ? ex2(fmaf(s[c], qk_scale, -mrow)) : 0.0f;
+          const float p1 = ((vb >> (c + 1)) & 1ull) ? ex2(fmaf(s[c + 1], qk_scale, -mrow)) : 0.0f;
+          pd[c / 2] = pack_bf16(p0 * (dp[c] - drow), p1 * (dp[c + 1] - drow));
+        }
+      }
+      if (n >= 2 && !warp_wait(bar(L::B_DE + b), ((n >> 1) - 1) & 1, abort_flag, kErrDqSoftmax)) {
+        ok = false;
+        break;
+      }
+      uint8_t* sDS = sm + L::DS + b * 16384;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(sDS + sw128_off(r, ch)) =
+            make_uint4(pd[ch * 4], pd[ch * 4 + 1], pd[ch * 4 + 2], pd[ch * 4 + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_DF + b));
+      ++n;
+    }
+    if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDqSoftmax)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t raw[32], pk[16];
+        tmem_ld32(t_lane + L::T_DQ + c * 32, raw);
+        tmem_wait_ld_dep(raw);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]) * sm_scale, u2f(raw[2 * i + 1]) * sm_scale);
+        uint4* dst = reinterpret_cast<uint4*>(dq + grow * D + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+    } else if (ok && n == 0) {
+      uint4* a = reinterpret_cast<uint4*>(dq + grow * D);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) a[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ================================================================ preprocess
+// delta[h][s] = sum_d O * dO (fp32), one warp per row; with o_lo (the
+// forward's rounding residual) the row uses O = hi + lo.
+template <int D>
+__global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ o_lo,
+                             const __nv_bfloat16* __restrict__ dout, int64_t rows,
+                             float* __restrict__ delta) {
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float acc = 0.0f;
+#pragma unroll
+  for (int c = lane * 2; c < D; c += 64) {
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(o + r * D + c);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(dout + r * D + c);
+    float a0 = __low2float(a), a1 = __high2float(a);
+    if (o_lo != nullptr) {
+      const __nv_bfloat162 l = *reinterpret_cast<const __nv_bfloat162*>(o_lo + r * D + c);
+      a0 += __low2float(l);
+      a1 += __high2float(l);
+    }
+    acc += a0 * __low2float(b) + a1 * __high2float(b);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) delta[r] = acc;
+}
+
+// ================================================================ host side
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+// [rows, D] bf16 row-major, 64 x 64 boxes, 128-byte swizzle.
+static prism_status_t make_map(CUtensorMap* map, const void* ptr, int64_t rows, int D, const char* what) {
+  EncodeFn enc = encode_fn();
+  if (enc == nullptr) {
+    set_error("%s: cuTensorMapEncodeTiled is unavailable from the driver", what);
+    return PRISM_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+    return PRISM_ERR_CUDA;
+  }
+  return PRISM_OK;
+}
+
+#define PRISM_TRY(x)                       \
+  do {                                     \
+    prism_status_t st_ = (x);              \
+    if (st_ != PRISM_OK) return st_;       \
+  } while (0)
+
+template <int D>
+prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
+                          float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits, void* o,
+                          void* o_lo, float* lse, cudaStream_t stream) {
+  const int64_t n_tiles = S / 64;
+  const int wq = (int)((n_tiles + 31) / 32);
+  const size_t sm = FwdLayout<D>::kBytes > kMinSmem ? FwdLayout<D>::kBytes : kMinSmem;
+  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_fwd: shared memory layout exceeds 227 KB");
+  CUtensorMap mq, mk, mv;
+  const int64_t rows = (int64_t)heads * S;
+  PRISM_TRY(make_map(&mq, q, rows, D, "prism_bsa_fwd"));
+  PRISM_TRY(make_map(&mk, k, rows, D, "prism_bsa_fwd"));
+  PRISM_TRY(make_map(&mv, v, rows, D, "prism_bsa_fwd"));
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "prism_bsa_fwd: smem attribute");
+  fwd_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kThreads, sm, stream>>>(
+      mq, mk, mv, S, wq, sm_scale * kRcpLn2, bits_q, tile_bits, (__nv_bfloat16*)o, (__nv_bfloat16*)o_lo, lse);
+  PRISM_CHECK_LAUNCH("prism_bsa_fwd");
+  return PRISM_OK;
+}
+
+template <int D>
+prism_status_t launch_delta(const void* o, const void* o_lo, const void* dout, int heads, int64_t S,
+                            float* delta, cudaStream_t stream) {
+  const int64_t rows = (int64_t)heads * S;
+  delta_kernel<D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      (const __nv_bfloat16*)o, (const __nv_bfloat16*)o_lo, (const __nv_bfloat16*)dout, rows, delta);
+  PRISM_CHECK_LAUNCH("prism_bsa_bwd_delta");
+  return PRISM_OK;
+}
+
+template <int D>
+prism_status_t launch_dkdv(const void* q, const void* k, const void* v, const void* dout,
+                           const float* lse, const float* delta, int heads, int64_t S,
+                           float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
+                           void* dk, void* dv, cudaStream_t stream) {
+  const int64_t n_tiles = S / 64;
+  const int wq = (int)((n_tiles + 31) / 32);
+  const size_t sm = DkdvLayout<D>::kBytes > kMinSmem ? DkdvLayout<D>::kBytes : kMinSmem;
+  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
+  CUtensorMap mq, mk, mv, mdo;
+  const int64_t rows = (int64_t)heads * S;
+  PRISM_TRY(make_map(&mq, q, rows, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mk, k, rows, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mv, v, rows, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mdo, dout, rows, D, "prism_bsa_bwd_dkdv"));
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(dkdv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "prism_bsa_bwd: smem attribute");
+  dkdv_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kThreads, sm, stream>>>(
+      mq, mk, mv, mdo, lse, delta, S, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
+      (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
+  PRISM_CHECK_LAUNCH("prism_bsa_bwd_dkdv");
+  return PRISM_OK;
+}
+
+template <int D>
+prism_status_t launch_dq(const void* q, const void* k, const void* v, const void* dout,
+                         const float* lse, const float* delta, int heads, int64_t S,
+                         float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
+                         void* dq, cudaStream_t stream) {
+  const int64_t n_tiles = S / 64;
+  const int wq = (int)((n_tiles + 31) / 32);
+  const size_t sm = DqLayout<D>::kBytes > kMinSmem ? DqLayout<D>::kBytes : kMinSmem;
+  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
+  CUtensorMap mq, mk, mv, mdo;
+  const int64_t rows = (int64_t)heads * S;
+  PRISM_TRY(make_map(&mq, q, rows, D, "prism_bsa_bwd_dq"));
+  PRISM_TRY(make_map(&mk, k, rows, D, "prism_bsa_bwd_dq"));
+  PRISM_TRY(make_map(&mv, v, rows, D, "prism_bsa_bwd_dq"));
+  PRISM_TRY(make_map(&mdo, dout, rows, D, "prism_bsa_bwd_dq"));
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(dq_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "prism_bsa_bwd: smem attribute");
+  dq_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kThreads, sm, stream>>>(
+      mq, mk, mv, mdo, lse, delta, S, wq, sm_scale * kRcpLn2, sm_scale, bits_q, tile_bits,
+      (__nv_bfloat16*)dq);
+  PRISM_CHECK_LAUNCH("prism_bsa_bwd_dq");
+  return PRISM_OK;
+}
+
+}  // namespace tc
+}  // namespace prism
+
+using namespace prism;
+
+extern "C" {
+
+int prism_device_status(void) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tc::g_tc_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(tc::g_tc_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+// Row indices of the [heads * S, D] view are 32-bit TMA coordinates.
+#define PRISM_ATTN_SHAPE_CHECKS(name)                                                              \
+  PRISM_CHECK_ARG(S > 0 && S % 128 == 0 && heads >= 1, name ": S must be a positive multiple of 128"); \
+  PRISM_CHECK_ARG((int64_t)heads * S < ((int64_t)1 << 31), name ": heads * S must be below 2^31");     \
+  PRISM_CHECK_ARG(D == 64 || D == 128, name ": head dim %d not supported (64, 128)", D)
+
+prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
+                             int D, float sm_scale, const uint32_t* bits_q,
+                             const uint64_t* tile_bits, void* o, void* o_lo, float* lse,
+                             cudaStream_t stream) {
+  PRISM_CHECK_ARG(q && k && v && bits_q && tile_bits && o && lse, "prism_bsa_fwd: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_fwd");
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o), "prism_bsa_fwd: tensors must be 16-byte aligned");
+  PRISM_CHECK_ARG(o_lo == nullptr || aligned16(o_lo), "prism_bsa_fwd: o_lo must be 16-byte aligned");
+  if (D == 128) return tc::launch_fwd<128>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
+  return tc::launch_fwd<64>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
+}
+
+size_t prism_bsa_bwd_workspace_bytes(int heads, int64_t S) {
+  return (size_t)heads * (size_t)S * sizeof(float);
+}
+
+prism_status_t prism_bsa_bwd_delta(const void* o, const void* o_lo, const void* dout, int heads,
+                                   int64_t S, int D, float* delta, cudaStream_t stream) {
+  PRISM_CHECK_ARG(o && dout && delta, "prism_bsa_bwd_delta: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_delta");
+  return D == 128 ? tc::launch_delta<128>(o, o_lo, dout, heads, S, delta, stream)
+                  : tc::launch_delta<64>(o, o_lo, dout, heads, S, delta, stream);
+}
+
+prism_status_t prism_bsa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout,
+                                  const float* lse, const float* delta, int heads, int64_t S, int D,
+                                  float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
+                                  void* dk, void* dv, cudaStream_t stream) {
+  PRISM_CHECK_ARG(q && k && v && dout && lse && delta && bits_k && tile_bits && dk && dv,
+                  "prism_bsa_bwd_dkdv: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_dkdv");
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dk) &&
+                      aligned16(dv) && aligned16(lse) && aligned16(delta),
+                  "prism_bsa_bwd_dkdv: tensors must be 16-byte aligned");
+  return D == 128 ? tc::launch_dkdv<128>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_k, tile_bits, dk, dv, stream)
+                  : tc::launch_dkdv<64>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_k, tile_bits, dk, dv, stream);
+}
+
+prism_status_t prism_bsa_bwd_dq(const void* q, const void* k, const void* v, const void* dout,
+                                const float* lse, const float* delta, int heads, int64_t S, int D,
+                                float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
+                                void* dq, cudaStream_t stream) {
+  PRISM_CHECK_ARG(q && k && v && dout && lse && delta && bits_q && tile_bits && dq, "prism_bsa_bwd_dq: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_dq");
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dq),
+                  "prism_bsa_bwd_dq: tensors must be 16-byte aligned");
+  return D == 128 ? tc::launch_dq<128>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_q, tile_bits, dq, stream)
+                  : tc::launch_dq<64>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_q, tile_bits, dq, stream);
+}
+
+prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const void* o,
+                             const void* o_lo, const void* dout, const float* lse, int heads,
+                             int64_t S, int D,
+                             float sm_scale, const uint32_t* bits_q, const uint32_t* bits_k,
+                             const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
+                             void* dv, cudaStream_t stream) {
+  PRISM_CHECK_ARG(workspace, "prism_bsa_bwd: null pointer");
+  float* delta = (float*)workspace;
+  prism_status_t st = prism_bsa_bwd_delta(o, o_lo, dout, heads, S, D, delta, stream);
+  if (st != PRISM_OK) return st;
+  st = prism_bsa_bwd_dkdv(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  if (st != PRISM_OK) return st;
+  return prism_bsa_bwd_dq(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_q, tile_bits, dq, stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------
+// Backward without any device allocation (prism_bsa_bwd_noalloc).
+//
+// The only scratch the backward needs is delta[h][s] (one float per query
+// row).  Here it lives in a file-scope device array of a fixed size, so the
+// caller passes inputs and outputs only.  The array is part of this library's
+// device image: every GPU that loads the library reserves it until the
+// process exits.  Host code cannot use the array's name as a device address
+// (on the host it names a stand-in object), so its real address is looked up
+// with cudaGetSymbolAddress, once per device, with that device current, on
+// the first call made on that device.
+namespace prism {
+namespace tc {
+static __device__ __align__(256) float g_noalloc_delta[PRISM_BSA_BWD_NOALLOC_MAX_ROWS];
+}  // namespace tc
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_addr[128] = {nullptr};
+
+static prism_status_t noalloc_scratch(float** out) {
+  int dev = -1;
+  PRISM_CHECK_CUDA(cudaGetDevice(&dev), "prism_bsa_bwd_noalloc: cudaGetDevice");
+  PRISM_CHECK_ARG(dev >= 0 && dev < 128, "prism_bsa_bwd_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, tc::g_noalloc_delta);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("prism_bsa_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      return PRISM_ERR_CUDA;
+    }
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return PRISM_OK;
+}
+}  // namespace prism
+
+extern "C" prism_status_t prism_bsa_bwd_noalloc(
+    const void* q, const void* k, const void* v, const void* o, const void* o_lo, const void* dout,
+    const float* lse, int heads, int64_t S, int D, float sm_scale, const uint32_t* bits_q,
+    const uint32_t* bits_k, const uint64_t* tile_bits, void* dq, void* dk, void* dv,
+    cudaStream_t stream) {
+  PRISM_CHECK_ARG(heads >= 1 && S > 0, "prism_bsa_bwd_noalloc: heads and S must be positive");
+  PRISM_CHECK_ARG((uint64_t)heads * (uint64_t)S <= (uint64_t)PRISM_BSA_BWD_NOALLOC_MAX_ROWS,
+                  "prism_bsa_bwd_noalloc: heads*S = %lld query rows exceed the built-in scratch "
+                  "of %u rows; use prism_bsa_bwd with a caller-provided workspace",
+                  (long long)heads * (long long)S, (unsigned)PRISM_BSA_BWD_NOALLOC_MAX_ROWS);
+  float* delta = nullptr;
+  const prism_status_t st0 = noalloc_scratch(&delta);
+  if (st0 != PRISM_OK) return st0;
+  // Every delta row is written by the first stage before the other two read
+  // it, so nothing left in the array by an earlier call is ever used.
+  prism_status_t st = prism_bsa_bwd_delta(o, o_lo, dout, heads, S, D, delta, stream);
+  if (st != PRISM_OK) return st;
+  st = prism_bsa_bwd_dkdv(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  if (st != PRISM_OK) return st;
+  return prism_bsa_bwd_dq(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_q, tile_bits, dq, stream);
+}

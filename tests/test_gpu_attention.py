@@ -12,7 +12,7 @@ import torch
 from helpers import bits, load_fixture, rel_l2
 from inputs import CASES, Case, make_inputs
 from oracle import oracle as O
-from prism_b200 import flash_attn_bsa_3d_dynamic, ops, run_bsa_dynamic
+from prism_b200 import _lib, flash_attn_bsa_3d_dynamic, ops, run_bsa_dynamic
 
 pytestmark = pytest.mark.gpu
 
@@ -91,6 +91,31 @@ def test_sparse_kernels_vs_oracle(D, density, cuda):
     dq2, dk2, dv2 = ops.bsa_bwd(d["q"], d["k"], d["v"], o, d["do"], lse, d["bq"], d["bk"], d["tb"], sm,
                                 o_lo=o_lo)
     assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)
+    assert _lib.load().prism_device_status() == 0, "a bounded wait inside a kernel gave up"
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_sparse_kernels_multiword_rows(D, cuda):
+    """72 tiles per head (3 bitmap words per row), half density with padded
+    and fully padded key tiles: exercises the K/V and Q/dO rings wrapping many
+    times, odd tile counts in the forward's tile pairs, and word boundaries."""
+    pr = _random_problem(2, 72, D, 0.5, seed=7 + D, dev=cuda,
+                         masked_tiles=[(0, 40), (31, 1), (32, 0), (63, 64), (71, 33)],
+                         empty_rows=[10, 57])
+    d = pr["dev"]
+    sm = 1.0 / math.sqrt(D)
+    o, lse, o_lo = ops.bsa_fwd(d["q"], d["k"], d["v"], d["bq"], d["tb"], sm, want_lo=True)
+    f = lambda t: t.float().numpy()
+    ro, _ = O.bsa_forward(f(pr["q"]), f(pr["k"]), f(pr["v"]), pr["bq"], pr["valid"], sm)
+    _close(o.float().cpu(), ro, "O")
+    dq, dk, dv = ops.bsa_bwd(d["q"], d["k"], d["v"], o, d["do"], lse, d["bq"], d["bk"], d["tb"], sm,
+                             o_lo=o_lo)
+    rdq, rdk, rdv = O.bsa_backward(f(pr["q"]), f(pr["k"]), f(pr["v"]), ro, f(pr["do"]), pr["bq"],
+                                   pr["valid"], sm)
+    _close(dq.float().cpu(), rdq, "dQ")
+    _close(dk.float().cpu(), rdk, "dK")
+    _close(dv.float().cpu(), rdv, "dV")
+    assert _lib.load().prism_device_status() == 0, "a bounded wait inside a kernel gave up"
 
 
 @pytest.mark.parametrize("name", [n for n, c in CASES.items() if c.needs_pad])
