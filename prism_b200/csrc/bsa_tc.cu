@@ -51,9 +51,11 @@ using namespace sm100;
 
 constexpr float kLn2 = 0.6931471824645996f;
 constexpr float kRcpLn2 = 1.4426950408889634f;
-constexpr int kThreads = 192;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+// Backward kernels: 8 softmax warps (two warpgroups splitting each step's
+// columns) + producer + MMA.
+constexpr int kBwdThreads = 320;
+constexpr int kBwdProducerWarp = 8;
+constexpr int kBwdMmaWarp = 9;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Device error word: 0 = ok, otherwise the code of the first bounded wait that
@@ -132,27 +134,71 @@ __device__ __forceinline__ void tmem_load(uint32_t taddr, float (&out)[32 * N]) 
 constexpr size_t kMinSmem = 116 * 1024;
 
 // ===================================================================== forward
+// CTA = 256 queries = tiles 4p..4p+3, as two groups of 128 rows (g = 0: tiles
+// 4p, 4p+1; g = 1: tiles 4p+2, 4p+3) that share one stream of key tiles (the
+// union of the four bitmap rows).  Each group has its own softmax warpgroup,
+// S double buffer and O accumulator in TMEM, so while one group's softmax
+// runs the tensor core works on the other group's products.
+struct UnionIter4 {
+  const uint32_t* r[4];
+  int wq, wi;
+  uint32_t w[4];
+  __device__ __forceinline__ void init(const uint32_t* r0, const uint32_t* r1, const uint32_t* r2,
+                                       const uint32_t* r3, int n) {
+    r[0] = r0;
+    r[1] = r1;
+    r[2] = r2;
+    r[3] = r3;
+    wq = n;
+    wi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = (n > 0 && r[i] != nullptr) ? __ldg(r[i]) : 0u;
+  }
+  // next tile index, or -1; bit i of sel: row i selected it
+  __device__ __forceinline__ int next(int& sel) {
+    while ((w[0] | w[1] | w[2] | w[3]) == 0u) {
+      if (++wi >= wq) return -1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = r[i] != nullptr ? __ldg(r[i] + wi) : 0u;
+    }
+    const int bit = __ffs(w[0] | w[1] | w[2] | w[3]) - 1;
+    const uint32_t m = 1u << bit;
+    sel = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sel |= (w[i] & m) ? (1 << i) : 0;
+      w[i] &= ~m;
+    }
+    return wi * 32 + bit;
+  }
+};
+
+constexpr int kFwdThreads = 320;
+constexpr int kFwdProducerWarp = 8;
+constexpr int kFwdMmaWarp = 9;
+
 template <int D>
 struct FwdLayout {
   static constexpr int kRing = 4;                       // K tiles and V tiles in flight
   static constexpr int kSub = D / 64;                   // 128-byte sub-buffers per row
-  static constexpr int Q = 0;                           // 128 rows
-  static constexpr int K = Q + kSub * 16384;            // kRing x 64 rows
+  static constexpr int Q = 0;                           // 2 groups x 128 rows
+  static constexpr int K = Q + 2 * kSub * 16384;        // kRing x 64 rows
   static constexpr int V = K + kRing * kSub * 8192;
-  static constexpr int P = V + kRing * kSub * 8192;     // 128 rows x 128 keys bf16
+  static constexpr int P = V + kRing * kSub * 8192;     // 2 groups x (128 rows x 64 keys)
   static constexpr int BAR = P + 2 * 16384;
   static constexpr int B_Q = 0, B_KF = 1, B_KE = B_KF + kRing, B_VF = B_KE + kRing,
-                       B_VE = B_VF + kRing, B_SF = B_VE + kRing, B_SE = B_SF + 2, B_PF = B_SE + 2,
-                       B_PV = B_PF + 1, B_DRAIN = B_PV + 1, NBAR = B_DRAIN + 1;
+                       B_VE = B_VF + kRing, B_SF = B_VE + kRing,  // [g][b] at B_SF + 2g + b
+                       B_SE = B_SF + 4, B_PF = B_SE + 4,           // [g]
+                       B_PV = B_PF + 2, B_DRAIN = B_PV + 2, NBAR = B_DRAIN + 1;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int ABORT = TMEM_SLOT + 4;
   static constexpr size_t kBytes = 1024 + ABORT + 4;
-  static constexpr int T_S = 0;      // S[b] at 128 b, 128 columns each
-  static constexpr int T_O = 256;    // O, D columns
+  static constexpr int T_S = 0;      // S[g][b] at 128 g + 64 b
+  static constexpr int T_O = 256;    // O[g] at 256 + D g
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, int64_t S, int wq, float qk_scale,
                   const uint32_t* __restrict__ bits_q, const uint64_t* __restrict__ tile_bits,
@@ -164,14 +210,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sm = align1024(smem_raw);
   const uint32_t sb = smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pair = blockIdx.x, h = blockIdx.y;
+  const int quad = blockIdx.x, h = blockIdx.y;
   const int64_t n_tiles = S / 64;
-  const int row_base = (int)((int64_t)h * S + (int64_t)pair * 128);  // row of [heads*S, D]
+  const bool g1_live = 4 * (int64_t)quad + 2 < n_tiles;  // S % 256 == 128: last CTA has one group
+  const int row_base = (int)((int64_t)h * S + (int64_t)quad * 256);  // row of [heads*S, D]
   const int head_row = (int)((int64_t)h * S);
   auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
-  const uint32_t* row_a = bits_q + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
-  const uint32_t* row_b = row_a + wq;
+  const uint32_t* r0 = bits_q + ((int64_t)h * n_tiles + 4 * (int64_t)quad) * wq;
+  const uint32_t* r2 = g1_live ? r0 + 2 * wq : nullptr;
+  const uint32_t* r3 = g1_live ? r0 + 3 * wq : nullptr;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(L::B_Q), 1);
@@ -181,17 +229,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(L::B_VF + i), 1);
       mbar_init(bar(L::B_VE + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(bar(L::B_SF + i), 1);
       mbar_init(bar(L::B_SE + i), 4);
     }
-    mbar_init(bar(L::B_PF), 4);
-    mbar_init(bar(L::B_PV), 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(L::B_PF + g), 4);
+      mbar_init(bar(L::B_PV + g), 1);
+    }
     mbar_init(bar(L::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == kFwdMmaWarp) {
     tmem_alloc(sb + L::TMEM_SLOT, 512);
     tmem_relinquish();
     tc_fence_before();
@@ -200,17 +250,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
 
-  if (warp == kProducerWarp) {
+  if (warp == kFwdProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_expect_tx(bar(L::B_Q), 128 * D * 2);
+      const int nq = g1_live ? 4 : 2;  // 64-row Q blocks
+      mbar_expect_tx(bar(L::B_Q), nq * 64 * D * 2);
+      for (int qb = 0; qb < nq; ++qb)
 #pragma unroll
-      for (int s = 0; s < L::kSub; ++s)
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-          tma_load_2d(sb + L::Q + s * 16384 + r * 8192, &tm_q, s * 64, row_base + r * 64, bar(L::B_Q));
-      UnionIter it;
-      it.init(row_a, row_b, wq);
+        for (int s = 0; s < L::kSub; ++s)
+          tma_load_2d(sb + L::Q + (qb >> 1) * L::kSub * 16384 + s * 16384 + (qb & 1) * 8192, &tm_q,
+                      s * 64, row_base + qb * 64, bar(L::B_Q));
+      UnionIter4 it;
+      it.init(r0, r0 + wq, r2, r3, wq);
       int nk = 0, nv = 0, sel = 0, t;
       while ((t = it.next(sel)) >= 0) {
         const int st = nk % R;
@@ -240,129 +291,98 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(bar(L::B_VF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrFwdProducer);
       mbar_wait(bar(L::B_Q), 0, abort_flag, &g_tc_error, kErrFwdProducer);
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kFwdMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
       constexpr uint32_t IDESC_PV = idesc_bf16(128, D, false, true);
+      const int ng = g1_live ? 2 : 1;
+      // descriptor bases (start-address field advanced by byte offset >> 4)
+      const uint64_t dQ = desc_k_sw128(sb + L::Q), dK = desc_k_sw128(sb + L::K),
+                     dP = desc_k_sw128(sb + L::P), dV = desc_mn_sw128(sb + L::V, 8192);
       bool ok = mbar_wait(bar(L::B_Q), 0, abort_flag, &g_tc_error, kErrFwdMma);
       tc_fence_after();
-      UnionIter it;
-      it.init(row_a, row_b, wq);
-      int n = 0, iter = 0, prev_cnt = 0, prev_n = 0;
-      auto issue_pv = [&](int j, int cnt, int n0) -> bool {
-        if (!mbar_wait(bar(L::B_PF), j & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
-        tc_fence_after();
-        for (int u = 0; u < cnt; ++u) {
-          const int st = (n0 + u) % R;
-          if (!mbar_wait(bar(L::B_VF + st), ((n0 + u) / R) & 1, abort_flag, &g_tc_error, kErrFwdMma))
-            return false;
+      UnionIter4 it;
+      it.init(r0, r0 + wq, r2, r3, wq);
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j % R;
+        if (!mbar_wait(bar(L::B_VF + st), (j / R) & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
+        for (int g = 0; g < ng; ++g) {
+          if (!mbar_wait(bar(L::B_PF + g), j & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
           tc_fence_after();
-#pragma unroll
-          for (int k16 = 0; k16 < 4; ++k16) {
-            const uint64_t a = desc_k_sw128(sb + L::P + u * 16384 + k16 * 32);
-            const uint64_t b = desc_mn_sw128(sb + L::V + st * L::kSub * 8192 + k16 * 2048, 8192);
-            mma_bf16(tmem + L::T_O, a, b, IDESC_PV, (j > 0 || u > 0 || k16 > 0) ? 1u : 0u);
-          }
-          mma_commit(bar(L::B_VE + st));
+          mma_k64_kmn(tmem + L::T_O + g * D, dP + g * (16384 >> 4),
+                      dV + st * (L::kSub * 8192 >> 4), IDESC_PV, j > 0 ? 1u : 0u);
+          mma_commit(bar(L::B_PV + g));
         }
-        mma_commit(bar(L::B_PV));
+        mma_commit(bar(L::B_VE + st));
         return true;
       };
-      while (ok) {
-        int sel0 = 0, sel1 = 0;
-        const int t0 = it.next(sel0);
-        if (t0 < 0) break;
-        const int t1 = it.next(sel1);
-        const int cnt = t1 >= 0 ? 2 : 1;
-        const int b = iter & 1;
-        if (iter >= 2 && !mbar_wait(bar(L::B_SE + b), ((iter >> 1) - 1) & 1, abort_flag, &g_tc_error,
-                                    kErrFwdMma)) {
+      int n = 0, sel = 0, t;
+      while (ok && (t = it.next(sel)) >= 0) {
+        const int st = n % R, b = n & 1;
+        if (!mbar_wait(bar(L::B_KF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrFwdMma)) {
           ok = false;
           break;
         }
-        for (int u = 0; u < cnt; ++u) {
-          const int st = (n + u) % R;
-          if (!mbar_wait(bar(L::B_KF + st), ((n + u) / R) & 1, abort_flag, &g_tc_error, kErrFwdMma)) {
+        for (int g = 0; g < ng && ok; ++g) {
+          if (n >= 2 && !mbar_wait(bar(L::B_SE + 2 * g + b), ((n >> 1) - 1) & 1, abort_flag,
+                                   &g_tc_error, kErrFwdMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t a = desc_k_sw128(sb + L::Q + (kk >> 2) * 16384 + (kk & 3) * 32);
-            const uint64_t bd =
-                desc_k_sw128(sb + L::K + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
-            mma_bf16(tmem + L::T_S + b * 128 + u * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
-          }
-          mma_commit(bar(L::B_KE + st));
+          mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + g * 128 + b * 64,
+                                       dQ + g * (L::kSub * 16384 >> 4),
+                                       dK + st * (L::kSub * 8192 >> 4), IDESC_S, 0u);
+          mma_commit(bar(L::B_SF + 2 * g + b));
         }
         if (!ok) break;
-        mma_commit(bar(L::B_SF + b));
-        if (iter >= 1 && !issue_pv(iter - 1, prev_cnt, prev_n)) {
+        mma_commit(bar(L::B_KE + st));
+        if (n >= 1 && !issue_pv(n - 1)) {
           ok = false;
           break;
         }
-        prev_cnt = cnt;
-        prev_n = n;
-        n += cnt;
-        ++iter;
-        if (t1 < 0) break;
+        ++n;
       }
-      if (ok && iter >= 1) issue_pv(iter - 1, prev_cnt, prev_n);
+      if (ok && n >= 1) issue_pv(n - 1);
       // drain: all issued MMAs complete before TMEM is released
       mma_commit(bar(L::B_DRAIN));
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrFwdMma);
     }
-  } else {
+  } else if (warp < 4 || g1_live) {
     // ------------------------------------------------------ softmax warps
-    const int r = threadIdx.x;  // row within the CTA == TMEM lane
-    const int half = r >> 6;
-    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+    const int g = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // row within the group == TMEM lane
+    const int sbit = 2 * g + (r >> 6);     // bitmap row of this thread's q tile
+    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     float m = -INFINITY, l = 1.0f;
-    UnionIter it;
-    it.init(row_a, row_b, wq);
-    int iter = 0;
+    UnionIter4 it;
+    it.init(r0, r0 + wq, r2, r3, wq);
+    int n = 0, sel = 0, t;
     bool ok = true;
-    uint8_t* sP = sm + L::P;
-    for (;;) {
-      int sel0 = 0, sel1 = 0;
-      const int t0 = it.next(sel0);
-      if (t0 < 0) break;
-      const int t1 = it.next(sel1);
-      const int b = iter & 1;
-      if (!warp_wait(bar(L::B_SF + b), (iter >> 1) & 1, abort_flag, kErrFwdSoftmax)) {
+    uint8_t* sP = sm + L::P + g * 16384;
+    while ((t = it.next(sel)) >= 0) {
+      const int b = n & 1;
+      const uint64_t vb = ((sel >> sbit) & 1) ? tile_bits[t] : 0ull;
+      if (!warp_wait(bar(L::B_SF + 2 * g + b), (n >> 1) & 1, abort_flag, kErrFwdSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[128];
-      {
-        float* s0 = s;
-        tmem_load<2>(t_lane + L::T_S + b * 128, *reinterpret_cast<float(*)[64]>(s0));
-        if (t1 >= 0) tmem_load<2>(t_lane + L::T_S + b * 128 + 64, *reinterpret_cast<float(*)[64]>(s0 + 64));
-      }
+      float s[64];
+      tmem_load<2>(t_lane + L::T_S + g * 128 + b * 64, s);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_SE + b));
+      if (lane == 0) mbar_arrive(bar(L::B_SE + 2 * g + b));
       // masks: row did not select the tile -> all keys masked; else key validity
-      {
-        const uint64_t vb0 = ((sel0 >> half) & 1) ? tile_bits[t0] : 0ull;
-        if (vb0 != ~0ull) {
+      if (vb != ~0ull) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (!((vb0 >> c) & 1ull)) s[c] = -INFINITY;
-        }
-        const uint64_t vb1 = (t1 >= 0 && ((sel1 >> half) & 1)) ? tile_bits[t1] : 0ull;
-        if (vb1 != ~0ull) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (!((vb1 >> c) & 1ull)) s[64 + c] = -INFINITY;
-        }
+        for (int c = 0; c < 64; ++c)
+          if (!((vb >> c) & 1ull)) s[c] = -INFINITY;
       }
       float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
 #pragma unroll
-      for (int c = 4; c < 128; c += 4) {
+      for (int c = 4; c < 64; c += 4) {
         mx0 = fmaxf(mx0, s[c]);
         mx1 = fmaxf(mx1, s[c + 1]);
         mx2 = fmaxf(mx2, s[c + 2]);
@@ -377,8 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool o_live = __any_sync(0xffffffffu, need && m != -INFINITY);
         l *= alpha;
         m = m_new;
-        if (iter > 0 && o_live) {
-          if (!warp_wait(bar(L::B_PV), (iter - 1) & 1, abort_flag, kErrFwdSoftmax)) {
+        if (n > 0 && o_live) {
+          if (!warp_wait(bar(L::B_PV + g), (n - 1) & 1, abort_flag, kErrFwdSoftmax)) {
             ok = false;
             break;
           }
@@ -387,20 +407,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t raw[32];
-            tmem_ld32(t_lane + L::T_O + c * 32, raw);
+            tmem_ld32(t_lane + L::T_O + g * D + c * 32, raw);
             tmem_wait_ld_dep(raw);
 #pragma unroll
             for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
-            tmem_st32(t_lane + L::T_O + c * 32, raw);
+            tmem_st32(t_lane + L::T_O + g * D + c * 32, raw);
           }
           tmem_wait_st();
         }
       }
       const float mb = (m == -INFINITY) ? 0.0f : m;
       float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-      uint32_t pk[64];
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 128; c += 4) {
+      for (int c = 0; c < 64; c += 4) {
         const float p0 = ex2(fmaf(s[c], qk_scale, -mb));
         const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mb));
         const float p2 = ex2(fmaf(s[c + 2], qk_scale, -mb));
@@ -413,38 +433,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[c / 2 + 1] = pack_bf16(p2, p3);
       }
       l += (sum0 + sum1) + (sum2 + sum3);
-      if (iter > 0 && !waited_pv) {
-        if (!warp_wait(bar(L::B_PV), (iter - 1) & 1, abort_flag, kErrFwdSoftmax)) {
+      if (n > 0 && !waited_pv) {
+        if (!warp_wait(bar(L::B_PV + g), (n - 1) & 1, abort_flag, kErrFwdSoftmax)) {
           ok = false;
           break;
         }
       }
-      // P row -> two 128B-swizzled sub-buffers (keys 0-63 and 64-127)
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint4 v4 = make_uint4(pk[u * 32 + ch * 4], pk[u * 32 + ch * 4 + 1],
-                                      pk[u * 32 + ch * 4 + 2], pk[u * 32 + ch * 4 + 3]);
-          *reinterpret_cast<uint4*>(sP + u * 16384 + sw128_off(r, ch)) = v4;
-        }
-      }
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(sP + sw128_off(r, ch)) =
+            make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_PF));
-      ++iter;
-      if (t1 < 0) break;
+      if (lane == 0) mbar_arrive(bar(L::B_PF + g));
+      ++n;
     }
     // epilogue
-    const int64_t grow = (int64_t)row_base + r;
-    if (ok && iter > 0 && warp_wait(bar(L::B_PV), (iter - 1) & 1, abort_flag, kErrFwdSoftmax)) {
+    const int64_t grow = (int64_t)row_base + g * 128 + r;
+    if (ok && n > 0 && warp_wait(bar(L::B_PV + g), (n - 1) & 1, abort_flag, kErrFwdSoftmax)) {
       tc_fence_after();
       const float inv = 1.0f / l;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t raw[32];
-        tmem_ld32(t_lane + L::T_O + c * 32, raw);
+        tmem_ld32(t_lane + L::T_O + g * D + c * 32, raw);
         tmem_wait_ld_dep(raw);
         uint32_t hi[16], lo[16];
 #pragma unroll
@@ -463,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       lse[grow] = (m + __log2f(l)) * kLn2;
-    } else if (ok && iter == 0) {
+    } else if (ok && n == 0) {
       // no selected tile at all: O = 0, lse = -inf (m = -inf, l = 1)
       uint4* dst = reinterpret_cast<uint4*>(o + grow * D);
 #pragma unroll
@@ -478,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kFwdMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -508,7 +521,7 @@ struct DkdvLayout {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                    const float* __restrict__ lse, const float* __restrict__ delta, int64_t S, int wq,
@@ -538,8 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(L::B_SF + i), 1);
-      mbar_init(bar(L::B_SE + i), 4);
-      mbar_init(bar(L::B_DF + i), 4);
+      mbar_init(bar(L::B_SE + i), 8);
+      mbar_init(bar(L::B_DF + i), 8);
       mbar_init(bar(L::B_DE + i), 1);
     }
     mbar_init(bar(L::B_FIN), 1);
@@ -547,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == kBwdMmaWarp) {
     tmem_alloc(sb + L::TMEM_SLOT, 512);
     tmem_relinquish();
     tc_fence_before();
@@ -556,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
 
-  if (warp == kProducerWarp) {
+  if (warp == kBwdProducerWarp) {
     if (lane == 0) {
       mbar_expect_tx(bar(L::B_KV), 2 * 128 * D * 2);
 #pragma unroll
@@ -590,10 +603,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(bar(L::B_QF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
       mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kBwdMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
+      const uint64_t dK = desc_k_sw128(sb + L::K), dV = desc_k_sw128(sb + L::V),
+                     dQk = desc_k_sw128(sb + L::Q), dDOk = desc_k_sw128(sb + L::DO),
+                     dQmn = desc_mn_sw128(sb + L::Q, 8192), dDOmn = desc_mn_sw128(sb + L::DO, 8192),
+                     dPT = desc_k_sw128(sb + L::PT), dDST = desc_k_sw128(sb + L::DST);
       bool ok = mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
       tc_fence_after();
       UnionIter it;
@@ -603,18 +620,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = j & 1, st = j % R;
         if (!mbar_wait(bar(L::B_DF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
         tc_fence_after();
-#pragma unroll
-        for (int k16 = 0; k16 < 4; ++k16) {
-          const uint64_t a = desc_k_sw128(sb + L::PT + b * 16384 + k16 * 32);
-          const uint64_t bd = desc_mn_sw128(sb + L::DO + st * L::kSub * 8192 + k16 * 2048, 8192);
-          mma_bf16(tmem + L::T_DV, a, bd, IDESC_G, (j > 0 || k16 > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int k16 = 0; k16 < 4; ++k16) {
-          const uint64_t a = desc_k_sw128(sb + L::DST + b * 16384 + k16 * 32);
-          const uint64_t bd = desc_mn_sw128(sb + L::Q + st * L::kSub * 8192 + k16 * 2048, 8192);
-          mma_bf16(tmem + L::T_DK, a, bd, IDESC_G, (j > 0 || k16 > 0) ? 1u : 0u);
-        }
+        mma_k64_kmn(tmem + L::T_DV, dPT + b * (16384 >> 4), dDOmn + st * (L::kSub * 8192 >> 4),
+                    IDESC_G, j > 0 ? 1u : 0u);
+        mma_k64_kmn(tmem + L::T_DK, dDST + b * (16384 >> 4), dQmn + st * (L::kSub * 8192 >> 4),
+                    IDESC_G, j > 0 ? 1u : 0u);
         mma_commit(bar(L::B_QE + st));
         mma_commit(bar(L::B_DE + b));
         return true;
@@ -632,20 +641,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = desc_k_sw128(sb + L::K + (kk >> 2) * 16384 + (kk & 3) * 32);
-          const uint64_t bd =
-              desc_k_sw128(sb + L::Q + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
-          mma_bf16(tmem + L::T_S + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = desc_k_sw128(sb + L::V + (kk >> 2) * 16384 + (kk & 3) * 32);
-          const uint64_t bd =
-              desc_k_sw128(sb + L::DO + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
-          mma_bf16(tmem + L::T_DP + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
-        }
+        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + b * 64, dK, dQk + st * (L::kSub * 8192 >> 4),
+                                     IDESC_S, 0u);
+        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_DP + b * 64, dV, dDOk + st * (L::kSub * 8192 >> 4),
+                                     IDESC_S, 0u);
         mma_commit(bar(L::B_SF + b));
         if (n >= 1 && !grads(n - 1)) {
           ok = false;
@@ -659,9 +658,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
     }
   } else {
-    const int r = threadIdx.x;  // key row within the CTA
+    // softmax warpgroups: wg 0 takes query columns 0-31 of each step, wg 1 32-63
+    const int wg = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // key row within the CTA == TMEM lane
     const int half = r >> 6;
-    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const bool kvalid = (tile_bits[2 * pair + half] >> (r & 63)) & 1ull;
     UnionIter it;
     it.init(row_a, row_b, wq);
@@ -677,19 +678,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float s[64], dp[64];
-      tmem_load<2>(t_lane + L::T_S + b * 64, s);
-      tmem_load<2>(t_lane + L::T_DP + b * 64, dp);
+      float s[32], dp[32];
+      tmem_load<1>(t_lane + L::T_S + b * 64 + wg * 32, s);
+      tmem_load<1>(t_lane + L::T_DP + b * 64 + wg * 32, dp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(L::B_SE + b));
       const bool on = kvalid && ((sel >> half) & 1);
-      uint32_t pp[32], pd[32];
-      const float* m_st = sM + st * 64;
-      const float* d_st = sDl + st * 64;
+      uint32_t pp[16], pd[16];
+      const float* m_st = sM + st * 64 + wg * 32;
+      const float* d_st = sDl + st * 64 + wg * 32;
       if (on) {
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           const float p0 = ex2(fmaf(s[c], qk_scale, -m_st[c] * kRcpLn2));
           const float p1 = ex2(fmaf(s[c + 1], qk_scale, -m_st[c + 1] * kRcpLn2));
           pp[c / 2] = pack_bf16(p0, p1);
@@ -697,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pp[i] = pd[i] = 0u;
+        for (int i = 0; i < 16; ++i) pp[i] = pd[i] = 0u;
       }
       if (n >= 2 && !warp_wait(bar(L::B_DE + b), ((n >> 1) - 1) & 1, abort_flag, kErrDkdvSoftmax)) {
         ok = false;
@@ -706,10 +707,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* sPT = sm + L::PT + b * 16384;
       uint8_t* sDST = sm + L::DST + b * 16384;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        *reinterpret_cast<uint4*>(sPT + sw128_off(r, ch)) =
+      for (int ch = 0; ch < 4; ++ch) {
+        *reinterpret_cast<uint4*>(sPT + sw128_off(r, wg * 4 + ch)) =
             make_uint4(pp[ch * 4], pp[ch * 4 + 1], pp[ch * 4 + 2], pp[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(sDST + sw128_off(r, ch)) =
+        *reinterpret_cast<uint4*>(sDST + sw128_off(r, wg * 4 + ch)) =
             make_uint4(pd[ch * 4], pd[ch * 4 + 1], pd[ch * 4 + 2], pd[ch * 4 + 3]);
       }
       fence_proxy_async_smem();
@@ -717,37 +718,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar(L::B_DF + b));
       ++n;
     }
+    // epilogue: wg 0 writes dK (scaled by sm_scale), wg 1 writes dV
     const int64_t grow = (int64_t)row_base + r;
+    __nv_bfloat16* out = (wg == 0 ? dk : dv) + grow * D;
+    const float scale = wg == 0 ? sm_scale : 1.0f;
+    const int tcol = wg == 0 ? L::T_DK : L::T_DV;
     if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDkdvSoftmax)) {
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t raw[32], pk[16];
-        tmem_ld32(t_lane + L::T_DK + c * 32, raw);
+        tmem_ld32(t_lane + tcol + c * 32, raw);
         tmem_wait_ld_dep(raw);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]) * sm_scale, u2f(raw[2 * i + 1]) * sm_scale);
-        uint4* dst = reinterpret_cast<uint4*>(dk + grow * D + c * 32);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-        tmem_ld32(t_lane + L::T_DV + c * 32, raw);
-        tmem_wait_ld_dep(raw);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]), u2f(raw[2 * i + 1]));
-        dst = reinterpret_cast<uint4*>(dv + grow * D + c * 32);
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]) * scale, u2f(raw[2 * i + 1]) * scale);
+        uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
 #pragma unroll
         for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
     } else if (ok && n == 0) {
-      uint4* a = reinterpret_cast<uint4*>(dk + grow * D);
-      uint4* c = reinterpret_cast<uint4*>(dv + grow * D);
+      uint4* a = reinterpret_cast<uint4*>(out);
 #pragma unroll
-      for (int i = 0; i < D / 8; ++i) a[i] = c[i] = make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < D / 8; ++i) a[i] = make_uint4(0, 0, 0, 0);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kBwdMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -774,7 +771,7 @@ struct DqLayout {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                  const float* __restrict__ lse, const float* __restrict__ delta, int64_t S, int wq,
@@ -805,8 +802,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(L::B_SF + i), 1);
-      mbar_init(bar(L::B_SE + i), 4);
-      mbar_init(bar(L::B_DF + i), 4);
+      mbar_init(bar(L::B_SE + i), 8);
+      mbar_init(bar(L::B_DF + i), 8);
       mbar_init(bar(L::B_DE + i), 1);
     }
     mbar_init(bar(L::B_FIN), 1);
@@ -814,7 +811,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == kBwdMmaWarp) {
     tmem_alloc(sb + L::TMEM_SLOT, 512);
     tmem_relinquish();
     tc_fence_before();
@@ -823,7 +820,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
 
-  if (warp == kProducerWarp) {
+  if (warp == kBwdProducerWarp) {
     if (lane == 0) {
       mbar_expect_tx(bar(L::B_QD), 2 * 128 * D * 2);
 #pragma unroll
@@ -863,10 +860,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(bar(L::B_VF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDqProducer);
       mbar_wait(bar(L::B_QD), 0, abort_flag, &g_tc_error, kErrDqProducer);
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kBwdMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
+      const uint64_t dQ = desc_k_sw128(sb + L::Q), dDO = desc_k_sw128(sb + L::DO),
+                     dKk = desc_k_sw128(sb + L::K), dVk = desc_k_sw128(sb + L::V),
+                     dKmn = desc_mn_sw128(sb + L::K, 8192), dDS = desc_k_sw128(sb + L::DS);
       bool ok = mbar_wait(bar(L::B_QD), 0, abort_flag, &g_tc_error, kErrDqMma);
       tc_fence_after();
       UnionIter it;
@@ -876,12 +876,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = j & 1, st = j % R;
         if (!mbar_wait(bar(L::B_DF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDqMma)) return false;
         tc_fence_after();
-#pragma unroll
-        for (int k16 = 0; k16 < 4; ++k16) {
-          const uint64_t a = desc_k_sw128(sb + L::DS + b * 16384 + k16 * 32);
-          const uint64_t bd = desc_mn_sw128(sb + L::K + st * L::kSub * 8192 + k16 * 2048, 8192);
-          mma_bf16(tmem + L::T_DQ, a, bd, IDESC_G, (j > 0 || k16 > 0) ? 1u : 0u);
-        }
+        mma_k64_kmn(tmem + L::T_DQ, dDS + b * (16384 >> 4), dKmn + st * (L::kSub * 8192 >> 4),
+                    IDESC_G, j > 0 ? 1u : 0u);
         mma_commit(bar(L::B_KE + st));
         mma_commit(bar(L::B_DE + b));
         return true;
@@ -899,25 +895,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = desc_k_sw128(sb + L::Q + (kk >> 2) * 16384 + (kk & 3) * 32);
-          const uint64_t bd =
-              desc_k_sw128(sb + L::K + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
-          mma_bf16(tmem + L::T_S + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
-        }
+        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + b * 64, dQ, dKk + st * (L::kSub * 8192 >> 4),
+                                     IDESC_S, 0u);
         if (!mbar_wait(bar(L::B_VF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDqMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = desc_k_sw128(sb + L::DO + (kk >> 2) * 16384 + (kk & 3) * 32);
-          const uint64_t bd =
-              desc_k_sw128(sb + L::V + st * L::kSub * 8192 + (kk >> 2) * 8192 + (kk & 3) * 32);
-          mma_bf16(tmem + L::T_DP + b * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
-        }
+        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_DP + b * 64, dDO, dVk + st * (L::kSub * 8192 >> 4),
+                                     IDESC_S, 0u);
         mma_commit(bar(L::B_VE + st));
         mma_commit(bar(L::B_SF + b));
         if (n >= 1 && !grads(n - 1)) {
@@ -932,9 +918,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDqMma);
     }
   } else {
-    const int r = threadIdx.x;
+    // softmax warpgroups: wg 0 takes key columns 0-31 of each step, wg 1 32-63
+    const int wg = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // query row within the CTA == TMEM lane
     const int half = r >> 6;
-    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const int64_t grow = (int64_t)row_base + r;
     const float mrow = lse[grow] * kRcpLn2;
     const float drow = delta[grow];
@@ -944,31 +932,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     while ((t = it.next(sel)) >= 0) {
       const int b = n & 1;
+      const uint64_t vb64 = ((sel >> half) & 1) ? tile_bits[t] : 0ull;
       if (!warp_wait(bar(L::B_SF + b), (n >> 1) & 1, abort_flag, kErrDqSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[64], dp[64];
-      tmem_load<2>(t_lane + L::T_S + b * 64, s);
-      tmem_load<2>(t_lane + L::T_DP + b * 64, dp);
+      float s[32], dp[32];
+      tmem_load<1>(t_lane + L::T_S + b * 64 + wg * 32, s);
+      tmem_load<1>(t_lane + L::T_DP + b * 64 + wg * 32, dp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(L::B_SE + b));
-      const uint64_t vb = ((sel >> half) & 1) ? tile_bits[t] : 0ull;
-      uint32_t pd[32];
-      if (vb == ~0ull) {
+      const uint32_t vb = (uint32_t)(vb64 >> (32 * wg));
+      uint32_t pd[16];
+      if (vb == 0xffffffffu) {
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           const float p0 = ex2(fmaf(s[c], qk_scale, -mrow));
           const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mrow));
           pd[c / 2] = pack_bf16(p0 * (dp[c] - drow), p1 * (dp[c + 1] - drow));
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
-          const float p0 = ((vb >> c) & 1ull) ? ex2(fmaf(s[c], qk_scale, -mrow)) : 0.0f;
-          const float p1 = ((vb >> (c + 1)) & 1ull) ? ex2(fmaf(s[c + 1], qk_scale, -mrow)) : 0.0f;
+        for (int c = 0; c < 32; c += 2) {
+          const float p0 = ((vb >> c) & 1u) ? ex2(fmaf(s[c], qk_scale, -mrow)) : 0.0f;
+          const float p1 = ((vb >> (c + 1)) & 1u) ? ex2(fmaf(s[c + 1], qk_scale, -mrow)) : 0.0f;
           pd[c / 2] = pack_bf16(p0 * (dp[c] - drow), p1 * (dp[c + 1] - drow));
         }
       }
@@ -978,36 +967,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint8_t* sDS = sm + L::DS + b * 16384;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(sDS + sw128_off(r, ch)) =
+      for (int ch = 0; ch < 4; ++ch)
+        *reinterpret_cast<uint4*>(sDS + sw128_off(r, wg * 4 + ch)) =
             make_uint4(pd[ch * 4], pd[ch * 4 + 1], pd[ch * 4 + 2], pd[ch * 4 + 3]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(L::B_DF + b));
       ++n;
     }
+    // epilogue: wg 0 writes dQ columns [0, D/2), wg 1 [D/2, D)
     if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDqSoftmax)) {
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < D / 64; ++c) {
+        const int col = wg * (D / 2) + c * 32;
         uint32_t raw[32], pk[16];
-        tmem_ld32(t_lane + L::T_DQ + c * 32, raw);
+        tmem_ld32(t_lane + L::T_DQ + col, raw);
         tmem_wait_ld_dep(raw);
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]) * sm_scale, u2f(raw[2 * i + 1]) * sm_scale);
-        uint4* dst = reinterpret_cast<uint4*>(dq + grow * D + c * 32);
+        uint4* dst = reinterpret_cast<uint4*>(dq + grow * D + col);
 #pragma unroll
         for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
     } else if (ok && n == 0) {
-      uint4* a = reinterpret_cast<uint4*>(dq + grow * D);
+      uint4* a = reinterpret_cast<uint4*>(dq + grow * D + wg * (D / 2));
 #pragma unroll
-      for (int i = 0; i < D / 8; ++i) a[i] = make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < D / 16; ++i) a[i] = make_uint4(0, 0, 0, 0);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kBwdMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -1099,7 +1090,7 @@ prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads
   PRISM_TRY(make_map(&mv, v, rows, D, "prism_bsa_fwd"));
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                    "prism_bsa_fwd: smem attribute");
-  fwd_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kThreads, sm, stream>>>(
+  fwd_tc_kernel<D><<<dim3((unsigned)((n_tiles + 3) / 4), heads), kFwdThreads, sm, stream>>>(
       mq, mk, mv, S, wq, sm_scale * kRcpLn2, bits_q, tile_bits, (__nv_bfloat16*)o, (__nv_bfloat16*)o_lo, lse);
   PRISM_CHECK_LAUNCH("prism_bsa_fwd");
   return PRISM_OK;
@@ -1132,7 +1123,7 @@ prism_status_t launch_dkdv(const void* q, const void* k, const void* v, const vo
   PRISM_TRY(make_map(&mdo, dout, rows, D, "prism_bsa_bwd_dkdv"));
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(dkdv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                    "prism_bsa_bwd: smem attribute");
-  dkdv_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kThreads, sm, stream>>>(
+  dkdv_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kBwdThreads, sm, stream>>>(
       mq, mk, mv, mdo, lse, delta, S, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
       (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
   PRISM_CHECK_LAUNCH("prism_bsa_bwd_dkdv");
@@ -1156,7 +1147,7 @@ prism_status_t launch_dq(const void* q, const void* k, const void* v, const void
   PRISM_TRY(make_map(&mdo, dout, rows, D, "prism_bsa_bwd_dq"));
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(dq_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                    "prism_bsa_bwd: smem attribute");
-  dq_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kThreads, sm, stream>>>(
+  dq_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kBwdThreads, sm, stream>>>(
       mq, mk, mv, mdo, lse, delta, S, wq, sm_scale * kRcpLn2, sm_scale, bits_q, tile_bits,
       (__nv_bfloat16*)dq);
   PRISM_CHECK_LAUNCH("prism_bsa_bwd_dq");

@@ -134,6 +134,75 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// A chain of 8 (or 4) MMAs into one accumulator, issued from one asm block:
+// D (+)= sum_i A_i * B_i with descriptors a_i = a0 + i-th A step, b_i = b0 +
+// i-th B step (steps in 16-byte units, compile-time).  The first product
+// accumulates into D only if `accumulate` is non-zero; the rest always do.
+// Issuing the chain from one block keeps the single MMA thread's per-MMA
+// work to one add and one instruction, so the tensor pipe never starves
+// behind descriptor arithmetic.
+template <int A1, int A2, int A3, int B1, int B2, int B3>
+__device__ __forceinline__ void mma_chain4(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p0, p1;\n .reg .b64 a1, a2, a3, b1, b2, b3;\n"
+      " setp.ne.b32 p0, %4, 0;\n setp.eq.b32 p1, %4, %4;\n"
+      " add.s64 a1, %1, %5;\n add.s64 a2, %1, %6;\n add.s64 a3, %1, %7;\n"
+      " add.s64 b1, %2, %8;\n add.s64 b2, %2, %9;\n add.s64 b3, %2, %10;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, p1;\n}\n" ::"r"(d_tmem),
+      "l"(a0), "l"(b0), "r"(idesc), "r"(accumulate), "n"(A1), "n"(A2), "n"(A3), "n"(B1), "n"(B2),
+      "n"(B3)
+      : "memory");
+}
+// K = 64 * KSUB reduction of two K-major SW128 operands: steps of 32 bytes
+// inside a 128-byte row, then the next sub-buffer (A_SUB / B_SUB bytes on).
+template <int KSUB, int A_SUB, int B_SUB>
+__device__ __forceinline__ void mma_kd(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc,
+                                       uint32_t accumulate) {
+  mma_chain4<2, 4, 6, 2, 4, 6>(d_tmem, a0, b0, idesc, accumulate);
+  if (KSUB > 1) mma_chain4<2, 4, 6, 2, 4, 6>(d_tmem, a0 + (A_SUB >> 4), b0 + (B_SUB >> 4), idesc, 1u);
+}
+// K = 64 reduction: K-major A (32-byte steps) x MN-major B (16 rows = 2048-byte steps).
+__device__ __forceinline__ void mma_k64_kmn(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc,
+                                            uint32_t accumulate) {
+  mma_chain4<2, 4, 6, 128, 256, 384>(d_tmem, a0, b0, idesc, accumulate);
+}
+// Same chain with A read from TMEM ("TS" form): A is M=128 rows (one per
+// lane) x K bf16, two K-consecutive elements per 32-bit column (even element
+// in the low half), so one K=16 step is 8 columns.  A steps are column
+// offsets, B steps descriptor offsets (16-byte units).  Only B is read from
+// shared memory, which halves the operand traffic of the SS form.
+template <int A1, int A2, int A3, int B1, int B2, int B3>
+__device__ __forceinline__ void mma_ts_chain4(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p0, p1;\n .reg .b32 a1, a2, a3;\n .reg .b64 b1, b2, b3;\n"
+      " setp.ne.b32 p0, %4, 0;\n setp.eq.b32 p1, %4, %4;\n"
+      " add.s32 a1, %1, %5;\n add.s32 a2, %1, %6;\n add.s32 a3, %1, %7;\n"
+      " add.s64 b1, %2, %8;\n add.s64 b2, %2, %9;\n add.s64 b3, %2, %10;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, p1;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate), "n"(A1), "n"(A2), "n"(A3), "n"(B1),
+      "n"(B2), "n"(B3)
+      : "memory");
+}
+// K = 64 * KSUB reduction, A from TMEM (K-packed columns), B K-major SW128.
+template <int KSUB, int B_SUB>
+__device__ __forceinline__ void mma_ts_kd(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
+                                          uint32_t accumulate) {
+  mma_ts_chain4<8, 16, 24, 2, 4, 6>(d_tmem, a_tmem, b0, idesc, accumulate);
+  if (KSUB > 1) mma_ts_chain4<8, 16, 24, 2, 4, 6>(d_tmem, a_tmem + 32, b0 + (B_SUB >> 4), idesc, 1u);
+}
+// K = 64 reduction, A from TMEM, B MN-major SW128 (16 rows = 2048-byte steps).
+__device__ __forceinline__ void mma_ts_k64_mn(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0,
+                                              uint32_t idesc, uint32_t accumulate) {
+  mma_ts_chain4<8, 16, 24, 128, 256, 384>(d_tmem, a_tmem, b0, idesc, accumulate);
+}
 // Arrive (once) on an mbarrier when all previously issued tcgen05.mma of this thread completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile(
