@@ -177,24 +177,35 @@ constexpr int kFwdThreads = 320;
 constexpr int kFwdProducerWarp = 8;
 constexpr int kFwdMmaWarp = 9;
 
+// Design budget: shared-memory bandwidth (128 B/clk/SM), which the TMA fills,
+// the tensor core's shared-memory operand reads and the mbarrier traffic all
+// share, and the tcgen05.mma shape: an M = 128 product costs at least ~45
+// clocks whatever its N, so N >= 128 is needed to run at the math rate.
+// The forward therefore takes key tiles two at a time (S = Q [K_a; K_b]^T,
+// N = 128), keeps P in TMEM (written by the softmax over the S columns it has
+// read) as the A operand of P V, and shares each K/V pair between two groups
+// of 128 query rows (256 rows per CTA), which halves the TMA bytes per FLOP.
 template <int D>
 struct FwdLayout {
-  static constexpr int kRing = 4;                       // K tiles and V tiles in flight
+  static constexpr int kRing = 2;                       // K pairs and V pairs in flight
   static constexpr int kSub = D / 64;                   // 128-byte sub-buffers per row
+  static constexpr int kPair = kSub * 16384;            // one 128-row pair slot
   static constexpr int Q = 0;                           // 2 groups x 128 rows
-  static constexpr int K = Q + 2 * kSub * 16384;        // kRing x 64 rows
-  static constexpr int V = K + kRing * kSub * 8192;
-  static constexpr int P = V + kRing * kSub * 8192;     // 2 groups x (128 rows x 64 keys)
-  static constexpr int BAR = P + 2 * 16384;
+  static constexpr int K = Q + 2 * kPair;               // kRing pair slots
+  static constexpr int V = K + kRing * kPair;
+  static constexpr int BAR = V + kRing * kPair;
   static constexpr int B_Q = 0, B_KF = 1, B_KE = B_KF + kRing, B_VF = B_KE + kRing,
-                       B_VE = B_VF + kRing, B_SF = B_VE + kRing,  // [g][b] at B_SF + 2g + b
-                       B_SE = B_SF + 4, B_PF = B_SE + 4,           // [g]
-                       B_PV = B_PF + 2, B_DRAIN = B_PV + 2, NBAR = B_DRAIN + 1;
+                       B_VE = B_VF + kRing,
+                       B_SF = B_VE + kRing,  // [g]: S_g ready
+                       B_PF = B_SF + 2,      // [g]: P_g in TMEM (and O_g rescaled)
+                       B_OF = B_PF + 2,      // [g]: last P V done
+                       B_DRAIN = B_OF + 2, NBAR = B_DRAIN + 1;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int ABORT = TMEM_SLOT + 4;
   static constexpr size_t kBytes = 1024 + ABORT + 4;
-  static constexpr int T_S = 0;      // S[g][b] at 128 g + 64 b
-  static constexpr int T_O = 256;    // O[g] at 256 + D g
+  // TMEM per group g at 256 g: S (128 f32 columns; P as 64 bf16x2 columns over
+  // its first half), O (D f32 columns)
+  static constexpr int T_S = 0, T_O = 128;
 };
 
 template <int D>
@@ -229,13 +240,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(bar(L::B_VF + i), 1);
       mbar_init(bar(L::B_VE + i), 1);
     }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(bar(L::B_SF + i), 1);
-      mbar_init(bar(L::B_SE + i), 4);
-    }
     for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(L::B_SF + g), 1);
       mbar_init(bar(L::B_PF + g), 4);
-      mbar_init(bar(L::B_PV + g), 1);
+      mbar_init(bar(L::B_OF + g), 1);
     }
     mbar_init(bar(L::B_DRAIN), 1);
     *abort_flag = 0;
@@ -258,93 +266,118 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int qb = 0; qb < nq; ++qb)
 #pragma unroll
         for (int s = 0; s < L::kSub; ++s)
-          tma_load_2d(sb + L::Q + (qb >> 1) * L::kSub * 16384 + s * 16384 + (qb & 1) * 8192, &tm_q,
-                      s * 64, row_base + qb * 64, bar(L::B_Q));
+          tma_load_2d(sb + L::Q + (qb >> 1) * L::kPair + s * 16384 + (qb & 1) * 8192, &tm_q, s * 64,
+                      row_base + qb * 64, bar(L::B_Q));
       UnionIter4 it;
       it.init(r0, r0 + wq, r2, r3, wq);
-      int nk = 0, nv = 0, sel = 0, t;
-      while ((t = it.next(sel)) >= 0) {
-        const int st = nk % R;
-        if (nk >= R && !mbar_wait(bar(L::B_KE + st), ((nk / R) - 1) & 1, abort_flag, &g_tc_error,
-                                  kErrFwdProducer))
+      int np = 0, sel = 0;
+      bool ok = true;
+      for (;;) {
+        const int t0 = it.next(sel);
+        if (t0 < 0) break;
+        const int t1 = it.next(sel);
+        const int cnt = t1 >= 0 ? 2 : 1;
+        const int st = np % R;
+        // K pair, then V pair, each into one 128-row slot (tile a rows 0-63, tile b 64-127)
+        if (np >= R && !mbar_wait(bar(L::B_KE + st), ((np / R) - 1) & 1, abort_flag, &g_tc_error,
+                                  kErrFwdProducer)) {
+          ok = false;
           break;
-        mbar_expect_tx(bar(L::B_KF + st), 64 * D * 2);
+        }
+        mbar_expect_tx(bar(L::B_KF + st), cnt * 64 * D * 2);
+        for (int u = 0; u < cnt; ++u)
 #pragma unroll
-        for (int s = 0; s < L::kSub; ++s)
-          tma_load_2d(sb + L::K + st * L::kSub * 8192 + s * 8192, &tm_k, s * 64, head_row + t * 64,
-                      bar(L::B_KF + st));
-        ++nk;
-        if (nv >= R && !mbar_wait(bar(L::B_VE + st), ((nv / R) - 1) & 1, abort_flag, &g_tc_error,
-                                  kErrFwdProducer))
+          for (int s = 0; s < L::kSub; ++s)
+            tma_load_2d(sb + L::K + st * L::kPair + s * 16384 + u * 8192, &tm_k, s * 64,
+                        head_row + (u ? t1 : t0) * 64, bar(L::B_KF + st));
+        if (np >= R && !mbar_wait(bar(L::B_VE + st), ((np / R) - 1) & 1, abort_flag, &g_tc_error,
+                                  kErrFwdProducer)) {
+          ok = false;
+          ++np;  // the K pair of this step is in flight: drain it below
           break;
-        mbar_expect_tx(bar(L::B_VF + st), 64 * D * 2);
+        }
+        mbar_expect_tx(bar(L::B_VF + st), cnt * 64 * D * 2);
+        for (int u = 0; u < cnt; ++u)
 #pragma unroll
-        for (int s = 0; s < L::kSub; ++s)
-          tma_load_2d(sb + L::V + st * L::kSub * 8192 + s * 8192, &tm_v, s * 64, head_row + t * 64,
-                      bar(L::B_VF + st));
-        ++nv;
+          for (int s = 0; s < L::kSub; ++s)
+            tma_load_2d(sb + L::V + st * L::kPair + s * 16384 + u * 8192, &tm_v, s * 64,
+                        head_row + (u ? t1 : t0) * 64, bar(L::B_VF + st));
+        ++np;
+        if (t1 < 0) break;
       }
       // drain: every issued load has landed before the CTA may exit
-      for (int m = (nk > R ? nk - R : 0); m < nk; ++m)
+      for (int m = (np > R ? np - R : 0); m < np; ++m) {
         mbar_wait(bar(L::B_KF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrFwdProducer);
-      for (int m = (nv > R ? nv - R : 0); m < nv; ++m)
-        mbar_wait(bar(L::B_VF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrFwdProducer);
+        if (ok || m + 1 < np)
+          mbar_wait(bar(L::B_VF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrFwdProducer);
+      }
       mbar_wait(bar(L::B_Q), 0, abort_flag, &g_tc_error, kErrFwdProducer);
     }
   } else if (warp == kFwdMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
+    // Per key pair n: PV_0(n-1), S_0(n), PV_1(n-1), S_1(n).  S_g(n) overwrites
+    // the columns that held P_g(n-1); it is issued after PV_g(n-1), and the
+    // tensor pipe performs one thread's MMAs in issue order.
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t IDESC_S2 = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t IDESC_S1 = idesc_bf16(128, 64, false, false);
       constexpr uint32_t IDESC_PV = idesc_bf16(128, D, false, true);
       const int ng = g1_live ? 2 : 1;
-      // descriptor bases (start-address field advanced by byte offset >> 4)
       const uint64_t dQ = desc_k_sw128(sb + L::Q), dK = desc_k_sw128(sb + L::K),
-                     dP = desc_k_sw128(sb + L::P), dV = desc_mn_sw128(sb + L::V, 8192);
+                     dV = desc_mn_sw128(sb + L::V, 16384);
       bool ok = mbar_wait(bar(L::B_Q), 0, abort_flag, &g_tc_error, kErrFwdMma);
       tc_fence_after();
       UnionIter4 it;
       it.init(r0, r0 + wq, r2, r3, wq);
-      auto issue_pv = [&](int j) -> bool {
-        const int st = j % R;
-        if (!mbar_wait(bar(L::B_VF + st), (j / R) & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
-        for (int g = 0; g < ng; ++g) {
-          if (!mbar_wait(bar(L::B_PF + g), j & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
-          tc_fence_after();
-          mma_k64_kmn(tmem + L::T_O + g * D, dP + g * (16384 >> 4),
-                      dV + st * (L::kSub * 8192 >> 4), IDESC_PV, j > 0 ? 1u : 0u);
-          mma_commit(bar(L::B_PV + g));
-        }
-        mma_commit(bar(L::B_VE + st));
+      // P V of pair j for group g: K = 64 keys per tile of the pair
+      auto pv = [&](int g, int j, int cnt) -> bool {
+        if (!mbar_wait(bar(L::B_PF + g), j & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
+        tc_fence_after();
+        const uint64_t bv = dV + (j % R) * (L::kPair >> 4);
+        mma_ts_k64_mn(tmem + g * 256 + L::T_O, tmem + g * 256 + L::T_S, bv, IDESC_PV, j > 0 ? 1u : 0u);
+        if (cnt == 2)
+          mma_ts_k64_mn(tmem + g * 256 + L::T_O, tmem + g * 256 + L::T_S + 32, bv + (8192 >> 4),
+                        IDESC_PV, 1u);
         return true;
       };
-      int n = 0, sel = 0, t;
-      while (ok && (t = it.next(sel)) >= 0) {
-        const int st = n % R, b = n & 1;
-        if (!mbar_wait(bar(L::B_KF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrFwdMma)) {
+      int n = 0, sel = 0, prev_cnt = 0;
+      while (ok) {
+        const int t0 = it.next(sel);
+        if (t0 < 0) break;
+        const int t1 = it.next(sel);
+        const int cnt = t1 >= 0 ? 2 : 1;
+        const int st = n % R;
+        if (!mbar_wait(bar(L::B_KF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrFwdMma) ||
+            (n > 0 && !mbar_wait(bar(L::B_VF + (n - 1) % R), ((n - 1) / R) & 1, abort_flag,
+                                 &g_tc_error, kErrFwdMma))) {
           ok = false;
           break;
         }
-        for (int g = 0; g < ng && ok; ++g) {
-          if (n >= 2 && !mbar_wait(bar(L::B_SE + 2 * g + b), ((n >> 1) - 1) & 1, abort_flag,
-                                   &g_tc_error, kErrFwdMma)) {
+        for (int g = 0; g < ng; ++g) {
+          if (n > 0 && !pv(g, n - 1, prev_cnt)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + g * 128 + b * 64,
-                                       dQ + g * (L::kSub * 16384 >> 4),
-                                       dK + st * (L::kSub * 8192 >> 4), IDESC_S, 0u);
-          mma_commit(bar(L::B_SF + 2 * g + b));
+          mma_kd<L::kSub, 16384, 16384>(tmem + g * 256 + L::T_S, dQ + g * (L::kPair >> 4),
+                                        dK + st * (L::kPair >> 4), cnt == 2 ? IDESC_S2 : IDESC_S1, 0u);
+          mma_commit(bar(L::B_SF + g));
         }
         if (!ok) break;
         mma_commit(bar(L::B_KE + st));
-        if (n >= 1 && !issue_pv(n - 1)) {
-          ok = false;
-          break;
-        }
+        if (n > 0) mma_commit(bar(L::B_VE + (n - 1) % R));
+        prev_cnt = cnt;
         ++n;
+        if (t1 < 0) break;
       }
-      if (ok && n >= 1) issue_pv(n - 1);
+      if (ok && n > 0) {
+        if (mbar_wait(bar(L::B_VF + (n - 1) % R), ((n - 1) / R) & 1, abort_flag, &g_tc_error,
+                      kErrFwdMma)) {
+          for (int g = 0; g < ng; ++g) {
+            if (!pv(g, n - 1, prev_cnt)) break;
+            mma_commit(bar(L::B_OF + g));
+          }
+        }
+      }
       // drain: all issued MMAs complete before TMEM is released
       mma_commit(bar(L::B_DRAIN));
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrFwdMma);
@@ -354,110 +387,116 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int g = warp >> 2;
     const int r = (warp & 3) * 32 + lane;  // row within the group == TMEM lane
     const int sbit = 2 * g + (r >> 6);     // bitmap row of this thread's q tile
-    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + g * 256;
     float m = -INFINITY, l = 1.0f;
     UnionIter4 it;
     it.init(r0, r0 + wq, r2, r3, wq);
-    int n = 0, sel = 0, t;
+    int n = 0, sel0 = 0, sel1 = 0;
     bool ok = true;
-    uint8_t* sP = sm + L::P + g * 16384;
-    while ((t = it.next(sel)) >= 0) {
-      const int b = n & 1;
-      const uint64_t vb = ((sel >> sbit) & 1) ? tile_bits[t] : 0ull;
-      if (!warp_wait(bar(L::B_SF + 2 * g + b), (n >> 1) & 1, abort_flag, kErrFwdSoftmax)) {
+    for (;;) {
+      const int t0 = it.next(sel0);
+      if (t0 < 0) break;
+      const int t1 = it.next(sel1);
+      const uint64_t vb0 = ((sel0 >> sbit) & 1) ? tile_bits[t0] : 0ull;
+      const uint64_t vb1 = (t1 >= 0 && ((sel1 >> sbit) & 1)) ? tile_bits[t1] : 0ull;
+      if (!warp_wait(bar(L::B_SF + g), n & 1, abort_flag, kErrFwdSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[64];
-      tmem_load<2>(t_lane + L::T_S + g * 128 + b * 64, s);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_SE + 2 * g + b));
-      // masks: row did not select the tile -> all keys masked; else key validity
-      if (vb != ~0ull) {
+      // pass 1: row maximum over the valid, selected keys (64 columns at a time)
+      float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (!((vb >> c) & 1ull)) s[c] = -INFINITY;
-      }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+      for (int u = 0; u < 2; ++u) {
+        const uint64_t vb = u ? vb1 : vb0;
+        if (vb == 0ull) continue;  // warp-uniform: the whole half-row of this tile is masked
+        float s[64];
+        tmem_load<2>(t_lane + L::T_S + u * 64, s);
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+        if (vb == ~0ull) {
 #pragma unroll
-      for (int c = 4; c < 64; c += 4) {
-        mx0 = fmaxf(mx0, s[c]);
-        mx1 = fmaxf(mx1, s[c + 1]);
-        mx2 = fmaxf(mx2, s[c + 2]);
-        mx3 = fmaxf(mx3, s[c + 3]);
+          for (int c = 0; c < 64; c += 4) {
+            m0 = fmaxf(m0, s[c]);
+            m1 = fmaxf(m1, s[c + 1]);
+            m2 = fmaxf(m2, s[c + 2]);
+            m3 = fmaxf(m3, s[c + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if ((vb >> c) & 1ull) m0 = fmaxf(m0, s[c]);
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
       }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * qk_scale;
+      mx *= qk_scale;
       const bool need = mx > m + kRescaleThreshold;  // m = -inf: any valid key
-      bool waited_pv = false;
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = need ? mx : m;
         const float alpha = need ? ex2(m - m_new) : 1.0f;  // m = -inf -> 0
         const bool o_live = __any_sync(0xffffffffu, need && m != -INFINITY);
         l *= alpha;
         m = m_new;
+        // every P V before this pair has completed: S_g(n) was issued after them
         if (n > 0 && o_live) {
-          if (!warp_wait(bar(L::B_PV + g), (n - 1) & 1, abort_flag, kErrFwdSoftmax)) {
-            ok = false;
-            break;
-          }
-          waited_pv = true;
-          tc_fence_after();
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t raw[32];
-            tmem_ld32(t_lane + L::T_O + g * D + c * 32, raw);
+            tmem_ld32(t_lane + L::T_O + c * 32, raw);
             tmem_wait_ld_dep(raw);
 #pragma unroll
             for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
-            tmem_st32(t_lane + L::T_O + g * D + c * 32, raw);
+            tmem_st32(t_lane + L::T_O + c * 32, raw);
           }
-          tmem_wait_st();
         }
       }
+      // pass 2: p = exp2(s * scale - m) -> bf16 P over the first 64 columns of S
       const float mb = (m == -INFINITY) ? 0.0f : m;
-      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-      uint32_t pk[32];
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) {
-        const float p0 = ex2(fmaf(s[c], qk_scale, -mb));
-        const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mb));
-        const float p2 = ex2(fmaf(s[c + 2], qk_scale, -mb));
-        const float p3 = ex2(fmaf(s[c + 3], qk_scale, -mb));
-        sum0 += p0;
-        sum1 += p1;
-        sum2 += p2;
-        sum3 += p3;
-        pk[c / 2] = pack_bf16(p0, p1);
-        pk[c / 2 + 1] = pack_bf16(p2, p3);
-      }
-      l += (sum0 + sum1) + (sum2 + sum3);
-      if (n > 0 && !waited_pv) {
-        if (!warp_wait(bar(L::B_PV + g), (n - 1) & 1, abort_flag, kErrFwdSoftmax)) {
-          ok = false;
-          break;
+      for (int u = 0; u < 2; ++u) {
+        const uint64_t vb = u ? vb1 : vb0;
+        uint32_t pk[32];
+        if (vb == 0ull) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = 0u;
+        } else {
+          float s[64];
+          tmem_load<2>(t_lane + L::T_S + u * 64, s);
+          if (vb != ~0ull) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if (!((vb >> c) & 1ull)) s[c] = -INFINITY;
+          }
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float p0 = ex2(fmaf(s[c], qk_scale, -mb));
+            const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mb));
+            sum0 += p0;
+            sum1 += p1;
+            pk[c / 2] = pack_bf16(p0, p1);
+          }
         }
+        // P columns [32 u, 32 u + 32) overlap S columns [0, 64), which pass 2
+        // has already read for u = 0 and does not read again
+        tmem_st32(t_lane + L::T_S + u * 32, pk);
       }
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(sP + sw128_off(r, ch)) =
-            make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-      fence_proxy_async_smem();
+      l += sum0 + sum1;
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(L::B_PF + g));
       ++n;
+      if (t1 < 0) break;
     }
     // epilogue
     const int64_t grow = (int64_t)row_base + g * 128 + r;
-    if (ok && n > 0 && warp_wait(bar(L::B_PV + g), (n - 1) & 1, abort_flag, kErrFwdSoftmax)) {
+    if (ok && n > 0 && warp_wait(bar(L::B_OF + g), 0, abort_flag, kErrFwdSoftmax)) {
       tc_fence_after();
       const float inv = 1.0f / l;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t raw[32];
-        tmem_ld32(t_lane + L::T_O + g * D + c * 32, raw);
+        tmem_ld32(t_lane + L::T_O + c * 32, raw);
         tmem_wait_ld_dep(raw);
         uint32_t hi[16], lo[16];
 #pragma unroll
