@@ -537,26 +537,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ================================================================== dK / dV
+// CTA = 128 keys (tiles 2p, 2p+1); per step one query tile of the transposed
+// selection (N = 64), with S^T and dP^T double-buffered in TMEM so that the
+// softmax of step n overlaps the products of steps n-1 and n+1.  The softmax
+// warpgroups (wg 0: query columns 0-31, wg 1: 32-63) write P^T and
+// dS^T = P^T (dP^T - delta) as bf16 over the S^T / dP^T columns they have
+// read, and dV += P^T dO, dK += dS^T Q take them from TMEM (TS form: only dO /
+// Q are read from shared memory).  TMEM is full (dK, dV: 2 x 128 columns;
+// S^T, dP^T: 2 x 2 x 64), which is what fixes N = 64 here.
 template <int D>
 struct DkdvLayout {
-  static constexpr int kRing = 3;
+  static constexpr int kRing = 4;
   static constexpr int kSub = D / 64;
   static constexpr int K = 0;                              // 128 keys
   static constexpr int V = K + kSub * 16384;
   static constexpr int Q = V + kSub * 16384;               // kRing x 64 queries
   static constexpr int DO = Q + kRing * kSub * 8192;
-  static constexpr int PT = DO + kRing * kSub * 8192;      // 2 x (128 keys x 64 queries)
-  static constexpr int DST = PT + 2 * 16384;
-  static constexpr int M = DST + 2 * 16384;                // kRing x 64 f32 (lse)
+  static constexpr int M = DO + kRing * kSub * 8192;       // kRing x 64 f32 (lse)
   static constexpr int DL = M + kRing * 256;               // kRing x 64 f32 (delta)
   static constexpr int BAR = DL + kRing * 256;
-  static constexpr int B_KV = 0, B_QF = 1, B_QE = 1 + kRing, B_SF = 1 + 2 * kRing, B_SE = B_SF + 2,
-                       B_DF = B_SE + 2, B_DE = B_DF + 2, B_FIN = B_DE + 2, B_DRAIN = B_FIN + 1,
-                       NBAR = B_DRAIN + 1;
+  static constexpr int B_KV = 0, B_QF = 1, B_QE = 1 + kRing, B_SF = 1 + 2 * kRing,  // [b]
+                       B_DPF = B_SF + 2, B_PF = B_DPF + 2, B_DSF = B_PF + 2,        // [b]
+                       B_FIN = B_DSF + 2, B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int ABORT = TMEM_SLOT + 4;
   static constexpr size_t kBytes = 1024 + ABORT + 4;
-  static constexpr int T_DK = 0, T_DV = D, T_S = 2 * D, T_DP = 2 * D + 128;
+  // TMEM: dK, dV (D f32 columns each), S^T[b], dP^T[b] (64 f32 columns each;
+  // the bf16 P^T / dS^T of query columns [32 w, 32 w + 32) over columns
+  // [32 w, 32 w + 16) of them)
+  static constexpr int T_DK = 0, T_DV = 128, T_S = 256, T_DP = 384;
 };
 
 template <int D>
@@ -590,9 +599,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(L::B_SF + i), 1);
-      mbar_init(bar(L::B_SE + i), 8);
-      mbar_init(bar(L::B_DF + i), 8);
-      mbar_init(bar(L::B_DE + i), 1);
+      mbar_init(bar(L::B_DPF + i), 1);
+      mbar_init(bar(L::B_PF + i), 8);
+      mbar_init(bar(L::B_DSF + i), 8);
     }
     mbar_init(bar(L::B_FIN), 1);
     mbar_init(bar(L::B_DRAIN), 1);
@@ -643,55 +652,55 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
     }
   } else if (warp == kBwdMmaWarp) {
+    // Issue order: S^T(0) dP^T(0) | S^T(1) dP^T(1) dV(0) dK(0) | S^T(2) ...
+    // S^T(n+2) / dP^T(n+2) overwrite the P^T / dS^T of step n; they are issued
+    // after dV(n) / dK(n), and one thread's MMAs are performed in order.
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
       const uint64_t dK = desc_k_sw128(sb + L::K), dV = desc_k_sw128(sb + L::V),
                      dQk = desc_k_sw128(sb + L::Q), dDOk = desc_k_sw128(sb + L::DO),
-                     dQmn = desc_mn_sw128(sb + L::Q, 8192), dDOmn = desc_mn_sw128(sb + L::DO, 8192),
-                     dPT = desc_k_sw128(sb + L::PT), dDST = desc_k_sw128(sb + L::DST);
+                     dQmn = desc_mn_sw128(sb + L::Q, 8192), dDOmn = desc_mn_sw128(sb + L::DO, 8192);
       bool ok = mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
       tc_fence_after();
       UnionIter it;
       it.init(row_a, row_b, wq);
-      int n = 0;
       auto grads = [&](int j) -> bool {
         const int b = j & 1, st = j % R;
-        if (!mbar_wait(bar(L::B_DF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
+        if (!mbar_wait(bar(L::B_PF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
         tc_fence_after();
-        mma_k64_kmn(tmem + L::T_DV, dPT + b * (16384 >> 4), dDOmn + st * (L::kSub * 8192 >> 4),
-                    IDESC_G, j > 0 ? 1u : 0u);
-        mma_k64_kmn(tmem + L::T_DK, dDST + b * (16384 >> 4), dQmn + st * (L::kSub * 8192 >> 4),
-                    IDESC_G, j > 0 ? 1u : 0u);
+        mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S + b * 64,
+                                                dDOmn + st * (L::kSub * 8192 >> 4), IDESC_G,
+                                                j > 0 ? 1u : 0u);
+        if (!mbar_wait(bar(L::B_DSF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
+        tc_fence_after();
+        mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP + b * 64,
+                                                dQmn + st * (L::kSub * 8192 >> 4), IDESC_G,
+                                                j > 0 ? 1u : 0u);
         mma_commit(bar(L::B_QE + st));
-        mma_commit(bar(L::B_DE + b));
         return true;
       };
-      int sel = 0, t;
+      int n = 0, sel = 0, t;
       while (ok && (t = it.next(sel)) >= 0) {
         const int st = n % R, b = n & 1;
         if (!mbar_wait(bar(L::B_QF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) {
           ok = false;
           break;
         }
-        if (n >= 2 && !mbar_wait(bar(L::B_SE + b), ((n >> 1) - 1) & 1, abort_flag, &g_tc_error,
-                                 kErrDkdvMma)) {
-          ok = false;
-          break;
-        }
         tc_fence_after();
         mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + b * 64, dK, dQk + st * (L::kSub * 8192 >> 4),
                                      IDESC_S, 0u);
+        mma_commit(bar(L::B_SF + b));
         mma_kd<L::kSub, 16384, 8192>(tmem + L::T_DP + b * 64, dV, dDOk + st * (L::kSub * 8192 >> 4),
                                      IDESC_S, 0u);
-        mma_commit(bar(L::B_SF + b));
+        mma_commit(bar(L::B_DPF + b));
         if (n >= 1 && !grads(n - 1)) {
           ok = false;
           break;
         }
         ++n;
       }
-      if (ok && n >= 1) ok = grads(n - 1);
+      if (ok && n >= 1) grads(n - 1);
       mma_commit(bar(L::B_FIN));
       mma_commit(bar(L::B_DRAIN));
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
@@ -711,50 +720,66 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
     while ((t = it.next(sel)) >= 0) {
       const int st = n % R, b = n & 1;
+      const bool tile_on = (sel >> half) & 1;  // warp-uniform
+      const bool on = tile_on && kvalid;
       if (!warp_wait(bar(L::B_QF + st), (n / R) & 1, abort_flag, kErrDkdvSoftmax) ||
           !warp_wait(bar(L::B_SF + b), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[32], dp[32];
-      tmem_load<1>(t_lane + L::T_S + b * 64 + wg * 32, s);
-      tmem_load<1>(t_lane + L::T_DP + b * 64 + wg * 32, dp);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_SE + b));
-      const bool on = kvalid && ((sel >> half) & 1);
-      uint32_t pp[16], pd[16];
-      const float* m_st = sM + st * 64 + wg * 32;
-      const float* d_st = sDl + st * 64 + wg * 32;
-      if (on) {
+      // lse / delta of this warpgroup's 32 query columns: every lane reads the
+      // same 16 bytes at a time (broadcast)
+      const float4* m_st = reinterpret_cast<const float4*>(sM + st * 64 + wg * 32);
+      const float4* d_st = reinterpret_cast<const float4*>(sDl + st * 64 + wg * 32);
+      float p[32];
+      uint32_t pk[16];
+      if (tile_on) {
+        tmem_load<1>(t_lane + L::T_S + b * 64 + wg * 32, p);
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float p0 = ex2(fmaf(s[c], qk_scale, -m_st[c] * kRcpLn2));
-          const float p1 = ex2(fmaf(s[c + 1], qk_scale, -m_st[c + 1] * kRcpLn2));
-          pp[c / 2] = pack_bf16(p0, p1);
-          pd[c / 2] = pack_bf16(p0 * (dp[c] - d_st[c]), p1 * (dp[c + 1] - d_st[c + 1]));
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 mv = m_st[c4];
+          const float mm[4] = {mv.x * kRcpLn2, mv.y * kRcpLn2, mv.z * kRcpLn2, mv.w * kRcpLn2};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = 4 * c4 + j;
+            p[c] = on ? ex2(fmaf(p[c], qk_scale, -mm[j])) : 0.0f;
+          }
         }
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) pk[c / 2] = pack_bf16(p[c], p[c + 1]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pp[i] = pd[i] = 0u;
+        for (int c = 0; c < 32; ++c) p[c] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = 0u;
       }
-      if (n >= 2 && !warp_wait(bar(L::B_DE + b), ((n >> 1) - 1) & 1, abort_flag, kErrDkdvSoftmax)) {
+      tmem_st16(t_lane + L::T_S + b * 64 + wg * 32, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_PF + b));
+      if (!warp_wait(bar(L::B_DPF + b), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax)) {
         ok = false;
         break;
       }
-      uint8_t* sPT = sm + L::PT + b * 16384;
-      uint8_t* sDST = sm + L::DST + b * 16384;
+      tc_fence_after();
+      if (tile_on) {
+        float dp[32];
+        tmem_load<1>(t_lane + L::T_DP + b * 64 + wg * 32, dp);
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        *reinterpret_cast<uint4*>(sPT + sw128_off(r, wg * 4 + ch)) =
-            make_uint4(pp[ch * 4], pp[ch * 4 + 1], pp[ch * 4 + 2], pp[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(sDST + sw128_off(r, wg * 4 + ch)) =
-            make_uint4(pd[ch * 4], pd[ch * 4 + 1], pd[ch * 4 + 2], pd[ch * 4 + 3]);
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 dv4 = d_st[c4];
+          const int c = 4 * c4;
+          pk[c / 2] = pack_bf16(p[c] * (dp[c] - dv4.x), p[c + 1] * (dp[c + 1] - dv4.y));
+          pk[c / 2 + 1] = pack_bf16(p[c + 2] * (dp[c + 2] - dv4.z), p[c + 3] * (dp[c + 3] - dv4.w));
+        }
       }
-      fence_proxy_async_smem();
+      tmem_st16(t_lane + L::T_DP + b * 64 + wg * 32, pk);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_DF + b));
+      if (lane == 0) mbar_arrive(bar(L::B_DSF + b));
       ++n;
     }
     // epilogue: wg 0 writes dK (scaled by sm_scale), wg 1 writes dV
@@ -766,14 +791,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
-        uint32_t raw[32], pk[16];
+        uint32_t raw[32], pk2[16];
         tmem_ld32(t_lane + tcol + c * 32, raw);
         tmem_wait_ld_dep(raw);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(u2f(raw[2 * i]) * scale, u2f(raw[2 * i + 1]) * scale);
+        for (int i = 0; i < 16; ++i) pk2[i] = pack_bf16(u2f(raw[2 * i]) * scale, u2f(raw[2 * i + 1]) * scale);
         uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk2[4 * i], pk2[4 * i + 1], pk2[4 * i + 2], pk2[4 * i + 3]);
       }
     } else if (ok && n == 0) {
       uint4* a = reinterpret_cast<uint4*>(out);
@@ -790,23 +815,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 // ======================================================================= dQ
+// CTA = 128 queries (tiles 2p, 2p+1); per step a PAIR of key tiles (N = 128):
+// S = Q [K_a; K_b]^T and dP = dO [V_a; V_b]^T in TMEM; the softmax warpgroups
+// (wg 0: key tile a, wg 1: key tile b) compute dS = P (dP - delta) into TMEM
+// columns of its own, and dQ += dS [K_a; K_b] reads them from there.  The MMA
+// thread issues S(n+1) and dP(n+1) as soon as the softmax has read S(n) and
+// dP(n), and dQ(n) when dS(n) is written, so the tensor core works on the next
+// pair while the softmax of this one runs.
 template <int D>
 struct DqLayout {
-  static constexpr int kRing = 4;
+  static constexpr int kRingK = 3;                         // K pairs (used by S and dQ)
+  static constexpr int kRingV = 2;                         // V pairs (used by dP)
   static constexpr int kSub = D / 64;
+  static constexpr int kPair = kSub * 16384;
   static constexpr int Q = 0;                              // 128 queries
-  static constexpr int DO = Q + kSub * 16384;
-  static constexpr int K = DO + kSub * 16384;              // kRing x 64 keys
-  static constexpr int V = K + kRing * kSub * 8192;
-  static constexpr int DS = V + kRing * kSub * 8192;       // 2 x (128 queries x 64 keys)
-  static constexpr int BAR = DS + 2 * 16384;
-  static constexpr int B_QD = 0, B_KF = 1, B_KE = B_KF + kRing, B_VF = B_KE + kRing,
-                       B_VE = B_VF + kRing, B_SF = B_VE + kRing, B_SE = B_SF + 2, B_DF = B_SE + 2,
-                       B_DE = B_DF + 2, B_FIN = B_DE + 2, B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
+  static constexpr int DO = Q + kPair;
+  static constexpr int K = DO + kPair;
+  static constexpr int V = K + kRingK * kPair;
+  static constexpr int BAR = V + kRingV * kPair;
+  static constexpr int B_QD = 0, B_KF = 1, B_KE = B_KF + kRingK, B_VF = B_KE + kRingK,
+                       B_VE = B_VF + kRingV, B_SF = B_VE + kRingV, B_SE = B_SF + 1, B_DPF = B_SE + 1,
+                       B_DPE = B_DPF + 1, B_DSF = B_DPE + 1, B_DSE = B_DSF + 1, B_FIN = B_DSE + 1,
+                       B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int ABORT = TMEM_SLOT + 4;
   static constexpr size_t kBytes = 1024 + ABORT + 4;
-  static constexpr int T_DQ = 0, T_S = D, T_DP = D + 128;
+  // TMEM: dQ (D f32 columns), S and dP (128 f32 columns each), dS (key tile u
+  // as 32 bf16x2 columns at T_DS + 32 u)
+  static constexpr int T_DQ = 0, T_S = 128, T_DP = 256, T_DS = 384;
 };
 
 template <int D>
@@ -817,7 +853,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                  float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_q,
                  const uint64_t* __restrict__ tile_bits, __nv_bfloat16* __restrict__ dq) {
   using L = DqLayout<D>;
-  constexpr int R = L::kRing;
+  constexpr int RK = L::kRingK, RV = L::kRingV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const uint32_t sb = smem_u32(sm);
@@ -833,18 +869,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(L::B_QD), 1);
-    for (int i = 0; i < R; ++i) {
+    for (int i = 0; i < RK; ++i) {
       mbar_init(bar(L::B_KF + i), 1);
       mbar_init(bar(L::B_KE + i), 1);
+    }
+    for (int i = 0; i < RV; ++i) {
       mbar_init(bar(L::B_VF + i), 1);
       mbar_init(bar(L::B_VE + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(L::B_SF + i), 1);
-      mbar_init(bar(L::B_SE + i), 8);
-      mbar_init(bar(L::B_DF + i), 8);
-      mbar_init(bar(L::B_DE + i), 1);
-    }
+    mbar_init(bar(L::B_SF), 1);
+    mbar_init(bar(L::B_SE), 8);
+    mbar_init(bar(L::B_DPF), 1);
+    mbar_init(bar(L::B_DPE), 8);
+    mbar_init(bar(L::B_DSF), 8);
+    mbar_init(bar(L::B_DSE), 1);
     mbar_init(bar(L::B_FIN), 1);
     mbar_init(bar(L::B_DRAIN), 1);
     *abort_flag = 0;
@@ -871,93 +909,106 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       UnionIter it;
       it.init(row_a, row_b, wq);
-      int nk = 0, nv = 0, sel = 0, t;
-      while ((t = it.next(sel)) >= 0) {
-        const int st = nk % R;
-        if (nk >= R && !mbar_wait(bar(L::B_KE + st), ((nk / R) - 1) & 1, abort_flag, &g_tc_error,
-                                  kErrDqProducer))
+      int nk = 0, nv = 0, sel = 0;
+      for (;;) {
+        const int t0 = it.next(sel);
+        if (t0 < 0) break;
+        const int t1 = it.next(sel);
+        const int cnt = t1 >= 0 ? 2 : 1;
+        const int sk = nk % RK, sv = nv % RV;
+        if (nk >= RK && !mbar_wait(bar(L::B_KE + sk), ((nk / RK) - 1) & 1, abort_flag, &g_tc_error,
+                                   kErrDqProducer))
           break;
-        mbar_expect_tx(bar(L::B_KF + st), 64 * D * 2);
+        mbar_expect_tx(bar(L::B_KF + sk), cnt * 64 * D * 2);
+        for (int u = 0; u < cnt; ++u)
 #pragma unroll
-        for (int s = 0; s < L::kSub; ++s)
-          tma_load_2d(sb + L::K + st * L::kSub * 8192 + s * 8192, &tm_k, s * 64, head_row + t * 64,
-                      bar(L::B_KF + st));
+          for (int s = 0; s < L::kSub; ++s)
+            tma_load_2d(sb + L::K + sk * L::kPair + s * 16384 + u * 8192, &tm_k, s * 64,
+                        head_row + (u ? t1 : t0) * 64, bar(L::B_KF + sk));
         ++nk;
-        if (nv >= R && !mbar_wait(bar(L::B_VE + st), ((nv / R) - 1) & 1, abort_flag, &g_tc_error,
-                                  kErrDqProducer))
+        if (nv >= RV && !mbar_wait(bar(L::B_VE + sv), ((nv / RV) - 1) & 1, abort_flag, &g_tc_error,
+                                   kErrDqProducer))
           break;
-        mbar_expect_tx(bar(L::B_VF + st), 64 * D * 2);
+        mbar_expect_tx(bar(L::B_VF + sv), cnt * 64 * D * 2);
+        for (int u = 0; u < cnt; ++u)
 #pragma unroll
-        for (int s = 0; s < L::kSub; ++s)
-          tma_load_2d(sb + L::V + st * L::kSub * 8192 + s * 8192, &tm_v, s * 64, head_row + t * 64,
-                      bar(L::B_VF + st));
+          for (int s = 0; s < L::kSub; ++s)
+            tma_load_2d(sb + L::V + sv * L::kPair + s * 16384 + u * 8192, &tm_v, s * 64,
+                        head_row + (u ? t1 : t0) * 64, bar(L::B_VF + sv));
         ++nv;
+        if (t1 < 0) break;
       }
-      for (int m = (nk > R ? nk - R : 0); m < nk; ++m)
-        mbar_wait(bar(L::B_KF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDqProducer);
-      for (int m = (nv > R ? nv - R : 0); m < nv; ++m)
-        mbar_wait(bar(L::B_VF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDqProducer);
+      for (int m = (nk > RK ? nk - RK : 0); m < nk; ++m)
+        mbar_wait(bar(L::B_KF + m % RK), (m / RK) & 1, abort_flag, &g_tc_error, kErrDqProducer);
+      for (int m = (nv > RV ? nv - RV : 0); m < nv; ++m)
+        mbar_wait(bar(L::B_VF + m % RV), (m / RV) & 1, abort_flag, &g_tc_error, kErrDqProducer);
       mbar_wait(bar(L::B_QD), 0, abort_flag, &g_tc_error, kErrDqProducer);
     }
   } else if (warp == kBwdMmaWarp) {
+    // Issue order: S(0) dP(0) | S(1) dP(1) dQ(0) | S(2) dP(2) dQ(1) | ...
+    // S(n+1) waits until the softmax has read S(n), dP(n+1) until it has read
+    // dP(n), dQ(n) until dS(n) is written.
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t IDESC_2 = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t IDESC_1 = idesc_bf16(128, 64, false, false);
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
       const uint64_t dQ = desc_k_sw128(sb + L::Q), dDO = desc_k_sw128(sb + L::DO),
                      dKk = desc_k_sw128(sb + L::K), dVk = desc_k_sw128(sb + L::V),
-                     dKmn = desc_mn_sw128(sb + L::K, 8192), dDS = desc_k_sw128(sb + L::DS);
+                     dKmn = desc_mn_sw128(sb + L::K, 16384);
       bool ok = mbar_wait(bar(L::B_QD), 0, abort_flag, &g_tc_error, kErrDqMma);
       tc_fence_after();
       UnionIter it;
       it.init(row_a, row_b, wq);
-      int n = 0;
-      auto grads = [&](int j) -> bool {
-        const int b = j & 1, st = j % R;
-        if (!mbar_wait(bar(L::B_DF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDqMma)) return false;
+      int n = 0, sel = 0, prev_cnt = 0;
+      auto dq_step = [&](int j, int cnt) -> bool {
+        if (!mbar_wait(bar(L::B_DSF), j & 1, abort_flag, &g_tc_error, kErrDqMma)) return false;
         tc_fence_after();
-        mma_k64_kmn(tmem + L::T_DQ, dDS + b * (16384 >> 4), dKmn + st * (L::kSub * 8192 >> 4),
-                    IDESC_G, j > 0 ? 1u : 0u);
-        mma_commit(bar(L::B_KE + st));
-        mma_commit(bar(L::B_DE + b));
+        const uint64_t bk = dKmn + (j % RK) * (L::kPair >> 4);
+        mma_ts_k64_mn(tmem + L::T_DQ, tmem + L::T_DS, bk, IDESC_G, j > 0 ? 1u : 0u);
+        if (cnt == 2) mma_ts_k64_mn(tmem + L::T_DQ, tmem + L::T_DS + 32, bk + (8192 >> 4), IDESC_G, 1u);
+        mma_commit(bar(L::B_DSE));
+        mma_commit(bar(L::B_KE + j % RK));
         return true;
       };
-      int sel = 0, t;
-      while (ok && (t = it.next(sel)) >= 0) {
-        const int st = n % R, b = n & 1;
-        if (!mbar_wait(bar(L::B_KF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDqMma)) {
-          ok = false;
-          break;
-        }
-        if (n >= 2 && !mbar_wait(bar(L::B_SE + b), ((n >> 1) - 1) & 1, abort_flag, &g_tc_error,
-                                 kErrDqMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + b * 64, dQ, dKk + st * (L::kSub * 8192 >> 4),
-                                     IDESC_S, 0u);
-        if (!mbar_wait(bar(L::B_VF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDqMma)) {
+      while (ok) {
+        const int t0 = it.next(sel);
+        if (t0 < 0) break;
+        const int t1 = it.next(sel);
+        const int cnt = t1 >= 0 ? 2 : 1;
+        const uint32_t idn = cnt == 2 ? IDESC_2 : IDESC_1;
+        const int sk = n % RK, sv = n % RV;
+        if (!mbar_wait(bar(L::B_KF + sk), (n / RK) & 1, abort_flag, &g_tc_error, kErrDqMma) ||
+            (n > 0 && !mbar_wait(bar(L::B_SE), (n - 1) & 1, abort_flag, &g_tc_error, kErrDqMma))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_DP + b * 64, dDO, dVk + st * (L::kSub * 8192 >> 4),
-                                     IDESC_S, 0u);
-        mma_commit(bar(L::B_VE + st));
-        mma_commit(bar(L::B_SF + b));
-        if (n >= 1 && !grads(n - 1)) {
+        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_S, dQ, dKk + sk * (L::kPair >> 4), idn, 0u);
+        mma_commit(bar(L::B_SF));
+        if (!mbar_wait(bar(L::B_VF + sv), (n / RV) & 1, abort_flag, &g_tc_error, kErrDqMma) ||
+            (n > 0 && !mbar_wait(bar(L::B_DPE), (n - 1) & 1, abort_flag, &g_tc_error, kErrDqMma))) {
           ok = false;
           break;
         }
+        tc_fence_after();
+        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_DP, dDO, dVk + sv * (L::kPair >> 4), idn, 0u);
+        mma_commit(bar(L::B_DPF));
+        mma_commit(bar(L::B_VE + sv));
+        if (n > 0 && !dq_step(n - 1, prev_cnt)) {
+          ok = false;
+          break;
+        }
+        prev_cnt = cnt;
         ++n;
+        if (t1 < 0) break;
       }
-      if (ok && n >= 1) ok = grads(n - 1);
+      if (ok && n > 0) dq_step(n - 1, prev_cnt);
       mma_commit(bar(L::B_FIN));
       mma_commit(bar(L::B_DRAIN));
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDqMma);
     }
   } else {
-    // softmax warpgroups: wg 0 takes key columns 0-31 of each step, wg 1 32-63
+    // softmax warpgroups: wg 0 takes key tile a of each pair, wg 1 tile b
     const int wg = warp >> 2;
     const int r = (warp & 3) * 32 + lane;  // query row within the CTA == TMEM lane
     const int half = r >> 6;
@@ -967,52 +1018,69 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float drow = delta[grow];
     UnionIter it;
     it.init(row_a, row_b, wq);
-    int n = 0, sel = 0, t;
+    int n = 0, sel0 = 0, sel1 = 0;
     bool ok = true;
-    while ((t = it.next(sel)) >= 0) {
-      const int b = n & 1;
-      const uint64_t vb64 = ((sel >> half) & 1) ? tile_bits[t] : 0ull;
-      if (!warp_wait(bar(L::B_SF + b), (n >> 1) & 1, abort_flag, kErrDqSoftmax)) {
+    for (;;) {
+      const int t0 = it.next(sel0);
+      if (t0 < 0) break;
+      const int t1 = it.next(sel1);
+      const bool live = wg == 0 || t1 >= 0;  // warp-uniform
+      const int tw = wg == 0 ? t0 : t1;
+      const int selw = wg == 0 ? sel0 : sel1;
+      const uint64_t vb = (live && ((selw >> half) & 1)) ? tile_bits[tw] : 0ull;  // warp-uniform
+      if (!warp_wait(bar(L::B_SF), n & 1, abort_flag, kErrDqSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[32], dp[32];
-      tmem_load<1>(t_lane + L::T_S + b * 64 + wg * 32, s);
-      tmem_load<1>(t_lane + L::T_DP + b * 64 + wg * 32, dp);
+      float p[64];
+      if (vb != 0ull) tmem_load<2>(t_lane + L::T_S + wg * 64, p);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_SE + b));
-      const uint32_t vb = (uint32_t)(vb64 >> (32 * wg));
-      uint32_t pd[16];
-      if (vb == 0xffffffffu) {
+      if (lane == 0) mbar_arrive(bar(L::B_SE));
+      if (vb == ~0ull) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float p0 = ex2(fmaf(s[c], qk_scale, -mrow));
-          const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mrow));
-          pd[c / 2] = pack_bf16(p0 * (dp[c] - drow), p1 * (dp[c + 1] - drow));
-        }
-      } else {
+        for (int c = 0; c < 64; ++c) p[c] = ex2(fmaf(p[c], qk_scale, -mrow));
+      } else if (vb != 0ull) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float p0 = ((vb >> c) & 1u) ? ex2(fmaf(s[c], qk_scale, -mrow)) : 0.0f;
-          const float p1 = ((vb >> (c + 1)) & 1u) ? ex2(fmaf(s[c + 1], qk_scale, -mrow)) : 0.0f;
-          pd[c / 2] = pack_bf16(p0 * (dp[c] - drow), p1 * (dp[c + 1] - drow));
-        }
+        for (int c = 0; c < 64; ++c) p[c] = ((vb >> c) & 1ull) ? ex2(fmaf(p[c], qk_scale, -mrow)) : 0.0f;
       }
-      if (n >= 2 && !warp_wait(bar(L::B_DE + b), ((n >> 1) - 1) & 1, abort_flag, kErrDqSoftmax)) {
+      if (!warp_wait(bar(L::B_DPF), n & 1, abort_flag, kErrDqSoftmax)) {
         ok = false;
         break;
       }
-      uint8_t* sDS = sm + L::DS + b * 16384;
+      tc_fence_after();
+      uint32_t pk[32];
+      if (vb != 0ull) {
+        float dp[64];
+        tmem_load<2>(t_lane + L::T_DP + wg * 64, dp);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::B_DPE));
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch)
-        *reinterpret_cast<uint4*>(sDS + sw128_off(r, wg * 4 + ch)) =
-            make_uint4(pd[ch * 4], pd[ch * 4 + 1], pd[ch * 4 + 2], pd[ch * 4 + 3]);
-      fence_proxy_async_smem();
+        for (int c = 0; c < 64; c += 2)
+          pk[c / 2] = pack_bf16(p[c] * (dp[c] - drow), p[c + 1] * (dp[c + 1] - drow));
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::B_DPE));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = 0u;
+      }
+      // dS(n) overwrites dS(n-1): wait until dQ(n-1) has read it
+      if (n > 0 && !warp_wait(bar(L::B_DSE), (n - 1) & 1, abort_flag, kErrDqSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (live) {
+        tmem_st32(t_lane + L::T_DS + wg * 32, pk);
+        tmem_wait_st();
+      }
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_DF + b));
+      if (lane == 0) mbar_arrive(bar(L::B_DSF));
       ++n;
+      if (t1 < 0) break;
     }
     // epilogue: wg 0 writes dQ columns [0, D/2), wg 1 [D/2, D)
     if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDqSoftmax)) {
