@@ -62,14 +62,30 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 // The word stays set until the host reads it (prism_device_status).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `ns` nanoseconds pass, instead of polling the barrier
+// (each poll is a shared-memory access that competes with the tensor core's
+// operand reads and the TMA fills).
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int code) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (;;) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try(bar, parity)) return true;
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
     if (*reinterpret_cast<volatile int*>(err) != 0) {
       *abort_flag = 1;
