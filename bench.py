@@ -10,8 +10,11 @@ layer runs under Ulysses sequence parallelism (each rank holds S/N tokens of
 all 40 heads; all-to-all to 40/N heads of the full sequence and back), so the
 total work is fixed: "scaling": "strong".
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 720p|1080p|2k]
     torchrun --nproc-per-node N bench.py --gpus N ...
+
+--config picks BASELINE config 1 (720p, default: the metric's workload), 2 (1080p,
+21x68x120) or 3 (2K, 31x90x160, top-k 5%); every config has 40 heads of 128.
 
 value = whole-job effective TFLOPS = FLOPs of the selected 64x64 tile pairs
 (4*D*64*64 per pair for the forward, 2.5x that for the backward) / time.
@@ -34,6 +37,14 @@ sys.path.insert(0, ROOT)
 CONFIG = dict(workload="720p dynamic BSA layer fwd+bwd (BASELINE config 1)", model="prism-video-self-attn",
               grid=(21, 45, 80), heads=40, head_dim=128, audio_tokens=125, hidden=5120,
               sparsity=0.92, cdf_threshold=0.9, method="ivpq")
+# BASELINE configs 2 and 3 (same value generator and selection rule; 2K uses top-k 5%)
+CONFIGS = {
+    "720p": dict(CONFIG),
+    "1080p": dict(CONFIG, workload="1080p dynamic BSA layer fwd+bwd (BASELINE config 2)",
+                  grid=(21, 68, 120)),
+    "2k": dict(CONFIG, workload="2K dynamic BSA layer fwd+bwd (BASELINE config 3)",
+               grid=(31, 90, 160), audio_tokens=189, sparsity=0.95),
+}
 FWD_BWD_FACTOR = 3.5  # 1 (forward) + 2.5 (backward), SURVEY 8(d)
 
 
@@ -143,16 +154,20 @@ def selected_pairs(q, k, v, a2v, S, world):
         _, plan = run_bsa_dynamic(q4, k4, v4, CONFIG["grid"], layout="bshd", method=CONFIG["method"],
                                   sparsity=CONFIG["sparsity"], cdf_threshold=CONFIG["cdf_threshold"],
                                   audio_token_norms=norms, return_plan=True)
-        pc = torch.zeros(1, dtype=torch.int64, device=q.device)
+        def popcount(words):
+            x = words.to(torch.int64) & 0xFFFFFFFF
+            cnt = torch.zeros_like(x)
+            for _ in range(32):
+                cnt += x & 1
+                x = x >> 1
+            return int(cnt.sum().item())
         bq = plan.bits_q.view(torch.int32)
-        # popcount over int32 words
-        x = bq.to(torch.int64) & 0xFFFFFFFF
-        cnt = torch.zeros_like(x)
-        for _ in range(32):
-            cnt += x & 1
-            x = x >> 1
-        pc += cnt.sum()
-    return int(pc.item()), plan, (q4, k4, v4, norms)
+        pairs = popcount(bq)
+        # 64x64 products the kernels execute: a CTA walks the union of its query tiles' rows
+        hq, nt, wq = bq.shape
+        union2 = bq.view(hq, nt // 2, 2, wq)
+        executed = 2 * popcount(union2[:, :, 0] | union2[:, :, 1])
+    return pairs, plan, (q4, k4, v4, norms), executed
 
 
 def kernel_times(plan, q4, k4, v4, reps=3):
@@ -274,10 +289,13 @@ def main():
     ap.add_argument("--impl", default="prism", choices=["prism", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--config", default="720p", choices=sorted(CONFIGS),
+                    help="BASELINE config: 720p (config 1, default), 1080p (config 2), 2k (config 3)")
     ap.add_argument("--heads", type=int, default=CONFIG["heads"],
-                    help="attention heads of the layer (40 in BASELINE config 1; smaller only "
+                    help="attention heads of the layer (40 in every BASELINE config; smaller only "
                          "for profiler captures)")
     args = ap.parse_args()
+    CONFIG.update(CONFIGS[args.config])
     CONFIG["heads"] = args.heads
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -358,11 +376,13 @@ def main():
     ms = float(t.item())
 
     # FLOPs actually computed (selected tile pairs, all ranks)
-    pairs, plan, (q4, k4, v4, norms) = selected_pairs(q.detach(), k.detach(), v.detach(), a2v, S, world)
-    pt = torch.tensor([pairs], device=dev, dtype=torch.float64)
+    pairs, plan, (q4, k4, v4, norms), executed = selected_pairs(q.detach(), k.detach(), v.detach(),
+                                                                a2v, S, world)
+    pt = torch.tensor([pairs, executed], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(pt)
-    total_pairs = float(pt.item())
+    total_pairs = float(pt[0].item())
+    total_executed = float(pt[1].item())
     D = CONFIG["head_dim"]
     flops = FWD_BWD_FACTOR * 4 * D * 64 * 64 * total_pairs
     tflops = flops / (ms * 1e-3) / 1e12
@@ -443,7 +463,8 @@ def main():
                 "data": "synthetic (seeded zone-structured q/k/v, N(0,1) a2v residual)",
                 "config": dict(CONFIG, grid=list(CONFIG["grid"]), parallelism=f"ulysses_sp{world}",
                                global_batch=1, seq_len=S, selected_tile_pairs=int(total_pairs),
-                               pair_density=density, l2="inputs larger than L2 (q/k/v 774 MB each)"),
+                               executed_tile_pairs_dq=int(total_executed), pair_density=density,
+                               l2="inputs larger than L2 (q/k/v >= 774 MB each)"),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clocks}
         print(json.dumps(line), flush=True)
