@@ -1,5 +1,5 @@
 """Benchmark: dynamic block-shape block-sparse attention, forward + backward of
-one video self-attention layer (720p: B=1, 40 heads,
+one video self-attention layer (benchmark config 1, 720p: B=1, 40 heads,
 head_dim 128, grid 21x45x80 = 75,600 tokens + 125 audio tokens, zone-structured
 q/k/v, top-k 8% + cumulative mass 0.9) on 1..N B200s of one node.
 
@@ -13,7 +13,7 @@ total work is fixed: "scaling": "strong".
     python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 720p|1080p|2k]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
---config picks BASELINE config 1 (720p, default: the metric's workload), 2 (1080p,
+--config picks benchmark config 1 (720p, default: the metric's workload), 2 (1080p,
 21x68x120) or 3 (2K, 31x90x160, top-k 5%); every config has 40 heads of 128.
 
 value = whole-job effective TFLOPS = FLOPs of the selected 64x64 tile pairs
@@ -34,18 +34,25 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONFIG = dict(workload="720p dynamic BSA layer fwd+bwd (BASELINE config 1)", model="prism-video-self-attn",
+CONFIG = dict(workload="720p dynamic BSA layer fwd+bwd (benchmark config 1)", model="prism-video-self-attn",
               grid=(21, 45, 80), heads=40, head_dim=128, audio_tokens=125, hidden=5120,
               sparsity=0.92, cdf_threshold=0.9, method="ivpq")
-# BASELINE configs 2 and 3 (same value generator and selection rule; 2K uses top-k 5%)
+# benchmark configs 2 and 3 (same value generator and selection rule; 2K uses top-k 5%)
 CONFIGS = {
     "720p": dict(CONFIG),
-    "1080p": dict(CONFIG, workload="1080p dynamic BSA layer fwd+bwd (BASELINE config 2)",
+    "1080p": dict(CONFIG, workload="1080p dynamic BSA layer fwd+bwd (benchmark config 2)",
                   grid=(21, 68, 120)),
-    "2k": dict(CONFIG, workload="2K dynamic BSA layer fwd+bwd (BASELINE config 3)",
+    "2k": dict(CONFIG, workload="2K dynamic BSA layer fwd+bwd (benchmark config 3)",
                grid=(31, 90, 160), audio_tokens=189, sparsity=0.95),
 }
-FWD_BWD_FACTOR = 3.5  # 1 (forward) + 2.5 (backward), SURVEY 8(d)
+# DRAM bytes (read + write) per head of one launch of each attention kernel on the 720p
+# layer: ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-head capture / 4.  Heads
+# are independent (one head's K/V tiles stay in L2), so a launch over h heads moves h times
+# this; roofline.traffic reports it for the dominant kernel.
+TRAFFIC_PER_HEAD_720P = {"bsa_fwd": (525.5e6 + 172.8e6) / 4,
+                         "bsa_bwd_dkdv": (581.9e6 + 175.0e6) / 4,
+                         "bsa_bwd_dq": (594.0e6 + 92.8e6) / 4}
+FWD_BWD_FACTOR = 3.5  # 1 (forward) + 2.5 (backward): the canonical FLOP count of one fwd+bwd
 
 
 # ------------------------------------------------------------------ inputs
@@ -290,9 +297,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", default="720p", choices=sorted(CONFIGS),
-                    help="BASELINE config: 720p (config 1, default), 1080p (config 2), 2k (config 3)")
+                    help="benchmark config: 720p (config 1, default), 1080p (config 2), 2k (config 3)")
     ap.add_argument("--heads", type=int, default=CONFIG["heads"],
-                    help="attention heads of the layer (40 in every BASELINE config; smaller only "
+                    help="attention heads of the layer (40 in every benchmark config; smaller only "
                          "for profiler captures)")
     args = ap.parse_args()
     CONFIG.update(CONFIGS[args.config])
@@ -405,8 +412,13 @@ def main():
     algo = {"bsa_fwd": 2 * mm, "bsa_bwd_dkdv": 4 * mm, "bsa_bwd_dq": 3 * mm}
     dom = max(("bsa_fwd", "bsa_bwd_dkdv", "bsa_bwd_dq"), key=lambda n: kt[n])
     achieved = algo[dom] / (kt[dom] * 1e-3) / 1e12
+    traffic = None
+    if args.config == "720p" and D == 128:
+        traffic = TRAFFIC_PER_HEAD_720P[dom] * (CONFIG["heads"] // world)
     roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
-                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 720p layer "
+                                  "at 4 heads, scaled by heads per launch" if traffic else None,
                 "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if peaks else "fallback",
                 "kernel_ms": kt}
 

@@ -4,7 +4,7 @@ Generated with torch's CPU generator, so the same seeds give the same values on
 any machine with the same torch build; the fixtures therefore store seeds and
 reference outputs, not the input tensors.
 
-Value models:
+Value models (benchmark configs):
 * ``normal``: q, k, v ~ N(0, 1) (config 0).
 * ``zoned``: each 8x8x8 macro-zone of the padded grid holds tokens
   ``zone_mean + 0.3 * noise`` with zone_mean, noise ~ N(0, 0.5^2) (configs 1-2),
@@ -52,7 +52,7 @@ class Case:
 
 
 CASES = {
-    # 4 heads, D=64, 4x8x8 grid (padded to 8x8x8), 32 audio tokens,
+    # benchmark config 0: 4 heads, D=64, 4x8x8 grid (padded to 8x8x8), 32 audio tokens,
     # top-k 2 of 8 blocks (sparsity 0.75) + cumulative mass 0.9.
     "c0": Case("c0", (4, 8, 8), 4, 64),
     "c0_tau25_penalty": Case("c0_tau25_penalty", (4, 8, 8), 4, 64, method="penalty", tau_128=0.25),

@@ -138,7 +138,9 @@ def run_case(dba, dbs, case):
 
 
 def main():
-    root = os.environ.get("PRISM_REFERENCE", "/root/reference")
+    root = os.environ.get("PRISM_REFERENCE")
+    if not root:
+        sys.exit("set PRISM_REFERENCE to the root of a Prism checkout")
     dba, dbs = import_reference(root)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     names = sys.argv[1:] or list(CASES)
