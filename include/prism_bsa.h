@@ -16,6 +16,8 @@
  *   tile order  the per-zone anisotropic rearrangement: zone z holds tokens
  *               [512 z, 512 z + 512), split into 64-token tiles; built by
  *               prism_build_layout (src_idx[r] = padded THW index of row r).
+ *               The uniform fixed-shape path instead uses the global 3D-chunk
+ *               order of prism_uniform_layout (grid padded to the chunk).
  *   bitmaps     bits_q[h][q_tile][w] bit b set <=> q tile attends key tile
  *               32 w + b; bits_k is its transpose (key tile -> q tiles).
  *               Row length WQ = ceil(N_tiles / 32) 32-bit words.
@@ -101,21 +103,26 @@ prism_status_t prism_build_layout(const int64_t* shape_ids, int Tp, int Hp, int 
  * set iff padded token src_idx[64 j + i] lies inside the source grid
  * (T, H, W) and (valid == NULL or valid[src_idx[64 j + i]]); tile_count[j] is
  * its popcount (the reference's valid_re / tile_counts,
- * dynamic_block_attention.py:253, 260). */
-prism_status_t prism_tile_valid(const int32_t* src_idx, const uint8_t* valid, int T, int H, int W,
-                                int Tp, int Hp, int Wp, uint64_t* tile_bits, int32_t* tile_count,
-                                cudaStream_t stream);
+ * dynamic_block_attention.py:253, 260; rearrange_THW_to_3d_block_1d,
+ * bsa_interface.py:1117-1121, for the uniform path).  n_rows = length of
+ * src_idx, a multiple of 64; entries >= Tp*Hp*Wp are padding rows. */
+prism_status_t prism_tile_valid(const int32_t* src_idx, int64_t n_rows, const uint8_t* valid, int T,
+                                int H, int W, int Tp, int Hp, int Wp, uint64_t* tile_bits,
+                                int32_t* tile_count, cudaStream_t stream);
 
 /* Gather rows into tile order: out[h][r] = x[h][thw(src_idx[r])], where
  * src_idx holds padded-grid THW indices and x is laid out on the grid
  * (T, H, W) <= (Tp, Hp, Wp); rows outside (T, H, W) are written as zeros
  * (the F.pad of wan_video_dit.py:382-389 fused with
- * q.index_select(2, src_idx), dynamic_block_attention.py:250-252).
+ * q.index_select(2, src_idx), dynamic_block_attention.py:250-252; the uniform
+ * path's pad, wan_video_dit.py:485-505, and rearrange_THW_to_3d_block,
+ * bsa_interface.py:1105-1109).  n_rows = length of src_idx (output rows per
+ * head); entries >= Tp*Hp*Wp give zero rows.
  * Strides in elements; rows are D contiguous bf16, D % 8 == 0. */
 prism_status_t prism_gather_rows(const void* x, int64_t x_stride_h, int64_t x_stride_s, int heads,
                                  int D, int T, int H, int W, int Tp, int Hp, int Wp,
-                                 const int32_t* src_idx, void* out, int64_t out_stride_h,
-                                 cudaStream_t stream);
+                                 const int32_t* src_idx, int64_t n_rows, void* out,
+                                 int64_t out_stride_h, cudaStream_t stream);
 
 /* Inverse of prism_gather_rows for the tokens inside (T, H, W):
  * out[h][thw] = x_re[h][inv_idx[padded thw]] (o_re.index_select(2, inv_idx)
@@ -141,6 +148,42 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
                                   const uint64_t* tile_bits, int mode, double sparsity,
                                   double cdf_threshold, void* workspace, uint32_t* bits_q,
                                   uint32_t* bits_k, cudaStream_t stream);
+
+/* Uniform fixed-shape path (flash_attn_bsa_3d, bsa_interface.py:1123-1176).
+ *
+ * prism_uniform_layout: the permutation of rearrange_THW_to_3d_block
+ * (bsa_interface.py:1105-1109) for chunk (ct, ch, cw) over the padded grid
+ * (Tp, Hp, Wp) (multiples of the chunk): row p of the chunk order holds padded
+ * THW token src_idx[p]; inv_idx [Tp*Hp*Wp] is its inverse
+ * (rearrange_3d_block_to_THW, :1111-1115).  n_rows >= Tp*Hp*Wp rows are
+ * written; rows p >= Tp*Hp*Wp get the sentinel Tp*Hp*Wp (zero rows, padding),
+ * so that the attention kernels see whole 128-row tile pairs. */
+prism_status_t prism_uniform_layout(int Tp, int Hp, int Wp, int ct, int ch, int cw, int64_t n_rows,
+                                    int32_t* src_idx, int32_t* inv_idx, cudaStream_t stream);
+
+/* Chunk pooling, scores and selection of _attention_bsa.forward
+ * (bsa_interface.py:600-633: masked_mean_pooling_compression /
+ * mean_pooling_compression :164-201, cal_score :203-207,
+ * get_select_indices_{topk,cdf,cdf_topk}_from_score :235-304), expanded to
+ * 64-token tile bitmaps.  q_re is in the q chunk order, k_re in the key chunk
+ * order, both [heads, S, D] bf16 with S a multiple of 64; the first `seq` rows
+ * are real (seq a multiple of chunk_q and chunk_k, both multiples of 64).
+ * tile_bits [S/64]: key validity in the key order; the q pooling uses the same
+ * mask at the same positions, as the reference does
+ * (masked_mean_pooling_compression(q, chunk_size_q, kv_valid_mask), :609-610).
+ * Pooling is fp32 (sequential sums / max(count, 1)); no key chunk is excluded
+ * from the top-k (the uniform path has no block-validity mask); selected
+ * tiles without a valid key are dropped (they contribute nothing).  Bitmap
+ * rows of padding tiles are zero.  mode as for prism_block_select.
+ * workspace: prism_block_select_uniform_workspace_bytes(heads, seq/chunk_q,
+ * seq/chunk_k, D). */
+size_t prism_block_select_uniform_workspace_bytes(int heads, int64_t n_chunks_q, int64_t n_chunks_k,
+                                                  int D);
+prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t S,
+                                          int D, int64_t seq, int chunk_q, int chunk_k,
+                                          const uint64_t* tile_bits, int mode, double sparsity,
+                                          double cdf_threshold, void* workspace, uint32_t* bits_q,
+                                          uint32_t* bits_k, cudaStream_t stream);
 
 /* Block-sparse attention forward over tile-ordered q/k/v [heads, S, D] bf16
  * (attn_fwd_bsa_varlen_triton + _attn_fwd_bsa_varlen_align,

@@ -61,6 +61,8 @@ def lib():
         L.oracle_layout.argtypes = [P, i32, i32, i32, P, P, P, P]
         L.oracle_layout.restype = i64
         L.oracle_block_select.argtypes = [P, P, i32, i64, i32, P, i64, P, i32, f64, f64, P, P, P]
+        L.oracle_block_select_uniform.argtypes = [P, P, i32, i64, i32, i64, i32, i32, P, i32, f64,
+                                                  f64, P, P, P]
         _lib = L
     return _lib
 
@@ -164,6 +166,47 @@ def block_select(q_re_bits, k_re_bits, valid_re, block_tiles, nb, sparsity, cdf_
                               mode, float(sparsity if sparsity is not None else 0.0),
                               float(cdf_threshold if cdf_threshold is not None else 0.0),
                               _p(bits_q), _p(bits_k), _p(sel))
+    return bits_q, bits_k, sel
+
+
+def uniform_layout(grid_padded, chunk, n_rows=None):
+    """3D-chunk order of the uniform path (rearrange_THW_to_3d_block,
+    bsa_interface.py:1105-1109): src_idx [n_rows] (padded THW index of each
+    row; rows past the grid hold the sentinel Tp*Hp*Wp) and inv_idx [Tp*Hp*Wp]."""
+    Tp, Hp, Wp = grid_padded
+    ct, ch, cw = chunk
+    S = Tp * Hp * Wp
+    n_rows = S if n_rows is None else n_rows
+    order = np.arange(S).reshape(Tp // ct, ct, Hp // ch, ch, Wp // cw, cw)
+    order = order.transpose(0, 2, 4, 1, 3, 5).reshape(-1)
+    src = np.full(n_rows, S, np.int64)
+    src[:S] = order
+    inv = np.empty(S, np.int64)
+    inv[order] = np.arange(S)
+    return src, inv
+
+
+def block_select_uniform(q_re_bits, k_re_bits, seq, chunk_q, chunk_k, valid_re, sparsity,
+                         cdf_threshold, want_chunks=False):
+    """Uniform-path selection (oracle_block_select_uniform).  q_re_bits in the q
+    chunk order, k_re_bits in the key chunk order, [h, S, D] bf16 bits; valid_re
+    [S] key validity in the key order (None = all real rows valid).
+    Returns (bits_q, bits_k, sel_chunks [h, nq, nk] or None)."""
+    q_re_bits = np.ascontiguousarray(q_re_bits, np.uint16)
+    k_re_bits = np.ascontiguousarray(k_re_bits, np.uint16)
+    heads, S, D = q_re_bits.shape
+    n_tiles = S // 64
+    wq = (n_tiles + 31) // 32
+    bits_q = np.zeros((heads, n_tiles, wq), np.uint32)
+    bits_k = np.zeros((heads, n_tiles, wq), np.uint32)
+    sel = (np.zeros((heads, seq // chunk_q, seq // chunk_k), np.uint8) if want_chunks else None)
+    valid_re = None if valid_re is None else np.ascontiguousarray(valid_re, np.uint8)
+    mode = selection_mode(sparsity, cdf_threshold)
+    lib().oracle_block_select_uniform(
+        _p(q_re_bits), _p(k_re_bits), heads, S, D, seq, chunk_q, chunk_k, _p(valid_re), mode,
+        float(sparsity if sparsity is not None else 0.0),
+        float(cdf_threshold if cdf_threshold is not None else 0.0), _p(bits_q), _p(bits_k),
+        _p(sel))
     return bits_q, bits_k, sel
 
 

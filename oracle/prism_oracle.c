@@ -15,6 +15,9 @@
  *   oracle_layout        dynamic_block_attention.py:21-63, 107-170
  *   oracle_block_select  bsa_interface.py:177-201, 203-207, 235-304,
  *                        dynamic_block_attention.py:173-188, 256-319
+ *   oracle_block_select_uniform
+ *                        bsa_interface.py:164-201, 203-207, 235-304, 600-633
+ *                        (uniform fixed-shape path, flash_attn_bsa_3d :1123-1176)
  *
  * Floating-point order.  The reference leaves summation order to torch; this
  * restatement fixes one order (the one the CUDA kernels use) so that GPU and
@@ -510,6 +513,72 @@ static void pool_blocks(const uint16_t* x_re, int64_t S, int D, const uint8_t* v
   free(tm);
 }
 
+/* Selection sizes of get_select_indices_{cdf_topk,cdf,topk}_from_score
+ * (bsa_interface.py:236-304) for nb key blocks: k_topk and the candidate
+ * count ub (torch.topk's k). */
+static void select_sizes(int mode, double sparsity, double cdf, int64_t nb, int64_t* k_topk_out,
+                         int64_t* ub_out) {
+  int64_t k_topk = 0, ub = nb;
+  if (mode == 0) {
+    k_topk = (int64_t)((1.0 - sparsity) * (double)nb);
+    if (k_topk < 1) k_topk = 1;
+    int64_t u = (int64_t)(cdf * (double)nb) + 1;
+    ub = k_topk > u ? k_topk : u;
+    if (ub > nb) ub = nb;
+  } else if (mode == 1) {
+    k_topk = 1;
+    ub = (int64_t)(cdf * (double)nb) + 1;
+    if (ub > nb) ub = nb;
+  } else {
+    k_topk = (int64_t)((1.0 - sparsity) * (double)nb);
+  }
+  *k_topk_out = k_topk;
+  *ub_out = ub;
+}
+
+/* One row of block scores (score[b], -INFINITY for excluded blocks; clobbered)
+ * -> arr sorted by descending key with ties by lower index; returns how many
+ * leading entries of arr are selected.  Mode 2 ranks raw scores; modes 0/1
+ * rank softmax(score * scale) weights and keep the top-k / cumulative-mass
+ * count (cdf_m = round_f32(sum of the top-m weights) with the sum exact in
+ * 2^-63 fixed point, as torch's CPU cumsum accumulates in double and rounds
+ * each partial sum to float; softmax denominator exact in 2^-50 fixed point,
+ * rounded once to float). */
+static int64_t select_row(float* score, int64_t nb, int mode, int64_t k_topk, int64_t ub,
+                          float scale, float pf, wi_t* arr) {
+  if (mode == 2) {
+    for (int64_t b = 0; b < nb; ++b) { arr[b].w = score[b]; arr[b].idx = (int32_t)b; }
+    qsort(arr, nb, sizeof(wi_t), cmp_wdesc);
+    return k_topk;
+  }
+  float mx = -INFINITY;
+  for (int64_t b = 0; b < nb; ++b) {
+    float x = score[b] * scale;
+    score[b] = x;
+    if (x > mx) mx = x;
+  }
+  uint64_t Z = 0;
+  for (int64_t b = 0; b < nb; ++b) {
+    float e = oracle_det_expf(score[b] - mx);
+    score[b] = e;
+    Z += (uint64_t)(e * 0x1p50f);
+  }
+  const float Zf = (float)Z * 0x1p-50f;
+  for (int64_t b = 0; b < nb; ++b) { arr[b].w = score[b] / Zf; arr[b].idx = (int32_t)b; }
+  qsort(arr, nb, sizeof(wi_t), cmp_wdesc);
+  uint64_t run = 0;
+  int64_t cnt_lt = 0;
+  for (int64_t m = 0; m < ub; ++m) {
+    run += (uint64_t)(arr[m].w * 0x1p63f);
+    float cf = (float)run * 0x1p-63f;
+    if (cf < pf) ++cnt_lt;
+  }
+  int64_t n = cnt_lt + 1;
+  if (n < k_topk) n = k_topk;
+  if (n > nb) n = nb;
+  return n < ub ? n : ub;
+}
+
 /* Block selection for one head, writing q-tile-major and k-tile-major
  * bitmaps.  mode: 0 = top-k + cdf (get_select_indices_cdf_topk_from_score,
  * bsa_interface.py:284-304), 1 = cdf only (:257-275), 2 = top-k only
@@ -550,20 +619,8 @@ void oracle_block_select(const uint16_t* q_re, const uint16_t* k_re, int heads, 
     }
     bvalid[b] = c > 0;
   }
-  int64_t k_topk = 0, ub = nb;
-  if (mode == 0) {
-    k_topk = (int64_t)((1.0 - sparsity) * (double)nb);
-    if (k_topk < 1) k_topk = 1;
-    int64_t u = (int64_t)(cdf * (double)nb) + 1;
-    ub = k_topk > u ? k_topk : u;
-    if (ub > nb) ub = nb;
-  } else if (mode == 1) {
-    k_topk = 1;
-    ub = (int64_t)(cdf * (double)nb) + 1;
-    if (ub > nb) ub = nb;
-  } else {
-    k_topk = (int64_t)((1.0 - sparsity) * (double)nb);
-  }
+  int64_t k_topk, ub;
+  select_sizes(mode, sparsity, cdf, nb, &k_topk, &ub);
   for (int h = 0; h < heads; ++h) {
     pool_blocks(q_re + (int64_t)h * S * D, S, D, valid_re, nb, block_tiles, qc);
     pool_blocks(k_re + (int64_t)h * S * D, S, D, valid_re, nb, block_tiles, kc);
@@ -576,39 +633,7 @@ void oracle_block_select(const uint16_t* q_re, const uint16_t* k_re, int heads, 
         for (int d = 0; d < D; ++d) acc = fmaf(qc[a * D + d], kc[b * D + d], acc);
         score[b] = acc;
       }
-      int64_t n_eff;
-      if (mode == 2) {
-        for (int64_t b = 0; b < nb; ++b) { arr[b].w = score[b]; arr[b].idx = (int32_t)b; }
-        qsort(arr, nb, sizeof(wi_t), cmp_wdesc);
-        n_eff = k_topk;
-      } else {
-        float mx = -INFINITY;
-        for (int64_t b = 0; b < nb; ++b) {
-          float x = score[b] * scale;
-          score[b] = x;
-          if (x > mx) mx = x;
-        }
-        uint64_t Z = 0;
-        for (int64_t b = 0; b < nb; ++b) {
-          float e = oracle_det_expf(score[b] - mx);
-          score[b] = e;
-          Z += (uint64_t)(e * 0x1p50f);
-        }
-        const float Zf = (float)Z * 0x1p-50f;
-        for (int64_t b = 0; b < nb; ++b) { arr[b].w = score[b] / Zf; arr[b].idx = (int32_t)b; }
-        qsort(arr, nb, sizeof(wi_t), cmp_wdesc);
-        uint64_t run = 0;
-        int64_t cnt_lt = 0;
-        for (int64_t m = 0; m < ub; ++m) {
-          run += (uint64_t)(arr[m].w * 0x1p63f);
-          float cf = (float)run * 0x1p-63f;
-          if (cf < pf) ++cnt_lt;
-        }
-        int64_t n = cnt_lt + 1;
-        if (n < k_topk) n = k_topk;
-        if (n > nb) n = nb;
-        n_eff = n < ub ? n : ub;
-      }
+      const int64_t n_eff = select_row(score, nb, mode, k_topk, ub, scale, pf, arr);
       if (sel_blocks) memset(sel_blocks + ((int64_t)h * nb + a) * nb, 0, nb);
       for (int64_t m = 0; m < n_eff; ++m) {
         const int64_t b = arr[m].idx;
@@ -632,4 +657,91 @@ void oracle_block_select(const uint16_t* q_re, const uint16_t* k_re, int heads, 
   free(arr);
   free(tile_cnt);
   free(bvalid);
+}
+
+/* Uniform fixed-shape path (_attention_bsa.forward, bsa_interface.py:600-633)
+ * on chunk-ordered q_re / k_re [heads, S, D] bf16 whose first `seq` rows are
+ * real.  Pooling (masked_mean_pooling_compression / mean_pooling_compression,
+ * :164-201): chunk mean = sequential fp32 sum over the chunk's valid rows /
+ * max(count, 1), with the KEY-order mask valid_re [S] applied to q as well
+ * (:609-610; NULL = every real row valid).  Scores: fmaf chain over d
+ * (cal_score, :203-207).  No chunk is excluded from the ranking.  Selected key
+ * chunk b covers tiles [b*tk, b*tk + tk) (tk = chunk_k / 64), tiles without a
+ * valid key are dropped; q chunk a's row goes to tiles [a*tq, a*tq + tq).
+ * sel_chunks [heads, nq, nk] u8 receives the chunk-level selection if non-NULL.
+ * Callers zero bits_q / bits_k. */
+void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int heads, int64_t S,
+                                 int D, int64_t seq, int chunk_q, int chunk_k,
+                                 const uint8_t* valid_re, int mode, double sparsity, double cdf,
+                                 uint32_t* bits_q, uint32_t* bits_k, uint8_t* sel_chunks) {
+  const int64_t N_tiles = S / 64;
+  const int64_t WQ = (N_tiles + 31) / 32;
+  const int64_t nq = seq / chunk_q, nk = seq / chunk_k;
+  const int tq = chunk_q / 64, tk = chunk_k / 64;
+  const float scale = (float)(1.0 / sqrt((double)D));
+  const float pf = (float)cdf;
+  float* qc = (float*)malloc(sizeof(float) * nq * D);
+  float* kc = (float*)malloc(sizeof(float) * nk * D);
+  float* score = (float*)malloc(sizeof(float) * nk);
+  wi_t* arr = (wi_t*)malloc(sizeof(wi_t) * nk);
+  int* tile_cnt = (int*)malloc(sizeof(int) * N_tiles);
+  for (int64_t j = 0; j < N_tiles; ++j) {
+    int c = 0;
+    for (int i = 0; i < 64; ++i) {
+      const int64_t s = j * 64 + i;
+      c += s < seq && (valid_re ? valid_re[s] != 0 : 1);
+    }
+    tile_cnt[j] = c;
+  }
+  int64_t k_topk, ub;
+  select_sizes(mode, sparsity, cdf, nk, &k_topk, &ub);
+  for (int h = 0; h < heads; ++h) {
+    for (int pass = 0; pass < 2; ++pass) {
+      const uint16_t* x = (pass ? k_re : q_re) + (int64_t)h * S * D;
+      const int chunk = pass ? chunk_k : chunk_q;
+      const int64_t n = pass ? nk : nq;
+      float* out = pass ? kc : qc;
+      for (int64_t c = 0; c < n; ++c) {
+        int cnt = 0;
+        for (int d = 0; d < D; ++d) out[c * D + d] = 0.0f;
+        for (int i = 0; i < chunk; ++i) {
+          const int64_t s = c * chunk + i;
+          if (valid_re && !valid_re[s]) continue;
+          ++cnt;
+          for (int d = 0; d < D; ++d) out[c * D + d] += bf16_to_f32(x[s * D + d]);
+        }
+        const float den = cnt > 0 ? (float)cnt : 1.0f;
+        for (int d = 0; d < D; ++d) out[c * D + d] = out[c * D + d] / den;
+      }
+    }
+    uint32_t* bq = bits_q + (int64_t)h * N_tiles * WQ;
+    uint32_t* bk = bits_k + (int64_t)h * N_tiles * WQ;
+    for (int64_t a = 0; a < nq; ++a) {
+      for (int64_t b = 0; b < nk; ++b) {
+        float acc = 0.0f;
+        for (int d = 0; d < D; ++d) acc = fmaf(qc[a * D + d], kc[b * D + d], acc);
+        score[b] = acc;
+      }
+      const int64_t n_eff = select_row(score, nk, mode, k_topk, ub, scale, pf, arr);
+      if (sel_chunks) memset(sel_chunks + ((int64_t)h * nq + a) * nk, 0, nk);
+      for (int64_t m = 0; m < n_eff; ++m) {
+        const int64_t b = arr[m].idx;
+        if (sel_chunks) sel_chunks[((int64_t)h * nq + a) * nk + b] = 1;
+        for (int p = 0; p < tk; ++p) {
+          const int64_t kt = b * tk + p;
+          if (tile_cnt[kt] == 0) continue;
+          for (int pq = 0; pq < tq; ++pq) {
+            const int64_t qt = a * tq + pq;
+            bq[qt * WQ + kt / 32] |= 1u << (kt % 32);
+            bk[kt * WQ + qt / 32] |= 1u << (qt % 32);
+          }
+        }
+      }
+    }
+  }
+  free(qc);
+  free(kc);
+  free(score);
+  free(arr);
+  free(tile_cnt);
 }

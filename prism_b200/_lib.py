@@ -28,11 +28,14 @@ SIGNATURES = {
     "prism_zone_stats": (_I, [_P, _I, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "prism_shape_select": (_I, [_P, _P, _P, _I, _I, _I, _I, _F, _F, _F, _P, _P, _P, _P]),
     "prism_build_layout": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
-    "prism_tile_valid": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
-    "prism_gather_rows": (_I, [_P, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _P]),
+    "prism_tile_valid": (_I, [_P, _I64, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "prism_gather_rows": (_I, [_P, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I64, _P, _I64, _P]),
     "prism_scatter_rows": (_I, [_P, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _I64, _P]),
     "prism_block_select_workspace_bytes": (_SZ, [_I, _I64, _I]),
     "prism_block_select": (_I, [_P, _P, _I, _I64, _I, _P, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
+    "prism_uniform_layout": (_I, [_I, _I, _I, _I, _I, _I, _I64, _P, _P, _P]),
+    "prism_block_select_uniform_workspace_bytes": (_SZ, [_I, _I64, _I64, _I]),
+    "prism_block_select_uniform": (_I, [_P, _P, _I, _I64, _I, _I64, _I, _I, _P, _I, _D, _D, _P, _P, _P, _P]),
     "prism_bsa_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_workspace_bytes": (_SZ, [_I, _I64]),
     "prism_bsa_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
@@ -48,7 +51,7 @@ KERNELS = {
     "prism_build_layout": 2, "prism_tile_valid": 1, "prism_gather_rows": 1,
     "prism_scatter_rows": 1, "prism_block_select": 4, "prism_bsa_fwd": 1, "prism_bsa_bwd": 3,
     "prism_bsa_bwd_delta": 1, "prism_bsa_bwd_dkdv": 1, "prism_bsa_bwd_dq": 1,
-    "prism_bsa_bwd_noalloc": 3,
+    "prism_bsa_bwd_noalloc": 3, "prism_uniform_layout": 1, "prism_block_select_uniform": 4,
 }
 launch_count = 0
 

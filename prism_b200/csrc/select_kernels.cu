@@ -611,22 +611,27 @@ __global__ void pool_kernel(const uint16_t* __restrict__ q, const uint16_t* __re
 // ================================================================ a12
 // Register-tiled fp32 GEMM: score[a][b] = fma-chain over d = 0..D-1 of
 // qc[a][d] * kc[b][d] (each accumulator updated once per d, in order).
+// Per head: qc [na_max, D], kc [nb_max, D], score [na_max, nb_max].  The live
+// sizes are *n_blocks x *n_blocks when n_blocks is given (dynamic layouts,
+// known on the device only), else na_max x nb_max.
 constexpr int kScoreTile = 64;
 __global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc,
                                                     const float* __restrict__ kc, int D,
                                                     const int32_t* __restrict__ n_blocks,
-                                                    int nb_max, float* __restrict__ score) {
+                                                    int na_max, int nb_max,
+                                                    float* __restrict__ score) {
   extern __shared__ float ssm[];
-  const int nb = *n_blocks;
+  const int na = n_blocks ? *n_blocks : na_max;
+  const int nb = n_blocks ? *n_blocks : nb_max;
   const int a0 = blockIdx.y * kScoreTile, b0 = blockIdx.x * kScoreTile, h = blockIdx.z;
-  if (a0 >= nb || b0 >= nb) return;
+  if (a0 >= na || b0 >= nb) return;
   float* Qs = ssm;                       // [D][64+4]
   float* Ks = ssm + D * (kScoreTile + 4);
-  const float* qh = qc + (int64_t)h * nb_max * D;
+  const float* qh = qc + (int64_t)h * na_max * D;
   const float* kh = kc + (int64_t)h * nb_max * D;
   for (int i = threadIdx.x; i < kScoreTile * D; i += blockDim.x) {
     const int r = i / D, d = i % D;
-    Qs[d * (kScoreTile + 4) + r] = (a0 + r < nb) ? qh[(int64_t)(a0 + r) * D + d] : 0.0f;
+    Qs[d * (kScoreTile + 4) + r] = (a0 + r < na) ? qh[(int64_t)(a0 + r) * D + d] : 0.0f;
     Ks[d * (kScoreTile + 4) + r] = (b0 + r < nb) ? kh[(int64_t)(b0 + r) * D + d] : 0.0f;
   }
   __syncthreads();
@@ -647,11 +652,11 @@ __global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
   }
-  float* sh = score + (int64_t)h * nb_max * nb_max;
+  float* sh = score + (int64_t)h * na_max * nb_max;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int a = a0 + ty * 4 + i;
-    if (a >= nb) continue;
+    if (a >= na) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int b = b0 + tx * 4 + j;
@@ -664,6 +669,10 @@ __global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc
 // One CTA per (q block a, head h).  Keys are 32-bit patterns that order like
 // the values: non-negative softmax weights as raw float bits (modes 0/1), raw
 // scores mapped to an order-preserving unsigned integer (mode 2).
+// Block -> tile maps: with block_tiles (dynamic layouts) block b covers the
+// tiles block_tiles[2b], block_tiles[2b+1] (n_tiles = none); without it q block
+// a covers tiles [a*tq, a*tq+tq) and key block b tiles [b*tk, b*tk+tk)
+// (uniform chunks).  bvalid == nullptr means every key block is eligible.
 constexpr int kSelThreads = 256;
 
 __device__ __forceinline__ uint32_t f2key(float f) {
@@ -769,7 +778,8 @@ __device__ void radix_walk(const uint32_t* hist_cnt, const unsigned long long* h
 
 __global__ void __launch_bounds__(kSelThreads) select_kernel(
     const float* __restrict__ score, const uint8_t* __restrict__ bvalid,
-    const int32_t* __restrict__ n_blocks, int nb_max, const int32_t* __restrict__ block_tiles,
+    const int32_t* __restrict__ n_blocks, int na_max, int nb_max,
+    const int32_t* __restrict__ block_tiles, int tq, int tk,
     const uint64_t* __restrict__ tile_bits, int64_t n_tiles, int wq, int mode, double sparsity,
     double cdf, float sm_scale, uint32_t* __restrict__ bits_q) {
   extern __shared__ uint32_t keys[];  // [nb_max] then row bitmap [wq]
@@ -780,10 +790,11 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   __shared__ float redf[32];
   __shared__ RadixState st;
   __shared__ int tie_base[kSelThreads];
-  const int nb = *n_blocks;
+  const int na = n_blocks ? *n_blocks : na_max;
+  const int nb = n_blocks ? *n_blocks : nb_max;
   const int a = blockIdx.x, h = blockIdx.y;
-  if (a >= nb) return;
-  const float* srow = score + ((int64_t)h * nb_max + a) * nb_max;
+  if (a >= na) return;
+  const float* srow = score + ((int64_t)h * na_max + a) * nb_max;
   const int tid = threadIdx.x;
 
   // selection sizes (computed in double exactly as Python does on the host)
@@ -806,13 +817,14 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   long long n_eff;
 
   if (mode == 2) {
-    for (int i = tid; i < nb; i += blockDim.x) keys[i] = f2key(bvalid[i] ? srow[i] : -INFINITY);
+    for (int i = tid; i < nb; i += blockDim.x)
+      keys[i] = f2key((!bvalid || bvalid[i]) ? srow[i] : -INFINITY);
     n_eff = k_topk;
     __syncthreads();
   } else {
     float lmax = -INFINITY;
     for (int i = tid; i < nb; i += blockDim.x) {
-      const float x = bvalid[i] ? __fmul_rn(srow[i], sm_scale) : -INFINITY;
+      const float x = (!bvalid || bvalid[i]) ? __fmul_rn(srow[i], sm_scale) : -INFINITY;
       keys[i] = __float_as_uint(x);
       lmax = fmaxf(lmax, x);
     }
@@ -938,16 +950,18 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
         ++rank;
       }
       if (!sel) continue;
-      for (int p = 0; p < 2; ++p) {
-        const int kt = block_tiles[2 * i + p];
+      const int np = block_tiles ? 2 : tk;
+      for (int p = 0; p < np; ++p) {
+        const int kt = block_tiles ? block_tiles[2 * i + p] : i * tk + p;
         if (kt >= n_tiles || tile_bits[kt] == 0ull) continue;
         atomicOr(&row[kt >> 5], 1u << (kt & 31));
       }
     }
   }
   __syncthreads();
-  for (int p = 0; p < 2; ++p) {
-    const int qt = block_tiles[2 * a + p];
+  const int nq = block_tiles ? 2 : tq;
+  for (int p = 0; p < nq; ++p) {
+    const int qt = block_tiles ? block_tiles[2 * a + p] : a * tq + p;
     if (qt >= n_tiles) continue;
     uint32_t* dst = bits_q + ((int64_t)h * n_tiles + qt) * wq;
     for (int i = tid; i < wq; i += blockDim.x) dst[i] = row[i];
@@ -970,6 +984,65 @@ __global__ void transpose_bits_kernel(const uint32_t* __restrict__ bq, int64_t n
   }
 }
 
+// ============================================================ uniform chunks
+// rearrange_THW_to_3d_block order (bsa_interface.py:1105-1109): position
+// p = ((((nt*Nh + nh)*Nw + nw)*ct + t)*ch + h)*cw + w holds the token at
+// (nt*ct + t, nh*ch + h, nw*cw + w) of the padded grid.  Positions p >= Sp
+// (rows that round the sequence up to whole tile pairs) get the sentinel Sp,
+// which the gather reads as a zero row and the validity as padding.
+__global__ void uniform_perm_kernel(int Hp, int Wp, int ct, int ch, int cw, int64_t Sp,
+                                    int64_t n_rows, int32_t* __restrict__ src_idx,
+                                    int32_t* __restrict__ inv_idx) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n_rows) return;
+  if (p >= Sp) {
+    src_idx[p] = (int32_t)Sp;
+    return;
+  }
+  const int Nh = Hp / ch, Nw = Wp / cw;
+  int64_t r = p;
+  const int w = (int)(r % cw);
+  r /= cw;
+  const int h = (int)(r % ch);
+  r /= ch;
+  const int t = (int)(r % ct);
+  r /= ct;
+  const int nw = (int)(r % Nw);
+  r /= Nw;
+  const int nh = (int)(r % Nh);
+  const int64_t nt = r / Nh;
+  const int64_t g = ((nt * ct + t) * Hp + (int64_t)nh * ch + h) * Wp + (int64_t)nw * cw + w;
+  src_idx[p] = (int32_t)g;
+  inv_idx[g] = (int32_t)p;
+}
+
+// masked_mean_pooling_compression / mean_pooling_compression
+// (bsa_interface.py:164-201) over chunks of consecutive rows: sequential fp32
+// sum over the chunk's valid rows (bit s of the tile_bits words), divided by
+// max(count, 1).  One CTA per (chunk, head, tensor), D threads; blockIdx.z
+// picks x0 (n0 chunks of chunk0 rows -> out0) or x1 (n1 of chunk1 -> out1).
+__global__ void pool_chunk_kernel(const uint16_t* __restrict__ x0, const uint16_t* __restrict__ x1,
+                                  int64_t S, int D, int chunk0, int n0, int chunk1, int n1,
+                                  const uint64_t* __restrict__ tile_bits, float* __restrict__ out0,
+                                  float* __restrict__ out1) {
+  const int c = blockIdx.x, h = blockIdx.y, which = blockIdx.z;
+  const int chunk = which ? chunk1 : chunk0;
+  const int n = which ? n1 : n0;
+  if (c >= n) return;
+  const int64_t base = (int64_t)c * chunk;
+  const uint16_t* x = (which ? x1 : x0) + ((int64_t)h * S + base) * D + threadIdx.x;
+  float sum = 0.0f;
+  int cnt = 0;
+  for (int i = 0; i < chunk; ++i) {
+    const int64_t sidx = base + i;
+    if (!((tile_bits[sidx >> 6] >> (sidx & 63)) & 1ull)) continue;
+    sum = __fadd_rn(sum, bfbits2f(x[(int64_t)i * D]));
+    ++cnt;
+  }
+  const float den = cnt > 0 ? (float)cnt : 1.0f;
+  (which ? out1 : out0)[((int64_t)h * n + c) * D + threadIdx.x] = __fdiv_rn(sum, den);
+}
+
 }  // namespace prism
 
 using namespace prism;
@@ -978,7 +1051,7 @@ using namespace prism;
 extern "C" {
 
 const char* prism_last_error(void) { return prism::last_error(); }
-int prism_abi_version(void) { return 1; }
+int prism_abi_version(void) { return 2; }
 
 prism_status_t prism_token_norms(const void* x, int64_t n_tokens, int dim, void* out,
                                  cudaStream_t stream) {
@@ -1062,13 +1135,14 @@ prism_status_t prism_build_layout(const int64_t* shape_ids, int Tp, int Hp, int 
   return PRISM_OK;
 }
 
-prism_status_t prism_tile_valid(const int32_t* src_idx, const uint8_t* valid, int T, int H, int W,
-                                int Tp, int Hp, int Wp, uint64_t* tile_bits, int32_t* tile_count,
-                                cudaStream_t stream) {
+prism_status_t prism_tile_valid(const int32_t* src_idx, int64_t n_rows, const uint8_t* valid, int T,
+                                int H, int W, int Tp, int Hp, int Wp, uint64_t* tile_bits,
+                                int32_t* tile_count, cudaStream_t stream) {
   PRISM_CHECK_ARG(src_idx && tile_bits && tile_count, "prism_tile_valid: null pointer");
-  PRISM_CHECK_ARG(Tp % 8 == 0 && Hp % 8 == 0 && Wp % 8 == 0 && Tp > 0 && Hp > 0 && Wp > 0 &&
-                  T <= Tp && H <= Hp && W <= Wp, "prism_tile_valid: bad grids");
-  const int64_t nt = (int64_t)Tp * Hp * Wp / 64;
+  PRISM_CHECK_ARG(Tp > 0 && Hp > 0 && Wp > 0 && T <= Tp && H <= Hp && W <= Wp,
+                  "prism_tile_valid: bad grids");
+  PRISM_CHECK_ARG(n_rows >= 0 && n_rows % 64 == 0, "prism_tile_valid: row count must be a multiple of 64");
+  const int64_t nt = n_rows / 64;
   tile_valid_kernel<<<(unsigned)((nt * 32 + 255) / 256), 256, 0, stream>>>(src_idx, valid, nt, T, H, W, Hp, Wp,
                                                                             tile_bits, tile_count);
   PRISM_CHECK_LAUNCH("prism_tile_valid");
@@ -1077,14 +1151,15 @@ prism_status_t prism_tile_valid(const int32_t* src_idx, const uint8_t* valid, in
 
 prism_status_t prism_gather_rows(const void* x, int64_t x_stride_h, int64_t x_stride_s, int heads,
                                  int D, int T, int H, int W, int Tp, int Hp, int Wp,
-                                 const int32_t* src_idx, void* out, int64_t out_stride_h,
-                                 cudaStream_t stream) {
+                                 const int32_t* src_idx, int64_t n_rows, void* out,
+                                 int64_t out_stride_h, cudaStream_t stream) {
   PRISM_CHECK_ARG(x && src_idx && out, "prism_gather_rows: null pointer");
   PRISM_CHECK_ARG(D % 8 == 0 && x_stride_h % 8 == 0 && x_stride_s % 8 == 0 && out_stride_h % 8 == 0 &&
                   aligned16(x) && aligned16(out), "prism_gather_rows: rows must be 16-byte aligned (D %% 8 == 0)");
-  PRISM_CHECK_ARG(T <= Tp && H <= Hp && W <= Wp && Tp % 8 == 0 && Hp % 8 == 0 && Wp % 8 == 0,
+  PRISM_CHECK_ARG(T >= 1 && H >= 1 && W >= 1 && T <= Tp && H <= Hp && W <= Wp,
                   "prism_gather_rows: bad grids");
-  const int64_t Sp = (int64_t)Tp * Hp * Wp;
+  PRISM_CHECK_ARG(n_rows >= 0 && n_rows < (int64_t)1 << 31, "prism_gather_rows: bad row count");
+  const int64_t Sp = n_rows;
   const int chunks = D / 8;
   const int64_t total = (int64_t)heads * Sp * chunks;
   if (total == 0) return PRISM_OK;
@@ -1148,18 +1223,88 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),
                    "prism_block_select: smem attribute");
   const int nt = (nb_max + kScoreTile - 1) / kScoreTile;
-  score_kernel<<<dim3(nt, nt, heads), 256, ssm, stream>>>(qc, kc, D, n_blocks, nb_max, sc);
+  score_kernel<<<dim3(nt, nt, heads), 256, ssm, stream>>>(qc, kc, D, n_blocks, nb_max, nb_max, sc);
   PRISM_CHECK_LAUNCH("prism_block_select/score");
   const float sm_scale = (float)(1.0 / sqrt((double)D));
   const size_t selsm = ((size_t)nb_max + wq) * sizeof(uint32_t);
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)selsm),
                    "prism_block_select: smem attribute");
   select_kernel<<<dim3(nb_max, heads), kSelThreads, selsm, stream>>>(
-      sc, bvalid, n_blocks, nb_max, block_tiles, tile_bits, n_tiles, wq, mode, sparsity,
-      cdf_threshold, sm_scale, bits_q);
+      sc, bvalid, n_blocks, nb_max, nb_max, block_tiles, 2, 2, tile_bits, n_tiles, wq, mode,
+      sparsity, cdf_threshold, sm_scale, bits_q);
   PRISM_CHECK_LAUNCH("prism_block_select/select");
   transpose_bits_kernel<<<dim3(wq, wq, heads), 32, 0, stream>>>(bits_q, n_tiles, wq, bits_k);
   PRISM_CHECK_LAUNCH("prism_block_select/transpose");
+  return PRISM_OK;
+}
+
+prism_status_t prism_uniform_layout(int Tp, int Hp, int Wp, int ct, int ch, int cw, int64_t n_rows,
+                                    int32_t* src_idx, int32_t* inv_idx, cudaStream_t stream) {
+  PRISM_CHECK_ARG(src_idx && inv_idx, "prism_uniform_layout: null pointer");
+  PRISM_CHECK_ARG(ct > 0 && ch > 0 && cw > 0 && Tp > 0 && Hp > 0 && Wp > 0 && Tp % ct == 0 &&
+                  Hp % ch == 0 && Wp % cw == 0,
+                  "prism_uniform_layout: grid (%d,%d,%d) is not a multiple of the chunk (%d,%d,%d)",
+                  Tp, Hp, Wp, ct, ch, cw);
+  const int64_t Sp = (int64_t)Tp * Hp * Wp;
+  PRISM_CHECK_ARG(n_rows >= Sp && n_rows < (int64_t)1 << 31,
+                  "prism_uniform_layout: n_rows must cover the grid and stay below 2^31");
+  uniform_perm_kernel<<<(unsigned)((n_rows + 255) / 256), 256, 0, stream>>>(Hp, Wp, ct, ch, cw, Sp,
+                                                                             n_rows, src_idx, inv_idx);
+  PRISM_CHECK_LAUNCH("prism_uniform_layout");
+  return PRISM_OK;
+}
+
+size_t prism_block_select_uniform_workspace_bytes(int heads, int64_t n_chunks_q, int64_t n_chunks_k,
+                                                  int D) {
+  size_t b = (size_t)heads * (size_t)(n_chunks_q + n_chunks_k) * D * sizeof(float);  // pooled q, k
+  b += (size_t)heads * (size_t)n_chunks_q * (size_t)n_chunks_k * sizeof(float);     // scores
+  return b;
+}
+
+prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t S,
+                                          int D, int64_t seq, int chunk_q, int chunk_k,
+                                          const uint64_t* tile_bits, int mode, double sparsity,
+                                          double cdf_threshold, void* workspace, uint32_t* bits_q,
+                                          uint32_t* bits_k, cudaStream_t stream) {
+  PRISM_CHECK_ARG(q_re && k_re && tile_bits && workspace && bits_q && bits_k,
+                  "prism_block_select_uniform: null pointer");
+  PRISM_CHECK_ARG(mode >= 0 && mode <= 2, "prism_block_select_uniform: Either sparsity or cdf_threshold must be provided");
+  PRISM_CHECK_ARG(S > 0 && S % 64 == 0 && heads >= 1, "prism_block_select_uniform: S must be a positive multiple of 64");
+  PRISM_CHECK_ARG(D >= 16 && D <= 256, "prism_block_select_uniform: D=%d unsupported", D);
+  PRISM_CHECK_ARG(chunk_q > 0 && chunk_k > 0 && chunk_q % 64 == 0 && chunk_k % 64 == 0,
+                  "prism_block_select_uniform: chunk sizes (%d, %d) must be multiples of 64 tokens",
+                  chunk_q, chunk_k);
+  PRISM_CHECK_ARG(seq > 0 && seq <= S && seq % chunk_q == 0 && seq % chunk_k == 0,
+                  "prism_block_select_uniform: sequence %lld is not a whole number of chunks",
+                  (long long)seq);
+  const int64_t n_tiles = S / 64;
+  const int nq = (int)(seq / chunk_q), nk = (int)(seq / chunk_k);
+  PRISM_CHECK_ARG(nk <= 40000, "prism_block_select_uniform: %d key chunks exceed the per-row shared-memory limit", nk);
+  const int wq = (int)((n_tiles + 31) / 32);
+  float* qc = (float*)workspace;
+  float* kc = qc + (size_t)heads * nq * D;
+  float* sc = kc + (size_t)heads * nk * D;
+  PRISM_CHECK_CUDA(cudaMemsetAsync(bits_q, 0, (size_t)heads * n_tiles * wq * sizeof(uint32_t), stream),
+                   "prism_block_select_uniform: clear bitmaps");
+  pool_chunk_kernel<<<dim3(nq > nk ? nq : nk, heads, 2), D, 0, stream>>>(
+      (const uint16_t*)q_re, (const uint16_t*)k_re, S, D, chunk_q, nq, chunk_k, nk, tile_bits, qc, kc);
+  PRISM_CHECK_LAUNCH("prism_block_select_uniform/pool");
+  const size_t ssm = 2 * (size_t)D * (kScoreTile + 4) * sizeof(float);
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),
+                   "prism_block_select_uniform: smem attribute");
+  score_kernel<<<dim3((nk + kScoreTile - 1) / kScoreTile, (nq + kScoreTile - 1) / kScoreTile, heads), 256,
+                 ssm, stream>>>(qc, kc, D, nullptr, nq, nk, sc);
+  PRISM_CHECK_LAUNCH("prism_block_select_uniform/score");
+  const float sm_scale = (float)(1.0 / sqrt((double)D));
+  const size_t selsm = ((size_t)nk + wq) * sizeof(uint32_t);
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)selsm),
+                   "prism_block_select_uniform: smem attribute");
+  select_kernel<<<dim3(nq, heads), kSelThreads, selsm, stream>>>(
+      sc, nullptr, nullptr, nq, nk, nullptr, chunk_q / 64, chunk_k / 64, tile_bits, n_tiles, wq, mode,
+      sparsity, cdf_threshold, sm_scale, bits_q);
+  PRISM_CHECK_LAUNCH("prism_block_select_uniform/select");
+  transpose_bits_kernel<<<dim3(wq, wq, heads), 32, 0, stream>>>(bits_q, n_tiles, wq, bits_k);
+  PRISM_CHECK_LAUNCH("prism_block_select_uniform/transpose");
   return PRISM_OK;
 }
 

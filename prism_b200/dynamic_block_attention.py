@@ -33,20 +33,40 @@ _TILE = 64  # dynamic_block_attention.py:15
 
 
 class SparsePlan:
-    """Everything the kernels need for one attention call, built without grad."""
+    """Everything the kernels need for one attention call, built without grad.
 
-    def __init__(self, grid, grid_padded, layout, tile_bits, sparsity, cdf_threshold, sm_scale):
+    ``layout`` orders the queries (src_idx: row -> padded THW token, inv_idx its
+    inverse); ``layout_k`` orders keys and values when it differs (the uniform
+    path with different q / key chunk shapes).  ``uniform`` = dict(seq, chunk_q,
+    chunk_k) selects the uniform path's chunk selection instead of the dynamic
+    path's logical-block selection."""
+
+    def __init__(self, grid, grid_padded, layout, tile_bits, sparsity, cdf_threshold, sm_scale,
+                 layout_k=None, uniform=None):
         self.grid = tuple(grid)
         self.grid_padded = tuple(grid_padded)
         self.layout = layout
         self.src_idx = layout["src_idx"]
         self.inv_idx = layout["inv_idx"]
+        lk = layout if layout_k is None else layout_k
+        self.src_idx_k = lk["src_idx"]
+        self.inv_idx_k = lk["inv_idx"]
+        self.uniform = uniform
         self.tile_bits = tile_bits
         self.sparsity = sparsity
         self.cdf_threshold = cdf_threshold
         self.sm_scale = sm_scale
         self.bits_q = None
         self.bits_k = None
+
+    def select(self, q_re, k_re):
+        """Tile bitmaps (bits_q, bits_k) for tile-ordered q / k."""
+        if self.uniform is not None:
+            u = self.uniform
+            return ops.block_select_uniform(q_re, k_re, u["seq"], u["chunk_q"], u["chunk_k"],
+                                            self.tile_bits, self.sparsity, self.cdf_threshold)
+        return ops.block_select(q_re, k_re, self.layout, self.tile_bits, self.sparsity,
+                                self.cdf_threshold)
 
 
 def _hsd(x: torch.Tensor, layout: str) -> torch.Tensor:
@@ -64,20 +84,20 @@ def _new_like_layout(heads, S, D, layout, dtype, device):
     return t, t[0].transpose(0, 1)
 
 
-class _DynBsaFunction(torch.autograd.Function):
+class _BsaFunction(torch.autograd.Function):
     """Gather -> select -> sparse attention -> scatter, with the matching backward.
     Gradients flow to q, k, v only (selection is non-differentiable, as in the
-    reference's no_grad blocks at dynamic_block_attention.py:234, 256)."""
+    reference's no_grad blocks at dynamic_block_attention.py:234, 256 and the
+    index tensors of _attention_bsa, bsa_interface.py:597-683)."""
 
     @staticmethod
     def forward(ctx, q, k, v, plan: SparsePlan, layout: str):
         qh, kh, vh = _hsd(q, layout), _hsd(k, layout), _hsd(v, layout)
         heads, S, D = qh.shape
         q_re = ops.gather_rows(qh, plan.grid, plan.grid_padded, plan.src_idx)
-        k_re = ops.gather_rows(kh, plan.grid, plan.grid_padded, plan.src_idx)
-        v_re = ops.gather_rows(vh, plan.grid, plan.grid_padded, plan.src_idx)
-        bits_q, bits_k = ops.block_select(q_re, k_re, plan.layout, plan.tile_bits, plan.sparsity,
-                                          plan.cdf_threshold)
+        k_re = ops.gather_rows(kh, plan.grid, plan.grid_padded, plan.src_idx_k)
+        v_re = ops.gather_rows(vh, plan.grid, plan.grid_padded, plan.src_idx_k)
+        bits_q, bits_k = plan.select(q_re, k_re)
         plan.bits_q, plan.bits_k = bits_q, bits_k
         o_re, lse, o_lo = ops.bsa_fwd(q_re, k_re, v_re, bits_q, plan.tile_bits, plan.sm_scale,
                                       want_lo=True)
@@ -99,11 +119,14 @@ class _DynBsaFunction(torch.autograd.Function):
         dq_re, dk_re, dv_re = ops.bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k,
                                           plan.tile_bits, plan.sm_scale, o_lo=o_lo)
         grads = []
-        for g_re in (dq_re, dk_re, dv_re):
+        for g_re, inv in ((dq_re, plan.inv_idx), (dk_re, plan.inv_idx_k), (dv_re, plan.inv_idx_k)):
             g, g_hsd = _new_like_layout(heads, S, D, layout, dout.dtype, dout.device)
-            ops.scatter_rows(g_re, plan.grid, plan.grid_padded, plan.inv_idx, out=g_hsd)
+            ops.scatter_rows(g_re, plan.grid, plan.grid_padded, inv, out=g_hsd)
             grads.append(g)
         return grads[0], grads[1], grads[2], None, None
+
+
+_DynBsaFunction = _BsaFunction
 
 
 def _check_head_dim(D: int):

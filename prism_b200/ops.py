@@ -132,29 +132,31 @@ def tile_valid(src_idx, valid, grid, grid_padded):
     _check_cuda(src_idx, valid)
     T, H, W = grid
     Tp, Hp, Wp = grid_padded
-    n_tiles = src_idx.numel() // 64
+    n_rows = src_idx.numel()
+    n_tiles = n_rows // 64
     dev = src_idx.device
     bits = torch.empty(n_tiles, dtype=torch.int64, device=dev)
     cnt = torch.empty(n_tiles, dtype=torch.int32, device=dev)
     vm = None if valid is None else valid.to(torch.uint8).contiguous()
-    _lib.call("prism_tile_valid", _p(src_idx), _p(vm), T, H, W, Tp, Hp, Wp, _p(bits), _p(cnt),
-              _stream(src_idx))
+    _lib.call("prism_tile_valid", _p(src_idx), n_rows, _p(vm), T, H, W, Tp, Hp, Wp, _p(bits),
+              _p(cnt), _stream(src_idx))
     return bits, cnt
 
 
 # -------------------------------------------------------------- a10/a17
 def gather_rows(x_hsd: torch.Tensor, grid, grid_padded, src_idx: torch.Tensor) -> torch.Tensor:
-    """x_hsd [heads, T*H*W, D] (D contiguous) -> [heads, S_p, D] tile order, zero rows
-    for padded tokens."""
+    """x_hsd [heads, T*H*W, D] (D contiguous) -> [heads, len(src_idx), D] tile order,
+    zero rows for padded tokens."""
     _check_cuda(x_hsd, src_idx)
     heads, S, D = x_hsd.shape
     T, H, W = grid
     Tp, Hp, Wp = grid_padded
     if x_hsd.stride(2) != 1:
         raise ValueError("rows must be contiguous")
-    out = torch.empty(heads, Tp * Hp * Wp, D, dtype=x_hsd.dtype, device=x_hsd.device)
+    n_rows = src_idx.numel()
+    out = torch.empty(heads, n_rows, D, dtype=x_hsd.dtype, device=x_hsd.device)
     _lib.call("prism_gather_rows", _p(x_hsd), x_hsd.stride(0), x_hsd.stride(1), heads, D, T, H, W,
-              Tp, Hp, Wp, _p(src_idx), _p(out), out.stride(0), _stream(x_hsd))
+              Tp, Hp, Wp, _p(src_idx), n_rows, _p(out), out.stride(0), _stream(x_hsd))
     return out
 
 
@@ -186,6 +188,39 @@ def block_select(q_re, k_re, layout, tile_bits, sparsity, cdf_threshold):
     _lib.call("prism_block_select", _p(q_re), _p(k_re), heads, S, D, _p(layout["block_tiles"]),
               _p(layout["n_blocks"]), _p(tile_bits), mode,
               float(sparsity if sparsity is not None else 0.0),
+              float(cdf_threshold if cdf_threshold is not None else 0.0), _p(ws), _p(bits_q),
+              _p(bits_k), _stream(q_re))
+    return bits_q, bits_k
+
+
+# ------------------------------------------------------- uniform chunks
+def uniform_layout(grid_padded, chunk, n_rows: int, device):
+    """src_idx [n_rows] / inv_idx [Tp*Hp*Wp] int32 of the 3D-chunk order
+    (rearrange_THW_to_3d_block, bsa_interface.py:1105-1109)."""
+    Tp, Hp, Wp = grid_padded
+    ct, ch, cw = chunk
+    src = torch.empty(n_rows, dtype=torch.int32, device=device)
+    inv = torch.empty(Tp * Hp * Wp, dtype=torch.int32, device=device)
+    _lib.call("prism_uniform_layout", Tp, Hp, Wp, ct, ch, cw, n_rows, _p(src), _p(inv),
+              ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+    return src, inv
+
+
+def block_select_uniform(q_re, k_re, seq: int, chunk_q: int, chunk_k: int, tile_bits, sparsity,
+                         cdf_threshold):
+    """Chunk pooling + scores + selection of the uniform path -> (bits_q, bits_k)."""
+    _check_cuda(q_re, k_re, tile_bits)
+    heads, S, D = q_re.shape
+    mode = selection_mode(sparsity, cdf_threshold)
+    n_tiles = S // 64
+    wq = (n_tiles + 31) // 32
+    dev = q_re.device
+    bits_q = torch.empty(heads, n_tiles, wq, dtype=torch.int32, device=dev)
+    bits_k = torch.empty(heads, n_tiles, wq, dtype=torch.int32, device=dev)
+    ws = _ws(_lib.query("prism_block_select_uniform_workspace_bytes", heads, seq // chunk_q,
+                        seq // chunk_k, D), dev)
+    _lib.call("prism_block_select_uniform", _p(q_re), _p(k_re), heads, S, D, seq, chunk_q, chunk_k,
+              _p(tile_bits), mode, float(sparsity if sparsity is not None else 0.0),
               float(cdf_threshold if cdf_threshold is not None else 0.0), _p(ws), _p(bits_q),
               _p(bits_k), _stream(q_re))
     return bits_q, bits_k

@@ -41,9 +41,21 @@ class Case:
     lambda_128: float = 1.0
     seed: int = 0
     extra: dict = field(default_factory=dict)
+    # uniform fixed-shape path (flash_attn_bsa_3d) when set: q / key chunk shapes
+    chunk_q: Optional[Tuple[int, int, int]] = None
+    chunk_k: Optional[Tuple[int, int, int]] = None
+
+    @property
+    def uniform(self):
+        return self.chunk_q is not None
 
     @property
     def grid_padded(self):
+        if self.uniform:
+            # the uniform dispatch pads each axis to the larger chunk extent
+            # (wan_video_dit.py:473-481)
+            m = [max(a, b) for a, b in zip(self.chunk_q, self.chunk_k)]
+            return tuple(int(math.ceil(x / c) * c) for x, c in zip(self.grid, m))
         return tuple(int(math.ceil(x / 8) * 8) for x in self.grid)
 
     @property
@@ -75,6 +87,27 @@ CASES = {
     "nopad_bf16": Case("nopad_bf16", (8, 8, 16), 2, 64, values="aniso", amp=(0.1, 1.0),
                        sparsity=0.75, cdf_threshold=0.9, seed=50),
 }
+
+# Uniform fixed-shape path (flash_attn_bsa_3d, bsa_interface.py:1123-1176).
+UNIFORM_CASES = {
+    # 4x4x4 chunks with the training configs' sparsity 0.75 / cdf 0.2; padded grid
+    "u64_pad": Case("u64_pad", (6, 10, 12), 2, 64, values="aniso", amp=(0.05, 1.0), audio=False,
+                    sparsity=0.75, cdf_threshold=0.2, chunk_q=(4, 4, 4), chunk_k=(4, 4, 4),
+                    seed=60),
+    # 4x4x8 chunks (the function's default), no padding, top-k only, head_dim 128
+    "u128_nopad": Case("u128_nopad", (8, 8, 16), 2, 128, values="aniso", amp=(0.1, 1.0),
+                       audio=False, sparsity=0.5, cdf_threshold=None, chunk_q=(4, 4, 8),
+                       chunk_k=(4, 4, 8), seed=61),
+    # 64-token q chunks against 128-token key chunks, cumulative mass only, padded
+    "umix_cdf": Case("umix_cdf", (5, 9, 14), 2, 64, values="aniso", amp=(0.05, 1.0), audio=False,
+                     sparsity=None, cdf_threshold=0.6, chunk_q=(4, 4, 4), chunk_k=(4, 4, 8),
+                     seed=62),
+    # three chunks (an odd number of tiles), head_dim 128, top-k + cumulative mass
+    "u_odd_d128": Case("u_odd_d128", (3, 4, 12), 2, 128, audio=False, sparsity=0.5,
+                       cdf_threshold=0.9, chunk_q=(4, 4, 4), chunk_k=(4, 4, 4), seed=63),
+}
+
+ALL_CASES = dict(CASES, **UNIFORM_CASES)
 
 
 def _zoned(gen, heads, grid_p, D, amp):
@@ -119,12 +152,14 @@ def make_inputs(case: Case):
     Tp, Hp, Wp = case.grid_padded
     h, D = case.heads, case.head_dim
     out = {}
+    # value models live on 8x8x8 macro-zones: generate on the grid rounded up to 8
+    Tg, Hg, Wg = (int(math.ceil(x / 8) * 8) for x in (Tp, Hp, Wp))
     for i, name in enumerate(("q", "k", "v", "do")):
         gen = torch.Generator().manual_seed(case.seed + i)
         if case.values in ("zoned", "aniso") and name != "do":
             fn = _zoned if case.values == "zoned" else _aniso
-            full = fn(gen, h, (Tp, Hp, Wp), D, case.amp)
-            x = full.reshape(h, Tp, Hp, Wp, D)[:, :T, :H, :W].reshape(1, h, T * H * W, D)
+            full = fn(gen, h, (Tg, Hg, Wg), D, case.amp)
+            x = full.reshape(h, Tg, Hg, Wg, D)[:, :T, :H, :W].reshape(1, h, T * H * W, D)
         else:
             x = torch.randn(1, h, T * H * W, D, generator=gen)
         out[name + "_u"] = x.to(torch.bfloat16)

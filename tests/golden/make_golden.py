@@ -45,7 +45,7 @@ import torch  # noqa: E402
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
-from inputs import CASES, make_inputs  # noqa: E402
+from inputs import ALL_CASES, make_inputs  # noqa: E402
 
 N_ROWS = 128  # output rows stored per head (a fixed random subset)
 
@@ -62,7 +62,8 @@ def import_reference(root):
     stub("hymm.utils", f"{root}/hymm/utils")
     from hymm.models.modules.block_sparse_attention import dynamic_block_attention as dba
     from hymm.models.modules.block_sparse_attention import dynamic_block_shape as dbs
-    return dba, dbs
+    from hymm.models.modules.block_sparse_attention import bsa_interface as bsa
+    return dba, dbs, bsa
 
 
 def run_case(dba, dbs, case):
@@ -137,17 +138,100 @@ def run_case(dba, dbs, case):
     return res
 
 
+def chunk_lists_to_dense(block_indices, lens, n_cols):
+    """Reference chunk selection (block_indices [B,h,nq,W], lens [B,h,nq]) -> [h, nq, n_cols]."""
+    bi = np.asarray(block_indices)[0]
+    ln = np.asarray(lens)[0]
+    h, nq, w = bi.shape
+    dense = np.zeros((h, nq, n_cols), bool)
+    keep = np.arange(w)[None, None, :] < ln[..., None]
+    hh, rr, cc = np.nonzero(keep)
+    dense[hh, rr, bi[hh, rr, cc]] = True
+    return dense
+
+
+def run_uniform_case(bsa, case):
+    """flash_attn_bsa_3d (bsa_interface.py:1123-1176) on the padded grid, as the
+    uniform dispatch of wan_video_dit.py:470-560 calls it.  Stores the chunk
+    orders, the chunk-level selection of a bf16 and an fp32 pass, and the fp32
+    outputs / gradients on a fixed subset of rows (padded THW order)."""
+    from oracle.oracle import dense_to_bits
+
+    inp = make_inputs(case)
+    Tp, Hp, Wp = case.grid_padded
+    S = Tp * Hp * Wp
+    q, k, v, do, valid = inp["q"], inp["k"], inp["v"], inp["do"], inp["valid"]
+    cq, ck = case.chunk_q, case.chunk_k
+    nq, nk = S // (cq[0] * cq[1] * cq[2]), S // (ck[0] * ck[1] * ck[2])
+    kw = dict(sparsity=case.sparsity, cdf_threshold=case.cdf_threshold,
+              chunk_3d_shape_q=list(cq), chunk_3d_shape_k=list(ck), valid_mask=valid)
+    captured = []
+    orig = bsa.attn_fwd_bsa_varlen_triton
+
+    def skip(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2):
+        captured.append(dict(bi=block_indices.clone(), lens=lens.clone()))
+        return torch.zeros_like(q_), torch.zeros(q_.shape[:3])
+
+    def capture(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2):
+        captured.append(dict(bi=block_indices.clone(), lens=lens.clone()))
+        return orig(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2)
+
+    try:
+        # pass 1: bf16 inputs, selection only (the kernel call is captured and skipped)
+        bsa.attn_fwd_bsa_varlen_triton = skip
+        with torch.no_grad():
+            bsa.flash_attn_bsa_3d(q, k, v, case.grid_padded, case.grid_padded, **kw)
+        sel16 = captured.pop()
+        # pass 2: fp32 values (bf16-representable), real kernels, autograd
+        bsa.attn_fwd_bsa_varlen_triton = capture
+        q32, k32, v32 = (t.float().requires_grad_(True) for t in (q, k, v))
+        out = bsa.flash_attn_bsa_3d(q32, k32, v32, case.grid_padded, case.grid_padded, **kw)
+        (out * do.float()).sum().backward()
+        sel32 = captured.pop()
+    finally:
+        bsa.attn_fwd_bsa_varlen_triton = orig
+
+    dense16 = chunk_lists_to_dense(sel16["bi"].numpy(), sel16["lens"].numpy(), nk)
+    dense32 = chunk_lists_to_dense(sel32["bi"].numpy(), sel32["lens"].numpy(), nk)
+    if valid is not None:
+        assert (dense16 == dense32).all(), "selection differs between bf16 and fp32 passes"
+    ar = torch.arange(S, dtype=torch.float64).view(1, 1, S, 1)
+    src = []
+    for c in (cq, ck):
+        n3 = (Tp // c[0], Hp // c[1], Wp // c[2])
+        src.append(bsa.rearrange_THW_to_3d_block(ar, *n3, *c, 1).view(-1).long().numpy())
+    res = dict(grid=np.array(case.grid), grid_padded=np.array(case.grid_padded),
+               chunk_q=np.array(cq), chunk_k=np.array(ck),
+               src_idx_q=src[0].astype(np.int32), src_idx_k=src[1].astype(np.int32),
+               sel_chunks=dense_to_bits(dense16), sel_chunks_f32=dense_to_bits(dense32))
+    o = out.detach()[0].numpy()
+    grads = [t.grad[0].numpy() for t in (q32, k32, v32)]
+    rng = np.random.default_rng(1234)
+    rows = np.sort(rng.choice(S, size=min(S, N_ROWS), replace=False))
+    res["rows"] = rows.astype(np.int64)
+    res["o"] = o[:, rows]
+    res["dq"], res["dk"], res["dv"] = (gr[:, rows] for gr in grads)
+    res["sums"] = np.array([np.abs(x).astype(np.float64).sum() for x in [o] + grads])
+    return res
+
+
 def main():
     root = os.environ.get("PRISM_REFERENCE")
     if not root:
         sys.exit("set PRISM_REFERENCE to the root of a Prism checkout")
-    dba, dbs = import_reference(root)
+    dba, dbs, bsa = import_reference(root)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    names = sys.argv[1:] or list(CASES)
+    names = sys.argv[1:] or list(ALL_CASES)
     for name in names:
-        case = CASES[name]
-        res = run_case(dba, dbs, case)
+        case = ALL_CASES[name]
         path = os.path.join(HERE, f"{name}.npz")
+        if case.uniform:
+            res = run_uniform_case(bsa, case)
+            np.savez_compressed(path, **res)
+            print(f"{name}: uniform chunks {case.chunk_q}/{case.chunk_k} -> {path} "
+                  f"({os.path.getsize(path)} B)")
+            continue
+        res = run_case(dba, dbs, case)
         np.savez_compressed(path, **res)
         print(f"{name}: shapes {np.bincount(res['shape_ids'], minlength=13).tolist()} "
               f"-> {path} ({os.path.getsize(path)} B)")
