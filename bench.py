@@ -53,6 +53,20 @@ TRAFFIC_PER_HEAD_720P = {"bsa_fwd": (525.5e6 + 172.8e6) / 4,
                          "bsa_bwd_dkdv": (581.9e6 + 175.0e6) / 4,
                          "bsa_bwd_dq": (594.0e6 + 92.8e6) / 4}
 FWD_BWD_FACTOR = 3.5  # 1 (forward) + 2.5 (backward): the canonical FLOP count of one fwd+bwd
+# --path uniform: the uniform fixed-shape path (flash_attn_bsa_3d) with the training
+# configs' block-sparse settings (4x4x4 chunks, sparsity 0.75, cdf threshold 0.2)
+UNIFORM = dict(chunk=(4, 4, 4), sparsity=0.75, cdf_threshold=0.2)
+
+
+def uniform_grid():
+    c = CONFIG["chunk"]
+    return tuple(math.ceil(x / ci) * ci for x, ci in zip(CONFIG["grid"], c))
+
+
+def padded_grid():
+    if CONFIG.get("path") == "uniform":
+        return uniform_grid()
+    return tuple(math.ceil(x / 8) * 8 for x in CONFIG["grid"])
 
 
 # ------------------------------------------------------------------ inputs
@@ -126,19 +140,24 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ step
-def make_step(inp, S, world, capture=None):
-    import torch
-    from prism_b200.attention import dynamic_self_attention
-
-    T, H, W = CONFIG["grid"]
-    h = CONFIG["heads"]
-
-    def step(q, k, v, do, a2v):
-        x, _ = dynamic_self_attention(q, k, v, (T, H, W), h, a2v_bridge_residual=a2v,
-                                      full_seq_len=S, method=CONFIG["method"],
+def attend(q, k, v, a2v, S):
+    """The layer's attention core through the package's public API (either path)."""
+    from prism_b200.attention import dynamic_self_attention, uniform_self_attention
+    if CONFIG.get("path") == "uniform":
+        return uniform_self_attention(q, k, v, CONFIG["grid"], CONFIG["heads"], full_seq_len=S,
                                       sparsity=CONFIG["sparsity"],
                                       cdf_threshold=CONFIG["cdf_threshold"],
-                                      return_shape_ids=True)
+                                      chunk_3d_shape_q=CONFIG["chunk"],
+                                      chunk_3d_shape_k=CONFIG["chunk"])
+    return dynamic_self_attention(q, k, v, CONFIG["grid"], CONFIG["heads"], a2v_bridge_residual=a2v,
+                                  full_seq_len=S, method=CONFIG["method"],
+                                  sparsity=CONFIG["sparsity"],
+                                  cdf_threshold=CONFIG["cdf_threshold"])
+
+
+def make_step(inp, S, world, capture=None):
+    def step(q, k, v, do, a2v):
+        x = attend(q, k, v, a2v, S)
         x.backward(do)
         return x
     return step
@@ -149,6 +168,7 @@ def selected_pairs(q, k, v, a2v, S, world):
     import torch
     from prism_b200.attention import audio_token_norms
     from prism_b200.communications import all_to_all_4D
+    from prism_b200.bsa_interface import run_bsa_uniform
     from prism_b200.dynamic_block_attention import run_bsa_dynamic
     from prism_b200.parallel_states import get_sequence_parallel_state, nccl_info
     h, D = CONFIG["heads"], CONFIG["head_dim"]
@@ -158,9 +178,17 @@ def selected_pairs(q, k, v, a2v, S, world):
         if get_sequence_parallel_state():
             g = nccl_info.sp_group
             q4, k4, v4 = (all_to_all_4D(t, g, 2, 1, S) for t in (q4, k4, v4))
-        _, plan = run_bsa_dynamic(q4, k4, v4, CONFIG["grid"], layout="bshd", method=CONFIG["method"],
-                                  sparsity=CONFIG["sparsity"], cdf_threshold=CONFIG["cdf_threshold"],
-                                  audio_token_norms=norms, return_plan=True)
+        if CONFIG.get("path") == "uniform":
+            _, plan = run_bsa_uniform(q4, k4, v4, CONFIG["grid"], layout="bshd",
+                                      sparsity=CONFIG["sparsity"],
+                                      cdf_threshold=CONFIG["cdf_threshold"],
+                                      chunk_3d_shape_q=CONFIG["chunk"],
+                                      chunk_3d_shape_k=CONFIG["chunk"], return_plan=True)
+        else:
+            _, plan = run_bsa_dynamic(q4, k4, v4, CONFIG["grid"], layout="bshd",
+                                      method=CONFIG["method"], sparsity=CONFIG["sparsity"],
+                                      cdf_threshold=CONFIG["cdf_threshold"],
+                                      audio_token_norms=norms, return_plan=True)
         def popcount(words):
             x = words.to(torch.int64) & 0xFFFFFFFF
             cnt = torch.zeros_like(x)
@@ -184,8 +212,8 @@ def kernel_times(plan, q4, k4, v4, reps=3):
     from prism_b200.dynamic_block_attention import _hsd
     qh, kh, vh = (_hsd(t, "bshd") for t in (q4, k4, v4))
     q_re = ops.gather_rows(qh, plan.grid, plan.grid_padded, plan.src_idx)
-    k_re = ops.gather_rows(kh, plan.grid, plan.grid_padded, plan.src_idx)
-    v_re = ops.gather_rows(vh, plan.grid, plan.grid_padded, plan.src_idx)
+    k_re = ops.gather_rows(kh, plan.grid, plan.grid_padded, plan.src_idx_k)
+    v_re = ops.gather_rows(vh, plan.grid, plan.grid_padded, plan.src_idx_k)
     heads, Sp, D = q_re.shape
     stream = torch.cuda.current_stream()
     ev = lambda: torch.cuda.Event(enable_timing=True)
@@ -231,27 +259,34 @@ def cpu_baseline(seconds=15.0, threads=None):
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     T, H, W = CONFIG["grid"]
     D = CONFIG["head_dim"]
-    Tp, Hp, Wp = (math.ceil(x / 8) * 8 for x in (T, H, W))
+    Tp, Hp, Wp = padded_grid()
     rng = np.random.default_rng(0)
-    Nz = (Tp // 8) * (Hp // 8) * (Wp // 8)
     S = Tp * Hp * Wp
     nt = S // 64
+    n_groups = S // 512
 
     def zoned():
-        mean = rng.standard_normal((Nz, D), dtype=np.float32) * 0.5
+        mean = rng.standard_normal((n_groups, D), dtype=np.float32) * 0.5
         x = np.repeat(mean, 512, axis=0) + 0.15 * rng.standard_normal((S, D), dtype=np.float32)
         return x
 
     q, k, v = zoned(), zoned(), zoned()
     do = rng.standard_normal((S, D), dtype=np.float32)
     valid = np.ones(S, np.uint8)
-    # selection (C oracle, one head) -- all 64-token shape-0 layout of the bench grid
-    t0 = time.perf_counter()
-    ids = np.zeros(Nz, np.int64)
-    src, inv, bot, bt, nb = O.layout(ids, (Tp, Hp, Wp))
     qb = O.f32_to_bf16_bits(q)[None]
     kb = O.f32_to_bf16_bits(k)[None]
-    bq, bk, _ = O.block_select(qb, kb, valid, bt, nb, CONFIG["sparsity"], CONFIG["cdf_threshold"])
+    t0 = time.perf_counter()
+    if CONFIG.get("path") == "uniform":
+        # selection (C oracle, one head) over the uniform chunk order
+        c = int(math.prod(CONFIG["chunk"]))
+        bq, bk, _ = O.block_select_uniform(qb, kb, S, c, c, None, CONFIG["sparsity"],
+                                           CONFIG["cdf_threshold"])
+    else:
+        # selection (C oracle, one head) -- all 64-token shape-0 layout of the bench grid
+        ids = np.zeros(S // 512, np.int64)
+        src, inv, bot, bt, nb = O.layout(ids, (Tp, Hp, Wp))
+        bq, bk, _ = O.block_select(qb, kb, valid, bt, nb, CONFIG["sparsity"],
+                                   CONFIG["cdf_threshold"])
     t_sel = time.perf_counter() - t0
     dense = O.bits_to_dense(bq, nt)[0]
     # attention: as many q tiles as fit the time budget
@@ -298,12 +333,21 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", default="720p", choices=sorted(CONFIGS),
                     help="benchmark config: 720p (config 1, default), 1080p (config 2), 2k (config 3)")
+    ap.add_argument("--path", default="dynamic", choices=["dynamic", "uniform"],
+                    help="dynamic block shapes (flash_attn_bsa_3d_dynamic, the metric's path) or "
+                         "the uniform fixed-shape path (flash_attn_bsa_3d, 4x4x4 chunks, "
+                         "sparsity 0.75, cdf 0.2)")
     ap.add_argument("--heads", type=int, default=CONFIG["heads"],
                     help="attention heads of the layer (40 in every benchmark config; smaller only "
                          "for profiler captures)")
     args = ap.parse_args()
     CONFIG.update(CONFIGS[args.config])
     CONFIG["heads"] = args.heads
+    CONFIG["path"] = args.path
+    if args.path == "uniform":
+        CONFIG.update(UNIFORM, method=None)
+        CONFIG["workload"] = CONFIG["workload"].replace(
+            "dynamic BSA", "uniform BSA (4x4x4 chunks, sparsity 0.75, cdf 0.2)")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -393,7 +437,7 @@ def main():
     D = CONFIG["head_dim"]
     flops = FWD_BWD_FACTOR * 4 * D * 64 * 64 * total_pairs
     tflops = flops / (ms * 1e-3) / 1e12
-    Tp, Hp, Wp = (math.ceil(x / 8) * 8 for x in CONFIG["grid"])
+    Tp, Hp, Wp = padded_grid()
     n_tiles = Tp * Hp * Wp // 64
     density = total_pairs / (CONFIG["heads"] * n_tiles * n_tiles)
 
@@ -413,7 +457,7 @@ def main():
     dom = max(("bsa_fwd", "bsa_bwd_dkdv", "bsa_bwd_dq"), key=lambda n: kt[n])
     achieved = algo[dom] / (kt[dom] * 1e-3) / 1e12
     traffic = None
-    if args.config == "720p" and D == 128:
+    if args.config == "720p" and D == 128 and args.path == "dynamic":
         traffic = TRAFFIC_PER_HEAD_720P[dom] * (CONFIG["heads"] // world)
     roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
@@ -429,15 +473,11 @@ def main():
         outs = {n: torch.empty(inp["q"].shape, dtype=torch.bfloat16).pin_memory() for n in ("o", "dq", "dk", "dv")}
         h2d = sum(x.numel() * x.element_size() for x in host.values())
         d2h = sum(x.numel() * x.element_size() for x in outs.values())
-        from prism_b200.attention import dynamic_self_attention
-
         def e2e_step():
             dq_, dk_, dv_ = (host[n].to(dev, non_blocking=True).requires_grad_(True) for n in ("q", "k", "v"))
             dd = host["do"].to(dev, non_blocking=True)
             aa = host["a2v"].to(dev, non_blocking=True)
-            x = dynamic_self_attention(dq_, dk_, dv_, CONFIG["grid"], CONFIG["heads"], a2v_bridge_residual=aa,
-                                       full_seq_len=S, method=CONFIG["method"], sparsity=CONFIG["sparsity"],
-                                       cdf_threshold=CONFIG["cdf_threshold"])
+            x = attend(dq_, dk_, dv_, aa, S)
             x.backward(dd)
             outs["o"].copy_(x.detach(), non_blocking=True)
             outs["dq"].copy_(dq_.grad, non_blocking=True)

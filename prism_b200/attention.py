@@ -14,6 +14,9 @@ for the dynamic block-shape path:
   into the gather kernel);
 * padding-only ranks stay connected to the graph (:814-823);
 * heads->sequence all-to-all of the output and head truncation (:824-828).
+
+``uniform_self_attention`` is the same branch for the uniform fixed-shape path
+(the plain-BSA dispatch, :470-560).
 """
 from __future__ import annotations
 
@@ -24,6 +27,7 @@ import torch
 from . import ops
 from .communications import (all_gather, all_to_all_4D, sp_num_local_real_heads,
                              sp_pad_heads, sp_pad_num_heads)
+from .bsa_interface import run_bsa_uniform
 from .dynamic_block_attention import run_bsa_dynamic
 from .parallel_states import get_sequence_parallel_state, nccl_info
 
@@ -41,6 +45,49 @@ def audio_token_norms(a2v_bridge_residual: Optional[torch.Tensor], full_seq_len:
         return local[0]
 
 
+def _sp_self_attention(q, k, v, num_heads: int, full_seq_len, run_local, idle_local=None):
+    """The Ulysses SP branch of SelfAttention.forward (wan_video_dit.py:764-828)
+    around a local attention.  q, k, v: [B=1, S_local, num_heads*D].
+    run_local(q4, k4, v4) gets [1, S, h, D] views (bshd) of the local heads and
+    returns (x [1, S, h, D], extra); idle_local() runs on a rank that holds only
+    padding heads, before its output all-to-all (collectives the local
+    attention would have joined).  Returns (x [B, S_local, num_heads*D], extra)."""
+    b, s_local, hd = q.shape
+    D = hd // num_heads
+    q4, k4, v4 = (t.view(b, s_local, num_heads, D) for t in (q, k, v))
+    if not get_sequence_parallel_state():
+        x, extra = run_local(q4, k4, v4)
+        return x.flatten(2), extra
+    P = nccl_info.sp_size
+    rank = nccl_info.rank_within_spgroup
+    padded = sp_pad_num_heads(num_heads, P)
+    if padded != num_heads:
+        q4, k4, v4 = (sp_pad_heads(t, padded) for t in (q4, k4, v4))
+    group = nccl_info.sp_group
+    q4 = all_to_all_4D(q4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
+    k4 = all_to_all_4D(k4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
+    v4 = all_to_all_4D(v4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
+    hpr = q4.shape[2]
+    local = sp_num_local_real_heads(num_heads, padded, P, rank)
+    extra = None
+    if local > 0:
+        if local != hpr:
+            q4, k4, v4 = q4[:, :, :local], k4[:, :, :local], v4[:, :, :local]
+        x, extra = run_local(q4, k4, v4)
+        if x.shape[2] != hpr:
+            x = sp_pad_heads(x, hpr)
+    else:
+        # padding-only rank: keep the graph connected so the backward
+        # all-to-alls fire symmetrically on every rank (wan_video_dit.py:814-823)
+        if idle_local is not None:
+            idle_local()
+        x = (q4 + k4 + v4) * 0.0
+    x = all_to_all_4D(x, group, scatter_dim=1, gather_dim=2, full_seq_len=full_seq_len)
+    if padded != num_heads:
+        x = x[:, :, :num_heads]
+    return x.flatten(2), extra
+
+
 def dynamic_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            grid_size: Tuple[int, int, int], num_heads: int, *,
                            a2v_bridge_residual: Optional[torch.Tensor] = None,
@@ -52,52 +99,42 @@ def dynamic_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            return_shape_ids: bool = False):
     """q, k, v: [B=1, S_local, num_heads*D] (projected, normed, rotated).
     Returns x [B, S_local, num_heads*D] (input of the output projection)."""
-    b, s_local, hd = q.shape
-    D = hd // num_heads
+    D = q.shape[2] // num_heads
     norms = audio_token_norms(a2v_bridge_residual, full_seq_len)
     kw = dict(method=method, sparsity=sparsity, cdf_threshold=cdf_threshold, lambda_a=lambda_a,
               tau_128=tau_128, lambda_128=lambda_128, shape_ids=shape_ids, return_shape_ids=True,
               audio_token_norms=norms, layout="bshd")
-    q4, k4, v4 = (t.view(b, s_local, num_heads, D) for t in (q, k, v))
-    used = shape_ids
-    if get_sequence_parallel_state():
-        P = nccl_info.sp_size
-        rank = nccl_info.rank_within_spgroup
-        padded = sp_pad_num_heads(num_heads, P)
-        if padded != num_heads:
-            q4, k4, v4 = (sp_pad_heads(t, padded) for t in (q4, k4, v4))
-        group = nccl_info.sp_group
-        q4 = all_to_all_4D(q4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
-        k4 = all_to_all_4D(k4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
-        v4 = all_to_all_4D(v4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
-        hpr = q4.shape[2]
-        local = sp_num_local_real_heads(num_heads, padded, P, rank)
-        if local > 0:
-            if local != hpr:
-                q4, k4, v4 = q4[:, :, :local], k4[:, :, :local], v4[:, :, :local]
-            x, used = run_bsa_dynamic(q4, k4, v4, grid_size, **kw)
-            if x.shape[2] != hpr:
-                x = sp_pad_heads(x, hpr)
-        else:
-            # padding-only rank: keep the graph connected so the backward
-            # all-to-alls fire symmetrically on every rank (wan_video_dit.py:814-823).
-            # The zone statistics all-reduce must still be joined.
+
+    def idle():
+        # the zone statistics all-reduce must still be joined
+        if shape_ids is None:
             from .dynamic_block_shape import _maybe_sp_average
             Tp, Hp, Wp = ops.padded_grid(grid_size)
             Nz = (Tp // 8) * (Hp // 8) * (Wp // 8)
-            if shape_ids is None:
-                _maybe_sp_average(torch.zeros(Nz, 25 * D, device=q.device))
-            x = (q4 + k4 + v4) * 0.0
-        x = all_to_all_4D(x, group, scatter_dim=1, gather_dim=2, full_seq_len=full_seq_len)
-        if padded != num_heads:
-            x = x[:, :, :num_heads]
-        x = x.flatten(2)
-    else:
-        x, used = run_bsa_dynamic(q4, k4, v4, grid_size, **kw)
-        x = x.flatten(2)
+            _maybe_sp_average(torch.zeros(Nz, 25 * D, device=q.device))
+
+    x, used = _sp_self_attention(q, k, v, num_heads, full_seq_len,
+                                 lambda a, b_, c: run_bsa_dynamic(a, b_, c, grid_size, **kw), idle)
+    used = shape_ids if used is None else used
     if return_shape_ids:
         return x, used
     return x
 
 
-__all__ = ["dynamic_self_attention", "audio_token_norms"]
+def uniform_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           grid_size: Tuple[int, int, int], num_heads: int, *,
+                           full_seq_len: Optional[int] = None,
+                           sparsity: Optional[float] = 0.875,
+                           cdf_threshold: Optional[float] = None,
+                           chunk_3d_shape_q=(4, 4, 4), chunk_3d_shape_k=(4, 4, 4)):
+    """The same SP branch for the uniform fixed-shape path (the plain-BSA
+    dispatch of wan_video_dit.py:470-560): q, k, v [B=1, S_local, num_heads*D]
+    -> x [B, S_local, num_heads*D].  No collective besides the all-to-alls."""
+    kw = dict(sparsity=sparsity, cdf_threshold=cdf_threshold, chunk_3d_shape_q=chunk_3d_shape_q,
+              chunk_3d_shape_k=chunk_3d_shape_k, layout="bshd")
+    x, _ = _sp_self_attention(q, k, v, num_heads, full_seq_len,
+                              lambda a, b_, c: (run_bsa_uniform(a, b_, c, grid_size, **kw), None))
+    return x
+
+
+__all__ = ["dynamic_self_attention", "uniform_self_attention", "audio_token_norms"]

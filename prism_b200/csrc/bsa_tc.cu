@@ -2,27 +2,30 @@
 // (tcgen05.mma, accumulators in TMEM, operands staged by TMA in 128B-swizzled
 // shared memory).
 //
-// Work decomposition.  Tokens are in tile order (64-token tiles, zone by
-// zone).  A CTA owns 128 rows = the tile pair (2p, 2p+1) of one head and walks
-// the union of the two tiles' selection bitmap rows in increasing tile order;
-// rows of the half that did not select a tile get p = 0 for it, so the result
-// is exactly the per-tile sparse attention of the reference.
+// Work decomposition.  Tokens are in tile order (64-token tiles).  Selections
+// are bitmaps: bits_q[h][q tile] marks the key tiles a query tile attends,
+// bits_k is its transpose.
 //
-//   forward   CTA = 128 queries; per step two selected key tiles (N = 128):
-//             S = Q K^T -> TMEM, online softmax in registers (one thread per
-//             query row), P (bf16) -> smem, O += P V in TMEM.
-//   dK / dV   CTA = 128 keys; per step one query tile (N = 64) of the
-//             transposed selection: S^T = K Q^T, dP^T = V dO^T -> TMEM,
-//             P^T and dS^T = P^T (dP^T - delta) -> smem, dV += P^T dO,
-//             dK += dS^T Q in TMEM.
-//   dQ        CTA = 128 queries; per step one key tile: S = Q K^T,
-//             dP = dO V^T -> TMEM, dS -> smem, dQ += dS K in TMEM.
+//   forward   CTA = 256 queries (tiles 4p..4p+3) as two groups of 128 rows;
+//             per step a pair of key tiles (N = 128) computed by one or both
+//             groups (FwdSched): S = Q K^T -> TMEM, online softmax in
+//             registers (one thread per query row), P (bf16) written over S in
+//             TMEM, O += P V with P read from TMEM.
+//   dK / dV   CTA = 128 keys (tiles 2p, 2p+1); per step one query tile (N = 64)
+//             of the union of the two key tiles' transposed rows: S^T = K Q^T,
+//             dP^T = V dO^T -> TMEM, P^T and dS^T written over them in TMEM,
+//             dV += P^T dO, dK += dS^T Q.
+//   dQ        CTA = 128 queries (tiles 2p, 2p+1); per step a pair of key tiles
+//             of the union of the two rows: S, dP -> TMEM, dS -> TMEM,
+//             dQ += dS K.
+// Rows of a tile that did not select a key tile get p = 0 for it, so every
+// kernel computes exactly the per-tile sparse attention of the reference.
 //
-// Warp roles (192 threads): warps 0-3 = softmax / epilogue (thread i owns
-// TMEM lane i = row i of the CTA), warp 4 = TMA producer, warp 5 = MMA
-// issuer (one thread) and TMEM owner.  Producer, MMA issuer and softmax warps
-// all walk the same bitmap union, so they agree on the sequence of tiles
-// without exchanging it.
+// Warp roles (320 threads): warps 0-7 = softmax / epilogue (thread i of a
+// warpgroup owns TMEM lane i), warp 8 = TMA producer, warp 9 = MMA issuer
+// (one thread) and TMEM owner.  Producer, MMA issuer and softmax warps all
+// walk the same tile sequence from the bitmaps, so they agree on it without
+// exchanging it.
 //
 // Numerics follow the reference Triton kernels
 // (hymm/models/modules/block_sparse_attention/flash_attn_bsa_varlen_mask.py:
@@ -135,43 +138,164 @@ constexpr size_t kMinSmem = 116 * 1024;
 
 // ===================================================================== forward
 // CTA = 256 queries = tiles 4p..4p+3, as two groups of 128 rows (g = 0: tiles
-// 4p, 4p+1; g = 1: tiles 4p+2, 4p+3) that share one stream of key tiles (the
-// union of the four bitmap rows).  Each group has its own softmax warpgroup,
-// S double buffer and O accumulator in TMEM, so while one group's softmax
-// runs the tensor core works on the other group's products.
-struct UnionIter4 {
-  const uint32_t* r[4];
-  int wq, wi;
-  uint32_t w[4];
-  __device__ __forceinline__ void init(const uint32_t* r0, const uint32_t* r1, const uint32_t* r2,
-                                       const uint32_t* r3, int n) {
-    r[0] = r0;
-    r[1] = r1;
-    r[2] = r2;
-    r[3] = r3;
-    wq = n;
-    wi = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) w[i] = (n > 0 && r[i] != nullptr) ? __ldg(r[i]) : 0u;
+// 4p, 4p+1; g = 1: tiles 4p+2, 4p+3) that share one stream of key-tile pairs
+// (FwdSched below).  Each group has its own softmax warpgroup, S buffer and
+// O accumulator in TMEM, so while one group's softmax runs the tensor core
+// works on the other group's products.
+// The forward's steps.  The key tiles of the four-row union fall into three
+// classes: tiles some row of BOTH groups selected (A), tiles only group 0
+// selected (B), only group 1 (C).  At the start of the kernel all threads
+// write the three classes' tiles, each in increasing tile order, into one
+// shared-memory list (A, then B, then C: build_fwd_lists); each class is then
+// paired in list order, and step n is decoded from the three counts in O(1):
+//   1. couples: B pair i (mask 1: group 0 computes it), C pair i (mask 2),
+//      for i < k = min(pairs B, pairs C) -- the groups alternate on the
+//      tensor core as with two-group steps, and no product is spent on key
+//      tiles a group did not select;
+//   2. the class left over, X (B or C), interleaved with A pairs: A pair i
+//      (mask 3), X pair k + i (mask of X), for i < j = min(pairs A, pairs X - k);
+//   3. the remaining A pairs, then the remaining X pairs computed by both
+//      groups (mask 3; the other group's rows get p = 0), the unpaired A tile
+//      (mask 3) and the unpaired B / C tiles (one step, mask 3).
+// At the uniform path's 25 % density the four-row union is ~1.8x each group's
+// own union; this schedule computes ~1.04x the selected products (dynamic
+// path, 85 %: ~1.01x, as before).
+struct FwdSched {
+  const uint16_t* list;
+  int nA, nB, nC, pA, k, j, X, remX, total;
+  __device__ __forceinline__ void init(const uint16_t* l, const int* counts) {
+    list = l;
+    nA = counts[0], nB = counts[1], nC = counts[2];
+    pA = nA >> 1;
+    const int pB = nB >> 1, pC = nC >> 1;
+    k = min(pB, pC);
+    X = pB > k ? 1 : 2;
+    remX = max(pB, pC) - k;
+    j = min(pA, remX);
+    total = 2 * k + 2 * j + (pA - j) + (remX - j) + (nA & 1) + (((nB | nC) & 1) ? 1 : 0);
   }
-  // next tile index, or -1; bit i of sel: row i selected it
-  __device__ __forceinline__ int next(int& sel) {
-    while ((w[0] | w[1] | w[2] | w[3]) == 0u) {
-      if (++wi >= wq) return -1;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = r[i] != nullptr ? __ldg(r[i] + wi) : 0u;
+  // tiles of pair i of class c (0 = A, 1 = B, 2 = C)
+  __device__ __forceinline__ void pair(int c, int i, int& t0, int& t1) const {
+    const uint16_t* b = list + (c == 0 ? 0 : (c == 1 ? nA : nA + nB)) + 2 * i;
+    t0 = b[0];
+    t1 = b[1];
+  }
+  __device__ __forceinline__ void step(int n, int& t0, int& t1, int& mask) const {
+    if (n < 2 * k) {
+      pair((n & 1) ? 2 : 1, n >> 1, t0, t1);
+      mask = (n & 1) ? 2 : 1;
+      return;
     }
-    const int bit = __ffs(w[0] | w[1] | w[2] | w[3]) - 1;
-    const uint32_t m = 1u << bit;
-    sel = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      sel |= (w[i] & m) ? (1 << i) : 0;
-      w[i] &= ~m;
+    n -= 2 * k;
+    if (n < 2 * j) {
+      if (n & 1) {
+        pair(X, k + (n >> 1), t0, t1);
+        mask = X;
+      } else {
+        pair(0, n >> 1, t0, t1);
+        mask = 3;
+      }
+      return;
     }
-    return wi * 32 + bit;
+    n -= 2 * j;
+    mask = 3;
+    if (n < pA - j) {
+      pair(0, j + n, t0, t1);
+      return;
+    }
+    n -= pA - j;
+    if (n < remX - j) {
+      pair(X, k + j + n, t0, t1);
+      return;
+    }
+    n -= remX - j;
+    if (nA & 1) {
+      if (n == 0) {
+        t0 = list[nA - 1];
+        t1 = -1;
+        return;
+      }
+      --n;
+    }
+    const int sb = (nB & 1) ? (int)list[nA + nB - 1] : -1;
+    const int sc = (nC & 1) ? (int)list[nA + nB + nC - 1] : -1;
+    t0 = sb >= 0 ? sb : sc;
+    t1 = sb >= 0 ? sc : -1;
   }
 };
+
+// All threads of the CTA: the class lists of FwdSched from the four bitmap rows
+// (r2 = r3 = nullptr for a CTA with one group): A at [0, nA), B at [nA, nA + nB),
+// C after, each in increasing tile order, from a block-wide exclusive scan of
+// the per-word class counts.  Rows of up to blockDim.x words take one pass;
+// longer rows count first and write in a second pass.  When single-group tiles
+// are rare (8 (nB + nC) < nA, the dynamic path's dense selections) the whole
+// union is written as class A instead: both groups walk it in tile order.
+// counts[0..2] = nA, nB, nC.  The caller's __syncthreads publishes the lists.
+__device__ void build_fwd_lists(const uint32_t* r0, const uint32_t* r1, const uint32_t* r2,
+                                const uint32_t* r3, int wq, uint16_t* list, int* counts,
+                                int* scratch /* 3 * warps ints */) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const bool one_pass = wq <= (int)blockDim.x;
+  int totA = 0, totB = 0;
+  bool merged = false;
+  for (int pass = one_pass ? 1 : 0; pass < 2; ++pass) {
+    int baseA = 0, baseB = 0, baseC = 0;
+    for (int w0 = 0; w0 < wq; w0 += blockDim.x) {
+      const int w = w0 + tid;
+      uint32_t g0 = 0, g1 = 0;
+      if (w < wq) {
+        g0 = __ldg(r0 + w) | __ldg(r1 + w);
+        g1 = r2 != nullptr ? (__ldg(r2 + w) | __ldg(r3 + w)) : 0u;
+      }
+      uint32_t ca = g0 & g1, cb = g0 & ~g1, cc = g1 & ~g0;
+      int xa = __popc(ca), xb = __popc(cb), xc = __popc(cc);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {  // inclusive warp scans
+        const int ya = __shfl_up_sync(0xffffffffu, xa, o), yb = __shfl_up_sync(0xffffffffu, xb, o),
+                  yc = __shfl_up_sync(0xffffffffu, xc, o);
+        if (lane >= o) xa += ya, xb += yb, xc += yc;
+      }
+      if (lane == 31) scratch[3 * warp] = xa, scratch[3 * warp + 1] = xb, scratch[3 * warp + 2] = xc;
+      __syncthreads();
+      int ea = 0, eb = 0, ec = 0, ta = 0, tb = 0, tc = 0;
+      for (int i = 0; i < nw; ++i) {
+        const int sa = scratch[3 * i], sbb = scratch[3 * i + 1], scc = scratch[3 * i + 2];
+        if (i < warp) ea += sa, eb += sbb, ec += scc;
+        ta += sa, tb += sbb, tc += scc;
+      }
+      __syncthreads();
+      if (one_pass) {  // the totals of the only chunk are the class sizes
+        totA = ta, totB = tb;
+        merged = 8 * (tb + tc) < ta;
+      }
+      if (pass == 1) {
+        if (merged) {
+          // union in tile order: class-A offsets plus the B and C entries before this word
+          int o = baseA + baseB + baseC + ea + eb + ec + (xa - __popc(ca)) + (xb - __popc(cb)) +
+                  (xc - __popc(cc));
+          for (uint32_t m = g0 | g1; m; m &= m - 1u) list[o++] = (uint16_t)(w * 32 + __ffs(m) - 1);
+        } else {
+          int oa = baseA + ea + xa - __popc(ca);
+          int ob = totA + baseB + eb + xb - __popc(cb);
+          int oc = totA + totB + baseC + ec + xc - __popc(cc);
+          for (uint32_t m = ca; m; m &= m - 1u) list[oa++] = (uint16_t)(w * 32 + __ffs(m) - 1);
+          for (uint32_t m = cb; m; m &= m - 1u) list[ob++] = (uint16_t)(w * 32 + __ffs(m) - 1);
+          for (uint32_t m = cc; m; m &= m - 1u) list[oc++] = (uint16_t)(w * 32 + __ffs(m) - 1);
+        }
+      }
+      baseA += ta, baseB += tb, baseC += tc;
+    }
+    if (pass == 0) {
+      totA = baseA;
+      totB = baseB;
+      merged = 8 * (baseB + baseC) < baseA;  // identical in every thread
+    } else if (tid == 0) {
+      if (merged) counts[0] = baseA + baseB + baseC, counts[1] = 0, counts[2] = 0;
+      else counts[0] = baseA, counts[1] = baseB, counts[2] = baseC;
+    }
+  }
+}
 
 constexpr int kFwdThreads = 320;
 constexpr int kFwdProducerWarp = 8;
@@ -202,7 +326,11 @@ struct FwdLayout {
                        B_DRAIN = B_OF + 2, NBAR = B_DRAIN + 1;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int ABORT = TMEM_SLOT + 4;
-  static constexpr size_t kBytes = 1024 + ABORT + 4;
+  static constexpr int COUNTS = ABORT + 4;           // 3 ints: class sizes
+  static constexpr int SCRATCH = COUNTS + 16;        // 3 ints per warp (list build)
+  static constexpr int LIST = SCRATCH + 3 * 4 * (kFwdThreads / 32);  // u16 per union tile
+  // shared memory for n_tiles tiles (the class lists hold at most one entry per tile)
+  static constexpr size_t bytes(int64_t n_tiles) { return 1024 + LIST + 2 * (size_t)n_tiles; }
   // TMEM per group g at 256 g: S (128 f32 columns; P as 64 bf16x2 columns over
   // its first half), O (D f32 columns)
   static constexpr int T_S = 0, T_O = 128;
@@ -254,28 +382,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tmem_relinquish();
     tc_fence_before();
   }
+  __syncthreads();  // barrier initialisation visible: the Q load overlaps the list build
+  if (warp == kFwdProducerWarp && lane == 0) {
+    const int nq = g1_live ? 4 : 2;  // 64-row Q blocks
+    mbar_expect_tx(bar(L::B_Q), nq * 64 * D * 2);
+    for (int qb = 0; qb < nq; ++qb)
+#pragma unroll
+      for (int s = 0; s < L::kSub; ++s)
+        tma_load_2d(sb + L::Q + (qb >> 1) * L::kPair + s * 16384 + (qb & 1) * 8192, &tm_q, s * 64,
+                    row_base + qb * 64, bar(L::B_Q));
+  }
+  uint16_t* list = reinterpret_cast<uint16_t*>(sm + L::LIST);
+  build_fwd_lists(r0, r0 + wq, r2, r3, wq, list, reinterpret_cast<int*>(sm + L::COUNTS),
+                  reinterpret_cast<int*>(sm + L::SCRATCH));
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
+  FwdSched sched;
+  sched.init(list, reinterpret_cast<const int*>(sm + L::COUNTS));
 
   if (warp == kFwdProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const int nq = g1_live ? 4 : 2;  // 64-row Q blocks
-      mbar_expect_tx(bar(L::B_Q), nq * 64 * D * 2);
-      for (int qb = 0; qb < nq; ++qb)
-#pragma unroll
-        for (int s = 0; s < L::kSub; ++s)
-          tma_load_2d(sb + L::Q + (qb >> 1) * L::kPair + s * 16384 + (qb & 1) * 8192, &tm_q, s * 64,
-                      row_base + qb * 64, bar(L::B_Q));
-      UnionIter4 it;
-      it.init(r0, r0 + wq, r2, r3, wq);
-      int np = 0, sel = 0;
+      int np = 0, t0, t1, mask;
       bool ok = true;
-      for (;;) {
-        const int t0 = it.next(sel);
-        if (t0 < 0) break;
-        const int t1 = it.next(sel);
+      for (int step = 0; step < sched.total; ++step) {
+        sched.step(step, t0, t1, mask);
         const int cnt = t1 >= 0 ? 2 : 1;
         const int st = np % R;
         // K pair, then V pair, each into one 128-row slot (tile a rows 0-63, tile b 64-127)
@@ -303,7 +435,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tma_load_2d(sb + L::V + st * L::kPair + s * 16384 + u * 8192, &tm_v, s * 64,
                         head_row + (u ? t1 : t0) * 64, bar(L::B_VF + st));
         ++np;
-        if (t1 < 0) break;
       }
       // drain: every issued load has landed before the CTA may exit
       for (int m = (np > R ? np - R : 0); m < np; ++m) {
@@ -315,9 +446,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   } else if (warp == kFwdMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
-    // Per key pair n: PV_0(n-1), S_0(n), PV_1(n-1), S_1(n).  S_g(n) overwrites
-    // the columns that held P_g(n-1); it is issued after PV_g(n-1), and the
-    // tensor pipe performs one thread's MMAs in issue order.
+    // Per step n, for the groups in its mask: PV_g(prev), S_g(n); then PV_g of
+    // step n-1 for a group not in the mask.  S_g(n) overwrites the columns that
+    // held P_g of the group's previous step, whose P V was issued at the step
+    // after it (at the latest just before S_g(n)); the tensor pipe performs one
+    // thread's MMAs in issue order.  Barrier parities count each group's steps.
     if (lane == 0) {
       constexpr uint32_t IDESC_S2 = idesc_bf16(128, 128, false, false);
       constexpr uint32_t IDESC_S1 = idesc_bf16(128, 64, false, false);
@@ -327,24 +460,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                      dV = desc_mn_sw128(sb + L::V, 16384);
       bool ok = mbar_wait(bar(L::B_Q), 0, abort_flag, &g_tc_error, kErrFwdMma);
       tc_fence_after();
-      UnionIter4 it;
-      it.init(r0, r0 + wq, r2, r3, wq);
-      // P V of pair j for group g: K = 64 keys per tile of the pair
-      auto pv = [&](int g, int j, int cnt) -> bool {
+      // P V of group g's step j: K = 64 keys per tile of the pair, V in ring slot `slot`
+      auto pv = [&](int g, int j, int cnt, int slot) -> bool {
         if (!mbar_wait(bar(L::B_PF + g), j & 1, abort_flag, &g_tc_error, kErrFwdMma)) return false;
         tc_fence_after();
-        const uint64_t bv = dV + (j % R) * (L::kPair >> 4);
+        const uint64_t bv = dV + slot * (L::kPair >> 4);
         mma_ts_k64_mn(tmem + g * 256 + L::T_O, tmem + g * 256 + L::T_S, bv, IDESC_PV, j > 0 ? 1u : 0u);
         if (cnt == 2)
           mma_ts_k64_mn(tmem + g * 256 + L::T_O, tmem + g * 256 + L::T_S + 32, bv + (8192 >> 4),
                         IDESC_PV, 1u);
         return true;
       };
-      int n = 0, sel = 0, prev_cnt = 0;
-      while (ok) {
-        const int t0 = it.next(sel);
-        if (t0 < 0) break;
-        const int t1 = it.next(sel);
+      int n = 0, prev_cnt = 0, prev_mask = 0, t0, t1, mask;
+      int ns[2] = {0, 0};  // steps issued per group
+      for (int step = 0; ok && step < sched.total; ++step) {
+        sched.step(step, t0, t1, mask);
+        if (!g1_live) mask &= 1;  // a CTA with one group: fallback steps are group 0's
         const int cnt = t1 >= 0 ? 2 : 1;
         const int st = n % R;
         if (!mbar_wait(bar(L::B_KF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrFwdMma) ||
@@ -353,29 +484,49 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           ok = false;
           break;
         }
-        for (int g = 0; g < ng; ++g) {
-          if (n > 0 && !pv(g, n - 1, prev_cnt)) {
+        // groups of this step: P V of their previous step (its P occupies the
+        // columns S is written to), then S; then P V for groups that sit this
+        // step out, after the S products they need not wait for
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          if (!((mask >> g) & 1)) continue;
+          if (((prev_mask >> g) & 1) && !pv(g, ns[g] - 1, prev_cnt, (n - 1) % R)) {
             ok = false;
             break;
           }
           mma_kd<L::kSub, 16384, 16384>(tmem + g * 256 + L::T_S, dQ + g * (L::kPair >> 4),
-                                        dK + st * (L::kPair >> 4), cnt == 2 ? IDESC_S2 : IDESC_S1, 0u);
+                                        dK + st * (L::kPair >> 4),
+                                        cnt == 2 ? IDESC_S2 : IDESC_S1, 0u);
           mma_commit(bar(L::B_SF + g));
+          ++ns[g];
         }
+        if (!ok) break;
+#pragma unroll
+        for (int g = 0; g < 2; ++g)
+          if (((prev_mask >> g) & 1) && !((mask >> g) & 1) &&
+              !pv(g, ns[g] - 1, prev_cnt, (n - 1) % R)) {
+            ok = false;
+            break;
+          }
         if (!ok) break;
         mma_commit(bar(L::B_KE + st));
         if (n > 0) mma_commit(bar(L::B_VE + (n - 1) % R));
         prev_cnt = cnt;
+        prev_mask = mask;
         ++n;
-        if (t1 < 0) break;
       }
       if (ok && n > 0) {
         if (mbar_wait(bar(L::B_VF + (n - 1) % R), ((n - 1) / R) & 1, abort_flag, &g_tc_error,
                       kErrFwdMma)) {
-          for (int g = 0; g < ng; ++g) {
-            if (!pv(g, n - 1, prev_cnt)) break;
-            mma_commit(bar(L::B_OF + g));
-          }
+#pragma unroll
+          for (int g = 0; g < 2; ++g)
+            if (((prev_mask >> g) & 1) && !pv(g, ns[g] - 1, prev_cnt, (n - 1) % R)) {
+              ok = false;
+              break;
+            }
+          if (ok)
+            for (int g = 0; g < ng; ++g)
+              if (ns[g] > 0) mma_commit(bar(L::B_OF + g));
         }
       }
       // drain: all issued MMAs complete before TMEM is released
@@ -389,16 +540,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int sbit = 2 * g + (r >> 6);     // bitmap row of this thread's q tile
     const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + g * 256;
     float m = -INFINITY, l = 1.0f;
-    UnionIter4 it;
-    it.init(r0, r0 + wq, r2, r3, wq);
-    int n = 0, sel0 = 0, sel1 = 0;
+    const uint32_t* my_row = r0 + sbit * wq;  // this thread's q tile's bitmap row
+    int n = 0, t0, t1, mask;                   // n: this group's steps
     bool ok = true;
-    for (;;) {
-      const int t0 = it.next(sel0);
-      if (t0 < 0) break;
-      const int t1 = it.next(sel1);
-      const uint64_t vb0 = ((sel0 >> sbit) & 1) ? tile_bits[t0] : 0ull;
-      const uint64_t vb1 = (t1 >= 0 && ((sel1 >> sbit) & 1)) ? tile_bits[t1] : 0ull;
+    for (int step = 0; step < sched.total; ++step) {
+      sched.step(step, t0, t1, mask);
+      if (!((mask >> g) & 1)) continue;
+      const uint64_t vb0 = ((__ldg(my_row + (t0 >> 5)) >> (t0 & 31)) & 1u) ? tile_bits[t0] : 0ull;
+      const uint64_t vb1 =
+          (t1 >= 0 && ((__ldg(my_row + (t1 >> 5)) >> (t1 & 31)) & 1u)) ? tile_bits[t1] : 0ull;
       if (!warp_wait(bar(L::B_SF + g), n & 1, abort_flag, kErrFwdSoftmax)) {
         ok = false;
         break;
@@ -486,7 +636,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(L::B_PF + g));
       ++n;
-      if (t1 < 0) break;
     }
     // epilogue
     const int64_t grow = (int64_t)row_base + g * 128 + r;
@@ -1188,8 +1337,11 @@ prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads
                           void* o_lo, float* lse, cudaStream_t stream) {
   const int64_t n_tiles = S / 64;
   const int wq = (int)((n_tiles + 31) / 32);
-  const size_t sm = FwdLayout<D>::kBytes > kMinSmem ? FwdLayout<D>::kBytes : kMinSmem;
-  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_fwd: shared memory layout exceeds 227 KB");
+  const size_t need = FwdLayout<D>::bytes(n_tiles);
+  const size_t sm = need > kMinSmem ? need : kMinSmem;
+  PRISM_CHECK_ARG(n_tiles <= 65536 && sm <= 227 * 1024,
+                  "prism_bsa_fwd: %lld tiles per head exceed the shared-memory tile lists",
+                  (long long)n_tiles);
   CUtensorMap mq, mk, mv;
   const int64_t rows = (int64_t)heads * S;
   PRISM_TRY(make_map(&mq, q, rows, D, "prism_bsa_fwd"));

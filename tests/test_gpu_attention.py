@@ -118,6 +118,30 @@ def test_sparse_kernels_multiword_rows(D, cuda):
     assert _lib.load().prism_device_status() == 0, "a bounded wait inside a kernel gave up"
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("density", [0.08, 0.5])
+def test_sparse_kernels_odd_tile_pairs(D, density, cuda):
+    """S % 256 == 128: the last forward CTA holds a single group of 128 rows;
+    low densities make most key tiles selected by one group only."""
+    pr = _random_problem(2, 18, D, density, seed=7 * D + int(density * 100), dev=cuda,
+                         masked_tiles=[(17, 20), (3, 0)], empty_rows=[16])
+    d = pr["dev"]
+    sm = 1.0 / math.sqrt(D)
+    o, lse, o_lo = ops.bsa_fwd(d["q"], d["k"], d["v"], d["bq"], d["tb"], sm, want_lo=True)
+    f = lambda t: t.float().numpy()
+    ro, rlse = O.bsa_forward(f(pr["q"]), f(pr["k"]), f(pr["v"]), pr["bq"], pr["valid"], sm)
+    _close(o.float().cpu(), ro, "O")
+    dq, dk, dv = ops.bsa_bwd(d["q"], d["k"], d["v"], o, d["do"], lse, d["bq"], d["bk"], d["tb"], sm,
+                             o_lo=o_lo)
+    rdq, rdk, rdv = O.bsa_backward(f(pr["q"]), f(pr["k"]), f(pr["v"]), ro, f(pr["do"]), pr["bq"],
+                                   pr["valid"], sm)
+    _close(dq.float().cpu(), rdq, "dQ")
+    _close(dk.float().cpu(), rdk, "dK")
+    _close(dv.float().cpu(), rdv, "dV")
+    assert (o[:, 16 * 64:17 * 64] == 0).all()
+    assert _lib.load().prism_device_status() == 0, "a bounded wait inside a kernel gave up"
+
+
 @pytest.mark.parametrize("name", [n for n, c in CASES.items() if c.needs_pad])
 def test_dynamic_path_vs_reference_golden(name, cuda):
     """flash_attn_bsa_3d_dynamic (reference signature, padded THW input) against
