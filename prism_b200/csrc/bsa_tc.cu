@@ -103,6 +103,13 @@ struct UnionIter {
   }
 };
 
+// Number of tiles in the union of two bitmap rows (the steps a backward CTA takes).
+__device__ __forceinline__ int union_count(const uint32_t* ra, const uint32_t* rb, int wq) {
+  int c = 0;
+  for (int w = 0; w < wq; ++w) c += __popc(__ldg(ra + w) | __ldg(rb + w));
+  return c;
+}
+
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
 }
@@ -706,7 +713,7 @@ struct DkdvLayout {
   static constexpr int DL = M + kRing * 256;               // kRing x 64 f32 (delta)
   static constexpr int BAR = DL + kRing * 256;
   static constexpr int B_KV = 0, B_QF = 1, B_QE = 1 + kRing, B_SF = 1 + 2 * kRing,  // [b]
-                       B_DPF = B_SF + 2, B_PF = B_DPF + 2, B_DSF = B_PF + 2,        // [b]
+                       B_DPF = B_SF + 2, B_DSF = B_DPF + 2,                         // [b]
                        B_FIN = B_DSF + 2, B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int ABORT = TMEM_SLOT + 4;
@@ -749,7 +756,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(L::B_SF + i), 1);
       mbar_init(bar(L::B_DPF + i), 1);
-      mbar_init(bar(L::B_PF + i), 8);
       mbar_init(bar(L::B_DSF + i), 8);
     }
     mbar_init(bar(L::B_FIN), 1);
@@ -804,52 +810,50 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // Issue order: S^T(0) dP^T(0) | S^T(1) dP^T(1) dV(0) dK(0) | S^T(2) ...
     // S^T(n+2) / dP^T(n+2) overwrite the P^T / dS^T of step n; they are issued
     // after dV(n) / dK(n), and one thread's MMAs are performed in order.
+    // The issuing thread keeps its loop minimal -- the tensor pipe's issue queue
+    // is shallow, so every instruction between MMAs is time the pipe may idle:
+    // it needs no tile indices (only the step count and ring slots), and waits
+    // once per step for P^T and dS^T together (B_DSF).
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
+      static_assert(R == 4, "ring arithmetic below assumes 4 slots");
       const uint64_t dK = desc_k_sw128(sb + L::K), dV = desc_k_sw128(sb + L::V),
                      dQk = desc_k_sw128(sb + L::Q), dDOk = desc_k_sw128(sb + L::DO),
                      dQmn = desc_mn_sw128(sb + L::Q, 8192), dDOmn = desc_mn_sw128(sb + L::DO, 8192);
+      constexpr uint32_t kSlot = L::kSub * 8192 >> 4;  // descriptor step of one ring slot
+      const int steps = union_count(row_a, row_b, wq);
       bool ok = mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
       tc_fence_after();
-      UnionIter it;
-      it.init(row_a, row_b, wq);
-      auto grads = [&](int j) -> bool {
-        const int b = j & 1, st = j % R;
-        if (!mbar_wait(bar(L::B_PF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
-        tc_fence_after();
-        mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S + b * 64,
-                                                dDOmn + st * (L::kSub * 8192 >> 4), IDESC_G,
-                                                j > 0 ? 1u : 0u);
-        if (!mbar_wait(bar(L::B_DSF + b), (j >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
-        tc_fence_after();
-        mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP + b * 64,
-                                                dQmn + st * (L::kSub * 8192 >> 4), IDESC_G,
-                                                j > 0 ? 1u : 0u);
-        mma_commit(bar(L::B_QE + st));
-        return true;
-      };
-      int n = 0, sel = 0, t;
-      while (ok && (t = it.next(sel)) >= 0) {
-        const int st = n % R, b = n & 1;
-        if (!mbar_wait(bar(L::B_QF + st), (n / R) & 1, abort_flag, &g_tc_error, kErrDkdvMma)) {
-          ok = false;
-          break;
+      for (int n = 0; ok && n <= steps; ++n) {
+        if (n < steps) {
+          const uint32_t st = (uint32_t)n & 3u, b = (uint32_t)n & 1u;
+          if (!mbar_wait(bar(L::B_QF + st), ((uint32_t)n >> 2) & 1u, abort_flag, &g_tc_error,
+                         kErrDkdvMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + b * 64, dK, dQk + st * kSlot, IDESC_S, 0u);
+          mma_commit(bar(L::B_SF + b));
+          mma_kd<L::kSub, 16384, 8192>(tmem + L::T_DP + b * 64, dV, dDOk + st * kSlot, IDESC_S, 0u);
+          mma_commit(bar(L::B_DPF + b));
         }
-        tc_fence_after();
-        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + b * 64, dK, dQk + st * (L::kSub * 8192 >> 4),
-                                     IDESC_S, 0u);
-        mma_commit(bar(L::B_SF + b));
-        mma_kd<L::kSub, 16384, 8192>(tmem + L::T_DP + b * 64, dV, dDOk + st * (L::kSub * 8192 >> 4),
-                                     IDESC_S, 0u);
-        mma_commit(bar(L::B_DPF + b));
-        if (n >= 1 && !grads(n - 1)) {
-          ok = false;
-          break;
+        if (n >= 1) {
+          // dV(j) += P^T(j) dO(j), dK(j) += dS^T(j) Q(j) for the previous step j
+          const uint32_t j = (uint32_t)n - 1u, jb = j & 1u, js = j & 3u;
+          if (!mbar_wait(bar(L::B_DSF + jb), (j >> 1) & 1u, abort_flag, &g_tc_error, kErrDkdvMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S + jb * 64,
+                                                  dDOmn + js * kSlot, IDESC_G, j > 0 ? 1u : 0u);
+          mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP + jb * 64,
+                                                  dQmn + js * kSlot, IDESC_G, j > 0 ? 1u : 0u);
+          mma_commit(bar(L::B_QE + js));
         }
-        ++n;
       }
-      if (ok && n >= 1) grads(n - 1);
       mma_commit(bar(L::B_FIN));
       mma_commit(bar(L::B_DRAIN));
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
@@ -903,11 +907,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = 0u;
       }
+      // P^T is published together with dS^T (the MMA issuer waits once, on B_DSF)
       tmem_st16(t_lane + L::T_S + b * 64 + wg * 32, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_PF + b));
       if (!warp_wait(bar(L::B_DPF + b), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax)) {
         ok = false;
         break;
