@@ -279,7 +279,7 @@ def cpu_baseline(seconds=15.0, threads=None):
     if CONFIG.get("path") == "uniform":
         # selection (C oracle, one head) over the uniform chunk order
         c = int(math.prod(CONFIG["chunk"]))
-        bq, bk, _ = O.block_select_uniform(qb, kb, S, c, c, None, CONFIG["sparsity"],
+        bq, bk, _ = O.block_select_uniform(qb, kb, S, S, c, c, None, None, CONFIG["sparsity"],
                                            CONFIG["cdf_threshold"])
     else:
         # selection (C oracle, one head) -- all 64-token shape-0 layout of the bench grid

@@ -165,23 +165,25 @@ prism_status_t prism_uniform_layout(int Tp, int Hp, int Wp, int ct, int ch, int 
  * (bsa_interface.py:600-633: masked_mean_pooling_compression /
  * mean_pooling_compression :164-201, cal_score :203-207,
  * get_select_indices_{topk,cdf,cdf_topk}_from_score :235-304), expanded to
- * 64-token tile bitmaps.  q_re is in the q chunk order, k_re in the key chunk
- * order, both [heads, S, D] bf16 with S a multiple of 64; the first `seq` rows
- * are real (seq a multiple of chunk_q and chunk_k, both multiples of 64).
- * tile_bits [S/64]: key validity in the key order; the q pooling uses the same
- * mask at the same positions, as the reference does
- * (masked_mean_pooling_compression(q, chunk_size_q, kv_valid_mask), :609-610).
- * Pooling is fp32 (sequential sums / max(count, 1)); no key chunk is excluded
- * from the top-k (the uniform path has no block-validity mask); selected
- * tiles without a valid key are dropped (they contribute nothing).  Bitmap
- * rows of padding tiles are zero.  mode as for prism_block_select.
- * workspace: prism_block_select_uniform_workspace_bytes(heads, seq/chunk_q,
- * seq/chunk_k, D). */
+ * 64-token tile bitmaps.  q_re [heads, Sq, D] is in the q chunk order, k_re
+ * [heads, Sk, D] in the key chunk order (bf16, Sq and Sk multiples of 64); the
+ * first seq_q / seq_k rows are real (multiples of chunk_q / chunk_k, which are
+ * multiples of 64).  k_bits [Sk/64]: key validity (64 rows per word); q_bits
+ * [Sq/64] or NULL: the rows the q pooling counts (the reference pools q under
+ * q_valid_mask if given, else under the key mask when Sq == Sk, else all rows,
+ * :606-611; NULL = all rows).  Pooling is fp32 (sequential sums /
+ * max(count, 1)); no key chunk is excluded from the ranking; selected tiles
+ * without a valid key are dropped (they contribute nothing).
+ * bits_q [heads, Sq/64, ceil(Sk/2048)] (rows of padding tiles are zero) and
+ * its transpose bits_k [heads, Sk/64, ceil(Sq/2048)].  mode as for
+ * prism_block_select.  workspace: prism_block_select_uniform_workspace_bytes(
+ * heads, seq_q/chunk_q, seq_k/chunk_k, D). */
 size_t prism_block_select_uniform_workspace_bytes(int heads, int64_t n_chunks_q, int64_t n_chunks_k,
                                                   int D);
-prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t S,
-                                          int D, int64_t seq, int chunk_q, int chunk_k,
-                                          const uint64_t* tile_bits, int mode, double sparsity,
+prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t Sq,
+                                          int64_t Sk, int D, int64_t seq_q, int64_t seq_k,
+                                          int chunk_q, int chunk_k, const uint64_t* q_bits,
+                                          const uint64_t* k_bits, int mode, double sparsity,
                                           double cdf_threshold, void* workspace, uint32_t* bits_q,
                                           uint32_t* bits_k, cudaStream_t stream);
 
@@ -208,6 +210,24 @@ prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const 
                              float sm_scale, const uint32_t* bits_q, const uint32_t* bits_k,
                              const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
                              void* dv, cudaStream_t stream);
+
+/* Attention with different query and key lengths (cross-modal BSA,
+ * flash_attn_bsa_cross, bsa_interface.py:1276-1392, and flash_attn_bsa_3d
+ * with latent_shape_q != latent_shape_k): q, o, dO, dq [heads, Sq, D];
+ * k, v, dk, dv [heads, Sk, D]; lse [heads, Sq]; bits_q [heads, Sq/64,
+ * ceil(Sk/2048)], bits_k [heads, Sk/64, ceil(Sq/2048)], tile_bits [Sk/64];
+ * workspace prism_bsa_bwd_workspace_bytes(heads, Sq).  Sq and Sk are positive
+ * multiples of 128.  prism_bsa_fwd / prism_bsa_bwd are these with Sq == Sk. */
+prism_status_t prism_bsa_fwd_qk(const void* q, const void* k, const void* v, int heads, int64_t Sq,
+                                int64_t Sk, int D, float sm_scale, const uint32_t* bits_q,
+                                const uint64_t* tile_bits, void* o, void* o_lo, float* lse,
+                                cudaStream_t stream);
+prism_status_t prism_bsa_bwd_qk(const void* q, const void* k, const void* v, const void* o,
+                                const void* o_lo, const void* dout, const float* lse, int heads,
+                                int64_t Sq, int64_t Sk, int D, float sm_scale,
+                                const uint32_t* bits_q, const uint32_t* bits_k,
+                                const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
+                                void* dv, cudaStream_t stream);
 
 /* The three stages of prism_bsa_bwd, callable one by one:
  * delta[h][s] = sum_d O * dO (_attn_bwd_preprocess, common.py:94-111);

@@ -61,8 +61,8 @@ def lib():
         L.oracle_layout.argtypes = [P, i32, i32, i32, P, P, P, P]
         L.oracle_layout.restype = i64
         L.oracle_block_select.argtypes = [P, P, i32, i64, i32, P, i64, P, i32, f64, f64, P, P, P]
-        L.oracle_block_select_uniform.argtypes = [P, P, i32, i64, i32, i64, i32, i32, P, i32, f64,
-                                                  f64, P, P, P]
+        L.oracle_block_select_uniform.argtypes = [P, P, i32, i64, i64, i32, i64, i64, i32, i32, P,
+                                                  P, i32, f64, f64, P, P, P]
         _lib = L
     return _lib
 
@@ -186,25 +186,27 @@ def uniform_layout(grid_padded, chunk, n_rows=None):
     return src, inv
 
 
-def block_select_uniform(q_re_bits, k_re_bits, seq, chunk_q, chunk_k, valid_re, sparsity,
-                         cdf_threshold, want_chunks=False):
-    """Uniform-path selection (oracle_block_select_uniform).  q_re_bits in the q
-    chunk order, k_re_bits in the key chunk order, [h, S, D] bf16 bits; valid_re
-    [S] key validity in the key order (None = all real rows valid).
-    Returns (bits_q, bits_k, sel_chunks [h, nq, nk] or None)."""
+def block_select_uniform(q_re_bits, k_re_bits, seq_q, seq_k, chunk_q, chunk_k, q_valid, k_valid,
+                         sparsity, cdf_threshold, want_chunks=False):
+    """Uniform-path selection (oracle_block_select_uniform).  q_re_bits [h, Sq, D]
+    in the q chunk order, k_re_bits [h, Sk, D] in the key chunk order (bf16 bits);
+    q_valid [Sq] / k_valid [Sk]: rows the q / k pooling counts and key validity
+    (None = every row).  Returns (bits_q [h, Sq/64, ceil(Sk/2048)], bits_k
+    [h, Sk/64, ceil(Sq/2048)], sel_chunks [h, nq, nk] or None)."""
     q_re_bits = np.ascontiguousarray(q_re_bits, np.uint16)
     k_re_bits = np.ascontiguousarray(k_re_bits, np.uint16)
-    heads, S, D = q_re_bits.shape
-    n_tiles = S // 64
-    wq = (n_tiles + 31) // 32
-    bits_q = np.zeros((heads, n_tiles, wq), np.uint32)
-    bits_k = np.zeros((heads, n_tiles, wq), np.uint32)
-    sel = (np.zeros((heads, seq // chunk_q, seq // chunk_k), np.uint8) if want_chunks else None)
-    valid_re = None if valid_re is None else np.ascontiguousarray(valid_re, np.uint8)
+    heads, Sq, D = q_re_bits.shape
+    Sk = k_re_bits.shape[1]
+    nqt, nkt = Sq // 64, Sk // 64
+    bits_q = np.zeros((heads, nqt, (nkt + 31) // 32), np.uint32)
+    bits_k = np.zeros((heads, nkt, (nqt + 31) // 32), np.uint32)
+    sel = (np.zeros((heads, seq_q // chunk_q, seq_k // chunk_k), np.uint8) if want_chunks else None)
+    q_valid = None if q_valid is None else np.ascontiguousarray(q_valid, np.uint8)
+    k_valid = None if k_valid is None else np.ascontiguousarray(k_valid, np.uint8)
     mode = selection_mode(sparsity, cdf_threshold)
     lib().oracle_block_select_uniform(
-        _p(q_re_bits), _p(k_re_bits), heads, S, D, seq, chunk_q, chunk_k, _p(valid_re), mode,
-        float(sparsity if sparsity is not None else 0.0),
+        _p(q_re_bits), _p(k_re_bits), heads, Sq, Sk, D, seq_q, seq_k, chunk_q, chunk_k,
+        _p(q_valid), _p(k_valid), mode, float(sparsity if sparsity is not None else 0.0),
         float(cdf_threshold if cdf_threshold is not None else 0.0), _p(bits_q), _p(bits_k),
         _p(sel))
     return bits_q, bits_k, sel
@@ -239,10 +241,10 @@ def tile_lists_to_dense(tile_block_indices, lens, n_tiles):
 
 
 # ------------------------------------------------------------ attention side
-def token_mask(bits_q: np.ndarray, valid_re, S: int) -> np.ndarray:
-    """[h, S, S] bool: query token i may attend key token j."""
-    n_tiles = S // 64
-    dense = bits_to_dense(bits_q, n_tiles)  # [h, Nt, Nt]
+def token_mask(bits_q: np.ndarray, valid_re, S: int, Sk: int = None) -> np.ndarray:
+    """[h, S, Sk] bool: query token i may attend key token j (Sk defaults to S)."""
+    Sk = S if Sk is None else Sk
+    dense = bits_to_dense(bits_q, Sk // 64)[:, :S // 64]  # [h, Nq, Nk]
     m = np.repeat(np.repeat(dense, 64, axis=1), 64, axis=2)
     if valid_re is not None:
         m = m & np.asarray(valid_re, bool)[None, None, :]
@@ -250,7 +252,7 @@ def token_mask(bits_q: np.ndarray, valid_re, S: int) -> np.ndarray:
 
 
 def bsa_forward(q, k, v, bits_q, valid_re, sm_scale=None):
-    """Float64 restatement of the sparse forward.  q,k,v [h, S, D] float.
+    """Float64 restatement of the sparse forward.  q [h, S, D], k, v [h, Sk, D] float.
 
     Returns (o [h,S,D], lse [h,S]) with lse natural-log (bsa_interface.py:382-383);
     rows with no selected valid key give o = 0 and lse = -inf, as the
@@ -261,7 +263,7 @@ def bsa_forward(q, k, v, bits_q, valid_re, sm_scale=None):
     h, S, D = q.shape
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    m = token_mask(bits_q, valid_re, S)
+    m = token_mask(bits_q, valid_re, S, k.shape[1])
     s = np.matmul(q, k.transpose(0, 2, 1)) * sm_scale
     s = np.where(m, s, -np.inf)
     mx = s.max(-1, keepdims=True)
@@ -287,7 +289,7 @@ def bsa_backward(q, k, v, o, do, bits_q, valid_re, sm_scale=None):
     h, S, D = q.shape
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    m = token_mask(bits_q, valid_re, S)
+    m = token_mask(bits_q, valid_re, S, k.shape[1])
     s = np.matmul(q, k.transpose(0, 2, 1)) * sm_scale
     s = np.where(m, s, -np.inf)
     mx = s.max(-1, keepdims=True)

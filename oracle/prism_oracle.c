@@ -660,23 +660,27 @@ void oracle_block_select(const uint16_t* q_re, const uint16_t* k_re, int heads, 
 }
 
 /* Uniform fixed-shape path (_attention_bsa.forward, bsa_interface.py:600-633)
- * on chunk-ordered q_re / k_re [heads, S, D] bf16 whose first `seq` rows are
- * real.  Pooling (masked_mean_pooling_compression / mean_pooling_compression,
- * :164-201): chunk mean = sequential fp32 sum over the chunk's valid rows /
- * max(count, 1), with the KEY-order mask valid_re [S] applied to q as well
- * (:609-610; NULL = every real row valid).  Scores: fmaf chain over d
- * (cal_score, :203-207).  No chunk is excluded from the ranking.  Selected key
- * chunk b covers tiles [b*tk, b*tk + tk) (tk = chunk_k / 64), tiles without a
- * valid key are dropped; q chunk a's row goes to tiles [a*tq, a*tq + tq).
+ * on chunk-ordered q_re [heads, Sq, D] / k_re [heads, Sk, D] bf16 whose first
+ * seq_q / seq_k rows are real.  Pooling (masked_mean_pooling_compression /
+ * mean_pooling_compression, :164-201): chunk mean = sequential fp32 sum over
+ * the chunk's valid rows / max(count, 1); q counts the rows with q_valid set
+ * (the caller passes the key mask for q and k of one sequence, :609-610, q's
+ * own mask for cross attention, or NULL = every row), k the rows with k_valid
+ * set (NULL = every real row).  Scores: fmaf chain over d (cal_score,
+ * :203-207).  No chunk is excluded from the ranking.  Selected key chunk b
+ * covers key tiles [b*tk, b*tk + tk) (tk = chunk_k / 64), tiles without a
+ * valid key are dropped; q chunk a's row goes to q tiles [a*tq, a*tq + tq).
+ * bits_q [heads, Sq/64, ceil(Sk/2048)], bits_k [heads, Sk/64, ceil(Sq/2048)];
  * sel_chunks [heads, nq, nk] u8 receives the chunk-level selection if non-NULL.
  * Callers zero bits_q / bits_k. */
-void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int heads, int64_t S,
-                                 int D, int64_t seq, int chunk_q, int chunk_k,
-                                 const uint8_t* valid_re, int mode, double sparsity, double cdf,
-                                 uint32_t* bits_q, uint32_t* bits_k, uint8_t* sel_chunks) {
-  const int64_t N_tiles = S / 64;
-  const int64_t WQ = (N_tiles + 31) / 32;
-  const int64_t nq = seq / chunk_q, nk = seq / chunk_k;
+void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int heads, int64_t Sq,
+                                 int64_t Sk, int D, int64_t seq_q, int64_t seq_k, int chunk_q,
+                                 int chunk_k, const uint8_t* q_valid, const uint8_t* k_valid,
+                                 int mode, double sparsity, double cdf, uint32_t* bits_q,
+                                 uint32_t* bits_k, uint8_t* sel_chunks) {
+  const int64_t NQ_tiles = Sq / 64, NK_tiles = Sk / 64;
+  const int64_t WK = (NK_tiles + 31) / 32, WQ = (NQ_tiles + 31) / 32;
+  const int64_t nq = seq_q / chunk_q, nk = seq_k / chunk_k;
   const int tq = chunk_q / 64, tk = chunk_k / 64;
   const float scale = (float)(1.0 / sqrt((double)D));
   const float pf = (float)cdf;
@@ -684,12 +688,12 @@ void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int
   float* kc = (float*)malloc(sizeof(float) * nk * D);
   float* score = (float*)malloc(sizeof(float) * nk);
   wi_t* arr = (wi_t*)malloc(sizeof(wi_t) * nk);
-  int* tile_cnt = (int*)malloc(sizeof(int) * N_tiles);
-  for (int64_t j = 0; j < N_tiles; ++j) {
+  int* tile_cnt = (int*)malloc(sizeof(int) * NK_tiles);
+  for (int64_t j = 0; j < NK_tiles; ++j) {
     int c = 0;
     for (int i = 0; i < 64; ++i) {
       const int64_t s = j * 64 + i;
-      c += s < seq && (valid_re ? valid_re[s] != 0 : 1);
+      c += s < seq_k && (k_valid ? k_valid[s] != 0 : 1);
     }
     tile_cnt[j] = c;
   }
@@ -697,16 +701,17 @@ void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int
   select_sizes(mode, sparsity, cdf, nk, &k_topk, &ub);
   for (int h = 0; h < heads; ++h) {
     for (int pass = 0; pass < 2; ++pass) {
-      const uint16_t* x = (pass ? k_re : q_re) + (int64_t)h * S * D;
+      const uint16_t* x = pass ? k_re + (int64_t)h * Sk * D : q_re + (int64_t)h * Sq * D;
       const int chunk = pass ? chunk_k : chunk_q;
       const int64_t n = pass ? nk : nq;
+      const uint8_t* valid = pass ? k_valid : q_valid;
       float* out = pass ? kc : qc;
       for (int64_t c = 0; c < n; ++c) {
         int cnt = 0;
         for (int d = 0; d < D; ++d) out[c * D + d] = 0.0f;
         for (int i = 0; i < chunk; ++i) {
           const int64_t s = c * chunk + i;
-          if (valid_re && !valid_re[s]) continue;
+          if (valid && !valid[s]) continue;
           ++cnt;
           for (int d = 0; d < D; ++d) out[c * D + d] += bf16_to_f32(x[s * D + d]);
         }
@@ -714,8 +719,8 @@ void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int
         for (int d = 0; d < D; ++d) out[c * D + d] = out[c * D + d] / den;
       }
     }
-    uint32_t* bq = bits_q + (int64_t)h * N_tiles * WQ;
-    uint32_t* bk = bits_k + (int64_t)h * N_tiles * WQ;
+    uint32_t* bq = bits_q + (int64_t)h * NQ_tiles * WK;
+    uint32_t* bk = bits_k + (int64_t)h * NK_tiles * WQ;
     for (int64_t a = 0; a < nq; ++a) {
       for (int64_t b = 0; b < nk; ++b) {
         float acc = 0.0f;
@@ -732,7 +737,7 @@ void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int
           if (tile_cnt[kt] == 0) continue;
           for (int pq = 0; pq < tq; ++pq) {
             const int64_t qt = a * tq + pq;
-            bq[qt * WQ + kt / 32] |= 1u << (kt % 32);
+            bq[qt * WK + kt / 32] |= 1u << (kt % 32);
             bk[kt * WQ + qt / 32] |= 1u << (qt % 32);
           }
         }

@@ -35,7 +35,9 @@ SIGNATURES = {
     "prism_block_select": (_I, [_P, _P, _I, _I64, _I, _P, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
     "prism_uniform_layout": (_I, [_I, _I, _I, _I, _I, _I, _I64, _P, _P, _P]),
     "prism_block_select_uniform_workspace_bytes": (_SZ, [_I, _I64, _I64, _I]),
-    "prism_block_select_uniform": (_I, [_P, _P, _I, _I64, _I, _I64, _I, _I, _P, _I, _D, _D, _P, _P, _P, _P]),
+    "prism_block_select_uniform": (_I, [_P, _P, _I, _I64, _I64, _I, _I64, _I64, _I, _I, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
+    "prism_bsa_fwd_qk": (_I, [_P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
+    "prism_bsa_bwd_qk": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_workspace_bytes": (_SZ, [_I, _I64]),
     "prism_bsa_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
@@ -52,6 +54,7 @@ KERNELS = {
     "prism_scatter_rows": 1, "prism_block_select": 4, "prism_bsa_fwd": 1, "prism_bsa_bwd": 3,
     "prism_bsa_bwd_delta": 1, "prism_bsa_bwd_dkdv": 1, "prism_bsa_bwd_dq": 1,
     "prism_bsa_bwd_noalloc": 3, "prism_uniform_layout": 1, "prism_block_select_uniform": 4,
+    "prism_bsa_fwd_qk": 1, "prism_bsa_bwd_qk": 3,
 }
 launch_count = 0
 

@@ -346,7 +346,7 @@ struct FwdLayout {
 template <int D>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, int64_t S, int wq, float qk_scale,
+                  const __grid_constant__ CUtensorMap tm_v, int64_t Sq, int64_t Sk, int wq, float qk_scale,
                   const uint32_t* __restrict__ bits_q, const uint64_t* __restrict__ tile_bits,
                   __nv_bfloat16* __restrict__ o, __nv_bfloat16* __restrict__ o_lo,
                   float* __restrict__ lse) {
@@ -357,10 +357,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t sb = smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = blockIdx.x, h = blockIdx.y;
-  const int64_t n_tiles = S / 64;
-  const bool g1_live = 4 * (int64_t)quad + 2 < n_tiles;  // S % 256 == 128: last CTA has one group
-  const int row_base = (int)((int64_t)h * S + (int64_t)quad * 256);  // row of [heads*S, D]
-  const int head_row = (int)((int64_t)h * S);
+  // queries: Sq rows per head (tiles in bits_q rows), keys: Sk rows per head; wq = words per
+  // bits_q row (ceil(Sk / 2048))
+  const int64_t n_tiles = Sq / 64;
+  const bool g1_live = 4 * (int64_t)quad + 2 < n_tiles;  // Sq % 256 == 128: last CTA has one group
+  const int row_base = (int)((int64_t)h * Sq + (int64_t)quad * 256);  // row of [heads*Sq, D]
+  const int head_row = (int)((int64_t)h * Sk);                        // key rows of head h
   auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
   const uint32_t* r0 = bits_q + ((int64_t)h * n_tiles + 4 * (int64_t)quad) * wq;
@@ -728,8 +730,8 @@ template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                   const float* __restrict__ lse, const float* __restrict__ delta, int64_t S, int wq,
-                   float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_k,
+                   const float* __restrict__ lse, const float* __restrict__ delta, int64_t Sq, int64_t Sk,
+                   int wq, float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_k,
                    const uint64_t* __restrict__ tile_bits, __nv_bfloat16* __restrict__ dk,
                    __nv_bfloat16* __restrict__ dv) {
   using L = DkdvLayout<D>;
@@ -739,9 +741,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t sb = smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pair = blockIdx.x, h = blockIdx.y;
-  const int64_t n_tiles = S / 64;
-  const int row_base = (int)((int64_t)h * S + (int64_t)pair * 128);
-  const int head_row = (int)((int64_t)h * S);
+  // keys: tile pair `pair` of Sk rows per head (rows of bits_k); queries: Sq rows per
+  // head, wq = words per bits_k row (ceil(Sq / 2048))
+  const int64_t n_tiles = Sk / 64;
+  const int row_base = (int)((int64_t)h * Sk + (int64_t)pair * 128);  // key rows of this CTA
+  const int head_row = (int)((int64_t)h * Sq);                        // query rows of head h
   auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
   const uint32_t* row_a = bits_k + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
@@ -999,8 +1003,8 @@ template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                 const float* __restrict__ lse, const float* __restrict__ delta, int64_t S, int wq,
-                 float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_q,
+                 const float* __restrict__ lse, const float* __restrict__ delta, int64_t Sq, int64_t Sk,
+                 int wq, float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_q,
                  const uint64_t* __restrict__ tile_bits, __nv_bfloat16* __restrict__ dq) {
   using L = DqLayout<D>;
   constexpr int RK = L::kRingK, RV = L::kRingV;
@@ -1009,9 +1013,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t sb = smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pair = blockIdx.x, h = blockIdx.y;
-  const int64_t n_tiles = S / 64;
-  const int row_base = (int)((int64_t)h * S + (int64_t)pair * 128);
-  const int head_row = (int)((int64_t)h * S);
+  // queries: tile pair `pair` of Sq rows per head (rows of bits_q); keys: Sk rows per head,
+  // wq = words per bits_q row (ceil(Sk / 2048))
+  const int64_t n_tiles = Sq / 64;
+  const int row_base = (int)((int64_t)h * Sq + (int64_t)pair * 128);  // query rows of this CTA
+  const int head_row = (int)((int64_t)h * Sk);                        // key rows of head h
   auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
   const uint32_t* row_a = bits_q + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
@@ -1333,25 +1339,25 @@ static prism_status_t make_map(CUtensorMap* map, const void* ptr, int64_t rows, 
   } while (0)
 
 template <int D>
-prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
-                          float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits, void* o,
-                          void* o_lo, float* lse, cudaStream_t stream) {
-  const int64_t n_tiles = S / 64;
-  const int wq = (int)((n_tiles + 31) / 32);
-  const size_t need = FwdLayout<D>::bytes(n_tiles);
+prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads, int64_t Sq,
+                          int64_t Sk, float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
+                          void* o, void* o_lo, float* lse, cudaStream_t stream) {
+  const int64_t n_tiles = Sq / 64, n_ktiles = Sk / 64;
+  const int wq = (int)((n_ktiles + 31) / 32);
+  const size_t need = FwdLayout<D>::bytes(n_ktiles);
   const size_t sm = need > kMinSmem ? need : kMinSmem;
-  PRISM_CHECK_ARG(n_tiles <= 65536 && sm <= 227 * 1024,
-                  "prism_bsa_fwd: %lld tiles per head exceed the shared-memory tile lists",
-                  (long long)n_tiles);
+  PRISM_CHECK_ARG(n_ktiles <= 65536 && sm <= 227 * 1024,
+                  "prism_bsa_fwd: %lld key tiles per head exceed the shared-memory tile lists",
+                  (long long)n_ktiles);
   CUtensorMap mq, mk, mv;
-  const int64_t rows = (int64_t)heads * S;
-  PRISM_TRY(make_map(&mq, q, rows, D, "prism_bsa_fwd"));
-  PRISM_TRY(make_map(&mk, k, rows, D, "prism_bsa_fwd"));
-  PRISM_TRY(make_map(&mv, v, rows, D, "prism_bsa_fwd"));
+  PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_fwd"));
+  PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_fwd"));
+  PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_fwd"));
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                    "prism_bsa_fwd: smem attribute");
   fwd_tc_kernel<D><<<dim3((unsigned)((n_tiles + 3) / 4), heads), kFwdThreads, sm, stream>>>(
-      mq, mk, mv, S, wq, sm_scale * kRcpLn2, bits_q, tile_bits, (__nv_bfloat16*)o, (__nv_bfloat16*)o_lo, lse);
+      mq, mk, mv, Sq, Sk, wq, sm_scale * kRcpLn2, bits_q, tile_bits, (__nv_bfloat16*)o,
+      (__nv_bfloat16*)o_lo, lse);
   PRISM_CHECK_LAUNCH("prism_bsa_fwd");
   return PRISM_OK;
 }
@@ -1368,23 +1374,22 @@ prism_status_t launch_delta(const void* o, const void* o_lo, const void* dout, i
 
 template <int D>
 prism_status_t launch_dkdv(const void* q, const void* k, const void* v, const void* dout,
-                           const float* lse, const float* delta, int heads, int64_t S,
+                           const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
                            float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
                            void* dk, void* dv, cudaStream_t stream) {
-  const int64_t n_tiles = S / 64;
-  const int wq = (int)((n_tiles + 31) / 32);
+  const int64_t n_ktiles = Sk / 64;
+  const int wq = (int)((Sq / 64 + 31) / 32);  // words per bits_k row (query tiles)
   const size_t sm = DkdvLayout<D>::kBytes > kMinSmem ? DkdvLayout<D>::kBytes : kMinSmem;
   PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
   CUtensorMap mq, mk, mv, mdo;
-  const int64_t rows = (int64_t)heads * S;
-  PRISM_TRY(make_map(&mq, q, rows, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mk, k, rows, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mv, v, rows, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mdo, dout, rows, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mdo, dout, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(dkdv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                    "prism_bsa_bwd: smem attribute");
-  dkdv_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kBwdThreads, sm, stream>>>(
-      mq, mk, mv, mdo, lse, delta, S, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
+  dkdv_tc_kernel<D><<<dim3((unsigned)(n_ktiles / 2), heads), kBwdThreads, sm, stream>>>(
+      mq, mk, mv, mdo, lse, delta, Sq, Sk, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
       (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
   PRISM_CHECK_LAUNCH("prism_bsa_bwd_dkdv");
   return PRISM_OK;
@@ -1392,23 +1397,22 @@ prism_status_t launch_dkdv(const void* q, const void* k, const void* v, const vo
 
 template <int D>
 prism_status_t launch_dq(const void* q, const void* k, const void* v, const void* dout,
-                         const float* lse, const float* delta, int heads, int64_t S,
+                         const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
                          float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
                          void* dq, cudaStream_t stream) {
-  const int64_t n_tiles = S / 64;
-  const int wq = (int)((n_tiles + 31) / 32);
+  const int64_t n_tiles = Sq / 64;
+  const int wq = (int)((Sk / 64 + 31) / 32);  // words per bits_q row (key tiles)
   const size_t sm = DqLayout<D>::kBytes > kMinSmem ? DqLayout<D>::kBytes : kMinSmem;
   PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
   CUtensorMap mq, mk, mv, mdo;
-  const int64_t rows = (int64_t)heads * S;
-  PRISM_TRY(make_map(&mq, q, rows, D, "prism_bsa_bwd_dq"));
-  PRISM_TRY(make_map(&mk, k, rows, D, "prism_bsa_bwd_dq"));
-  PRISM_TRY(make_map(&mv, v, rows, D, "prism_bsa_bwd_dq"));
-  PRISM_TRY(make_map(&mdo, dout, rows, D, "prism_bsa_bwd_dq"));
+  PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_bwd_dq"));
+  PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_bwd_dq"));
+  PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_bwd_dq"));
+  PRISM_TRY(make_map(&mdo, dout, (int64_t)heads * Sq, D, "prism_bsa_bwd_dq"));
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(dq_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                    "prism_bsa_bwd: smem attribute");
   dq_tc_kernel<D><<<dim3((unsigned)(n_tiles / 2), heads), kBwdThreads, sm, stream>>>(
-      mq, mk, mv, mdo, lse, delta, S, wq, sm_scale * kRcpLn2, sm_scale, bits_q, tile_bits,
+      mq, mk, mv, mdo, lse, delta, Sq, Sk, wq, sm_scale * kRcpLn2, sm_scale, bits_q, tile_bits,
       (__nv_bfloat16*)dq);
   PRISM_CHECK_LAUNCH("prism_bsa_bwd_dq");
   return PRISM_OK;
@@ -1431,22 +1435,33 @@ int prism_device_status(void) {
   return v;
 }
 
-// Row indices of the [heads * S, D] view are 32-bit TMA coordinates.
-#define PRISM_ATTN_SHAPE_CHECKS(name)                                                              \
-  PRISM_CHECK_ARG(S > 0 && S % 128 == 0 && heads >= 1, name ": S must be a positive multiple of 128"); \
-  PRISM_CHECK_ARG((int64_t)heads * S < ((int64_t)1 << 31), name ": heads * S must be below 2^31");     \
+// Row indices of the [heads * S, D] views are 32-bit TMA coordinates.
+#define PRISM_ATTN_LEN_CHECKS(name, S)                                                            \
+  PRISM_CHECK_ARG(S > 0 && S % 128 == 0 && heads >= 1,                                            \
+                  name ": sequence lengths must be positive multiples of 128");                   \
+  PRISM_CHECK_ARG((int64_t)heads * S < ((int64_t)1 << 31), name ": heads * S must be below 2^31")
+#define PRISM_ATTN_SHAPE_CHECKS(name, Sq, Sk)                                                     \
+  PRISM_ATTN_LEN_CHECKS(name, Sq);                                                                \
+  PRISM_ATTN_LEN_CHECKS(name, Sk);                                                                \
   PRISM_CHECK_ARG(D == 64 || D == 128, name ": head dim %d not supported (64, 128)", D)
+
+prism_status_t prism_bsa_fwd_qk(const void* q, const void* k, const void* v, int heads, int64_t Sq,
+                                int64_t Sk, int D, float sm_scale, const uint32_t* bits_q,
+                                const uint64_t* tile_bits, void* o, void* o_lo, float* lse,
+                                cudaStream_t stream) {
+  PRISM_CHECK_ARG(q && k && v && bits_q && tile_bits && o && lse, "prism_bsa_fwd: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_fwd", Sq, Sk);
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o), "prism_bsa_fwd: tensors must be 16-byte aligned");
+  PRISM_CHECK_ARG(o_lo == nullptr || aligned16(o_lo), "prism_bsa_fwd: o_lo must be 16-byte aligned");
+  if (D == 128) return tc::launch_fwd<128>(q, k, v, heads, Sq, Sk, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
+  return tc::launch_fwd<64>(q, k, v, heads, Sq, Sk, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
+}
 
 prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,
                              int D, float sm_scale, const uint32_t* bits_q,
                              const uint64_t* tile_bits, void* o, void* o_lo, float* lse,
                              cudaStream_t stream) {
-  PRISM_CHECK_ARG(q && k && v && bits_q && tile_bits && o && lse, "prism_bsa_fwd: null pointer");
-  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_fwd");
-  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o), "prism_bsa_fwd: tensors must be 16-byte aligned");
-  PRISM_CHECK_ARG(o_lo == nullptr || aligned16(o_lo), "prism_bsa_fwd: o_lo must be 16-byte aligned");
-  if (D == 128) return tc::launch_fwd<128>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
-  return tc::launch_fwd<64>(q, k, v, heads, S, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
+  return prism_bsa_fwd_qk(q, k, v, heads, S, S, D, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
 }
 
 size_t prism_bsa_bwd_workspace_bytes(int heads, int64_t S) {
@@ -1456,35 +1471,64 @@ size_t prism_bsa_bwd_workspace_bytes(int heads, int64_t S) {
 prism_status_t prism_bsa_bwd_delta(const void* o, const void* o_lo, const void* dout, int heads,
                                    int64_t S, int D, float* delta, cudaStream_t stream) {
   PRISM_CHECK_ARG(o && dout && delta, "prism_bsa_bwd_delta: null pointer");
-  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_delta");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_delta", S, S);
   return D == 128 ? tc::launch_delta<128>(o, o_lo, dout, heads, S, delta, stream)
                   : tc::launch_delta<64>(o, o_lo, dout, heads, S, delta, stream);
+}
+
+static prism_status_t bwd_dkdv_qk(const void* q, const void* k, const void* v, const void* dout,
+                                  const float* lse, const float* delta, int heads, int64_t Sq,
+                                  int64_t Sk, int D, float sm_scale, const uint32_t* bits_k,
+                                  const uint64_t* tile_bits, void* dk, void* dv, cudaStream_t stream) {
+  PRISM_CHECK_ARG(q && k && v && dout && lse && delta && bits_k && tile_bits && dk && dv,
+                  "prism_bsa_bwd_dkdv: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_dkdv", Sq, Sk);
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dk) &&
+                      aligned16(dv) && aligned16(lse) && aligned16(delta),
+                  "prism_bsa_bwd_dkdv: tensors must be 16-byte aligned");
+  return D == 128 ? tc::launch_dkdv<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream)
+                  : tc::launch_dkdv<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
+}
+
+static prism_status_t bwd_dq_qk(const void* q, const void* k, const void* v, const void* dout,
+                                const float* lse, const float* delta, int heads, int64_t Sq,
+                                int64_t Sk, int D, float sm_scale, const uint32_t* bits_q,
+                                const uint64_t* tile_bits, void* dq, cudaStream_t stream) {
+  PRISM_CHECK_ARG(q && k && v && dout && lse && delta && bits_q && tile_bits && dq, "prism_bsa_bwd_dq: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_dq", Sq, Sk);
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dq),
+                  "prism_bsa_bwd_dq: tensors must be 16-byte aligned");
+  return D == 128 ? tc::launch_dq<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_q, tile_bits, dq, stream)
+                  : tc::launch_dq<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_q, tile_bits, dq, stream);
 }
 
 prism_status_t prism_bsa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout,
                                   const float* lse, const float* delta, int heads, int64_t S, int D,
                                   float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
                                   void* dk, void* dv, cudaStream_t stream) {
-  PRISM_CHECK_ARG(q && k && v && dout && lse && delta && bits_k && tile_bits && dk && dv,
-                  "prism_bsa_bwd_dkdv: null pointer");
-  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_dkdv");
-  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dk) &&
-                      aligned16(dv) && aligned16(lse) && aligned16(delta),
-                  "prism_bsa_bwd_dkdv: tensors must be 16-byte aligned");
-  return D == 128 ? tc::launch_dkdv<128>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_k, tile_bits, dk, dv, stream)
-                  : tc::launch_dkdv<64>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  return bwd_dkdv_qk(q, k, v, dout, lse, delta, heads, S, S, D, sm_scale, bits_k, tile_bits, dk, dv, stream);
 }
 
 prism_status_t prism_bsa_bwd_dq(const void* q, const void* k, const void* v, const void* dout,
                                 const float* lse, const float* delta, int heads, int64_t S, int D,
                                 float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
                                 void* dq, cudaStream_t stream) {
-  PRISM_CHECK_ARG(q && k && v && dout && lse && delta && bits_q && tile_bits && dq, "prism_bsa_bwd_dq: null pointer");
-  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_bwd_dq");
-  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dq),
-                  "prism_bsa_bwd_dq: tensors must be 16-byte aligned");
-  return D == 128 ? tc::launch_dq<128>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_q, tile_bits, dq, stream)
-                  : tc::launch_dq<64>(q, k, v, dout, lse, delta, heads, S, sm_scale, bits_q, tile_bits, dq, stream);
+  return bwd_dq_qk(q, k, v, dout, lse, delta, heads, S, S, D, sm_scale, bits_q, tile_bits, dq, stream);
+}
+
+prism_status_t prism_bsa_bwd_qk(const void* q, const void* k, const void* v, const void* o,
+                                const void* o_lo, const void* dout, const float* lse, int heads,
+                                int64_t Sq, int64_t Sk, int D, float sm_scale,
+                                const uint32_t* bits_q, const uint32_t* bits_k,
+                                const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
+                                void* dv, cudaStream_t stream) {
+  PRISM_CHECK_ARG(workspace, "prism_bsa_bwd: null pointer");
+  float* delta = (float*)workspace;
+  prism_status_t st = prism_bsa_bwd_delta(o, o_lo, dout, heads, Sq, D, delta, stream);
+  if (st != PRISM_OK) return st;
+  st = bwd_dkdv_qk(q, k, v, dout, lse, delta, heads, Sq, Sk, D, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  if (st != PRISM_OK) return st;
+  return bwd_dq_qk(q, k, v, dout, lse, delta, heads, Sq, Sk, D, sm_scale, bits_q, tile_bits, dq, stream);
 }
 
 prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const void* o,
@@ -1493,13 +1537,8 @@ prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const 
                              float sm_scale, const uint32_t* bits_q, const uint32_t* bits_k,
                              const uint64_t* tile_bits, void* workspace, void* dq, void* dk,
                              void* dv, cudaStream_t stream) {
-  PRISM_CHECK_ARG(workspace, "prism_bsa_bwd: null pointer");
-  float* delta = (float*)workspace;
-  prism_status_t st = prism_bsa_bwd_delta(o, o_lo, dout, heads, S, D, delta, stream);
-  if (st != PRISM_OK) return st;
-  st = prism_bsa_bwd_dkdv(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_k, tile_bits, dk, dv, stream);
-  if (st != PRISM_OK) return st;
-  return prism_bsa_bwd_dq(q, k, v, dout, lse, delta, heads, S, D, sm_scale, bits_q, tile_bits, dq, stream);
+  return prism_bsa_bwd_qk(q, k, v, o, o_lo, dout, lse, heads, S, S, D, sm_scale, bits_q, bits_k,
+                          tile_bits, workspace, dq, dk, dv, stream);
 }
 
 }  // extern "C"

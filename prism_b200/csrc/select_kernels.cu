@@ -780,8 +780,8 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
     const float* __restrict__ score, const uint8_t* __restrict__ bvalid,
     const int32_t* __restrict__ n_blocks, int na_max, int nb_max,
     const int32_t* __restrict__ block_tiles, int tq, int tk,
-    const uint64_t* __restrict__ tile_bits, int64_t n_tiles, int wq, int mode, double sparsity,
-    double cdf, float sm_scale, uint32_t* __restrict__ bits_q) {
+    const uint64_t* __restrict__ tile_bits, int64_t n_qt, int64_t n_kt, int wq, int mode,
+    double sparsity, double cdf, float sm_scale, uint32_t* __restrict__ bits_q) {
   extern __shared__ uint32_t keys[];  // [nb_max] then row bitmap [wq]
   uint32_t* row = keys + nb_max;
   __shared__ uint32_t hist_cnt[256];
@@ -953,7 +953,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
       const int np = block_tiles ? 2 : tk;
       for (int p = 0; p < np; ++p) {
         const int kt = block_tiles ? block_tiles[2 * i + p] : i * tk + p;
-        if (kt >= n_tiles || tile_bits[kt] == 0ull) continue;
+        if (kt >= n_kt || tile_bits[kt] == 0ull) continue;
         atomicOr(&row[kt >> 5], 1u << (kt & 31));
       }
     }
@@ -962,25 +962,26 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   const int nq = block_tiles ? 2 : tq;
   for (int p = 0; p < nq; ++p) {
     const int qt = block_tiles ? block_tiles[2 * a + p] : a * tq + p;
-    if (qt >= n_tiles) continue;
-    uint32_t* dst = bits_q + ((int64_t)h * n_tiles + qt) * wq;
+    if (qt >= n_qt) continue;
+    uint32_t* dst = bits_q + ((int64_t)h * n_qt + qt) * wq;
     for (int i = tid; i < wq; i += blockDim.x) dst[i] = row[i];
   }
 }
 
-// bits_k = transpose of bits_q per head, by 32x32 bit blocks (warp ballots).
-__global__ void transpose_bits_kernel(const uint32_t* __restrict__ bq, int64_t n_tiles, int wq,
-                                      uint32_t* __restrict__ bk) {
+// bits_k = transpose of bits_q per head, by 32x32 bit blocks (warp ballots):
+// bits_q [n_qt][wk] (wk = ceil(n_kt / 32)) -> bits_k [n_kt][wq] (wq = ceil(n_qt / 32)).
+__global__ void transpose_bits_kernel(const uint32_t* __restrict__ bq, int64_t n_qt, int64_t n_kt,
+                                      int wq, int wk, uint32_t* __restrict__ bk) {
   const int bi = blockIdx.x;  // q-tile word block
   const int bj = blockIdx.y;  // k-tile word block
   const int h = blockIdx.z;
   const int lane = threadIdx.x;
   const int64_t qt = (int64_t)bi * 32 + lane;
-  const uint32_t w = qt < n_tiles ? bq[((int64_t)h * n_tiles + qt) * wq + bj] : 0u;
+  const uint32_t w = qt < n_qt ? bq[((int64_t)h * n_qt + qt) * wk + bj] : 0u;
   for (int b = 0; b < 32; ++b) {
     const uint32_t col = __ballot_sync(0xffffffffu, (w >> b) & 1u);
     const int64_t kt = (int64_t)bj * 32 + b;
-    if (lane == 0 && kt < n_tiles) bk[((int64_t)h * n_tiles + kt) * wq + bi] = col;
+    if (lane == 0 && kt < n_kt) bk[((int64_t)h * n_kt + kt) * wq + bi] = col;
   }
 }
 
@@ -1018,24 +1019,27 @@ __global__ void uniform_perm_kernel(int Hp, int Wp, int ct, int ch, int cw, int6
 
 // masked_mean_pooling_compression / mean_pooling_compression
 // (bsa_interface.py:164-201) over chunks of consecutive rows: sequential fp32
-// sum over the chunk's valid rows (bit s of the tile_bits words), divided by
-// max(count, 1).  One CTA per (chunk, head, tensor), D threads; blockIdx.z
-// picks x0 (n0 chunks of chunk0 rows -> out0) or x1 (n1 of chunk1 -> out1).
+// sum over the chunk's valid rows (bit s of the validity words; nullptr = all
+// rows valid), divided by max(count, 1).  One CTA per (chunk, head, tensor),
+// D threads; blockIdx.z picks x0 (S0 rows per head, n0 chunks of chunk0 rows,
+// validity bits0 -> out0) or x1 (S1, n1, chunk1, bits1 -> out1).
 __global__ void pool_chunk_kernel(const uint16_t* __restrict__ x0, const uint16_t* __restrict__ x1,
-                                  int64_t S, int D, int chunk0, int n0, int chunk1, int n1,
-                                  const uint64_t* __restrict__ tile_bits, float* __restrict__ out0,
+                                  int64_t S0, int64_t S1, int D, int chunk0, int n0, int chunk1,
+                                  int n1, const uint64_t* __restrict__ bits0,
+                                  const uint64_t* __restrict__ bits1, float* __restrict__ out0,
                                   float* __restrict__ out1) {
   const int c = blockIdx.x, h = blockIdx.y, which = blockIdx.z;
   const int chunk = which ? chunk1 : chunk0;
   const int n = which ? n1 : n0;
   if (c >= n) return;
   const int64_t base = (int64_t)c * chunk;
-  const uint16_t* x = (which ? x1 : x0) + ((int64_t)h * S + base) * D + threadIdx.x;
+  const uint16_t* x = (which ? x1 : x0) + ((int64_t)h * (which ? S1 : S0) + base) * D + threadIdx.x;
+  const uint64_t* vbits = which ? bits1 : bits0;
   float sum = 0.0f;
   int cnt = 0;
   for (int i = 0; i < chunk; ++i) {
     const int64_t sidx = base + i;
-    if (!((tile_bits[sidx >> 6] >> (sidx & 63)) & 1ull)) continue;
+    if (vbits != nullptr && !((vbits[sidx >> 6] >> (sidx & 63)) & 1ull)) continue;
     sum = __fadd_rn(sum, bfbits2f(x[(int64_t)i * D]));
     ++cnt;
   }
@@ -1051,7 +1055,7 @@ using namespace prism;
 extern "C" {
 
 const char* prism_last_error(void) { return prism::last_error(); }
-int prism_abi_version(void) { return 2; }
+int prism_abi_version(void) { return 3; }
 
 prism_status_t prism_token_norms(const void* x, int64_t n_tokens, int dim, void* out,
                                  cudaStream_t stream) {
@@ -1230,10 +1234,10 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)selsm),
                    "prism_block_select: smem attribute");
   select_kernel<<<dim3(nb_max, heads), kSelThreads, selsm, stream>>>(
-      sc, bvalid, n_blocks, nb_max, nb_max, block_tiles, 2, 2, tile_bits, n_tiles, wq, mode,
-      sparsity, cdf_threshold, sm_scale, bits_q);
+      sc, bvalid, n_blocks, nb_max, nb_max, block_tiles, 2, 2, tile_bits, n_tiles, n_tiles, wq,
+      mode, sparsity, cdf_threshold, sm_scale, bits_q);
   PRISM_CHECK_LAUNCH("prism_block_select/select");
-  transpose_bits_kernel<<<dim3(wq, wq, heads), 32, 0, stream>>>(bits_q, n_tiles, wq, bits_k);
+  transpose_bits_kernel<<<dim3(wq, wq, heads), 32, 0, stream>>>(bits_q, n_tiles, n_tiles, wq, wq, bits_k);
   PRISM_CHECK_LAUNCH("prism_block_select/transpose");
   return PRISM_OK;
 }
@@ -1261,33 +1265,37 @@ size_t prism_block_select_uniform_workspace_bytes(int heads, int64_t n_chunks_q,
   return b;
 }
 
-prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t S,
-                                          int D, int64_t seq, int chunk_q, int chunk_k,
-                                          const uint64_t* tile_bits, int mode, double sparsity,
+prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t Sq,
+                                          int64_t Sk, int D, int64_t seq_q, int64_t seq_k,
+                                          int chunk_q, int chunk_k, const uint64_t* q_bits,
+                                          const uint64_t* k_bits, int mode, double sparsity,
                                           double cdf_threshold, void* workspace, uint32_t* bits_q,
                                           uint32_t* bits_k, cudaStream_t stream) {
-  PRISM_CHECK_ARG(q_re && k_re && tile_bits && workspace && bits_q && bits_k,
+  PRISM_CHECK_ARG(q_re && k_re && k_bits && workspace && bits_q && bits_k,
                   "prism_block_select_uniform: null pointer");
   PRISM_CHECK_ARG(mode >= 0 && mode <= 2, "prism_block_select_uniform: Either sparsity or cdf_threshold must be provided");
-  PRISM_CHECK_ARG(S > 0 && S % 64 == 0 && heads >= 1, "prism_block_select_uniform: S must be a positive multiple of 64");
+  PRISM_CHECK_ARG(Sq > 0 && Sq % 64 == 0 && Sk > 0 && Sk % 64 == 0 && heads >= 1,
+                  "prism_block_select_uniform: sequence lengths must be positive multiples of 64");
   PRISM_CHECK_ARG(D >= 16 && D <= 256, "prism_block_select_uniform: D=%d unsupported", D);
   PRISM_CHECK_ARG(chunk_q > 0 && chunk_k > 0 && chunk_q % 64 == 0 && chunk_k % 64 == 0,
                   "prism_block_select_uniform: chunk sizes (%d, %d) must be multiples of 64 tokens",
                   chunk_q, chunk_k);
-  PRISM_CHECK_ARG(seq > 0 && seq <= S && seq % chunk_q == 0 && seq % chunk_k == 0,
-                  "prism_block_select_uniform: sequence %lld is not a whole number of chunks",
-                  (long long)seq);
-  const int64_t n_tiles = S / 64;
-  const int nq = (int)(seq / chunk_q), nk = (int)(seq / chunk_k);
+  PRISM_CHECK_ARG(seq_q > 0 && seq_q <= Sq && seq_q % chunk_q == 0 && seq_k > 0 && seq_k <= Sk &&
+                      seq_k % chunk_k == 0,
+                  "prism_block_select_uniform: sequences (%lld, %lld) are not whole numbers of chunks",
+                  (long long)seq_q, (long long)seq_k);
+  const int64_t n_qt = Sq / 64, n_kt = Sk / 64;
+  const int nq = (int)(seq_q / chunk_q), nk = (int)(seq_k / chunk_k);
   PRISM_CHECK_ARG(nk <= 40000, "prism_block_select_uniform: %d key chunks exceed the per-row shared-memory limit", nk);
-  const int wq = (int)((n_tiles + 31) / 32);
+  const int wk = (int)((n_kt + 31) / 32), wq = (int)((n_qt + 31) / 32);
   float* qc = (float*)workspace;
   float* kc = qc + (size_t)heads * nq * D;
   float* sc = kc + (size_t)heads * nk * D;
-  PRISM_CHECK_CUDA(cudaMemsetAsync(bits_q, 0, (size_t)heads * n_tiles * wq * sizeof(uint32_t), stream),
+  PRISM_CHECK_CUDA(cudaMemsetAsync(bits_q, 0, (size_t)heads * n_qt * wk * sizeof(uint32_t), stream),
                    "prism_block_select_uniform: clear bitmaps");
   pool_chunk_kernel<<<dim3(nq > nk ? nq : nk, heads, 2), D, 0, stream>>>(
-      (const uint16_t*)q_re, (const uint16_t*)k_re, S, D, chunk_q, nq, chunk_k, nk, tile_bits, qc, kc);
+      (const uint16_t*)q_re, (const uint16_t*)k_re, Sq, Sk, D, chunk_q, nq, chunk_k, nk, q_bits,
+      k_bits, qc, kc);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/pool");
   const size_t ssm = 2 * (size_t)D * (kScoreTile + 4) * sizeof(float);
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),
@@ -1296,14 +1304,14 @@ prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, in
                  ssm, stream>>>(qc, kc, D, nullptr, nq, nk, sc);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/score");
   const float sm_scale = (float)(1.0 / sqrt((double)D));
-  const size_t selsm = ((size_t)nk + wq) * sizeof(uint32_t);
+  const size_t selsm = ((size_t)nk + wk) * sizeof(uint32_t);
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)selsm),
                    "prism_block_select_uniform: smem attribute");
   select_kernel<<<dim3(nq, heads), kSelThreads, selsm, stream>>>(
-      sc, nullptr, nullptr, nq, nk, nullptr, chunk_q / 64, chunk_k / 64, tile_bits, n_tiles, wq, mode,
+      sc, nullptr, nullptr, nq, nk, nullptr, chunk_q / 64, chunk_k / 64, k_bits, n_qt, n_kt, wk, mode,
       sparsity, cdf_threshold, sm_scale, bits_q);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/select");
-  transpose_bits_kernel<<<dim3(wq, wq, heads), 32, 0, stream>>>(bits_q, n_tiles, wq, bits_k);
+  transpose_bits_kernel<<<dim3(wq, wk, heads), 32, 0, stream>>>(bits_q, n_qt, n_kt, wq, wk, bits_k);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/transpose");
   return PRISM_OK;
 }

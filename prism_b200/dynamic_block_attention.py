@@ -39,12 +39,16 @@ class SparsePlan:
     inverse); ``layout_k`` orders keys and values when it differs (the uniform
     path with different q / key chunk shapes).  ``uniform`` = dict(seq, chunk_q,
     chunk_k) selects the uniform path's chunk selection instead of the dynamic
-    path's logical-block selection."""
+    path's logical-block selection; ``grid_k`` / ``grid_padded_k`` give the keys'
+    own grid when it differs from the queries' (cross attention)."""
 
     def __init__(self, grid, grid_padded, layout, tile_bits, sparsity, cdf_threshold, sm_scale,
-                 layout_k=None, uniform=None):
+                 layout_k=None, uniform=None, grid_k=None, grid_padded_k=None):
         self.grid = tuple(grid)
         self.grid_padded = tuple(grid_padded)
+        # keys / values may live on their own grid (cross attention)
+        self.grid_k = self.grid if grid_k is None else tuple(grid_k)
+        self.grid_padded_k = self.grid_padded if grid_padded_k is None else tuple(grid_padded_k)
         self.layout = layout
         self.src_idx = layout["src_idx"]
         self.inv_idx = layout["inv_idx"]
@@ -63,8 +67,9 @@ class SparsePlan:
         """Tile bitmaps (bits_q, bits_k) for tile-ordered q / k."""
         if self.uniform is not None:
             u = self.uniform
-            return ops.block_select_uniform(q_re, k_re, u["seq"], u["chunk_q"], u["chunk_k"],
-                                            self.tile_bits, self.sparsity, self.cdf_threshold)
+            return ops.block_select_uniform(q_re, k_re, u["seq_q"], u["seq_k"], u["chunk_q"],
+                                            u["chunk_k"], u["q_bits"], self.tile_bits,
+                                            self.sparsity, self.cdf_threshold)
         return ops.block_select(q_re, k_re, self.layout, self.tile_bits, self.sparsity,
                                 self.cdf_threshold)
 
@@ -94,9 +99,10 @@ class _BsaFunction(torch.autograd.Function):
     def forward(ctx, q, k, v, plan: SparsePlan, layout: str):
         qh, kh, vh = _hsd(q, layout), _hsd(k, layout), _hsd(v, layout)
         heads, S, D = qh.shape
+        Sk = kh.shape[1]
         q_re = ops.gather_rows(qh, plan.grid, plan.grid_padded, plan.src_idx)
-        k_re = ops.gather_rows(kh, plan.grid, plan.grid_padded, plan.src_idx_k)
-        v_re = ops.gather_rows(vh, plan.grid, plan.grid_padded, plan.src_idx_k)
+        k_re = ops.gather_rows(kh, plan.grid_k, plan.grid_padded_k, plan.src_idx_k)
+        v_re = ops.gather_rows(vh, plan.grid_k, plan.grid_padded_k, plan.src_idx_k)
         bits_q, bits_k = plan.select(q_re, k_re)
         plan.bits_q, plan.bits_k = bits_q, bits_k
         o_re, lse, o_lo = ops.bsa_fwd(q_re, k_re, v_re, bits_q, plan.tile_bits, plan.sm_scale,
@@ -106,7 +112,7 @@ class _BsaFunction(torch.autograd.Function):
         ctx.save_for_backward(q_re, k_re, v_re, o_re, o_lo, lse, bits_q, bits_k)
         ctx.plan = plan
         ctx.layout = layout
-        ctx.shape = (heads, S, D)
+        ctx.shape = (heads, S, Sk, D)
         return out
 
     @staticmethod
@@ -114,14 +120,17 @@ class _BsaFunction(torch.autograd.Function):
         q_re, k_re, v_re, o_re, o_lo, lse, bits_q, bits_k = ctx.saved_tensors
         plan = ctx.plan
         layout = ctx.layout
-        heads, S, D = ctx.shape
+        heads, S, Sk, D = ctx.shape
         do_re = ops.gather_rows(_hsd(dout, layout), plan.grid, plan.grid_padded, plan.src_idx)
         dq_re, dk_re, dv_re = ops.bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k,
                                           plan.tile_bits, plan.sm_scale, o_lo=o_lo)
         grads = []
-        for g_re, inv in ((dq_re, plan.inv_idx), (dk_re, plan.inv_idx_k), (dv_re, plan.inv_idx_k)):
-            g, g_hsd = _new_like_layout(heads, S, D, layout, dout.dtype, dout.device)
-            ops.scatter_rows(g_re, plan.grid, plan.grid_padded, inv, out=g_hsd)
+        for g_re, is_k in ((dq_re, False), (dk_re, True), (dv_re, True)):
+            g, g_hsd = _new_like_layout(heads, Sk if is_k else S, D, layout, dout.dtype, dout.device)
+            if is_k:
+                ops.scatter_rows(g_re, plan.grid_k, plan.grid_padded_k, plan.inv_idx_k, out=g_hsd)
+            else:
+                ops.scatter_rows(g_re, plan.grid, plan.grid_padded, plan.inv_idx, out=g_hsd)
             grads.append(g)
         return grads[0], grads[1], grads[2], None, None
 

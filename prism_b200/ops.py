@@ -206,21 +206,23 @@ def uniform_layout(grid_padded, chunk, n_rows: int, device):
     return src, inv
 
 
-def block_select_uniform(q_re, k_re, seq: int, chunk_q: int, chunk_k: int, tile_bits, sparsity,
-                         cdf_threshold):
-    """Chunk pooling + scores + selection of the uniform path -> (bits_q, bits_k)."""
-    _check_cuda(q_re, k_re, tile_bits)
-    heads, S, D = q_re.shape
+def block_select_uniform(q_re, k_re, seq_q: int, seq_k: int, chunk_q: int, chunk_k: int, q_bits,
+                         k_bits, sparsity, cdf_threshold):
+    """Chunk pooling + scores + selection of the uniform path -> (bits_q, bits_k).
+    q_bits: rows the q pooling counts (None: all); k_bits: key validity."""
+    _check_cuda(q_re, k_re, q_bits, k_bits)
+    heads, Sq, D = q_re.shape
+    Sk = k_re.shape[1]
     mode = selection_mode(sparsity, cdf_threshold)
-    n_tiles = S // 64
-    wq = (n_tiles + 31) // 32
+    n_qt, n_kt = Sq // 64, Sk // 64
     dev = q_re.device
-    bits_q = torch.empty(heads, n_tiles, wq, dtype=torch.int32, device=dev)
-    bits_k = torch.empty(heads, n_tiles, wq, dtype=torch.int32, device=dev)
-    ws = _ws(_lib.query("prism_block_select_uniform_workspace_bytes", heads, seq // chunk_q,
-                        seq // chunk_k, D), dev)
-    _lib.call("prism_block_select_uniform", _p(q_re), _p(k_re), heads, S, D, seq, chunk_q, chunk_k,
-              _p(tile_bits), mode, float(sparsity if sparsity is not None else 0.0),
+    bits_q = torch.empty(heads, n_qt, (n_kt + 31) // 32, dtype=torch.int32, device=dev)
+    bits_k = torch.empty(heads, n_kt, (n_qt + 31) // 32, dtype=torch.int32, device=dev)
+    ws = _ws(_lib.query("prism_block_select_uniform_workspace_bytes", heads, seq_q // chunk_q,
+                        seq_k // chunk_k, D), dev)
+    _lib.call("prism_block_select_uniform", _p(q_re), _p(k_re), heads, Sq, Sk, D, seq_q, seq_k,
+              chunk_q, chunk_k, _p(q_bits), _p(k_bits), mode,
+              float(sparsity if sparsity is not None else 0.0),
               float(cdf_threshold if cdf_threshold is not None else 0.0), _p(ws), _p(bits_q),
               _p(bits_k), _stream(q_re))
     return bits_q, bits_k
@@ -230,11 +232,12 @@ def block_select_uniform(q_re, k_re, seq: int, chunk_q: int, chunk_k: int, tile_
 def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float, want_lo: bool = False):
     """Returns (o, lse) or (o, lse, o_lo) with o_lo the bf16 rounding residual of o."""
     _check_cuda(q_re, k_re, v_re)
-    heads, S, D = q_re.shape
+    heads, Sq, D = q_re.shape
+    Sk = k_re.shape[1]
     o = torch.empty_like(q_re)
     o_lo = torch.empty_like(q_re) if want_lo else None
-    lse = torch.empty(heads, S, dtype=torch.float32, device=q_re.device)
-    _lib.call("prism_bsa_fwd", _p(q_re), _p(k_re), _p(v_re), heads, S, D, float(sm_scale),
+    lse = torch.empty(heads, Sq, dtype=torch.float32, device=q_re.device)
+    _lib.call("prism_bsa_fwd_qk", _p(q_re), _p(k_re), _p(v_re), heads, Sq, Sk, D, float(sm_scale),
               _p(bits_q), _p(tile_bits), _p(o), _p(o_lo), _p(lse), _stream(q_re))
     if want_lo:
         return o, lse, o_lo
@@ -244,12 +247,13 @@ def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float, want_lo: bool 
 def bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k, tile_bits, sm_scale: float,
             o_lo=None):
     _check_cuda(q_re, do_re)
-    heads, S, D = q_re.shape
+    heads, Sq, D = q_re.shape
+    Sk = k_re.shape[1]
     dq = torch.empty_like(q_re)
     dk = torch.empty_like(k_re)
     dv = torch.empty_like(v_re)
-    ws = _ws(_lib.query("prism_bsa_bwd_workspace_bytes", heads, S), q_re.device)
-    _lib.call("prism_bsa_bwd", _p(q_re), _p(k_re), _p(v_re), _p(o_re), _p(o_lo), _p(do_re), _p(lse),
-              heads, S, D, float(sm_scale), _p(bits_q), _p(bits_k), _p(tile_bits), _p(ws), _p(dq), _p(dk),
-              _p(dv), _stream(q_re))
+    ws = _ws(_lib.query("prism_bsa_bwd_workspace_bytes", heads, Sq), q_re.device)
+    _lib.call("prism_bsa_bwd_qk", _p(q_re), _p(k_re), _p(v_re), _p(o_re), _p(o_lo), _p(do_re),
+              _p(lse), heads, Sq, Sk, D, float(sm_scale), _p(bits_q), _p(bits_k), _p(tile_bits),
+              _p(ws), _p(dq), _p(dk), _p(dv), _stream(q_re))
     return dq, dk, dv

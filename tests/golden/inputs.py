@@ -110,6 +110,85 @@ UNIFORM_CASES = {
 ALL_CASES = dict(CASES, **UNIFORM_CASES)
 
 
+@dataclass
+class CrossCase:
+    """Cross-modal BSA (flash_attn_bsa_cross, bsa_interface.py:1276-1392): each side
+    is "3d" (shape = latent grid T, H, W) or "1d" (shape = (tokens,))."""
+    name: str
+    q_structure: str
+    k_structure: str
+    q_shape: Tuple[int, ...]
+    k_shape: Tuple[int, ...]
+    heads: int
+    head_dim: int
+    sparsity: Optional[float] = 0.75
+    cdf_threshold: Optional[float] = None
+    chunk_size_q: int = 64
+    chunk_size_k: int = 64
+    chunk_3d_q: Optional[Tuple[int, int, int]] = None
+    chunk_3d_k: Optional[Tuple[int, int, int]] = None
+    seed: int = 0
+
+    @staticmethod
+    def _len(shape):
+        n = 1
+        for x in shape:
+            n *= x
+        return n
+
+    @property
+    def Sq(self):
+        return self._len(self.q_shape)
+
+    @property
+    def Sk(self):
+        return self._len(self.k_shape)
+
+
+CROSS_CASES = {
+    # the v2a bridge's form: audio queries (1D, padded 150 -> 192) over video keys
+    # (3D 6x10x12, padded to 8x12x12 with 4x4x4 chunks)
+    "x_a2v": CrossCase("x_a2v", "1d", "3d", (150,), (6, 10, 12), 2, 64, sparsity=0.75,
+                       cdf_threshold=0.5, chunk_3d_k=(4, 4, 4), seed=70),
+    # video queries (3D 5x8x12 -> 8x8x12) over audio keys (1D 200 -> 256), head_dim 128
+    "x_v2a": CrossCase("x_v2a", "3d", "1d", (5, 8, 12), (200,), 2, 128, sparsity=0.5,
+                       cdf_threshold=None, chunk_3d_q=(4, 4, 4), seed=71),
+    # two 3D grids of different sizes, 64- against 128-token chunks; neither side is
+    # padded (the reference's bf16 pass cannot run with exactly one masked side: its
+    # masked pooling is fp32, the unmasked one bf16, and cal_score rejects the mix)
+    "x_3d3d": CrossCase("x_3d3d", "3d", "3d", (4, 8, 8), (8, 8, 16), 2, 64, sparsity=None,
+                        cdf_threshold=0.6, chunk_3d_q=(4, 4, 4), chunk_3d_k=(4, 4, 8), seed=72),
+}
+
+
+def _side(gen, structure, shape, heads, D):
+    """Seeded values of one side, [1, h, S, D] bf16 in its own token order."""
+    if structure == "3d":
+        T, H, W = shape
+        Tg, Hg, Wg = (int(math.ceil(x / 8) * 8) for x in shape)
+        x = _aniso(gen, heads, (Tg, Hg, Wg), D, (0.05, 1.0))
+        x = x.reshape(heads, Tg, Hg, Wg, D)[:, :T, :H, :W].reshape(1, heads, T * H * W, D)
+    else:
+        (S,) = shape
+        n_seg = int(math.ceil(S / 16))
+        seg = torch.randn(heads, n_seg, 1, D, generator=gen) * 0.5
+        x = (seg.expand(heads, n_seg, 16, D).reshape(heads, n_seg * 16, D)[:, :S]
+             + 0.2 * torch.randn(heads, S, D, generator=gen)).reshape(1, heads, S, D)
+    return x.to(torch.bfloat16)
+
+
+def make_cross_inputs(case: CrossCase):
+    """q, do [1, h, Sq, D]; k, v [1, h, Sk, D] bf16, unpadded, each in its own order."""
+    out = {}
+    for i, (name, st, shape) in enumerate((("q", case.q_structure, case.q_shape),
+                                           ("k", case.k_structure, case.k_shape),
+                                           ("v", case.k_structure, case.k_shape),
+                                           ("do", case.q_structure, case.q_shape))):
+        gen = torch.Generator().manual_seed(case.seed + i)
+        out[name] = _side(gen, st, shape, case.heads, case.head_dim)
+    return out
+
+
 def _zoned(gen, heads, grid_p, D, amp):
     T, H, W = grid_p
     ZT, ZH, ZW = T // 8, H // 8, W // 8

@@ -45,7 +45,7 @@ import torch  # noqa: E402
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
-from inputs import ALL_CASES, make_inputs  # noqa: E402
+from inputs import ALL_CASES, CROSS_CASES, make_cross_inputs, make_inputs  # noqa: E402
 
 N_ROWS = 128  # output rows stored per head (a fixed random subset)
 
@@ -215,16 +215,76 @@ def run_uniform_case(bsa, case):
     return res
 
 
+def run_cross_case(bsa, case):
+    """flash_attn_bsa_cross (bsa_interface.py:1276-1392) on unpadded inputs.  Stores
+    the chunk-level selection of a bf16 and an fp32 pass and the fp32 output / dQ on
+    a fixed subset of query rows and dK / dV on a subset of key rows."""
+    from oracle.oracle import dense_to_bits
+
+    inp = make_cross_inputs(case)
+    q, k, v, do = inp["q"], inp["k"], inp["v"], inp["do"]
+    kw = dict(q_grid_size=case.q_shape if case.q_structure == "3d" else None,
+              k_grid_size=case.k_shape if case.k_structure == "3d" else None,
+              sparsity=case.sparsity, cdf_threshold=case.cdf_threshold,
+              chunk_size_q=case.chunk_size_q, chunk_size_k=case.chunk_size_k,
+              chunk_3d_shape_q=list(case.chunk_3d_q) if case.chunk_3d_q else None,
+              chunk_3d_shape_k=list(case.chunk_3d_k) if case.chunk_3d_k else None)
+    captured = []
+    orig = bsa.attn_fwd_bsa_varlen_triton
+
+    def skip(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2):
+        captured.append(dict(bi=block_indices.clone(), lens=lens.clone(), nk=k_.shape[2]))
+        return torch.zeros_like(q_), torch.zeros(q_.shape[:3])
+
+    def capture(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2):
+        captured.append(dict(bi=block_indices.clone(), lens=lens.clone(), nk=k_.shape[2]))
+        return orig(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2)
+
+    try:
+        bsa.attn_fwd_bsa_varlen_triton = skip
+        with torch.no_grad():
+            bsa.flash_attn_bsa_cross(q, k, v, case.q_structure, case.k_structure, **kw)
+        sel16 = captured.pop()
+        bsa.attn_fwd_bsa_varlen_triton = capture
+        q32, k32, v32 = (t.float().requires_grad_(True) for t in (q, k, v))
+        out = bsa.flash_attn_bsa_cross(q32, k32, v32, case.q_structure, case.k_structure, **kw)
+        (out * do.float()).sum().backward()
+        sel32 = captured.pop()
+    finally:
+        bsa.attn_fwd_bsa_varlen_triton = orig
+    ck = (case.chunk_size_k if case.k_structure == "1d"
+          else case.chunk_3d_k[0] * case.chunk_3d_k[1] * case.chunk_3d_k[2])
+    nk = sel32["nk"] // ck
+    dense16 = chunk_lists_to_dense(sel16["bi"].numpy(), sel16["lens"].numpy(), nk)
+    dense32 = chunk_lists_to_dense(sel32["bi"].numpy(), sel32["lens"].numpy(), nk)
+    res = dict(sel_chunks=dense_to_bits(dense16), sel_chunks_f32=dense_to_bits(dense32))
+    o = out.detach()[0].numpy()
+    grads = [t.grad[0].numpy() for t in (q32, k32, v32)]
+    rng = np.random.default_rng(1234)
+    rows_q = np.sort(rng.choice(case.Sq, size=min(case.Sq, N_ROWS), replace=False))
+    rows_k = np.sort(rng.choice(case.Sk, size=min(case.Sk, N_ROWS), replace=False))
+    res["rows_q"], res["rows_k"] = rows_q.astype(np.int64), rows_k.astype(np.int64)
+    res["o"], res["dq"] = o[:, rows_q], grads[0][:, rows_q]
+    res["dk"], res["dv"] = grads[1][:, rows_k], grads[2][:, rows_k]
+    res["sums"] = np.array([np.abs(x).astype(np.float64).sum() for x in [o] + grads])
+    return res
+
+
 def main():
     root = os.environ.get("PRISM_REFERENCE")
     if not root:
         sys.exit("set PRISM_REFERENCE to the root of a Prism checkout")
     dba, dbs, bsa = import_reference(root)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    names = sys.argv[1:] or list(ALL_CASES)
+    names = sys.argv[1:] or list(ALL_CASES) + list(CROSS_CASES)
     for name in names:
-        case = ALL_CASES[name]
         path = os.path.join(HERE, f"{name}.npz")
+        if name in CROSS_CASES:
+            res = run_cross_case(bsa, CROSS_CASES[name])
+            np.savez_compressed(path, **res)
+            print(f"{name}: cross -> {path} ({os.path.getsize(path)} B)")
+            continue
+        case = ALL_CASES[name]
         if case.uniform:
             res = run_uniform_case(bsa, case)
             np.savez_compressed(path, **res)

@@ -66,7 +66,7 @@ def test_uniform_selection_bit_exact(name, cuda):
     case = UNIFORM_CASES[name]
     inp = make_inputs(case)
     plan, q_re, k_re = _plan_and_gather(case, inp, cuda)
-    seq = plan.uniform["seq"]
+    seq = plan.uniform["seq_q"]
     n_rows = q_re.shape[1]
     # the gather is the oracle's permutation, with zero rows past the grid
     src_q = plan.src_idx.cpu().numpy()
@@ -76,9 +76,9 @@ def test_uniform_selection_bit_exact(name, cuda):
     bq, bk = plan.select(q_re, k_re)
     src_k = plan.src_idx_k.cpu().numpy()[:seq]
     valid_re = None if inp["valid"] is None else inp["valid"].numpy()[src_k]
-    rq, rk, _ = O.block_select_uniform(qb[:, src_q[:seq]], bits(inp["k"][0])[:, src_k], seq,
+    rq, rk, _ = O.block_select_uniform(qb[:, src_q[:seq]], bits(inp["k"][0])[:, src_k], seq, seq,
                                        plan.uniform["chunk_q"], plan.uniform["chunk_k"], valid_re,
-                                       case.sparsity, case.cdf_threshold)
+                                       valid_re, case.sparsity, case.cdf_threshold)
     nt, ntr = seq // 64, n_rows // 64
     gq = O.bits_to_dense(bq.cpu().numpy().view(np.uint32), ntr)
     gk = O.bits_to_dense(bk.cpu().numpy().view(np.uint32), ntr)
@@ -116,8 +116,8 @@ def test_flash_attn_bsa_3d_parity(name, cuda):
     valid_re = None if inp["valid"] is None else inp["valid"].numpy()[src_k]
     f = O.bf16_bits_to_f32
     qb, kb, vb, dob = (bits(inp[n][0]) for n in ("q", "k", "v", "do"))
-    bq, _, _ = O.block_select_uniform(qb[:, src_q], kb[:, src_k], S, _vol(case.chunk_q),
-                                      _vol(case.chunk_k), valid_re, case.sparsity,
+    bq, _, _ = O.block_select_uniform(qb[:, src_q], kb[:, src_k], S, S, _vol(case.chunk_q),
+                                      _vol(case.chunk_k), valid_re, valid_re, case.sparsity,
                                       case.cdf_threshold)
     qr, kr, vr = f(qb[:, src_q]), f(kb[:, src_k]), f(vb[:, src_k])
     o, _ = O.bsa_forward(qr, kr, vr, bq, valid_re)

@@ -62,9 +62,11 @@ def test_uniform_layout_matches_reference(name):
 
 def _select(r):
     case = r["case"]
-    return O.block_select_uniform(r["q"][:, r["src_q"]], r["k"][:, r["src_k"]], r["S"], r["cq"],
-                                  r["ck"], r["valid_re"], case.sparsity, case.cdf_threshold,
-                                  want_chunks=True)
+    # q is pooled under the key-order mask, as the reference does for q and k of
+    # one sequence (bsa_interface.py:609-610)
+    return O.block_select_uniform(r["q"][:, r["src_q"]], r["k"][:, r["src_k"]], r["S"], r["S"],
+                                  r["cq"], r["ck"], r["valid_re"], r["valid_re"], case.sparsity,
+                                  case.cdf_threshold, want_chunks=True)
 
 
 @pytest.mark.parametrize("name", list(UNIFORM_CASES))
