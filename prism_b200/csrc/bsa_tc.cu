@@ -968,6 +968,329 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ============================================================= dK / dV, N = 128
+// CTA = 128 keys (tiles 2p, 2p+1); per step TWO query tiles of the transposed
+// selection's union (N = 128; the last step holds one tile when the union is
+// odd).  TMEM: dK, dV (D f32 columns each), S^T and dP^T (128 f32 columns
+// each, single-buffered): S^T = K Q^T, dP^T = V dO^T; warpgroup w (w = query
+// tile w of the step) writes P^T and dS^T = P^T (dP^T - delta) as bf16 over
+// its own 64 columns [64 w, 64 w + 32) of them; dV += P^T dO and dK += dS^T Q
+// read them from TMEM.  Per step the tensor pipe runs S^T, dP^T, dV, dK with
+// N >= 128 (the math rate), and the issuer synchronises once per two query
+// tiles instead of once per tile.
+template <int D>
+struct Dkdv2Layout {
+  static constexpr int kRing = 2;                          // query-tile pairs in flight
+  static constexpr int kSub = D / 64;
+  static constexpr int kPair = kSub * 16384;               // 128 rows (two tiles) x D bf16
+  static constexpr int K = 0;                              // 128 keys
+  static constexpr int V = K + kPair;
+  static constexpr int Q = V + kPair;                      // kRing pairs of query tiles
+  static constexpr int DO = Q + kRing * kPair;
+  static constexpr int M = DO + kRing * kPair;             // kRing x 128 f32 (lse)
+  static constexpr int DL = M + kRing * 512;               // kRing x 128 f32 (delta)
+  static constexpr int BAR = DL + kRing * 512;
+  static constexpr int B_KV = 0, B_QF = 1, B_QE = 1 + kRing, B_SF = 1 + 2 * kRing,
+                       B_DPF = B_SF + 1, B_PF = B_DPF + 1, B_DSF = B_PF + 1, B_FIN = B_DSF + 1,
+                       B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
+  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
+  static constexpr int ABORT = TMEM_SLOT + 4;
+  static constexpr size_t kBytes = 1024 + ABORT + 4;
+  static constexpr int T_DK = 0, T_DV = D, T_S = 2 * D, T_DP = 2 * D + 128;
+  static_assert(T_DP + 128 <= 512, "TMEM budget");
+};
+
+// Pairs of consecutive union tiles: (t0, sel0, t1, sel1), t1 = -1 for a lone last tile.
+struct UnionPairIter {
+  UnionIter it;
+  __device__ __forceinline__ void init(const uint32_t* ra, const uint32_t* rb, int wq) {
+    it.init(ra, rb, wq);
+  }
+  __device__ __forceinline__ bool next(int& t0, int& s0, int& t1, int& s1) {
+    t0 = it.next(s0);
+    if (t0 < 0) return false;
+    t1 = it.next(s1);
+    if (t1 < 0) s1 = 0;
+    return true;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    dkdv2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                    const float* __restrict__ lse, const float* __restrict__ delta, int64_t Sq,
+                    int64_t Sk, int wq, float qk_scale, float sm_scale,
+                    const uint32_t* __restrict__ bits_k, const uint64_t* __restrict__ tile_bits,
+                    __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv) {
+  using L = Dkdv2Layout<D>;
+  constexpr int R = L::kRing;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const uint32_t sb = smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x, h = blockIdx.y;
+  const int64_t n_tiles = Sk / 64;
+  const int row_base = (int)((int64_t)h * Sk + (int64_t)pair * 128);  // key rows of this CTA
+  const int head_row = (int)((int64_t)h * Sq);                        // query rows of head h
+  auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
+  const uint32_t* row_a = bits_k + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
+  const uint32_t* row_b = row_a + wq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::B_KV), 1);
+    for (int i = 0; i < R; ++i) {
+      mbar_init(bar(L::B_QF + i), 1);
+      mbar_init(bar(L::B_QE + i), 1);
+    }
+    mbar_init(bar(L::B_SF), 1);
+    mbar_init(bar(L::B_DPF), 1);
+    mbar_init(bar(L::B_PF), 8);
+    mbar_init(bar(L::B_DSF), 8);
+    mbar_init(bar(L::B_FIN), 1);
+    mbar_init(bar(L::B_DRAIN), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kBwdMmaWarp) {
+    tmem_alloc(sb + L::TMEM_SLOT, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
+
+  if (warp == kBwdProducerWarp) {
+    if (lane == 0) {
+      mbar_expect_tx(bar(L::B_KV), 2 * 128 * D * 2);
+#pragma unroll
+      for (int s = 0; s < L::kSub; ++s)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          tma_load_2d(sb + L::K + s * 16384 + r * 8192, &tm_k, s * 64, row_base + r * 64, bar(L::B_KV));
+          tma_load_2d(sb + L::V + s * 16384 + r * 8192, &tm_v, s * 64, row_base + r * 64, bar(L::B_KV));
+        }
+      UnionPairIter it;
+      it.init(row_a, row_b, wq);
+      int n = 0, t0, s0, t1, s1;
+      while (it.next(t0, s0, t1, s1)) {
+        const int st = n & 1, cnt = t1 >= 0 ? 2 : 1;
+        if (n >= R && !mbar_wait(bar(L::B_QE + st), ((n >> 1) - 1) & 1, abort_flag, &g_tc_error,
+                                 kErrDkdvProducer))
+          break;
+        mbar_expect_tx(bar(L::B_QF + st), cnt * (2 * 64 * D * 2 + 2 * 256));
+        for (int u = 0; u < cnt; ++u) {
+          const int t = u ? t1 : t0;
+#pragma unroll
+          for (int s = 0; s < L::kSub; ++s) {
+            tma_load_2d(sb + L::Q + st * L::kPair + s * 16384 + u * 8192, &tm_q, s * 64,
+                        head_row + t * 64, bar(L::B_QF + st));
+            tma_load_2d(sb + L::DO + st * L::kPair + s * 16384 + u * 8192, &tm_do, s * 64,
+                        head_row + t * 64, bar(L::B_QF + st));
+          }
+          bulk_load(sb + L::M + st * 512 + u * 256, lse + head_row + (int64_t)t * 64, 256,
+                    bar(L::B_QF + st));
+          bulk_load(sb + L::DL + st * 512 + u * 256, delta + head_row + (int64_t)t * 64, 256,
+                    bar(L::B_QF + st));
+        }
+        ++n;
+      }
+      for (int m = (n > R ? n - R : 0); m < n; ++m)
+        mbar_wait(bar(L::B_QF + (m & 1)), (m >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
+      mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
+    }
+  } else if (warp == kBwdMmaWarp) {
+    // Issue order: S^T(n) | dK(n-1) | dP^T(n) | dV(n), ... , dK(last).
+    // The softmax computes P^T(n) while the tensor pipe runs dK(n-1) and dP^T(n),
+    // and dS^T(n) while it runs dV(n) and S^T(n+1).  S^T(n) overwrites P^T(n-1),
+    // read by dV(n-1); dP^T(n) overwrites dS^T(n-1), read by dK(n-1): both readers
+    // are issued earlier, and one thread's MMAs run in issue order.
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S2 = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t IDESC_S1 = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
+      const uint64_t dK = desc_k_sw128(sb + L::K), dV = desc_k_sw128(sb + L::V),
+                     dQk = desc_k_sw128(sb + L::Q), dDOk = desc_k_sw128(sb + L::DO),
+                     dQmn = desc_mn_sw128(sb + L::Q, 16384), dDOmn = desc_mn_sw128(sb + L::DO, 16384);
+      constexpr uint32_t kSlot = L::kPair >> 4;  // descriptor step of one ring slot
+      const int tiles = union_count(row_a, row_b, wq);
+      const int steps = (tiles + 1) >> 1;
+      // dK += dS^T Q for step j (slot j & 1), after its dS^T is written
+      auto dk_step = [&](int j) -> bool {
+        const uint32_t js = (uint32_t)j & 1u;
+        if (!mbar_wait(bar(L::B_DSF), js, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
+        tc_fence_after();
+        mma_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP, dQmn + js * kSlot,
+                                                IDESC_G, j > 0 ? 1u : 0u);
+        if (2 * j + 1 < tiles)
+          mma_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP + 64,
+                                                  dQmn + js * kSlot + 512, IDESC_G, 1u);
+        mma_commit(bar(L::B_QE + js));
+        return true;
+      };
+      bool ok = mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
+      tc_fence_after();
+      for (int n = 0; ok && n < steps; ++n) {
+        const uint32_t st = (uint32_t)n & 1u, ph = (uint32_t)n & 1u;
+        const bool two = 2 * n + 1 < tiles;
+        const uint32_t idn = two ? IDESC_S2 : IDESC_S1;
+        if (!mbar_wait(bar(L::B_QF + st), ((uint32_t)n >> 1) & 1u, abort_flag, &g_tc_error,
+                       kErrDkdvMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_S, dK, dQk + st * kSlot, idn, 0u);
+        mma_commit(bar(L::B_SF));
+        if (n > 0 && !dk_step(n - 1)) {
+          ok = false;
+          break;
+        }
+        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_DP, dV, dDOk + st * kSlot, idn, 0u);
+        mma_commit(bar(L::B_DPF));
+        if (!mbar_wait(bar(L::B_PF), ph, abort_flag, &g_tc_error, kErrDkdvMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // K = query rows: tile 0's P^T in columns [0, 32), tile 1's in [64, 96)
+        mma_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S, dDOmn + st * kSlot,
+                                                IDESC_G, n > 0 ? 1u : 0u);
+        if (two)
+          mma_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S + 64,
+                                                  dDOmn + st * kSlot + 512, IDESC_G, 1u);
+      }
+      if (ok && steps > 0) dk_step(steps - 1);
+      mma_commit(bar(L::B_FIN));
+      mma_commit(bar(L::B_DRAIN));
+      mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
+    }
+  } else {
+    // softmax warpgroups: wg w takes query tile w of each step (64 columns)
+    const int wg = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // key row within the CTA == TMEM lane
+    const int half = r >> 6;
+    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const bool kvalid = (tile_bits[2 * pair + half] >> (r & 63)) & 1ull;
+    UnionPairIter it;
+    it.init(row_a, row_b, wq);
+    int n = 0, t0, s0, t1, s1;
+    bool ok = true;
+    const float* sM = reinterpret_cast<const float*>(sm + L::M);
+    const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
+    while (it.next(t0, s0, t1, s1)) {
+      const int st = n & 1, ph = n & 1;
+      const int sel = wg ? s1 : s0;
+      const bool tile_on = (wg == 0 || t1 >= 0) && ((sel >> half) & 1);  // warp-uniform
+      const bool on = tile_on && kvalid;
+      if (!warp_wait(bar(L::B_QF + st), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax) ||
+          !warp_wait(bar(L::B_SF), ph, abort_flag, kErrDkdvSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float4* m_st = reinterpret_cast<const float4*>(sM + st * 128 + wg * 64);
+      const float4* d_st = reinterpret_cast<const float4*>(sDl + st * 128 + wg * 64);
+      const uint32_t tcol = wg * 64;
+      float p[64];
+      if (tile_on) {
+        tmem_load<2>(t_lane + L::T_S + tcol, p);
+#pragma unroll
+        for (int c4 = 0; c4 < 16; ++c4) {
+          const float4 mv = m_st[c4];
+          const float mm[4] = {mv.x * kRcpLn2, mv.y * kRcpLn2, mv.z * kRcpLn2, mv.w * kRcpLn2};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = 4 * c4 + j;
+            p[c] = on ? ex2(fmaf(p[c], qk_scale, -mm[j])) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) pk[c / 2] = pack_bf16(p[32 * hh + c], p[32 * hh + c + 1]);
+          tmem_st16(t_lane + L::T_S + tcol + 16 * hh, pk);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) p[c] = 0.0f;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = 0u;
+        tmem_st16(t_lane + L::T_S + tcol, pk);
+        tmem_st16(t_lane + L::T_S + tcol + 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_PF));
+      if (!warp_wait(bar(L::B_DPF), ph, abort_flag, kErrDkdvSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t pk[16];
+        if (tile_on) {
+          float dp[32];
+          tmem_load<1>(t_lane + L::T_DP + tcol + 32 * hh, dp);
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 dv4 = d_st[8 * hh + c4];
+            const int c = 4 * c4, pc = 32 * hh + c;
+            pk[c / 2] = pack_bf16(p[pc] * (dp[c] - dv4.x), p[pc + 1] * (dp[c + 1] - dv4.y));
+            pk[c / 2 + 1] = pack_bf16(p[pc + 2] * (dp[c + 2] - dv4.z), p[pc + 3] * (dp[c + 3] - dv4.w));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = 0u;
+        }
+        // dS^T columns [64 w + 16 hh, +16) overlap dP^T columns [64 w, 64 w + 32),
+        // which the first half has read already (hh = 0 writes over columns it read)
+        tmem_st16(t_lane + L::T_DP + tcol + 16 * hh, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_DSF));
+      ++n;
+    }
+    // epilogue: wg 0 writes dK (scaled by sm_scale), wg 1 writes dV
+    const int64_t grow = (int64_t)row_base + r;
+    __nv_bfloat16* out = (wg == 0 ? dk : dv) + grow * D;
+    const float scale = wg == 0 ? sm_scale : 1.0f;
+    const int tcolo = wg == 0 ? L::T_DK : L::T_DV;
+    if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDkdvSoftmax)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t raw[32], pk2[16];
+        tmem_ld32(t_lane + tcolo + c * 32, raw);
+        tmem_wait_ld_dep(raw);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk2[i] = pack_bf16(u2f(raw[2 * i]) * scale, u2f(raw[2 * i + 1]) * scale);
+        uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk2[4 * i], pk2[4 * i + 1], pk2[4 * i + 2], pk2[4 * i + 3]);
+      }
+    } else if (ok && n == 0) {
+      uint4* a = reinterpret_cast<uint4*>(out);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) a[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kBwdMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ======================================================================= dQ
 // CTA = 128 queries (tiles 2p, 2p+1); per step a PAIR of key tiles (N = 128):
 // S = Q [K_a; K_b]^T and dP = dO [V_a; V_b]^T in TMEM; the softmax warpgroups
@@ -1396,6 +1719,29 @@ prism_status_t launch_dkdv(const void* q, const void* k, const void* v, const vo
 }
 
 template <int D>
+prism_status_t launch_dkdv2(const void* q, const void* k, const void* v, const void* dout,
+                            const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
+                            float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
+                            void* dk, void* dv, cudaStream_t stream) {
+  const int64_t n_ktiles = Sk / 64;
+  const int wq = (int)((Sq / 64 + 31) / 32);  // words per bits_k row (query tiles)
+  const size_t sm = Dkdv2Layout<D>::kBytes > kMinSmem ? Dkdv2Layout<D>::kBytes : kMinSmem;
+  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
+  CUtensorMap mq, mk, mv, mdo;
+  PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mdo, dout, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(dkdv2_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "prism_bsa_bwd: smem attribute");
+  dkdv2_tc_kernel<D><<<dim3((unsigned)(n_ktiles / 2), heads), kBwdThreads, sm, stream>>>(
+      mq, mk, mv, mdo, lse, delta, Sq, Sk, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
+      (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
+  PRISM_CHECK_LAUNCH("prism_bsa_bwd_dkdv");
+  return PRISM_OK;
+}
+
+template <int D>
 prism_status_t launch_dq(const void* q, const void* k, const void* v, const void* dout,
                          const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
                          float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
@@ -1486,8 +1832,13 @@ static prism_status_t bwd_dkdv_qk(const void* q, const void* k, const void* v, c
   PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dk) &&
                       aligned16(dv) && aligned16(lse) && aligned16(delta),
                   "prism_bsa_bwd_dkdv: tensors must be 16-byte aligned");
+#ifndef PRISM_DKDV_N64
+  return D == 128 ? tc::launch_dkdv2<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream)
+                  : tc::launch_dkdv2<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
+#else
   return D == 128 ? tc::launch_dkdv<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream)
                   : tc::launch_dkdv<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
+#endif
 }
 
 static prism_status_t bwd_dq_qk(const void* q, const void* k, const void* v, const void* dout,
