@@ -1311,7 +1311,7 @@ struct DqLayout {
   static constexpr int V = K + kRingK * kPair;
   static constexpr int BAR = V + kRingV * kPair;
   static constexpr int B_QD = 0, B_KF = 1, B_KE = B_KF + kRingK, B_VF = B_KE + kRingK,
-                       B_VE = B_VF + kRingV, B_SF = B_VE + kRingV, B_SE = B_SF + 1, B_DPF = B_SE + 1,
+                       B_VE = B_VF + kRingV, B_SF = B_VE + kRingV, B_DPF = B_SF + 1,
                        B_DPE = B_DPF + 1, B_DSF = B_DPE + 1, B_DSE = B_DSF + 1, B_FIN = B_DSE + 1,
                        B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
@@ -1357,7 +1357,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(bar(L::B_VE + i), 1);
     }
     mbar_init(bar(L::B_SF), 1);
-    mbar_init(bar(L::B_SE), 8);
     mbar_init(bar(L::B_DPF), 1);
     mbar_init(bar(L::B_DPE), 8);
     mbar_init(bar(L::B_DSF), 8);
@@ -1425,8 +1424,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == kBwdMmaWarp) {
     // Issue order: S(0) dP(0) | S(1) dP(1) dQ(0) | S(2) dP(2) dQ(1) | ...
-    // S(n+1) waits until the softmax has read S(n), dP(n+1) until it has read
-    // dP(n), dQ(n) until dS(n) is written.
+    // S(n+1) and dP(n+1) wait until the softmax has read S(n) and dP(n) (one
+    // signal, B_DPE: it reads dP after S), dQ(n) until dS(n) is written.  The
+    // issuing thread keeps its loop minimal -- the tensor pipe's issue queue is
+    // shallow, so every instruction and wait between MMAs is time the pipe may
+    // idle: a counted loop (the tile sequence itself is not needed here) with
+    // the ring slots advanced incrementally.
     if (lane == 0) {
       constexpr uint32_t IDESC_2 = idesc_bf16(128, 128, false, false);
       constexpr uint32_t IDESC_1 = idesc_bf16(128, 64, false, false);
@@ -1434,54 +1437,56 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t dQ = desc_k_sw128(sb + L::Q), dDO = desc_k_sw128(sb + L::DO),
                      dKk = desc_k_sw128(sb + L::K), dVk = desc_k_sw128(sb + L::V),
                      dKmn = desc_mn_sw128(sb + L::K, 16384);
+      static_assert(RV == 2, "V ring arithmetic below assumes 2 slots");
+      constexpr uint32_t kSlot = L::kPair >> 4;  // descriptor step of one ring slot
+      const int tiles = union_count(row_a, row_b, wq);
+      const int steps = (tiles + 1) >> 1;
       bool ok = mbar_wait(bar(L::B_QD), 0, abort_flag, &g_tc_error, kErrDqMma);
       tc_fence_after();
-      UnionIter it;
-      it.init(row_a, row_b, wq);
-      int n = 0, sel = 0, prev_cnt = 0;
-      auto dq_step = [&](int j, int cnt) -> bool {
-        if (!mbar_wait(bar(L::B_DSF), j & 1, abort_flag, &g_tc_error, kErrDqMma)) return false;
+      // dQ += dS K for step j (K pair in ring slot `slot`)
+      auto dq_step = [&](int j, uint32_t slot, bool two) -> bool {
+        if (!mbar_wait(bar(L::B_DSF), (uint32_t)j & 1u, abort_flag, &g_tc_error, kErrDqMma)) return false;
         tc_fence_after();
-        const uint64_t bk = dKmn + (j % RK) * (L::kPair >> 4);
+        const uint64_t bk = dKmn + slot * kSlot;
         mma_ts_k64_mn(tmem + L::T_DQ, tmem + L::T_DS, bk, IDESC_G, j > 0 ? 1u : 0u);
-        if (cnt == 2) mma_ts_k64_mn(tmem + L::T_DQ, tmem + L::T_DS + 32, bk + (8192 >> 4), IDESC_G, 1u);
+        if (two) mma_ts_k64_mn(tmem + L::T_DQ, tmem + L::T_DS + 32, bk + (8192 >> 4), IDESC_G, 1u);
         mma_commit(bar(L::B_DSE));
-        mma_commit(bar(L::B_KE + j % RK));
+        mma_commit(bar(L::B_KE + slot));
         return true;
       };
-      while (ok) {
-        const int t0 = it.next(sel);
-        if (t0 < 0) break;
-        const int t1 = it.next(sel);
-        const int cnt = t1 >= 0 ? 2 : 1;
-        const uint32_t idn = cnt == 2 ? IDESC_2 : IDESC_1;
-        const int sk = n % RK, sv = n % RV;
-        if (!mbar_wait(bar(L::B_KF + sk), (n / RK) & 1, abort_flag, &g_tc_error, kErrDqMma) ||
-            (n > 0 && !mbar_wait(bar(L::B_SE), (n - 1) & 1, abort_flag, &g_tc_error, kErrDqMma))) {
+      uint32_t sk = 0, kpar = 0, psk = 0;  // K slot / phase of step n, K slot of step n - 1
+      for (int n = 0; ok && n < steps; ++n) {
+        const bool two = 2 * n + 1 < tiles;
+        const uint32_t idn = two ? IDESC_2 : IDESC_1, sv = (uint32_t)n & 1u;
+        if (!mbar_wait(bar(L::B_KF + sk), kpar, abort_flag, &g_tc_error, kErrDqMma) ||
+            (n > 0 && !mbar_wait(bar(L::B_DPE), (uint32_t)(n - 1) & 1u, abort_flag, &g_tc_error,
+                                 kErrDqMma))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_S, dQ, dKk + sk * (L::kPair >> 4), idn, 0u);
+        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_S, dQ, dKk + sk * kSlot, idn, 0u);
         mma_commit(bar(L::B_SF));
-        if (!mbar_wait(bar(L::B_VF + sv), (n / RV) & 1, abort_flag, &g_tc_error, kErrDqMma) ||
-            (n > 0 && !mbar_wait(bar(L::B_DPE), (n - 1) & 1, abort_flag, &g_tc_error, kErrDqMma))) {
+        if (!mbar_wait(bar(L::B_VF + sv), ((uint32_t)n >> 1) & 1u, abort_flag, &g_tc_error,
+                       kErrDqMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_DP, dDO, dVk + sv * (L::kPair >> 4), idn, 0u);
+        mma_kd<L::kSub, 16384, 16384>(tmem + L::T_DP, dDO, dVk + sv * kSlot, idn, 0u);
         mma_commit(bar(L::B_DPF));
         mma_commit(bar(L::B_VE + sv));
-        if (n > 0 && !dq_step(n - 1, prev_cnt)) {
+        if (n > 0 && !dq_step(n - 1, psk, true)) {  // only the last step can be a single tile
           ok = false;
           break;
         }
-        prev_cnt = cnt;
-        ++n;
-        if (t1 < 0) break;
+        psk = sk;
+        if (++sk == (uint32_t)RK) {
+          sk = 0;
+          kpar ^= 1u;
+        }
       }
-      if (ok && n > 0) dq_step(n - 1, prev_cnt);
+      if (ok && steps > 0) dq_step(steps - 1, psk, 2 * (steps - 1) + 1 < tiles);
       mma_commit(bar(L::B_FIN));
       mma_commit(bar(L::B_DRAIN));
       mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDqMma);
@@ -1514,9 +1519,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       float p[64];
       if (vb != 0ull) tmem_load<2>(t_lane + L::T_S + wg * 64, p);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_SE));
       if (vb == ~0ull) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) p[c] = ex2(fmaf(p[c], qk_scale, -mrow));
