@@ -563,81 +563,199 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         break;
       }
       tc_fence_after();
-      // pass 1: row maximum over the valid, selected keys (64 columns at a time)
-      float mx = -INFINITY;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const uint64_t vb = u ? vb1 : vb0;
-        if (vb == 0ull) continue;  // warp-uniform: the whole half-row of this tile is masked
-        float s[64];
-        tmem_load<2>(t_lane + L::T_S + u * 64, s);
-        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-        if (vb == ~0ull) {
-#pragma unroll
-          for (int c = 0; c < 64; c += 4) {
-            m0 = fmaxf(m0, s[c]);
-            m1 = fmaxf(m1, s[c + 1]);
-            m2 = fmaxf(m2, s[c + 2]);
-            m3 = fmaxf(m3, s[c + 3]);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if ((vb >> c) & 1ull) m0 = fmaxf(m0, s[c]);
-        }
-        mx = fmaxf(mx, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
-      }
-      mx *= qk_scale;
-      const bool need = mx > m + kRescaleThreshold;  // m = -inf: any valid key
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_new = need ? mx : m;
-        const float alpha = need ? ex2(m - m_new) : 1.0f;  // m = -inf -> 0
-        const bool o_live = __any_sync(0xffffffffu, need && m != -INFINITY);
-        l *= alpha;
-        m = m_new;
-        // every P V before this pair has completed: S_g(n) was issued after them
-        if (n > 0 && o_live) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t raw[32];
-            tmem_ld32(t_lane + L::T_O + c * 32, raw);
-            tmem_wait_ld_dep(raw);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
-            tmem_st32(t_lane + L::T_O + c * 32, raw);
-          }
-        }
-      }
-      // pass 2: p = exp2(s * scale - m) -> bf16 P over the first 64 columns of S
-      const float mb = (m == -INFINITY) ? 0.0f : m;
       float sum0 = 0.f, sum1 = 0.f;
+      // Exponentials against the running maximum m in one pass over S while this
+      // block's maximum is tracked; a row's first block (m = -inf) and a first key
+      // tile whose maximum exceeds m by more than the rescale threshold take two
+      // passes (maximum, then exponentials: S is still intact then).  If only the
+      // second key tile exceeds it, P of the first (<= 2^8, already in TMEM) and
+      // l, O are scaled to the new maximum and the second tile is recomputed from
+      // its scores (columns [64, 128), intact).  Without a rescale the result
+      // equals the two-pass form's bit for bit.
+      bool two_pass = __any_sync(0xffffffffu, m == -INFINITY);
+      uint32_t pk0[32];
+      if (!two_pass) {
+        float xmax = -INFINITY;
+        if (vb0 == 0ull) {
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const uint64_t vb = u ? vb1 : vb0;
-        uint32_t pk[32];
-        if (vb == 0ull) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pk[i] = 0u;
+          for (int i = 0; i < 32; ++i) pk0[i] = 0u;
         } else {
-          float s[64];
-          tmem_load<2>(t_lane + L::T_S + u * 64, s);
-          if (vb != ~0ull) {
+          float sv[64];
+          tmem_load<2>(t_lane + L::T_S, sv);
+          if (vb0 != ~0ull) {
 #pragma unroll
             for (int c = 0; c < 64; ++c)
-              if (!((vb >> c) & 1ull)) s[c] = -INFINITY;
+              if (!((vb0 >> c) & 1ull)) sv[c] = -INFINITY;
           }
+          float su0 = 0.f, su1 = 0.f;
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
-            const float p0 = ex2(fmaf(s[c], qk_scale, -mb));
-            const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mb));
-            sum0 += p0;
-            sum1 += p1;
-            pk[c / 2] = pack_bf16(p0, p1);
+            const float x0 = fmaf(sv[c], qk_scale, -m), x1 = fmaf(sv[c + 1], qk_scale, -m);
+            xmax = fmaxf(xmax, fmaxf(x0, x1));
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            su0 += p0;
+            su1 += p1;
+            pk0[c / 2] = pack_bf16(p0, p1);
+          }
+          sum0 = su0 + su1;
+        }
+        two_pass = __any_sync(0xffffffffu, xmax > kRescaleThreshold);
+      }
+      if (two_pass) {
+        sum0 = 0.f;
+        // pass 1: row maximum over the valid, selected keys (64 columns at a time)
+        float mx = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint64_t vb = u ? vb1 : vb0;
+          if (vb == 0ull) continue;  // warp-uniform: the whole half-row of this tile is masked
+          float s[64];
+          tmem_load<2>(t_lane + L::T_S + u * 64, s);
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+          if (vb == ~0ull) {
+#pragma unroll
+            for (int c = 0; c < 64; c += 4) {
+              m0 = fmaxf(m0, s[c]);
+              m1 = fmaxf(m1, s[c + 1]);
+              m2 = fmaxf(m2, s[c + 2]);
+              m3 = fmaxf(m3, s[c + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if ((vb >> c) & 1ull) m0 = fmaxf(m0, s[c]);
+          }
+          mx = fmaxf(mx, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
+        }
+        mx *= qk_scale;
+        const bool need = mx > m + kRescaleThreshold;  // m = -inf: any valid key
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_new = need ? mx : m;
+          const float alpha = need ? ex2(m - m_new) : 1.0f;  // m = -inf -> 0
+          const bool o_live = __any_sync(0xffffffffu, need && m != -INFINITY);
+          l *= alpha;
+          m = m_new;
+          // every P V before this pair has completed: S_g(n) was issued after them
+          if (n > 0 && o_live) {
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t raw[32];
+              tmem_ld32(t_lane + L::T_O + c * 32, raw);
+              tmem_wait_ld_dep(raw);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
+              tmem_st32(t_lane + L::T_O + c * 32, raw);
+            }
           }
         }
-        // P columns [32 u, 32 u + 32) overlap S columns [0, 64), which pass 2
-        // has already read for u = 0 and does not read again
-        tmem_st32(t_lane + L::T_S + u * 32, pk);
+        // pass 2: p = exp2(s * scale - m) -> bf16 P over the first 64 columns of S
+        const float mb = (m == -INFINITY) ? 0.0f : m;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint64_t vb = u ? vb1 : vb0;
+          uint32_t pk[32];
+          if (vb == 0ull) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pk[i] = 0u;
+          } else {
+            float s[64];
+            tmem_load<2>(t_lane + L::T_S + u * 64, s);
+            if (vb != ~0ull) {
+#pragma unroll
+              for (int c = 0; c < 64; ++c)
+                if (!((vb >> c) & 1ull)) s[c] = -INFINITY;
+            }
+#pragma unroll
+            for (int c = 0; c < 64; c += 2) {
+              const float p0 = ex2(fmaf(s[c], qk_scale, -mb));
+              const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mb));
+              sum0 += p0;
+              sum1 += p1;
+              pk[c / 2] = pack_bf16(p0, p1);
+            }
+          }
+          // P columns [32 u, 32 u + 32) overlap S columns [0, 64), which pass 2
+          // has already read for u = 0 and does not read again
+          tmem_st32(t_lane + L::T_S + u * 32, pk);
+        }
+      } else {
+        // P columns [0, 32) overlap S columns [0, 64) of the first key tile (read)
+        tmem_st32(t_lane + L::T_S, pk0);
+        float xmax = -INFINITY;
+        uint32_t pk1[32];
+        if (vb1 == 0ull) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk1[i] = 0u;
+        } else {
+          float sv[64];
+          tmem_load<2>(t_lane + L::T_S + 64, sv);
+          if (vb1 != ~0ull) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if (!((vb1 >> c) & 1ull)) sv[c] = -INFINITY;
+          }
+          float su0 = 0.f, su1 = 0.f;
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float x0 = fmaf(sv[c], qk_scale, -m), x1 = fmaf(sv[c + 1], qk_scale, -m);
+            xmax = fmaxf(xmax, fmaxf(x0, x1));
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            su0 += p0;
+            su1 += p1;
+            pk1[c / 2] = pack_bf16(p0, p1);
+          }
+          sum1 = su0 + su1;
+        }
+        const bool need = xmax > kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_new = need ? m + xmax : m;
+          const float alpha = need ? ex2(m - m_new) : 1.0f;
+          if (n > 0) {
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t raw[32];
+              tmem_ld32(t_lane + L::T_O + c * 32, raw);
+              tmem_wait_ld_dep(raw);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
+              tmem_st32(t_lane + L::T_O + c * 32, raw);
+            }
+          }
+          tmem_wait_st();
+          {
+            uint32_t raw[32];
+            tmem_ld32(t_lane + L::T_S, raw);
+            tmem_wait_ld_dep(raw);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              raw[i] = pack_bf16(u2f(raw[i] << 16) * alpha, u2f(raw[i] & 0xffff0000u) * alpha);
+            tmem_st32(t_lane + L::T_S, raw);
+          }
+          l = (l + sum0) * alpha;
+          sum0 = 0.f;
+          m = m_new;
+          sum1 = 0.f;
+          if (vb1 != 0ull) {
+            float sv[64];
+            tmem_load<2>(t_lane + L::T_S + 64, sv);
+            if (vb1 != ~0ull) {
+#pragma unroll
+              for (int c = 0; c < 64; ++c)
+                if (!((vb1 >> c) & 1ull)) sv[c] = -INFINITY;
+            }
+            float su0 = 0.f, su1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < 64; c += 2) {
+              const float p0 = ex2(fmaf(sv[c], qk_scale, -m)), p1 = ex2(fmaf(sv[c + 1], qk_scale, -m));
+              su0 += p0;
+              su1 += p1;
+              pk1[c / 2] = pack_bf16(p0, p1);
+            }
+            sum1 = su0 + su1;
+          }
+        }
+        // P columns [32, 64) overlap S columns [32, 64) of the first key tile (read)
+        tmem_st32(t_lane + L::T_S + 32, pk1);
       }
       l += sum0 + sum1;
       tmem_wait_st();
