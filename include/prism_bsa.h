@@ -177,15 +177,85 @@ prism_status_t prism_uniform_layout(int Tp, int Hp, int Wp, int ct, int ch, int 
  * bits_q [heads, Sq/64, ceil(Sk/2048)] (rows of padding tiles are zero) and
  * its transpose bits_k [heads, Sk/64, ceil(Sq/2048)].  mode as for
  * prism_block_select.  workspace: prism_block_select_uniform_workspace_bytes(
- * heads, seq_q/chunk_q, seq_k/chunk_k, D). */
+ * heads, seq_q/chunk_q, seq_k/chunk_k, D).
+ * Guided selection (flash_attn_bsa_3d_variance_guided / _audio_guided,
+ * bsa_interface.py:1179-1260, 1395-1501): k_weights [seq_k] fp32 or NULL
+ * replaces the key validity in the key pooling by per-row weights (sum of
+ * x*w / max(sum of w, 1), audio_weighted_mean_pooling_compression :902-970;
+ * see prism_audio_pool_weights); col_scale [seq_k/chunk_k] fp32 or NULL
+ * multiplies every score of key chunk c by col_scale[c] before the selection
+ * (score * score_modifier :626-627, score * (1 + boost) :764; see
+ * prism_guidance_scale). */
 size_t prism_block_select_uniform_workspace_bytes(int heads, int64_t n_chunks_q, int64_t n_chunks_k,
                                                   int D);
 prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t Sq,
                                           int64_t Sk, int D, int64_t seq_q, int64_t seq_k,
                                           int chunk_q, int chunk_k, const uint64_t* q_bits,
-                                          const uint64_t* k_bits, int mode, double sparsity,
+                                          const uint64_t* k_bits, const float* k_weights,
+                                          const float* col_scale, int mode, double sparsity,
                                           double cdf_threshold, void* workspace, uint32_t* bits_q,
                                           uint32_t* bits_k, cudaStream_t stream);
+
+/* Inputs of the guided selection.  Keys are in the key chunk order of
+ * prism_uniform_layout (chunk (ct, ch, cw), chunk_k = ct*ch*cw rows, the first
+ * seq_k rows real); k_bits [Sk/64] key validity (NULL = every row valid, the
+ * reference's valid_mask = None).
+ *
+ * prism_gather_values: per-token fp32 values x [T*H*W] on the grid (T, H, W)
+ * <= (Tp, Hp, Wp) into the chunk order (out[r] = x at src_idx[r], 0 at padding);
+ * the padding of wan_video_dit.py:301-306 fused with
+ * rearrange_THW_to_3d_block_1d (bsa_interface.py:1117-1121).
+ *
+ * prism_variance_density: compute_channel_variance_density
+ * (bsa_interface.py:973-1062) of v_re [heads, Sk, D] bf16 -> rho [seq_k/chunk_k]
+ * fp32 in [0, 1]: per chunk, the head-averaged V's spatial channel variance
+ * (variance over channels of the masked chunk means) plus temporal channel
+ * variance (mean over channels of the squared differences of consecutive
+ * masked frame means, ct frames of ch*cw rows, pairs with both frames
+ * non-empty), normalised by the maximum over chunks (floor 1e-6).  Sums are
+ * sequential fp32.  D a multiple of 32 up to 256.
+ *
+ * prism_audio_saliency: compute_block_audio_saliency (bsa_interface.py:
+ * 1065-1102) of the audio norms in chunk order: masked chunk means / their
+ * maximum (floor 1e-6).
+ *
+ * prism_audio_pool_weights: the per-row weights of Path B
+ * (audio_weighted_mean_pooling_compression, bsa_interface.py:902-970):
+ * w = 1 + lambda_w * a / max(1e-6, chunk max of valid a) on valid rows, 0 on
+ * invalid rows; pass to prism_block_select_uniform as k_weights.
+ *
+ * prism_guidance_scale: scale [n_chunks] = 1 + boost with
+ *   ext   = modifier[c] + variance_gamma * rho[c]  (terms present when non-NULL)
+ *   boost = audio_gamma * (g * saliency[c] + (1 - g) / n_chunks) + ext
+ * in that order of operations (_attention_bsa_audio_guided.forward,
+ * bsa_interface.py:744-764, variance term folded as :1467-1470; the
+ * variance-only path's 1 + gamma * rho, :1240-1245, is the case with
+ * saliency = modifier = NULL).  audio_gate: device scalar g (NULL = 1);
+ * saliency NULL = no audio term. */
+prism_status_t prism_gather_values(const float* x, int T, int H, int W, int Tp, int Hp, int Wp,
+                                   const int32_t* src_idx, int64_t n_rows, float* out,
+                                   cudaStream_t stream);
+prism_status_t prism_variance_density(const void* v_re, int heads, int64_t Sk, int D, int64_t seq_k,
+                                      int ct, int ch, int cw, const uint64_t* k_bits, float* rho,
+                                      cudaStream_t stream);
+prism_status_t prism_audio_saliency(const float* norms_re, int64_t seq_k, int chunk_k,
+                                    const uint64_t* k_bits, float* saliency, cudaStream_t stream);
+prism_status_t prism_audio_pool_weights(const float* norms_re, int64_t seq_k, int chunk_k,
+                                        const uint64_t* k_bits, float lambda_w, float* weights,
+                                        cudaStream_t stream);
+/* Chunk means of x_re [heads, S, D] bf16 over chunks of `chunk` consecutive rows
+ * (the first seq rows) -> out [heads, seq/chunk, D] fp32: with weights [seq] fp32
+ * the Path B form (sum of rounded x*w / max(sum of w, 1),
+ * audio_weighted_mean_pooling_compression, bsa_interface.py:902-970), else the
+ * mean over the rows valid in bits (NULL = all) / max(count, 1)
+ * (masked_mean_pooling_compression, :177-201).  The same pooling as the
+ * selection's. */
+prism_status_t prism_pool_chunks(const void* x_re, int heads, int64_t S, int D, int64_t seq,
+                                int chunk, const uint64_t* bits, const float* weights, float* out,
+                                cudaStream_t stream);
+prism_status_t prism_guidance_scale(int64_t n_chunks, const float* rho, float variance_gamma,
+                                    const float* saliency, const float* audio_gate, float audio_gamma,
+                                    const float* modifier, float* scale, cudaStream_t stream);
 
 /* Block-sparse attention forward over tile-ordered q/k/v [heads, S, D] bf16
  * (attn_fwd_bsa_varlen_triton + _attn_fwd_bsa_varlen_align,

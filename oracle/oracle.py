@@ -62,7 +62,11 @@ def lib():
         L.oracle_layout.restype = i64
         L.oracle_block_select.argtypes = [P, P, i32, i64, i32, P, i64, P, i32, f64, f64, P, P, P]
         L.oracle_block_select_uniform.argtypes = [P, P, i32, i64, i64, i32, i64, i64, i32, i32, P,
-                                                  P, i32, f64, f64, P, P, P]
+                                                  P, P, P, i32, f64, f64, P, P, P]
+        L.oracle_variance_density.argtypes = [P, i32, i64, i32, i64, i32, i32, i32, P, P]
+        L.oracle_audio_saliency.argtypes = [P, i64, i32, P, P]
+        L.oracle_audio_pool_weights.argtypes = [P, i64, i32, P, f32, P]
+        L.oracle_guidance_scale.argtypes = [i64, P, f32, P, f32, f32, P, P]
         _lib = L
     return _lib
 
@@ -187,12 +191,15 @@ def uniform_layout(grid_padded, chunk, n_rows=None):
 
 
 def block_select_uniform(q_re_bits, k_re_bits, seq_q, seq_k, chunk_q, chunk_k, q_valid, k_valid,
-                         sparsity, cdf_threshold, want_chunks=False):
+                         sparsity, cdf_threshold, want_chunks=False, k_weights=None,
+                         col_scale=None):
     """Uniform-path selection (oracle_block_select_uniform).  q_re_bits [h, Sq, D]
     in the q chunk order, k_re_bits [h, Sk, D] in the key chunk order (bf16 bits);
     q_valid [Sq] / k_valid [Sk]: rows the q / k pooling counts and key validity
-    (None = every row).  Returns (bits_q [h, Sq/64, ceil(Sk/2048)], bits_k
-    [h, Sk/64, ceil(Sq/2048)], sel_chunks [h, nq, nk] or None)."""
+    (None = every row).  Guided selection: k_weights [seq_k] f32 (Path B key
+    pooling weights) and col_scale [nk] f32 (per-key-chunk score scale).
+    Returns (bits_q [h, Sq/64, ceil(Sk/2048)], bits_k [h, Sk/64, ceil(Sq/2048)],
+    sel_chunks [h, nq, nk] or None)."""
     q_re_bits = np.ascontiguousarray(q_re_bits, np.uint16)
     k_re_bits = np.ascontiguousarray(k_re_bits, np.uint16)
     heads, Sq, D = q_re_bits.shape
@@ -203,13 +210,58 @@ def block_select_uniform(q_re_bits, k_re_bits, seq_q, seq_k, chunk_q, chunk_k, q
     sel = (np.zeros((heads, seq_q // chunk_q, seq_k // chunk_k), np.uint8) if want_chunks else None)
     q_valid = None if q_valid is None else np.ascontiguousarray(q_valid, np.uint8)
     k_valid = None if k_valid is None else np.ascontiguousarray(k_valid, np.uint8)
+    k_weights = None if k_weights is None else np.ascontiguousarray(k_weights, np.float32)
+    col_scale = None if col_scale is None else np.ascontiguousarray(col_scale, np.float32)
     mode = selection_mode(sparsity, cdf_threshold)
     lib().oracle_block_select_uniform(
         _p(q_re_bits), _p(k_re_bits), heads, Sq, Sk, D, seq_q, seq_k, chunk_q, chunk_k,
-        _p(q_valid), _p(k_valid), mode, float(sparsity if sparsity is not None else 0.0),
+        _p(q_valid), _p(k_valid), _p(k_weights), _p(col_scale), mode,
+        float(sparsity if sparsity is not None else 0.0),
         float(cdf_threshold if cdf_threshold is not None else 0.0), _p(bits_q), _p(bits_k),
         _p(sel))
     return bits_q, bits_k, sel
+
+
+# ------------------------------------------------------------ guided selection
+def variance_density(v_re_bits, seq_k, chunk, k_valid):
+    """oracle_variance_density: rho [seq_k / chunk volume] f32 of chunk-ordered V
+    [h, Sk, D] (bf16 bits); chunk = (ct, ch, cw); k_valid [Sk] or None."""
+    v = np.ascontiguousarray(v_re_bits, np.uint16)
+    heads, Sk, D = v.shape
+    ct, ch, cw = (int(c) for c in chunk)
+    rho = np.zeros(seq_k // (ct * ch * cw), np.float32)
+    kv = None if k_valid is None else np.ascontiguousarray(k_valid, np.uint8)
+    lib().oracle_variance_density(_p(v), heads, Sk, D, seq_k, ct, ch, cw, _p(kv), _p(rho))
+    return rho
+
+
+def audio_saliency(norms_re, seq_k, chunk, k_valid):
+    """oracle_audio_saliency: masked chunk means of the norms / their max."""
+    x = np.ascontiguousarray(norms_re, np.float32)
+    out = np.zeros(seq_k // chunk, np.float32)
+    kv = None if k_valid is None else np.ascontiguousarray(k_valid, np.uint8)
+    lib().oracle_audio_saliency(_p(x), seq_k, chunk, _p(kv), _p(out))
+    return out
+
+
+def audio_pool_weights(norms_re, seq_k, chunk, k_valid, lambda_w):
+    """oracle_audio_pool_weights: Path B per-row key pooling weights [seq_k] f32."""
+    x = np.ascontiguousarray(norms_re, np.float32)
+    out = np.zeros(seq_k, np.float32)
+    kv = None if k_valid is None else np.ascontiguousarray(k_valid, np.uint8)
+    lib().oracle_audio_pool_weights(_p(x), seq_k, chunk, _p(kv), float(lambda_w), _p(out))
+    return out
+
+
+def guidance_scale(n, rho=None, variance_gamma=0.0, saliency=None, gate=1.0, audio_gamma=0.0,
+                   modifier=None):
+    """oracle_guidance_scale: 1 + boost per key chunk."""
+    f = lambda a: None if a is None else np.ascontiguousarray(a, np.float32)
+    rho, saliency, modifier = f(rho), f(saliency), f(modifier)
+    out = np.zeros(n, np.float32)
+    lib().oracle_guidance_scale(n, _p(rho), float(variance_gamma), _p(saliency), float(gate),
+                                float(audio_gamma), _p(modifier), _p(out))
+    return out
 
 
 def bits_to_dense(bits: np.ndarray, n_cols: int) -> np.ndarray:

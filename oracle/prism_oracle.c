@@ -17,7 +17,13 @@
  *                        dynamic_block_attention.py:173-188, 256-319
  *   oracle_block_select_uniform
  *                        bsa_interface.py:164-201, 203-207, 235-304, 600-633
- *                        (uniform fixed-shape path, flash_attn_bsa_3d :1123-1176)
+ *                        (uniform fixed-shape path, flash_attn_bsa_3d :1123-1176;
+ *                        guided: k pooling weights :902-970, score scale :626-627,
+ *                        :736-764)
+ *   oracle_variance_density   bsa_interface.py:973-1062
+ *   oracle_audio_saliency     bsa_interface.py:1065-1102
+ *   oracle_audio_pool_weights bsa_interface.py:902-970 (the weights)
+ *   oracle_guidance_scale     bsa_interface.py:744-764, 1240-1245, 1467-1470
  *
  * Floating-point order.  The reference leaves summation order to torch; this
  * restatement fixes one order (the one the CUDA kernels use) so that GPU and
@@ -676,8 +682,9 @@ void oracle_block_select(const uint16_t* q_re, const uint16_t* k_re, int heads, 
 void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int heads, int64_t Sq,
                                  int64_t Sk, int D, int64_t seq_q, int64_t seq_k, int chunk_q,
                                  int chunk_k, const uint8_t* q_valid, const uint8_t* k_valid,
-                                 int mode, double sparsity, double cdf, uint32_t* bits_q,
-                                 uint32_t* bits_k, uint8_t* sel_chunks) {
+                                 const float* k_weights, const float* col_scale, int mode,
+                                 double sparsity, double cdf, uint32_t* bits_q, uint32_t* bits_k,
+                                 uint8_t* sel_chunks) {
   const int64_t NQ_tiles = Sq / 64, NK_tiles = Sk / 64;
   const int64_t WK = (NK_tiles + 31) / 32, WQ = (NQ_tiles + 31) / 32;
   const int64_t nq = seq_q / chunk_q, nk = seq_k / chunk_k;
@@ -707,6 +714,19 @@ void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int
       const uint8_t* valid = pass ? k_valid : q_valid;
       float* out = pass ? kc : qc;
       for (int64_t c = 0; c < n; ++c) {
+        if (pass && k_weights) { /* Path B: sum of rounded x*w / max(sum w, 1) */
+          for (int d = 0; d < D; ++d) {
+            float sum = 0.0f, wsum = 0.0f;
+            for (int i = 0; i < chunk; ++i) {
+              const int64_t s = c * chunk + i;
+              const float prod = bf16_to_f32(x[s * D + d]) * k_weights[s];
+              sum = sum + prod;
+              wsum = wsum + k_weights[s];
+            }
+            out[c * D + d] = sum / (wsum < 1.0f ? 1.0f : wsum);
+          }
+          continue;
+        }
         int cnt = 0;
         for (int d = 0; d < D; ++d) out[c * D + d] = 0.0f;
         for (int i = 0; i < chunk; ++i) {
@@ -725,7 +745,7 @@ void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int
       for (int64_t b = 0; b < nk; ++b) {
         float acc = 0.0f;
         for (int d = 0; d < D; ++d) acc = fmaf(qc[a * D + d], kc[b * D + d], acc);
-        score[b] = acc;
+        score[b] = col_scale ? acc * col_scale[b] : acc;
       }
       const int64_t n_eff = select_row(score, nk, mode, k_topk, ub, scale, pf, arr);
       if (sel_chunks) memset(sel_chunks + ((int64_t)h * nq + a) * nk, 0, nk);
@@ -749,4 +769,141 @@ void oracle_block_select_uniform(const uint16_t* q_re, const uint16_t* k_re, int
   free(score);
   free(arr);
   free(tile_cnt);
+}
+
+/* ------------------------------------------------------ guided selection
+ * Keys in chunk order; k_valid [seq_k] u8 or NULL (= all rows valid).  Same
+ * operation order as the CUDA kernels (sequential fp32 sums). */
+
+/* compute_channel_variance_density (bsa_interface.py:973-1062): per chunk of
+ * ct frames x (ch*cw) rows, x_avg = (sum over heads) / heads; masked chunk and
+ * frame channel means / max(count, 1); spatial = mean_d (cm_d - mean_d cm)^2;
+ * temporal = mean_d (sum over pairs of non-empty consecutive frames of the
+ * squared frame-mean difference) / max(pairs, 1); rho = combined / max(max, 1e-6). */
+void oracle_variance_density(const uint16_t* v_re, int heads, int64_t Sk, int D, int64_t seq_k,
+                             int ct, int ch, int cw, const uint8_t* k_valid, float* rho) {
+  const int chunk = ct * ch * cw, frame = ch * cw;
+  const int64_t n = seq_k / chunk;
+  float* cm = (float*)malloc(sizeof(float) * D);
+  float* tv = (float*)malloc(sizeof(float) * D);
+  for (int64_t c = 0; c < n; ++c) {
+    for (int d = 0; d < D; ++d) {
+      float csum = 0.0f, fsum = 0.0f, prev = 0.0f, tsum = 0.0f;
+      int ccnt = 0, fcnt = 0, pairs = 0, prev_ok = 0;
+      for (int i = 0; i < chunk; ++i) {
+        const int64_t r = c * chunk + i;
+        if (!k_valid || k_valid[r]) {
+          float xs = 0.0f;
+          for (int h = 0; h < heads; ++h) xs = xs + bf16_to_f32(v_re[((int64_t)h * Sk + r) * D + d]);
+          const float xa = xs / (float)heads;
+          csum = csum + xa;
+          fsum = fsum + xa;
+          ++ccnt;
+          ++fcnt;
+        }
+        if ((i + 1) % frame == 0) {
+          const float fm = fsum / (fcnt > 0 ? (float)fcnt : 1.0f);
+          const int ok = fcnt > 0;
+          if (i + 1 > frame && ok && prev_ok) {
+            const float df = fm - prev;
+            tsum = tsum + df * df;
+          }
+          if (i + 1 > frame) pairs += ok && prev_ok;
+          prev = fm;
+          prev_ok = ok;
+          fsum = 0.0f;
+          fcnt = 0;
+        }
+      }
+      cm[d] = csum / (ccnt > 0 ? (float)ccnt : 1.0f);
+      tv[d] = ct > 1 ? tsum / (pairs > 0 ? (float)pairs : 1.0f) : 0.0f;
+    }
+    float s = 0.0f;
+    for (int d = 0; d < D; ++d) s = s + cm[d];
+    const float g = s / (float)D;
+    float sv = 0.0f, st = 0.0f;
+    for (int d = 0; d < D; ++d) {
+      const float dv = cm[d] - g;
+      sv = sv + dv * dv;
+    }
+    for (int d = 0; d < D; ++d) st = st + tv[d];
+    const float spatial = sv / (float)D;
+    const float temporal = ct > 1 ? st / (float)D : 0.0f;
+    rho[c] = spatial + temporal;
+  }
+  float mx = -INFINITY;
+  for (int64_t c = 0; c < n; ++c) mx = rho[c] > mx ? rho[c] : mx;
+  if (mx < 1e-6f) mx = 1e-6f;
+  for (int64_t c = 0; c < n; ++c) rho[c] = rho[c] / mx;
+  free(cm);
+  free(tv);
+}
+
+/* compute_block_audio_saliency (bsa_interface.py:1065-1102): masked chunk means
+ * of the norms / max(max, 1e-6). */
+void oracle_audio_saliency(const float* norms_re, int64_t seq_k, int chunk, const uint8_t* k_valid,
+                           float* out) {
+  const int64_t n = seq_k / chunk;
+  float mx = -INFINITY;
+  for (int64_t c = 0; c < n; ++c) {
+    float s = 0.0f;
+    int cnt = 0;
+    for (int i = 0; i < chunk; ++i) {
+      const int64_t r = c * chunk + i;
+      if (k_valid && !k_valid[r]) continue;
+      s = s + norms_re[r];
+      ++cnt;
+    }
+    out[c] = s / (cnt > 0 ? (float)cnt : 1.0f);
+    mx = out[c] > mx ? out[c] : mx;
+  }
+  if (mx < 1e-6f) mx = 1e-6f;
+  for (int64_t c = 0; c < n; ++c) out[c] = out[c] / mx;
+}
+
+/* Path B weights (audio_weighted_mean_pooling_compression, bsa_interface.py:944-961):
+ * valid rows 1 + lambda * a / max(1e-6, chunk max of valid a), invalid rows 0. */
+void oracle_audio_pool_weights(const float* norms_re, int64_t seq_k, int chunk,
+                               const uint8_t* k_valid, float lambda_w, float* w) {
+  for (int64_t c = 0; c < seq_k / chunk; ++c) {
+    float mx = -1e9f;
+    for (int i = 0; i < chunk; ++i) {
+      const int64_t r = c * chunk + i;
+      if ((!k_valid || k_valid[r]) && norms_re[r] > mx) mx = norms_re[r];
+    }
+    if (mx < 1e-6f) mx = 1e-6f;
+    for (int i = 0; i < chunk; ++i) {
+      const int64_t r = c * chunk + i;
+      w[r] = (!k_valid || k_valid[r]) ? 1.0f + lambda_w * (norms_re[r] / mx) : 0.0f;
+    }
+  }
+}
+
+/* 1 + boost per key chunk (_attention_bsa_audio_guided.forward, bsa_interface.py:
+ * 744-764, with the variance term folded into the external modifier as :1467-1470;
+ * the variance-only scale 1 + gamma * rho, :1240-1245, is rho alone). */
+void oracle_guidance_scale(int64_t n, const float* rho, float var_gamma, const float* sal,
+                           float gate, float audio_gamma, const float* modifier, float* scale) {
+  const float uni = (float)(1.0 / (double)n);
+  for (int64_t c = 0; c < n; ++c) {
+    int has_ext = 0;
+    float ext = 0.0f;
+    if (modifier) {
+      ext = modifier[c];
+      has_ext = 1;
+    }
+    if (rho) {
+      const float t = var_gamma * rho[c];
+      ext = has_ext ? ext + t : t;
+      has_ext = 1;
+    }
+    float boost = 0.0f;
+    if (sal) {
+      const float a = gate * sal[c];
+      const float b = (1.0f - gate) * uni;
+      boost = audio_gamma * (a + b);
+    }
+    if (has_ext) boost = boost + ext;
+    scale[c] = 1.0f + boost;
+  }
 }

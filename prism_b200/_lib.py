@@ -35,7 +35,13 @@ SIGNATURES = {
     "prism_block_select": (_I, [_P, _P, _I, _I64, _I, _P, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
     "prism_uniform_layout": (_I, [_I, _I, _I, _I, _I, _I, _I64, _P, _P, _P]),
     "prism_block_select_uniform_workspace_bytes": (_SZ, [_I, _I64, _I64, _I]),
-    "prism_block_select_uniform": (_I, [_P, _P, _I, _I64, _I64, _I, _I64, _I64, _I, _I, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
+    "prism_block_select_uniform": (_I, [_P, _P, _I, _I64, _I64, _I, _I64, _I64, _I, _I, _P, _P, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
+    "prism_gather_values": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _I64, _P, _P]),
+    "prism_variance_density": (_I, [_P, _I, _I64, _I, _I64, _I, _I, _I, _P, _P, _P]),
+    "prism_audio_saliency": (_I, [_P, _I64, _I, _P, _P, _P]),
+    "prism_audio_pool_weights": (_I, [_P, _I64, _I, _P, _F, _P, _P]),
+    "prism_guidance_scale": (_I, [_I64, _P, _F, _P, _P, _F, _P, _P, _P]),
+    "prism_pool_chunks": (_I, [_P, _I, _I64, _I, _I64, _I, _P, _P, _P, _P]),
     "prism_bsa_fwd_qk": (_I, [_P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_qk": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
@@ -54,7 +60,9 @@ KERNELS = {
     "prism_scatter_rows": 1, "prism_block_select": 4, "prism_bsa_fwd": 1, "prism_bsa_bwd": 3,
     "prism_bsa_bwd_delta": 1, "prism_bsa_bwd_dkdv": 1, "prism_bsa_bwd_dq": 1,
     "prism_bsa_bwd_noalloc": 3, "prism_uniform_layout": 1, "prism_block_select_uniform": 4,
-    "prism_bsa_fwd_qk": 1, "prism_bsa_bwd_qk": 3,
+    "prism_bsa_fwd_qk": 1, "prism_bsa_bwd_qk": 3, "prism_gather_values": 1,
+    "prism_variance_density": 2, "prism_audio_saliency": 2, "prism_audio_pool_weights": 1,
+    "prism_guidance_scale": 1, "prism_pool_chunks": 1,
 }
 launch_count = 0
 

@@ -16,6 +16,10 @@ dispatch one level up (pad to the chunk, valid mask, attention, unpad) on
 UNPADDED tokens, with the padding and both permutations fused into the
 gather / scatter kernels.
 
+``flash_attn_bsa_3d_variance_guided`` / ``flash_attn_bsa_3d_audio_guided``
+(bsa_interface.py:1179-1260, 1395-1501) add a per-key-chunk score factor
+(prism_b200/guidance.py) to the same selection.
+
 ``flash_attn_bsa_cross`` (bsa_interface.py:1276-1392) is the cross-modal form
 (3D video and/or 1D audio queries and keys, each side padded to its own chunk)
 on the same plan and kernels.
@@ -35,6 +39,7 @@ import torch
 
 from . import ops
 from .dynamic_block_attention import SparsePlan, _BsaFunction, _check_head_dim, _hsd
+from .guidance import make_guidance
 
 _TILE = 64
 _PAIR = 128  # the attention kernels work on whole 128-row tile pairs
@@ -92,22 +97,8 @@ def build_uniform_plan(grid, grid_padded, chunk_q, chunk_k, D: int, device, *, s
                       grid_k=grid_k, grid_padded_k=grid_padded_k)
 
 
-def flash_attn_bsa_3d(
-    q: torch.Tensor,  # [B, H, Sq, D]
-    k: torch.Tensor,  # [B, H, Skv, D]
-    v: torch.Tensor,  # [B, H, Skv, D]
-    latent_shape_q,
-    latent_shape_k,
-    sparsity: Optional[float] = 0.875,
-    cdf_threshold: Optional[float] = None,
-    chunk_3d_shape_q: Sequence[int] = (4, 4, 8),
-    chunk_3d_shape_k: Sequence[int] = (4, 4, 8),
-    valid_mask: Optional[torch.Tensor] = None,  # [Skv] bool, True = valid token
-) -> torch.Tensor:
-    """Uniform fixed-shape BSA; returns [B, H, Sq, D] in THW order
-    (bsa_interface.py:1123-1176).  Batches are independent heads here.  valid_mask
-    masks the keys (rearranged with the key chunk, :1160-1162); q is pooled under it
-    when q and k have the same length (:609-610), else over every row."""
+def _bsa_3d(q, k, v, latent_shape_q, latent_shape_k, sparsity, cdf_threshold, chunk_3d_shape_q,
+            chunk_3d_shape_k, valid_mask, guidance_kw=None):
     B, Hn, Sq, head_dim_q = q.shape
     _, _, Sk, head_dim_k = k.shape
     assert head_dim_q == head_dim_k
@@ -128,9 +119,89 @@ def flash_attn_bsa_3d(
     plan = build_uniform_plan(gq, gq, chunk_3d_shape_q, chunk_3d_shape_k, head_dim_q, q.device,
                               sparsity=sparsity, cdf_threshold=cdf_threshold,
                               valid_mask=valid_mask, grid_k=gk, grid_padded_k=gk, q_pool=q_pool)
+    if guidance_kw is not None:
+        if B != 1:
+            raise NotImplementedError("guided selection runs batch 1 (the reference's statistics "
+                                      "read batch 0, bsa_interface.py:1033)")
+        nk = Sk // _chunk_volume(chunk_3d_shape_k)
+        plan.uniform["guidance"] = make_guidance(chunk_3d_shape_k, n_chunks_k=nk, device=q.device,
+                                                 **guidance_kw)
     fold = lambda t: t.reshape(1, B * Hn, t.shape[2], t.shape[3])
     out = _BsaFunction.apply(fold(q), fold(k), fold(v), plan, "bhsd")
     return out.view(B, Hn, Sq, head_dim_q)
+
+
+def flash_attn_bsa_3d(
+    q: torch.Tensor,  # [B, H, Sq, D]
+    k: torch.Tensor,  # [B, H, Skv, D]
+    v: torch.Tensor,  # [B, H, Skv, D]
+    latent_shape_q,
+    latent_shape_k,
+    sparsity: Optional[float] = 0.875,
+    cdf_threshold: Optional[float] = None,
+    chunk_3d_shape_q: Sequence[int] = (4, 4, 8),
+    chunk_3d_shape_k: Sequence[int] = (4, 4, 8),
+    valid_mask: Optional[torch.Tensor] = None,  # [Skv] bool, True = valid token
+) -> torch.Tensor:
+    """Uniform fixed-shape BSA; returns [B, H, Sq, D] in THW order
+    (bsa_interface.py:1123-1176).  Batches are independent heads here.  valid_mask
+    masks the keys (rearranged with the key chunk, :1160-1162); q is pooled under it
+    when q and k have the same length (:609-610), else over every row."""
+    return _bsa_3d(q, k, v, latent_shape_q, latent_shape_k, sparsity, cdf_threshold,
+                   chunk_3d_shape_q, chunk_3d_shape_k, valid_mask)
+
+
+def flash_attn_bsa_3d_variance_guided(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    latent_shape_q,
+    latent_shape_k,
+    variance_boost_gamma: float = 1.0,
+    sparsity: Optional[float] = 0.875,
+    cdf_threshold: Optional[float] = None,
+    chunk_3d_shape_q: Sequence[int] = (4, 4, 4),
+    chunk_3d_shape_k: Sequence[int] = (4, 4, 4),
+    valid_mask: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """flash_attn_bsa_3d with each key chunk's scores scaled by 1 + gamma * rho_j,
+    rho the channel-variance density of V (bsa_interface.py:1179-1260)."""
+    return _bsa_3d(q, k, v, latent_shape_q, latent_shape_k, sparsity, cdf_threshold,
+                   chunk_3d_shape_q, chunk_3d_shape_k, valid_mask,
+                   guidance_kw=dict(variance_gamma=float(variance_boost_gamma)))
+
+
+def flash_attn_bsa_3d_audio_guided(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    latent_shape_q,
+    latent_shape_k,
+    audio_token_norms: Optional[torch.Tensor] = None,
+    audio_gate_value=None,
+    audio_boost_gamma=None,
+    sparsity: Optional[float] = 0.875,
+    cdf_threshold: Optional[float] = None,
+    chunk_3d_shape_q: Sequence[int] = (4, 4, 4),
+    chunk_3d_shape_k: Sequence[int] = (4, 4, 4),
+    valid_mask: Optional[torch.Tensor] = None,
+    audio_weighted_lambda: float = 0.0,
+    score_modifier: Optional[torch.Tensor] = None,
+    variance_boost_gamma: float = 0.0,
+) -> torch.Tensor:
+    """flash_attn_bsa_3d with audio-saliency score modulation
+    (bsa_interface.py:1395-1501): scores of key chunk j scaled by
+    1 + gamma_a * (g * S_j + (1 - g) / N) [+ gamma_v * rho_j] [+ score_modifier_j],
+    S the block saliency of audio_token_norms (per key token, THW order; None = no
+    audio term), keys pooled with the audio weights when audio_weighted_lambda > 0
+    (Path B)."""
+    return _bsa_3d(q, k, v, latent_shape_q, latent_shape_k, sparsity, cdf_threshold,
+                   chunk_3d_shape_q, chunk_3d_shape_k, valid_mask,
+                   guidance_kw=dict(variance_gamma=float(variance_boost_gamma or 0.0),
+                                    audio_token_norms=audio_token_norms,
+                                    audio_gate=audio_gate_value, audio_gamma=audio_boost_gamma,
+                                    audio_weighted_lambda=float(audio_weighted_lambda or 0.0),
+                                    score_modifier=score_modifier))
 
 
 def _structure_grid(structure: str, n_tokens: int, grid_size, chunk_1d: int, chunk_3d):
@@ -225,12 +296,20 @@ def run_bsa_uniform(
     chunk_3d_shape_k: Sequence[int] = (4, 4, 4),
     layout: str = "bhsd",
     return_plan: bool = False,
+    audio_token_norms: Optional[torch.Tensor] = None,
+    audio_gate=None,
+    audio_boost_gamma=None,
+    audio_weighted_lambda: float = 0.0,
+    variance_boost_gamma: float = 0.0,
 ):
-    """The plain-BSA branch of the uniform dispatch (wan_video_dit.py:470-560) on
-    unpadded tokens: q, k, v [1, H, T*H*W, D] (layout="bhsd") or [1, T*H*W, H, D]
-    (layout="bshd").  Pads each axis to the larger chunk extent; the padded
-    tokens are masked exactly when padding was needed (valid_mask is None
-    otherwise, wan_video_dit.py:485-507).  Output has q's layout."""
+    """The uniform dispatch (wan_video_dit.py:470-560, 637-672) on unpadded tokens:
+    q, k, v [1, H, T*H*W, D] (layout="bhsd") or [1, T*H*W, H, D] (layout="bshd").
+    Pads each axis to the larger chunk extent; the padded tokens are masked exactly
+    when padding was needed (valid_mask is None otherwise, wan_video_dit.py:485-507).
+    Guidance as the dispatch picks it: variance_boost_gamma > 0 = the variance
+    term; audio_token_norms [T*H*W] (unpadded) = the audio-guided path with gate
+    audio_gate, gain audio_boost_gamma and Path B weight audio_weighted_lambda
+    (zero-padded norms, wan_video_dit.py:299-306).  Output has q's layout."""
     if layout not in ("bhsd", "bshd"):
         raise ValueError("layout must be 'bhsd' or 'bshd'")
     T, H, W = grid_size
@@ -244,9 +323,17 @@ def run_bsa_uniform(
     plan = build_uniform_plan(tuple(grid_size), gp, chunk_3d_shape_q, chunk_3d_shape_k, D,
                               q.device, sparsity=sparsity, cdf_threshold=cdf_threshold,
                               q_pool="k" if padded else None)
+    if variance_boost_gamma or audio_token_norms is not None:
+        nk = plan.uniform["seq_k"] // plan.uniform["chunk_k"]
+        plan.uniform["guidance"] = make_guidance(
+            chunk_3d_shape_k, variance_gamma=float(variance_boost_gamma or 0.0),
+            audio_token_norms=audio_token_norms, audio_gate=audio_gate,
+            audio_gamma=audio_boost_gamma, audio_weighted_lambda=float(audio_weighted_lambda or 0.0),
+            n_chunks_k=nk, device=q.device)
     out = _BsaFunction.apply(q, k, v, plan, layout)
     return (out, plan) if return_plan else out
 
 
-__all__ = ["flash_attn_bsa_3d", "flash_attn_bsa_cross", "run_bsa_uniform", "build_uniform_plan",
-           "build_cross_plan", "uniform_padded_grid"]
+__all__ = ["flash_attn_bsa_3d", "flash_attn_bsa_3d_variance_guided", "flash_attn_bsa_3d_audio_guided",
+           "flash_attn_bsa_cross", "run_bsa_uniform", "build_uniform_plan", "build_cross_plan",
+           "uniform_padded_grid"]

@@ -613,12 +613,14 @@ __global__ void pool_kernel(const uint16_t* __restrict__ q, const uint16_t* __re
 // qc[a][d] * kc[b][d] (each accumulator updated once per d, in order).
 // Per head: qc [na_max, D], kc [nb_max, D], score [na_max, nb_max].  The live
 // sizes are *n_blocks x *n_blocks when n_blocks is given (dynamic layouts,
-// known on the device only), else na_max x nb_max.
+// known on the device only), else na_max x nb_max.  col_scale (nullable) multiplies
+// column b's scores by col_scale[b] (score * score_modifier, bsa_interface.py:626-627).
 constexpr int kScoreTile = 64;
 __global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc,
                                                     const float* __restrict__ kc, int D,
                                                     const int32_t* __restrict__ n_blocks,
                                                     int na_max, int nb_max,
+                                                    const float* __restrict__ col_scale,
                                                     float* __restrict__ score) {
   extern __shared__ float ssm[];
   const int na = n_blocks ? *n_blocks : na_max;
@@ -660,7 +662,8 @@ __global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int b = b0 + tx * 4 + j;
-      if (b < nb) sh[(int64_t)a * nb_max + b] = acc[i][j];
+      if (b < nb)
+        sh[(int64_t)a * nb_max + b] = col_scale ? __fmul_rn(acc[i][j], col_scale[b]) : acc[i][j];
     }
   }
 }
@@ -1023,10 +1026,15 @@ __global__ void uniform_perm_kernel(int Hp, int Wp, int ct, int ch, int cw, int6
 // rows valid), divided by max(count, 1).  One CTA per (chunk, head, tensor),
 // D threads; blockIdx.z picks x0 (S0 rows per head, n0 chunks of chunk0 rows,
 // validity bits0 -> out0) or x1 (S1, n1, chunk1, bits1 -> out1).
+// weights1 (nullable) replaces x1's validity by per-row weights w (Path B of
+// the audio-guided path, audio_weighted_mean_pooling_compression,
+// bsa_interface.py:902-970): sum of the rounded products x * w over the chunk
+// divided by max(sum of w, 1).
 __global__ void pool_chunk_kernel(const uint16_t* __restrict__ x0, const uint16_t* __restrict__ x1,
                                   int64_t S0, int64_t S1, int D, int chunk0, int n0, int chunk1,
                                   int n1, const uint64_t* __restrict__ bits0,
-                                  const uint64_t* __restrict__ bits1, float* __restrict__ out0,
+                                  const uint64_t* __restrict__ bits1,
+                                  const float* __restrict__ weights1, float* __restrict__ out0,
                                   float* __restrict__ out1) {
   const int c = blockIdx.x, h = blockIdx.y, which = blockIdx.z;
   const int chunk = which ? chunk1 : chunk0;
@@ -1034,6 +1042,17 @@ __global__ void pool_chunk_kernel(const uint16_t* __restrict__ x0, const uint16_
   if (c >= n) return;
   const int64_t base = (int64_t)c * chunk;
   const uint16_t* x = (which ? x1 : x0) + ((int64_t)h * (which ? S1 : S0) + base) * D + threadIdx.x;
+  float* out = (which ? out1 : out0) + ((int64_t)h * n + c) * D + threadIdx.x;
+  if (which && weights1 != nullptr) {
+    float sum = 0.0f, wsum = 0.0f;
+    for (int i = 0; i < chunk; ++i) {
+      const float w = weights1[base + i];
+      sum = __fadd_rn(sum, __fmul_rn(bfbits2f(x[(int64_t)i * D]), w));
+      wsum = __fadd_rn(wsum, w);
+    }
+    *out = __fdiv_rn(sum, wsum < 1.0f ? 1.0f : wsum);
+    return;
+  }
   const uint64_t* vbits = which ? bits1 : bits0;
   float sum = 0.0f;
   int cnt = 0;
@@ -1044,7 +1063,190 @@ __global__ void pool_chunk_kernel(const uint16_t* __restrict__ x0, const uint16_
     ++cnt;
   }
   const float den = cnt > 0 ? (float)cnt : 1.0f;
-  (which ? out1 : out0)[((int64_t)h * n + c) * D + threadIdx.x] = __fdiv_rn(sum, den);
+  *out = __fdiv_rn(sum, den);
+}
+
+// ================================================================ guided selection
+// Score guidance of the uniform path: per key chunk c a scale 1 + boost_c that
+// multiplies every score of column c before the selection
+// (_attention_bsa.forward, bsa_interface.py:626-627; _attention_bsa_audio_guided
+// .forward, :736-764).  Keys in chunk order; row r valid iff bit r of k_bits
+// (nullptr = every row valid).
+
+__device__ __forceinline__ bool row_valid(const uint64_t* bits, int64_t r) {
+  return bits == nullptr || ((bits[r >> 6] >> (r & 63)) & 1ull);
+}
+
+// compute_channel_variance_density (bsa_interface.py:973-1062), one CTA per key
+// chunk, thread d = channel d.  x_avg[r][d] = (sequential sum over heads) / heads;
+// chunk channel means and frame means (ct frames of ch*cw rows) over the valid
+// rows / max(count, 1); spatial = mean over d of (cm_d - mean_d cm)^2; temporal =
+// mean over d of (sum over frame pairs with both frames non-empty of
+// (fm[f+1] - fm[f])^2) / max(pairs, 1) (0 when ct == 1).  The means over d are
+// sequential sums by thread 0, divided by D.  Writes spatial + temporal.
+__global__ void variance_chunk_kernel(const uint16_t* __restrict__ v, int heads, int64_t Sk, int D,
+                                      int chunk, int frame, const uint64_t* __restrict__ k_bits,
+                                      float* __restrict__ combined) {
+  __shared__ float red[2][256];
+  __shared__ float gmean;
+  const int c = blockIdx.x, d = threadIdx.x;
+  const int64_t base = (int64_t)c * chunk;
+  const float fh = (float)heads;
+  float csum = 0.0f, fsum = 0.0f, prev = 0.0f, tsum = 0.0f;
+  int ccnt = 0, fcnt = 0, pairs = 0;
+  bool prev_ok = false;
+  for (int i = 0; i < chunk; ++i) {
+    const int64_t r = base + i;
+    if (row_valid(k_bits, r)) {
+      const uint16_t* p = v + r * D + d;
+      float xs = 0.0f;
+#pragma unroll 4
+      for (int h = 0; h < heads; ++h) xs = __fadd_rn(xs, bfbits2f(p[(int64_t)h * Sk * D]));
+      const float xa = __fdiv_rn(xs, fh);
+      csum = __fadd_rn(csum, xa);
+      fsum = __fadd_rn(fsum, xa);
+      ++ccnt;
+      ++fcnt;
+    }
+    if ((i + 1) % frame == 0) {  // frame end
+      const float fm = __fdiv_rn(fsum, fcnt > 0 ? (float)fcnt : 1.0f);
+      const bool ok = fcnt > 0;
+      if (i + 1 > frame && ok && prev_ok) {
+        const float df = __fsub_rn(fm, prev);
+        tsum = __fadd_rn(tsum, __fmul_rn(df, df));
+      }
+      if (i + 1 > frame) pairs += (ok && prev_ok);
+      prev = fm;
+      prev_ok = ok;
+      fsum = 0.0f;
+      fcnt = 0;
+    }
+  }
+  const float cm = __fdiv_rn(csum, ccnt > 0 ? (float)ccnt : 1.0f);
+  const int n_frames = chunk / frame;
+  const float tv = n_frames > 1 ? __fdiv_rn(tsum, pairs > 0 ? (float)pairs : 1.0f) : 0.0f;
+  red[0][d] = cm;
+  red[1][d] = tv;
+  __syncthreads();
+  if (d == 0) {
+    float s = 0.0f;
+    for (int j = 0; j < D; ++j) s = __fadd_rn(s, red[0][j]);
+    gmean = __fdiv_rn(s, (float)D);
+  }
+  __syncthreads();
+  const float dv = __fsub_rn(cm, gmean);
+  __syncthreads();
+  red[0][d] = __fmul_rn(dv, dv);
+  __syncthreads();
+  if (d == 0) {
+    float s = 0.0f, t = 0.0f;
+    for (int j = 0; j < D; ++j) s = __fadd_rn(s, red[0][j]);
+    for (int j = 0; j < D; ++j) t = __fadd_rn(t, red[1][j]);
+    const float spatial = __fdiv_rn(s, (float)D);
+    const float temporal = n_frames > 1 ? __fdiv_rn(t, (float)D) : 0.0f;
+    combined[c] = __fadd_rn(spatial, temporal);
+  }
+}
+
+// x[c] /= max(max_c x[c], floor), one CTA (rho = combined / combined.max().clamp(min=1e-6),
+// bsa_interface.py:1059-1060; block_means / max_val, :1100-1101).
+__global__ void __launch_bounds__(1024) normalize_max_kernel(float* __restrict__ x, int64_t n,
+                                                             float floor_) {
+  __shared__ float red[32];
+  float m = -INFINITY;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, x[i]);
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) red[0] = m < floor_ ? floor_ : m;
+  }
+  __syncthreads();
+  const float den = red[0];
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fdiv_rn(x[i], den);
+}
+
+// compute_block_audio_saliency's block means (bsa_interface.py:1094-1098): sequential
+// sum of the valid rows' norms / max(count, 1), one thread per chunk.
+__global__ void chunk_mean_kernel(const float* __restrict__ x, int64_t n_chunks, int chunk,
+                                  const uint64_t* __restrict__ k_bits, float* __restrict__ out) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n_chunks) return;
+  float s = 0.0f;
+  int cnt = 0;
+  for (int i = 0; i < chunk; ++i) {
+    const int64_t r = c * chunk + i;
+    if (!row_valid(k_bits, r)) continue;
+    s = __fadd_rn(s, x[r]);
+    ++cnt;
+  }
+  out[c] = __fdiv_rn(s, cnt > 0 ? (float)cnt : 1.0f);
+}
+
+// Path B weights (audio_weighted_mean_pooling_compression, bsa_interface.py:944-961):
+// w = (1 + lambda * (a / max(1e-6, max of the chunk's valid a))) on valid rows, 0
+// elsewhere; one thread per chunk.
+__global__ void audio_pool_weights_kernel(const float* __restrict__ a, int64_t n_chunks, int chunk,
+                                          const uint64_t* __restrict__ k_bits, float lambda_w,
+                                          float* __restrict__ w) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n_chunks) return;
+  float mx = -1e9f;
+  for (int i = 0; i < chunk; ++i) {
+    const int64_t r = c * chunk + i;
+    if (row_valid(k_bits, r)) mx = fmaxf(mx, a[r]);
+  }
+  if (mx < 1e-6f) mx = 1e-6f;
+  for (int i = 0; i < chunk; ++i) {
+    const int64_t r = c * chunk + i;
+    w[r] = row_valid(k_bits, r) ? __fadd_rn(1.0f, __fmul_rn(lambda_w, __fdiv_rn(a[r], mx))) : 0.0f;
+  }
+}
+
+// 1 + boost per key chunk, in the reference's order of operations:
+//   ext   = modifier[c] (+ var_gamma * rho[c])  or  var_gamma * rho[c]   (:1467-1470)
+//   boost = audio_gamma * (g * sal[c] + (1 - g) * uni)  (+ ext)           (:748-762)
+//   scale = 1 + boost                                                     (:764, :1243-1245)
+__global__ void guidance_scale_kernel(int64_t n, const float* __restrict__ rho, float var_gamma,
+                                      const float* __restrict__ sal, const float* __restrict__ gate,
+                                      float audio_gamma, float uni, const float* __restrict__ modifier,
+                                      float* __restrict__ scale) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  bool has_ext = false;
+  float ext = 0.0f;
+  if (modifier != nullptr) {
+    ext = modifier[c];
+    has_ext = true;
+  }
+  if (rho != nullptr) {
+    const float t = __fmul_rn(var_gamma, rho[c]);
+    ext = has_ext ? __fadd_rn(ext, t) : t;
+    has_ext = true;
+  }
+  float boost = 0.0f;
+  if (sal != nullptr) {
+    const float g = gate != nullptr ? *gate : 1.0f;
+    const float gs = __fadd_rn(__fmul_rn(g, sal[c]), __fmul_rn(__fsub_rn(1.0f, g), uni));
+    boost = __fmul_rn(audio_gamma, gs);
+  }
+  if (has_ext) boost = __fadd_rn(boost, ext);
+  scale[c] = __fadd_rn(1.0f, boost);
+}
+
+// Per-token scalar gather into a chunk order (0 at padding), like gather_rows.
+__global__ void gather_values_kernel(const float* __restrict__ x, int T, int H, int W, int Hp, int Wp,
+                                     const int32_t* __restrict__ src_idx, int64_t n_rows,
+                                     float* __restrict__ out) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n_rows) return;
+  const int64_t g = src_idx[r];
+  const int t = (int)(g / ((int64_t)Hp * Wp));
+  const int hh = (int)((g / Wp) % Hp);
+  const int w = (int)(g % Wp);
+  out[r] = (t < T && hh < H && w < W) ? x[((int64_t)t * H + hh) * W + w] : 0.0f;
 }
 
 }  // namespace prism
@@ -1055,7 +1257,7 @@ using namespace prism;
 extern "C" {
 
 const char* prism_last_error(void) { return prism::last_error(); }
-int prism_abi_version(void) { return 3; }
+int prism_abi_version(void) { return 4; }
 
 prism_status_t prism_token_norms(const void* x, int64_t n_tokens, int dim, void* out,
                                  cudaStream_t stream) {
@@ -1227,7 +1429,8 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),
                    "prism_block_select: smem attribute");
   const int nt = (nb_max + kScoreTile - 1) / kScoreTile;
-  score_kernel<<<dim3(nt, nt, heads), 256, ssm, stream>>>(qc, kc, D, n_blocks, nb_max, nb_max, sc);
+  score_kernel<<<dim3(nt, nt, heads), 256, ssm, stream>>>(qc, kc, D, n_blocks, nb_max, nb_max,
+                                                          nullptr, sc);
   PRISM_CHECK_LAUNCH("prism_block_select/score");
   const float sm_scale = (float)(1.0 / sqrt((double)D));
   const size_t selsm = ((size_t)nb_max + wq) * sizeof(uint32_t);
@@ -1268,7 +1471,8 @@ size_t prism_block_select_uniform_workspace_bytes(int heads, int64_t n_chunks_q,
 prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, int heads, int64_t Sq,
                                           int64_t Sk, int D, int64_t seq_q, int64_t seq_k,
                                           int chunk_q, int chunk_k, const uint64_t* q_bits,
-                                          const uint64_t* k_bits, int mode, double sparsity,
+                                          const uint64_t* k_bits, const float* k_weights,
+                                          const float* col_scale, int mode, double sparsity,
                                           double cdf_threshold, void* workspace, uint32_t* bits_q,
                                           uint32_t* bits_k, cudaStream_t stream) {
   PRISM_CHECK_ARG(q_re && k_re && k_bits && workspace && bits_q && bits_k,
@@ -1295,13 +1499,13 @@ prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, in
                    "prism_block_select_uniform: clear bitmaps");
   pool_chunk_kernel<<<dim3(nq > nk ? nq : nk, heads, 2), D, 0, stream>>>(
       (const uint16_t*)q_re, (const uint16_t*)k_re, Sq, Sk, D, chunk_q, nq, chunk_k, nk, q_bits,
-      k_bits, qc, kc);
+      k_bits, k_weights, qc, kc);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/pool");
   const size_t ssm = 2 * (size_t)D * (kScoreTile + 4) * sizeof(float);
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),
                    "prism_block_select_uniform: smem attribute");
   score_kernel<<<dim3((nk + kScoreTile - 1) / kScoreTile, (nq + kScoreTile - 1) / kScoreTile, heads), 256,
-                 ssm, stream>>>(qc, kc, D, nullptr, nq, nk, sc);
+                 ssm, stream>>>(qc, kc, D, nullptr, nq, nk, col_scale, sc);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/score");
   const float sm_scale = (float)(1.0 / sqrt((double)D));
   const size_t selsm = ((size_t)nk + wk) * sizeof(uint32_t);
@@ -1313,6 +1517,101 @@ prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, in
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/select");
   transpose_bits_kernel<<<dim3(wq, wk, heads), 32, 0, stream>>>(bits_q, n_qt, n_kt, wq, wk, bits_k);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/transpose");
+  return PRISM_OK;
+}
+
+
+// ------------------------------------------------------------ guided selection
+prism_status_t prism_gather_values(const float* x, int T, int H, int W, int Tp, int Hp, int Wp,
+                                   const int32_t* src_idx, int64_t n_rows, float* out,
+                                   cudaStream_t stream) {
+  PRISM_CHECK_ARG(x && src_idx && out, "prism_gather_values: null pointer");
+  PRISM_CHECK_ARG(T >= 1 && H >= 1 && W >= 1 && T <= Tp && H <= Hp && W <= Wp,
+                  "prism_gather_values: bad grids");
+  PRISM_CHECK_ARG(n_rows >= 0 && n_rows < (int64_t)1 << 31, "prism_gather_values: bad row count");
+  if (n_rows == 0) return PRISM_OK;
+  gather_values_kernel<<<(unsigned)((n_rows + 255) / 256), 256, 0, stream>>>(x, T, H, W, Hp, Wp,
+                                                                            src_idx, n_rows, out);
+  PRISM_CHECK_LAUNCH("prism_gather_values");
+  return PRISM_OK;
+}
+
+prism_status_t prism_variance_density(const void* v_re, int heads, int64_t Sk, int D, int64_t seq_k,
+                                      int ct, int ch, int cw, const uint64_t* k_bits, float* rho,
+                                      cudaStream_t stream) {
+  PRISM_CHECK_ARG(v_re && rho, "prism_variance_density: null pointer");
+  PRISM_CHECK_ARG(heads >= 1 && D >= 32 && D <= 256 && D % 32 == 0,
+                  "prism_variance_density: D=%d must be a multiple of 32 in [32, 256]", D);
+  PRISM_CHECK_ARG(ct >= 1 && ch >= 1 && cw >= 1, "prism_variance_density: bad chunk shape");
+  const int chunk = ct * ch * cw;
+  PRISM_CHECK_ARG(seq_k > 0 && seq_k <= Sk && seq_k % chunk == 0,
+                  "prism_variance_density: %lld keys are not a whole number of %d-token chunks",
+                  (long long)seq_k, chunk);
+  const int64_t n = seq_k / chunk;
+  PRISM_CHECK_ARG(n < (int64_t)1 << 31, "prism_variance_density: too many chunks");
+  variance_chunk_kernel<<<(unsigned)n, D, 0, stream>>>((const uint16_t*)v_re, heads, Sk, D, chunk,
+                                                       ch * cw, k_bits, rho);
+  PRISM_CHECK_LAUNCH("prism_variance_density/chunks");
+  normalize_max_kernel<<<1, 1024, 0, stream>>>(rho, n, 1e-6f);
+  PRISM_CHECK_LAUNCH("prism_variance_density/normalize");
+  return PRISM_OK;
+}
+
+prism_status_t prism_audio_saliency(const float* norms_re, int64_t seq_k, int chunk_k,
+                                    const uint64_t* k_bits, float* saliency, cudaStream_t stream) {
+  PRISM_CHECK_ARG(norms_re && saliency, "prism_audio_saliency: null pointer");
+  PRISM_CHECK_ARG(chunk_k >= 1 && seq_k > 0 && seq_k % chunk_k == 0,
+                  "prism_audio_saliency: %lld keys are not a whole number of %d-token chunks",
+                  (long long)seq_k, chunk_k);
+  const int64_t n = seq_k / chunk_k;
+  chunk_mean_kernel<<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(norms_re, n, chunk_k, k_bits,
+                                                                     saliency);
+  PRISM_CHECK_LAUNCH("prism_audio_saliency/means");
+  normalize_max_kernel<<<1, 1024, 0, stream>>>(saliency, n, 1e-6f);
+  PRISM_CHECK_LAUNCH("prism_audio_saliency/normalize");
+  return PRISM_OK;
+}
+
+prism_status_t prism_audio_pool_weights(const float* norms_re, int64_t seq_k, int chunk_k,
+                                        const uint64_t* k_bits, float lambda_w, float* weights,
+                                        cudaStream_t stream) {
+  PRISM_CHECK_ARG(norms_re && weights, "prism_audio_pool_weights: null pointer");
+  PRISM_CHECK_ARG(chunk_k >= 1 && seq_k > 0 && seq_k % chunk_k == 0,
+                  "prism_audio_pool_weights: %lld keys are not a whole number of %d-token chunks",
+                  (long long)seq_k, chunk_k);
+  const int64_t n = seq_k / chunk_k;
+  audio_pool_weights_kernel<<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(norms_re, n, chunk_k,
+                                                                             k_bits, lambda_w, weights);
+  PRISM_CHECK_LAUNCH("prism_audio_pool_weights");
+  return PRISM_OK;
+}
+
+prism_status_t prism_pool_chunks(const void* x_re, int heads, int64_t S, int D, int64_t seq,
+                                int chunk, const uint64_t* bits, const float* weights, float* out,
+                                cudaStream_t stream) {
+  PRISM_CHECK_ARG(x_re && out, "prism_pool_chunks: null pointer");
+  PRISM_CHECK_ARG(heads >= 1 && D >= 1 && D <= 1024, "prism_pool_chunks: bad heads / D");
+  PRISM_CHECK_ARG(chunk >= 1 && seq > 0 && seq <= S && seq % chunk == 0,
+                  "prism_pool_chunks: %lld rows are not a whole number of %d-row chunks",
+                  (long long)seq, chunk);
+  const int64_t n = seq / chunk;
+  PRISM_CHECK_ARG(n < (int64_t)1 << 31, "prism_pool_chunks: too many chunks");
+  // the second tensor slot of pool_chunk_kernel (the one with weights); the first is empty
+  pool_chunk_kernel<<<dim3((unsigned)n, heads, 2), D, 0, stream>>>(
+      (const uint16_t*)x_re, (const uint16_t*)x_re, S, S, D, chunk, 0, chunk, (int)n, nullptr, bits,
+      weights, out, out);
+  PRISM_CHECK_LAUNCH("prism_pool_chunks");
+  return PRISM_OK;
+}
+
+prism_status_t prism_guidance_scale(int64_t n_chunks, const float* rho, float variance_gamma,
+                                    const float* saliency, const float* audio_gate, float audio_gamma,
+                                    const float* modifier, float* scale, cudaStream_t stream) {
+  PRISM_CHECK_ARG(scale && n_chunks > 0, "prism_guidance_scale: null pointer or no chunks");
+  const float uni = (float)(1.0 / (double)n_chunks);
+  guidance_scale_kernel<<<(unsigned)((n_chunks + 255) / 256), 256, 0, stream>>>(
+      n_chunks, rho, variance_gamma, saliency, audio_gate, audio_gamma, uni, modifier, scale);
+  PRISM_CHECK_LAUNCH("prism_guidance_scale");
   return PRISM_OK;
 }
 

@@ -28,6 +28,7 @@ import torch
 
 from . import ops
 from .dynamic_block_shape import ZONE_SIZE, shapes_from_qkv
+from .guidance import guidance_inputs
 
 _TILE = 64  # dynamic_block_attention.py:15
 
@@ -63,13 +64,18 @@ class SparsePlan:
         self.bits_q = None
         self.bits_k = None
 
-    def select(self, q_re, k_re):
-        """Tile bitmaps (bits_q, bits_k) for tile-ordered q / k."""
+    def select(self, q_re, k_re, v_re=None):
+        """Tile bitmaps (bits_q, bits_k) for tile-ordered q / k (v: the guided
+        uniform path's variance statistics)."""
         if self.uniform is not None:
             u = self.uniform
+            k_weights = col_scale = None
+            if u.get("guidance") is not None:
+                k_weights, col_scale = guidance_inputs(self, u["guidance"], v_re)
             return ops.block_select_uniform(q_re, k_re, u["seq_q"], u["seq_k"], u["chunk_q"],
                                             u["chunk_k"], u["q_bits"], self.tile_bits,
-                                            self.sparsity, self.cdf_threshold)
+                                            self.sparsity, self.cdf_threshold,
+                                            k_weights=k_weights, col_scale=col_scale)
         return ops.block_select(q_re, k_re, self.layout, self.tile_bits, self.sparsity,
                                 self.cdf_threshold)
 
@@ -103,7 +109,7 @@ class _BsaFunction(torch.autograd.Function):
         q_re = ops.gather_rows(qh, plan.grid, plan.grid_padded, plan.src_idx)
         k_re = ops.gather_rows(kh, plan.grid_k, plan.grid_padded_k, plan.src_idx_k)
         v_re = ops.gather_rows(vh, plan.grid_k, plan.grid_padded_k, plan.src_idx_k)
-        bits_q, bits_k = plan.select(q_re, k_re)
+        bits_q, bits_k = plan.select(q_re, k_re, v_re)
         plan.bits_q, plan.bits_k = bits_q, bits_k
         o_re, lse, o_lo = ops.bsa_fwd(q_re, k_re, v_re, bits_q, plan.tile_bits, plan.sm_scale,
                                       want_lo=True)

@@ -207,25 +207,94 @@ def uniform_layout(grid_padded, chunk, n_rows: int, device):
 
 
 def block_select_uniform(q_re, k_re, seq_q: int, seq_k: int, chunk_q: int, chunk_k: int, q_bits,
-                         k_bits, sparsity, cdf_threshold):
+                         k_bits, sparsity, cdf_threshold, k_weights=None, col_scale=None):
     """Chunk pooling + scores + selection of the uniform path -> (bits_q, bits_k).
-    q_bits: rows the q pooling counts (None: all); k_bits: key validity."""
-    _check_cuda(q_re, k_re, q_bits, k_bits)
+    q_bits: rows the q pooling counts (None: all); k_bits: key validity.
+    k_weights [seq_k] fp32: per-row key pooling weights (Path B) instead of k_bits;
+    col_scale [seq_k/chunk_k] fp32: per-key-chunk score scale (guided selection)."""
+    _check_cuda(q_re, k_re, q_bits, k_bits, k_weights, col_scale)
     heads, Sq, D = q_re.shape
     Sk = k_re.shape[1]
     mode = selection_mode(sparsity, cdf_threshold)
     n_qt, n_kt = Sq // 64, Sk // 64
     dev = q_re.device
+    for t, n in ((k_weights, seq_k), (col_scale, seq_k // chunk_k)):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < n):
+            raise ValueError("k_weights / col_scale must be contiguous fp32 of the key rows / chunks")
     bits_q = torch.empty(heads, n_qt, (n_kt + 31) // 32, dtype=torch.int32, device=dev)
     bits_k = torch.empty(heads, n_kt, (n_qt + 31) // 32, dtype=torch.int32, device=dev)
     ws = _ws(_lib.query("prism_block_select_uniform_workspace_bytes", heads, seq_q // chunk_q,
                         seq_k // chunk_k, D), dev)
     _lib.call("prism_block_select_uniform", _p(q_re), _p(k_re), heads, Sq, Sk, D, seq_q, seq_k,
-              chunk_q, chunk_k, _p(q_bits), _p(k_bits), mode,
+              chunk_q, chunk_k, _p(q_bits), _p(k_bits), _p(k_weights), _p(col_scale), mode,
               float(sparsity if sparsity is not None else 0.0),
               float(cdf_threshold if cdf_threshold is not None else 0.0), _p(ws), _p(bits_q),
               _p(bits_k), _stream(q_re))
     return bits_q, bits_k
+
+
+# --------------------------------------------------------- guided selection
+def gather_values(x: torch.Tensor, grid, grid_padded, src_idx: torch.Tensor) -> torch.Tensor:
+    """Per-token values [T*H*W] on grid -> fp32 [len(src_idx)] in the chunk order, 0 at padding."""
+    _check_cuda(x, src_idx)
+    xf = x.reshape(-1).to(torch.float32).contiguous()
+    T, H, W = grid
+    assert xf.numel() == T * H * W, "values must cover the grid"
+    out = torch.empty(src_idx.numel(), dtype=torch.float32, device=x.device)
+    _lib.call("prism_gather_values", _p(xf), T, H, W, *grid_padded, _p(src_idx), src_idx.numel(),
+              _p(out), _stream(x))
+    return out
+
+
+def variance_density(v_re: torch.Tensor, seq_k: int, chunk, k_bits) -> torch.Tensor:
+    """compute_channel_variance_density of chunk-ordered V [heads, Sk, D] -> rho [n_chunks] fp32."""
+    _check_cuda(v_re, k_bits)
+    heads, Sk, D = v_re.shape
+    ct, ch, cw = (int(c) for c in chunk)
+    rho = torch.empty(seq_k // (ct * ch * cw), dtype=torch.float32, device=v_re.device)
+    _lib.call("prism_variance_density", _p(v_re), heads, Sk, D, seq_k, ct, ch, cw, _p(k_bits),
+              _p(rho), _stream(v_re))
+    return rho
+
+
+def audio_saliency(norms_re: torch.Tensor, seq_k: int, chunk_k: int, k_bits) -> torch.Tensor:
+    """compute_block_audio_saliency of chunk-ordered fp32 norms -> [n_chunks] fp32."""
+    _check_cuda(norms_re, k_bits)
+    out = torch.empty(seq_k // chunk_k, dtype=torch.float32, device=norms_re.device)
+    _lib.call("prism_audio_saliency", _p(norms_re), seq_k, chunk_k, _p(k_bits), _p(out),
+              _stream(norms_re))
+    return out
+
+
+def audio_pool_weights(norms_re: torch.Tensor, seq_k: int, chunk_k: int, k_bits,
+                       lambda_w: float) -> torch.Tensor:
+    """Path B key pooling weights [seq_k] fp32 (0 on invalid rows)."""
+    _check_cuda(norms_re, k_bits)
+    out = torch.empty(seq_k, dtype=torch.float32, device=norms_re.device)
+    _lib.call("prism_audio_pool_weights", _p(norms_re), seq_k, chunk_k, _p(k_bits),
+              float(lambda_w), _p(out), _stream(norms_re))
+    return out
+
+
+def pool_chunks(x_re: torch.Tensor, seq: int, chunk: int, bits=None, weights=None) -> torch.Tensor:
+    """Chunk means [heads, seq/chunk, D] fp32 of x_re [heads, S, D] bf16 (masked by
+    bits, or the Path B weighted form with weights)."""
+    _check_cuda(x_re, bits, weights)
+    heads, S, D = x_re.shape
+    out = torch.empty(heads, seq // chunk, D, dtype=torch.float32, device=x_re.device)
+    _lib.call("prism_pool_chunks", _p(x_re), heads, S, D, seq, chunk, _p(bits), _p(weights), _p(out),
+              _stream(x_re))
+    return out
+
+
+def guidance_scale(n_chunks: int, device, *, rho=None, variance_gamma: float = 0.0, saliency=None,
+                   audio_gate=None, audio_gamma: float = 0.0, modifier=None) -> torch.Tensor:
+    """Per-key-chunk score scale 1 + boost [n_chunks] fp32 (see prism_guidance_scale)."""
+    _check_cuda(rho, saliency, audio_gate, modifier)
+    out = torch.empty(n_chunks, dtype=torch.float32, device=device)
+    _lib.call("prism_guidance_scale", n_chunks, _p(rho), float(variance_gamma), _p(saliency),
+              _p(audio_gate), float(audio_gamma), _p(modifier), _p(out), _stream(out))
+    return out
 
 
 # -------------------------------------------------------------- a15/a16

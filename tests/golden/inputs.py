@@ -44,6 +44,10 @@ class Case:
     # uniform fixed-shape path (flash_attn_bsa_3d) when set: q / key chunk shapes
     chunk_q: Optional[Tuple[int, int, int]] = None
     chunk_k: Optional[Tuple[int, int, int]] = None
+    # guided uniform path (flash_attn_bsa_3d_variance_guided / _audio_guided) when set:
+    # kind "variance" (variance_gamma) or "audio" (gate, audio_gamma, lambda_w,
+    # variance_gamma)
+    guidance: Optional[dict] = None
 
     @property
     def uniform(self):
@@ -107,7 +111,33 @@ UNIFORM_CASES = {
                        cdf_threshold=0.9, chunk_q=(4, 4, 4), chunk_k=(4, 4, 4), seed=63),
 }
 
-ALL_CASES = dict(CASES, **UNIFORM_CASES)
+# Guided uniform path: per-key-chunk score scale from V's channel-variance density
+# (flash_attn_bsa_3d_variance_guided, bsa_interface.py:1179-1260) and/or the audio
+# saliency of the a2v norms, with optional audio-weighted key pooling
+# (flash_attn_bsa_3d_audio_guided, :1395-1501).  Gate and gains are bf16-exact.
+GUIDED_CASES = {
+    # variance only, padded grid (masked statistics), 4x4x4 chunks, top-k + cdf
+    "g_var_pad": Case("g_var_pad", (6, 10, 12), 2, 64, values="aniso", amp=(0.05, 1.0),
+                      audio=False, sparsity=0.75, cdf_threshold=0.2, chunk_q=(4, 4, 4),
+                      chunk_k=(4, 4, 4), seed=80, guidance=dict(kind="variance", variance_gamma=1.0)),
+    # variance only, no padding, 4x4x8 chunks (4 frames of 32), head_dim 128, top-k only
+    "g_var_d128": Case("g_var_d128", (8, 16, 24), 2, 128, values="aniso", amp=(0.1, 1.0),
+                       audio=False, sparsity=0.5, cdf_threshold=None, chunk_q=(4, 4, 8),
+                       chunk_k=(4, 4, 8), seed=81, guidance=dict(kind="variance", variance_gamma=2.0)),
+    # audio saliency with the concentration gate and audio-weighted key pooling, padded
+    "g_audio_pathb": Case("g_audio_pathb", (6, 10, 12), 2, 64, values="aniso", amp=(0.05, 1.0),
+                          sparsity=0.75, cdf_threshold=0.5, chunk_q=(4, 4, 4), chunk_k=(4, 4, 4),
+                          seed=82, guidance=dict(kind="audio", gate=0.625, audio_gamma=1.5,
+                                                 lambda_w=1.0, variance_gamma=0.0)),
+    # audio + variance in one boost bracket, cumulative mass only, no padding
+    "g_audio_var": Case("g_audio_var", (8, 8, 16), 2, 64, values="aniso", amp=(0.1, 1.0),
+                        sparsity=None, cdf_threshold=0.6, chunk_q=(4, 4, 8), chunk_k=(4, 4, 8),
+                        seed=83, guidance=dict(kind="audio", gate=0.75, audio_gamma=1.0,
+                                               lambda_w=0.0, variance_gamma=0.5)),
+}
+UNIFORM_CASES_ALL = dict(UNIFORM_CASES, **GUIDED_CASES)
+
+ALL_CASES = dict(CASES, **UNIFORM_CASES_ALL)
 
 
 @dataclass
@@ -257,12 +287,14 @@ def make_inputs(case: Case):
         gen = torch.Generator().manual_seed(case.seed + 4)
         a2v = torch.randn(T * H * W, case.audio_tokens * 2, generator=gen)
         gen = torch.Generator().manual_seed(case.seed + 5)
-        zscale = torch.rand((Tp // 8) * (Hp // 8) * (Wp // 8), generator=gen) * 1.8 + 0.2
-        # per-zone amplitude U(0.2, 2) on the cross-attention output
+        # per-zone amplitude U(0.2, 2) on the cross-attention output (8x8x8 zones; a
+        # grid padded only to a smaller chunk has a partial last zone)
+        zt, zh, zw = (int(math.ceil(x / 8)) for x in (Tp, Hp, Wp))
+        zscale = torch.rand(zt * zh * zw, generator=gen) * 1.8 + 0.2
         tt = torch.arange(T)[:, None, None] // 8
         hh = torch.arange(H)[None, :, None] // 8
         ww = torch.arange(W)[None, None, :] // 8
-        zid = ((tt * (Hp // 8) + hh) * (Wp // 8) + ww).reshape(-1)
+        zid = ((tt * zh + hh) * zw + ww).reshape(-1)
         a2v = (a2v * zscale[zid][:, None]).to(torch.bfloat16)
         out["a2v"] = a2v
         norms = a2v.norm(dim=-1)  # wan_video_dit.py:744, bf16 in -> bf16 out

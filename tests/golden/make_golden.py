@@ -150,11 +150,62 @@ def chunk_lists_to_dense(block_indices, lens, n_cols):
     return dense
 
 
+def _uniform_entry(bsa, case, inp, dtype):
+    """The reference entry point of a uniform case as f(q, k, v, **kw) for one pass
+    (dtype = the pass's floating type: guidance gains, gate and norms follow it, as
+    in wan_video_dit.py:309-335 where they take q's dtype)."""
+    g = case.guidance
+    gp = case.grid_padded
+    if g is None:
+        return lambda q, k, v, **kw: bsa.flash_attn_bsa_3d(q, k, v, gp, gp, **kw)
+    if g["kind"] == "variance":
+        return lambda q, k, v, **kw: bsa.flash_attn_bsa_3d_variance_guided(
+            q, k, v, gp, gp, variance_boost_gamma=g["variance_gamma"], **kw)
+    norms = inp["norms"].to(dtype)
+    gate = torch.tensor([g["gate"]], dtype=dtype)
+    gamma = torch.tensor(g["audio_gamma"], dtype=dtype)
+    return lambda q, k, v, **kw: bsa.flash_attn_bsa_3d_audio_guided(
+        q, k, v, gp, gp, audio_token_norms=norms, audio_gate_value=gate, audio_boost_gamma=gamma,
+        audio_weighted_lambda=g["lambda_w"], variance_boost_gamma=g["variance_gamma"], **kw)
+
+
+def _guidance_parts(bsa, case, inp):
+    """The reference's guidance statistics on fp32 values: rho
+    (compute_channel_variance_density), the audio block saliency
+    (compute_block_audio_saliency) and Path B's pooled keys
+    (audio_weighted_mean_pooling_compression), each on the key chunk order."""
+    g = case.guidance
+    Tp, Hp, Wp = case.grid_padded
+    tk, hk, wk = case.chunk_k
+    n3 = (Tp // tk, Hp // hk, Wp // wk)
+    ck = tk * hk * wk
+    D = case.head_dim
+    valid = inp["valid"]
+    vm = None if valid is None else bsa.rearrange_THW_to_3d_block_1d(valid, *n3, tk, hk, wk)
+    out = {}
+    with torch.no_grad():
+        if g.get("variance_gamma", 0.0) > 0:
+            v_ro = bsa.rearrange_THW_to_3d_block(inp["v"].float(), *n3, tk, hk, wk, D)
+            out["rho"] = bsa.compute_channel_variance_density(v_ro, ck, tk, hk, wk, vm).numpy()
+        if g["kind"] == "audio":
+            a_ro = bsa.rearrange_THW_to_3d_block_1d(inp["norms"].float(), *n3, tk, hk, wk)
+            out["saliency"] = bsa.compute_block_audio_saliency(a_ro, ck, valid_mask=vm).numpy()
+            if g["lambda_w"] > 0:
+                k_ro = bsa.rearrange_THW_to_3d_block(inp["k"].float(), *n3, tk, hk, wk, D)
+                kc = bsa.audio_weighted_mean_pooling_compression(k_ro, ck, a_ro, valid_mask=vm,
+                                                                 lambda_w=g["lambda_w"])
+                out["kcmp_pathb"] = kc[0].numpy()
+    return out
+
+
 def run_uniform_case(bsa, case):
     """flash_attn_bsa_3d (bsa_interface.py:1123-1176) on the padded grid, as the
-    uniform dispatch of wan_video_dit.py:470-560 calls it.  Stores the chunk
+    uniform dispatch of wan_video_dit.py:470-560 calls it, or its guided forms
+    (flash_attn_bsa_3d_variance_guided :1179-1260, flash_attn_bsa_3d_audio_guided
+    :1395-1501, dispatched at wan_video_dit.py:637-672).  Stores the chunk
     orders, the chunk-level selection of a bf16 and an fp32 pass, and the fp32
-    outputs / gradients on a fixed subset of rows (padded THW order)."""
+    outputs / gradients on a fixed subset of rows (padded THW order); guided cases
+    add the reference's guidance statistics."""
     from oracle.oracle import dense_to_bits
 
     inp = make_inputs(case)
@@ -180,12 +231,12 @@ def run_uniform_case(bsa, case):
         # pass 1: bf16 inputs, selection only (the kernel call is captured and skipped)
         bsa.attn_fwd_bsa_varlen_triton = skip
         with torch.no_grad():
-            bsa.flash_attn_bsa_3d(q, k, v, case.grid_padded, case.grid_padded, **kw)
+            _uniform_entry(bsa, case, inp, torch.bfloat16)(q, k, v, **kw)
         sel16 = captured.pop()
         # pass 2: fp32 values (bf16-representable), real kernels, autograd
         bsa.attn_fwd_bsa_varlen_triton = capture
         q32, k32, v32 = (t.float().requires_grad_(True) for t in (q, k, v))
-        out = bsa.flash_attn_bsa_3d(q32, k32, v32, case.grid_padded, case.grid_padded, **kw)
+        out = _uniform_entry(bsa, case, inp, torch.float32)(q32, k32, v32, **kw)
         (out * do.float()).sum().backward()
         sel32 = captured.pop()
     finally:
@@ -193,7 +244,7 @@ def run_uniform_case(bsa, case):
 
     dense16 = chunk_lists_to_dense(sel16["bi"].numpy(), sel16["lens"].numpy(), nk)
     dense32 = chunk_lists_to_dense(sel32["bi"].numpy(), sel32["lens"].numpy(), nk)
-    if valid is not None:
+    if valid is not None and case.guidance is None:
         assert (dense16 == dense32).all(), "selection differs between bf16 and fp32 passes"
     ar = torch.arange(S, dtype=torch.float64).view(1, 1, S, 1)
     src = []
@@ -212,6 +263,8 @@ def run_uniform_case(bsa, case):
     res["o"] = o[:, rows]
     res["dq"], res["dk"], res["dv"] = (gr[:, rows] for gr in grads)
     res["sums"] = np.array([np.abs(x).astype(np.float64).sum() for x in [o] + grads])
+    if case.guidance is not None:
+        res.update(_guidance_parts(bsa, case, inp))
     return res
 
 

@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 
 from helpers import load_fixture
-from inputs import UNIFORM_CASES, make_inputs
+from inputs import UNIFORM_CASES, UNIFORM_CASES_ALL, make_inputs
 from oracle import oracle as O
 
 
@@ -25,7 +25,7 @@ def _b(t):
 
 
 def _setup(name):
-    case = UNIFORM_CASES[name]
+    case = UNIFORM_CASES_ALL[name]
     fx = load_fixture(name)
     inp = make_inputs(case)
     gp = case.grid_padded
