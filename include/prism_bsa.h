@@ -257,6 +257,12 @@ prism_status_t prism_guidance_scale(int64_t n_chunks, const float* rho, float va
                                     const float* saliency, const float* audio_gate, float audio_gamma,
                                     const float* modifier, float* scale, cudaStream_t stream);
 
+/* Raw chunk scores (cal_score, bsa_interface.py:203-207): score[h][a][b] = fp32
+ * dot product of pooled q chunk a and pooled key chunk b (qc [heads, nq, D], kc
+ * [heads, nk, D]), the same products as the selection's, without its col_scale. */
+prism_status_t prism_chunk_scores(const float* qc, const float* kc, int heads, int nq, int nk, int D,
+                                  float* scores, cudaStream_t stream);
+
 /* Block-sparse attention forward over tile-ordered q/k/v [heads, S, D] bf16
  * (attn_fwd_bsa_varlen_triton + _attn_fwd_bsa_varlen_align,
  * bsa_interface.py:328-385, flash_attn_bsa_varlen_mask.py:193-319).
@@ -268,6 +274,71 @@ prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int he
                              int D, float sm_scale, const uint32_t* bits_q,
                              const uint64_t* tile_bits, void* o, void* o_lo, float* lse,
                              cudaStream_t stream);
+
+/* Key-bias form of the forward (the pooled-key pass of the Taylor merge,
+ * _taylor_merge_fwd_kernel, bias_rectification_triton.py:156-293): as
+ * prism_bsa_fwd_qk, with the key validity per (head, query tile, key tile),
+ * key_masks [heads, Sq/64, Sk/64] u64, and a score offset per key, key_bias [Sk]
+ * fp32 added to the raw score q.k before sm_scale (a log-weight w is passed as
+ * w / sm_scale).  Rows without a selected key give O = 0, lse = -inf. */
+prism_status_t prism_bsa_fwd_keybias(const void* q, const void* k, const void* v, int heads, int64_t Sq,
+                                     int64_t Sk, int D, float sm_scale, const uint32_t* bits_q,
+                                     const uint64_t* key_masks, const float* key_bias, void* o,
+                                     void* o_lo, float* lse, cudaStream_t stream);
+
+/* Bias rectification of the uniform path, inference (bsa_rectified_sparse_attn /
+ * bsa_taylor_sparse_attn, bias_rectification.py:261-446; fused kernels
+ * bias_rectification_triton.py:9-363).
+ *
+ * prism_correction_stats: per head h and q chunk a, from the raw chunk scores
+ * [heads, nq, nk] fp32, the selection bitmap bits_q [heads, n_qt, ceil(n_kt/32)]
+ * (q chunk a = tiles [a*tq, a*tq+tq), key chunk j = tiles [j*tk, j*tk+tk); chunk j
+ * is selected iff one of its tiles is set) and the key validity tile_bits [n_kt]
+ * (chunk j valid iff one of its tiles holds a valid key):
+ *   A_j = softmax over valid j of score * sm_scale (_masked_softmax_along_last :146-152)
+ *   R[h][a] = max(1 - sum of A over valid unselected j, 1e-6)           (:435-436)
+ *   M[h][a] = variance of A over the valid j (_masked_var_along_last :155-170)
+ * nonsel [heads, nq, ceil(nk/64)] u64 (NULL = not written): the valid unselected
+ * chunks; a_rect [heads, nq, nk] fp32 (NULL = not written): A on them, 0 elsewhere.
+ * Sums in a fixed order (256 strided partials, then a halving tree), deterministic
+ * exponentials.
+ *
+ * prism_taylor_prep: the pooled-key pass inputs for n_ut = Sk_pooled/64 key tiles:
+ * masks [heads, n_qt, n_ut] u64 = nonsel of the q tile's chunk where M < *tau
+ * (is_flat, :300-303), else 0; bits_t [heads, n_qt, ceil(n_ut/32)] bit u set iff
+ * masks[..][u] != 0.  tau: device scalar.
+ *
+ * prism_key_log_bias: bias [n_pad] = log(max(valid tokens of chunk j, 1)) / sm_scale
+ * for j < nk (the log-count offsets of :218-221), 0 beyond.
+ *
+ * prism_rows_to_bf16: fp32 rows [heads, n, D] -> bf16 [heads, n_pad, D], zero rows past n.
+ *
+ * prism_taylor_merge: rows r < seq_q of chunk a = r / chunk_q with M[h][a] < *tau:
+ * out = w_spa O_spa + w_t O_t with w = exp(lse - lse_total) (natural-log lse,
+ * bias_rectification_triton.py:270-292); other rows out = O_spa.  O given as bf16
+ * plus an optional bf16 residual (o_lo of the forward).  Rows [heads, S, D].
+ *
+ * prism_rectified_apply: rows r < seq_q: out = R[h][a] O_spa + o_ncri[h][a][:]
+ * (o_ncri [heads, nq, D] fp32 = a_rect V_cmp); other rows out = O_spa
+ * (_rectified_correction_fwd_kernel, bias_rectification_triton.py:9-95). */
+prism_status_t prism_correction_stats(const float* scores, int heads, int nq, int nk, int tq, int tk,
+                                      const uint32_t* bits_q, int64_t n_qt, int64_t n_kt,
+                                      const uint64_t* tile_bits, float sm_scale, float* R, float* M,
+                                      uint64_t* nonsel, float* a_rect, cudaStream_t stream);
+prism_status_t prism_taylor_prep(const uint64_t* nonsel, const float* M, const float* tau, int heads,
+                                 int64_t n_qt, int tq, int nq, int nk, int64_t n_ut, uint64_t* masks,
+                                 uint32_t* bits_t, cudaStream_t stream);
+prism_status_t prism_key_log_bias(const uint64_t* tile_bits, int nk, int tk, int n_pad, float sm_scale,
+                                  float* bias, cudaStream_t stream);
+prism_status_t prism_rows_to_bf16(const float* x, int heads, int n, int D, int n_pad, void* out,
+                                  cudaStream_t stream);
+prism_status_t prism_taylor_merge(const void* o_spa, const void* o_spa_lo, const float* lse_spa,
+                                  const void* o_t, const void* o_t_lo, const float* lse_t,
+                                  const float* M, const float* tau, int heads, int64_t S, int64_t seq_q,
+                                  int chunk_q, int D, void* out, cudaStream_t stream);
+prism_status_t prism_rectified_apply(const void* o_spa, const void* o_spa_lo, const float* R,
+                                     const float* o_ncri, int heads, int64_t S, int64_t seq_q, int chunk_q,
+                                     int D, void* out, cudaStream_t stream);
 
 /* Block-sparse attention backward (attn_bwd_bsa_varlen_triton,
  * bsa_interface.py:387-523): delta, then dK/dV over bits_k, then dQ over

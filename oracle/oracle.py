@@ -67,6 +67,9 @@ def lib():
         L.oracle_audio_saliency.argtypes = [P, i64, i32, P, P]
         L.oracle_audio_pool_weights.argtypes = [P, i64, i32, P, f32, P]
         L.oracle_guidance_scale.argtypes = [i64, P, f32, P, f32, f32, P, P]
+        L.oracle_uniform_pooled.argtypes = [P, P, i32, i64, i64, i32, i64, i64, i32, i32, P, P, P,
+                                            P, P]
+        L.oracle_correction_stats.argtypes = [P, i32, i32, i32, P, P, f32, P, P, P, P]
         _lib = L
     return _lib
 
@@ -261,6 +264,79 @@ def guidance_scale(n, rho=None, variance_gamma=0.0, saliency=None, gate=1.0, aud
     out = np.zeros(n, np.float32)
     lib().oracle_guidance_scale(n, _p(rho), float(variance_gamma), _p(saliency), float(gate),
                                 float(audio_gamma), _p(modifier), _p(out))
+    return out
+
+
+# ---------------------------------------------------------- bias rectification
+def uniform_pooled(q_re_bits, k_re_bits, seq_q, seq_k, chunk_q, chunk_k, q_valid, k_valid):
+    """oracle_uniform_pooled: (qc [h, nq, D], kc [h, nk, D], raw scores [h, nq, nk]) f32."""
+    q = np.ascontiguousarray(q_re_bits, np.uint16)
+    k = np.ascontiguousarray(k_re_bits, np.uint16)
+    heads, Sq, D = q.shape
+    Sk = k.shape[1]
+    nq, nk = seq_q // chunk_q, seq_k // chunk_k
+    qc = np.zeros((heads, nq, D), np.float32)
+    kc = np.zeros((heads, nk, D), np.float32)
+    sc = np.zeros((heads, nq, nk), np.float32)
+    qv = None if q_valid is None else np.ascontiguousarray(q_valid, np.uint8)
+    kv = None if k_valid is None else np.ascontiguousarray(k_valid, np.uint8)
+    lib().oracle_uniform_pooled(_p(q), _p(k), heads, Sq, Sk, D, seq_q, seq_k, chunk_q, chunk_k,
+                                _p(qv), _p(kv), _p(qc), _p(kc), _p(sc))
+    return qc, kc, sc
+
+
+def correction_stats(scores, sel, chunk_valid, sm_scale, want_a_rect=False):
+    """oracle_correction_stats: (R [h, nq], M [h, nq], nonsel [h, nq, ceil(nk/64)] u64,
+    a_rect [h, nq, nk] or None) from raw scores, the chunk selection and validity."""
+    sc = np.ascontiguousarray(scores, np.float32)
+    heads, nq, nk = sc.shape
+    sl = np.ascontiguousarray(sel, np.uint8)
+    cv = np.ascontiguousarray(chunk_valid, np.uint8)
+    R = np.zeros((heads, nq), np.float32)
+    M = np.zeros((heads, nq), np.float32)
+    nonsel = np.zeros((heads, nq, (nk + 63) // 64), np.uint64)
+    a_rect = np.zeros((heads, nq, nk), np.float32) if want_a_rect else None
+    lib().oracle_correction_stats(_p(sc), heads, nq, nk, _p(sl), _p(cv), float(sm_scale), _p(R),
+                                  _p(M), _p(nonsel), _p(a_rect))
+    return R, M, nonsel, a_rect
+
+
+def rectified_output(o_spa, R, a_rect, v_cmp, chunk_q):
+    """O' = R_n O_spa + (A_pool * unselected) V_cmp per q chunk, float64
+    (_rectified_correction_pytorch, bias_rectification.py:335-377).  o_spa [h, S, D]."""
+    h, S, D = o_spa.shape
+    o_ncri = np.einsum("hab,hbd->had", a_rect.astype(np.float64), v_cmp.astype(np.float64))
+    return (np.repeat(R.astype(np.float64), chunk_q, axis=1)[:, :, None] * o_spa
+            + np.repeat(o_ncri, chunk_q, axis=1))
+
+
+def taylor_output(q, o_spa, lse_spa, k_cmp, v_cmp, nonsel_dense, flat, log_counts, chunk_q,
+                  sm_scale):
+    """_taylor_merge_pytorch (bias_rectification.py:190-257) in float64: for flat q
+    chunks, softmax over the unselected pooled keys of q k_cmp * sm_scale + log
+    count, merged with the sparse output by log-sum-exp.  q, o_spa [h, S, D],
+    lse_spa [h, S] (natural log), k_cmp / v_cmp [h, nk, D], nonsel_dense
+    [h, nq, nk] bool, flat [h, nq] bool, log_counts [nk]."""
+    q = q.astype(np.float64)
+    out = o_spa.astype(np.float64).copy()
+    h, S, D = q.shape
+    for hh in range(h):
+        for a in np.nonzero(flat[hh])[0]:
+            rows = slice(a * chunk_q, (a + 1) * chunk_q)
+            m = nonsel_dense[hh, a]
+            if not m.any():
+                continue
+            z = q[hh, rows] @ k_cmp[hh, m].astype(np.float64).T * sm_scale + log_counts[m][None]
+            zm = z.max(axis=1, keepdims=True)
+            p = np.exp(z - zm)
+            l = p.sum(axis=1, keepdims=True)
+            lse_t = (zm + np.log(l))[:, 0]
+            o_t = (p / l) @ v_cmp[hh, m].astype(np.float64)
+            ls = lse_spa[hh, rows].astype(np.float64)
+            lm = np.maximum(ls, lse_t)
+            tot = lm + np.log(np.exp(ls - lm) + np.exp(lse_t - lm))
+            out[hh, rows] = (np.exp(ls - tot)[:, None] * out[hh, rows]
+                             + np.exp(lse_t - tot)[:, None] * o_t)
     return out
 
 

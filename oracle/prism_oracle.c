@@ -24,6 +24,9 @@
  *   oracle_audio_saliency     bsa_interface.py:1065-1102
  *   oracle_audio_pool_weights bsa_interface.py:902-970 (the weights)
  *   oracle_guidance_scale     bsa_interface.py:744-764, 1240-1245, 1467-1470
+ *   oracle_uniform_pooled     bsa_interface.py:164-207 (pooled chunks, raw scores)
+ *   oracle_correction_stats   bias_rectification.py:146-170, 421-436 (A_pool, R_n,
+ *                             variance M, unselected chunks)
  *
  * Floating-point order.  The reference leaves summation order to torch; this
  * restatement fixes one order (the one the CUDA kernels use) so that GPU and
@@ -906,4 +909,119 @@ void oracle_guidance_scale(int64_t n, const float* rho, float var_gamma, const f
     if (has_ext) boost = boost + ext;
     scale[c] = 1.0f + boost;
   }
+}
+
+/* ---------------------------------------------------- bias rectification */
+
+/* Pooled q / k chunks (fp32 sequential masked means, as oracle_block_select_uniform)
+ * and the raw chunk scores (fmaf chain over d).  qc [h, nq, D], kc [h, nk, D],
+ * scores [h, nq, nk]. */
+void oracle_uniform_pooled(const uint16_t* q_re, const uint16_t* k_re, int heads, int64_t Sq, int64_t Sk,
+                           int D, int64_t seq_q, int64_t seq_k, int chunk_q, int chunk_k,
+                           const uint8_t* q_valid, const uint8_t* k_valid, float* qc, float* kc,
+                           float* scores) {
+  const int64_t nq = seq_q / chunk_q, nk = seq_k / chunk_k;
+  for (int h = 0; h < heads; ++h) {
+    for (int pass = 0; pass < 2; ++pass) {
+      const uint16_t* x = pass ? k_re + (int64_t)h * Sk * D : q_re + (int64_t)h * Sq * D;
+      const int chunk = pass ? chunk_k : chunk_q;
+      const int64_t n = pass ? nk : nq;
+      const uint8_t* valid = pass ? k_valid : q_valid;
+      float* out = (pass ? kc : qc) + (int64_t)h * n * D;
+      for (int64_t c = 0; c < n; ++c) {
+        int cnt = 0;
+        for (int d = 0; d < D; ++d) out[c * D + d] = 0.0f;
+        for (int i = 0; i < chunk; ++i) {
+          const int64_t s = c * chunk + i;
+          if (valid && !valid[s]) continue;
+          ++cnt;
+          for (int d = 0; d < D; ++d) out[c * D + d] += bf16_to_f32(x[s * D + d]);
+        }
+        const float den = cnt > 0 ? (float)cnt : 1.0f;
+        for (int d = 0; d < D; ++d) out[c * D + d] = out[c * D + d] / den;
+      }
+    }
+    const float* qh = qc + (int64_t)h * nq * D;
+    const float* kh = kc + (int64_t)h * nk * D;
+    for (int64_t a = 0; a < nq; ++a)
+      for (int64_t b = 0; b < nk; ++b) {
+        float acc = 0.0f;
+        for (int d = 0; d < D; ++d) acc = fmaf(qh[a * D + d], kh[b * D + d], acc);
+        scores[((int64_t)h * nq + a) * nk + b] = acc;
+      }
+  }
+}
+
+/* Sum of 256 strided partials (partial t = sequential sum of x[j], j = t mod 256)
+ * combined by halving: p[t] += p[t + s], s = 128, ..., 1. */
+static float tree_sum256(const float* p_in) {
+  float p[256];
+  memcpy(p, p_in, sizeof(p));
+  for (int s = 128; s > 0; s >>= 1)
+    for (int t = 0; t < s; ++t) p[t] = p[t] + p[t + s];
+  return p[0];
+}
+
+/* Per head h and q chunk a: A = softmax over valid key chunks of score * sm_scale
+ * (deterministic exp), R = max(1 - sum of A over valid unselected chunks, 1e-6),
+ * M = variance of A over the valid chunks; sel [h, nq, nk] u8 is the chunk
+ * selection, chunk_valid [nk] u8.  nonsel [h, nq, ceil(nk/64)] u64 and a_rect
+ * [h, nq, nk] optional.  The operation order of prism_correction_stats. */
+void oracle_correction_stats(const float* scores, int heads, int nq, int nk, const uint8_t* sel,
+                             const uint8_t* chunk_valid, float sm_scale, float* R, float* M,
+                             uint64_t* nonsel, float* a_rect) {
+  float* e = (float*)malloc(sizeof(float) * nk);
+  const int wn = (nk + 63) / 64;
+  float part[256];
+  for (int h = 0; h < heads; ++h)
+    for (int a = 0; a < nq; ++a) {
+      const float* s = scores + ((int64_t)h * nq + a) * nk;
+      const uint8_t* sl = sel + ((int64_t)h * nq + a) * nk;
+      float mx = -INFINITY;
+      int cnt = 0;
+      for (int j = 0; j < nk; ++j) {
+        e[j] = chunk_valid[j] ? s[j] * sm_scale : -INFINITY;
+        if (e[j] > mx) mx = e[j];
+        cnt += chunk_valid[j] != 0;
+      }
+      for (int t = 0; t < 256; ++t) part[t] = 0.0f;
+      for (int j = 0; j < nk; ++j) {
+        e[j] = e[j] == -INFINITY ? 0.0f : oracle_det_expf(e[j] - mx);
+        part[j % 256] = part[j % 256] + e[j];
+      }
+      const float sum = tree_sum256(part);
+      float prect[256], pmean[256];
+      for (int t = 0; t < 256; ++t) prect[t] = pmean[t] = 0.0f;
+      for (int j = 0; j < nk; ++j) {
+        const float A = e[j] / sum;
+        e[j] = A;
+        const int rect = chunk_valid[j] && !sl[j];
+        if (rect) prect[j % 256] = prect[j % 256] + A;
+        if (chunk_valid[j]) pmean[j % 256] = pmean[j % 256] + A;
+        if (a_rect) a_rect[((int64_t)h * nq + a) * nk + j] = rect ? A : 0.0f;
+      }
+      const float rsum = tree_sum256(prect);
+      const float fn = cnt > 0 ? (float)cnt : 1.0f;
+      const float mean = tree_sum256(pmean) / fn;
+      for (int t = 0; t < 256; ++t) part[t] = 0.0f;
+      for (int j = 0; j < nk; ++j) {
+        if (!chunk_valid[j]) continue;
+        const float d = e[j] - mean;
+        part[j % 256] = part[j % 256] + d * d;
+      }
+      const float var = tree_sum256(part) / fn;
+      const float r = 1.0f - rsum;
+      R[(int64_t)h * nq + a] = r < 1e-6f ? 1e-6f : r;
+      M[(int64_t)h * nq + a] = var;
+      if (nonsel)
+        for (int w = 0; w < wn; ++w) {
+          uint64_t b = 0;
+          for (int i = 0; i < 64; ++i) {
+            const int j = w * 64 + i;
+            if (j < nk && chunk_valid[j] && !sl[j]) b |= 1ull << i;
+          }
+          nonsel[((int64_t)h * nq + a) * wn + w] = b;
+        }
+    }
+  free(e);
 }

@@ -12,10 +12,13 @@ Public entry points mirror the reference names:
   audio_weighted_mean_pooling_compression, compute_audio_spatial_concentration_gate,
   compute_timestep_reliability_gate   bsa_interface.py:831-1102 (guidance statistics)
   flash_attn_bsa_cross        block_sparse_attention/bsa_interface.py:1276 (3D / 1D cross-modal)
+  bsa_rectified_sparse_attn / bsa_taylor_sparse_attn
+                              block_sparse_attention/bias_rectification.py:380, 261 (inference)
   select_zone_shapes          block_sparse_attention/dynamic_block_shape.py:358
   all_to_all_4D / all_gather  hymm/utils/communications.py:277, 401
 The kernels live in libprism_bsa.so (C ABI: include/prism_bsa.h).
 """
+from .bias_rectification import bsa_rectified_sparse_attn, bsa_taylor_sparse_attn  # noqa: F401
 from .bsa_interface import (  # noqa: F401
     flash_attn_bsa_3d, flash_attn_bsa_3d_audio_guided, flash_attn_bsa_3d_variance_guided,
     flash_attn_bsa_cross, run_bsa_uniform,

@@ -42,6 +42,14 @@ SIGNATURES = {
     "prism_audio_pool_weights": (_I, [_P, _I64, _I, _P, _F, _P, _P]),
     "prism_guidance_scale": (_I, [_I64, _P, _F, _P, _P, _F, _P, _P, _P]),
     "prism_pool_chunks": (_I, [_P, _I, _I64, _I, _I64, _I, _P, _P, _P, _P]),
+    "prism_chunk_scores": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
+    "prism_bsa_fwd_keybias": (_I, [_P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P]),
+    "prism_correction_stats": (_I, [_P, _I, _I, _I, _I, _I, _P, _I64, _I64, _P, _F, _P, _P, _P, _P, _P]),
+    "prism_taylor_prep": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _P, _P, _P]),
+    "prism_key_log_bias": (_I, [_P, _I, _I, _I, _F, _P, _P]),
+    "prism_rows_to_bf16": (_I, [_P, _I, _I, _I, _I, _P, _P]),
+    "prism_taylor_merge": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _I, _P, _P]),
+    "prism_rectified_apply": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I, _I, _P, _P]),
     "prism_bsa_fwd_qk": (_I, [_P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_qk": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
@@ -62,7 +70,10 @@ KERNELS = {
     "prism_bsa_bwd_noalloc": 3, "prism_uniform_layout": 1, "prism_block_select_uniform": 4,
     "prism_bsa_fwd_qk": 1, "prism_bsa_bwd_qk": 3, "prism_gather_values": 1,
     "prism_variance_density": 2, "prism_audio_saliency": 2, "prism_audio_pool_weights": 1,
-    "prism_guidance_scale": 1, "prism_pool_chunks": 1,
+    "prism_guidance_scale": 1, "prism_pool_chunks": 1, "prism_chunk_scores": 1,
+    "prism_bsa_fwd_keybias": 1, "prism_correction_stats": 1, "prism_taylor_prep": 1,
+    "prism_key_log_bias": 1, "prism_rows_to_bf16": 1, "prism_taylor_merge": 1,
+    "prism_rectified_apply": 1,
 }
 launch_count = 0
 

@@ -39,7 +39,7 @@ import torch
 
 from . import ops
 from .dynamic_block_attention import SparsePlan, _BsaFunction, _check_head_dim, _hsd
-from .guidance import make_guidance
+from .guidance import guidance_inputs, make_guidance
 
 _TILE = 64
 _PAIR = 128  # the attention kernels work on whole 128-row tile pairs
@@ -301,6 +301,8 @@ def run_bsa_uniform(
     audio_boost_gamma=None,
     audio_weighted_lambda: float = 0.0,
     variance_boost_gamma: float = 0.0,
+    correction: Optional[str] = None,
+    taylor_alpha_f: float = 0.5,
 ):
     """The uniform dispatch (wan_video_dit.py:470-560, 637-672) on unpadded tokens:
     q, k, v [1, H, T*H*W, D] (layout="bhsd") or [1, T*H*W, H, D] (layout="bshd").
@@ -309,7 +311,11 @@ def run_bsa_uniform(
     Guidance as the dispatch picks it: variance_boost_gamma > 0 = the variance
     term; audio_token_norms [T*H*W] (unpadded) = the audio-guided path with gate
     audio_gate, gain audio_boost_gamma and Path B weight audio_weighted_lambda
-    (zero-padded norms, wan_video_dit.py:299-306).  Output has q's layout."""
+    (zero-padded norms, wan_video_dit.py:299-306).  correction = "rectified" or
+    "taylor" runs the bias-rectified forward instead (inference only, the
+    correction dispatch of wan_video_dit.py:550-640: the guidance then only scales
+    the selection's scores and Path B is ignored, as there).  Output has q's
+    layout."""
     if layout not in ("bhsd", "bshd"):
         raise ValueError("layout must be 'bhsd' or 'bshd'")
     T, H, W = grid_size
@@ -330,6 +336,18 @@ def run_bsa_uniform(
             audio_token_norms=audio_token_norms, audio_gate=audio_gate,
             audio_gamma=audio_boost_gamma, audio_weighted_lambda=float(audio_weighted_lambda or 0.0),
             n_chunks_k=nk, device=q.device)
+    if correction is not None:
+        from .bias_rectification import run_corrected
+        scale = None
+        g = plan.uniform.pop("guidance", None)
+        if g is not None:
+            g = dict(g, lambda_w=0.0)
+            with torch.no_grad():
+                v_re = ops.gather_rows(_hsd(v, layout), plan.grid_k, plan.grid_padded_k,
+                                       plan.src_idx_k) if g["variance_gamma"] > 0 else None
+                _, scale = guidance_inputs(plan, g, v_re)
+        out = run_corrected(q, k, v, plan, layout, correction, taylor_alpha_f, scale)
+        return (out, plan) if return_plan else out
     out = _BsaFunction.apply(q, k, v, plan, layout)
     return (out, plan) if return_plan else out
 

@@ -2,8 +2,9 @@
 
     python -m prism_b200.build          # or prism_b200.build.build()
 
-Selection-side sources are compiled with -fmad=false (every floating-point
-step rounds once, in a fixed order); attention kernels use default contraction.
+Selection-side and correction-statistics sources are compiled with -fmad=false
+(every floating-point step rounds once, in a fixed order); attention kernels use
+default contraction.
 """
 from __future__ import annotations
 
@@ -23,6 +24,7 @@ COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path
           "--expt-relaxed-constexpr"]
 SOURCES = {
     "select_kernels.cu": ["-fmad=false"],
+    "correction_kernels.cu": ["-fmad=false"],
     "bsa_tc.cu": [],
 }
 

@@ -343,13 +343,37 @@ struct FwdLayout {
   static constexpr int T_S = 0, T_O = 128;
 };
 
-template <int D>
+// Per-key score offset (the kKeyBias form of the forward): S[r][c] += bias[64 t + c]
+// for key tile t, in units of raw scores (a log-weight w becomes w / sm_scale).
+template <bool kKeyBias>
+__device__ __forceinline__ void add_key_bias(float (&s)[64], const float* __restrict__ key_bias,
+                                             int t) {
+  if constexpr (kKeyBias) {
+    const float4* b4 = reinterpret_cast<const float4*>(key_bias + (int64_t)t * 64);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 b = __ldg(b4 + i);
+      s[4 * i] += b.x;
+      s[4 * i + 1] += b.y;
+      s[4 * i + 2] += b.z;
+      s[4 * i + 3] += b.w;
+    }
+  }
+}
+
+// kKeyBias = false: the block-sparse forward (key validity tile_bits[key tile],
+// shared by every query tile and head).  kKeyBias = true: the same kernel with a
+// per-key score offset key_bias [Sk] and key masks per (head, query tile, key
+// tile) at tile_bits[h * tb_hstride + q_tile * tb_qstride + key tile] (the
+// pooled-key pass of the Taylor merge).
+template <int D, bool kKeyBias = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, int64_t Sq, int64_t Sk, int wq, float qk_scale,
                   const uint32_t* __restrict__ bits_q, const uint64_t* __restrict__ tile_bits,
                   __nv_bfloat16* __restrict__ o, __nv_bfloat16* __restrict__ o_lo,
-                  float* __restrict__ lse) {
+                  float* __restrict__ lse, const float* __restrict__ key_bias = nullptr,
+                  int64_t tb_hstride = 0, int64_t tb_qstride = 0) {
   using L = FwdLayout<D>;
   constexpr int R = L::kRing;
   extern __shared__ uint8_t smem_raw[];
@@ -550,14 +574,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + g * 256;
     float m = -INFINITY, l = 1.0f;
     const uint32_t* my_row = r0 + sbit * wq;  // this thread's q tile's bitmap row
+    const uint64_t* tb = tile_bits;            // key masks of this thread's q tile
+    if constexpr (kKeyBias) tb += (int64_t)h * tb_hstride + (4 * (int64_t)quad + sbit) * tb_qstride;
     int n = 0, t0, t1, mask;                   // n: this group's steps
     bool ok = true;
     for (int step = 0; step < sched.total; ++step) {
       sched.step(step, t0, t1, mask);
       if (!((mask >> g) & 1)) continue;
-      const uint64_t vb0 = ((__ldg(my_row + (t0 >> 5)) >> (t0 & 31)) & 1u) ? tile_bits[t0] : 0ull;
+      const uint64_t vb0 = ((__ldg(my_row + (t0 >> 5)) >> (t0 & 31)) & 1u) ? tb[t0] : 0ull;
       const uint64_t vb1 =
-          (t1 >= 0 && ((__ldg(my_row + (t1 >> 5)) >> (t1 & 31)) & 1u)) ? tile_bits[t1] : 0ull;
+          (t1 >= 0 && ((__ldg(my_row + (t1 >> 5)) >> (t1 & 31)) & 1u)) ? tb[t1] : 0ull;
       if (!warp_wait(bar(L::B_SF + g), n & 1, abort_flag, kErrFwdSoftmax)) {
         ok = false;
         break;
@@ -582,6 +608,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         } else {
           float sv[64];
           tmem_load<2>(t_lane + L::T_S, sv);
+          add_key_bias<kKeyBias>(sv, key_bias, t0);
           if (vb0 != ~0ull) {
 #pragma unroll
             for (int c = 0; c < 64; ++c)
@@ -611,6 +638,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (vb == 0ull) continue;  // warp-uniform: the whole half-row of this tile is masked
           float s[64];
           tmem_load<2>(t_lane + L::T_S + u * 64, s);
+          add_key_bias<kKeyBias>(s, key_bias, u ? t1 : t0);
           float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
           if (vb == ~0ull) {
 #pragma unroll
@@ -660,6 +688,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           } else {
             float s[64];
             tmem_load<2>(t_lane + L::T_S + u * 64, s);
+            add_key_bias<kKeyBias>(s, key_bias, u ? t1 : t0);
             if (vb != ~0ull) {
 #pragma unroll
               for (int c = 0; c < 64; ++c)
@@ -689,6 +718,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         } else {
           float sv[64];
           tmem_load<2>(t_lane + L::T_S + 64, sv);
+          add_key_bias<kKeyBias>(sv, key_bias, t1);
           if (vb1 != ~0ull) {
 #pragma unroll
             for (int c = 0; c < 64; ++c)
@@ -738,6 +768,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (vb1 != 0ull) {
             float sv[64];
             tmem_load<2>(t_lane + L::T_S + 64, sv);
+            add_key_bias<kKeyBias>(sv, key_bias, t1);
             if (vb1 != ~0ull) {
 #pragma unroll
               for (int c = 0; c < 64; ++c)
@@ -1781,10 +1812,12 @@ static prism_status_t make_map(CUtensorMap* map, const void* ptr, int64_t rows, 
     if (st_ != PRISM_OK) return st_;       \
   } while (0)
 
-template <int D>
+template <int D, bool kKeyBias = false>
 prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads, int64_t Sq,
                           int64_t Sk, float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
-                          void* o, void* o_lo, float* lse, cudaStream_t stream) {
+                          void* o, void* o_lo, float* lse, cudaStream_t stream,
+                          const float* key_bias = nullptr, int64_t tb_hstride = 0,
+                          int64_t tb_qstride = 0) {
   const int64_t n_tiles = Sq / 64, n_ktiles = Sk / 64;
   const int wq = (int)((n_ktiles + 31) / 32);
   const size_t need = FwdLayout<D>::bytes(n_ktiles);
@@ -1796,11 +1829,12 @@ prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads
   PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_fwd"));
   PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_fwd"));
   PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_fwd"));
-  PRISM_CHECK_CUDA(cudaFuncSetAttribute(fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(fwd_tc_kernel<D, kKeyBias>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                    "prism_bsa_fwd: smem attribute");
-  fwd_tc_kernel<D><<<dim3((unsigned)((n_tiles + 3) / 4), heads), kFwdThreads, sm, stream>>>(
+  fwd_tc_kernel<D, kKeyBias><<<dim3((unsigned)((n_tiles + 3) / 4), heads), kFwdThreads, sm, stream>>>(
       mq, mk, mv, Sq, Sk, wq, sm_scale * kRcpLn2, bits_q, tile_bits, (__nv_bfloat16*)o,
-      (__nv_bfloat16*)o_lo, lse);
+      (__nv_bfloat16*)o_lo, lse, key_bias, tb_hstride, tb_qstride);
   PRISM_CHECK_LAUNCH("prism_bsa_fwd");
   return PRISM_OK;
 }
@@ -1921,6 +1955,24 @@ prism_status_t prism_bsa_fwd_qk(const void* q, const void* k, const void* v, int
   PRISM_CHECK_ARG(o_lo == nullptr || aligned16(o_lo), "prism_bsa_fwd: o_lo must be 16-byte aligned");
   if (D == 128) return tc::launch_fwd<128>(q, k, v, heads, Sq, Sk, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
   return tc::launch_fwd<64>(q, k, v, heads, Sq, Sk, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
+}
+
+prism_status_t prism_bsa_fwd_keybias(const void* q, const void* k, const void* v, int heads, int64_t Sq,
+                                     int64_t Sk, int D, float sm_scale, const uint32_t* bits_q,
+                                     const uint64_t* key_masks, const float* key_bias, void* o,
+                                     void* o_lo, float* lse, cudaStream_t stream) {
+  PRISM_CHECK_ARG(q && k && v && bits_q && key_masks && key_bias && o && lse,
+                  "prism_bsa_fwd_keybias: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_bsa_fwd_keybias", Sq, Sk);
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) && aligned16(key_bias),
+                  "prism_bsa_fwd_keybias: tensors must be 16-byte aligned");
+  PRISM_CHECK_ARG(o_lo == nullptr || aligned16(o_lo), "prism_bsa_fwd_keybias: o_lo must be 16-byte aligned");
+  const int64_t n_qt = Sq / 64, n_kt = Sk / 64;
+  if (D == 128)
+    return tc::launch_fwd<128, true>(q, k, v, heads, Sq, Sk, sm_scale, bits_q, key_masks, o, o_lo, lse,
+                                     stream, key_bias, n_qt * n_kt, n_kt);
+  return tc::launch_fwd<64, true>(q, k, v, heads, Sq, Sk, sm_scale, bits_q, key_masks, o, o_lo, lse,
+                                  stream, key_bias, n_qt * n_kt, n_kt);
 }
 
 prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int heads, int64_t S,

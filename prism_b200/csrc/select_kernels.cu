@@ -1586,6 +1586,19 @@ prism_status_t prism_audio_pool_weights(const float* norms_re, int64_t seq_k, in
   return PRISM_OK;
 }
 
+prism_status_t prism_chunk_scores(const float* qc, const float* kc, int heads, int nq, int nk, int D,
+                                  float* scores, cudaStream_t stream) {
+  PRISM_CHECK_ARG(qc && kc && scores, "prism_chunk_scores: null pointer");
+  PRISM_CHECK_ARG(heads >= 1 && nq >= 1 && nk >= 1 && D >= 16 && D <= 256, "prism_chunk_scores: bad sizes");
+  const size_t ssm = 2 * (size_t)D * (kScoreTile + 4) * sizeof(float);
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),
+                   "prism_chunk_scores: smem attribute");
+  score_kernel<<<dim3((nk + kScoreTile - 1) / kScoreTile, (nq + kScoreTile - 1) / kScoreTile, heads), 256,
+                 ssm, stream>>>(qc, kc, D, nullptr, nq, nk, nullptr, scores);
+  PRISM_CHECK_LAUNCH("prism_chunk_scores");
+  return PRISM_OK;
+}
+
 prism_status_t prism_pool_chunks(const void* x_re, int heads, int64_t S, int D, int64_t seq,
                                 int chunk, const uint64_t* bits, const float* weights, float* out,
                                 cudaStream_t stream) {

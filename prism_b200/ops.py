@@ -207,11 +207,13 @@ def uniform_layout(grid_padded, chunk, n_rows: int, device):
 
 
 def block_select_uniform(q_re, k_re, seq_q: int, seq_k: int, chunk_q: int, chunk_k: int, q_bits,
-                         k_bits, sparsity, cdf_threshold, k_weights=None, col_scale=None):
-    """Chunk pooling + scores + selection of the uniform path -> (bits_q, bits_k).
-    q_bits: rows the q pooling counts (None: all); k_bits: key validity.
-    k_weights [seq_k] fp32: per-row key pooling weights (Path B) instead of k_bits;
-    col_scale [seq_k/chunk_k] fp32: per-key-chunk score scale (guided selection)."""
+                         k_bits, sparsity, cdf_threshold, k_weights=None, col_scale=None,
+                         want_pooled: bool = False):
+    """Chunk pooling + scores + selection of the uniform path -> (bits_q, bits_k)
+    (+ dict(qc, kc, scores) of the pooled chunks and their (scaled) scores with
+    want_pooled).  q_bits: rows the q pooling counts (None: all); k_bits: key
+    validity.  k_weights [seq_k] fp32: per-row key pooling weights (Path B) instead
+    of k_bits; col_scale [seq_k/chunk_k] fp32: per-key-chunk score scale."""
     _check_cuda(q_re, k_re, q_bits, k_bits, k_weights, col_scale)
     heads, Sq, D = q_re.shape
     Sk = k_re.shape[1]
@@ -230,7 +232,107 @@ def block_select_uniform(q_re, k_re, seq_q: int, seq_k: int, chunk_q: int, chunk
               float(sparsity if sparsity is not None else 0.0),
               float(cdf_threshold if cdf_threshold is not None else 0.0), _p(ws), _p(bits_q),
               _p(bits_k), _stream(q_re))
+    if want_pooled:
+        nq, nk = seq_q // chunk_q, seq_k // chunk_k
+        f = ws.view(torch.float32)
+        qc = f[:heads * nq * D].view(heads, nq, D)
+        kc = f[heads * nq * D:heads * (nq + nk) * D].view(heads, nk, D)
+        sc = f[heads * (nq + nk) * D:heads * (nq + nk) * D + heads * nq * nk].view(heads, nq, nk)
+        return bits_q, bits_k, dict(qc=qc, kc=kc, scores=sc)
     return bits_q, bits_k
+
+
+# --------------------------------------------------------- bias rectification
+def chunk_scores(qc: torch.Tensor, kc: torch.Tensor) -> torch.Tensor:
+    """Raw chunk scores [heads, nq, nk] fp32 of pooled q / k chunks."""
+    _check_cuda(qc, kc)
+    heads, nq, D = qc.shape
+    nk = kc.shape[1]
+    out = torch.empty(heads, nq, nk, dtype=torch.float32, device=qc.device)
+    _lib.call("prism_chunk_scores", _p(qc), _p(kc), heads, nq, nk, D, _p(out), _stream(qc))
+    return out
+
+
+def correction_stats(scores, bits_q, tile_bits, tq: int, tk: int, sm_scale: float, *,
+                     want_nonsel: bool = False, want_a_rect: bool = False):
+    """(R, M, nonsel, a_rect) of the bias rectification (see prism_correction_stats)."""
+    _check_cuda(scores, bits_q, tile_bits)
+    heads, nq, nk = scores.shape
+    n_qt, n_kt = bits_q.shape[1], tile_bits.shape[0]
+    dev = scores.device
+    R = torch.empty(heads, nq, dtype=torch.float32, device=dev)
+    M = torch.empty(heads, nq, dtype=torch.float32, device=dev)
+    nonsel = (torch.empty(heads, nq, (nk + 63) // 64, dtype=torch.int64, device=dev)
+              if want_nonsel else None)
+    a_rect = torch.empty(heads, nq, nk, dtype=torch.float32, device=dev) if want_a_rect else None
+    _lib.call("prism_correction_stats", _p(scores), heads, nq, nk, tq, tk, _p(bits_q), n_qt, n_kt,
+              _p(tile_bits), float(sm_scale), _p(R), _p(M), _p(nonsel), _p(a_rect), _stream(scores))
+    return R, M, nonsel, a_rect
+
+
+def taylor_prep(nonsel, M, tau, n_qt: int, tq: int, nk: int, n_ut: int):
+    """(masks [heads, n_qt, n_ut] u64, bits_t [heads, n_qt, ceil(n_ut/32)]) of the pooled-key pass."""
+    _check_cuda(nonsel, M, tau)
+    heads, nq = M.shape
+    dev = M.device
+    masks = torch.empty(heads, n_qt, n_ut, dtype=torch.int64, device=dev)
+    bits_t = torch.empty(heads, n_qt, (n_ut + 31) // 32, dtype=torch.int32, device=dev)
+    _lib.call("prism_taylor_prep", _p(nonsel), _p(M), _p(tau), heads, n_qt, tq, nq, nk, n_ut,
+              _p(masks), _p(bits_t), _stream(M))
+    return masks, bits_t
+
+
+def key_log_bias(tile_bits, nk: int, tk: int, n_pad: int, sm_scale: float) -> torch.Tensor:
+    _check_cuda(tile_bits)
+    out = torch.empty(n_pad, dtype=torch.float32, device=tile_bits.device)
+    _lib.call("prism_key_log_bias", _p(tile_bits), nk, tk, n_pad, float(sm_scale), _p(out),
+              _stream(tile_bits))
+    return out
+
+
+def rows_to_bf16(x: torch.Tensor, n_pad: int) -> torch.Tensor:
+    """fp32 [heads, n, D] -> bf16 [heads, n_pad, D], zero rows past n."""
+    _check_cuda(x)
+    heads, n, D = x.shape
+    xc = x.contiguous()
+    out = torch.empty(heads, n_pad, D, dtype=torch.bfloat16, device=x.device)
+    _lib.call("prism_rows_to_bf16", _p(xc), heads, n, D, n_pad, _p(out), _stream(x))
+    return out
+
+
+def bsa_fwd_keybias(q_re, k_re, v_re, bits_q, key_masks, key_bias, sm_scale: float):
+    """Forward with per-(head, q tile, key tile) key masks and per-key score offsets
+    -> (o, lse, o_lo)."""
+    _check_cuda(q_re, k_re, v_re, bits_q, key_masks, key_bias)
+    heads, Sq, D = q_re.shape
+    Sk = k_re.shape[1]
+    o = torch.empty_like(q_re)
+    o_lo = torch.empty_like(q_re)
+    lse = torch.empty(heads, Sq, dtype=torch.float32, device=q_re.device)
+    _lib.call("prism_bsa_fwd_keybias", _p(q_re), _p(k_re), _p(v_re), heads, Sq, Sk, D,
+              float(sm_scale), _p(bits_q), _p(key_masks), _p(key_bias), _p(o), _p(o_lo), _p(lse),
+              _stream(q_re))
+    return o, lse, o_lo
+
+
+def taylor_merge(o_spa, o_spa_lo, lse_spa, o_t, o_t_lo, lse_t, M, tau, seq_q: int, chunk_q: int,
+                 out=None):
+    _check_cuda(o_spa, lse_spa, o_t, lse_t, M, tau)
+    heads, S, D = o_spa.shape
+    out = torch.empty_like(o_spa) if out is None else out
+    _lib.call("prism_taylor_merge", _p(o_spa), _p(o_spa_lo), _p(lse_spa), _p(o_t), _p(o_t_lo),
+              _p(lse_t), _p(M), _p(tau), heads, S, seq_q, chunk_q, D, _p(out), _stream(o_spa))
+    return out
+
+
+def rectified_apply(o_spa, o_spa_lo, R, o_ncri, seq_q: int, chunk_q: int, out=None):
+    _check_cuda(o_spa, R, o_ncri)
+    heads, S, D = o_spa.shape
+    out = torch.empty_like(o_spa) if out is None else out
+    oc = o_ncri.contiguous()
+    _lib.call("prism_rectified_apply", _p(o_spa), _p(o_spa_lo), _p(R), _p(oc), heads, S, seq_q,
+              chunk_q, D, _p(out), _stream(o_spa))
+    return out
 
 
 # --------------------------------------------------------- guided selection

@@ -48,6 +48,10 @@ class Case:
     # kind "variance" (variance_gamma) or "audio" (gate, audio_gamma, lambda_w,
     # variance_gamma)
     guidance: Optional[dict] = None
+    # bias rectification of the uniform path (bsa_rectified_sparse_attn /
+    # bsa_taylor_sparse_attn, bias_rectification.py:261-446) when set: kind
+    # "rectified" or "taylor" (alpha_f), optional variance_gamma for a score modifier
+    correction: Optional[dict] = None
 
     @property
     def uniform(self):
@@ -135,7 +139,28 @@ GUIDED_CASES = {
                         seed=83, guidance=dict(kind="audio", gate=0.75, audio_gamma=1.0,
                                                lambda_w=0.0, variance_gamma=0.5)),
 }
-UNIFORM_CASES_ALL = dict(UNIFORM_CASES, **GUIDED_CASES)
+# Bias rectification (inference): the sparse output corrected for the mass of the
+# chunks the selection dropped, on inputs already in the 3D-chunk order.
+CORRECTION_CASES = {
+    # Rectified SpaAttn on a padded grid, 4x4x4 chunks, top-k + cdf
+    "r_rect_pad": Case("r_rect_pad", (6, 10, 12), 2, 64, values="aniso", amp=(0.05, 1.0),
+                       audio=False, sparsity=0.75, cdf_threshold=0.5, chunk_q=(4, 4, 4),
+                       chunk_k=(4, 4, 4), seed=90, correction=dict(kind="rectified")),
+    # Rectified with a variance score modifier (selection on modified scores, A_pool on raw)
+    "r_rect_mod": Case("r_rect_mod", (8, 12, 16), 2, 128, values="aniso", amp=(0.1, 1.0),
+                       audio=False, sparsity=0.75, cdf_threshold=None, chunk_q=(4, 4, 4),
+                       chunk_k=(4, 4, 4), seed=91,
+                       correction=dict(kind="rectified", variance_gamma=1.0)),
+    # Taylor (LIVEditor) merge on a padded grid, median split of the chunk variances
+    "r_taylor_pad": Case("r_taylor_pad", (6, 10, 12), 2, 64, values="aniso", amp=(0.05, 1.0),
+                         audio=False, sparsity=0.75, cdf_threshold=0.5, chunk_q=(4, 4, 4),
+                         chunk_k=(4, 4, 4), seed=92, correction=dict(kind="taylor", alpha_f=0.5)),
+    # Taylor with 128-token chunks, head_dim 128, no padding, cumulative mass only
+    "r_taylor_d128": Case("r_taylor_d128", (8, 16, 16), 2, 128, values="aniso", amp=(0.1, 1.0),
+                          audio=False, sparsity=None, cdf_threshold=0.6, chunk_q=(4, 4, 8),
+                          chunk_k=(4, 4, 8), seed=93, correction=dict(kind="taylor", alpha_f=0.3)),
+}
+UNIFORM_CASES_ALL = dict(UNIFORM_CASES, **GUIDED_CASES, **CORRECTION_CASES)
 
 ALL_CASES = dict(CASES, **UNIFORM_CASES_ALL)
 

@@ -66,6 +66,11 @@ def import_reference(root):
     return dba, dbs, bsa
 
 
+def import_bias_rectification():
+    from hymm.models.modules.block_sparse_attention import bias_rectification as br
+    return br
+
+
 def run_case(dba, dbs, case):
     from oracle.oracle import dense_to_bits, tile_lists_to_dense
 
@@ -268,6 +273,77 @@ def run_uniform_case(bsa, case):
     return res
 
 
+def run_correction_case(bsa, br, case):
+    """bsa_rectified_sparse_attn / bsa_taylor_sparse_attn (bias_rectification.py:
+    261-446) under no_grad on CPU (the PyTorch merge, the reference's definition of
+    the fused inference kernels), on fp32 values in the 3D-chunk order as the
+    correction dispatch of wan_video_dit.py:550-640 passes them.  Stores the chunk
+    selection, the reference's R_n, M_n (and is_flat), and the corrected output on
+    a fixed subset of rows (chunk order)."""
+    from oracle.oracle import dense_to_bits
+
+    inp = make_inputs(case)
+    c = case.correction
+    Tp, Hp, Wp = case.grid_padded
+    S = Tp * Hp * Wp
+    D = case.head_dim
+    (tq, hq, wq), (tk, hk, wk) = case.chunk_q, case.chunk_k
+    cq, ck = tq * hq * wq, tk * hk * wk
+    n3q = (Tp // tq, Hp // hq, Wp // wq)
+    n3k = (Tp // tk, Hp // hk, Wp // wk)
+    q_ro = bsa.rearrange_THW_to_3d_block(inp["q"].float(), *n3q, tq, hq, wq, D)
+    k_ro = bsa.rearrange_THW_to_3d_block(inp["k"].float(), *n3k, tk, hk, wk, D)
+    v_ro = bsa.rearrange_THW_to_3d_block(inp["v"].float(), *n3k, tk, hk, wk, D)
+    valid = inp["valid"]
+    vm = None if valid is None else bsa.rearrange_THW_to_3d_block_1d(valid, *n3k, tk, hk, wk)
+    sm = 1.0 / D ** 0.5
+    mod = None
+    if c.get("variance_gamma", 0.0) > 0:
+        rho = bsa.compute_channel_variance_density(v_ro, ck, tk, hk, wk, vm)
+        mod = (1.0 + c["variance_gamma"] * rho.view(1, 1, 1, -1)).contiguous()
+    captured = []
+    orig = br.attn_fwd_bsa_varlen_triton
+
+    def capture(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2):
+        captured.append(dict(bi=block_indices.clone(), lens=lens.clone()))
+        return orig(q_, k_, v_, sm_scale, block_indices, lens, *a, **kw2)
+
+    kw = dict(chunk_size_q=cq, chunk_size_k=ck, sparsity=case.sparsity,
+              cdf_threshold=case.cdf_threshold, sm_scale=sm, kv_valid_mask=vm, score_modifier=mod)
+    try:
+        br.attn_fwd_bsa_varlen_triton = capture
+        with torch.no_grad():
+            if c["kind"] == "taylor":
+                out = br.bsa_taylor_sparse_attn(q_ro, k_ro, v_ro, alpha_f=c["alpha_f"], **kw)
+            else:
+                out = br.bsa_rectified_sparse_attn(q_ro, k_ro, v_ro, **kw)
+    finally:
+        br.attn_fwd_bsa_varlen_triton = orig
+    sel = captured.pop()
+    nk = S // ck
+    dense = chunk_lists_to_dense(sel["bi"].numpy(), sel["lens"].numpy(), nk)
+    with torch.no_grad():
+        q_cmp, k_cmp = br._pool_qk(q_ro, k_ro, cq, ck, vm, None)
+        raw = bsa.cal_score(q_cmp, k_cmp)
+        bv = None if vm is None else br._compute_block_valid_mask(vm, ck)
+        A = br._masked_softmax_along_last(raw, sm, bv)
+        rect = torch.from_numpy(~dense)[None]
+        if bv is not None:
+            rect = rect & bv.view(1, 1, 1, -1)
+        R = (1.0 - (A * rect.to(A.dtype)).sum(dim=-1)).clamp(min=1e-6)
+        M = br._masked_var_along_last(A, bv)
+    res = dict(sel_chunks_f32=dense_to_bits(dense), R=R[0].numpy(), M=M[0].numpy())
+    if c["kind"] == "taylor":
+        res["tau"] = np.array(float(torch.quantile(M.float().reshape(-1), c["alpha_f"])))
+    o = out[0].numpy()
+    rng = np.random.default_rng(1234)
+    rows = np.sort(rng.choice(S, size=min(S, 4 * N_ROWS), replace=False))
+    res["rows"] = rows.astype(np.int64)
+    res["o"] = o[:, rows]
+    res["sums"] = np.array([np.abs(o).astype(np.float64).sum()])
+    return res
+
+
 def run_cross_case(bsa, case):
     """flash_attn_bsa_cross (bsa_interface.py:1276-1392) on unpadded inputs.  Stores
     the chunk-level selection of a bf16 and an fp32 pass and the fp32 output / dQ on
@@ -338,6 +414,11 @@ def main():
             print(f"{name}: cross -> {path} ({os.path.getsize(path)} B)")
             continue
         case = ALL_CASES[name]
+        if case.correction is not None:
+            res = run_correction_case(bsa, import_bias_rectification(), case)
+            np.savez_compressed(path, **res)
+            print(f"{name}: {case.correction['kind']} -> {path} ({os.path.getsize(path)} B)")
+            continue
         if case.uniform:
             res = run_uniform_case(bsa, case)
             np.savez_compressed(path, **res)
