@@ -144,19 +144,38 @@ def attend(q, k, v, a2v, S):
     """The layer's attention core through the package's public API (either path)."""
     from prism_b200.attention import dynamic_self_attention, uniform_self_attention
     if CONFIG.get("path") == "uniform":
+        g = CONFIG.get("guidance", "none")
+        gkw = {}
+        if g in ("variance", "audio_variance"):
+            gkw["variance_boost_gamma"] = 1.0
+        if g in ("audio", "audio_variance"):
+            gkw.update(a2v_bridge_residual=a2v, audio_boost_gamma=1.0, audio_weighted_lambda=1.0)
+        corr = CONFIG.get("correction", "none")
+        if corr != "none":
+            gkw.update(correction=corr, taylor_alpha_f=0.5)
         return uniform_self_attention(q, k, v, CONFIG["grid"], CONFIG["heads"], full_seq_len=S,
                                       sparsity=CONFIG["sparsity"],
                                       cdf_threshold=CONFIG["cdf_threshold"],
                                       chunk_3d_shape_q=CONFIG["chunk"],
-                                      chunk_3d_shape_k=CONFIG["chunk"])
+                                      chunk_3d_shape_k=CONFIG["chunk"], **gkw)
     return dynamic_self_attention(q, k, v, CONFIG["grid"], CONFIG["heads"], a2v_bridge_residual=a2v,
                                   full_seq_len=S, method=CONFIG["method"],
                                   sparsity=CONFIG["sparsity"],
                                   cdf_threshold=CONFIG["cdf_threshold"])
 
 
+def inference_only():
+    """The bias-rectified path runs forward only (inference)."""
+    return CONFIG.get("correction", "none") != "none"
+
+
 def make_step(inp, S, world, capture=None):
+    import torch
+
     def step(q, k, v, do, a2v):
+        if inference_only():
+            with torch.no_grad():
+                return attend(q, k, v, a2v, S)
         x = attend(q, k, v, a2v, S)
         x.backward(do)
         return x
@@ -337,6 +356,13 @@ def main():
                     help="dynamic block shapes (flash_attn_bsa_3d_dynamic, the metric's path) or "
                          "the uniform fixed-shape path (flash_attn_bsa_3d, 4x4x4 chunks, "
                          "sparsity 0.75, cdf 0.2)")
+    ap.add_argument("--guidance", default="none",
+                    choices=["none", "variance", "audio", "audio_variance"],
+                    help="--path uniform: guided selection (variance density gain 1; audio "
+                         "saliency gain 1 with Path B pooling weight 1)")
+    ap.add_argument("--correction", default="none", choices=["none", "rectified", "taylor"],
+                    help="--path uniform: bias-rectified forward (inference: the step is the "
+                         "forward alone, the metric its effective TFLOPS)")
     ap.add_argument("--heads", type=int, default=CONFIG["heads"],
                     help="attention heads of the layer (40 in every benchmark config; smaller only "
                          "for profiler captures)")
@@ -345,9 +371,16 @@ def main():
     CONFIG["heads"] = args.heads
     CONFIG["path"] = args.path
     if args.path == "uniform":
-        CONFIG.update(UNIFORM, method=None)
+        CONFIG.update(UNIFORM, method=None, guidance=args.guidance, correction=args.correction)
         CONFIG["workload"] = CONFIG["workload"].replace(
             "dynamic BSA", "uniform BSA (4x4x4 chunks, sparsity 0.75, cdf 0.2)")
+        if args.guidance != "none":
+            CONFIG["workload"] += f", {args.guidance}-guided selection"
+        if args.correction != "none":
+            CONFIG["workload"] = CONFIG["workload"].replace(
+                "fwd+bwd", f"forward with {args.correction} bias rectification (inference)")
+    elif args.guidance != "none" or args.correction != "none":
+        ap.error("--guidance / --correction need --path uniform")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -394,6 +427,8 @@ def main():
     do, a2v = inp["do"], inp["a2v"]
     step = make_step(inp, S, world)
 
+    infer = inference_only()
+
     def run_step():
         q.grad = k.grad = v.grad = None
         step(q, k, v, do, a2v)
@@ -435,7 +470,7 @@ def main():
     total_pairs = float(pt[0].item())
     total_executed = float(pt[1].item())
     D = CONFIG["head_dim"]
-    flops = FWD_BWD_FACTOR * 4 * D * 64 * 64 * total_pairs
+    flops = (1.0 if infer else FWD_BWD_FACTOR) * 4 * D * 64 * 64 * total_pairs
     tflops = flops / (ms * 1e-3) / 1e12
     Tp, Hp, Wp = padded_grid()
     n_tiles = Tp * Hp * Wp // 64
@@ -454,7 +489,7 @@ def main():
     # computes 2 of them (QK^T, PV), dK/dV 4 (S^T, dP^T, dV, dK), dQ 3 (S, dP, dQ)
     mm = 2 * 64 * 64 * D * local_pairs
     algo = {"bsa_fwd": 2 * mm, "bsa_bwd_dkdv": 4 * mm, "bsa_bwd_dq": 3 * mm}
-    dom = max(("bsa_fwd", "bsa_bwd_dkdv", "bsa_bwd_dq"), key=lambda n: kt[n])
+    dom = "bsa_fwd" if infer else max(("bsa_fwd", "bsa_bwd_dkdv", "bsa_bwd_dq"), key=lambda n: kt[n])
     achieved = algo[dom] / (kt[dom] * 1e-3) / 1e12
     traffic = None
     if args.config == "720p" and D == 128 and args.path == "dynamic":
@@ -470,10 +505,22 @@ def main():
     e2e = None
     if not args.no_e2e:
         host = {n: inp[n].detach().cpu().pin_memory() for n in ("q", "k", "v", "do", "a2v")}
-        outs = {n: torch.empty(inp["q"].shape, dtype=torch.bfloat16).pin_memory() for n in ("o", "dq", "dk", "dv")}
+        outs = {n: torch.empty(inp["q"].shape, dtype=torch.bfloat16).pin_memory()
+                for n in (("o",) if infer else ("o", "dq", "dk", "dv"))}
         h2d = sum(x.numel() * x.element_size() for x in host.values())
         d2h = sum(x.numel() * x.element_size() for x in outs.values())
+        if infer:
+            host.pop("do")
+            h2d = sum(x.numel() * x.element_size() for x in host.values())
+
         def e2e_step():
+            if infer:
+                with torch.no_grad():
+                    dq_, dk_, dv_, aa = (host[n].to(dev, non_blocking=True)
+                                         for n in ("q", "k", "v", "a2v"))
+                    x = attend(dq_, dk_, dv_, aa, S)
+                    outs["o"].copy_(x, non_blocking=True)
+                return
             dq_, dk_, dv_ = (host[n].to(dev, non_blocking=True).requires_grad_(True) for n in ("q", "k", "v"))
             dd = host["do"].to(dev, non_blocking=True)
             aa = host["a2v"].to(dev, non_blocking=True)
@@ -509,7 +556,8 @@ def main():
         cpu = cpu_baseline(seconds=12.0)
 
     if rank == 0:
-        line = {"metric": "bsa_fwd_bwd_effective_tflops", "value": tflops, "unit": "TFLOPS",
+        line = {"metric": "bsa_fwd_effective_tflops" if infer else "bsa_fwd_bwd_effective_tflops",
+                "value": tflops, "unit": "TFLOPS",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded zone-structured q/k/v, N(0,1) a2v residual)",

@@ -130,20 +130,24 @@ def uniform_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            a2v_bridge_residual: Optional[torch.Tensor] = None,
                            audio_gate=None, audio_boost_gamma=None,
                            audio_weighted_lambda: float = 0.0,
-                           variance_boost_gamma: float = 0.0):
+                           variance_boost_gamma: float = 0.0,
+                           correction: Optional[str] = None, taylor_alpha_f: float = 0.5):
     """The same SP branch for the uniform fixed-shape path (the plain-BSA
     dispatch of wan_video_dit.py:470-560, and its variance- / audio-guided forms,
     :637-672): q, k, v [B=1, S_local, num_heads*D] -> x [B, S_local, num_heads*D].
     With a2v_bridge_residual its token norms (all-gathered over SP) drive the
     audio guidance; each rank's variance statistic uses its local heads, as the
-    reference's does (bsa_interface.py:989-994).  No collective besides the
-    all-to-alls and the norms' all-gather."""
+    reference's does (bsa_interface.py:989-994).  correction = "rectified" /
+    "taylor": the bias-rectified forward (inference; the Taylor split's quantile
+    is all-gathered over SP, bias_rectification.py:173-187).  No other collective
+    besides the all-to-alls and the norms' all-gather."""
     norms = audio_token_norms(a2v_bridge_residual, full_seq_len)
     kw = dict(sparsity=sparsity, cdf_threshold=cdf_threshold, chunk_3d_shape_q=chunk_3d_shape_q,
               chunk_3d_shape_k=chunk_3d_shape_k, layout="bshd", audio_token_norms=norms,
               audio_gate=audio_gate, audio_boost_gamma=audio_boost_gamma,
               audio_weighted_lambda=audio_weighted_lambda,
-              variance_boost_gamma=variance_boost_gamma)
+              variance_boost_gamma=variance_boost_gamma, correction=correction,
+              taylor_alpha_f=taylor_alpha_f)
     x, _ = _sp_self_attention(q, k, v, num_heads, full_seq_len,
                               lambda a, b_, c: (run_bsa_uniform(a, b_, c, grid_size, **kw), None))
     return x

@@ -528,46 +528,46 @@ __global__ void tile_valid_kernel(const int32_t* __restrict__ src_idx,
 }
 
 // ================================================================ a10/a17
-// 16-byte chunks; rows of D bf16.
-__global__ void gather_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int64_t xss, int heads,
-                                   int chunks, int T, int H, int W, int Hp, int Wp, int64_t Sp,
+// 16-byte chunks; rows of D bf16.  Grid: (ceil(rows * chunks / 256), heads); the
+// index arithmetic is 32-bit (rows * chunks < 2^31, checked by the entry points).
+__global__ void gather_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int64_t xss, int chunks,
+                                   int T, int H, int W, int Hp, int Wp, int Sp,
                                    const int32_t* __restrict__ src_idx, uint4* __restrict__ out,
                                    int64_t osh) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t total = (int64_t)heads * Sp * chunks;
-  if (i >= total) return;
-  const int c = (int)(i % chunks);
-  const int64_t r = (i / chunks) % Sp;
-  const int h = (int)(i / ((int64_t)chunks * Sp));
-  const int64_t g = src_idx[r];
-  const int t = (int)(g / ((int64_t)Hp * Wp));
-  const int hh = (int)((g / Wp) % Hp);
-  const int w = (int)(g % Wp);
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= Sp * chunks) return;
+  const int h = blockIdx.y;
+  const int r = j / chunks, c = j - r * chunks;
+  const int g = src_idx[r];
+  const int hw = Hp * Wp;
+  const int t = g / hw;
+  const int rem = g - t * hw;
+  const int hh = rem / Wp;
+  const int w = rem - hh * Wp;
   uint4 val = make_uint4(0, 0, 0, 0);
   if (t < T && hh < H && w < W) {
     const int64_t s = ((int64_t)t * H + hh) * W + w;
     val = __ldg(x + ((int64_t)h * xsh + s * xss) / 8 + c);
   }
-  out[((int64_t)h * osh + r * chunks * 8) / 8 + c] = val;
+  out[((int64_t)h * osh) / 8 + (int64_t)j] = val;
 }
 
-__global__ void scatter_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int heads, int chunks,
-                                    int T, int H, int W, int Hp, int Wp,
-                                    const int32_t* __restrict__ inv_idx, uint4* __restrict__ out,
-                                    int64_t osh, int64_t oss) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t S = (int64_t)T * H * W;
-  const int64_t total = (int64_t)heads * S * chunks;
-  if (i >= total) return;
-  const int c = (int)(i % chunks);
-  const int64_t s = (i / chunks) % S;
-  const int h = (int)(i / ((int64_t)chunks * S));
-  const int t = (int)(s / ((int64_t)H * W));
-  const int hh = (int)((s / W) % H);
-  const int w = (int)(s % W);
+__global__ void scatter_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int chunks, int T, int H,
+                                    int W, int Hp, int Wp, const int32_t* __restrict__ inv_idx,
+                                    uint4* __restrict__ out, int64_t osh, int64_t oss) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int S = T * H * W;
+  if (j >= S * chunks) return;
+  const int h = blockIdx.y;
+  const int s = j / chunks, c = j - s * chunks;
+  const int hw = H * W;
+  const int t = s / hw;
+  const int rem = s - t * hw;
+  const int hh = rem / W;
+  const int w = rem - hh * W;
   const int64_t g = ((int64_t)t * Hp + hh) * Wp + w;
   const int64_t r = inv_idx[g];
-  out[((int64_t)h * osh + s * oss) / 8 + c] = __ldg(x + ((int64_t)h * xsh + r * chunks * 8) / 8 + c);
+  out[((int64_t)h * osh + (int64_t)s * oss) / 8 + c] = __ldg(x + ((int64_t)h * xsh + r * chunks * 8) / 8 + c);
 }
 
 // ================================================================ a11
@@ -779,6 +779,30 @@ __device__ void radix_walk(const uint32_t* hist_cnt, const unsigned long long* h
   __syncwarp();
 }
 
+// Histogram update aggregated per warp: lanes holding the same bucket add their
+// count (and fixed-point mass) through one leader.  The keys of one radix pass
+// concentrate in few buckets (probabilities share exponent bytes), so per-lane
+// shared atomics would serialise on them; sums are integers, so the result is the
+// same in any order.  Called by every lane of the warp (active = lane has a key).
+__device__ __forceinline__ void hist_add_warp(uint32_t* hist_cnt, unsigned long long* hist_mass,
+                                              bool active, int bkt, unsigned long long mass,
+                                              bool with_mass) {
+  const int lane = threadIdx.x & 31;
+  const unsigned peers = __match_any_sync(0xffffffffu, active ? bkt : -1 - lane);
+  unsigned long long sum = 0;
+  if (with_mass) {
+#pragma unroll 4
+    for (int src = 0; src < 32; ++src) {
+      const unsigned long long v = __shfl_sync(0xffffffffu, mass, src);
+      if ((peers >> src) & 1u) sum += v;
+    }
+  }
+  if (active && lane == __ffs(peers) - 1) {
+    atomicAdd(&hist_cnt[bkt], (uint32_t)__popc(peers));
+    if (with_mass) atomicAdd(&hist_mass[bkt], sum);
+  }
+}
+
 __global__ void __launch_bounds__(kSelThreads) select_kernel(
     const float* __restrict__ score, const uint8_t* __restrict__ bvalid,
     const int32_t* __restrict__ n_blocks, int na_max, int nb_max,
@@ -861,13 +885,11 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
       }
       __syncthreads();
       const uint32_t prefix = st.prefix, pmask = st.pmask;
-      for (int i = tid; i < nb; i += blockDim.x) {
-        const uint32_t kk = keys[i];
-        if ((kk & pmask) == prefix) {
-          const int bkt = (kk >> shift) & 0xff;
-          atomicAdd(&hist_cnt[bkt], 1u);
-          atomicAdd(&hist_mass[bkt], fix63(kk));
-        }
+      for (int i0 = 0; i0 < nb; i0 += blockDim.x) {  // warp-uniform trip count
+        const int i = i0 + tid;
+        const uint32_t kk = i < nb ? keys[i] : 0u;
+        const bool in = i < nb && (kk & pmask) == prefix;
+        hist_add_warp(hist_cnt, hist_mass, in, (kk >> shift) & 0xff, in ? fix63(kk) : 0ull, true);
       }
       __syncthreads();
       if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 1, 0, pf, &st);
@@ -914,9 +936,11 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
       for (int i = tid; i < 256; i += blockDim.x) hist_cnt[i] = 0;
       __syncthreads();
       const uint32_t prefix = st.prefix, pmask = st.pmask;
-      for (int i = tid; i < nb; i += blockDim.x) {
-        const uint32_t kk = keys[i];
-        if ((kk & pmask) == prefix) atomicAdd(&hist_cnt[(kk >> shift) & 0xff], 1u);
+      for (int i0 = 0; i0 < nb; i0 += blockDim.x) {  // warp-uniform trip count
+        const int i = i0 + tid;
+        const uint32_t kk = i < nb ? keys[i] : 0u;
+        hist_add_warp(hist_cnt, hist_mass, i < nb && (kk & pmask) == prefix, (kk >> shift) & 0xff,
+                      0ull, false);
       }
       __syncthreads();
       if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 0, (int)n_eff, pf, &st);
@@ -1021,49 +1045,80 @@ __global__ void uniform_perm_kernel(int Hp, int Wp, int ct, int ch, int cw, int6
 }
 
 // masked_mean_pooling_compression / mean_pooling_compression
-// (bsa_interface.py:164-201) over chunks of consecutive rows: sequential fp32
-// sum over the chunk's valid rows (bit s of the validity words; nullptr = all
-// rows valid), divided by max(count, 1).  One CTA per (chunk, head, tensor),
-// D threads; blockIdx.z picks x0 (S0 rows per head, n0 chunks of chunk0 rows,
-// validity bits0 -> out0) or x1 (S1, n1, chunk1, bits1 -> out1).
-// weights1 (nullable) replaces x1's validity by per-row weights w (Path B of
-// the audio-guided path, audio_weighted_mean_pooling_compression,
-// bsa_interface.py:902-970): sum of the rounded products x * w over the chunk
-// divided by max(sum of w, 1).
-__global__ void pool_chunk_kernel(const uint16_t* __restrict__ x0, const uint16_t* __restrict__ x1,
-                                  int64_t S0, int64_t S1, int D, int chunk0, int n0, int chunk1,
-                                  int n1, const uint64_t* __restrict__ bits0,
-                                  const uint64_t* __restrict__ bits1,
-                                  const float* __restrict__ weights1, float* __restrict__ out0,
-                                  float* __restrict__ out1) {
-  const int c = blockIdx.x, h = blockIdx.y, which = blockIdx.z;
+// (bsa_interface.py:164-201) over chunks of consecutive rows: per channel a
+// sequential fp32 sum over the chunk's valid rows (bit s of the validity words;
+// nullptr = all rows valid), divided by max(count, 1).  blockIdx.z picks x0 (S0
+// rows per head, n0 chunks of chunk0 rows, validity bits0 -> out0) or x1 (S1, n1,
+// chunk1, bits1 -> out1).  A thread owns 8 channels of one chunk (16-byte loads);
+// a CTA of kPoolThreads threads covers kPoolThreads / (D / 8) chunks of a head.
+// weights1 (nullable) replaces x1's validity by per-row weights w (Path B of the
+// audio-guided path, audio_weighted_mean_pooling_compression, bsa_interface.py:
+// 902-970): sum of the rounded products x * w divided by max(sum of w, 1).
+constexpr int kPoolThreads = 128;
+__global__ void __launch_bounds__(kPoolThreads) pool_chunk_kernel(
+    const uint16_t* __restrict__ x0, const uint16_t* __restrict__ x1, int64_t S0, int64_t S1, int D,
+    int chunk0, int n0, int chunk1, int n1, const uint64_t* __restrict__ bits0,
+    const uint64_t* __restrict__ bits1, const float* __restrict__ weights1, float* __restrict__ out0,
+    float* __restrict__ out1) {
+  const int h = blockIdx.y, which = blockIdx.z;
+  const int g8 = D / 8;                       // threads per chunk
+  const int c = blockIdx.x * (kPoolThreads / g8) + threadIdx.x / g8;
+  const int dg = (threadIdx.x % g8) * 8;      // first channel of this thread
   const int chunk = which ? chunk1 : chunk0;
   const int n = which ? n1 : n0;
-  if (c >= n) return;
+  if (threadIdx.x >= (kPoolThreads / g8) * g8 || c >= n) return;
   const int64_t base = (int64_t)c * chunk;
-  const uint16_t* x = (which ? x1 : x0) + ((int64_t)h * (which ? S1 : S0) + base) * D + threadIdx.x;
-  float* out = (which ? out1 : out0) + ((int64_t)h * n + c) * D + threadIdx.x;
+  const uint4* x = reinterpret_cast<const uint4*>((which ? x1 : x0) +
+                                                  ((int64_t)h * (which ? S1 : S0) + base) * D + dg);
+  const int64_t rs = D / 8;                   // row stride in uint4
+  float sum[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) sum[j] = 0.0f;
+  float den;
   if (which && weights1 != nullptr) {
-    float sum = 0.0f, wsum = 0.0f;
+    float wsum = 0.0f;
+#pragma unroll 4
     for (int i = 0; i < chunk; ++i) {
       const float w = weights1[base + i];
-      sum = __fadd_rn(sum, __fmul_rn(bfbits2f(x[(int64_t)i * D]), w));
+      const uint4 v = __ldg(x + i * rs);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sum[2 * j] = __fadd_rn(sum[2 * j], __fmul_rn(__uint_as_float(u[j] << 16), w));
+        sum[2 * j + 1] = __fadd_rn(sum[2 * j + 1], __fmul_rn(__uint_as_float(u[j] & 0xffff0000u), w));
+      }
       wsum = __fadd_rn(wsum, w);
     }
-    *out = __fdiv_rn(sum, wsum < 1.0f ? 1.0f : wsum);
-    return;
+    den = wsum < 1.0f ? 1.0f : wsum;
+  } else {
+    const uint64_t* vbits = which ? bits1 : bits0;
+    int cnt = 0;
+#pragma unroll 4
+    for (int i = 0; i < chunk; ++i) {
+      const int64_t sidx = base + i;
+      if (vbits != nullptr && !((vbits[sidx >> 6] >> (sidx & 63)) & 1ull)) continue;
+      const uint4 v = __ldg(x + i * rs);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sum[2 * j] = __fadd_rn(sum[2 * j], __uint_as_float(u[j] << 16));
+        sum[2 * j + 1] = __fadd_rn(sum[2 * j + 1], __uint_as_float(u[j] & 0xffff0000u));
+      }
+      ++cnt;
+    }
+    den = cnt > 0 ? (float)cnt : 1.0f;
   }
-  const uint64_t* vbits = which ? bits1 : bits0;
-  float sum = 0.0f;
-  int cnt = 0;
-  for (int i = 0; i < chunk; ++i) {
-    const int64_t sidx = base + i;
-    if (vbits != nullptr && !((vbits[sidx >> 6] >> (sidx & 63)) & 1ull)) continue;
-    sum = __fadd_rn(sum, bfbits2f(x[(int64_t)i * D]));
-    ++cnt;
-  }
-  const float den = cnt > 0 ? (float)cnt : 1.0f;
-  *out = __fdiv_rn(sum, den);
+  float4* out = reinterpret_cast<float4*>((which ? out1 : out0) + ((int64_t)h * n + c) * D + dg);
+  out[0] = make_float4(__fdiv_rn(sum[0], den), __fdiv_rn(sum[1], den), __fdiv_rn(sum[2], den),
+                       __fdiv_rn(sum[3], den));
+  out[1] = make_float4(__fdiv_rn(sum[4], den), __fdiv_rn(sum[5], den), __fdiv_rn(sum[6], den),
+                       __fdiv_rn(sum[7], den));
+}
+
+// grid of pool_chunk_kernel for n chunks of D channels
+static inline unsigned pool_blocks(int n, int D) {
+  const int cpb = kPoolThreads / (D / 8);
+  return (unsigned)((n + cpb - 1) / cpb);
 }
 
 // ================================================================ guided selection
@@ -1364,13 +1419,14 @@ prism_status_t prism_gather_rows(const void* x, int64_t x_stride_h, int64_t x_st
                   aligned16(x) && aligned16(out), "prism_gather_rows: rows must be 16-byte aligned (D %% 8 == 0)");
   PRISM_CHECK_ARG(T >= 1 && H >= 1 && W >= 1 && T <= Tp && H <= Hp && W <= Wp,
                   "prism_gather_rows: bad grids");
-  PRISM_CHECK_ARG(n_rows >= 0 && n_rows < (int64_t)1 << 31, "prism_gather_rows: bad row count");
-  const int64_t Sp = n_rows;
   const int chunks = D / 8;
-  const int64_t total = (int64_t)heads * Sp * chunks;
-  if (total == 0) return PRISM_OK;
-  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
-      (const uint4*)x, x_stride_h, x_stride_s, heads, chunks, T, H, W, Hp, Wp, Sp, src_idx,
+  PRISM_CHECK_ARG(n_rows >= 0 && n_rows * chunks < (int64_t)1 << 31 && heads <= 65535 &&
+                      (int64_t)Tp * Hp * Wp < (int64_t)1 << 31,
+                  "prism_gather_rows: bad row count");
+  const int64_t total = n_rows * chunks;
+  if (total == 0 || heads == 0) return PRISM_OK;
+  gather_rows_kernel<<<dim3((unsigned)((total + 255) / 256), heads), 256, 0, stream>>>(
+      (const uint4*)x, x_stride_h, x_stride_s, chunks, T, H, W, Hp, Wp, (int)n_rows, src_idx,
       (uint4*)out, out_stride_h);
   PRISM_CHECK_LAUNCH("prism_gather_rows");
   return PRISM_OK;
@@ -1386,10 +1442,11 @@ prism_status_t prism_scatter_rows(const void* x_re, int64_t x_stride_h, int head
   PRISM_CHECK_ARG(T <= Tp && H <= Hp && W <= Wp, "prism_scatter_rows: bad grids");
   const int64_t S = (int64_t)T * H * W;
   const int chunks = D / 8;
-  const int64_t total = (int64_t)heads * S * chunks;
-  if (total == 0) return PRISM_OK;
-  scatter_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
-      (const uint4*)x_re, x_stride_h, heads, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out,
+  PRISM_CHECK_ARG(S * chunks < (int64_t)1 << 31 && heads <= 65535, "prism_scatter_rows: too many rows");
+  const int64_t total = S * chunks;
+  if (total == 0 || heads == 0) return PRISM_OK;
+  scatter_rows_kernel<<<dim3((unsigned)((total + 255) / 256), heads), 256, 0, stream>>>(
+      (const uint4*)x_re, x_stride_h, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out,
       out_stride_h, out_stride_s);
   PRISM_CHECK_LAUNCH("prism_scatter_rows");
   return PRISM_OK;
@@ -1480,7 +1537,8 @@ prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, in
   PRISM_CHECK_ARG(mode >= 0 && mode <= 2, "prism_block_select_uniform: Either sparsity or cdf_threshold must be provided");
   PRISM_CHECK_ARG(Sq > 0 && Sq % 64 == 0 && Sk > 0 && Sk % 64 == 0 && heads >= 1,
                   "prism_block_select_uniform: sequence lengths must be positive multiples of 64");
-  PRISM_CHECK_ARG(D >= 16 && D <= 256, "prism_block_select_uniform: D=%d unsupported", D);
+  PRISM_CHECK_ARG(D >= 16 && D <= 256 && D % 8 == 0 && aligned16(q_re) && aligned16(k_re),
+                  "prism_block_select_uniform: D=%d unsupported (16-byte rows, 16..256)", D);
   PRISM_CHECK_ARG(chunk_q > 0 && chunk_k > 0 && chunk_q % 64 == 0 && chunk_k % 64 == 0,
                   "prism_block_select_uniform: chunk sizes (%d, %d) must be multiples of 64 tokens",
                   chunk_q, chunk_k);
@@ -1497,7 +1555,7 @@ prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, in
   float* sc = kc + (size_t)heads * nk * D;
   PRISM_CHECK_CUDA(cudaMemsetAsync(bits_q, 0, (size_t)heads * n_qt * wk * sizeof(uint32_t), stream),
                    "prism_block_select_uniform: clear bitmaps");
-  pool_chunk_kernel<<<dim3(nq > nk ? nq : nk, heads, 2), D, 0, stream>>>(
+  pool_chunk_kernel<<<dim3(pool_blocks(nq > nk ? nq : nk, D), heads, 2), kPoolThreads, 0, stream>>>(
       (const uint16_t*)q_re, (const uint16_t*)k_re, Sq, Sk, D, chunk_q, nq, chunk_k, nk, q_bits,
       k_bits, k_weights, qc, kc);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/pool");
@@ -1603,14 +1661,15 @@ prism_status_t prism_pool_chunks(const void* x_re, int heads, int64_t S, int D, 
                                 int chunk, const uint64_t* bits, const float* weights, float* out,
                                 cudaStream_t stream) {
   PRISM_CHECK_ARG(x_re && out, "prism_pool_chunks: null pointer");
-  PRISM_CHECK_ARG(heads >= 1 && D >= 1 && D <= 1024, "prism_pool_chunks: bad heads / D");
+  PRISM_CHECK_ARG(heads >= 1 && D >= 8 && D <= 1024 && D % 8 == 0 && aligned16(x_re) && aligned16(out),
+                  "prism_pool_chunks: D must be a multiple of 8 (16-byte rows)");
   PRISM_CHECK_ARG(chunk >= 1 && seq > 0 && seq <= S && seq % chunk == 0,
                   "prism_pool_chunks: %lld rows are not a whole number of %d-row chunks",
                   (long long)seq, chunk);
   const int64_t n = seq / chunk;
   PRISM_CHECK_ARG(n < (int64_t)1 << 31, "prism_pool_chunks: too many chunks");
   // the second tensor slot of pool_chunk_kernel (the one with weights); the first is empty
-  pool_chunk_kernel<<<dim3((unsigned)n, heads, 2), D, 0, stream>>>(
+  pool_chunk_kernel<<<dim3(pool_blocks((int)n, D), heads, 2), kPoolThreads, 0, stream>>>(
       (const uint16_t*)x_re, (const uint16_t*)x_re, S, S, D, chunk, 0, chunk, (int)n, nullptr, bits,
       weights, out, out);
   PRISM_CHECK_LAUNCH("prism_pool_chunks");
