@@ -340,6 +340,40 @@ def taylor_output(q, o_spa, lse_spa, k_cmp, v_cmp, nonsel_dense, flat, log_count
     return out
 
 
+# ---------------------------------------------------------------- producer side
+def f32_to_bf16_bits(x):
+    """float32 -> bf16 bits, round to nearest even (finite inputs)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return r.astype(np.uint16)
+
+
+def rms_norm(x_bits, gamma, eps=1e-6):
+    """torch.nn.RMSNorm of bf16 rows [S, C] (x * rsqrt(mean(x^2) + eps)) * gamma in
+    float32 (mean in float64 here), rounded to bf16 bits."""
+    x = bf16_bits_to_f32(x_bits)
+    ms = (x.astype(np.float64) ** 2).mean(axis=-1, keepdims=True)
+    r = (1.0 / np.sqrt(ms + eps)).astype(np.float32)
+    y = (x * r).astype(np.float32) * np.asarray(gamma, np.float32)
+    return f32_to_bf16_bits(y.astype(np.float32))
+
+
+def rope_apply(y_bits, rope_cs, D):
+    """rope_apply_head_dim (wan_video_dit.py:177-182) of bf16 rows [S, H*D]: each
+    (even, odd) pair times cos + i sin in float64, the result rounded to float32,
+    then to bf16 (torch's double -> bf16 conversion).  rope_cs [S, D/2, 2]."""
+    y = bf16_bits_to_f32(y_bits).astype(np.float64)
+    S, C = y.shape
+    H = C // D
+    p = y.reshape(S, H, D // 2, 2)
+    c = rope_cs[:, None, :, 0]
+    s = rope_cs[:, None, :, 1]
+    re = p[..., 0] * c - p[..., 1] * s
+    im = p[..., 0] * s + p[..., 1] * c
+    out = np.stack([re, im], axis=-1).reshape(S, C).astype(np.float32)
+    return f32_to_bf16_bits(out)
+
+
 def bits_to_dense(bits: np.ndarray, n_cols: int) -> np.ndarray:
     """[..., rows, WQ] u32 -> [..., rows, n_cols] bool."""
     b = bits.view(np.uint8).reshape(*bits.shape[:-1], bits.shape[-1] * 4)

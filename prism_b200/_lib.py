@@ -50,6 +50,10 @@ SIGNATURES = {
     "prism_rows_to_bf16": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "prism_taylor_merge": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _I, _P, _P]),
     "prism_rectified_apply": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I, _I, _P, _P]),
+    "prism_norm_rope_pack": (_I, [_P, _I64, _I64, _I64, _I, _I, _I, _I, _P, _F, _P, _I, _P, _P, _P]),
+    "prism_norm_rope_pack_bwd_workspace_bytes": (_SZ, [_I64, _I, _I]),
+    "prism_norm_rope_pack_bwd": (_I, [_P, _P, _I64, _I64, _I64, _I, _I, _I, _I, _P, _P, _P, _I, _P, _I64,
+                                      _P, _P, _P]),
     "prism_bsa_fwd_qk": (_I, [_P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_bwd_qk": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
     "prism_bsa_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _F, _P, _P, _P, _P, _P, _P]),
@@ -73,7 +77,7 @@ KERNELS = {
     "prism_guidance_scale": 1, "prism_pool_chunks": 1, "prism_chunk_scores": 1,
     "prism_bsa_fwd_keybias": 1, "prism_correction_stats": 1, "prism_taylor_prep": 1,
     "prism_key_log_bias": 1, "prism_rows_to_bf16": 1, "prism_taylor_merge": 1,
-    "prism_rectified_apply": 1,
+    "prism_rectified_apply": 1, "prism_norm_rope_pack": 1, "prism_norm_rope_pack_bwd": 2,
 }
 launch_count = 0
 

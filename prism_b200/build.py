@@ -25,6 +25,7 @@ COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path
 SOURCES = {
     "select_kernels.cu": ["-fmad=false"],
     "correction_kernels.cu": ["-fmad=false"],
+    "producer_kernels.cu": ["-fmad=false"],
     "bsa_tc.cu": [],
 }
 

@@ -335,6 +335,39 @@ def rectified_apply(o_spa, o_spa_lo, R, o_ncri, seq_q: int, chunk_q: int, out=No
     return out
 
 
+# --------------------------------------------------------- producer fusion
+def norm_rope_pack(x: torch.Tensor, heads: int, P: int, hp: int, S_pack: int, gamma=None,
+                   eps: float = 1e-6, rope_cs=None, norm: bool = True):
+    """x [S, heads*D] bf16 -> (packed [P, S_pack, hp, D] bf16, rstd [S] fp32 or None)."""
+    _check_cuda(x, gamma, rope_cs)
+    S, C = x.shape
+    D = C // heads
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    out = torch.empty(P, S_pack, hp, D, dtype=torch.bfloat16, device=x.device)
+    rstd = torch.empty(S, dtype=torch.float32, device=x.device) if norm else None
+    g = None if gamma is None else gamma.to(torch.float32).contiguous()
+    _lib.call("prism_norm_rope_pack", _p(x), x.stride(0), S, S_pack, heads, D, P, hp, _p(g),
+              float(eps), _p(rope_cs), int(norm), _p(out), _p(rstd), _stream(x))
+    return out, rstd
+
+
+def norm_rope_pack_bwd(g: torch.Tensor, x, heads: int, S: int, gamma=None, rstd=None, rope_cs=None,
+                       norm: bool = True):
+    """g [P, S_pack, hp, D] -> (dx [S, heads*D] bf16, dgamma [heads*D] fp32 or None)."""
+    _check_cuda(g, x, gamma, rstd, rope_cs)
+    P, S_pack, hp, D = g.shape
+    gc = g.contiguous()
+    dx = torch.empty(S, heads * D, dtype=torch.bfloat16, device=g.device)
+    dgamma = torch.empty(heads * D, dtype=torch.float32, device=g.device) if norm else None
+    ws = _ws(_lib.query("prism_norm_rope_pack_bwd_workspace_bytes", S, heads, D), g.device) if norm else None
+    gm = None if gamma is None else gamma.to(torch.float32).contiguous()
+    xs = 0 if x is None else x.stride(0)
+    _lib.call("prism_norm_rope_pack_bwd", _p(gc), _p(x), xs, S, S_pack, heads, D, P, hp, _p(gm),
+              _p(rstd), _p(rope_cs), int(norm), _p(dx), dx.stride(0), _p(ws), _p(dgamma), _stream(g))
+    return dx, dgamma
+
+
 # --------------------------------------------------------- guided selection
 def gather_values(x: torch.Tensor, grid, grid_padded, src_idx: torch.Tensor) -> torch.Tensor:
     """Per-token values [T*H*W] on grid -> fp32 [len(src_idx)] in the chunk order, 0 at padding."""

@@ -331,3 +331,17 @@ def make_inputs(case: Case):
         out["norms_u"] = None
         out["norms"] = None
     return out
+
+
+# Producer side (RMSNorm + 3D RoPE, wan_video_dit.py:699-705): (grid, heads, head_dim, seed)
+PRODUCER_CASES = {"p_rope_d128": ((3, 5, 7), 4, 128, 100), "p_rope_h1": ((2, 4, 6), 1, 128, 101)}
+
+
+def make_producer_inputs(grid, heads, D, seed):
+    """x [1, S, heads*D] bf16 (N(0, 4)) and gamma [heads*D] bf16 (1 + N(0, 1/16))."""
+    f, h, w = grid
+    S, C = f * h * w, heads * D
+    gen = torch.Generator().manual_seed(seed)
+    x = (torch.randn(1, S, C, generator=gen) * 2.0).to(torch.bfloat16)
+    gamma = (1.0 + 0.25 * torch.randn(C, generator=gen)).to(torch.bfloat16)
+    return x, gamma

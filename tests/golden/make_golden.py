@@ -46,6 +46,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 from inputs import ALL_CASES, CROSS_CASES, make_cross_inputs, make_inputs  # noqa: E402
+from inputs import PRODUCER_CASES as PRODUCER_FIXTURES, make_producer_inputs  # noqa: E402
 
 N_ROWS = 128  # output rows stored per head (a fixed random subset)
 
@@ -344,6 +345,50 @@ def run_correction_case(bsa, br, case):
     return res
 
 
+# producer fixtures (inputs.PRODUCER_CASES).  head_dim 128 only: the reference's
+# frame / height / width split (head_dim - 2*(head_dim//3), head_dim//3, head_dim//3
+# dimensions) covers head_dim/2 frequency pairs only when head_dim//3 is even
+# (128 -> 22 + 21 + 21 = 64; 64 -> 11 + 10 + 10 = 31 and rope_apply_head_dim fails)
+PRODUCER_CASES = [(n,) + c for n, c in PRODUCER_FIXTURES.items()]
+
+
+def import_rope_functions(root):
+    """precompute_freqs_cis_3d, precompute_freqs_cis and rope_apply_head_dim taken
+    unmodified from the reference's wan_video_dit.py (its module imports diffusers,
+    absent here, so only these definitions are executed)."""
+    import ast
+
+    import einops
+    path = f"{root}/hymm/models/modules/wan_video_dit.py"
+    tree = ast.parse(open(path).read())
+    keep = {"precompute_freqs_cis_3d", "precompute_freqs_cis", "rope_apply_head_dim"}
+    mod = ast.Module(body=[n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in keep],
+                     type_ignores=[])
+    ns = {"torch": torch, "rearrange": einops.rearrange}
+    exec(compile(mod, path, "exec"), ns)
+    return ns
+
+
+def run_producer_case(ns, grid, heads, D, seed):
+    """The reference's RoPE table for grid (assembled as wan_video_dit.py:1183-1187) and
+    q = rope_apply_head_dim(RMSNorm(x)) on seeded bf16 values (torch.nn.RMSNorm, the
+    module SelfAttention uses, :226-227)."""
+    f, h, w = grid
+    fr = ns["precompute_freqs_cis_3d"](D)
+    freqs = torch.cat([fr[0][:f].view(f, 1, 1, -1).expand(f, h, w, -1),
+                       fr[1][:h].view(1, h, 1, -1).expand(f, h, w, -1),
+                       fr[2][:w].view(1, 1, w, -1).expand(f, h, w, -1)], dim=-1).reshape(f * h * w, 1, -1)
+    C = heads * D
+    x, gamma = make_producer_inputs(grid, heads, D, seed)
+    norm = torch.nn.RMSNorm(C, eps=1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(gamma.float())
+        normed = norm(x)  # bf16 in -> bf16 out
+        y = ns["rope_apply_head_dim"](normed, freqs, D)
+    b16 = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return dict(freqs=torch.view_as_real(freqs[:, 0]).numpy(), normed=b16(normed[0]), y=b16(y[0]))
+
+
 def run_cross_case(bsa, case):
     """flash_attn_bsa_cross (bsa_interface.py:1276-1392) on unpadded inputs.  Stores
     the chunk-level selection of a bf16 and an fp32 pass and the fp32 output / dQ on
@@ -405,8 +450,16 @@ def main():
         sys.exit("set PRISM_REFERENCE to the root of a Prism checkout")
     dba, dbs, bsa = import_reference(root)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    names = sys.argv[1:] or list(ALL_CASES) + list(CROSS_CASES)
+    names = sys.argv[1:] or list(ALL_CASES) + list(CROSS_CASES) + [c[0] for c in PRODUCER_CASES]
+    prod = {c[0]: c for c in PRODUCER_CASES}
     for name in names:
+        if name in prod:
+            _, grid, heads, D, seed = prod[name]
+            res = run_producer_case(import_rope_functions(root), grid, heads, D, seed)
+            path = os.path.join(HERE, f"{name}.npz")
+            np.savez_compressed(path, **res)
+            print(f"{name}: rope {grid} x {heads} heads, D={D} -> {path} ({os.path.getsize(path)} B)")
+            continue
         path = os.path.join(HERE, f"{name}.npz")
         if name in CROSS_CASES:
             res = run_cross_case(bsa, CROSS_CASES[name])
