@@ -342,6 +342,88 @@ def cpu_baseline(seconds=15.0, threads=None):
 
 
 # ------------------------------------------------------------------ main
+def run_producer(args):
+    """--path producer: the producer side of the 720p layer (RMSNorm + 3D RoPE of q, k
+    and the all-to-all pack of q, k, v, forward + backward) fused
+    (prism_b200.producer.norm_rope_pack) against the reference's eager op sequence
+    (wan_video_dit.py:699-705: torch.nn.RMSNorm, rope_apply_head_dim in float64 complex,
+    the b s (n d) -> b n s d copy that feeds the attention), restated with torch ops."""
+    import torch
+    import torch.nn.functional as F
+    from prism_b200 import _lib
+    from prism_b200.producer import norm_rope_pack, rope_table
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.load(build_if_missing=False)
+    grid, H, D = CONFIG["grid"], CONFIG["heads"], CONFIG["head_dim"]
+    S, C = grid[0] * grid[1] * grid[2], H * D
+    gen = torch.Generator(device=dev).manual_seed(0)
+    lin = [torch.randn(S, C, generator=gen, device=dev).to(torch.bfloat16).requires_grad_(True)
+           for _ in range(3)]
+    gam = [(1 + 0.1 * torch.randn(C, generator=gen, device=dev)).requires_grad_(True) for _ in range(2)]
+    grads = [torch.randn(S, H, D, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
+    cs = rope_table(grid, D, device=dev)
+    freqs = torch.view_as_complex(cs.view(S, 1, D // 2, 2))
+
+    def fused():
+        q, k, v = norm_rope_pack(lin[0], lin[1], lin[2], gam[0], gam[1], 1e-6, cs, H)
+        torch.autograd.backward([q.view(S, H, D), k.view(S, H, D), v.view(S, H, D)], grads)
+
+    def eager():
+        outs = []
+        for i in range(3):
+            x = lin[i]
+            if i < 2:
+                x = F.rms_norm(x, (C,), gam[i].to(torch.bfloat16), 1e-6)
+                xc = torch.view_as_complex(x.view(S, H, D // 2, 2).to(torch.float64))
+                x = torch.view_as_real(xc * freqs).flatten(1).to(torch.bfloat16)
+            outs.append(x.view(1, S, H, D).permute(0, 2, 1, 3).contiguous())
+        torch.autograd.backward(outs, [g.view(1, S, H, D).permute(0, 2, 1, 3) for g in grads])
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    clk = ClockSampler(0)
+    clk.start()
+    l0 = _lib.launch_count
+    ms_f = timed(fused, args.steps, args.warmup)
+    launches = (_lib.launch_count - l0) // (args.steps + args.warmup)
+    clocks = clk.stop()
+    ms_e = timed(eager, args.steps, args.warmup)
+    # algorithmic bytes: forward reads q, k, v rows and writes the packed q, k, v (+ rstd);
+    # backward reads the packed gradients and the q, k rows, writes dq, dk, dv
+    row = S * C * 2
+    fwd_bytes, bwd_bytes = 6 * row + 8 * S, 8 * row + 8 * S
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs") or 6650.0
+    achieved = (fwd_bytes + bwd_bytes) / (ms_f * 1e-3) / 1e9
+    line = {"metric": "producer_fwd_bwd_ms", "value": ms_f, "unit": "ms", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_f, "higher_is_better": False,
+            "scaling": "none", "vs_baseline": None, "dtype": "bf16 (RoPE in f64)", "data": "synthetic",
+            "config": {"workload": "720p layer producer side: RMSNorm + 3D RoPE of q, k and the "
+                                   "all-to-all pack of q, k, v, forward + backward",
+                       "tokens": S, "heads": H, "head_dim": D, "grid": list(grid)},
+            "eager_torch_ms": ms_e, "speedup_vs_eager": ms_e / ms_f,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback"},
+            "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -352,7 +434,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", default="720p", choices=sorted(CONFIGS),
                     help="benchmark config: 720p (config 1, default), 1080p (config 2), 2k (config 3)")
-    ap.add_argument("--path", default="dynamic", choices=["dynamic", "uniform"],
+    ap.add_argument("--path", default="dynamic", choices=["dynamic", "uniform", "producer"],
                     help="dynamic block shapes (flash_attn_bsa_3d_dynamic, the metric's path) or "
                          "the uniform fixed-shape path (flash_attn_bsa_3d, 4x4x4 chunks, "
                          "sparsity 0.75, cdf 0.2)")
@@ -368,6 +450,10 @@ def main():
                          "for profiler captures)")
     args = ap.parse_args()
     CONFIG.update(CONFIGS[args.config])
+    if args.path == "producer":
+        CONFIG["heads"] = args.heads
+        run_producer(args)
+        return
     CONFIG["heads"] = args.heads
     CONFIG["path"] = args.path
     if args.path == "uniform":

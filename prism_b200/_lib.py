@@ -77,7 +77,7 @@ KERNELS = {
     "prism_guidance_scale": 1, "prism_pool_chunks": 1, "prism_chunk_scores": 1,
     "prism_bsa_fwd_keybias": 1, "prism_correction_stats": 1, "prism_taylor_prep": 1,
     "prism_key_log_bias": 1, "prism_rows_to_bf16": 1, "prism_taylor_merge": 1,
-    "prism_rectified_apply": 1, "prism_norm_rope_pack": 1, "prism_norm_rope_pack_bwd": 2,
+    "prism_rectified_apply": 1, "prism_norm_rope_pack": 1, "prism_norm_rope_pack_bwd": 4,
 }
 launch_count = 0
 

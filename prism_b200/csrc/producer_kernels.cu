@@ -48,7 +48,10 @@ __device__ float block_sum_f(float v, float* red) {
 // One CTA per packed row s < S_pack.  x rows [S, C] (C = H * D, row stride ld
 // elements); out [P][S_pack][hp][D] with P * hp >= H (heads h >= H are zero, rows
 // s >= S are zero: the last rank's padding of an uneven split).  norm = 0: v
-// (copy); norm = 1: RMSNorm + RoPE.  rope_cs [S][D/2][2] doubles (cos, sin).
+// (copy); norm = 1: RMSNorm + RoPE.  rope_cs [S][D/2][2] doubles (cos, sin).  A
+// thread holds its kV 8-column groups of the row in registers between the norm's
+// reduction and the rotation (kV = ceil(C / 8 / kProdThreads)).
+template <int kV>
 __global__ void __launch_bounds__(kProdThreads) norm_rope_pack_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t S, int64_t S_pack, int H, int D, int P,
     int hp, const float* __restrict__ gamma, float eps, const double* __restrict__ rope_cs, int norm,
@@ -66,13 +69,19 @@ __global__ void __launch_bounds__(kProdThreads) norm_rope_pack_kernel(
   const int C = H * D;
   const uint4* xr = reinterpret_cast<const uint4*>(x + s * ld);
   const int nv = C / 8;
+  uint4 xv[kV];
+#pragma unroll
+  for (int k = 0; k < kV; ++k) {
+    const int i = threadIdx.x + k * kProdThreads;
+    xv[k] = i < nv ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
+  }
   float r = 1.0f;
   if (norm) {
     for (int i = threadIdx.x; i < D; i += blockDim.x) cs[i] = rope_cs[s * D + i];
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-      const uint4 v = __ldg(xr + i);
-      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < kV; ++k) {
+      const uint32_t u[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float a = bf_lo(u[j]), b = bf_hi(u[j]);
@@ -84,150 +93,163 @@ __global__ void __launch_bounds__(kProdThreads) norm_rope_pack_kernel(
     if (threadIdx.x == 0) rstd_out[s] = r;
     __syncthreads();  // cs visible
   }
-  const int nvp = P * hp * D / 8;  // padded row of the packed layout
-  for (int i = threadIdx.x; i < nvp; i += blockDim.x) {
+#pragma unroll
+  for (int k = 0; k < kV; ++k) {
+    const int i = threadIdx.x + k * kProdThreads;
+    if (i >= nv) break;
     const int col = i * 8;
     const int h = col / D, d0 = col - h * D;
-    uint4 o = make_uint4(0, 0, 0, 0);
-    if (h < H) {
-      const uint4 v = __ldg(xr + i);
-      if (!norm) {
-        o = v;
-      } else {
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-        uint32_t w[4];
-        const float4 g0 = gamma ? reinterpret_cast<const float4*>(gamma + col)[0] : make_float4(1, 1, 1, 1);
-        const float4 g1 = gamma ? reinterpret_cast<const float4*>(gamma + col)[1] : make_float4(1, 1, 1, 1);
-        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    uint4 o = xv[k];
+    if (norm) {
+      const uint32_t u[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+      uint32_t w[4];
+      const float4 g0 = gamma ? reinterpret_cast<const float4*>(gamma + col)[0] : make_float4(1, 1, 1, 1);
+      const float4 g1 = gamma ? reinterpret_cast<const float4*>(gamma + col)[1] : make_float4(1, 1, 1, 1);
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          // normed pair, rounded to bf16 (the RMSNorm output dtype)
-          const double a = (double)__bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(bf_lo(u[j]), r), g[2 * j])));
-          const double b = (double)__bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(bf_hi(u[j]), r), g[2 * j + 1])));
-          const int pi = (d0 >> 1) + j;
-          const double c = cs[2 * pi], sn = cs[2 * pi + 1];
-          const double re = __dsub_rn(__dmul_rn(a, c), __dmul_rn(b, sn));
-          const double im = __dadd_rn(__dmul_rn(a, sn), __dmul_rn(b, c));
-          w[j] = pack2(d2bf(re), d2bf(im));
-        }
-        o = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int j = 0; j < 4; ++j) {
+        // normed pair, rounded to bf16 (the RMSNorm output dtype)
+        const double a = (double)__bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(bf_lo(u[j]), r), g[2 * j])));
+        const double b = (double)__bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(bf_hi(u[j]), r), g[2 * j + 1])));
+        const int pi = (d0 >> 1) + j;
+        const double c = cs[2 * pi], sn = cs[2 * pi + 1];
+        const double re = __dsub_rn(__dmul_rn(a, c), __dmul_rn(b, sn));
+        const double im = __dadd_rn(__dmul_rn(a, sn), __dmul_rn(b, c));
+        w[j] = pack2(d2bf(re), d2bf(im));
       }
+      o = make_uint4(w[0], w[1], w[2], w[3]);
     }
     const int p = h / hp, hh = h - p * hp;
     reinterpret_cast<uint4*>(out + (((int64_t)p * S_pack + s) * hp + hh) * D + d0)[0] = o;
   }
+  // padded heads of the packed row
+  for (int i = nv + threadIdx.x; i < P * hp * D / 8; i += blockDim.x) {
+    const int col = i * 8, h = col / D, d0 = col - h * D, p = h / hp, hh = h - p * hp;
+    reinterpret_cast<uint4*>(out + (((int64_t)p * S_pack + s) * hp + hh) * D + d0)[0] = make_uint4(0, 0, 0, 0);
+  }
 }
 
-// Backward, kProdRows token rows per CTA.  g [P][S][hp][D]: gradient of the
-// packed output.  norm = 0: dx = unpacked g.  norm = 1: dy = conj-rotated g
-// (double, rounded to bf16 through float), then the RMSNorm gradient with
-// r = rstd[s]: dx = r (gamma dy) - x r^3 / C * sum(gamma dy x); dgamma partials
-// [gridDim.x][C] = sum over the CTA's rows of dy x r.
-constexpr int kProdRows = 64;
-template <int kMaxV>  // 8-column groups per thread: ceil(C / 8 / kProdThreads)
-__global__ void __launch_bounds__(kProdThreads) norm_rope_pack_bwd_kernel(
+// Backward.  g [P][S_pack][hp][D]: gradient of the packed output.  With
+// dy = the conjugate rotation of g (double, rounded to bf16 through float) and
+// r = rstd[s]:
+//   dx = r (gamma dy) - x r^3 / C * dot,  dot = sum over the row of gamma dy x,
+//   dgamma = sum over rows of dy x r.
+// Phase A: one warp per row computes dot.  Phase B: one thread per 8 columns of a
+// 32-row tile writes dx and its tile's dgamma partial [S / 32][C]; norm = 0 is the
+// unpack alone.
+__device__ __forceinline__ void rot_back8(const uint4 gv, const double* csrow, int d0, float dy[8]) {
+  const uint32_t gu[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int pi = (d0 >> 1) + j;
+    const double c = csrow[2 * pi], sn = csrow[2 * pi + 1];
+    const double ga = (double)bf_lo(gu[j]), gb = (double)bf_hi(gu[j]);
+    dy[2 * j] = d2bf(__dadd_rn(__dmul_rn(ga, c), __dmul_rn(gb, sn)));
+    dy[2 * j + 1] = d2bf(__dsub_rn(__dmul_rn(gb, c), __dmul_rn(ga, sn)));
+  }
+}
+
+__global__ void norm_rope_dot_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ x,
+                                     int64_t ld, int64_t S, int64_t S_pack, int H, int D, int hp,
+                                     const float* __restrict__ gamma, const double* __restrict__ rope_cs,
+                                     float* __restrict__ dot) {
+  const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (s >= S) return;
+  const int nv = H * D / 8;
+  const double* csrow = rope_cs + s * D;
+  float acc = 0.0f;
+#pragma unroll 4
+  for (int i = lane; i < nv; i += 32) {
+    const int col = i * 8, h = col / D, d0 = col - h * D, p = h / hp, hh = h - p * hp;
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g + (((int64_t)p * S_pack + s) * hp + hh) * D + d0));
+    const uint4 xq = __ldg(reinterpret_cast<const uint4*>(x + s * ld) + i);
+    float gm[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+    if (gamma) {
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + col));
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + col) + 1);
+      gm[0] = g0.x; gm[1] = g0.y; gm[2] = g0.z; gm[3] = g0.w;
+      gm[4] = g1.x; gm[5] = g1.y; gm[6] = g1.z; gm[7] = g1.w;
+    }
+    float dy[8];
+    rot_back8(gv, csrow, d0, dy);
+    const uint32_t xu[4] = {xq.x, xq.y, xq.z, xq.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float xj = (j & 1) ? bf_hi(xu[j >> 1]) : bf_lo(xu[j >> 1]);
+      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(gm[j], dy[j]), xj));
+    }
+  }
+  for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  if (lane == 0) dot[s] = acc;
+}
+
+constexpr int kProdTileRows = 32;
+__global__ void __launch_bounds__(kProdThreads) norm_rope_dx_kernel(
     const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t S,
-    int64_t S_pack, int H, int D, int P, int hp, const float* __restrict__ gamma, const float* __restrict__ rstd,
-    const double* __restrict__ rope_cs, int norm, __nv_bfloat16* __restrict__ dx, int64_t ldx,
-    float* __restrict__ dgamma_part) {
-  extern __shared__ double cs[];
-  __shared__ float red[32];
-  const int C = H * D;
-  const int nv = C / 8;
-  // each thread owns the 8-column groups i = threadIdx.x + k * kProdThreads, k < kMaxV
-  float dg[kMaxV][8];
+    int64_t S_pack, int H, int D, int hp, const float* __restrict__ gamma, const float* __restrict__ rstd,
+    const float* __restrict__ dot, const double* __restrict__ rope_cs, int norm,
+    __nv_bfloat16* __restrict__ dx, int64_t ldx, float* __restrict__ dgamma_part) {
+  const int C = H * D, nv = C / 8;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // 8-column group
+  if (i >= nv) return;
+  const int col = i * 8, h = col / D, d0 = col - h * D, p = h / hp, hh = h - p * hp;
+  const int64_t s0 = (int64_t)blockIdx.y * kProdTileRows;
+  float gm[8], dg[8];
 #pragma unroll
-  for (int k = 0; k < kMaxV; ++k)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dg[k][j] = 0.0f;
-  const int64_t s0 = (int64_t)blockIdx.x * kProdRows;
-  for (int rr = 0; rr < kProdRows; ++rr) {
+  for (int j = 0; j < 8; ++j) {
+    gm[j] = (norm && gamma) ? __ldg(gamma + col + j) : 1.0f;
+    dg[j] = 0.0f;
+  }
+#pragma unroll 2
+  for (int rr = 0; rr < kProdTileRows; ++rr) {
     const int64_t s = s0 + rr;
     if (s >= S) break;
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g + (((int64_t)p * S_pack + s) * hp + hh) * D + d0));
+    uint4* dst = reinterpret_cast<uint4*>(dx + s * ldx + col);
     if (!norm) {
-      for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-        const int col = i * 8, h = col / D, d0 = col - h * D, p = h / hp, hh = h - p * hp;
-        reinterpret_cast<uint4*>(dx + s * ldx + col)[0] =
-            reinterpret_cast<const uint4*>(g + (((int64_t)p * S_pack + s) * hp + hh) * D + d0)[0];
-      }
+      *dst = gv;
       continue;
     }
-    __syncthreads();  // previous row's cs reads done
-    for (int i = threadIdx.x; i < D; i += blockDim.x) cs[i] = rope_cs[s * D + i];
-    __syncthreads();
-    const float r = rstd[s];
-    float dyv[kMaxV][8], xv[kMaxV][8];
-    float dot = 0.0f;
+    const uint4 xq = __ldg(reinterpret_cast<const uint4*>(x + s * ld) + i);
+    float dy[8];
+    rot_back8(gv, rope_cs + s * D, d0, dy);
+    const float r = __ldg(rstd + s);
+    const float coef = __fdiv_rn(__fmul_rn(__fmul_rn(__fmul_rn(r, r), r), __ldg(dot + s)), (float)C);
+    const uint32_t xu[4] = {xq.x, xq.y, xq.z, xq.w};
+    uint32_t w[4];
 #pragma unroll
-    for (int k = 0; k < kMaxV; ++k) {
-      const int i = threadIdx.x + k * kProdThreads;
-      if (i >= nv) break;
-      const int col = i * 8, h = col / D, d0 = col - h * D, p = h / hp, hh = h - p * hp;
-      const uint4 gv = reinterpret_cast<const uint4*>(g + (((int64_t)p * S_pack + s) * hp + hh) * D + d0)[0];
-      const uint4 xq = __ldg(reinterpret_cast<const uint4*>(x + s * ld) + i);
-      const uint32_t gu[4] = {gv.x, gv.y, gv.z, gv.w};
-      const uint32_t xu[4] = {xq.x, xq.y, xq.z, xq.w};
+    for (int j = 0; j < 4; ++j) {
+      float o[2];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int pi = (d0 >> 1) + j;
-        const double c = cs[2 * pi], sn = cs[2 * pi + 1];
-        const double ga = (double)bf_lo(gu[j]), gb = (double)bf_hi(gu[j]);
-        // gradient through (a + ib)(c + is): conj rotation
-        dyv[k][2 * j] = d2bf(__dadd_rn(__dmul_rn(ga, c), __dmul_rn(gb, sn)));
-        dyv[k][2 * j + 1] = d2bf(__dsub_rn(__dmul_rn(gb, c), __dmul_rn(ga, sn)));
-        xv[k][2 * j] = bf_lo(xu[j]);
-        xv[k][2 * j + 1] = bf_hi(xu[j]);
+      for (int e = 0; e < 2; ++e) {
+        const int jj = 2 * j + e;
+        const float xj = e ? bf_hi(xu[j]) : bf_lo(xu[j]);
+        o[e] = __fsub_rn(__fmul_rn(r, __fmul_rn(gm[jj], dy[jj])), __fmul_rn(xj, coef));
+        dg[jj] = __fadd_rn(dg[jj], __fmul_rn(dy[jj], __fmul_rn(xj, r)));
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float gm = gamma ? gamma[col + j] : 1.0f;
-        dot = __fadd_rn(dot, __fmul_rn(__fmul_rn(gm, dyv[k][j]), xv[k][j]));
-      }
+      w[j] = pack2(o[0], o[1]);
     }
-    const float tot = block_sum_f(dot, red);
-    const float coef = __fdiv_rn(__fmul_rn(__fmul_rn(__fmul_rn(r, r), r), tot), (float)C);
-#pragma unroll
-    for (int k = 0; k < kMaxV; ++k) {
-      const int i = threadIdx.x + k * kProdThreads;
-      if (i >= nv) break;
-      const int col = i * 8;
-      uint32_t w[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float o[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int jj = 2 * j + e;
-          const float gm = gamma ? gamma[col + jj] : 1.0f;
-          o[e] = __fsub_rn(__fmul_rn(r, __fmul_rn(gm, dyv[k][jj])), __fmul_rn(xv[k][jj], coef));
-          dg[k][jj] = __fadd_rn(dg[k][jj], __fmul_rn(dyv[k][jj], __fmul_rn(xv[k][jj], r)));
-        }
-        w[j] = pack2(o[0], o[1]);
-      }
-      reinterpret_cast<uint4*>(dx + s * ldx + col)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+    *dst = make_uint4(w[0], w[1], w[2], w[3]);
   }
   if (norm && dgamma_part != nullptr) {
-#pragma unroll
-    for (int k = 0; k < kMaxV; ++k) {
-      const int i = threadIdx.x + k * kProdThreads;
-      if (i >= nv) break;
-      float4* dst = reinterpret_cast<float4*>(dgamma_part + (int64_t)blockIdx.x * C + i * 8);
-      dst[0] = make_float4(dg[k][0], dg[k][1], dg[k][2], dg[k][3]);
-      dst[1] = make_float4(dg[k][4], dg[k][5], dg[k][6], dg[k][7]);
-    }
+    float4* dp = reinterpret_cast<float4*>(dgamma_part + (int64_t)blockIdx.y * C + col);
+    dp[0] = make_float4(dg[0], dg[1], dg[2], dg[3]);
+    dp[1] = make_float4(dg[4], dg[5], dg[6], dg[7]);
   }
 }
 
-// out[c] = sum over rows b of part[b][c] (sequential in b), one thread per column.
-__global__ void column_sum_kernel(const float* __restrict__ part, int64_t rows, int C,
+// out[y][c] = sum over rows b in [y * per, y * per + per) of part[b][c] (sequential in
+// b), one thread per column; blockIdx.y = row group.
+__global__ void column_sum_kernel(const float* __restrict__ part, int64_t rows, int64_t per, int C,
                                   float* __restrict__ out) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
+  const int64_t b0 = (int64_t)blockIdx.y * per, b1 = b0 + per < rows ? b0 + per : rows;
   float s = 0.0f;
 #pragma unroll 8
-  for (int64_t b = 0; b < rows; ++b) s = __fadd_rn(s, __ldg(part + b * C + c));
-  out[c] = s;
+  for (int64_t b = b0; b < b1; ++b) s = __fadd_rn(s, __ldg(part + b * C + c));
+  out[(int64_t)blockIdx.y * C + c] = s;
 }
 
 }  // namespace prism
@@ -241,20 +263,37 @@ prism_status_t prism_norm_rope_pack(const void* x, int64_t ld, int64_t S, int64_
                                     int norm, void* out, float* rstd, cudaStream_t stream) {
   PRISM_CHECK_ARG(x && out && (!norm || (rope_cs && rstd)), "prism_norm_rope_pack: null pointer");
   PRISM_CHECK_ARG(S >= 0 && S_pack >= S && S_pack < (int64_t)1 << 31 && H >= 1 && D >= 8 && D % 8 == 0 &&
-                      P >= 1 && hp >= 1 && P * hp >= H && ld % 8 == 0 && ld >= (int64_t)H * D,
-                  "prism_norm_rope_pack: bad sizes");
+                      P >= 1 && hp >= 1 && P * hp >= H && ld % 8 == 0 && ld >= (int64_t)H * D &&
+                      (int64_t)H * D <= 8 * 8 * kProdThreads,
+                  "prism_norm_rope_pack: bad sizes (hidden width <= %d)", 8 * 8 * kProdThreads);
   PRISM_CHECK_ARG(aligned16(x) && aligned16(out) && (gamma == nullptr || aligned16(gamma)),
                   "prism_norm_rope_pack: tensors must be 16-byte aligned");
   if (S_pack == 0) return PRISM_OK;
-  norm_rope_pack_kernel<<<(unsigned)S_pack, kProdThreads, norm ? D * sizeof(double) : 0, stream>>>(
-      (const __nv_bfloat16*)x, ld, S, S_pack, H, D, P, hp, gamma, eps, rope_cs, norm, (__nv_bfloat16*)out,
-      rstd);
+  const int nvt = (H * D / 8 + kProdThreads - 1) / kProdThreads;
+  const size_t sm = norm ? D * sizeof(double) : 0;
+#define PRISM_NRP_FWD(V)                                                                              \
+  norm_rope_pack_kernel<V><<<(unsigned)S_pack, kProdThreads, sm, stream>>>(                           \
+      (const __nv_bfloat16*)x, ld, S, S_pack, H, D, P, hp, gamma, eps, rope_cs, norm, (__nv_bfloat16*)out, \
+      rstd)
+  switch (nvt) {
+    case 1: PRISM_NRP_FWD(1); break;
+    case 2: PRISM_NRP_FWD(2); break;
+    case 3: PRISM_NRP_FWD(3); break;
+    case 4: PRISM_NRP_FWD(4); break;
+    case 5: PRISM_NRP_FWD(5); break;
+    case 6: PRISM_NRP_FWD(6); break;
+    case 7: PRISM_NRP_FWD(7); break;
+    default: PRISM_NRP_FWD(8); break;
+  }
+#undef PRISM_NRP_FWD
   PRISM_CHECK_LAUNCH("prism_norm_rope_pack");
   return PRISM_OK;
 }
 
 size_t prism_norm_rope_pack_bwd_workspace_bytes(int64_t S, int H, int D) {
-  return (size_t)((S + kProdRows - 1) / kProdRows) * (size_t)H * D * sizeof(float);
+  const size_t tiles = (size_t)((S + kProdTileRows - 1) / kProdTileRows);
+  // dot [S], dgamma partials [tiles][C], second-level partials [<= 64][C]
+  return ((size_t)S + (tiles + 64) * (size_t)H * D) * sizeof(float) + 256;
 }
 
 prism_status_t prism_norm_rope_pack_bwd(const void* g, const void* x, int64_t ld, int64_t S, int64_t S_pack,
@@ -263,36 +302,35 @@ prism_status_t prism_norm_rope_pack_bwd(const void* g, const void* x, int64_t ld
                                         void* workspace, float* dgamma, cudaStream_t stream) {
   PRISM_CHECK_ARG(g && dx && (!norm || (x && rstd && rope_cs && workspace && dgamma)),
                   "prism_norm_rope_pack_bwd: null pointer");
-  PRISM_CHECK_ARG(S >= 0 && S_pack >= S && H >= 1 && D >= 8 && D % 8 == 0 && P >= 1 && hp >= 1 && P * hp >= H &&
-                      (int64_t)H * D <= 8 * 8 * kProdThreads && ld % 8 == 0 && ldx % 8 == 0,
-                  "prism_norm_rope_pack_bwd: bad sizes (hidden width <= %d)", 8 * 8 * kProdThreads);
+  PRISM_CHECK_ARG(S >= 0 && S_pack >= S && S < (int64_t)1 << 31 && H >= 1 && D >= 8 && D % 8 == 0 &&
+                      P >= 1 && hp >= 1 && P * hp >= H && ld % 8 == 0 && ldx % 8 == 0,
+                  "prism_norm_rope_pack_bwd: bad sizes");
   PRISM_CHECK_ARG(aligned16(g) && aligned16(dx) && (x == nullptr || aligned16(x)) &&
-                      (gamma == nullptr || aligned16(gamma)),
+                      (gamma == nullptr || aligned16(gamma)) && (workspace == nullptr || aligned16(workspace)),
                   "prism_norm_rope_pack_bwd: tensors must be 16-byte aligned");
   if (S == 0) return PRISM_OK;
-  const int64_t blocks = (S + kProdRows - 1) / kProdRows;
-  const int nvt = (H * D / 8 + kProdThreads - 1) / kProdThreads;
-  const size_t sm = norm ? D * sizeof(double) : 0;
-  float* part = norm ? (float*)workspace : nullptr;
-#define PRISM_NRP_BWD(V)                                                                              \
-  norm_rope_pack_bwd_kernel<V><<<(unsigned)blocks, kProdThreads, sm, stream>>>(                        \
-      (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, ld, S, S_pack, H, D, P, hp, gamma, rstd, rope_cs,   \
-      norm, (__nv_bfloat16*)dx, ldx, part)
-  switch (nvt) {
-    case 1: PRISM_NRP_BWD(1); break;
-    case 2: PRISM_NRP_BWD(2); break;
-    case 3: PRISM_NRP_BWD(3); break;
-    case 4: PRISM_NRP_BWD(4); break;
-    case 5: PRISM_NRP_BWD(5); break;
-    case 6: PRISM_NRP_BWD(6); break;
-    case 7: PRISM_NRP_BWD(7); break;
-    default: PRISM_NRP_BWD(8); break;
-  }
-#undef PRISM_NRP_BWD
-  PRISM_CHECK_LAUNCH("prism_norm_rope_pack_bwd");
+  const int C = H * D, nv = C / 8;
+  const int64_t tiles = (S + kProdTileRows - 1) / kProdTileRows;
+  PRISM_CHECK_ARG(tiles <= 65535, "prism_norm_rope_pack_bwd: %lld rows exceed the tile grid", (long long)S);
+  float* dot = norm ? (float*)workspace : nullptr;
+  float* part = norm ? (float*)workspace + ((S + 63) / 64) * 64 : nullptr;
   if (norm) {
-    const int C = H * D;
-    column_sum_kernel<<<(C + 255) / 256, 256, 0, stream>>>((const float*)workspace, blocks, C, dgamma);
+    norm_rope_dot_kernel<<<(unsigned)((S * 32 + 255) / 256), 256, 0, stream>>>(
+        (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, ld, S, S_pack, H, D, hp, gamma, rope_cs, dot);
+    PRISM_CHECK_LAUNCH("prism_norm_rope_pack_bwd/dot");
+  }
+  norm_rope_dx_kernel<<<dim3((unsigned)((nv + kProdThreads - 1) / kProdThreads), (unsigned)tiles),
+                        kProdThreads, 0, stream>>>(
+      (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, ld, S, S_pack, H, D, hp, gamma, rstd, dot, rope_cs,
+      norm, (__nv_bfloat16*)dx, ldx, part);
+  PRISM_CHECK_LAUNCH("prism_norm_rope_pack_bwd/dx");
+  if (norm) {
+    // dgamma: tiles partial rows -> <= 64 groups -> 1 (fixed order)
+    const int64_t per = (tiles + 63) / 64;
+    const int64_t groups = (tiles + per - 1) / per;
+    float* part2 = part + tiles * C;
+    column_sum_kernel<<<dim3((C + 255) / 256, (unsigned)groups), 256, 0, stream>>>(part, tiles, per, C, part2);
+    column_sum_kernel<<<dim3((C + 255) / 256, 1), 256, 0, stream>>>(part2, groups, groups, C, dgamma);
     PRISM_CHECK_LAUNCH("prism_norm_rope_pack_bwd/dgamma");
   }
   return PRISM_OK;
