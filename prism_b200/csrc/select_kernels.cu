@@ -813,6 +813,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   uint32_t* row = keys + nb_max;
   __shared__ uint32_t hist_cnt[256];
   __shared__ unsigned long long hist_mass[256];
+  __shared__ unsigned long long hist_mass_w[kSelThreads / 32][256];  // per-warp mass histograms
   __shared__ unsigned long long red[32];
   __shared__ float redf[32];
   __shared__ RadixState st;
@@ -879,17 +880,24 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
     bool crossed = true;
     for (int pass = 0; pass < 4 && crossed; ++pass) {
       const int shift = 24 - 8 * pass;
-      for (int i = tid; i < 256; i += blockDim.x) {
-        hist_cnt[i] = 0;
-        hist_mass[i] = 0;
-      }
+      for (int i = tid; i < 256; i += blockDim.x) hist_cnt[i] = 0;
+      for (int i = tid; i < (kSelThreads / 32) * 256; i += blockDim.x) (&hist_mass_w[0][0])[i] = 0;
       __syncthreads();
       const uint32_t prefix = st.prefix, pmask = st.pmask;
+      unsigned long long* wmass = hist_mass_w[tid >> 5];
       for (int i0 = 0; i0 < nb; i0 += blockDim.x) {  // warp-uniform trip count
         const int i = i0 + tid;
         const uint32_t kk = i < nb ? keys[i] : 0u;
         const bool in = i < nb && (kk & pmask) == prefix;
-        hist_add_warp(hist_cnt, hist_mass, in, (kk >> shift) & 0xff, in ? fix63(kk) : 0ull, true);
+        hist_add_warp(hist_cnt, nullptr, in, (kk >> shift) & 0xff, 0ull, false);
+        if (in) atomicAdd(&wmass[(kk >> shift) & 0xff], fix63(kk));
+      }
+      __syncthreads();
+      for (int i = tid; i < 256; i += blockDim.x) {
+        unsigned long long m = 0;
+#pragma unroll
+        for (int w = 0; w < kSelThreads / 32; ++w) m += hist_mass_w[w][i];
+        hist_mass[i] = m;
       }
       __syncthreads();
       if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 1, 0, pf, &st);

@@ -1,0 +1,74 @@
+"""The fused layer's Ulysses plumbing on CPU ranks (gloo, world size 2 and 4): the
+packed all-to-all of prism_b200.producer (send layout [P, S_pack, hp, D] as
+prism_norm_rope_pack writes it, head padding, an uneven last shard), its autograd
+adjoint, and the K-split output projection on the inverse exchange's receive buffer
+against the unpacked projection (wan_video_dit.py:775-787, 824-841).  The attention
+in between is the identity, so two exchanges bring every rank its own tokens back."""
+import traceback
+
+import pytest
+import torch
+
+from test_sp_gloo import _init, _run
+
+
+def _worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from prism_b200 import parallel_states as ps
+        from prism_b200.communications import sp_chunk_sizes, sp_pad_num_heads
+        from prism_b200.producer import _PackedAllToAll, o_proj_packed
+        ps.initialize_sequence_parallel()
+        group = ps.nccl_info.sp_group
+        g = torch.Generator().manual_seed(0)
+        S, H, D = 13, 6, 4
+        full = torch.randn(S, H, D, generator=g, dtype=torch.float64)
+        W = torch.randn(7, H * D, generator=g, dtype=torch.float64)
+        b = torch.randn(7, generator=g, dtype=torch.float64)
+        sizes = sp_chunk_sizes(S, world)
+        S_pack = sizes[0]
+        s0 = sum(sizes[:rank])
+        mine = full[s0:s0 + sizes[rank]]
+        padded = sp_pad_num_heads(H, world)
+        hp = padded // world
+        # the producer's send layout: send[p, s, hh] = token s, head p * hp + hh
+        send = torch.zeros(world, S_pack, hp, D, dtype=torch.float64)
+        for p in range(world):
+            for hh in range(hp):
+                h = p * hp + hh
+                if h < H:
+                    send[p, :sizes[rank], hh] = mine[:, h]
+        send.requires_grad_(True)
+        recv = _PackedAllToAll.apply(send, group)
+        seq = recv.reshape(world * S_pack, hp, D)[:S]          # the full sequence, my heads
+        for hh in range(hp):
+            h = rank * hp + hh
+            want = full[:, h] if h < H else torch.zeros(S, D, dtype=torch.float64)
+            assert torch.equal(seq[:, hh], want), (rank, hh)
+        # inverse exchange of the (identity) attention output, then the K-split projection
+        back = torch.nn.functional.pad(seq, (0, 0, 0, 0, 0, world * S_pack - S)).reshape(world, S_pack, hp, D)
+        recv2 = _PackedAllToAll.apply(back, group)
+        out = o_proj_packed(recv2, W, b, H, sizes[rank])
+        ref = mine.reshape(sizes[rank], H * D) @ W.t() + b
+        assert torch.allclose(out, ref, rtol=1e-12, atol=1e-12)
+        # adjoint: the gradient of sum(out * w) reaches the send buffer's real entries as
+        # the unpacked projection's gradient, and zero on padding
+        w = torch.randn(out.shape, generator=g, dtype=torch.float64)
+        (out * w).sum().backward()
+        gref = (w @ W).reshape(sizes[rank], H, D)
+        for p in range(world):
+            for hh in range(hp):
+                h = p * hp + hh
+                gs = send.grad[p, :sizes[rank], hh]
+                assert torch.allclose(gs, gref[:, h] if h < H else torch.zeros_like(gs)), (p, hh)
+            assert not send.grad[p, sizes[rank]:].any()
+        q.put((rank, "ok"))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_packed_all_to_all_and_k_split_projection(world):
+    res = _run(_worker, world)
+    for r, msg in res.items():
+        assert msg == "ok", f"rank {r}: {msg}"
