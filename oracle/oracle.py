@@ -413,29 +413,53 @@ def token_mask(bits_q: np.ndarray, valid_re, S: int, Sk: int = None) -> np.ndarr
     return m
 
 
+_ROW_BLOCK = 512  # query rows per dense block (keeps the temporaries small)
+
+
+def _block_mask(dense_h, valid, r0, r1, Sk):
+    """[r1 - r0, Sk] token mask of query rows [r0, r1) from one head's tile mask."""
+    t = dense_h[r0 // 64:(r1 + 63) // 64]                      # [tiles, Nk]
+    m = np.repeat(np.repeat(t, 64, axis=0)[r0 % 64:r0 % 64 + (r1 - r0)], 64, axis=1)[:, :Sk]
+    if valid is not None:
+        m = m & valid[None, :]
+    return m
+
+
+def _blocks(bits_q, valid_re, S, Sk):
+    dense = bits_to_dense(bits_q, Sk // 64)[:, :S // 64]
+    valid = None if valid_re is None else np.asarray(valid_re, bool)
+    for hh in range(dense.shape[0]):
+        for r0 in range(0, S, _ROW_BLOCK):
+            r1 = min(S, r0 + _ROW_BLOCK)
+            yield hh, r0, r1, _block_mask(dense[hh], valid, r0, r1, Sk)
+
+
 def bsa_forward(q, k, v, bits_q, valid_re, sm_scale=None):
     """Float64 restatement of the sparse forward.  q [h, S, D], k, v [h, Sk, D] float.
 
     Returns (o [h,S,D], lse [h,S]) with lse natural-log (bsa_interface.py:382-383);
     rows with no selected valid key give o = 0 and lse = -inf, as the
-    reference's l_i = 1 initialisation does (flash_attn_bsa_varlen_mask.py:264)."""
+    reference's l_i = 1 initialisation does (flash_attn_bsa_varlen_mask.py:264).
+    Dense masked softmax per head over blocks of query rows."""
     q = np.asarray(q, np.float64)
     k = np.asarray(k, np.float64)
     v = np.asarray(v, np.float64)
     h, S, D = q.shape
+    Sk = k.shape[1]
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    m = token_mask(bits_q, valid_re, S, k.shape[1])
-    s = np.matmul(q, k.transpose(0, 2, 1)) * sm_scale
-    s = np.where(m, s, -np.inf)
-    mx = s.max(-1, keepdims=True)
-    empty = ~np.isfinite(mx)
-    mx = np.where(empty, 0.0, mx)
-    p = np.exp(s - mx)
-    l = p.sum(-1, keepdims=True)
-    lsafe = np.where(l > 0, l, 1.0)
-    o = np.matmul(p / lsafe, v)
-    lse = np.where(empty[..., 0], -np.inf, (mx + np.log(lsafe))[..., 0])
+    o = np.zeros((h, S, D))
+    lse = np.zeros((h, S))
+    for hh, r0, r1, m in _blocks(bits_q, valid_re, S, Sk):
+        s = np.where(m, (q[hh, r0:r1] @ k[hh].T) * sm_scale, -np.inf)
+        mx = s.max(-1, keepdims=True)
+        empty = ~np.isfinite(mx)
+        mx = np.where(empty, 0.0, mx)
+        p = np.exp(s - mx)
+        l = p.sum(-1, keepdims=True)
+        lsafe = np.where(l > 0, l, 1.0)
+        o[hh, r0:r1] = (p / lsafe) @ v[hh]
+        lse[hh, r0:r1] = np.where(empty[:, 0], -np.inf, (mx + np.log(lsafe))[:, 0])
     return o, lse
 
 
@@ -449,22 +473,25 @@ def bsa_backward(q, k, v, o, do, bits_q, valid_re, sm_scale=None):
     o = np.asarray(o, np.float64)
     do = np.asarray(do, np.float64)
     h, S, D = q.shape
+    Sk = k.shape[1]
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    m = token_mask(bits_q, valid_re, S, k.shape[1])
-    s = np.matmul(q, k.transpose(0, 2, 1)) * sm_scale
-    s = np.where(m, s, -np.inf)
-    mx = s.max(-1, keepdims=True)
-    mx = np.where(np.isfinite(mx), mx, 0.0)
-    p = np.exp(s - mx)
-    l = p.sum(-1, keepdims=True)
-    p = p / np.where(l > 0, l, 1.0)
-    delta = (o * do).sum(-1, keepdims=True)
-    dp = np.matmul(do, v.transpose(0, 2, 1))
-    ds = p * (dp - delta)
-    dq = np.matmul(ds, k) * sm_scale
-    dk = np.matmul(ds.transpose(0, 2, 1), q) * sm_scale
-    dv = np.matmul(p.transpose(0, 2, 1), do)
+    dq = np.zeros((h, S, D))
+    dk = np.zeros((h, Sk, D))
+    dv = np.zeros((h, Sk, D))
+    for hh, r0, r1, m in _blocks(bits_q, valid_re, S, Sk):
+        s = np.where(m, (q[hh, r0:r1] @ k[hh].T) * sm_scale, -np.inf)
+        mx = s.max(-1, keepdims=True)
+        mx = np.where(np.isfinite(mx), mx, 0.0)
+        p = np.exp(s - mx)
+        l = p.sum(-1, keepdims=True)
+        p = p / np.where(l > 0, l, 1.0)
+        delta = (o[hh, r0:r1] * do[hh, r0:r1]).sum(-1, keepdims=True)
+        dp = do[hh, r0:r1] @ v[hh].T
+        ds = p * (dp - delta)
+        dq[hh, r0:r1] = (ds @ k[hh]) * sm_scale
+        dk[hh] += (ds.T @ q[hh, r0:r1]) * sm_scale
+        dv[hh] += p.T @ do[hh, r0:r1]
     return dq, dk, dv
 
 

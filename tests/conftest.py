@@ -1,6 +1,11 @@
 import os
 import sys
 
+# The CPU oracle issues many small matrix products; OpenBLAS worker threads spend
+# their time spinning in the kernel on those, so the oracle runs single-threaded.
+for _v in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+    os.environ.setdefault(_v, "1")
+
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
