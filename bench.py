@@ -351,7 +351,7 @@ def run_producer(args):
     import torch
     import torch.nn.functional as F
     from prism_b200 import _lib
-    from prism_b200.producer import norm_rope_pack, rope_table
+    from prism_b200.producer import norm_rope_pack, rope_table, rope_table_ff
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     _lib.load(build_if_missing=False)
@@ -363,10 +363,11 @@ def run_producer(args):
     gam = [(1 + 0.1 * torch.randn(C, generator=gen, device=dev)).requires_grad_(True) for _ in range(2)]
     grads = [torch.randn(S, H, D, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
     cs = rope_table(grid, D, device=dev)
+    ff = rope_table_ff(cs)
     freqs = torch.view_as_complex(cs.view(S, 1, D // 2, 2))
 
     def fused():
-        q, k, v = norm_rope_pack(lin[0], lin[1], lin[2], gam[0], gam[1], 1e-6, cs, H)
+        q, k, v = norm_rope_pack(lin[0], lin[1], lin[2], gam[0], gam[1], 1e-6, ff, H)
         torch.autograd.backward([q.view(S, H, D), k.view(S, H, D), v.view(S, H, D)], grads)
 
     def eager():

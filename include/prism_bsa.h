@@ -347,22 +347,25 @@ prism_status_t prism_rectified_apply(const void* o_spa, const void* o_spa_lo, co
  * h >= H zero; rows s >= S zero, the last rank's padding of an uneven split).
  * norm = 1 (q, k): torch.nn.RMSNorm over the H*D row in fp32 (x rsqrt(mean(x^2) +
  * eps) gamma, gamma [H*D] fp32 or NULL), rounded to bf16, then the 3D RoPE of
- * rope_apply_head_dim (:177-182): each (even, odd) pair rotated in double by
- * rope_cs [S, D/2, 2] (cos, sin; the freqs of precompute_freqs_cis_3d, :125-139,
- * assembled as :1183-1187), rounded through float to bf16; rstd [S] receives the
- * norm's rsqrt.  norm = 0 (v): the pack alone.
+ * rope_apply_head_dim (:177-182): each (even, odd) pair rotated by rope_ff
+ * [S, D/2, 4] fp32 = (cos_hi, cos_lo, sin_hi, sin_lo), the double cos / sin of
+ * precompute_freqs_cis_3d (:125-139, assembled as :1183-1187) split into float
+ * hi + lo parts; the rotation is evaluated in float-float arithmetic and rounded to
+ * float, then bf16, which equals the reference's double evaluation rounded through
+ * float except within ~2^-46 of a float midpoint; rstd [S] receives the norm's
+ * rsqrt.  norm = 0 (v): the pack alone.
  * prism_norm_rope_pack_bwd: g [P, S_pack, hp, D] (gradient of out) -> dx [S, H*D]
- * (stride ldx): norm = 1 the conjugate rotation (double, rounded to bf16) then the
+ * (stride ldx): norm = 1 the conjugate rotation (float-float, rounded to bf16) then the
  * RMSNorm gradient (fp32) with x, rstd of the forward, and dgamma [H*D] fp32 (sum
  * over rows, fixed order); norm = 0 the unpack.  workspace:
  * prism_norm_rope_pack_bwd_workspace_bytes(S, H, D). */
 prism_status_t prism_norm_rope_pack(const void* x, int64_t ld, int64_t S, int64_t S_pack, int H, int D,
-                                    int P, int hp, const float* gamma, float eps, const double* rope_cs,
+                                    int P, int hp, const float* gamma, float eps, const float* rope_ff,
                                     int norm, void* out, float* rstd, cudaStream_t stream);
 size_t prism_norm_rope_pack_bwd_workspace_bytes(int64_t S, int H, int D);
 prism_status_t prism_norm_rope_pack_bwd(const void* g, const void* x, int64_t ld, int64_t S, int64_t S_pack,
                                         int H, int D, int P, int hp, const float* gamma, const float* rstd,
-                                        const double* rope_cs, int norm, void* dx, int64_t ldx,
+                                        const float* rope_ff, int norm, void* dx, int64_t ldx,
                                         void* workspace, float* dgamma, cudaStream_t stream);
 
 /* Block-sparse attention backward (attn_bwd_bsa_varlen_triton,

@@ -8,10 +8,18 @@
 //
 // Numerics follow the reference's op sequence: the norm in fp32
 // (x * rsqrt(mean(x^2) + eps)) * gamma rounded to bf16; the rotation of that bf16
-// pair in double, (a c - b s, a s + b c); the double result rounded to float, then
-// to bf16 (the double -> bf16 conversion goes through float).  Backward: the
-// conjugate rotation in double rounded the same way, then the RMSNorm gradient in
-// fp32.  Built with -fmad=false (every product and sum rounds once).
+// pair, (a c - b s, a s + b c), which the reference evaluates in double and rounds
+// to float, then to bf16 (its double -> bf16 conversion goes through float).  Here
+// the rotation is evaluated in float-float arithmetic from a table of cos / sin
+// split into float hi + lo parts (rope_ff [S][D/2][4] = cos_hi, cos_lo, sin_hi,
+// sin_lo): a * c_hi is exact as a two-product (a bf16 has 8 significant bits),
+// a * c_lo lies below the float rounding level, and the two products are added with
+// a two-sum, so the float result is the correctly rounded value of the exact
+// rotation except within ~2^-46 of a float rounding midpoint, where the reference's
+// double path may round differently (then the bf16 results still agree unless that
+// float lies on a bf16 midpoint).  Backward: the conjugate rotation the same way,
+// rounded to bf16, then the RMSNorm gradient in fp32.  Built with -fmad=false (every
+// product and sum rounds once; the two-products are explicit fmaf).
 #include <cuda_bf16.h>
 #include <math.h>
 #include <stdint.h>
@@ -29,9 +37,22 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
 }
-// double -> bf16 as torch converts it: through float
-__device__ __forceinline__ float d2bf(double x) {
-  return __bfloat162float(__float2bfloat16_rn(__double2float_rn(x)));
+__device__ __forceinline__ float f2bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// a c + b s (sign = +1) or a c - b s (sign = -1) with a, b bf16 values, c = c_hi + c_lo,
+// s = s_hi + s_lo: two-products of the hi parts, lo parts folded into the error
+// terms, a two-sum of the products, rounded once to float.
+__device__ __forceinline__ float ff_dot2(float a, float chi, float clo, float b, float shi, float slo,
+                                         float sign) {
+  const float p1 = __fmul_rn(a, chi);
+  const float e1 = __fmaf_rn(a, clo, __fmaf_rn(a, chi, -p1));
+  const float bs = sign * b;
+  const float p2 = __fmul_rn(bs, shi);
+  const float e2 = __fmaf_rn(bs, slo, __fmaf_rn(bs, shi, -p2));
+  const float sum = __fadd_rn(p1, p2);
+  const float bb = __fsub_rn(sum, p1);
+  const float err = __fadd_rn(__fsub_rn(p1, __fsub_rn(sum, bb)), __fsub_rn(p2, bb));
+  return __fadd_rn(sum, __fadd_rn(err, __fadd_rn(e1, e2)));
 }
 
 __device__ float block_sum_f(float v, float* red) {
@@ -48,15 +69,16 @@ __device__ float block_sum_f(float v, float* red) {
 // One CTA per packed row s < S_pack.  x rows [S, C] (C = H * D, row stride ld
 // elements); out [P][S_pack][hp][D] with P * hp >= H (heads h >= H are zero, rows
 // s >= S are zero: the last rank's padding of an uneven split).  norm = 0: v
-// (copy); norm = 1: RMSNorm + RoPE.  rope_cs [S][D/2][2] doubles (cos, sin).  A
+// (copy); norm = 1: RMSNorm + RoPE with rope_ff [S][D/2] float4 (cos_hi, cos_lo,
+// sin_hi, sin_lo).  A
 // thread holds its kV 8-column groups of the row in registers between the norm's
 // reduction and the rotation (kV = ceil(C / 8 / kProdThreads)).
 template <int kV>
 __global__ void __launch_bounds__(kProdThreads) norm_rope_pack_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t S, int64_t S_pack, int H, int D, int P,
-    int hp, const float* __restrict__ gamma, float eps, const double* __restrict__ rope_cs, int norm,
+    int hp, const float* __restrict__ gamma, float eps, const float4* __restrict__ rope_ff, int norm,
     __nv_bfloat16* __restrict__ out, float* __restrict__ rstd_out) {
-  extern __shared__ double cs[];  // D/2 (cos, sin) pairs of this token
+  extern __shared__ float4 cs[];  // D/2 rotations of this token
   __shared__ float red[32];
   const int64_t s = blockIdx.x;
   if (s >= S) {  // padding row (uniform per CTA)
@@ -77,7 +99,7 @@ __global__ void __launch_bounds__(kProdThreads) norm_rope_pack_kernel(
   }
   float r = 1.0f;
   if (norm) {
-    for (int i = threadIdx.x; i < D; i += blockDim.x) cs[i] = rope_cs[s * D + i];
+    for (int i = threadIdx.x; i < D / 2; i += blockDim.x) cs[i] = __ldg(rope_ff + s * (D / 2) + i);
     float ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < kV; ++k) {
@@ -109,13 +131,10 @@ __global__ void __launch_bounds__(kProdThreads) norm_rope_pack_kernel(
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         // normed pair, rounded to bf16 (the RMSNorm output dtype)
-        const double a = (double)__bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(bf_lo(u[j]), r), g[2 * j])));
-        const double b = (double)__bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(bf_hi(u[j]), r), g[2 * j + 1])));
-        const int pi = (d0 >> 1) + j;
-        const double c = cs[2 * pi], sn = cs[2 * pi + 1];
-        const double re = __dsub_rn(__dmul_rn(a, c), __dmul_rn(b, sn));
-        const double im = __dadd_rn(__dmul_rn(a, sn), __dmul_rn(b, c));
-        w[j] = pack2(d2bf(re), d2bf(im));
+        const float a = f2bf(__fmul_rn(__fmul_rn(bf_lo(u[j]), r), g[2 * j]));
+        const float b = f2bf(__fmul_rn(__fmul_rn(bf_hi(u[j]), r), g[2 * j + 1]));
+        const float4 t = cs[(d0 >> 1) + j];  // cos_hi, cos_lo, sin_hi, sin_lo
+        w[j] = pack2(ff_dot2(a, t.x, t.y, b, t.z, t.w, -1.0f), ff_dot2(a, t.z, t.w, b, t.x, t.y, 1.0f));
       }
       o = make_uint4(w[0], w[1], w[2], w[3]);
     }
@@ -130,34 +149,35 @@ __global__ void __launch_bounds__(kProdThreads) norm_rope_pack_kernel(
 }
 
 // Backward.  g [P][S_pack][hp][D]: gradient of the packed output.  With
-// dy = the conjugate rotation of g (double, rounded to bf16 through float) and
+// dy = the conjugate rotation of g (float-float, rounded to bf16) and
 // r = rstd[s]:
 //   dx = r (gamma dy) - x r^3 / C * dot,  dot = sum over the row of gamma dy x,
 //   dgamma = sum over rows of dy x r.
 // Phase A: one warp per row computes dot.  Phase B: one thread per 8 columns of a
 // 32-row tile writes dx and its tile's dgamma partial [S / 32][C]; norm = 0 is the
 // unpack alone.
-__device__ __forceinline__ void rot_back8(const uint4 gv, const double* csrow, int d0, float dy[8]) {
+__device__ __forceinline__ void rot_back8(const uint4 gv, const float4* __restrict__ ffrow, int d0,
+                                          float dy[8]) {
   const uint32_t gu[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int pi = (d0 >> 1) + j;
-    const double c = csrow[2 * pi], sn = csrow[2 * pi + 1];
-    const double ga = (double)bf_lo(gu[j]), gb = (double)bf_hi(gu[j]);
-    dy[2 * j] = d2bf(__dadd_rn(__dmul_rn(ga, c), __dmul_rn(gb, sn)));
-    dy[2 * j + 1] = d2bf(__dsub_rn(__dmul_rn(gb, c), __dmul_rn(ga, sn)));
+    const float4 t = __ldg(ffrow + (d0 >> 1) + j);  // cos_hi, cos_lo, sin_hi, sin_lo
+    const float ga = bf_lo(gu[j]), gb = bf_hi(gu[j]);
+    // gradient through (a + ib)(c + is): the conjugate rotation
+    dy[2 * j] = f2bf(ff_dot2(ga, t.x, t.y, gb, t.z, t.w, 1.0f));
+    dy[2 * j + 1] = f2bf(ff_dot2(gb, t.x, t.y, ga, t.z, t.w, -1.0f));
   }
 }
 
 __global__ void norm_rope_dot_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ x,
                                      int64_t ld, int64_t S, int64_t S_pack, int H, int D, int hp,
-                                     const float* __restrict__ gamma, const double* __restrict__ rope_cs,
+                                     const float* __restrict__ gamma, const float4* __restrict__ rope_ff,
                                      float* __restrict__ dot) {
   const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (s >= S) return;
   const int nv = H * D / 8;
-  const double* csrow = rope_cs + s * D;
+  const float4* csrow = rope_ff + s * (D / 2);
   float acc = 0.0f;
 #pragma unroll 4
   for (int i = lane; i < nv; i += 32) {
@@ -188,7 +208,7 @@ constexpr int kProdTileRows = 32;
 __global__ void __launch_bounds__(kProdThreads) norm_rope_dx_kernel(
     const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t S,
     int64_t S_pack, int H, int D, int hp, const float* __restrict__ gamma, const float* __restrict__ rstd,
-    const float* __restrict__ dot, const double* __restrict__ rope_cs, int norm,
+    const float* __restrict__ dot, const float4* __restrict__ rope_ff, int norm,
     __nv_bfloat16* __restrict__ dx, int64_t ldx, float* __restrict__ dgamma_part) {
   const int C = H * D, nv = C / 8;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;  // 8-column group
@@ -213,7 +233,7 @@ __global__ void __launch_bounds__(kProdThreads) norm_rope_dx_kernel(
     }
     const uint4 xq = __ldg(reinterpret_cast<const uint4*>(x + s * ld) + i);
     float dy[8];
-    rot_back8(gv, rope_cs + s * D, d0, dy);
+    rot_back8(gv, rope_ff + s * (D / 2), d0, dy);
     const float r = __ldg(rstd + s);
     const float coef = __fdiv_rn(__fmul_rn(__fmul_rn(__fmul_rn(r, r), r), __ldg(dot + s)), (float)C);
     const uint32_t xu[4] = {xq.x, xq.y, xq.z, xq.w};
@@ -259,21 +279,23 @@ using namespace prism;
 extern "C" {
 
 prism_status_t prism_norm_rope_pack(const void* x, int64_t ld, int64_t S, int64_t S_pack, int H, int D,
-                                    int P, int hp, const float* gamma, float eps, const double* rope_cs,
+                                    int P, int hp, const float* gamma, float eps, const float* rope_ff,
                                     int norm, void* out, float* rstd, cudaStream_t stream) {
-  PRISM_CHECK_ARG(x && out && (!norm || (rope_cs && rstd)), "prism_norm_rope_pack: null pointer");
+  PRISM_CHECK_ARG(x && out && (!norm || (rope_ff && rstd)), "prism_norm_rope_pack: null pointer");
   PRISM_CHECK_ARG(S >= 0 && S_pack >= S && S_pack < (int64_t)1 << 31 && H >= 1 && D >= 8 && D % 8 == 0 &&
                       P >= 1 && hp >= 1 && P * hp >= H && ld % 8 == 0 && ld >= (int64_t)H * D &&
                       (int64_t)H * D <= 8 * 8 * kProdThreads,
                   "prism_norm_rope_pack: bad sizes (hidden width <= %d)", 8 * 8 * kProdThreads);
-  PRISM_CHECK_ARG(aligned16(x) && aligned16(out) && (gamma == nullptr || aligned16(gamma)),
+  PRISM_CHECK_ARG(aligned16(x) && aligned16(out) && (gamma == nullptr || aligned16(gamma)) &&
+                      (rope_ff == nullptr || aligned16(rope_ff)),
                   "prism_norm_rope_pack: tensors must be 16-byte aligned");
   if (S_pack == 0) return PRISM_OK;
   const int nvt = (H * D / 8 + kProdThreads - 1) / kProdThreads;
-  const size_t sm = norm ? D * sizeof(double) : 0;
+  const size_t sm = norm ? (D / 2) * sizeof(float4) : 0;
 #define PRISM_NRP_FWD(V)                                                                              \
   norm_rope_pack_kernel<V><<<(unsigned)S_pack, kProdThreads, sm, stream>>>(                           \
-      (const __nv_bfloat16*)x, ld, S, S_pack, H, D, P, hp, gamma, eps, rope_cs, norm, (__nv_bfloat16*)out, \
+      (const __nv_bfloat16*)x, ld, S, S_pack, H, D, P, hp, gamma, eps, (const float4*)rope_ff, norm,       \
+      (__nv_bfloat16*)out,                                                                             \
       rstd)
   switch (nvt) {
     case 1: PRISM_NRP_FWD(1); break;
@@ -298,9 +320,9 @@ size_t prism_norm_rope_pack_bwd_workspace_bytes(int64_t S, int H, int D) {
 
 prism_status_t prism_norm_rope_pack_bwd(const void* g, const void* x, int64_t ld, int64_t S, int64_t S_pack,
                                         int H, int D, int P, int hp, const float* gamma, const float* rstd,
-                                        const double* rope_cs, int norm, void* dx, int64_t ldx,
+                                        const float* rope_ff, int norm, void* dx, int64_t ldx,
                                         void* workspace, float* dgamma, cudaStream_t stream) {
-  PRISM_CHECK_ARG(g && dx && (!norm || (x && rstd && rope_cs && workspace && dgamma)),
+  PRISM_CHECK_ARG(g && dx && (!norm || (x && rstd && rope_ff && workspace && dgamma)),
                   "prism_norm_rope_pack_bwd: null pointer");
   PRISM_CHECK_ARG(S >= 0 && S_pack >= S && S < (int64_t)1 << 31 && H >= 1 && D >= 8 && D % 8 == 0 &&
                       P >= 1 && hp >= 1 && P * hp >= H && ld % 8 == 0 && ldx % 8 == 0,
@@ -316,12 +338,14 @@ prism_status_t prism_norm_rope_pack_bwd(const void* g, const void* x, int64_t ld
   float* part = norm ? (float*)workspace + ((S + 63) / 64) * 64 : nullptr;
   if (norm) {
     norm_rope_dot_kernel<<<(unsigned)((S * 32 + 255) / 256), 256, 0, stream>>>(
-        (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, ld, S, S_pack, H, D, hp, gamma, rope_cs, dot);
+        (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, ld, S, S_pack, H, D, hp, gamma,
+        (const float4*)rope_ff, dot);
     PRISM_CHECK_LAUNCH("prism_norm_rope_pack_bwd/dot");
   }
   norm_rope_dx_kernel<<<dim3((unsigned)((nv + kProdThreads - 1) / kProdThreads), (unsigned)tiles),
                         kProdThreads, 0, stream>>>(
-      (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, ld, S, S_pack, H, D, hp, gamma, rstd, dot, rope_cs,
+      (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, ld, S, S_pack, H, D, hp, gamma, rstd, dot,
+      (const float4*)rope_ff,
       norm, (__nv_bfloat16*)dx, ldx, part);
   PRISM_CHECK_LAUNCH("prism_norm_rope_pack_bwd/dx");
   if (norm) {

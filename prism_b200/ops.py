@@ -337,9 +337,10 @@ def rectified_apply(o_spa, o_spa_lo, R, o_ncri, seq_q: int, chunk_q: int, out=No
 
 # --------------------------------------------------------- producer fusion
 def norm_rope_pack(x: torch.Tensor, heads: int, P: int, hp: int, S_pack: int, gamma=None,
-                   eps: float = 1e-6, rope_cs=None, norm: bool = True):
-    """x [S, heads*D] bf16 -> (packed [P, S_pack, hp, D] bf16, rstd [S] fp32 or None)."""
-    _check_cuda(x, gamma, rope_cs)
+                   eps: float = 1e-6, rope_ff=None, norm: bool = True):
+    """x [S, heads*D] bf16 -> (packed [P, S_pack, hp, D] bf16, rstd [S] fp32 or None);
+    rope_ff [S, D/2, 4] fp32 (cos_hi, cos_lo, sin_hi, sin_lo)."""
+    _check_cuda(x, gamma, rope_ff)
     S, C = x.shape
     D = C // heads
     if x.stride(1) != 1:
@@ -348,14 +349,14 @@ def norm_rope_pack(x: torch.Tensor, heads: int, P: int, hp: int, S_pack: int, ga
     rstd = torch.empty(S, dtype=torch.float32, device=x.device) if norm else None
     g = None if gamma is None else gamma.to(torch.float32).contiguous()
     _lib.call("prism_norm_rope_pack", _p(x), x.stride(0), S, S_pack, heads, D, P, hp, _p(g),
-              float(eps), _p(rope_cs), int(norm), _p(out), _p(rstd), _stream(x))
+              float(eps), _p(rope_ff), int(norm), _p(out), _p(rstd), _stream(x))
     return out, rstd
 
 
-def norm_rope_pack_bwd(g: torch.Tensor, x, heads: int, S: int, gamma=None, rstd=None, rope_cs=None,
+def norm_rope_pack_bwd(g: torch.Tensor, x, heads: int, S: int, gamma=None, rstd=None, rope_ff=None,
                        norm: bool = True):
     """g [P, S_pack, hp, D] -> (dx [S, heads*D] bf16, dgamma [heads*D] fp32 or None)."""
-    _check_cuda(g, x, gamma, rstd, rope_cs)
+    _check_cuda(g, x, gamma, rstd, rope_ff)
     P, S_pack, hp, D = g.shape
     gc = g.contiguous()
     dx = torch.empty(S, heads * D, dtype=torch.bfloat16, device=g.device)
@@ -364,7 +365,7 @@ def norm_rope_pack_bwd(g: torch.Tensor, x, heads: int, S: int, gamma=None, rstd=
     gm = None if gamma is None else gamma.to(torch.float32).contiguous()
     xs = 0 if x is None else x.stride(0)
     _lib.call("prism_norm_rope_pack_bwd", _p(gc), _p(x), xs, S, S_pack, heads, D, P, hp, _p(gm),
-              _p(rstd), _p(rope_cs), int(norm), _p(dx), dx.stride(0), _p(ws), _p(dgamma), _stream(g))
+              _p(rstd), _p(rope_ff), int(norm), _p(dx), dx.stride(0), _p(ws), _p(dgamma), _stream(g))
     return dx, dgamma
 
 

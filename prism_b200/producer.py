@@ -24,7 +24,10 @@ Here:
   GEMMs instead of an unpack copy plus one GEMM.
 
 ``rope_table`` restates ``precompute_freqs_cis_3d`` (:125-139) and the per-token
-assembly of :1183-1187 as a (cos, sin) float64 table.
+assembly of :1183-1187 as a (cos, sin) float64 table; the kernels take it split into
+float hi + lo parts (``rope_table_ff``) and evaluate the rotation in float-float
+arithmetic, which reproduces the reference's float64 evaluation after its rounding
+to bf16.
 """
 from __future__ import annotations
 
@@ -65,6 +68,17 @@ def rope_table(grid: Tuple[int, int, int], head_dim: int, theta: float = 10000.0
     return torch.view_as_real(freqs).contiguous().to(device)
 
 
+def rope_table_ff(table: torch.Tensor) -> torch.Tensor:
+    """A float64 (cos, sin) table [S, D/2, 2] -> the kernels' float-float form
+    [S, D/2, 4] fp32 = (cos_hi, cos_lo, sin_hi, sin_lo), hi = float(x),
+    lo = float(x - hi)."""
+    if table.dtype == torch.float32 and table.shape[-1] == 4:
+        return table
+    hi = table.to(torch.float32)
+    lo = (table - hi.to(torch.float64)).to(torch.float32)
+    return torch.stack([hi[..., 0], lo[..., 0], hi[..., 1], lo[..., 1]], dim=-1).contiguous()
+
+
 class _NormRopePack(torch.autograd.Function):
     """(q_lin, k_lin, v_lin) [S, H*D] -> packed (q, k, v) [P, S_pack, hp, D]."""
 
@@ -93,7 +107,9 @@ class _NormRopePack(torch.autograd.Function):
 
 def norm_rope_pack(q_lin, k_lin, v_lin, gamma_q, gamma_k, eps: float, rope_cs, heads: int,
                    P: int = 1, hp: Optional[int] = None, S_pack: Optional[int] = None):
-    """RMSNorm + 3D RoPE of q / k and the all-to-all pack of q / k / v (differentiable)."""
+    """RMSNorm + 3D RoPE of q / k and the all-to-all pack of q / k / v (differentiable).
+    rope_cs: rope_table's float64 table or its rope_table_ff form."""
+    rope_cs = rope_table_ff(rope_cs)
     hp = heads if hp is None else hp
     S_pack = q_lin.shape[0] if S_pack is None else S_pack
     return _NormRopePack.apply(q_lin, k_lin, v_lin, gamma_q, gamma_k, float(eps), rope_cs, heads, P,
@@ -207,4 +223,4 @@ def fused_self_attention(x: torch.Tensor, rope_cs: torch.Tensor, params: dict, n
     return out.unsqueeze(0)
 
 
-__all__ = ["rope_table", "norm_rope_pack", "o_proj_packed", "fused_self_attention"]
+__all__ = ["rope_table", "rope_table_ff", "norm_rope_pack", "o_proj_packed", "fused_self_attention"]

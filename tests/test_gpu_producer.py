@@ -20,7 +20,8 @@ from helpers import bits, load_fixture, rel_l2
 from inputs import PRODUCER_CASES, make_producer_inputs
 from oracle import oracle as O
 from prism_b200 import ops, run_bsa_uniform
-from prism_b200.producer import fused_self_attention, norm_rope_pack, o_proj_packed, rope_table
+from prism_b200.producer import (fused_self_attention, norm_rope_pack, o_proj_packed, rope_table,
+                                 rope_table_ff)
 
 pytestmark = pytest.mark.gpu
 
@@ -39,7 +40,7 @@ def test_norm_rope_forward(name, cuda):
     fx = load_fixture(name)
     x, gamma = make_producer_inputs(grid, heads, D, seed)
     S = x.shape[1]
-    cs = rope_table(grid, D, device=cuda)
+    cs = rope_table_ff(rope_table(grid, D, device=cuda))
     q_pk, rstd = ops.norm_rope_pack(x[0].to(cuda), heads, 1, heads, S, gamma.to(cuda).float(), 1e-6, cs,
                                     True)
     got = bits(q_pk.view(S, heads * D))
@@ -58,7 +59,7 @@ def test_pack_layout(cuda):
     grid, heads, D, seed = (2, 3, 5), 3, 128, 7
     x, gamma = make_producer_inputs(grid, heads, D, seed)
     S = x.shape[1]
-    cs = rope_table(grid, D, device=cuda)
+    cs = rope_table_ff(rope_table(grid, D, device=cuda))
     xc, gc = x[0].to(cuda), gamma.to(cuda).float()
     ref, _ = ops.norm_rope_pack(xc, heads, 1, heads, S, gc, 1e-6, cs, True)
     ref = ref.view(S, heads, D)
@@ -84,11 +85,12 @@ def test_norm_rope_backward(name, cuda):
     x, gamma = make_producer_inputs(grid, heads, D, seed)
     S, C = x.shape[1], heads * D
     cs = rope_table(grid, D, device=cuda)
+    ff = rope_table_ff(cs)
     gen = torch.Generator().manual_seed(seed + 50)
     g = torch.randn(S, C, generator=gen).to(torch.bfloat16)
     xc, gc = x[0].to(cuda), gamma.to(cuda).float()
-    _, rstd = ops.norm_rope_pack(xc, heads, 1, heads, S, gc, 1e-6, cs, True)
-    dx, dgamma = ops.norm_rope_pack_bwd(g.to(cuda).view(1, S, heads, D), xc, heads, S, gc, rstd, cs, True)
+    _, rstd = ops.norm_rope_pack(xc, heads, 1, heads, S, gc, 1e-6, ff, True)
+    dx, dgamma = ops.norm_rope_pack_bwd(g.to(cuda).view(1, S, heads, D), xc, heads, S, gc, rstd, ff, True)
     # float64 reference of the same math
     x64 = x[0].double().requires_grad_(True)
     g64 = gamma.double().requires_grad_(True)

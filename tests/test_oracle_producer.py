@@ -49,3 +49,38 @@ def test_rms_norm_restatement(name):
     ref = fx["normed"]
     diff = np.abs(got.astype(np.int32) - ref.astype(np.int32))
     assert diff.max() <= 1 and (diff == 0).mean() >= 0.99, (diff.max(), (diff == 0).mean())
+
+
+def _ff_dot2(a, chi, clo, b, shi, slo, sign):
+    """The kernels' float-float a c + sign b s, emulated exactly: each fmaf's exact
+    value is representable in float64 (a bf16 times a float needs <= 32 bits), so
+    float64 arithmetic rounded once to float32 is the fused multiply-add."""
+    f32 = np.float32
+    a, b = a.astype(f32), (sign * b).astype(f32)
+    p1 = (a * chi).astype(f32)
+    e1 = (a.astype(np.float64) * clo + ((a.astype(np.float64) * chi) - p1).astype(f32)).astype(f32)
+    p2 = (b * shi).astype(f32)
+    e2 = (b.astype(np.float64) * slo + ((b.astype(np.float64) * shi) - p2).astype(f32)).astype(f32)
+    s = (p1 + p2).astype(f32)
+    bb = (s - p1).astype(f32)
+    err = ((p1 - (s - bb).astype(f32)).astype(f32) + (p2 - bb).astype(f32)).astype(f32)
+    return (s + (err + (e1 + e2).astype(f32)).astype(f32)).astype(f32)
+
+
+def test_float_float_rotation_matches_double():
+    """The kernels' float-float rotation rounds to the same bf16 as the reference's
+    double evaluation (rounded through float) on random bf16 pairs and angles."""
+    rng = np.random.default_rng(0)
+    n = 1 << 20
+    a = O.bf16_bits_to_f32(O.f32_to_bf16_bits(rng.standard_normal(n).astype(np.float32) * 3))
+    b = O.bf16_bits_to_f32(O.f32_to_bf16_bits(rng.standard_normal(n).astype(np.float32) * 3))
+    ang = rng.uniform(0, 1000.0, n)
+    c, s = np.cos(ang), np.sin(ang)
+    chi, shi = c.astype(np.float32), s.astype(np.float32)
+    clo = (c - chi.astype(np.float64)).astype(np.float32)
+    slo = (s - shi.astype(np.float64)).astype(np.float32)
+    for got, ref in ((_ff_dot2(a, chi, clo, b, shi, slo, -1.0), a * c - b * s),
+                     (_ff_dot2(a, shi, slo, b, chi, clo, 1.0), a * s + b * c)):
+        g16 = O.f32_to_bf16_bits(got)
+        r16 = O.f32_to_bf16_bits(ref.astype(np.float32))
+        assert np.array_equal(g16, r16), int((g16 != r16).sum())
