@@ -809,7 +809,11 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
     const int32_t* __restrict__ block_tiles, int tq, int tk,
     const uint64_t* __restrict__ tile_bits, int64_t n_qt, int64_t n_kt, int wq, int mode,
     double sparsity, double cdf, float sm_scale, uint32_t* __restrict__ bits_q) {
-  extern __shared__ uint32_t keys[];  // [nb_max] then row bitmap [wq]
+  // dynamic shared memory: fixed-point masses [nb_max] (u64, modes 0 / 1), keys
+  // [nb_max], row bitmap [wq]
+  extern __shared__ unsigned long long smem_u64[];
+  unsigned long long* mass = smem_u64;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_u64 + (mode == 2 ? 0 : nb_max));
   uint32_t* row = keys + nb_max;
   __shared__ uint32_t hist_cnt[256];
   __shared__ unsigned long long hist_mass[256];
@@ -866,7 +870,11 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
     const unsigned long long Z = block_sum_u64<unsigned long long>(lz, red);
     const float Zf = __fmul_rn(__ull2float_rn(Z), 0x1p-50f);
     for (int i = tid; i < nb; i += blockDim.x)
-      keys[i] = __float_as_uint(__fdiv_rn(__uint_as_float(keys[i]), Zf));
+    {
+      const uint32_t kk = __float_as_uint(__fdiv_rn(__uint_as_float(keys[i]), Zf));
+      keys[i] = kk;
+      mass[i] = fix63(kk);  // one conversion per key, reused by every mass pass
+    }
     // crossing point m_c: smallest m with round(S(m)) >= pf, by mass radix descent
     if (tid == 0) {
       st.prefix = 0;
@@ -890,7 +898,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
         const uint32_t kk = i < nb ? keys[i] : 0u;
         const bool in = i < nb && (kk & pmask) == prefix;
         hist_add_warp(hist_cnt, nullptr, in, (kk >> shift) & 0xff, 0ull, false);
-        if (in) atomicAdd(&wmass[(kk >> shift) & 0xff], fix63(kk));
+        if (in) atomicAdd(&wmass[(kk >> shift) & 0xff], mass[i]);
       }
       __syncthreads();
       for (int i = tid; i < 256; i += blockDim.x) {
@@ -1480,7 +1488,7 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
   PRISM_CHECK_ARG(D >= 16 && D <= 256, "prism_block_select: D=%d unsupported", D);
   const int64_t n_tiles = S / 64;
   const int nb_max = (int)n_tiles;
-  PRISM_CHECK_ARG(nb_max <= 40000, "prism_block_select: %d blocks exceed the per-row shared-memory limit", nb_max);
+  PRISM_CHECK_ARG(nb_max <= 18000, "prism_block_select: %d blocks exceed the per-row shared-memory limit (18000)", nb_max);
   const int wq = (int)((n_tiles + 31) / 32);
   float* qc = (float*)workspace;
   float* kc = qc + (size_t)heads * nb_max * D;
@@ -1498,7 +1506,7 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
                                                           nullptr, sc);
   PRISM_CHECK_LAUNCH("prism_block_select/score");
   const float sm_scale = (float)(1.0 / sqrt((double)D));
-  const size_t selsm = ((size_t)nb_max + wq) * sizeof(uint32_t);
+  const size_t selsm = (size_t)nb_max * sizeof(unsigned long long) + ((size_t)nb_max + wq) * sizeof(uint32_t);
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)selsm),
                    "prism_block_select: smem attribute");
   select_kernel<<<dim3(nb_max, heads), kSelThreads, selsm, stream>>>(
@@ -1556,7 +1564,7 @@ prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, in
                   (long long)seq_q, (long long)seq_k);
   const int64_t n_qt = Sq / 64, n_kt = Sk / 64;
   const int nq = (int)(seq_q / chunk_q), nk = (int)(seq_k / chunk_k);
-  PRISM_CHECK_ARG(nk <= 40000, "prism_block_select_uniform: %d key chunks exceed the per-row shared-memory limit", nk);
+  PRISM_CHECK_ARG(nk <= 18000, "prism_block_select_uniform: %d key chunks exceed the per-row shared-memory limit (18000)", nk);
   const int wk = (int)((n_kt + 31) / 32), wq = (int)((n_qt + 31) / 32);
   float* qc = (float*)workspace;
   float* kc = qc + (size_t)heads * nq * D;
@@ -1574,7 +1582,7 @@ prism_status_t prism_block_select_uniform(const void* q_re, const void* k_re, in
                  ssm, stream>>>(qc, kc, D, nullptr, nq, nk, col_scale, sc);
   PRISM_CHECK_LAUNCH("prism_block_select_uniform/score");
   const float sm_scale = (float)(1.0 / sqrt((double)D));
-  const size_t selsm = ((size_t)nk + wk) * sizeof(uint32_t);
+  const size_t selsm = (size_t)nk * sizeof(unsigned long long) + ((size_t)nk + wk) * sizeof(uint32_t);
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)selsm),
                    "prism_block_select_uniform: smem attribute");
   select_kernel<<<dim3(nq, heads), kSelThreads, selsm, stream>>>(
