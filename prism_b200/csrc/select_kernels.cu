@@ -846,7 +846,38 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
     ub = nb;
   }
   const float pf = (float)cdf;
-  long long n_eff;
+  long long n_eff = 0;
+  uint32_t vstar = 0;  // the n_eff-th largest key
+  int need = 0;        // how many keys equal to vstar are taken (lowest indices first)
+  bool have_threshold = false;
+
+  // Count passes: st.prefix <- the target-th largest key, st.cnt_above <- the number
+  // of keys above it (4 byte-wise radix passes over the order-preserving keys).
+  auto count_select = [&](long long target) {
+    if (tid == 0) {
+      st.prefix = 0;
+      st.pmask = 0;
+      st.cnt_above = 0;
+      st.mass_above = 0;
+      st.found = 1;
+    }
+    __syncthreads();
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int i = tid; i < 256; i += blockDim.x) hist_cnt[i] = 0;
+      __syncthreads();
+      const uint32_t prefix = st.prefix, pmask = st.pmask;
+      for (int i0 = 0; i0 < nb; i0 += blockDim.x) {  // warp-uniform trip count
+        const int i = i0 + tid;
+        const uint32_t kk = i < nb ? keys[i] : 0u;
+        hist_add_warp(hist_cnt, hist_mass, i < nb && (kk & pmask) == prefix, (kk >> shift) & 0xff,
+                      0ull, false);
+      }
+      __syncthreads();
+      if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 0, (int)target, pf, &st);
+      __syncthreads();
+    }
+  };
 
   if (mode == 2) {
     for (int i = tid; i < nb; i += blockDim.x)
@@ -875,93 +906,104 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
       keys[i] = kk;
       mass[i] = fix63(kk);  // one conversion per key, reused by every mass pass
     }
-    // crossing point m_c: smallest m with round(S(m)) >= pf, by mass radix descent
-    if (tid == 0) {
-      st.prefix = 0;
-      st.pmask = 0;
-      st.cnt_above = 0;
-      st.mass_above = 0;
-      st.found = 1;
-      st.bucket_cnt = 0;
-    }
     __syncthreads();
-    bool crossed = true;
-    for (int pass = 0; pass < 4 && crossed; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int i = tid; i < 256; i += blockDim.x) hist_cnt[i] = 0;
-      for (int i = tid; i < (kSelThreads / 32) * 256; i += blockDim.x) (&hist_mass_w[0][0])[i] = 0;
-      __syncthreads();
-      const uint32_t prefix = st.prefix, pmask = st.pmask;
-      unsigned long long* wmass = hist_mass_w[tid >> 5];
-      for (int i0 = 0; i0 < nb; i0 += blockDim.x) {  // warp-uniform trip count
-        const int i = i0 + tid;
-        const uint32_t kk = i < nb ? keys[i] : 0u;
-        const bool in = i < nb && (kk & pmask) == prefix;
-        hist_add_warp(hist_cnt, nullptr, in, (kk >> shift) & 0xff, 0ull, false);
-        if (in) atomicAdd(&wmass[(kk >> shift) & 0xff], mass[i]);
+    // With S(m) the (fixed-point) mass of the m largest keys, the crossing point is
+    // m_c = min{m : round(S(m)) >= pf} and n_eff = min(max(m_c, k_topk), ub)
+    // (m_c - 1 clamped to ub first).  S is monotone, so round(S(k_topk)) >= pf means
+    // m_c <= k_topk and n_eff = k_topk: when the top-k term is likely to dominate
+    // (mode 0 with a small mass threshold) that is tested first, with the k_topk-th
+    // key found by count passes, and the mass passes are skipped when it holds.
+    // Both orders give the same n_eff, threshold and tie count.
+    if (mode == 0 && cdf < 0.5) {
+      count_select(k_topk);
+      const uint32_t vk = st.prefix;
+      const long long ca = st.cnt_above;
+      unsigned long long part = 0;
+      for (int i = tid; i < nb; i += blockDim.x)
+        if (keys[i] > vk) part += mass[i];
+      const unsigned long long Sk =
+          block_sum_u64<unsigned long long>(part, red) + (unsigned long long)(k_topk - ca) * fix63(vk);
+      if (round63(Sk) >= pf) {
+        n_eff = k_topk;
+        vstar = vk;
+        need = (int)(k_topk - ca);
+        have_threshold = true;
       }
       __syncthreads();
-      for (int i = tid; i < 256; i += blockDim.x) {
-        unsigned long long m = 0;
+    }
+    if (!have_threshold) {
+      // crossing point m_c by mass radix descent
+      if (tid == 0) {
+        st.prefix = 0;
+        st.pmask = 0;
+        st.cnt_above = 0;
+        st.mass_above = 0;
+        st.found = 1;
+        st.bucket_cnt = 0;
+      }
+      __syncthreads();
+      bool crossed = true;
+      for (int pass = 0; pass < 4 && crossed; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = tid; i < 256; i += blockDim.x) hist_cnt[i] = 0;
+        for (int i = tid; i < (kSelThreads / 32) * 256; i += blockDim.x) (&hist_mass_w[0][0])[i] = 0;
+        __syncthreads();
+        const uint32_t prefix = st.prefix, pmask = st.pmask;
+        unsigned long long* wmass = hist_mass_w[tid >> 5];
+        for (int i0 = 0; i0 < nb; i0 += blockDim.x) {  // warp-uniform trip count
+          const int i = i0 + tid;
+          const uint32_t kk = i < nb ? keys[i] : 0u;
+          const bool in = i < nb && (kk & pmask) == prefix;
+          hist_add_warp(hist_cnt, nullptr, in, (kk >> shift) & 0xff, 0ull, false);
+          if (in) atomicAdd(&wmass[(kk >> shift) & 0xff], mass[i]);
+        }
+        __syncthreads();
+        for (int i = tid; i < 256; i += blockDim.x) {
+          unsigned long long m = 0;
 #pragma unroll
-        for (int w = 0; w < kSelThreads / 32; ++w) m += hist_mass_w[w][i];
-        hist_mass[i] = m;
+          for (int w = 0; w < kSelThreads / 32; ++w) m += hist_mass_w[w][i];
+          hist_mass[i] = m;
+        }
+        __syncthreads();
+        if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 1, 0, pf, &st);
+        __syncthreads();
+        crossed = st.found != 0;
+      }
+      long long cnt_lt, m_c = 0, lo = 0;
+      if (!crossed) {
+        cnt_lt = ub;
+      } else {
+        // all remaining candidates share the value st.prefix; find j* in [1, bucket_cnt]
+        const unsigned long long fv = fix63(st.prefix);
+        long long hi = st.bucket_cnt;
+        lo = 1;
+        while (lo < hi) {
+          const long long mid = (lo + hi) >> 1;
+          if (round63(st.mass_above + (unsigned long long)mid * fv) >= pf) hi = mid;
+          else lo = mid + 1;
+        }
+        m_c = st.cnt_above + lo;
+        cnt_lt = m_c - 1 < ub ? m_c - 1 : ub;
+      }
+      long long n = cnt_lt + 1;
+      if (n < k_topk) n = k_topk;
+      if (n > nb) n = nb;
+      n_eff = n < ub ? n : ub;
+      if (crossed && n_eff == m_c) {
+        // the n_eff-th largest key is the crossing key itself: st.prefix, with
+        // st.cnt_above keys above it and lo of its ties taken
+        vstar = st.prefix;
+        need = (int)lo;
+        have_threshold = true;
       }
       __syncthreads();
-      if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 1, 0, pf, &st);
-      __syncthreads();
-      crossed = st.found != 0;
     }
-    long long cnt_lt;
-    if (!crossed) {
-      cnt_lt = ub;
-    } else {
-      // all remaining candidates share the value st.prefix; find j* in [1, bucket_cnt]
-      const unsigned long long fv = fix63(st.prefix);
-      long long lo = 1, hi = st.bucket_cnt;
-      while (lo < hi) {
-        const long long mid = (lo + hi) >> 1;
-        if (round63(st.mass_above + (unsigned long long)mid * fv) >= pf) hi = mid;
-        else lo = mid + 1;
-      }
-      const long long m_c = st.cnt_above + lo;
-      cnt_lt = m_c - 1 < ub ? m_c - 1 : ub;
-    }
-    long long n = cnt_lt + 1;
-    if (n < k_topk) n = k_topk;
-    if (n > nb) n = nb;
-    n_eff = n < ub ? n : ub;
-    __syncthreads();
   }
 
   // threshold element: the n_eff-th largest key (ties by lower index)
   for (int i = tid; i < wq; i += blockDim.x) row[i] = 0;
-  uint32_t vstar = 0;
-  int need = 0;
-  if (n_eff > 0) {
-    if (tid == 0) {
-      st.prefix = 0;
-      st.pmask = 0;
-      st.cnt_above = 0;
-      st.mass_above = 0;
-      st.found = 1;
-    }
-    __syncthreads();
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int i = tid; i < 256; i += blockDim.x) hist_cnt[i] = 0;
-      __syncthreads();
-      const uint32_t prefix = st.prefix, pmask = st.pmask;
-      for (int i0 = 0; i0 < nb; i0 += blockDim.x) {  // warp-uniform trip count
-        const int i = i0 + tid;
-        const uint32_t kk = i < nb ? keys[i] : 0u;
-        hist_add_warp(hist_cnt, hist_mass, i < nb && (kk & pmask) == prefix, (kk >> shift) & 0xff,
-                      0ull, false);
-      }
-      __syncthreads();
-      if (tid < 32) radix_walk(hist_cnt, hist_mass, shift, 0, (int)n_eff, pf, &st);
-      __syncthreads();
-    }
+  if (n_eff > 0 && !have_threshold) {
+    count_select(n_eff);
     vstar = st.prefix;
     need = (int)n_eff - st.cnt_above;
   }
