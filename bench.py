@@ -425,6 +425,53 @@ def run_producer(args):
     print(json.dumps(line), flush=True)
 
 
+def run_cross(args):
+    """--path cross: the v2a / a2v bridge's cross-modal BSA at 720p (flash_attn_bsa_cross,
+    bsa_interface.py:1276-1392): audio queries (1D, the config's audio tokens) over the
+    video keys (3D grid, 4x4x4 chunks) and video queries over the audio keys, forward +
+    backward, 40 heads x 128; sparsity 0.75 over the video chunks, 0.5 over the two audio
+    chunks (int((1 - 0.75) * 2) = 0 would keep none)."""
+    import torch
+    from prism_b200 import _lib, flash_attn_bsa_cross
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.load(build_if_missing=False)
+    grid, H, D, A = CONFIG["grid"], CONFIG["heads"], CONFIG["head_dim"], CONFIG["audio_tokens"]
+    Sv = grid[0] * grid[1] * grid[2]
+    gen = torch.Generator(device=dev).manual_seed(0)
+    mk = lambda S: torch.randn(1, H, S, D, generator=gen, device=dev).to(torch.bfloat16)
+    lines = {}
+    for name, (qs, ks, Sq, Sk, sp) in {"a2v": ("1d", "3d", A, Sv, 0.75),
+                                        "v2a": ("3d", "1d", Sv, A, 0.5)}.items():
+        q, k, v, do = mk(Sq).requires_grad_(True), mk(Sk).requires_grad_(True), mk(Sk).requires_grad_(True), mk(Sq)
+        kw = dict(q_grid_size=grid if qs == "3d" else None, k_grid_size=grid if ks == "3d" else None,
+                  sparsity=sp, cdf_threshold=None, chunk_3d_shape_q=(4, 4, 4), chunk_3d_shape_k=(4, 4, 4))
+
+        def step():
+            q.grad = k.grad = v.grad = None
+            out = flash_attn_bsa_cross(q, k, v, qs, ks, **kw)
+            out.backward(do)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        lines[name] = {"ms_per_step": e0.elapsed_time(e1) / args.steps, "queries": Sq, "keys": Sk,
+                       "sparsity": sp}
+    line = {"metric": "cross_bsa_fwd_bwd_ms", "value": lines["v2a"]["ms_per_step"], "unit": "ms",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1)",
+            "config": {"workload": "720p MOVA bridge cross-modal BSA (flash_attn_bsa_cross), fwd+bwd",
+                       "heads": H, "head_dim": D, "grid": list(grid), "audio_tokens": A},
+            "directions": lines}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -435,7 +482,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", default="720p", choices=sorted(CONFIGS),
                     help="benchmark config: 720p (config 1, default), 1080p (config 2), 2k (config 3)")
-    ap.add_argument("--path", default="dynamic", choices=["dynamic", "uniform", "producer"],
+    ap.add_argument("--path", default="dynamic", choices=["dynamic", "uniform", "producer", "cross"],
                     help="dynamic block shapes (flash_attn_bsa_3d_dynamic, the metric's path) or "
                          "the uniform fixed-shape path (flash_attn_bsa_3d, 4x4x4 chunks, "
                          "sparsity 0.75, cdf 0.2)")
@@ -451,9 +498,9 @@ def main():
                          "for profiler captures)")
     args = ap.parse_args()
     CONFIG.update(CONFIGS[args.config])
-    if args.path == "producer":
+    if args.path in ("producer", "cross"):
         CONFIG["heads"] = args.heads
-        run_producer(args)
+        (run_producer if args.path == "producer" else run_cross)(args)
         return
     CONFIG["heads"] = args.heads
     CONFIG["path"] = args.path
