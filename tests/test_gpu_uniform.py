@@ -202,3 +202,22 @@ def test_uniform_errors(cuda):
                           chunk_3d_shape_k=(2, 4, 4))
     with pytest.raises(AssertionError):
         flash_attn_bsa_3d(q, q, q, (8, 8, 8), (8, 8, 8), chunk_3d_shape_q=(3, 4, 4))
+
+
+@pytest.mark.parametrize("sparsity,cdf", [(0.95, 0.45), (0.9, 0.3), (0.5, 0.1), (0.75, 0.49)])
+def test_selection_paths_bit_exact(sparsity, cdf, cuda):
+    """Hybrid top-k + cumulative-mass selection on flat random scores (N(0, 1) rows
+    pooled over 64 tokens), where the top-k chunks often hold less than the mass
+    threshold: both the top-k-first shortcut and its fallback to the mass passes run,
+    and the bitmaps equal the oracle's."""
+    g = torch.Generator().manual_seed(int(sparsity * 100 + cdf * 1000))
+    heads, D, S = 2, 64, 64 * 96
+    q = torch.randn(heads, S, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(heads, S, D, generator=g).to(torch.bfloat16)
+    bits_k = torch.full((S // 64,), -1, dtype=torch.int64)  # every key valid
+    bq, bk = ops.block_select_uniform(q.to(cuda), k.to(cuda), S, S, 64, 64, None, bits_k.to(cuda),
+                                      sparsity, cdf)
+    rq, rk, _ = O.block_select_uniform(bits(q), bits(k), S, S, 64, 64, None, None, sparsity, cdf)
+    n = S // 64
+    assert np.array_equal(O.bits_to_dense(bq.cpu().numpy().view(np.uint32), n), O.bits_to_dense(rq, n))
+    assert np.array_equal(O.bits_to_dense(bk.cpu().numpy().view(np.uint32), n), O.bits_to_dense(rk, n))
