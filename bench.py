@@ -89,10 +89,9 @@ def make_layer_inputs(device, rank=0, world=1, seed=0):
     q, k, v = zoned(), zoned(), zoned()          # [S, h, D]  (sequence-major, like the projections)
     do = torch.randn(S, h, D, generator=g, device=device).to(torch.bfloat16)
     a2v = torch.randn(S, CONFIG["hidden"], generator=g, device=device).to(torch.bfloat16)
-    from prism_b200.communications import sp_chunk_sizes
-    sizes = sp_chunk_sizes(S, world)
-    s0 = sum(sizes[:rank])
-    sl = slice(s0, s0 + sizes[rank])
+    C = -(-S // world)  # ceil(S / P) rows per shard, the last one shorter
+    sl = slice(min(rank * C, S), min(rank * C + C, S))
+    sizes = [sl.stop - sl.start if r == rank else 0 for r in range(world)]
     out = {}
     for name, t in (("q", q), ("k", k), ("v", v), ("do", do)):
         out[name] = t[sl].reshape(1, sizes[rank], h * D).contiguous()
@@ -267,78 +266,115 @@ def kernel_times(plan, q4, k4, v4, reps=3):
 
 
 # ------------------------------------------------------------------ CPU leg
-def cpu_baseline(seconds=15.0, threads=None):
-    """The CPU oracle (numpy float32 block-gather attention + the C selection
-    restatement) timed on the host on a bounded sample of the config-1 layer:
-    one head, a random subset of q tiles, forward + backward."""
-    import numpy as np
-    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
-    from oracle import oracle as O  # CPU checker / baseline only
-    threads = threads or os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    T, H, W = CONFIG["grid"]
-    D = CONFIG["head_dim"]
-    Tp, Hp, Wp = padded_grid()
-    rng = np.random.default_rng(0)
-    S = Tp * Hp * Wp
-    nt = S // 64
-    n_groups = S // 512
+class CpuLayerSample:
+    """The CPU restatement of the layer (oracle/: the C selection side and numpy
+    float32 block-gather attention), timed on the host cores on the GPU arm's own
+    inputs: the same seeded tensors (generated on the device by torch's generator,
+    copied to the host once) and the same selection rule, so its shape ids and
+    head-0 selection are the GPU arm's (checked when the GPU bitmap is given).
 
-    def zoned():
-        mean = rng.standard_normal((n_groups, D), dtype=np.float32) * 0.5
-        x = np.repeat(mean, 512, axis=0) + 0.15 * rng.standard_normal((S, D), dtype=np.float32)
-        return x
+    One sample = audio token norms + zone statistics over all heads + shape choice
+    + permutation + the selection of head 0 (full, measured) + forward and backward
+    of as many of head 0's query tiles as fit the time budget (measured).  value =
+    FLOPs of the sampled tiles / their attention time; the layer time is
+    extrapolated separately (statistics once, selection and attention per head)."""
 
-    q, k, v = zoned(), zoned(), zoned()
-    do = rng.standard_normal((S, D), dtype=np.float32)
-    valid = np.ones(S, np.uint8)
-    qb = O.f32_to_bf16_bits(q)[None]
-    kb = O.f32_to_bf16_bits(k)[None]
-    t0 = time.perf_counter()
-    if CONFIG.get("path") == "uniform":
-        # selection (C oracle, one head) over the uniform chunk order
-        c = int(math.prod(CONFIG["chunk"]))
-        bq, bk, _ = O.block_select_uniform(qb, kb, S, S, c, c, None, None, CONFIG["sparsity"],
-                                           CONFIG["cdf_threshold"])
-    else:
-        # selection (C oracle, one head) -- all 64-token shape-0 layout of the bench grid
-        ids = np.zeros(S // 512, np.int64)
-        src, inv, bot, bt, nb = O.layout(ids, (Tp, Hp, Wp))
-        bq, bk, _ = O.block_select(qb, kb, valid, bt, nb, CONFIG["sparsity"],
-                                   CONFIG["cdf_threshold"])
-    t_sel = time.perf_counter() - t0
-    dense = O.bits_to_dense(bq, nt)[0]
-    # attention: as many q tiles as fit the time budget
-    sc = 1.0 / math.sqrt(D)
-    flops = 0.0
-    n_done = 0
-    t1 = time.perf_counter()
-    order = rng.permutation(nt)
-    for qt in order:
-        cols = np.nonzero(dense[qt])[0]
-        keys = (cols[:, None] * 64 + np.arange(64)).reshape(-1)
-        rows = slice(qt * 64, qt * 64 + 64)
-        Q, K, V, dO = q[rows], k[keys], v[keys], do[rows]
-        s = Q @ K.T * sc
-        p = np.exp(s - s.max(1, keepdims=True))
-        p /= p.sum(1, keepdims=True)
-        o = p @ V
-        dv = p.T @ dO
-        dp = dO @ V.T
-        ds = p * (dp - (o * dO).sum(1, keepdims=True))
-        dq = ds @ K * sc
-        dk = ds.T @ Q * sc
-        flops += FWD_BWD_FACTOR * 4 * D * 64 * 64 * cols.size
-        n_done += 1
-        if time.perf_counter() - t1 > seconds:
-            break
-    t_attn = time.perf_counter() - t1
-    tflops = flops / t_attn / 1e12
-    return {"value": tflops, "unit": "TFLOPS", "cores": threads, "kind": "port",
-            "sample": f"1 of 40 heads, {n_done} of {nt} q tiles fwd+bwd in numpy float32 "
-                      f"block-gather form ({t_attn:.1f} s); selection of that head by the C "
-                      f"oracle took {t_sel:.1f} s",
-            "ms_per_layer_extrapolated": (t_attn / max(n_done, 1) * nt * CONFIG["heads"] + t_sel * CONFIG["heads"]) * 1e3}
+    def __init__(self, inp, S, head0_bits=None):
+        import numpy as np
+        import torch
+        sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+        from oracle import oracle as O  # CPU checker / baseline only
+        self.O, self.np = O, np
+        T, H, W = CONFIG["grid"]
+        h, D = CONFIG["heads"], CONFIG["head_dim"]
+        self.gp = padded_grid()
+        Tp, Hp, Wp = self.gp
+        to_bits = lambda t: t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+        x = {n: to_bits(inp[n][0]) for n in ("q", "k", "v", "do", "a2v")}  # [S, h*D] / [S, hidden]
+        self.a2v = x["a2v"]
+
+        def pad(a):  # [S, c] THW order -> [Sp, c] on the padded grid
+            out = np.zeros((Tp, Hp, Wp, a.shape[-1]), np.uint16)
+            out[:T, :H, :W] = a.reshape(T, H, W, -1)
+            return out.reshape(Tp * Hp * Wp, -1)
+
+        self.v_all = np.ascontiguousarray(pad(x["v"]).reshape(-1, h, D).transpose(1, 0, 2))
+        self.q0 = pad(x["q"][:, :D])[None]
+        self.k0 = pad(x["k"][:, :D])[None]
+        self.v0 = pad(x["v"][:, :D])
+        self.do0 = pad(x["do"][:, :D])
+        valid = np.zeros((Tp, Hp, Wp), np.uint8)
+        valid[:T, :H, :W] = 1
+        self.valid = valid.reshape(-1)
+        self.head0_bits = head0_bits
+        self.pad = pad
+        self.S = S
+
+    def run(self, seconds):
+        np, O = self.np, self.O
+        D = CONFIG["head_dim"]
+        t0 = time.perf_counter()
+        norms = self.pad(O.token_norms(self.a2v)[:, None])[:, 0]
+        packed, av, audio = O.zone_stats(self.v_all, self.gp, self.valid, norms)
+        ids, _, _ = O.shape_select(packed, av, audio, True, CONFIG["method"])
+        t_stats = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        src, inv, bot, bt, nb = O.layout(ids, self.gp)
+        q_re, k_re = self.q0[:, src], self.k0[:, src]
+        valid_re = self.valid[src]
+        bq, _, _ = O.block_select(q_re, k_re, valid_re, bt, nb, CONFIG["sparsity"],
+                                  CONFIG["cdf_threshold"])
+        t_sel = time.perf_counter() - t1
+        nt = src.size // 64
+        dense = O.bits_to_dense(bq, nt)[0]
+        same = None if self.head0_bits is None else bool(np.array_equal(bq[0], self.head0_bits))
+        f = O.bf16_bits_to_f32
+        q, k = f(q_re[0]), f(k_re[0])
+        v, do = f(self.v0[src]), f(self.do0[src])
+        kvalid = valid_re.astype(bool)
+        sc = 1.0 / math.sqrt(D)
+        rng = np.random.default_rng(0)
+        flops, n_done, pairs = 0.0, 0, 0
+        t2 = time.perf_counter()
+        for qt in rng.permutation(nt):
+            cols = np.nonzero(dense[qt])[0]
+            keys = (cols[:, None] * 64 + np.arange(64)).reshape(-1)
+            kv = kvalid[keys]
+            rows = slice(qt * 64, qt * 64 + 64)
+            Q, K, V, dO = q[rows], k[keys], v[keys], do[rows]
+            s_ = Q @ K.T * sc
+            s_[:, ~kv] = -np.inf
+            mx = s_.max(1, keepdims=True)
+            mx[~np.isfinite(mx)] = 0.0
+            p = np.exp(s_ - mx)
+            p /= np.maximum(p.sum(1, keepdims=True), 1e-30)
+            o = p @ V
+            dv_ = p.T @ dO
+            dp = dO @ V.T
+            ds = p * (dp - (o * dO).sum(1, keepdims=True))
+            dq_ = ds @ K * sc
+            dk_ = ds.T @ Q * sc
+            flops += FWD_BWD_FACTOR * 4 * D * 64 * 64 * cols.size
+            pairs += cols.size
+            n_done += 1
+            if time.perf_counter() - t2 > seconds:
+                break
+        t_attn = time.perf_counter() - t2
+        wall = time.perf_counter() - t0
+        heads = CONFIG["heads"]
+        layer_ms = (t_stats + heads * (t_sel + t_attn / max(n_done, 1) * nt)) * 1e3
+        return {"value": flops / t_attn / 1e12, "unit": "TFLOPS", "cores": os.cpu_count() or 1,
+                "kind": "port", "wall_ms": wall * 1e3,
+                "sample": f"the GPU arm's inputs: audio norms + zone statistics over {heads} heads + "
+                          f"shape choice ({t_stats:.1f} s, C oracle), head 0's full selection "
+                          f"({t_sel:.1f} s, C oracle, {int(dense.sum())} tile pairs, density "
+                          f"{dense.sum() / nt / nt:.3f}"
+                          + ("" if same is None else f", identical to the GPU arm's: {same}")
+                          + f"), then {n_done} of head 0's {nt} q tiles fwd+bwd in numpy float32 "
+                          f"block-gather form ({t_attn:.1f} s)",
+                "same_selection_as_gpu": same, "sample_pair_density": float(dense.sum() / nt / nt),
+                "stats_ms": t_stats * 1e3, "selection_ms_per_head": t_sel * 1e3,
+                "ms_per_layer_extrapolated": layer_ms}
 
 
 # ------------------------------------------------------------------ main
@@ -523,21 +559,31 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
+        import torch
+        dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+        # the GPU arm's inputs (torch's seeded generator on the device; data generation
+        # only, nothing of prism_b200 runs in this arm), copied to the host once
+        inp, S = make_layer_inputs(dev)
+        sample = CpuLayerSample(inp, S)
+        del inp
         steps = []
-        cpu = None
         for i in range(args.warmup + args.steps):
-            r = cpu_baseline(seconds=8.0)
+            r = sample.run(seconds=6.0)
             if i >= args.warmup:
                 steps.append(r)
-            cpu = r
-        val = statistics.mean(s["value"] for s in steps)
+        val = statistics.mean(x["value"] for x in steps)
+        last = steps[-1]
         line = {"impl": "reference", "metric": "bsa_fwd_bwd_effective_tflops", "value": val,
                 "unit": "TFLOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": statistics.mean(s["ms_per_layer_extrapolated"] for s in steps),
+                "ms_per_step": statistics.mean(x["wall_ms"] for x in steps),
+                "step": "one bounded CPU sample of the layer (see cpu_baseline.sample); "
+                        "ms_per_step is its measured wall time",
+                "ms_per_layer_extrapolated": statistics.mean(x["ms_per_layer_extrapolated"] for x in steps),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "f32", "data": "synthetic",
+                "dtype": "f32", "data": "synthetic (the GPU arm's seeded inputs"
+                + ("" if dev.type == "cuda" else "; generated on the CPU here, other values") + ")",
                 "config": dict(CONFIG, grid=list(CONFIG["grid"])),
-                "cpu_baseline": {k: cpu[k] for k in ("kind", "cores", "sample")} | {"value": val, "unit": "TFLOPS"},
+                "cpu_baseline": {k: last[k] for k in ("kind", "cores", "sample")} | {"value": val, "unit": "TFLOPS"},
                 "e2e": {"value": val, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -572,11 +618,14 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    from prism_b200 import ops as _ops
     clk = ClockSampler(local_rank)
     clk.start()
     l0 = _lib.launch_count
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    timer = _ops.KernelTimer() if args.path == "dynamic" else None
+    _ops.set_kernel_timer(timer)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -587,10 +636,12 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    _ops.set_kernel_timer(None)
     clocks = clk.stop()
     launches = (_lib.launch_count - l0) // args.steps
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev)
+    ms_local = e0.elapsed_time(e1) / args.steps
+    kt_step = timer.totals_ms() if timer is not None else None
+    t = torch.tensor([ms_local], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
@@ -598,11 +649,16 @@ def main():
     # FLOPs actually computed (selected tile pairs, all ranks)
     pairs, plan, (q4, k4, v4, norms), executed = selected_pairs(q.detach(), k.detach(), v.detach(),
                                                                 a2v, S, world)
-    pt = torch.tensor([pairs, executed], device=dev, dtype=torch.float64)
+    mine = torch.tensor([pairs, executed, ms_local], device=dev, dtype=torch.float64)
+    every = torch.empty(world, 3, device=dev, dtype=torch.float64)
     if world > 1:
-        dist.all_reduce(pt)
-    total_pairs = float(pt[0].item())
-    total_executed = float(pt[1].item())
+        dist.all_gather_into_tensor(every, mine)
+    else:
+        every.copy_(mine[None])
+    per_rank = {"selected_tile_pairs": [int(x) for x in every[:, 0].tolist()],
+                "ms_per_step": [round(float(x), 3) for x in every[:, 2].tolist()]}
+    total_pairs = float(every[:, 0].sum().item())
+    total_executed = float(every[:, 1].sum().item())
     D = CONFIG["head_dim"]
     flops = (1.0 if infer else FWD_BWD_FACTOR) * 4 * D * 64 * 64 * total_pairs
     tflops = flops / (ms * 1e-3) / 1e12
@@ -610,14 +666,17 @@ def main():
     n_tiles = Tp * Hp * Wp // 64
     density = total_pairs / (CONFIG["heads"] * n_tiles * n_tiles)
 
-    # per-kernel times (rank 0's local heads) for the roofline of the dominant kernel
-    kt = kernel_times(plan, q4, k4, v4)
+    # per-kernel times of this rank's launches: inside the timed steps (CUDA events
+    # around each attention kernel, ops.KernelTimer) and each kernel timed alone
+    kt_iso = kernel_times(plan, q4, k4, v4)
+    kt = {n: kt_step[n] / args.steps for n in kt_step} if kt_step else kt_iso
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except Exception:
         pass
-    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    burst = peaks.get("bf16_tflops") or 1590.0
+    sustained = peaks.get("bf16_tflops_sustained") or 1400.0
     local_pairs = pairs
     # per (q tile, k tile) pair one 64x64xD product is 2*64*64*D FLOPs; the forward
     # computes 2 of them (QK^T, PV), dK/dV 4 (S^T, dP^T, dV, dK), dQ 3 (S, dP, dQ)
@@ -628,12 +687,16 @@ def main():
     traffic = None
     if args.config == "720p" and D == 128 and args.path == "dynamic":
         traffic = TRAFFIC_PER_HEAD_720P[dom] * (CONFIG["heads"] // world)
-    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
-                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": burst,
+                "unit": "TFLOP/s", "frac": achieved / burst, "traffic": traffic,
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 720p layer "
                                   "at 4 heads, scaled by heads per launch" if traffic else None,
-                "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if peaks else "fallback",
-                "kernel_ms": kt}
+                "peak_source": ("MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback"),
+                "frac_of_sustained": achieved / sustained,
+                "timing": "CUDA events around the kernel inside the timed steps" if kt_step
+                          else "the kernel timed alone",
+                "kernel_ms": kt, "kernel_ms_isolated": kt_iso,
+                "kernel_frac_of_burst": {n: algo[n] / (kt[n] * 1e-3) / 1e12 / burst for n in algo}}
 
     # end-to-end through host buffers (pinned), H2D inputs + D2H output and grads
     e2e = None
@@ -713,7 +776,10 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(seconds=12.0)
+        head0 = plan.bits_q[0].cpu().numpy().view("uint32")
+        cpu = CpuLayerSample(inp, S, head0_bits=head0).run(seconds=12.0)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "same_selection_as_gpu",
+                                   "sample_pair_density", "ms_per_layer_extrapolated")}
 
     if rank == 0:
         line = {"metric": "bsa_fwd_effective_tflops" if infer else "bsa_fwd_bwd_effective_tflops",
@@ -725,6 +791,7 @@ def main():
                                global_batch=1, seq_len=S, selected_tile_pairs=int(total_pairs),
                                executed_tile_pairs_dq=int(total_executed), pair_density=density,
                                l2="inputs larger than L2 (q/k/v >= 774 MB each)"),
+                "per_rank": per_rank,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clocks}
         print(json.dumps(line), flush=True)

@@ -55,6 +55,19 @@ int prism_abi_version(void);
  * No counterpart in the reference (Triton kernels have no device-side waits). */
 int prism_device_status(void);
 
+/* TEST ONLY -- proves that the bounded waits return.  Runs the forward kernel
+ * (prism_bsa_fwd, one head, S <= 256 tokens: one CTA) with its producer
+ * issuing no load, and the wait limit shortened to wait_limit_ns (0.1 ms..2 s)
+ * for this launch only (set and restored by stream-ordered writes around it).
+ * The MMA warp's first wait therefore ends at the limit: the kernel sets the
+ * device status (prism_device_status: 102 or 103), releases its tensor memory
+ * and returns with o / lse unwritten.  Synchronises `stream` before returning.
+ * Not for production use; no counterpart in the reference. */
+prism_status_t prism_test_fwd_withheld_load(const void* q, const void* k, const void* v, int64_t S,
+                                            int D, float sm_scale, const uint32_t* bits_q,
+                                            const uint64_t* tile_bits, void* o, float* lse,
+                                            uint64_t wait_limit_ns, cudaStream_t stream);
+
 /* Per-token L2 norm of the audio->video bridge residual, bf16 in/out, fp32
  * accumulation.  Replaces `a2v_bridge_residual.norm(dim=-1)`
  * (hymm/models/modules/wan_video_dit.py:742-744).  dim % 8 == 0. */
@@ -429,7 +442,10 @@ prism_status_t prism_bsa_bwd_dq(const void* q, const void* k, const void* v, con
  *     larger calls return PRISM_ERR_INVALID_ARG;
  *   - it calls no cudaMalloc / cudaFree and no allocating library routine;
  *   - the first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress); make that first call before any stream capture;
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *     The address is cached per device and per CUDA context: a call made
+ *     under another context of the device (or after cudaDeviceReset created a
+ *     new one) looks it up again;
  *   - all calls share the one array: calls whose kernels overlap on the GPU
  *     (different streams, or different host threads) race and must be
  *     serialised by the caller.  The array keeps the last call's contents;

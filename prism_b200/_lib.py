@@ -23,6 +23,7 @@ SIGNATURES = {
     "prism_last_error": (ctypes.c_char_p, []),
     "prism_abi_version": (_I, []),
     "prism_device_status": (_I, []),
+    "prism_test_fwd_withheld_load": (_I, [_P, _P, _P, _I64, _I, _F, _P, _P, _P, _P, ctypes.c_uint64, _P]),
     "prism_token_norms": (_I, [_P, _I64, _I, _P, _P]),
     "prism_zone_stats_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "prism_zone_stats": (_I, [_P, _I, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),

@@ -25,8 +25,8 @@ from typing import Optional, Tuple
 import torch
 
 from . import ops
-from .communications import (all_gather, all_to_all_4D, sp_num_local_real_heads,
-                             sp_pad_heads, sp_pad_num_heads)
+from .communications import (HeadGeometry, ShardGeometry, all_gather, all_to_all_4D,
+                             live_ranks, sp_pad_heads)
 from .bsa_interface import run_bsa_uniform
 from .dynamic_block_attention import run_bsa_dynamic
 from .parallel_states import get_sequence_parallel_state, nccl_info
@@ -48,41 +48,45 @@ def audio_token_norms(a2v_bridge_residual: Optional[torch.Tensor], full_seq_len:
 def _sp_self_attention(q, k, v, num_heads: int, full_seq_len, run_local, idle_local=None):
     """The Ulysses SP branch of SelfAttention.forward (wan_video_dit.py:764-828)
     around a local attention.  q, k, v: [B=1, S_local, num_heads*D].
-    run_local(q4, k4, v4) gets [1, S, h, D] views (bshd) of the local heads and
-    returns (x [1, S, h, D], extra); idle_local() runs on a rank that holds only
-    padding heads, before its output all-to-all (collectives the local
-    attention would have joined).  Returns (x [B, S_local, num_heads*D], extra)."""
+    run_local(q4, k4, v4, ctx) gets [1, S, h, D] views (bshd) of the local heads'
+    receive buffers and returns (x [1, S, h, D], extra); ctx carries
+    ``seq_capacity`` (rows of the exchange buffers: an output stored in such a
+    buffer is sent back without a copy) and ``live_ranks`` (ranks with real
+    heads).  idle_local(ctx) runs on a rank that holds only padding heads, before
+    its output exchange (collectives the local attention would have joined).
+    Returns (x [B, S_local, num_heads*D], extra)."""
     b, s_local, hd = q.shape
     D = hd // num_heads
     q4, k4, v4 = (t.view(b, s_local, num_heads, D) for t in (q, k, v))
     if not get_sequence_parallel_state():
-        x, extra = run_local(q4, k4, v4)
+        x, extra = run_local(q4, k4, v4, {"seq_capacity": None, "live_ranks": None})
         return x.flatten(2), extra
     P = nccl_info.sp_size
     rank = nccl_info.rank_within_spgroup
-    padded = sp_pad_num_heads(num_heads, P)
+    group = nccl_info.sp_group
+    S = int(full_seq_len) if full_seq_len is not None else s_local * P
+    heads = HeadGeometry(P, num_heads)
+    padded = heads.hp * P
     if padded != num_heads:
         q4, k4, v4 = (sp_pad_heads(t, padded) for t in (q4, k4, v4))
-    group = nccl_info.sp_group
-    q4 = all_to_all_4D(q4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
-    k4 = all_to_all_4D(k4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
-    v4 = all_to_all_4D(v4, group, scatter_dim=2, gather_dim=1, full_seq_len=full_seq_len)
-    hpr = q4.shape[2]
-    local = sp_num_local_real_heads(num_heads, padded, P, rank)
+    q4, k4, v4 = (all_to_all_4D(t, group, 2, 1, S) for t in (q4, k4, v4))
+    hpr = heads.hp
+    local = heads.real_on(rank)
+    ctx = {"seq_capacity": P * ShardGeometry(P, S).C, "live_ranks": live_ranks(num_heads, P)}
     extra = None
     if local > 0:
         if local != hpr:
             q4, k4, v4 = q4[:, :, :local], k4[:, :, :local], v4[:, :, :local]
-        x, extra = run_local(q4, k4, v4)
+        x, extra = run_local(q4, k4, v4, ctx)
         if x.shape[2] != hpr:
             x = sp_pad_heads(x, hpr)
     else:
         # padding-only rank: keep the graph connected so the backward
-        # all-to-alls fire symmetrically on every rank (wan_video_dit.py:814-823)
+        # exchanges fire symmetrically on every rank (wan_video_dit.py:814-823)
         if idle_local is not None:
-            idle_local()
+            idle_local(ctx)
         x = (q4 + k4 + v4) * 0.0
-    x = all_to_all_4D(x, group, scatter_dim=1, gather_dim=2, full_seq_len=full_seq_len)
+    x = all_to_all_4D(x, group, 1, 2, S)
     if padded != num_heads:
         x = x[:, :, :num_heads]
     return x.flatten(2), extra
@@ -105,16 +109,20 @@ def dynamic_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
               tau_128=tau_128, lambda_128=lambda_128, shape_ids=shape_ids, return_shape_ids=True,
               audio_token_norms=norms, layout="bshd")
 
-    def idle():
-        # the zone statistics all-reduce must still be joined
+    def idle(ctx):
+        # the zone statistics all-reduce must still be joined (with zeros; the
+        # average divides by the ranks that hold real heads)
         if shape_ids is None:
             from .dynamic_block_shape import _maybe_sp_average
             Tp, Hp, Wp = ops.padded_grid(grid_size)
             Nz = (Tp // 8) * (Hp // 8) * (Wp // 8)
-            _maybe_sp_average(torch.zeros(Nz, 25 * D, device=q.device))
+            _maybe_sp_average(torch.zeros(Nz, 25 * D, device=q.device), live_ranks=ctx["live_ranks"])
 
-    x, used = _sp_self_attention(q, k, v, num_heads, full_seq_len,
-                                 lambda a, b_, c: run_bsa_dynamic(a, b_, c, grid_size, **kw), idle)
+    def local(a, b_, c, ctx):
+        return run_bsa_dynamic(a, b_, c, grid_size, seq_capacity=ctx["seq_capacity"],
+                               sp_live_ranks=ctx["live_ranks"], **kw)
+
+    x, used = _sp_self_attention(q, k, v, num_heads, full_seq_len, local, idle)
     used = shape_ids if used is None else used
     if return_shape_ids:
         return x, used
@@ -149,7 +157,7 @@ def uniform_self_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
               variance_boost_gamma=variance_boost_gamma, correction=correction,
               taylor_alpha_f=taylor_alpha_f)
     x, _ = _sp_self_attention(q, k, v, num_heads, full_seq_len,
-                              lambda a, b_, c: (run_bsa_uniform(a, b_, c, grid_size, **kw), None))
+                              lambda a, b_, c, ctx: (run_bsa_uniform(a, b_, c, grid_size, **kw), None))
     return x
 
 

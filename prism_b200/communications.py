@@ -1,190 +1,349 @@
-"""Ulysses sequence-parallel collectives around the attention call.
+"""Ulysses sequence <-> head exchange around the attention call.
 
-Same names, argument meaning and shard bookkeeping as the reference's
-``hymm/utils/communications.py``:
+The reference reshards with ``all_to_all_4D`` / ``all_gather``
+(hymm/utils/communications.py:134-284, 346-413; callers
+wan_video_dit.py:739-787, 824-828).  The public names the DiT imports are kept
+(``all_to_all_4D``, ``all_gather``, ``sp_split``, ``sp_chunk_sizes``,
+``assert_sp_splittable``, ``sp_pad_num_heads``, ``sp_pad_heads``,
+``sp_num_local_real_heads``) with the same argument meaning; the exchange itself
+is built around one buffer layout chosen so that the attention side never copies.
 
-* ``sp_chunk_sizes`` / ``sp_split`` / ``assert_sp_splittable`` (:28-52):
-  ``torch.chunk`` shard sizes, the last rank may be shorter;
-* ``sp_pad_num_heads`` / ``sp_pad_heads`` / ``sp_num_local_real_heads``
-  (:80-110): zero head padding when heads % sp != 0;
-* ``all_to_all_4D`` (:134-284): sequence <-> heads reshard with one
-  ``all_to_all_single`` per call on the current stream, autograd backward =
-  the inverse reshard;
-* ``all_gather`` (:346-413) with locally derived shard sizes.
+Geometry.  A sequence of S tokens is cut into P shards of ``C = ceil(S / P)``
+rows; shard r starts at r * C and the last shard may be shorter (a rank whose
+shard would be empty is an error).  H heads are padded to ``P * hp`` with
+``hp = ceil(H / P)`` heads per rank; rank r owns heads [r * hp, r * hp + hp).
 
-The wire format is the reference's: the send buffer is ``[P, S/P, B, H/P, D]``
-(scatter 2 -> gather 1) or ``[P, H/P, S/P, B, D]`` (scatter 1 -> gather 2), so a
-rank running this module exchanges byte-identical buffers with a rank running
-the reference.  Pack and unpack are single strided copies on the GPU.
+Wire layout.  Both directions exchange ``[P, B, C, hp, D]`` buffers with one
+``all_to_all_single``: block p of a send buffer goes to rank p.
+* heads side: block p of rank r's buffer holds tokens [p * C, p * C + C) of
+  r's hp heads.  With B = 1 the whole buffer is ``[P * C, hp, D]`` - the full
+  sequence of r's heads, token-major - so the attention reads a receive buffer
+  in place (``[1, S, hp, D]`` view, no unpack) and its output, written into a
+  buffer of P * C rows (``seq_capacity``), is sent as it is (no pack).
+* sequence side: block p holds this rank's C rows of heads [p * hp, p * hp + hp).
+  Going there from the token-major ``[B, S_local, H, D]`` activations (and back)
+  is one strided copy, the only copy per exchange; the fused layer
+  (prism_b200.producer) removes it as well by writing and reading this layout
+  directly.  Rows past a short last shard travel as filler and are dropped.
+
+Everything runs on the current CUDA stream (NCCL) or on CPU tensors (gloo).
+Collectives carry no timeout handling of their own: a rank that misses one makes
+its peers fail through the process group's timeout, not hang silently.
 """
 from __future__ import annotations
 
-from typing import Any, List, Optional
+from dataclasses import dataclass
+from typing import List, Optional
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
+
+
+# ----------------------------------------------------------------- geometry
+@dataclass(frozen=True)
+class ShardGeometry:
+    """P shards of a sequence of S tokens, C = ceil(S / P) rows each (last shorter)."""
+
+    P: int
+    S: int
+
+    @property
+    def C(self) -> int:
+        return -(-self.S // self.P)
+
+    def start(self, r: int) -> int:
+        return min(r * self.C, self.S)
+
+    def rows(self, r: int) -> int:
+        return max(0, min(self.C, self.S - r * self.C))
+
+
+@dataclass(frozen=True)
+class HeadGeometry:
+    """H real heads over P ranks, hp = ceil(H / P) per rank (tail heads are padding)."""
+
+    P: int
+    H: int
+
+    @property
+    def hp(self) -> int:
+        return -(-self.H // self.P)
+
+    def real_on(self, r: int) -> int:
+        return max(0, min(self.hp, self.H - r * self.hp))
 
 
 def sp_chunk_sizes(total: int, world_size: int) -> List[int]:
-    chunk = (total + world_size - 1) // world_size
-    return [min(chunk, max(total - i * chunk, 0)) for i in range(world_size)]
+    """Shard lengths of a sequence of ``total`` tokens over ``world_size`` ranks."""
+    g = ShardGeometry(int(world_size), int(total))
+    return [g.rows(r) for r in range(g.P)]
 
 
 def assert_sp_splittable(total: int, world_size: int, name: str = "sequence"):
-    if world_size <= 1:
-        return
-    sizes = sp_chunk_sizes(total, world_size)
-    assert sizes[-1] > 0, (
-        f"{name} length {total} is too short for sp_size={world_size}: the trailing SP rank(s) "
-        f"would receive zero tokens.")
+    """Every rank must receive at least one token (an empty shard cannot join the exchange)."""
+    if world_size > 1:
+        g = ShardGeometry(int(world_size), int(total))
+        assert g.rows(g.P - 1) > 0, (
+            f"{name}: {total} tokens over {world_size} SP ranks leaves rank {world_size - 1} "
+            f"without tokens (shards of {g.C})")
 
 
 def sp_split(x: torch.Tensor, world_size: int, rank: int, dim: int) -> torch.Tensor:
+    """This rank's shard of ``x`` along ``dim`` (a view)."""
     if world_size <= 1:
         return x
-    sizes = sp_chunk_sizes(x.shape[dim], world_size)
-    return torch.split(x, sizes, dim=dim)[rank]
+    g = ShardGeometry(int(world_size), x.shape[dim])
+    return x.narrow(dim, g.start(rank), g.rows(rank))
 
 
 def sp_pad_num_heads(num_heads: int, sp_size: int) -> int:
-    r = num_heads % sp_size
-    return num_heads if r == 0 else num_heads + (sp_size - r)
+    """Head count after padding to a multiple of the SP size."""
+    g = HeadGeometry(int(sp_size), int(num_heads))
+    return g.hp * g.P
 
 
 def sp_pad_heads(x: torch.Tensor, padded_heads: int, dim: int = 2) -> torch.Tensor:
-    cur = x.shape[dim]
-    if cur >= padded_heads:
+    """Zero heads appended along ``dim`` up to ``padded_heads``."""
+    n = x.shape[dim]
+    if n >= padded_heads:
         return x
     shape = list(x.shape)
-    shape[dim] = padded_heads - cur
-    return torch.cat([x, x.new_zeros(shape)], dim=dim)
+    shape[dim] = padded_heads
+    out = x.new_zeros(shape)
+    out.narrow(dim, 0, n).copy_(x)
+    return out
 
 
-def sp_num_local_real_heads(num_real_heads: int, padded_heads: int, sp_size: int, sp_rank: int) -> int:
-    hpr = padded_heads // sp_size
-    return max(0, min(num_real_heads - sp_rank * hpr, hpr))
+def sp_num_local_real_heads(num_real_heads: int, padded_heads: int, sp_size: int,
+                            sp_rank: int) -> int:
+    """Real (non-padding) heads among the ``padded_heads / sp_size`` heads of ``sp_rank``."""
+    hp = padded_heads // sp_size
+    return max(0, min(hp, num_real_heads - sp_rank * hp))
 
 
-def _all_to_all_4D(input: torch.Tensor, scatter_idx: int = 2, gather_idx: int = 1, group=None,
-                   full_seq_len: Optional[int] = None) -> torch.Tensor:
-    assert input.dim() == 4, f"input must be 4D tensor, got {input.dim()}"
-    P = dist.get_world_size(group)
-    rank = dist.get_group_rank(group, dist.get_rank())
-    if scatter_idx == 2 and gather_idx == 1:
-        # (bs, S/P, hc, hs) -> (bs, S, hc/P, hs)
-        if full_seq_len is not None:
-            sizes = sp_chunk_sizes(int(full_seq_len), P)
-        else:
-            sizes = [None] * P
-            dist.all_gather_object(sizes, input.shape[1], group)
-        gap = sizes[0] - sizes[-1]
-        if gap > 0 and rank == P - 1:
-            input = F.pad(input, (0, 0, 0, 0, 0, gap))
-        bs, shard, hc, hs = input.shape
-        assert hc % P == 0, f"Invalid Head size: {hc}, which should be divisible by spsize {P}"
-        shc = hc // P
-        send = input.reshape(bs, shard, P, shc, hs).permute(2, 1, 0, 3, 4).contiguous()
-        if P > 1:
-            recv = torch.empty_like(send)
-            dist.all_to_all_single(recv, send, group=group)
-        else:
-            recv = send
-        out = recv.reshape(P * shard, bs, shc, hs).transpose(0, 1).contiguous()
-        if gap > 0:
-            out = out[:, : P * shard - gap]
-        return out
-    if scatter_idx == 1 and gather_idx == 2:
-        # (bs, S, hc/P, hs) -> (bs, S/P, hc, hs)
-        bs, S, shc, hs = input.shape
-        hc = shc * P
-        gap = 0
-        if S % P != 0:
-            gap = (S // P + 1) * P - S
-            input = F.pad(input, (0, 0, 0, 0, 0, gap))
-            S = S + gap
-        shard = S // P
-        send = input.reshape(bs, P, shard, shc, hs).permute(1, 3, 2, 0, 4).contiguous()
-        if P > 1:
-            recv = torch.empty_like(send)
-            dist.all_to_all_single(recv, send, group=group)
-        else:
-            recv = send
-        out = recv.reshape(hc, shard, bs, hs).permute(2, 1, 0, 3).contiguous()
-        if gap > 0 and rank == P - 1:
-            out = out[:, :-gap]
-        return out
-    raise RuntimeError("scatter_idx must be 1 or 2 and gather_idx must be 1 or 2")
+def live_ranks(num_real_heads: int, sp_size: int) -> int:
+    """Ranks that hold at least one real head."""
+    g = HeadGeometry(int(sp_size), int(num_real_heads))
+    return sum(1 for r in range(g.P) if g.real_on(r) > 0)
 
 
-class SeqAllToAll4D(torch.autograd.Function):
+# ------------------------------------------------------------ group helpers
+def _group_info(group):
+    return dist.get_world_size(group), dist.get_group_rank(group, dist.get_rank())
+
+
+def _negotiate_length(local: int, P: int, group, device) -> int:
+    """Full sequence length from every rank's shard length; the shards must follow
+    ShardGeometry (the wire layout assumes it)."""
+    mine = torch.tensor([int(local)], dtype=torch.int64, device=device)
+    every = torch.empty(P, dtype=torch.int64, device=device)
+    dist.all_gather_into_tensor(every, mine, group=group)
+    lens = [int(x) for x in every.tolist()]
+    S = sum(lens)
+    if lens != sp_chunk_sizes(S, P):
+        raise ValueError(f"shard lengths {lens} are not the ceil(S/P) split of {S} tokens")
+    return S
+
+
+def _exchange(send: torch.Tensor, group, P: int) -> torch.Tensor:
+    """One all_to_all_single over dim 0 of a contiguous [P, ...] buffer."""
+    if P == 1:
+        return send
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv
+
+
+# ------------------------------------------------------ layout conversions
+def _seq_to_wire(x: torch.Tensor, P: int, C: int, hp: int) -> torch.Tensor:
+    """[B, S_local, P*hp, D] (token-major) -> contiguous wire [P, B, C, hp, D]."""
+    B, n, Hp, D = x.shape
+    wire = x.new_empty(P, B, C, hp, D)
+    wire[:, :, :n].copy_(x.unflatten(2, (P, hp)).permute(2, 0, 1, 3, 4))
+    if n < C:
+        wire[:, :, n:].zero_()
+    return wire
+
+
+def _wire_to_seq(wire: torch.Tensor, n: int) -> torch.Tensor:
+    """Wire [P, B, C, hp, D] -> [B, n, P*hp, D] (this rank's first n rows)."""
+    P, B, C, hp, D = wire.shape
+    out = wire.new_empty(B, n, P, hp, D)
+    out.copy_(wire[:, :, :n].permute(1, 2, 0, 3, 4))
+    return out.view(B, n, P * hp, D)
+
+
+def _heads_as_wire(x: torch.Tensor, P: int, C: int) -> Optional[torch.Tensor]:
+    """A [1, S, hp, D] token-major tensor whose storage extends to P*C rows, viewed
+    as the wire [P, 1, C, hp, D] without a copy (None if it does not qualify).
+    The rows past S are filler: the receiver of that block drops them."""
+    B, S, hp, D = x.shape
+    if B != 1 or not x[0].is_contiguous():
+        return None
+    need = (x.storage_offset() + P * C * hp * D) * x.element_size()
+    if x.untyped_storage().nbytes() < need:
+        return None
+    return x.as_strided((P, 1, C, hp, D), (C * hp * D, P * C * hp * D, hp * D, D, 1),
+                        x.storage_offset())
+
+
+def _heads_to_wire(x: torch.Tensor, P: int, C: int) -> torch.Tensor:
+    """[B, S, hp, D] (full sequence of this rank's heads) -> wire [P, B, C, hp, D]
+    (a view of x when _heads_as_wire qualifies it, else one copy)."""
+    w = _heads_as_wire(x, P, C)
+    if w is not None:
+        return w
+    B, S, hp, D = x.shape
+    full = x.new_empty(B, P * C, hp, D)
+    full[:, :S].copy_(x)
+    if S < P * C:
+        full[:, S:].zero_()
+    return full.view(B, P, C, hp, D).permute(1, 0, 2, 3, 4)
+
+
+def _wire_to_heads(wire: torch.Tensor, S: int) -> torch.Tensor:
+    """Wire [P, B, C, hp, D] -> [B, S, hp, D]: a view for B = 1."""
+    P, B, C, hp, D = wire.shape
+    if B == 1:
+        return wire.view(1, P * C, hp, D)[:, :S]
+    return wire.permute(1, 0, 2, 3, 4).reshape(B, P * C, hp, D)[:, :S]
+
+
+# ------------------------------------------------------- autograd functions
+def _seq_to_heads(x, group, S):
+    P, r = _group_info(group)
+    g = ShardGeometry(P, S)
+    B, n, Hp, D = x.shape
+    if Hp % P:
+        raise ValueError(f"{Hp} heads do not split over {P} SP ranks; pad them first (sp_pad_heads)")
+    if n != g.rows(r):
+        raise ValueError(f"rank {r} holds {n} tokens, the split of {S} over {P} gives {g.rows(r)}")
+    recv = _exchange(_seq_to_wire(x, P, g.C, Hp // P), group, P)
+    return _wire_to_heads(recv, S)
+
+
+def _heads_to_seq(x, group, S):
+    P, r = _group_info(group)
+    g = ShardGeometry(P, S)
+    if x.shape[1] != S:
+        raise ValueError(f"expected the full sequence of {S} tokens, got {x.shape[1]}")
+    recv = _exchange(_heads_to_wire(x, P, g.C).contiguous(), group, P)
+    return _wire_to_seq(recv, g.rows(r))
+
+
+class SeqToHeads(torch.autograd.Function):
+    """[B, S_local, H, D] -> [B, S, H/P, D]; the backward is the inverse exchange."""
+
     @staticmethod
-    def forward(ctx: Any, group, input, scatter_idx, gather_idx, full_seq_len=None):
-        ctx.group = group
-        ctx.scatter_idx = scatter_idx
-        ctx.gather_idx = gather_idx
-        ctx.full_seq_len = full_seq_len
-        return _all_to_all_4D(input, scatter_idx, gather_idx, group=group, full_seq_len=full_seq_len)
+    def forward(ctx, x, group, S):
+        ctx.group, ctx.S = group, S
+        return _seq_to_heads(x, group, S)
 
     @staticmethod
-    def backward(ctx: Any, *grad_output):
-        return (None,
-                SeqAllToAll4D.apply(ctx.group, *grad_output, ctx.gather_idx, ctx.scatter_idx,
-                                    ctx.full_seq_len),
-                None, None, None)
+    def backward(ctx, g):
+        return _heads_to_seq(g, ctx.group, ctx.S), None, None
+
+
+class HeadsToSeq(torch.autograd.Function):
+    """[B, S, H/P, D] -> [B, S_local, H, D]; the backward is the inverse exchange."""
+
+    @staticmethod
+    def forward(ctx, x, group, S):
+        ctx.group, ctx.S = group, S
+        return _heads_to_seq(x, group, S)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _seq_to_heads(g, ctx.group, ctx.S), None, None
+
+
+class WireToHeads(torch.autograd.Function):
+    """A sequence-side wire buffer [P, B, C, hp, D] that a producer wrote directly
+    (prism_norm_rope_pack) -> exchange -> [B, S, hp, D] (a view of the receive
+    buffer for B = 1).  Backward: the heads-side gradient is sent back (without a
+    copy when it lives in a buffer of P * C rows) and arrives as the wire's gradient."""
+
+    @staticmethod
+    def forward(ctx, wire, group, S):
+        P, _ = _group_info(group)
+        ctx.group, ctx.P, ctx.C = group, P, wire.shape[2]
+        return _wire_to_heads(_exchange(wire.contiguous(), group, P), S)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _exchange(_heads_to_wire(g, ctx.P, ctx.C).contiguous(), ctx.group, ctx.P), None, None
+
+
+class HeadsToWire(torch.autograd.Function):
+    """[B, S, hp, D] -> exchange -> the sequence-side receive buffer [P, B, C, hp, D]
+    for a consumer that reads that layout directly (the K-split output projection).
+    The input is sent without a copy when it lives in a buffer of P * C rows."""
+
+    @staticmethod
+    def forward(ctx, x, group, S):
+        P, _ = _group_info(group)
+        C = ShardGeometry(P, S).C
+        ctx.group, ctx.P, ctx.S = group, P, S
+        return _exchange(_heads_to_wire(x, P, C).contiguous(), group, P)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _wire_to_heads(_exchange(g.contiguous(), ctx.group, ctx.P), ctx.S), None, None
 
 
 def all_to_all_4D(input_: torch.Tensor, group, scatter_dim: int = 2, gather_dim: int = 1,
                   full_seq_len: Optional[int] = None):
-    return SeqAllToAll4D.apply(group, input_, scatter_dim, gather_dim, full_seq_len)
+    """scatter_dim=2, gather_dim=1: [B, S/P, H, D] -> [B, S, H/P, D] (sequence to heads);
+    scatter_dim=1, gather_dim=2: the inverse.  ``full_seq_len`` is S (negotiated over
+    the group when None).  Differentiable; the result of the forward direction is a
+    view of the receive buffer."""
+    if input_.dim() != 4:
+        raise ValueError(f"all_to_all_4D expects a 4D tensor, got {input_.dim()}D")
+    P, _ = _group_info(group)
+    if (scatter_dim, gather_dim) == (2, 1):
+        S = full_seq_len if full_seq_len is not None else _negotiate_length(
+            input_.shape[1], P, group, input_.device)
+        return SeqToHeads.apply(input_, group, int(S))
+    if (scatter_dim, gather_dim) == (1, 2):
+        S = input_.shape[1] if full_seq_len is None else int(full_seq_len)
+        return HeadsToSeq.apply(input_, group, int(S))
+    raise ValueError("all_to_all_4D supports (scatter_dim, gather_dim) = (2, 1) or (1, 2)")
 
 
-class _AllGather(torch.autograd.Function):
+class _GatherSequence(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, input_, dim, group, full_seq_len=None):
-        world = dist.get_world_size(group)
-        rank = dist.get_group_rank(group, dist.get_rank())
-        if full_seq_len is not None:
-            sizes = sp_chunk_sizes(int(full_seq_len), world)
+    def forward(ctx, x, dim, group, S):
+        P, r = _group_info(group)
+        g = ShardGeometry(P, S)
+        if x.shape[dim] != g.rows(r):
+            raise ValueError(f"rank {r} holds {x.shape[dim]} rows, the split of {S} gives {g.rows(r)}")
+        ctx.dim, ctx.start, ctx.rows = dim, g.start(r), g.rows(r)
+        front = x.movedim(dim, 0)
+        slab = front.new_zeros((g.C,) + tuple(front.shape[1:]))
+        slab[: g.rows(r)].copy_(front)
+        full = slab.new_empty((P * g.C,) + tuple(slab.shape[1:]))
+        if P > 1:
+            dist.all_gather_into_tensor(full, slab, group=group)
         else:
-            shapes = [None] * world
-            dist.all_gather_object(shapes, input_.shape[dim], group)
-            sizes = [int(s) for s in shapes]
-        ctx.dim, ctx.group, ctx.sizes, ctx.rank = dim, group, sizes, rank
-        input_ = input_.contiguous()
-        if all(s == sizes[0] for s in sizes):
-            if dim == 0:
-                shape = list(input_.shape)
-                shape[0] = sizes[0] * world
-                flat = torch.empty(shape, dtype=input_.dtype, device=input_.device)
-                dist.all_gather_into_tensor(flat, input_, group=group)
-                return flat
-            lst = [torch.empty_like(input_) for _ in range(world)]
-            dist.all_gather(lst, input_, group=group)
-            return torch.cat(lst, dim=dim)
-        # ragged shards: pad to the largest shard, one uniform all-gather, slice
-        # (the reference issues a ragged dist.all_gather, i.e. one broadcast per rank)
-        mx = max(sizes)
-        pad = mx - input_.shape[dim]
-        if pad > 0:
-            shape = list(input_.shape)
-            shape[dim] = pad
-            input_ = torch.cat([input_, input_.new_zeros(shape)], dim=dim)
-        lst = [torch.empty_like(input_) for _ in range(world)]
-        dist.all_gather(lst, input_, group=group)
-        return torch.cat([t.narrow(dim, 0, s) for t, s in zip(lst, sizes)], dim=dim)
+            full.copy_(slab)
+        return full[:S].movedim(0, dim)
 
     @staticmethod
-    def backward(ctx, grad_output):
-        g = torch.split(grad_output, ctx.sizes, dim=ctx.dim)[ctx.rank]
-        return g.contiguous(), None, None, None
+    def backward(ctx, grad):
+        return grad.narrow(ctx.dim, ctx.start, ctx.rows), None, None, None
 
 
 def all_gather(input_: torch.Tensor, dim: int = 1, group=None, full_seq_len: Optional[int] = None):
-    return _AllGather.apply(input_, dim, group, full_seq_len)
+    """Concatenate every rank's shard along ``dim`` (shards follow ShardGeometry; S is
+    negotiated when ``full_seq_len`` is None).  The backward keeps this rank's rows."""
+    P, _ = _group_info(group)
+    S = full_seq_len if full_seq_len is not None else _negotiate_length(
+        input_.shape[dim], P, group, input_.device)
+    return _GatherSequence.apply(input_, dim, group, int(S))
 
 
 __all__ = [
-    "sp_chunk_sizes", "assert_sp_splittable", "sp_split", "sp_pad_num_heads", "sp_pad_heads",
-    "sp_num_local_real_heads", "all_to_all_4D", "SeqAllToAll4D", "all_gather",
+    "ShardGeometry", "HeadGeometry", "sp_chunk_sizes", "assert_sp_splittable", "sp_split",
+    "sp_pad_num_heads", "sp_pad_heads", "sp_num_local_real_heads", "live_ranks", "all_to_all_4D",
+    "SeqToHeads", "HeadsToSeq", "WireToHeads", "HeadsToWire", "all_gather",
 ]

@@ -11,10 +11,10 @@
 //             groups (FwdSched): S = Q K^T -> TMEM, online softmax in
 //             registers (one thread per query row), P (bf16) written over S in
 //             TMEM, O += P V with P read from TMEM.
-//   dK / dV   CTA = 128 keys (tiles 2p, 2p+1); per step one query tile (N = 64)
-//             of the union of the two key tiles' transposed rows: S^T = K Q^T,
-//             dP^T = V dO^T -> TMEM, P^T and dS^T written over them in TMEM,
-//             dV += P^T dO, dK += dS^T Q.
+//   dK / dV   CTA = 128 keys (tiles 2p, 2p+1); per step two query tiles (N =
+//             128) of the union of the two key tiles' transposed rows:
+//             S^T = K Q^T, dP^T = V dO^T -> TMEM, P^T and dS^T written over
+//             them in TMEM, dV += P^T dO, dK += dS^T Q.
 //   dQ        CTA = 128 queries (tiles 2p, 2p+1); per step a pair of key tiles
 //             of the union of the two rows: S, dP -> TMEM, dS -> TMEM,
 //             dQ += dS K.
@@ -373,7 +373,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                   const uint32_t* __restrict__ bits_q, const uint64_t* __restrict__ tile_bits,
                   __nv_bfloat16* __restrict__ o, __nv_bfloat16* __restrict__ o_lo,
                   float* __restrict__ lse, const float* __restrict__ key_bias = nullptr,
-                  int64_t tb_hstride = 0, int64_t tb_qstride = 0) {
+                  int64_t tb_hstride = 0, int64_t tb_qstride = 0, int test_withhold = 0) {
+  // test_withhold != 0 (prism_test_fwd_withheld_load only): the producer issues no
+  // load at all, so the first wait of the MMA warp can only end at the wait limit
   using L = FwdLayout<D>;
   constexpr int R = L::kRing;
   extern __shared__ uint8_t smem_raw[];
@@ -416,7 +418,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tc_fence_before();
   }
   __syncthreads();  // barrier initialisation visible: the Q load overlaps the list build
-  if (warp == kFwdProducerWarp && lane == 0) {
+  if (warp == kFwdProducerWarp && lane == 0 && !test_withhold) {
     const int nq = g1_live ? 4 : 2;  // 64-row Q blocks
     mbar_expect_tx(bar(L::B_Q), nq * 64 * D * 2);
     for (int qb = 0; qb < nq; ++qb)
@@ -436,7 +438,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (warp == kFwdProducerWarp) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    if (lane == 0 && !test_withhold) {
       int np = 0, t0, t1, mask;
       bool ok = true;
       for (int step = 0; step < sched.total; ++step) {
@@ -838,280 +840,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == kFwdMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ================================================================== dK / dV
-// CTA = 128 keys (tiles 2p, 2p+1); per step one query tile of the transposed
-// selection (N = 64), with S^T and dP^T double-buffered in TMEM so that the
-// softmax of step n overlaps the products of steps n-1 and n+1.  The softmax
-// warpgroups (wg 0: query columns 0-31, wg 1: 32-63) write P^T and
-// dS^T = P^T (dP^T - delta) as bf16 over the S^T / dP^T columns they have
-// read, and dV += P^T dO, dK += dS^T Q take them from TMEM (TS form: only dO /
-// Q are read from shared memory).  TMEM is full (dK, dV: 2 x 128 columns;
-// S^T, dP^T: 2 x 2 x 64), which is what fixes N = 64 here.
-template <int D>
-struct DkdvLayout {
-  static constexpr int kRing = 4;
-  static constexpr int kSub = D / 64;
-  static constexpr int K = 0;                              // 128 keys
-  static constexpr int V = K + kSub * 16384;
-  static constexpr int Q = V + kSub * 16384;               // kRing x 64 queries
-  static constexpr int DO = Q + kRing * kSub * 8192;
-  static constexpr int M = DO + kRing * kSub * 8192;       // kRing x 64 f32 (lse)
-  static constexpr int DL = M + kRing * 256;               // kRing x 64 f32 (delta)
-  static constexpr int BAR = DL + kRing * 256;
-  static constexpr int B_KV = 0, B_QF = 1, B_QE = 1 + kRing, B_SF = 1 + 2 * kRing,  // [b]
-                       B_DPF = B_SF + 2, B_DSF = B_DPF + 2,                         // [b]
-                       B_FIN = B_DSF + 2, B_DRAIN = B_FIN + 1, NBAR = B_DRAIN + 1;
-  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
-  static constexpr int ABORT = TMEM_SLOT + 4;
-  static constexpr size_t kBytes = 1024 + ABORT + 4;
-  // TMEM: dK, dV (D f32 columns each), S^T[b], dP^T[b] (64 f32 columns each;
-  // the bf16 P^T / dS^T of query columns [32 w, 32 w + 32) over columns
-  // [32 w, 32 w + 16) of them)
-  static constexpr int T_DK = 0, T_DV = 128, T_S = 256, T_DP = 384;
-};
-
-template <int D>
-__global__ void __launch_bounds__(kBwdThreads, 1)
-    dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                   const float* __restrict__ lse, const float* __restrict__ delta, int64_t Sq, int64_t Sk,
-                   int wq, float qk_scale, float sm_scale, const uint32_t* __restrict__ bits_k,
-                   const uint64_t* __restrict__ tile_bits, __nv_bfloat16* __restrict__ dk,
-                   __nv_bfloat16* __restrict__ dv) {
-  using L = DkdvLayout<D>;
-  constexpr int R = L::kRing;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = align1024(smem_raw);
-  const uint32_t sb = smem_u32(sm);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pair = blockIdx.x, h = blockIdx.y;
-  // keys: tile pair `pair` of Sk rows per head (rows of bits_k); queries: Sq rows per
-  // head, wq = words per bits_k row (ceil(Sq / 2048))
-  const int64_t n_tiles = Sk / 64;
-  const int row_base = (int)((int64_t)h * Sk + (int64_t)pair * 128);  // key rows of this CTA
-  const int head_row = (int)((int64_t)h * Sq);                        // query rows of head h
-  auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
-  const uint32_t* row_a = bits_k + ((int64_t)h * n_tiles + 2 * (int64_t)pair) * wq;
-  const uint32_t* row_b = row_a + wq;
-
-  if (threadIdx.x == 0) {
-    mbar_init(bar(L::B_KV), 1);
-    for (int i = 0; i < R; ++i) {
-      mbar_init(bar(L::B_QF + i), 1);
-      mbar_init(bar(L::B_QE + i), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(L::B_SF + i), 1);
-      mbar_init(bar(L::B_DPF + i), 1);
-      mbar_init(bar(L::B_DSF + i), 8);
-    }
-    mbar_init(bar(L::B_FIN), 1);
-    mbar_init(bar(L::B_DRAIN), 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == kBwdMmaWarp) {
-    tmem_alloc(sb + L::TMEM_SLOT, 512);
-    tmem_relinquish();
-    tc_fence_before();
-  }
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
-
-  if (warp == kBwdProducerWarp) {
-    if (lane == 0) {
-      mbar_expect_tx(bar(L::B_KV), 2 * 128 * D * 2);
-#pragma unroll
-      for (int s = 0; s < L::kSub; ++s)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          tma_load_2d(sb + L::K + s * 16384 + r * 8192, &tm_k, s * 64, row_base + r * 64, bar(L::B_KV));
-          tma_load_2d(sb + L::V + s * 16384 + r * 8192, &tm_v, s * 64, row_base + r * 64, bar(L::B_KV));
-        }
-      UnionIter it;
-      it.init(row_a, row_b, wq);
-      int n = 0, sel = 0, t;
-      while ((t = it.next(sel)) >= 0) {
-        const int st = n % R;
-        if (n >= R && !mbar_wait(bar(L::B_QE + st), ((n / R) - 1) & 1, abort_flag, &g_tc_error,
-                                 kErrDkdvProducer))
-          break;
-        mbar_expect_tx(bar(L::B_QF + st), 2 * 64 * D * 2 + 2 * 256);
-#pragma unroll
-        for (int s = 0; s < L::kSub; ++s) {
-          tma_load_2d(sb + L::Q + st * L::kSub * 8192 + s * 8192, &tm_q, s * 64, head_row + t * 64,
-                      bar(L::B_QF + st));
-          tma_load_2d(sb + L::DO + st * L::kSub * 8192 + s * 8192, &tm_do, s * 64, head_row + t * 64,
-                      bar(L::B_QF + st));
-        }
-        bulk_load(sb + L::M + st * 256, lse + head_row + (int64_t)t * 64, 256, bar(L::B_QF + st));
-        bulk_load(sb + L::DL + st * 256, delta + head_row + (int64_t)t * 64, 256, bar(L::B_QF + st));
-        ++n;
-      }
-      for (int m = (n > R ? n - R : 0); m < n; ++m)
-        mbar_wait(bar(L::B_QF + m % R), (m / R) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
-      mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
-    }
-  } else if (warp == kBwdMmaWarp) {
-    // Issue order: S^T(0) dP^T(0) | S^T(1) dP^T(1) dV(0) dK(0) | S^T(2) ...
-    // S^T(n+2) / dP^T(n+2) overwrite the P^T / dS^T of step n; they are issued
-    // after dV(n) / dK(n), and one thread's MMAs are performed in order.
-    // The issuing thread keeps its loop minimal -- the tensor pipe's issue queue
-    // is shallow, so every instruction between MMAs is time the pipe may idle:
-    // it needs no tile indices (only the step count and ring slots), and waits
-    // once per step for P^T and dS^T together (B_DSF).
-    if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_bf16(128, 64, false, false);
-      constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);
-      static_assert(R == 4, "ring arithmetic below assumes 4 slots");
-      const uint64_t dK = desc_k_sw128(sb + L::K), dV = desc_k_sw128(sb + L::V),
-                     dQk = desc_k_sw128(sb + L::Q), dDOk = desc_k_sw128(sb + L::DO),
-                     dQmn = desc_mn_sw128(sb + L::Q, 8192), dDOmn = desc_mn_sw128(sb + L::DO, 8192);
-      constexpr uint32_t kSlot = L::kSub * 8192 >> 4;  // descriptor step of one ring slot
-      const int steps = union_count(row_a, row_b, wq);
-      bool ok = mbar_wait(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
-      tc_fence_after();
-      for (int n = 0; ok && n <= steps; ++n) {
-        if (n < steps) {
-          const uint32_t st = (uint32_t)n & 3u, b = (uint32_t)n & 1u;
-          if (!mbar_wait(bar(L::B_QF + st), ((uint32_t)n >> 2) & 1u, abort_flag, &g_tc_error,
-                         kErrDkdvMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          mma_kd<L::kSub, 16384, 8192>(tmem + L::T_S + b * 64, dK, dQk + st * kSlot, IDESC_S, 0u);
-          mma_commit(bar(L::B_SF + b));
-          mma_kd<L::kSub, 16384, 8192>(tmem + L::T_DP + b * 64, dV, dDOk + st * kSlot, IDESC_S, 0u);
-          mma_commit(bar(L::B_DPF + b));
-        }
-        if (n >= 1) {
-          // dV(j) += P^T(j) dO(j), dK(j) += dS^T(j) Q(j) for the previous step j
-          const uint32_t j = (uint32_t)n - 1u, jb = j & 1u, js = j & 3u;
-          if (!mbar_wait(bar(L::B_DSF + jb), (j >> 1) & 1u, abort_flag, &g_tc_error, kErrDkdvMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S + jb * 64,
-                                                  dDOmn + js * kSlot, IDESC_G, j > 0 ? 1u : 0u);
-          mma_ts_chain4<8, 32, 40, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP + jb * 64,
-                                                  dQmn + js * kSlot, IDESC_G, j > 0 ? 1u : 0u);
-          mma_commit(bar(L::B_QE + js));
-        }
-      }
-      mma_commit(bar(L::B_FIN));
-      mma_commit(bar(L::B_DRAIN));
-      mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
-    }
-  } else {
-    // softmax warpgroups: wg 0 takes query columns 0-31 of each step, wg 1 32-63
-    const int wg = warp >> 2;
-    const int r = (warp & 3) * 32 + lane;  // key row within the CTA == TMEM lane
-    const int half = r >> 6;
-    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const bool kvalid = (tile_bits[2 * pair + half] >> (r & 63)) & 1ull;
-    UnionIter it;
-    it.init(row_a, row_b, wq);
-    int n = 0, sel = 0, t;
-    bool ok = true;
-    const float* sM = reinterpret_cast<const float*>(sm + L::M);
-    const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
-    while ((t = it.next(sel)) >= 0) {
-      const int st = n % R, b = n & 1;
-      const bool tile_on = (sel >> half) & 1;  // warp-uniform
-      const bool on = tile_on && kvalid;
-      if (!warp_wait(bar(L::B_QF + st), (n / R) & 1, abort_flag, kErrDkdvSoftmax) ||
-          !warp_wait(bar(L::B_SF + b), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // lse / delta of this warpgroup's 32 query columns: every lane reads the
-      // same 16 bytes at a time (broadcast)
-      const float4* m_st = reinterpret_cast<const float4*>(sM + st * 64 + wg * 32);
-      const float4* d_st = reinterpret_cast<const float4*>(sDl + st * 64 + wg * 32);
-      float p[32];
-      uint32_t pk[16];
-      if (tile_on) {
-        tmem_load<1>(t_lane + L::T_S + b * 64 + wg * 32, p);
-#pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 mv = m_st[c4];
-          const float mm[4] = {mv.x * kRcpLn2, mv.y * kRcpLn2, mv.z * kRcpLn2, mv.w * kRcpLn2};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = 4 * c4 + j;
-            p[c] = on ? ex2(fmaf(p[c], qk_scale, -mm[j])) : 0.0f;
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) pk[c / 2] = pack_bf16(p[c], p[c + 1]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) p[c] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = 0u;
-      }
-      // P^T is published together with dS^T (the MMA issuer waits once, on B_DSF)
-      tmem_st16(t_lane + L::T_S + b * 64 + wg * 32, pk);
-      if (!warp_wait(bar(L::B_DPF + b), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (tile_on) {
-        float dp[32];
-        tmem_load<1>(t_lane + L::T_DP + b * 64 + wg * 32, dp);
-#pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 dv4 = d_st[c4];
-          const int c = 4 * c4;
-          pk[c / 2] = pack_bf16(p[c] * (dp[c] - dv4.x), p[c + 1] * (dp[c + 1] - dv4.y));
-          pk[c / 2 + 1] = pack_bf16(p[c + 2] * (dp[c + 2] - dv4.z), p[c + 3] * (dp[c + 3] - dv4.w));
-        }
-      }
-      tmem_st16(t_lane + L::T_DP + b * 64 + wg * 32, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(L::B_DSF + b));
-      ++n;
-    }
-    // epilogue: wg 0 writes dK (scaled by sm_scale), wg 1 writes dV
-    const int64_t grow = (int64_t)row_base + r;
-    __nv_bfloat16* out = (wg == 0 ? dk : dv) + grow * D;
-    const float scale = wg == 0 ? sm_scale : 1.0f;
-    const int tcol = wg == 0 ? L::T_DK : L::T_DV;
-    if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDkdvSoftmax)) {
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t raw[32], pk2[16];
-        tmem_ld32(t_lane + tcol + c * 32, raw);
-        tmem_wait_ld_dep(raw);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk2[i] = pack_bf16(u2f(raw[2 * i]) * scale, u2f(raw[2 * i + 1]) * scale);
-        uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk2[4 * i], pk2[4 * i + 1], pk2[4 * i + 2], pk2[4 * i + 3]);
-      }
-    } else if (ok && n == 0) {
-      uint4* a = reinterpret_cast<uint4*>(out);
-#pragma unroll
-      for (int i = 0; i < D / 8; ++i) a[i] = make_uint4(0, 0, 0, 0);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kBwdMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -1817,7 +1545,7 @@ prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads
                           int64_t Sk, float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
                           void* o, void* o_lo, float* lse, cudaStream_t stream,
                           const float* key_bias = nullptr, int64_t tb_hstride = 0,
-                          int64_t tb_qstride = 0) {
+                          int64_t tb_qstride = 0, int test_withhold = 0) {
   const int64_t n_tiles = Sq / 64, n_ktiles = Sk / 64;
   const int wq = (int)((n_ktiles + 31) / 32);
   const size_t need = FwdLayout<D>::bytes(n_ktiles);
@@ -1834,7 +1562,7 @@ prism_status_t launch_fwd(const void* q, const void* k, const void* v, int heads
                    "prism_bsa_fwd: smem attribute");
   fwd_tc_kernel<D, kKeyBias><<<dim3((unsigned)((n_tiles + 3) / 4), heads), kFwdThreads, sm, stream>>>(
       mq, mk, mv, Sq, Sk, wq, sm_scale * kRcpLn2, bits_q, tile_bits, (__nv_bfloat16*)o,
-      (__nv_bfloat16*)o_lo, lse, key_bias, tb_hstride, tb_qstride);
+      (__nv_bfloat16*)o_lo, lse, key_bias, tb_hstride, tb_qstride, test_withhold);
   PRISM_CHECK_LAUNCH("prism_bsa_fwd");
   return PRISM_OK;
 }
@@ -1846,29 +1574,6 @@ prism_status_t launch_delta(const void* o, const void* o_lo, const void* dout, i
   delta_kernel<D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(
       (const __nv_bfloat16*)o, (const __nv_bfloat16*)o_lo, (const __nv_bfloat16*)dout, rows, delta);
   PRISM_CHECK_LAUNCH("prism_bsa_bwd_delta");
-  return PRISM_OK;
-}
-
-template <int D>
-prism_status_t launch_dkdv(const void* q, const void* k, const void* v, const void* dout,
-                           const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
-                           float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
-                           void* dk, void* dv, cudaStream_t stream) {
-  const int64_t n_ktiles = Sk / 64;
-  const int wq = (int)((Sq / 64 + 31) / 32);  // words per bits_k row (query tiles)
-  const size_t sm = DkdvLayout<D>::kBytes > kMinSmem ? DkdvLayout<D>::kBytes : kMinSmem;
-  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
-  CUtensorMap mq, mk, mv, mdo;
-  PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mdo, dout, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
-  PRISM_CHECK_CUDA(cudaFuncSetAttribute(dkdv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
-                   "prism_bsa_bwd: smem attribute");
-  dkdv_tc_kernel<D><<<dim3((unsigned)(n_ktiles / 2), heads), kBwdThreads, sm, stream>>>(
-      mq, mk, mv, mdo, lse, delta, Sq, Sk, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
-      (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
-  PRISM_CHECK_LAUNCH("prism_bsa_bwd_dkdv");
   return PRISM_OK;
 }
 
@@ -1982,6 +1687,37 @@ prism_status_t prism_bsa_fwd(const void* q, const void* k, const void* v, int he
   return prism_bsa_fwd_qk(q, k, v, heads, S, S, D, sm_scale, bits_q, tile_bits, o, o_lo, lse, stream);
 }
 
+prism_status_t prism_test_fwd_withheld_load(const void* q, const void* k, const void* v, int64_t S,
+                                            int D, float sm_scale, const uint32_t* bits_q,
+                                            const uint64_t* tile_bits, void* o, float* lse,
+                                            uint64_t wait_limit_ns, cudaStream_t stream) {
+  const int heads = 1;
+  PRISM_CHECK_ARG(q && k && v && bits_q && tile_bits && o && lse, "prism_test_fwd_withheld_load: null pointer");
+  PRISM_ATTN_SHAPE_CHECKS("prism_test_fwd_withheld_load", S, S);
+  PRISM_CHECK_ARG(S <= 256, "prism_test_fwd_withheld_load: S must be at most 256 (one CTA)");
+  PRISM_CHECK_ARG(wait_limit_ns >= 100000ull && wait_limit_ns <= tc::kDefaultWaitLimitNs,
+                  "prism_test_fwd_withheld_load: wait limit must be in [0.1 ms, 2 s]");
+  PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o),
+                  "prism_test_fwd_withheld_load: tensors must be 16-byte aligned");
+  // stream-ordered: the shortened limit is in place for this launch only
+  static const unsigned long long kDefault = tc::kDefaultWaitLimitNs;
+  static thread_local unsigned long long limit;
+  limit = (unsigned long long)wait_limit_ns;
+  PRISM_CHECK_CUDA(cudaMemcpyToSymbolAsync(tc::g_wait_limit_ns, &limit, sizeof(limit), 0,
+                                           cudaMemcpyHostToDevice, stream),
+                   "prism_test_fwd_withheld_load: set wait limit");
+  const prism_status_t st =
+      D == 128 ? tc::launch_fwd<128>(q, k, v, heads, S, S, sm_scale, bits_q, tile_bits, o, nullptr, lse,
+                                     stream, nullptr, 0, 0, 1)
+               : tc::launch_fwd<64>(q, k, v, heads, S, S, sm_scale, bits_q, tile_bits, o, nullptr, lse,
+                                    stream, nullptr, 0, 0, 1);
+  PRISM_CHECK_CUDA(cudaMemcpyToSymbolAsync(tc::g_wait_limit_ns, &kDefault, sizeof(kDefault), 0,
+                                           cudaMemcpyHostToDevice, stream),
+                   "prism_test_fwd_withheld_load: restore wait limit");
+  PRISM_CHECK_CUDA(cudaStreamSynchronize(stream), "prism_test_fwd_withheld_load: synchronize");
+  return st;
+}
+
 size_t prism_bsa_bwd_workspace_bytes(int heads, int64_t S) {
   return (size_t)heads * (size_t)S * sizeof(float);
 }
@@ -2004,13 +1740,8 @@ static prism_status_t bwd_dkdv_qk(const void* q, const void* k, const void* v, c
   PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dk) &&
                       aligned16(dv) && aligned16(lse) && aligned16(delta),
                   "prism_bsa_bwd_dkdv: tensors must be 16-byte aligned");
-#ifndef PRISM_DKDV_N64
   return D == 128 ? tc::launch_dkdv2<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream)
                   : tc::launch_dkdv2<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
-#else
-  return D == 128 ? tc::launch_dkdv<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream)
-                  : tc::launch_dkdv<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
-#endif
 }
 
 static prism_status_t bwd_dq_qk(const void* q, const void* k, const void* v, const void* dout,
@@ -2076,21 +1807,47 @@ prism_status_t prism_bsa_bwd(const void* q, const void* k, const void* v, const 
 // process exits.  Host code cannot use the array's name as a device address
 // (on the host it names a stand-in object), so its real address is looked up
 // with cudaGetSymbolAddress, once per device, with that device current, on
-// the first call made on that device.
+// the first call made on that device (again if the current context changed).
 namespace prism {
 namespace tc {
 static __device__ __align__(256) float g_noalloc_delta[PRISM_BSA_BWD_NOALLOC_MAX_ROWS];
 }  // namespace tc
 
 static std::mutex g_noalloc_mu;
-static float* g_noalloc_addr[128] = {nullptr};
+// Per device: the context the address was looked up under, and the address.
+struct NoallocSlot {
+  CUcontext ctx;
+  float* addr;
+};
+static NoallocSlot g_noalloc_slot[128] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+static CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
 
 static prism_status_t noalloc_scratch(float** out) {
   int dev = -1;
   PRISM_CHECK_CUDA(cudaGetDevice(&dev), "prism_bsa_bwd_noalloc: cudaGetDevice");
   PRISM_CHECK_ARG(dev >= 0 && dev < 128, "prism_bsa_bwd_noalloc: device ordinal %d out of range", dev);
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  PRISM_CHECK_ARG(get_ctx != nullptr, "prism_bsa_bwd_noalloc: cuCtxGetCurrent is unavailable from the driver");
+  // A host thread may not have a current context yet; the runtime call below
+  // makes the device's primary context current, so the context is read again.
+  CUcontext ctx = nullptr;
+  PRISM_CHECK_ARG(get_ctx(&ctx) == CUDA_SUCCESS, "prism_bsa_bwd_noalloc: cuCtxGetCurrent failed");
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  NoallocSlot& slot = g_noalloc_slot[dev];
+  if (slot.addr == nullptr || ctx == nullptr || slot.ctx != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, tc::g_noalloc_delta);
     if (e != cudaSuccess || p == nullptr) {
@@ -2098,9 +1855,12 @@ static prism_status_t noalloc_scratch(float** out) {
                 cudaGetErrorString(e));
       return PRISM_ERR_CUDA;
     }
-    g_noalloc_addr[dev] = static_cast<float*>(p);
+    PRISM_CHECK_ARG(get_ctx(&ctx) == CUDA_SUCCESS && ctx != nullptr,
+                    "prism_bsa_bwd_noalloc: no current CUDA context");
+    slot.ctx = ctx;
+    slot.addr = static_cast<float*>(p);
   }
-  *out = g_noalloc_addr[dev];
+  *out = slot.addr;
   return PRISM_OK;
 }
 }  // namespace prism

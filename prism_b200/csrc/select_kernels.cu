@@ -1370,7 +1370,7 @@ using namespace prism;
 extern "C" {
 
 const char* prism_last_error(void) { return prism::last_error(); }
-int prism_abi_version(void) { return 4; }
+int prism_abi_version(void) { return 5; }
 
 prism_status_t prism_token_norms(const void* x, int64_t n_tokens, int dim, void* out,
                                  cudaStream_t stream) {

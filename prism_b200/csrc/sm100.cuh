@@ -54,13 +54,17 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Every wait in these kernels is bounded.  A wait that has not completed
-// after kWaitLimitNs sets the CTA's abort flag and the device error word and
-// returns false; the caller then leaves its loop, and the kernel drains what
-// it has in flight (also with bounded waits), frees its TMEM and exits.  A
-// set device error word also makes every other CTA give up at its next slow
+// after g_wait_limit_ns sets the CTA's abort flag and the device error word
+// and returns false; the caller then leaves its loop, and the kernel drains
+// what it has in flight (also with bounded waits), frees its TMEM and exits.
+// A set device error word also makes every other CTA give up at its next slow
 // wait, so one failure does not cost every CTA of the grid the full limit.
-// The word stays set until the host reads it (prism_device_status).
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// The word stays set until the host reads it (prism_device_status).  The
+// limit is 2 s; only the test entry prism_test_fwd_withheld_load shortens it,
+// for its own launch (stream-ordered writes before and after it).  This
+// header is compiled into one translation unit (bsa_tc.cu).
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;  // 2 s
+__device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 // try_wait with a suspend-time hint: the thread sleeps until the phase
 // completes or about `ns` nanoseconds pass, instead of polling the barrier
@@ -91,7 +95,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       *abort_flag = 1;
       return false;
     }
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns)) {
       *abort_flag = 1;
       atomicCAS(err, 0, code);
       return false;

@@ -63,6 +63,7 @@ class SparsePlan:
         self.sm_scale = sm_scale
         self.bits_q = None
         self.bits_k = None
+        self.seq_capacity = None  # token rows of the outputs' storage (see _new_like_layout)
 
     def select(self, q_re, k_re, v_re=None):
         """Tile bitmaps (bits_q, bits_k) for tile-ordered q / k (v: the guided
@@ -87,11 +88,16 @@ def _hsd(x: torch.Tensor, layout: str) -> torch.Tensor:
     return x[0] if layout == "bhsd" else x[0].transpose(0, 1)
 
 
-def _new_like_layout(heads, S, D, layout, dtype, device):
+def _new_like_layout(heads, S, D, layout, dtype, device, capacity=None):
+    """A new [1,H,S,D] or [1,S,H,D] tensor and its [H,S,D] view.  capacity (bshd
+    only): the storage holds that many token rows and the tensor is its first S
+    rows, so a Ulysses exchange can send it without a copy (the rows past S are
+    never written or read)."""
     if layout == "bhsd":
         t = torch.empty(1, heads, S, D, dtype=dtype, device=device)
         return t, t[0]
-    t = torch.empty(1, S, heads, D, dtype=dtype, device=device)
+    rows = S if capacity is None else max(int(capacity), S)
+    t = torch.empty(1, rows, heads, D, dtype=dtype, device=device)[:, :S]
     return t, t[0].transpose(0, 1)
 
 
@@ -113,7 +119,7 @@ class _BsaFunction(torch.autograd.Function):
         plan.bits_q, plan.bits_k = bits_q, bits_k
         o_re, lse, o_lo = ops.bsa_fwd(q_re, k_re, v_re, bits_q, plan.tile_bits, plan.sm_scale,
                                       want_lo=True)
-        out, out_hsd = _new_like_layout(heads, S, D, layout, q.dtype, q.device)
+        out, out_hsd = _new_like_layout(heads, S, D, layout, q.dtype, q.device, plan.seq_capacity)
         ops.scatter_rows(o_re, plan.grid, plan.grid_padded, plan.inv_idx, out=out_hsd)
         ctx.save_for_backward(q_re, k_re, v_re, o_re, o_lo, lse, bits_q, bits_k)
         ctx.plan = plan
@@ -132,7 +138,8 @@ class _BsaFunction(torch.autograd.Function):
                                           plan.tile_bits, plan.sm_scale, o_lo=o_lo)
         grads = []
         for g_re, is_k in ((dq_re, False), (dk_re, True), (dv_re, True)):
-            g, g_hsd = _new_like_layout(heads, Sk if is_k else S, D, layout, dout.dtype, dout.device)
+            g, g_hsd = _new_like_layout(heads, Sk if is_k else S, D, layout, dout.dtype, dout.device,
+                                        plan.seq_capacity)
             if is_k:
                 ops.scatter_rows(g_re, plan.grid_k, plan.grid_padded_k, plan.inv_idx_k, out=g_hsd)
             else:
@@ -152,15 +159,17 @@ def _check_head_dim(D: int):
 
 def build_plan(q_hsd, k_hsd, v_hsd, grid, grid_padded, *, method, sparsity, cdf_threshold,
                audio_token_norms=None, valid_mask=None, lambda_a=0.5, tau_128=0.15,
-               lambda_128=1.0, shape_ids=None):
-    """Shape ids (unless given), permutation, tile maps and key validity; no grad."""
+               lambda_128=1.0, shape_ids=None, sp_live_ranks=None):
+    """Shape ids (unless given), permutation, tile maps and key validity; no grad.
+    sp_live_ranks: SP ranks that contribute zone statistics (default: all)."""
     ops.selection_mode(sparsity, cdf_threshold)
     D = q_hsd.shape[-1]
     with torch.no_grad():
         if shape_ids is None:
             shape_ids = shapes_from_qkv(v_hsd, grid, grid_padded, method,
                                         audio_norms=audio_token_norms, valid_mask=valid_mask,
-                                        lambda_a=lambda_a, tau_128=tau_128, lambda_128=lambda_128)
+                                        lambda_a=lambda_a, tau_128=tau_128, lambda_128=lambda_128,
+                                        sp_live_ranks=sp_live_ranks)
         layout = ops.build_layout(shape_ids, grid_padded)
         tile_bits, _ = ops.tile_valid(layout["src_idx"], valid_mask, grid, grid_padded)
     plan = SparsePlan(grid, grid_padded, layout, tile_bits, sparsity, cdf_threshold,
@@ -226,11 +235,17 @@ def run_bsa_dynamic(
     return_shape_ids: bool = False,
     layout: str = "bhsd",
     return_plan: bool = False,
+    seq_capacity: Optional[int] = None,
+    sp_live_ranks: Optional[int] = None,
 ):
     """``SelfAttention._run_bsa_dynamic`` (wan_video_dit.py:342-432) on unpadded
     tokens: q, k, v [1, H, T*H*W, D] (layout="bhsd") or [1, T*H*W, H, D]
     (layout="bshd"), audio_token_norms [T*H*W] or None.  Padding to the zone
-    grid, the valid mask and the unpad are implicit.  Output has q's layout."""
+    grid, the valid mask and the unpad are implicit.  Output has q's layout.
+    seq_capacity (bshd): the output and the input gradients are the first
+    T*H*W rows of buffers of that many rows (a Ulysses exchange sends them
+    without a copy); sp_live_ranks: SP ranks whose zone statistics are averaged
+    (ranks holding only padding heads contribute zeros)."""
     if layout not in ("bhsd", "bshd"):
         raise ValueError("layout must be 'bhsd' or 'bshd'")
     T, H, W = grid_size
@@ -243,7 +258,10 @@ def run_bsa_dynamic(
     plan, shape_ids = build_plan(
         qh, _hsd(k, layout), _hsd(v, layout), grid_size, gp, method=method, sparsity=sparsity,
         cdf_threshold=cdf_threshold, audio_token_norms=audio_token_norms, valid_mask=None,
-        lambda_a=lambda_a, tau_128=tau_128, lambda_128=lambda_128, shape_ids=shape_ids)
+        lambda_a=lambda_a, tau_128=tau_128, lambda_128=lambda_128, shape_ids=shape_ids,
+        sp_live_ranks=sp_live_ranks)
+    if layout == "bshd":
+        plan.seq_capacity = seq_capacity
     out = _DynBsaFunction.apply(q, k, v, plan, layout)
     res = [out]
     if return_shape_ids:

@@ -30,22 +30,27 @@ NUM_CANDIDATES = len(ALL_CANDIDATE_SHAPES)
 ZONE_SIZE = 8
 
 
-def _maybe_sp_average(packed: torch.Tensor, sp_reduce: bool = True) -> torch.Tensor:
-    """AVG all-reduce of the packed zone means over the SP group
-    (dynamic_block_shape.py:132-151).  No try/except: a rank that skipped the
-    collective must fail loudly, not hang its peers."""
+def _maybe_sp_average(packed: torch.Tensor, sp_reduce: bool = True,
+                      live_ranks: Optional[int] = None) -> torch.Tensor:
+    """Average of the packed zone means over the SP group (dynamic_block_shape.py:
+    132-151): one SUM all-reduce, divided by the number of ranks that hold real
+    heads (``live_ranks``, default every rank -- the reference's AVG).  A rank
+    holding only padding heads joins the collective with zeros; the reference's
+    such rank would not join at all (its peers would wait forever), so dividing
+    by the live ranks keeps the average that of the ranks with data.  No
+    try/except: a rank that skipped the collective must fail loudly."""
     if not sp_reduce or (not get_sequence_parallel_state()) or nccl_info.sp_size <= 1:
         return packed
     dist.all_reduce(packed, op=dist.ReduceOp.SUM, group=nccl_info.sp_group)
-    packed /= float(nccl_info.sp_size)
+    packed /= float(nccl_info.sp_size if live_ranks is None else live_ranks)
     return packed
 
 
 def zone_statistics(v_hsd: torch.Tensor, grid, grid_padded, valid_mask=None, audio_norms=None,
-                    sp_reduce: bool = True):
+                    sp_reduce: bool = True, sp_live_ranks: Optional[int] = None):
     """Head-averaged V zone means (SP-averaged) + axis validity + audio zone means."""
     packed, axis_valid, audio = ops.zone_stats(v_hsd, grid, grid_padded, valid_mask, audio_norms)
-    packed = _maybe_sp_average(packed, sp_reduce)
+    packed = _maybe_sp_average(packed, sp_reduce, sp_live_ranks)
     return packed, axis_valid, audio
 
 
@@ -84,12 +89,13 @@ def select_zone_shapes(v_headavg_thw_d: torch.Tensor, audio_norms_thw: Optional[
 
 def shapes_from_qkv(v_hsd: torch.Tensor, grid, grid_padded, method: str, audio_norms=None,
                     valid_mask=None, lambda_a=0.5, tau_128=0.15, lambda_128=1.0,
-                    sp_reduce: bool = True) -> torch.Tensor:
+                    sp_reduce: bool = True, sp_live_ranks: Optional[int] = None) -> torch.Tensor:
     """Shape ids straight from the per-head V of the attention call (fuses the
     head average of dynamic_block_attention.py:236 into the zone statistics)."""
     if method not in ("ivpq", "penalty"):
         raise ValueError(f"unknown dynamic-block method: {method!r}")
-    packed, av, audio = zone_statistics(v_hsd, grid, grid_padded, valid_mask, audio_norms, sp_reduce)
+    packed, av, audio = zone_statistics(v_hsd, grid, grid_padded, valid_mask, audio_norms, sp_reduce,
+                                        sp_live_ranks)
     return ops.shape_select(packed, av, audio, audio_norms is not None, method, lambda_a, tau_128,
                             lambda_128)
 

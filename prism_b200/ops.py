@@ -434,6 +434,46 @@ def guidance_scale(n_chunks: int, device, *, rho=None, variance_gamma: float = 0
 
 
 # -------------------------------------------------------------- a15/a16
+class KernelTimer:
+    """CUDA events around the attention kernels while a step runs (measurement
+    only: ``set_kernel_timer(KernelTimer())`` before the steps, ``totals_ms()``
+    after a synchronize).  With a timer set the backward issues its three stages
+    (delta, dK/dV, dQ) as three calls, which launch the same kernels in the same
+    order as the one-call form."""
+
+    def __init__(self):
+        self.spans = {}
+
+    def mark(self, name, device):
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record(torch.cuda.current_stream(device))
+        self.spans.setdefault(name, []).append(ev)
+        return ev[1]
+
+    def totals_ms(self):
+        return {n: sum(a.elapsed_time(b) for a, b in evs) for n, evs in self.spans.items()}
+
+    def counts(self):
+        return {n: len(evs) for n, evs in self.spans.items()}
+
+
+_timer: Optional[KernelTimer] = None
+
+
+def set_kernel_timer(timer: Optional[KernelTimer]):
+    global _timer
+    _timer = timer
+
+
+def _timed(name, device, fn):
+    if _timer is None:
+        return fn()
+    end = _timer.mark(name, device)
+    r = fn()
+    end.record(torch.cuda.current_stream(device))
+    return r
+
+
 def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float, want_lo: bool = False):
     """Returns (o, lse) or (o, lse, o_lo) with o_lo the bf16 rounding residual of o."""
     _check_cuda(q_re, k_re, v_re)
@@ -442,8 +482,9 @@ def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float, want_lo: bool 
     o = torch.empty_like(q_re)
     o_lo = torch.empty_like(q_re) if want_lo else None
     lse = torch.empty(heads, Sq, dtype=torch.float32, device=q_re.device)
-    _lib.call("prism_bsa_fwd_qk", _p(q_re), _p(k_re), _p(v_re), heads, Sq, Sk, D, float(sm_scale),
-              _p(bits_q), _p(tile_bits), _p(o), _p(o_lo), _p(lse), _stream(q_re))
+    _timed("bsa_fwd", q_re.device, lambda: _lib.call(
+        "prism_bsa_fwd_qk", _p(q_re), _p(k_re), _p(v_re), heads, Sq, Sk, D, float(sm_scale),
+        _p(bits_q), _p(tile_bits), _p(o), _p(o_lo), _p(lse), _stream(q_re)))
     if want_lo:
         return o, lse, o_lo
     return o, lse
@@ -458,7 +499,19 @@ def bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k, tile_bits, sm_sc
     dk = torch.empty_like(k_re)
     dv = torch.empty_like(v_re)
     ws = _ws(_lib.query("prism_bsa_bwd_workspace_bytes", heads, Sq), q_re.device)
+    st, sm = _stream(q_re), float(sm_scale)
+    if _timer is not None and Sq == Sk:
+        dev = q_re.device
+        _timed("bsa_bwd_delta", dev, lambda: _lib.call(
+            "prism_bsa_bwd_delta", _p(o_re), _p(o_lo), _p(do_re), heads, Sq, D, _p(ws), st))
+        _timed("bsa_bwd_dkdv", dev, lambda: _lib.call(
+            "prism_bsa_bwd_dkdv", _p(q_re), _p(k_re), _p(v_re), _p(do_re), _p(lse), _p(ws), heads, Sq,
+            D, sm, _p(bits_k), _p(tile_bits), _p(dk), _p(dv), st))
+        _timed("bsa_bwd_dq", dev, lambda: _lib.call(
+            "prism_bsa_bwd_dq", _p(q_re), _p(k_re), _p(v_re), _p(do_re), _p(lse), _p(ws), heads, Sq, D,
+            sm, _p(bits_q), _p(tile_bits), _p(dq), st))
+        return dq, dk, dv
     _lib.call("prism_bsa_bwd_qk", _p(q_re), _p(k_re), _p(v_re), _p(o_re), _p(o_lo), _p(do_re),
-              _p(lse), heads, Sq, Sk, D, float(sm_scale), _p(bits_q), _p(bits_k), _p(tile_bits),
-              _p(ws), _p(dq), _p(dk), _p(dv), _stream(q_re))
+              _p(lse), heads, Sq, Sk, D, sm, _p(bits_q), _p(bits_k), _p(tile_bits),
+              _p(ws), _p(dq), _p(dk), _p(dv), st)
     return dq, dk, dv

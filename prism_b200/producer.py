@@ -37,7 +37,8 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
-from .communications import sp_chunk_sizes, sp_num_local_real_heads, sp_pad_num_heads
+from .communications import (HeadsToWire, WireToHeads, live_ranks, sp_chunk_sizes,
+                             sp_num_local_real_heads, sp_pad_num_heads)
 from .parallel_states import get_sequence_parallel_state, nccl_info
 
 
@@ -116,23 +117,6 @@ def norm_rope_pack(q_lin, k_lin, v_lin, gamma_q, gamma_k, eps: float, rope_cs, h
                                hp, S_pack)
 
 
-class _PackedAllToAll(torch.autograd.Function):
-    """all_to_all_single over dim 0 of a [P, ...] buffer; its own adjoint."""
-
-    @staticmethod
-    def forward(ctx, x, group):
-        ctx.group = group
-        out = torch.empty_like(x)
-        torch.distributed.all_to_all_single(out, x.contiguous(), group=group)
-        return out
-
-    @staticmethod
-    def backward(ctx, g):
-        out = torch.empty_like(g)
-        torch.distributed.all_to_all_single(out, g.contiguous(), group=ctx.group)
-        return out, None
-
-
 def o_proj_packed(recv: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], heads: int,
                   S_local: int) -> torch.Tensor:
     """self.o of the rows held in the inverse all-to-all's receive buffer
@@ -186,10 +170,12 @@ def fused_self_attention(x: torch.Tensor, rope_cs: torch.Tensor, params: dict, n
                                       params.get("norm_k_weight"), params.get("eps", 1e-6), rope_cs,
                                       num_heads, P, hp, S_pack)
     if sp:
+        # exchange; the full sequence of this rank's hp heads as [1, S_full, hp, D]
+        # views of the receive buffers
         group = nccl_info.sp_group
-        q_pk, k_pk, v_pk = (_PackedAllToAll.apply(t, group) for t in (q_pk, k_pk, v_pk))
-    # the full sequence of this rank's hp heads: [1, S_full, hp, D] views
-    q4, k4, v4 = (t.view(1, P * S_pack, hp, D)[:, :S_full] for t in (q_pk, k_pk, v_pk))
+        q4, k4, v4 = (WireToHeads.apply(t.unsqueeze(1), group, S_full) for t in (q_pk, k_pk, v_pk))
+    else:
+        q4, k4, v4 = (t.view(1, S_local, hp, D) for t in (q_pk, k_pk, v_pk))
     rank = nccl_info.rank_within_spgroup if sp else 0
     local = sp_num_local_real_heads(num_heads, padded, P, rank)
     norms = audio_token_norms(a2v_bridge_residual, full_seq_len)
@@ -197,7 +183,8 @@ def fused_self_attention(x: torch.Tensor, rope_cs: torch.Tensor, params: dict, n
         q4, k4, v4 = (t[:, :, :local] for t in (q4, k4, v4))
         if attention == "dynamic":
             xo = run_bsa_dynamic(q4, k4, v4, grid_size, audio_token_norms=norms, layout="bshd",
-                                 **attn_kw)
+                                 seq_capacity=P * S_pack if sp else None,
+                                 sp_live_ranks=live_ranks(num_heads, P) if sp else None, **attn_kw)
         elif attention == "uniform":
             xo = run_bsa_uniform(q4, k4, v4, grid_size, layout="bshd", **attn_kw)
         else:
@@ -211,12 +198,12 @@ def fused_self_attention(x: torch.Tensor, rope_cs: torch.Tensor, params: dict, n
         if attention == "dynamic" and attn_kw.get("shape_ids") is None:
             from .dynamic_block_shape import _maybe_sp_average
             Tp, Hp_, Wp = ops.padded_grid(grid_size)
-            _maybe_sp_average(torch.zeros((Tp // 8) * (Hp_ // 8) * (Wp // 8), 25 * D, device=x.device))
+            _maybe_sp_average(torch.zeros((Tp // 8) * (Hp_ // 8) * (Wp // 8), 25 * D, device=x.device),
+                              live_ranks=live_ranks(num_heads, P))
         xo = (q4 + k4 + v4) * 0.0
     if sp:
-        if P * S_pack != S_full:
-            xo = F.pad(xo, (0, 0, 0, 0, 0, P * S_pack - S_full))
-        recv = _PackedAllToAll.apply(xo.reshape(P, S_pack, hp, D), nccl_info.sp_group)
+        # sent as it is when xo is the attention's output buffer of P * S_pack rows
+        recv = HeadsToWire.apply(xo, nccl_info.sp_group, S_full).squeeze(1)
     else:
         recv = xo.reshape(1, S_local, hp, D)
     out = o_proj_packed(recv, params["o_weight"], params.get("o_bias"), num_heads, S_local)

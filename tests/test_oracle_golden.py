@@ -118,3 +118,32 @@ def test_attention_restatement(name):
             ref, got = ref[:, real_rows], got[:, real_rows]
         err = np.abs(got - ref).max()
         assert err <= 1e-5 * max(1.0, np.abs(ref).max()), (nm, err)
+
+
+@pytest.mark.parametrize("name", ["mixed_d128_penalty", "c0"])
+def test_float64_torch_restatement_matches_oracle(name):
+    """helpers.torch_bsa_reference (the float64 checker of the configuration-grid GPU
+    test, which runs it on the GPU) equals the numpy oracle's restatement on the
+    oracle's own selection, on CPU."""
+    import torch
+    from helpers import torch_bsa_reference
+    case = CASES[name]
+    inp = make_inputs(case)
+    vm = inp["valid"].numpy().astype(np.uint8)
+    r = O.dynamic_forward_selection(_b(inp["q"][0]), _b(inp["k"][0]), _b(inp["v"][0]),
+                                    case.grid_padded, method=case.method, sparsity=case.sparsity,
+                                    cdf_threshold=case.cdf_threshold, norms_bits=_b(inp["norms"]),
+                                    valid=vm, lambda_a=case.lambda_a, tau_128=case.tau_128,
+                                    lambda_128=case.lambda_128)
+    f = O.bf16_bits_to_f32
+    qr, kr, vr = f(r["q_re"]), f(r["k_re"]), f(r["v_re"])
+    do_re = inp["do"][0].float().numpy()[:, r["src_idx"]]
+    o, _ = O.bsa_forward(qr, kr, vr, r["bits_q"], r["valid_re"])
+    dq, dk, dv = O.bsa_backward(qr, kr, vr, o, do_re, r["bits_q"], r["valid_re"])
+    tb = np.packbits(r["valid_re"].reshape(-1, 64).astype(bool), axis=1,
+                     bitorder="little").view(np.uint64)[:, 0]
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    got = torch_bsa_reference(t(qr), t(kr), t(vr), t(do_re), t(r["bits_q"].view(np.int32)),
+                              t(tb.view(np.int64)), 1.0 / np.sqrt(case.head_dim), block_rows=192)
+    for g, ref in zip((got[0], got[2], got[3], got[4]), (o, dq, dk, dv)):
+        assert np.abs(g.numpy() - ref).max() <= 1e-9 * max(1.0, np.abs(ref).max())

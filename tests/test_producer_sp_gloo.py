@@ -1,6 +1,6 @@
 """The fused layer's Ulysses plumbing on CPU ranks (gloo, world size 2 and 4): the
-packed all-to-all of prism_b200.producer (send layout [P, S_pack, hp, D] as
-prism_norm_rope_pack writes it, head padding, an uneven last shard), its autograd
+wire exchanges WireToHeads / HeadsToWire (send layout [P, S_pack, hp, D] as
+prism_norm_rope_pack writes it, head padding, an uneven last shard), their autograd
 adjoint, and the K-split output projection on the inverse exchange's receive buffer
 against the unpacked projection (wan_video_dit.py:775-787, 824-841).  The attention
 in between is the identity, so two exchanges bring every rank its own tokens back."""
@@ -17,7 +17,8 @@ def _worker(rank, world, port, q):
         _init(rank, world, port)
         from prism_b200 import parallel_states as ps
         from prism_b200.communications import sp_chunk_sizes, sp_pad_num_heads
-        from prism_b200.producer import _PackedAllToAll, o_proj_packed
+        from prism_b200.communications import HeadsToWire, WireToHeads
+        from prism_b200.producer import o_proj_packed
         ps.initialize_sequence_parallel()
         group = ps.nccl_info.sp_group
         g = torch.Generator().manual_seed(0)
@@ -39,15 +40,14 @@ def _worker(rank, world, port, q):
                 if h < H:
                     send[p, :sizes[rank], hh] = mine[:, h]
         send.requires_grad_(True)
-        recv = _PackedAllToAll.apply(send, group)
-        seq = recv.reshape(world * S_pack, hp, D)[:S]          # the full sequence, my heads
+        seq4 = WireToHeads.apply(send.unsqueeze(1), group, S)   # [1, S, hp, D]
+        seq = seq4[0]                                           # the full sequence, my heads
         for hh in range(hp):
             h = rank * hp + hh
             want = full[:, h] if h < H else torch.zeros(S, D, dtype=torch.float64)
             assert torch.equal(seq[:, hh], want), (rank, hh)
         # inverse exchange of the (identity) attention output, then the K-split projection
-        back = torch.nn.functional.pad(seq, (0, 0, 0, 0, 0, world * S_pack - S)).reshape(world, S_pack, hp, D)
-        recv2 = _PackedAllToAll.apply(back, group)
+        recv2 = HeadsToWire.apply(seq4, group, S).squeeze(1)    # [P, S_pack, hp, D]
         out = o_proj_packed(recv2, W, b, H, sizes[rank])
         ref = mine.reshape(sizes[rank], H * D) @ W.t() + b
         assert torch.allclose(out, ref, rtol=1e-12, atol=1e-12)

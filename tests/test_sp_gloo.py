@@ -69,6 +69,34 @@ def _worker_a2a(rank, world, port, q):
         packed = torch.full((3, 25 * 4), float(rank + 1))
         avg = _maybe_sp_average(packed.clone())
         assert torch.allclose(avg, torch.full_like(packed, (world + 1) / 2))
+        # with heads that leave the last rank idle (it joins with zeros), the average
+        # is that of the ranks holding real heads
+        from prism_b200.communications import HeadGeometry, live_ranks
+        Hs = world - 1
+        hg = HeadGeometry(world, Hs)
+        mine = torch.full((3, 25 * 4), float(rank + 1)) if hg.real_on(rank) else torch.zeros(3, 25 * 4)
+        avg = _maybe_sp_average(mine, live_ranks=live_ranks(Hs, world))
+        assert live_ranks(Hs, world) == world - 1
+        assert torch.allclose(avg, torch.full_like(avg, world / 2)), avg[0, 0]
+        # the heads-side result is a view of the receive buffer, and a heads-side
+        # tensor stored in a buffer of P * C rows is sent without a copy
+        from prism_b200.communications import ShardGeometry, _heads_as_wire
+        C = ShardGeometry(world, S).C
+        buf = torch.randn(1, world * C, hpr, D, generator=g)
+        view = buf[:, :S]
+        w = _heads_as_wire(view, world, C)
+        assert w is not None and w.data_ptr() == buf.data_ptr() and w.is_contiguous()
+        assert torch.equal(w.reshape(world * C, hpr, D), buf[0])
+        assert _heads_as_wire(torch.randn(1, S, hpr, D), world, C) is None or world * C == S
+        back2 = all_to_all_4D(view, group, scatter_dim=1, gather_dim=2, full_seq_len=S)
+        ref2 = all_to_all_4D(view.contiguous().clone(), group, scatter_dim=1, gather_dim=2, full_seq_len=S)
+        assert torch.equal(back2, ref2)
+        # batch 2 and the negotiated full length (full_seq_len=None)
+        xb = torch.randn(2, sizes[rank], H, D, generator=torch.Generator().manual_seed(rank + 7))
+        yb = all_to_all_4D(xb, group, 2, 1)
+        assert yb.shape == (2, S, hpr, D)
+        zb = all_to_all_4D(yb, group, 1, 2, S)
+        assert torch.equal(zb, xb)
         dist.barrier()
         q.put((rank, "ok"))
     except Exception:

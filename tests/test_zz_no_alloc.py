@@ -29,8 +29,9 @@ REL_L2 = 1e-2
 
 def _problem(seed, dev, heads=2, n_tiles=16, D=128, density=0.6):
     g = torch.Generator().manual_seed(seed)
+    gd = torch.Generator(device=dev).manual_seed(seed)
     S = n_tiles * 64
-    q, k, v, do = (torch.randn(heads, S, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(4))
+    q, k, v, do = (torch.randn(heads, S, D, generator=gd, device=dev).to(torch.bfloat16) for _ in range(4))
     sel = (torch.rand(heads, n_tiles, n_tiles, generator=g) < density).numpy()
     bq = torch.from_numpy(O.dense_to_bits(sel).view(np.int32)).to(dev)
     bk = torch.from_numpy(O.dense_to_bits(sel.transpose(0, 2, 1)).view(np.int32)).to(dev)
@@ -68,10 +69,28 @@ def test_noalloc_backward_matches_allocating_entry_twice(cuda):
             _check(a, b, f"{name} (seed {seed})")
 
 
+def test_noalloc_head_dim_64_at_the_full_scratch(cuda):
+    """D = 64 with heads * S equal to the limit: the whole array is used (rows at its
+    top included) and the result still equals the allocating entry point's."""
+    limit = 4 << 20
+    heads, n_tiles = 32, 2048
+    assert heads * n_tiles * 64 == limit
+    sm = 1.0 / math.sqrt(64)
+    q, k, v, do, bq, bk, tb = _problem(13, cuda, heads=heads, n_tiles=n_tiles, D=64, density=0.01)
+    o, lse, o_lo = ops.bsa_fwd(q, k, v, bq, tb, sm, want_lo=True)
+    ref = ops.bsa_bwd(q, k, v, o, do, lse, bq, bk, tb, sm, o_lo=o_lo)
+    got = _noalloc(q, k, v, o, o_lo, do, lse, bq, bk, tb, sm)
+    torch.cuda.synchronize()
+    for name, a, b in zip(("dQ", "dK", "dV"), got, ref):
+        _check(a, b, f"{name} (D=64, {heads} x {n_tiles * 64} rows)")
+
+
 def test_noalloc_rejects_sizes_beyond_the_builtin_scratch(cuda):
     L = _lib.load()
     heads, S = 64, 128 * 1024  # 8M rows > 4M-row limit; refused before any GPU work
-    rc = L.prism_bsa_bwd_noalloc(*([ctypes.c_void_p(16)] * 7), heads, S, 128, ctypes.c_float(0.1),
-                                 *([ctypes.c_void_p(16)] * 6), None)
+    # null tensors: the size check comes first; were it ever skipped, the null-pointer
+    # checks would still refuse the call on the host, with no kernel launched
+    rc = L.prism_bsa_bwd_noalloc(*([None] * 7), heads, S, 128, ctypes.c_float(0.1),
+                                 *([None] * 6), None)
     assert rc != 0
     assert b"exceed the built-in scratch" in L.prism_last_error()
