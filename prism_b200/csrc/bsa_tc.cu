@@ -42,6 +42,7 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "prism_common.cuh"
@@ -69,6 +70,7 @@ enum WaitCode : int {
   kErrFwdProducer = 101, kErrFwdMma = 102, kErrFwdSoftmax = 103,
   kErrDkdvProducer = 201, kErrDkdvMma = 202, kErrDkdvSoftmax = 203,
   kErrDqProducer = 301, kErrDqMma = 302, kErrDqSoftmax = 303,
+  kErrDkdvPairExit = 204,
 };
 
 // Union iterator over two bitmap rows (global memory, read through the
@@ -107,6 +109,18 @@ struct UnionIter {
 __device__ __forceinline__ int union_count(const uint32_t* ra, const uint32_t* rb, int wq) {
   int c = 0;
   for (int w = 0; w < wq; ++w) c += __popc(__ldg(ra + w) | __ldg(rb + w));
+  return c;
+}
+
+// Number of tiles in the union of up to four bitmap rows (nullptr = empty row).
+__device__ __forceinline__ int union4_count(const uint32_t* const (&r)[4], int wq) {
+  int c = 0;
+  for (int w = 0; w < wq; ++w) {
+    uint32_t x = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x |= r[i] ? __ldg(r[i] + w) : 0u;
+    c += __popc(x);
+  }
   return c;
 }
 
@@ -361,6 +375,71 @@ __device__ __forceinline__ void add_key_bias(float (&s)[64], const float* __rest
   }
 }
 
+// Forward one-pass limit on a key tile's exponential sum (see the softmax loop).
+constexpr float kFwdSumLimit = 65536.0f;
+
+// Scores of keys outside the valid mask (bit c of vb clear) -> -inf.
+__device__ __forceinline__ void mask_keys(float (&s)[64], uint64_t vb) {
+#pragma unroll
+  for (int c = 0; c < 64; ++c)
+    if (!((vb >> c) & 1ull)) s[c] = -INFINITY;
+}
+
+__device__ __forceinline__ float tile_max(const float (&s)[64]) {
+  float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
+#pragma unroll
+  for (int c = 4; c < 64; c += 4) {
+    m0 = fmaxf(m0, s[c]);
+    m1 = fmaxf(m1, s[c + 1]);
+    m2 = fmaxf(m2, s[c + 2]);
+    m3 = fmaxf(m3, s[c + 3]);
+  }
+  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+}
+
+// p = exp2(s * scale - m) for 64 scores as 32 bf16 pairs; returns the sum of the
+// fp32 p (even and odd columns summed separately, then added).  The exponent
+// arguments are packed f32x2 FFMAs (each lane rounds as fmaf does); the sums
+// stay scalar (a packed accumulator costs registers the softmax does not have).
+__device__ __forceinline__ float exp_tile(const float (&s)[64], float scale, float m, uint32_t (&pk)[32]) {
+  const float2 sc = make_float2(scale, scale), nm = make_float2(-m, -m);
+  float su0 = 0.f, su1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sc, nm);
+    const float p0 = ex2(x.x), p1 = ex2(x.y);
+    su0 += p0;
+    su1 += p1;
+    pk[c] = pack_bf16(p0, p1);
+  }
+  return su0 + su1;
+}
+
+// s[c] <- exp2(s[c] * scale + bias) for 64 scores (packed FFMA pairs).
+__device__ __forceinline__ void exp_rows(float (&s)[64], float scale, float bias) {
+  const float2 sc = make_float2(scale, scale), b = make_float2(bias, bias);
+#pragma unroll
+  for (int c = 0; c < 64; c += 2) {
+    const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sc, b);
+    s[c] = ex2(x.x);
+    s[c + 1] = ex2(x.y);
+  }
+}
+
+// Rows of this warp's TMEM lanes, columns [0, 32 * NC) of taddr, times alpha.
+template <int NC>
+__device__ __forceinline__ void scale_tmem_rows(uint32_t taddr, float alpha) {
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    uint32_t raw[32];
+    tmem_ld32(taddr + c * 32, raw);
+    tmem_wait_ld_dep(raw);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
+    tmem_st32(taddr + c * 32, raw);
+  }
+}
+
 // kKeyBias = false: the block-sparse forward (key validity tile_bits[key tile],
 // shared by every query tile and head).  kKeyBias = true: the same kernel with a
 // per-key score offset key_bias [Sk] and key masks per (head, query tile, key
@@ -592,18 +671,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       tc_fence_after();
       float sum0 = 0.f, sum1 = 0.f;
-      // Exponentials against the running maximum m in one pass over S while this
-      // block's maximum is tracked; a row's first block (m = -inf) and a first key
-      // tile whose maximum exceeds m by more than the rescale threshold take two
-      // passes (maximum, then exponentials: S is still intact then).  If only the
-      // second key tile exceeds it, P of the first (<= 2^8, already in TMEM) and
-      // l, O are scaled to the new maximum and the second tile is recomputed from
-      // its scores (columns [64, 128), intact).  Without a rescale the result
-      // equals the two-pass form's bit for bit.
+      // Exponentials against the running maximum m in one pass over S.  A row's
+      // first block (m = -inf) and a first key tile whose exponentials sum past
+      // kFwdSumLimit (some p > 2^10, or an overflow) take two passes (maximum,
+      // then exponentials: S is still intact then).  If only the second key tile
+      // passes the limit, P of the first (already in TMEM) and l, O are scaled to
+      // the new maximum and the second tile is recomputed from its scores
+      // (columns [64, 128), intact).  Between rescales p <= 2^16, exact in fp32
+      // and bf16's relative precision; the result is the same softmax in exact
+      // arithmetic.  The one-pass path costs per score one packed FFMA, one ex2,
+      // one packed FADD and half a bf16x2 conversion.
       bool two_pass = __any_sync(0xffffffffu, m == -INFINITY);
       uint32_t pk0[32];
       if (!two_pass) {
-        float xmax = -INFINITY;
         if (vb0 == 0ull) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) pk0[i] = 0u;
@@ -611,24 +691,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           float sv[64];
           tmem_load<2>(t_lane + L::T_S, sv);
           add_key_bias<kKeyBias>(sv, key_bias, t0);
-          if (vb0 != ~0ull) {
-#pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (!((vb0 >> c) & 1ull)) sv[c] = -INFINITY;
-          }
-          float su0 = 0.f, su1 = 0.f;
-#pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float x0 = fmaf(sv[c], qk_scale, -m), x1 = fmaf(sv[c + 1], qk_scale, -m);
-            xmax = fmaxf(xmax, fmaxf(x0, x1));
-            const float p0 = ex2(x0), p1 = ex2(x1);
-            su0 += p0;
-            su1 += p1;
-            pk0[c / 2] = pack_bf16(p0, p1);
-          }
-          sum0 = su0 + su1;
+          if (vb0 != ~0ull) mask_keys(sv, vb0);
+          sum0 = exp_tile(sv, qk_scale, m, pk0);
         }
-        two_pass = __any_sync(0xffffffffu, xmax > kRescaleThreshold);
+        two_pass = __any_sync(0xffffffffu, !(sum0 <= kFwdSumLimit));
       }
       if (two_pass) {
         sum0 = 0.f;
@@ -641,21 +707,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           float s[64];
           tmem_load<2>(t_lane + L::T_S + u * 64, s);
           add_key_bias<kKeyBias>(s, key_bias, u ? t1 : t0);
-          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-          if (vb == ~0ull) {
-#pragma unroll
-            for (int c = 0; c < 64; c += 4) {
-              m0 = fmaxf(m0, s[c]);
-              m1 = fmaxf(m1, s[c + 1]);
-              m2 = fmaxf(m2, s[c + 2]);
-              m3 = fmaxf(m3, s[c + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if ((vb >> c) & 1ull) m0 = fmaxf(m0, s[c]);
-          }
-          mx = fmaxf(mx, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
+          if (vb != ~0ull) mask_keys(s, vb);
+          mx = fmaxf(mx, tile_max(s));
         }
         mx *= qk_scale;
         const bool need = mx > m + kRescaleThreshold;  // m = -inf: any valid key
@@ -666,17 +719,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           l *= alpha;
           m = m_new;
           // every P V before this pair has completed: S_g(n) was issued after them
-          if (n > 0 && o_live) {
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-              uint32_t raw[32];
-              tmem_ld32(t_lane + L::T_O + c * 32, raw);
-              tmem_wait_ld_dep(raw);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
-              tmem_st32(t_lane + L::T_O + c * 32, raw);
-            }
-          }
+          if (n > 0 && o_live) scale_tmem_rows<D / 32>(t_lane + L::T_O, alpha);
         }
         // pass 2: p = exp2(s * scale - m) -> bf16 P over the first 64 columns of S
         const float mb = (m == -INFINITY) ? 0.0f : m;
@@ -691,19 +734,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             float s[64];
             tmem_load<2>(t_lane + L::T_S + u * 64, s);
             add_key_bias<kKeyBias>(s, key_bias, u ? t1 : t0);
-            if (vb != ~0ull) {
-#pragma unroll
-              for (int c = 0; c < 64; ++c)
-                if (!((vb >> c) & 1ull)) s[c] = -INFINITY;
-            }
-#pragma unroll
-            for (int c = 0; c < 64; c += 2) {
-              const float p0 = ex2(fmaf(s[c], qk_scale, -mb));
-              const float p1 = ex2(fmaf(s[c + 1], qk_scale, -mb));
-              sum0 += p0;
-              sum1 += p1;
-              pk[c / 2] = pack_bf16(p0, p1);
-            }
+            if (vb != ~0ull) mask_keys(s, vb);
+            const float t = exp_tile(s, qk_scale, mb, pk);
+            if (u) sum1 = t; else sum0 = t;
           }
           // P columns [32 u, 32 u + 32) overlap S columns [0, 64), which pass 2
           // has already read for u = 0 and does not read again
@@ -712,7 +745,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       } else {
         // P columns [0, 32) overlap S columns [0, 64) of the first key tile (read)
         tmem_st32(t_lane + L::T_S, pk0);
-        float xmax = -INFINITY;
         uint32_t pk1[32];
         if (vb1 == 0ull) {
 #pragma unroll
@@ -721,70 +753,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           float sv[64];
           tmem_load<2>(t_lane + L::T_S + 64, sv);
           add_key_bias<kKeyBias>(sv, key_bias, t1);
-          if (vb1 != ~0ull) {
-#pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (!((vb1 >> c) & 1ull)) sv[c] = -INFINITY;
-          }
-          float su0 = 0.f, su1 = 0.f;
-#pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float x0 = fmaf(sv[c], qk_scale, -m), x1 = fmaf(sv[c + 1], qk_scale, -m);
-            xmax = fmaxf(xmax, fmaxf(x0, x1));
-            const float p0 = ex2(x0), p1 = ex2(x1);
-            su0 += p0;
-            su1 += p1;
-            pk1[c / 2] = pack_bf16(p0, p1);
-          }
-          sum1 = su0 + su1;
+          if (vb1 != ~0ull) mask_keys(sv, vb1);
+          sum1 = exp_tile(sv, qk_scale, m, pk1);
         }
-        const bool need = xmax > kRescaleThreshold;
+        const bool need = !(sum1 <= kFwdSumLimit);
         if (__any_sync(0xffffffffu, need)) {
-          const float m_new = need ? m + xmax : m;
-          const float alpha = need ? ex2(m - m_new) : 1.0f;
-          if (n > 0) {
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
+          // rare: rescale to this row's new maximum (tile 1's scores, columns
+          // [64, 128) of S, are still intact in TMEM)
+          float sv[64];
+          tmem_load<2>(t_lane + L::T_S + 64, sv);
+          add_key_bias<kKeyBias>(sv, key_bias, t1);
+          if (vb1 != ~0ull) mask_keys(sv, vb1);
+          {
+            const float m_new = need ? fmaxf(m, tile_max(sv) * qk_scale) : m;
+            const float alpha = ex2(m - m_new);
+            if (n > 0) scale_tmem_rows<D / 32>(t_lane + L::T_O, alpha);
+            tmem_wait_st();
+            {
               uint32_t raw[32];
-              tmem_ld32(t_lane + L::T_O + c * 32, raw);
+              tmem_ld32(t_lane + L::T_S, raw);
               tmem_wait_ld_dep(raw);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(u2f(raw[i]) * alpha);
-              tmem_st32(t_lane + L::T_O + c * 32, raw);
+              for (int i = 0; i < 32; ++i)
+                raw[i] = pack_bf16(u2f(raw[i] << 16) * alpha, u2f(raw[i] & 0xffff0000u) * alpha);
+              tmem_st32(t_lane + L::T_S, raw);
             }
-          }
-          tmem_wait_st();
-          {
-            uint32_t raw[32];
-            tmem_ld32(t_lane + L::T_S, raw);
-            tmem_wait_ld_dep(raw);
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              raw[i] = pack_bf16(u2f(raw[i] << 16) * alpha, u2f(raw[i] & 0xffff0000u) * alpha);
-            tmem_st32(t_lane + L::T_S, raw);
-          }
-          l = (l + sum0) * alpha;
-          sum0 = 0.f;
-          m = m_new;
-          sum1 = 0.f;
-          if (vb1 != 0ull) {
-            float sv[64];
-            tmem_load<2>(t_lane + L::T_S + 64, sv);
-            add_key_bias<kKeyBias>(sv, key_bias, t1);
-            if (vb1 != ~0ull) {
-#pragma unroll
-              for (int c = 0; c < 64; ++c)
-                if (!((vb1 >> c) & 1ull)) sv[c] = -INFINITY;
-            }
-            float su0 = 0.f, su1 = 0.f;
-#pragma unroll
-            for (int c = 0; c < 64; c += 2) {
-              const float p0 = ex2(fmaf(sv[c], qk_scale, -m)), p1 = ex2(fmaf(sv[c + 1], qk_scale, -m));
-              su0 += p0;
-              su1 += p1;
-              pk1[c / 2] = pack_bf16(p0, p1);
-            }
-            sum1 = su0 + su1;
+            l = (l + sum0) * alpha;
+            sum0 = 0.f;
+            m = m_new;
+            sum1 = exp_tile(sv, qk_scale, m, pk1);
           }
         }
         // P columns [32, 64) overlap S columns [32, 64) of the first key tile (read)
@@ -1057,6 +1054,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     const float* sM = reinterpret_cast<const float*>(sm + L::M);
     const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
+    const float2 neg1 = make_float2(-1.0f, -1.0f);
     while (it.next(t0, s0, t1, s1)) {
       const int st = n & 1, ph = n & 1;
       const int sel = wg ? s1 : s0;
@@ -1074,15 +1072,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       float p[64];
       if (tile_on) {
         tmem_load<2>(t_lane + L::T_S + tcol, p);
+        if (on) {
+          // p = exp2(s * scale - lse / ln 2) in packed pairs (each lane rounds as
+          // fmaf / fmul; -(lse * c) == lse * (-c) exactly)
+          const float2 sc = make_float2(qk_scale, qk_scale), nr = make_float2(-kRcpLn2, -kRcpLn2);
 #pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4) {
-          const float4 mv = m_st[c4];
-          const float mm[4] = {mv.x * kRcpLn2, mv.y * kRcpLn2, mv.z * kRcpLn2, mv.w * kRcpLn2};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = 4 * c4 + j;
-            p[c] = on ? ex2(fmaf(p[c], qk_scale, -mm[j])) : 0.0f;
+          for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 mv = m_st[c4];
+            const float2 n0 = __fmul2_rn(make_float2(mv.x, mv.y), nr);
+            const float2 n1 = __fmul2_rn(make_float2(mv.z, mv.w), nr);
+            const float2 x0 = __ffma2_rn(make_float2(p[4 * c4], p[4 * c4 + 1]), sc, n0);
+            const float2 x1 = __ffma2_rn(make_float2(p[4 * c4 + 2], p[4 * c4 + 3]), sc, n1);
+            p[4 * c4] = ex2(x0.x);
+            p[4 * c4 + 1] = ex2(x0.y);
+            p[4 * c4 + 2] = ex2(x1.x);
+            p[4 * c4 + 3] = ex2(x1.y);
           }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) p[c] = 0.0f;
         }
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -1119,8 +1127,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int c4 = 0; c4 < 8; ++c4) {
             const float4 dv4 = d_st[8 * hh + c4];
             const int c = 4 * c4, pc = 32 * hh + c;
-            pk[c / 2] = pack_bf16(p[pc] * (dp[c] - dv4.x), p[pc + 1] * (dp[c + 1] - dv4.y));
-            pk[c / 2 + 1] = pack_bf16(p[pc + 2] * (dp[c + 2] - dv4.z), p[pc + 3] * (dp[c + 3] - dv4.w));
+            // dp - delta as fma(delta, -1, dp): the same single rounding as the subtraction
+            const float2 a = __fmul2_rn(make_float2(p[pc], p[pc + 1]),
+                                        __ffma2_rn(make_float2(dv4.x, dv4.y), neg1, make_float2(dp[c], dp[c + 1])));
+            const float2 b = __fmul2_rn(make_float2(p[pc + 2], p[pc + 3]),
+                                        __ffma2_rn(make_float2(dv4.z, dv4.w), neg1, make_float2(dp[c + 2], dp[c + 3])));
+            pk[c / 2] = pack_bf16(a.x, a.y);
+            pk[c / 2 + 1] = pack_bf16(b.x, b.y);
           }
         } else {
 #pragma unroll
@@ -1165,6 +1178,422 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == kBwdMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ======================================================= dK / dV on CTA pairs
+// A (2, 1, 1) cluster computes 256 keys (key tiles 4p..4p+3: the even CTA
+// holds tiles 4p, 4p+1, the odd one 4p+2, 4p+3) with cta_group::2 MMAs of
+// M = 256.  Per step two query tiles (t0, t1) of the union of the four key
+// tiles' transposed rows (N = 128 query columns).  The even CTA stores tile
+// t0's Q / dO rows (the N half of the B operand of S^T = K Q^T and
+// dP^T = V dO^T), the odd CTA tile t1's; each stores the D columns
+// [64 r, 64 r + 64) of both tiles (its N half of the B operand of dK += dS^T Q
+// and dV += P^T dO).  Each CTA therefore reads its own 128 key rows and only
+// half of every B operand from its shared memory: 128 KB of operand reads per
+// step instead of 192 KB on one CTA, for the same TMA bytes -- the one-CTA
+// kernel is bound on the shared-memory port (operand reads + fills ~ the tensor
+// time).  TMEM (each CTA, its 128 key rows): dK, dV, S^T, dP^T (128 columns
+// each).  Warp 9 of the even CTA issues every MMA and waits on barriers of the
+// even CTA that collect both CTAs' arrivals; MMA completions are committed to
+// both CTAs.  Each CTA's loads complete on its own barrier (so each CTA drains
+// its own copies), and a relay lane of its producer warp forwards each
+// completion to the even CTA.  The last step of an odd union repeats tile t0
+// as its second tile with no row selecting it (P = 0 there).  D = 128 only.
+template <int D>
+struct DkdvPairLayout {
+  static_assert(D == 128, "CTA-pair dK/dV: head dim 128");
+  static constexpr int kRing = 2;
+  static constexpr int K = 0;                         // 128 keys x D: 2 sub-buffers of 128 rows
+  static constexpr int V = K + 32768;
+  static constexpr int SLOT = V + 32768;              // kRing ring slots of kSlotBytes
+  // within a slot: QS / DOS = this CTA's query tile (2 sub-buffers of 64 rows);
+  // QK / DOK = D columns [64 r, 64 r + 64) of both tiles (1 sub-buffer of 128 rows)
+  static constexpr int QS = 0, DOS = 16384, QK = 32768, DOK = 49152, kSlotBytes = 65536;
+  static constexpr int M = SLOT + kRing * kSlotBytes;  // kRing x 128 f32 (lse of both tiles)
+  static constexpr int DL = M + kRing * 512;           // kRing x 128 f32 (delta)
+  static constexpr int BAR = DL + kRing * 512;
+  static constexpr int B_KVL = 0, B_KV = 1, B_QFL = 2, B_QF = B_QFL + kRing, B_QE = B_QF + kRing,
+                       B_SF = B_QE + kRing, B_DPF = B_SF + 1, B_PF = B_DPF + 1, B_DSF = B_PF + 1,
+                       B_FIN = B_DSF + 1, B_DRAIN = B_FIN + 1, B_EXIT = B_DRAIN + 1,
+                       NBAR = B_EXIT + 1;
+  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
+  static constexpr int ABORT = TMEM_SLOT + 4;
+  static constexpr size_t kBytes = 1024 + ABORT + 4;
+  static constexpr int T_DK = 0, T_DV = 128, T_S = 256, T_DP = 384;
+};
+
+// Union of up to four bitmap rows (nullptr = empty row), increasing tile order;
+// sel bit i: row i selected the tile.
+struct Union4Iter {
+  const uint32_t* r[4];
+  int wq, wi;
+  uint32_t w[4];
+  __device__ __forceinline__ uint32_t word(int i, int k) const { return r[i] ? __ldg(r[i] + k) : 0u; }
+  __device__ __forceinline__ void init(const uint32_t* const (&rows)[4], int n) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = rows[i];
+    wq = n;
+    wi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = n > 0 ? word(i, 0) : 0u;
+  }
+  __device__ __forceinline__ int next(int& sel) {
+    while ((w[0] | w[1] | w[2] | w[3]) == 0u) {
+      if (++wi >= wq) return -1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = word(i, wi);
+    }
+    const int bit = __ffs(w[0] | w[1] | w[2] | w[3]) - 1;
+    const uint32_t m = 1u << bit;
+    sel = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sel |= (w[i] & m) ? (1 << i) : 0;
+      w[i] &= ~m;
+    }
+    return wi * 32 + bit;
+  }
+  // the next two tiles; an odd last tile is paired with itself, selected by no row
+  __device__ __forceinline__ bool next_pair(int& t0, int& s0, int& t1, int& s1) {
+    t0 = next(s0);
+    if (t0 < 0) return false;
+    t1 = next(s1);
+    if (t1 < 0) {
+      t1 = t0;
+      s1 = 0;
+    }
+    return true;
+  }
+};
+
+// A bounded wait that ignores the CTA's abort flag: the pair's exit handshake
+// must wait for the peer even after an abort (the peer leaves its loops within
+// one slow-wait check of the error word).
+__device__ __forceinline__ bool exit_wait(uint32_t bar) {
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_sleep_cl(bar, 0u, 20000u)) return true;
+    if (globaltimer() - t0 > 2ull * *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns))
+      return false;
+  }
+}
+
+template <int KSUB, int A_SUB, int B_SUB>
+__device__ __forceinline__ void mma2_kd(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc,
+                                        uint32_t accumulate) {
+  mma2_chain4<2, 4, 6, 2, 4, 6>(d_tmem, a0, b0, idesc, accumulate);
+  if (KSUB > 1) mma2_chain4<2, 4, 6, 2, 4, 6>(d_tmem, a0 + (A_SUB >> 4), b0 + (B_SUB >> 4), idesc, 1u);
+}
+
+template <int D>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
+    dkdv_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                     const float* __restrict__ lse, const float* __restrict__ delta, int64_t Sq,
+                     int64_t Sk, int wq, float qk_scale, float sm_scale,
+                     const uint32_t* __restrict__ bits_k, const uint64_t* __restrict__ tile_bits,
+                     __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv) {
+  using L = DkdvPairLayout<D>;
+  constexpr int R = L::kRing;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const uint32_t sb = smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cr = cluster_ctarank();  // 0: the CTA that issues the MMAs
+  const int pair = blockIdx.x >> 1, h = blockIdx.y;
+  const int64_t n_ktiles = Sk / 64;
+  const int kt = 4 * pair + 2 * (int)cr;  // this CTA's first key tile
+  const bool live = kt < n_ktiles;         // n_ktiles is even: kt + 1 exists too
+  const int row_base = (int)((int64_t)h * Sk + (int64_t)kt * 64);
+  const int head_row = (int)((int64_t)h * Sq);
+  auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
+  auto bar0 = [&](int i) { return mapa_shared(sb + L::BAR + 8 * i, 0u); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
+  const uint32_t* rows[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    rows[i] = 4 * (int64_t)pair + i < n_ktiles ? bits_k + ((int64_t)h * n_ktiles + 4 * pair + i) * wq : nullptr;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::B_KVL), 1);
+    mbar_init(bar(L::B_KV), 2);
+    for (int i = 0; i < R; ++i) {
+      mbar_init(bar(L::B_QFL + i), 1);
+      mbar_init(bar(L::B_QF + i), 2);
+      mbar_init(bar(L::B_QE + i), 1);
+    }
+    mbar_init(bar(L::B_SF), 1);
+    mbar_init(bar(L::B_DPF), 1);
+    mbar_init(bar(L::B_PF), 16);
+    mbar_init(bar(L::B_DSF), 16);
+    mbar_init(bar(L::B_FIN), 1);
+    mbar_init(bar(L::B_DRAIN), 1);
+    mbar_init(bar(L::B_EXIT), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kBwdMmaWarp) {
+    tmem_alloc_pair(sb + L::TMEM_SLOT, 512);
+    tmem_relinquish_pair();
+    tc_fence_before();
+  }
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any arrival crosses
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
+
+  if (warp == kBwdProducerWarp) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- loads
+      mbar_expect_tx(bar(L::B_KVL), 2 * 128 * D * 2);
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          tma_load_2d(sb + L::K + s * 16384 + rr * 8192, &tm_k, s * 64, row_base + rr * 64, bar(L::B_KVL));
+          tma_load_2d(sb + L::V + s * 16384 + rr * 8192, &tm_v, s * 64, row_base + rr * 64, bar(L::B_KVL));
+        }
+      Union4Iter it;
+      it.init(rows, wq);
+      int n = 0, t0, s0, t1, s1;
+      while (it.next_pair(t0, s0, t1, s1)) {
+        const int st = n & 1;
+        if (n >= R && !mbar_wait(bar(L::B_QE + st), ((n >> 1) - 1) & 1, abort_flag, &g_tc_error,
+                                 kErrDkdvProducer))
+          break;
+        const uint32_t slot = sb + L::SLOT + st * L::kSlotBytes, fb = bar(L::B_QFL + st);
+        mbar_expect_tx(fb, 4 * 2 * 8192 + 2 * 512);
+        const int tm = cr ? t1 : t0;
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          tma_load_2d(slot + L::QS + s * 8192, &tm_q, s * 64, head_row + tm * 64, fb);
+          tma_load_2d(slot + L::DOS + s * 8192, &tm_do, s * 64, head_row + tm * 64, fb);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int t = u ? t1 : t0;
+          tma_load_2d(slot + L::QK + u * 8192, &tm_q, (int)cr * 64, head_row + t * 64, fb);
+          tma_load_2d(slot + L::DOK + u * 8192, &tm_do, (int)cr * 64, head_row + t * 64, fb);
+          bulk_load(sb + L::M + st * 512 + u * 256, lse + head_row + (int64_t)t * 64, 256, fb);
+          bulk_load(sb + L::DL + st * 512 + u * 256, delta + head_row + (int64_t)t * 64, 256, fb);
+        }
+        ++n;
+      }
+      // drain: every issued copy has landed before the CTA may leave
+      for (int m = (n > R ? n - R : 0); m < n; ++m)
+        mbar_wait(bar(L::B_QFL + (m & 1)), (m >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
+      mbar_wait(bar(L::B_KVL), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
+    } else if (lane == 1) {
+      // ---------------------------------------------------------- relay
+      bool ok = mbar_wait(bar(L::B_KVL), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
+      if (ok) mbar_arrive_cluster(bar0(L::B_KV));
+      const int steps = (union4_count(rows, wq) + 1) >> 1;
+      for (int n = 0; ok && n < steps; ++n) {
+        ok = mbar_wait(bar(L::B_QFL + (n & 1)), (n >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
+        if (ok) mbar_arrive_cluster(bar0(L::B_QF + (n & 1)));
+      }
+    }
+  } else if (warp == kBwdMmaWarp) {
+    // Even CTA only.  Issue order as in the one-CTA kernel: S^T(n) | dK(n-1) |
+    // dP^T(n) | dV(n), ..., dK(last).
+    if (cr == 0 && lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(256, 128, false, false);
+      constexpr uint32_t IDESC_G = idesc_bf16(256, D, false, true);
+      constexpr uint32_t kSlot = L::kSlotBytes >> 4;
+      const uint64_t dK = desc_k_sw128(sb + L::K), dV = desc_k_sw128(sb + L::V),
+                     dQS = desc_k_sw128(sb + L::SLOT + L::QS), dDOS = desc_k_sw128(sb + L::SLOT + L::DOS),
+                     dQK = desc_mn_sw128(sb + L::SLOT + L::QK, 16384),
+                     dDOK = desc_mn_sw128(sb + L::SLOT + L::DOK, 16384);
+      const int steps = (union4_count(rows, wq) + 1) >> 1;
+      auto dk_step = [&](int j) -> bool {
+        const uint32_t js = (uint32_t)j & 1u;
+        if (!mbar_wait_cl(bar(L::B_DSF), js, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
+        tc_fence_after();
+        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP, dQK + js * kSlot, IDESC_G,
+                                                 j > 0 ? 1u : 0u);
+        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP + 64,
+                                                 dQK + js * kSlot + (8192 >> 4), IDESC_G, 1u);
+        mma_commit_pair(bar(L::B_QE + js));
+        return true;
+      };
+      bool ok = mbar_wait_cl(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
+      tc_fence_after();
+      for (int n = 0; ok && n < steps; ++n) {
+        const uint32_t st = (uint32_t)n & 1u;
+        if (!mbar_wait_cl(bar(L::B_QF + st), ((uint32_t)n >> 1) & 1u, abort_flag, &g_tc_error, kErrDkdvMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        mma2_kd<2, 16384, 8192>(tmem + L::T_S, dK, dQS + st * kSlot, IDESC_S, 0u);
+        mma_commit_pair(bar(L::B_SF));
+        if (n > 0 && !dk_step(n - 1)) {
+          ok = false;
+          break;
+        }
+        mma2_kd<2, 16384, 8192>(tmem + L::T_DP, dV, dDOS + st * kSlot, IDESC_S, 0u);
+        mma_commit_pair(bar(L::B_DPF));
+        if (!mbar_wait_cl(bar(L::B_PF), st, abort_flag, &g_tc_error, kErrDkdvMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S, dDOK + st * kSlot, IDESC_G,
+                                                 n > 0 ? 1u : 0u);
+        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S + 64,
+                                                 dDOK + st * kSlot + (8192 >> 4), IDESC_G, 1u);
+      }
+      if (ok && steps > 0) dk_step(steps - 1);
+      mma_commit_pair(bar(L::B_FIN));
+      mma_commit_pair_local(bar(L::B_DRAIN));
+      mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
+    }
+  } else {
+    // softmax warpgroups of both CTAs: wg w takes query tile w of each step (64
+    // columns) for this CTA's 128 keys
+    const int wg = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // key row within the CTA == TMEM lane
+    const int half = r >> 6;               // this CTA's key tile of the row (warp-uniform)
+    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const bool kvalid = live && ((tile_bits[kt + half] >> (r & 63)) & 1ull);
+    const int selbit = 2 * (int)cr + half;
+    Union4Iter it;
+    it.init(rows, wq);
+    int n = 0, t0, s0, t1, s1;
+    bool ok = true;
+    const float* sM = reinterpret_cast<const float*>(sm + L::M);
+    const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
+    const float2 neg1 = make_float2(-1.0f, -1.0f);
+    while (it.next_pair(t0, s0, t1, s1)) {
+      const int st = n & 1, ph = n & 1;
+      const int sel = wg ? s1 : s0;
+      const bool tile_on = (sel >> selbit) & 1;  // warp-uniform
+      const bool on = tile_on && kvalid;
+      if (!warp_wait(bar(L::B_QFL + st), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax) ||
+          !warp_wait(bar(L::B_SF), ph, abort_flag, kErrDkdvSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float4* m_st = reinterpret_cast<const float4*>(sM + st * 128 + wg * 64);
+      const float4* d_st = reinterpret_cast<const float4*>(sDl + st * 128 + wg * 64);
+      const uint32_t tcol = wg * 64;
+      float p[64];
+      if (tile_on) {
+        tmem_load<2>(t_lane + L::T_S + tcol, p);
+        if (on) {
+          const float2 sc = make_float2(qk_scale, qk_scale), nr = make_float2(-kRcpLn2, -kRcpLn2);
+#pragma unroll
+          for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 mv = m_st[c4];
+            const float2 n0 = __fmul2_rn(make_float2(mv.x, mv.y), nr);
+            const float2 n1 = __fmul2_rn(make_float2(mv.z, mv.w), nr);
+            const float2 x0 = __ffma2_rn(make_float2(p[4 * c4], p[4 * c4 + 1]), sc, n0);
+            const float2 x1 = __ffma2_rn(make_float2(p[4 * c4 + 2], p[4 * c4 + 3]), sc, n1);
+            p[4 * c4] = ex2(x0.x);
+            p[4 * c4 + 1] = ex2(x0.y);
+            p[4 * c4 + 2] = ex2(x1.x);
+            p[4 * c4 + 3] = ex2(x1.y);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) p[c] = 0.0f;
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) pk[c / 2] = pack_bf16(p[32 * hh + c], p[32 * hh + c + 1]);
+          tmem_st16(t_lane + L::T_S + tcol + 16 * hh, pk);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) p[c] = 0.0f;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = 0u;
+        tmem_st16(t_lane + L::T_S + tcol, pk);
+        tmem_st16(t_lane + L::T_S + tcol + 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(bar0(L::B_PF));
+      if (!warp_wait(bar(L::B_DPF), ph, abort_flag, kErrDkdvSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t pk[16];
+        if (tile_on) {
+          float dp[32];
+          tmem_load<1>(t_lane + L::T_DP + tcol + 32 * hh, dp);
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 dv4 = d_st[8 * hh + c4];
+            const int c = 4 * c4, pc = 32 * hh + c;
+            const float2 a = __fmul2_rn(make_float2(p[pc], p[pc + 1]),
+                                        __ffma2_rn(make_float2(dv4.x, dv4.y), neg1, make_float2(dp[c], dp[c + 1])));
+            const float2 b = __fmul2_rn(make_float2(p[pc + 2], p[pc + 3]),
+                                        __ffma2_rn(make_float2(dv4.z, dv4.w), neg1, make_float2(dp[c + 2], dp[c + 3])));
+            pk[c / 2] = pack_bf16(a.x, a.y);
+            pk[c / 2 + 1] = pack_bf16(b.x, b.y);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = 0u;
+        }
+        tmem_st16(t_lane + L::T_DP + tcol + 16 * hh, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(bar0(L::B_DSF));
+      ++n;
+    }
+    // epilogue: wg 0 writes dK (scaled by sm_scale), wg 1 writes dV
+    if (live) {
+      const int64_t grow = (int64_t)row_base + r;
+      __nv_bfloat16* out = (wg == 0 ? dk : dv) + grow * D;
+      const float scale = wg == 0 ? sm_scale : 1.0f;
+      const int tcolo = wg == 0 ? L::T_DK : L::T_DV;
+      if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDkdvSoftmax)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t raw[32], pk2[16];
+          tmem_ld32(t_lane + tcolo + c * 32, raw);
+          tmem_wait_ld_dep(raw);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk2[i] = pack_bf16(u2f(raw[2 * i]) * scale, u2f(raw[2 * i + 1]) * scale);
+          uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk2[4 * i], pk2[4 * i + 1], pk2[4 * i + 2], pk2[4 * i + 3]);
+        }
+      } else if (ok && n == 0) {
+        uint4* a = reinterpret_cast<uint4*>(out);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) a[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  tc_fence_before();
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");  // this thread's arrivals at the peer are performed
+  __syncthreads();
+  // Neither CTA frees its TMEM or leaves while the other may still use it: the
+  // even CTA's MMAs have drained (B_DRAIN) before its thread 0 gets here, and
+  // each CTA's softmax and relay arrivals to the even CTA are done.
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(mapa_shared(bar(L::B_EXIT), cr ^ 1u));
+    if (!exit_wait(bar(L::B_EXIT))) atomicCAS(&g_tc_error, 0, kErrDkdvPairExit);
+  }
+  __syncthreads();
+  if (warp == kBwdMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -1395,13 +1824,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
       float p[64];
-      if (vb != 0ull) tmem_load<2>(t_lane + L::T_S + wg * 64, p);
-      if (vb == ~0ull) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) p[c] = ex2(fmaf(p[c], qk_scale, -mrow));
-      } else if (vb != 0ull) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) p[c] = ((vb >> c) & 1ull) ? ex2(fmaf(p[c], qk_scale, -mrow)) : 0.0f;
+      if (vb != 0ull) {
+        tmem_load<2>(t_lane + L::T_S + wg * 64, p);
+        if (vb != ~0ull) mask_keys(p, vb);  // masked keys: exp2(-inf) = 0
+        exp_rows(p, qk_scale, -mrow);
       }
       if (!warp_wait(bar(L::B_DPF), n & 1, abort_flag, kErrDqSoftmax)) {
         ok = false;
@@ -1415,9 +1841,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(L::B_DPE));
+        const float2 nd = make_float2(-drow, -drow);
 #pragma unroll
-        for (int c = 0; c < 64; c += 2)
-          pk[c / 2] = pack_bf16(p[c] * (dp[c] - drow), p[c + 1] * (dp[c + 1] - drow));
+        for (int c = 0; c < 64; c += 2) {
+          const float2 ds = __fmul2_rn(make_float2(p[c], p[c + 1]),
+                                       __fadd2_rn(make_float2(dp[c], dp[c + 1]), nd));
+          pk[c / 2] = pack_bf16(ds.x, ds.y);
+        }
       } else {
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(L::B_DPE));
@@ -1601,6 +2031,29 @@ prism_status_t launch_dkdv2(const void* q, const void* k, const void* v, const v
 }
 
 template <int D>
+prism_status_t launch_dkdv_pair(const void* q, const void* k, const void* v, const void* dout,
+                                const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
+                                float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
+                                void* dk, void* dv, cudaStream_t stream) {
+  const int64_t n_ktiles = Sk / 64;
+  const int wq = (int)((Sq / 64 + 31) / 32);  // words per bits_k row (query tiles)
+  const size_t sm = DkdvPairLayout<D>::kBytes > kMinSmem ? DkdvPairLayout<D>::kBytes : kMinSmem;
+  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
+  CUtensorMap mq, mk, mv, mdo;
+  PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
+  PRISM_TRY(make_map(&mdo, dout, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
+  PRISM_CHECK_CUDA(cudaFuncSetAttribute(dkdv_pair_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "prism_bsa_bwd: smem attribute");
+  dkdv_pair_kernel<D><<<dim3((unsigned)(2 * ((n_ktiles + 3) / 4)), heads), kBwdThreads, sm, stream>>>(
+      mq, mk, mv, mdo, lse, delta, Sq, Sk, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
+      (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
+  PRISM_CHECK_LAUNCH("prism_bsa_bwd_dkdv");
+  return PRISM_OK;
+}
+
+template <int D>
 prism_status_t launch_dq(const void* q, const void* k, const void* v, const void* dout,
                          const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
                          float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
@@ -1740,8 +2193,16 @@ static prism_status_t bwd_dkdv_qk(const void* q, const void* k, const void* v, c
   PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dk) &&
                       aligned16(dv) && aligned16(lse) && aligned16(delta),
                   "prism_bsa_bwd_dkdv: tensors must be 16-byte aligned");
-  return D == 128 ? tc::launch_dkdv2<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream)
-                  : tc::launch_dkdv2<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  if (D == 128) {
+    static const bool pair = [] {
+      const char* e = getenv("PRISM_DKDV_PAIR");
+      return e != nullptr && e[0] == '1';
+    }();
+    if (pair)
+      return tc::launch_dkdv_pair<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
+    return tc::launch_dkdv2<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  }
+  return tc::launch_dkdv2<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
 }
 
 static prism_status_t bwd_dq_qk(const void* q, const void* k, const void* v, const void* dout,

@@ -93,19 +93,16 @@ __global__ void zone_partial_kernel(const uint16_t* __restrict__ v, int heads, i
       const uint16_t* base = v + s * ss + c0;
       float a0 = 0.0f, a1 = 0.0f;
       int hh = 0;
-      for (; hh + 4 <= heads; hh += 4) {
-        uint32_t u0 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 0) * sh));
-        uint32_t u1 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 1) * sh));
-        uint32_t u2 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 2) * sh));
-        uint32_t u3 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + 3) * sh));
-        a0 = __fadd_rn(a0, __uint_as_float(u0 << 16));
-        a1 = __fadd_rn(a1, __uint_as_float(u0 & 0xffff0000u));
-        a0 = __fadd_rn(a0, __uint_as_float(u1 << 16));
-        a1 = __fadd_rn(a1, __uint_as_float(u1 & 0xffff0000u));
-        a0 = __fadd_rn(a0, __uint_as_float(u2 << 16));
-        a1 = __fadd_rn(a1, __uint_as_float(u2 & 0xffff0000u));
-        a0 = __fadd_rn(a0, __uint_as_float(u3 << 16));
-        a1 = __fadd_rn(a1, __uint_as_float(u3 & 0xffff0000u));
+      // eight heads' loads in flight, then their sums in head order
+      for (; hh + 8 <= heads; hh += 8) {
+        uint32_t u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u[i] = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + i) * sh));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a0 = __fadd_rn(a0, __uint_as_float(u[i] << 16));
+          a1 = __fadd_rn(a1, __uint_as_float(u[i] & 0xffff0000u));
+        }
       }
       for (; hh < heads; ++hh) {
         uint32_t u0 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)hh * sh));
@@ -552,6 +549,72 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int
   out[((int64_t)h * osh) / 8 + (int64_t)j] = val;
 }
 
+// The same gathers with each thread moving one 16-byte chunk of kRowsPerThread
+// rows (chunks | 256: the block covers 256 / chunks rows per pass): every load
+// is issued before the first store, so a thread keeps 64 bytes in flight -- a
+// one-chunk-per-thread copy holds too few bytes in flight to reach HBM rate.
+constexpr int kRowsPerThread = 4;
+__global__ void __launch_bounds__(256) gather_rows4_kernel(
+    const uint4* __restrict__ x, int64_t xsh, int64_t xss, int chunks, int T, int H, int W, int Hp,
+    int Wp, int Sp, const int32_t* __restrict__ src_idx, uint4* __restrict__ out, int64_t osh) {
+  const int rpp = 256 / chunks;  // rows per pass
+  const int c = threadIdx.x % chunks;
+  const int r0 = blockIdx.x * (rpp * kRowsPerThread) + threadIdx.x / chunks;
+  const int h = blockIdx.y;
+  const int hw = Hp * Wp;
+  const uint4* xh = x + ((int64_t)h * xsh) / 8 + c;
+  uint4* oh = out + ((int64_t)h * osh) / 8 + c;
+  uint4 val[kRowsPerThread];
+#pragma unroll
+  for (int u = 0; u < kRowsPerThread; ++u) {
+    const int r = r0 + u * rpp;
+    val[u] = make_uint4(0, 0, 0, 0);
+    if (r < Sp) {
+      const int g = __ldg(src_idx + r);
+      const int t = g / hw;
+      const int rem = g - t * hw;
+      const int hh = rem / Wp;
+      const int w = rem - hh * Wp;
+      if (t < T && hh < H && w < W) val[u] = __ldg(xh + ((((int64_t)t * H + hh) * W + w) * xss) / 8);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kRowsPerThread; ++u) {
+    const int r = r0 + u * rpp;
+    if (r < Sp) oh[(int64_t)r * chunks] = val[u];
+  }
+}
+
+__global__ void __launch_bounds__(256) scatter_rows4_kernel(
+    const uint4* __restrict__ x, int64_t xsh, int chunks, int T, int H, int W, int Hp, int Wp,
+    const int32_t* __restrict__ inv_idx, uint4* __restrict__ out, int64_t osh, int64_t oss) {
+  const int rpp = 256 / chunks;
+  const int c = threadIdx.x % chunks;
+  const int s0 = blockIdx.x * (rpp * kRowsPerThread) + threadIdx.x / chunks;
+  const int h = blockIdx.y;
+  const int S = T * H * W, hw = H * W;
+  const uint4* xh = x + ((int64_t)h * xsh) / 8 + c;
+  uint4* oh = out + ((int64_t)h * osh) / 8 + c;
+  uint4 val[kRowsPerThread];
+#pragma unroll
+  for (int u = 0; u < kRowsPerThread; ++u) {
+    const int sx = s0 + u * rpp;
+    if (sx < S) {
+      const int t = sx / hw;
+      const int rem = sx - t * hw;
+      const int hh = rem / W;
+      const int w = rem - hh * W;
+      const int r = __ldg(inv_idx + ((int64_t)t * Hp + hh) * Wp + w);
+      val[u] = __ldg(xh + (int64_t)r * chunks);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kRowsPerThread; ++u) {
+    const int sx = s0 + u * rpp;
+    if (sx < S) oh[((int64_t)sx * oss) / 8] = val[u];
+  }
+}
+
 __global__ void scatter_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int chunks, int T, int H,
                                     int W, int Hp, int Wp, const int32_t* __restrict__ inv_idx,
                                     uint4* __restrict__ out, int64_t osh, int64_t oss) {
@@ -591,10 +654,21 @@ __global__ void pool_kernel(const uint16_t* __restrict__ q, const uint16_t* __re
     const uint16_t* qr = q + ((int64_t)h * S + (int64_t)j * 64) * D + d;
     const uint16_t* kr = k + ((int64_t)h * S + (int64_t)j * 64) * D + d;
     float sq = 0.0f, sk = 0.0f;
-    for (int i = 0; i < 64; ++i) {
-      if (!((bits >> i) & 1ull)) continue;
-      sq = __fadd_rn(sq, bfbits2f(qr[(int64_t)i * D]));
-      sk = __fadd_rn(sk, bfbits2f(kr[(int64_t)i * D]));
+    // sixteen rows' loads in flight (every row of the tile is in bounds), then the
+    // masked sums in row order
+    for (int i0 = 0; i0 < 64; i0 += 16) {
+      uint16_t uq[16], uk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        uq[i] = __ldg(qr + (int64_t)(i0 + i) * D);
+        uk[i] = __ldg(kr + (int64_t)(i0 + i) * D);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (!((bits >> (i0 + i)) & 1ull)) continue;
+        sq = __fadd_rn(sq, bfbits2f(uq[i]));
+        sk = __fadd_rn(sk, bfbits2f(uk[i]));
+      }
     }
     const float fc = (float)c;
     const float den = c > 0 ? fc : 1.0f;
@@ -1483,9 +1557,16 @@ prism_status_t prism_gather_rows(const void* x, int64_t x_stride_h, int64_t x_st
                   "prism_gather_rows: bad row count");
   const int64_t total = n_rows * chunks;
   if (total == 0 || heads == 0) return PRISM_OK;
-  gather_rows_kernel<<<dim3((unsigned)((total + 255) / 256), heads), 256, 0, stream>>>(
-      (const uint4*)x, x_stride_h, x_stride_s, chunks, T, H, W, Hp, Wp, (int)n_rows, src_idx,
-      (uint4*)out, out_stride_h);
+  if (256 % chunks == 0) {
+    const int64_t per_block = (256 / chunks) * kRowsPerThread;
+    gather_rows4_kernel<<<dim3((unsigned)((n_rows + per_block - 1) / per_block), heads), 256, 0, stream>>>(
+        (const uint4*)x, x_stride_h, x_stride_s, chunks, T, H, W, Hp, Wp, (int)n_rows, src_idx,
+        (uint4*)out, out_stride_h);
+  } else {
+    gather_rows_kernel<<<dim3((unsigned)((total + 255) / 256), heads), 256, 0, stream>>>(
+        (const uint4*)x, x_stride_h, x_stride_s, chunks, T, H, W, Hp, Wp, (int)n_rows, src_idx,
+        (uint4*)out, out_stride_h);
+  }
   PRISM_CHECK_LAUNCH("prism_gather_rows");
   return PRISM_OK;
 }
@@ -1503,9 +1584,16 @@ prism_status_t prism_scatter_rows(const void* x_re, int64_t x_stride_h, int head
   PRISM_CHECK_ARG(S * chunks < (int64_t)1 << 31 && heads <= 65535, "prism_scatter_rows: too many rows");
   const int64_t total = S * chunks;
   if (total == 0 || heads == 0) return PRISM_OK;
-  scatter_rows_kernel<<<dim3((unsigned)((total + 255) / 256), heads), 256, 0, stream>>>(
-      (const uint4*)x_re, x_stride_h, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out,
-      out_stride_h, out_stride_s);
+  if (256 % chunks == 0) {
+    const int64_t per_block = (256 / chunks) * kRowsPerThread;
+    scatter_rows4_kernel<<<dim3((unsigned)((S + per_block - 1) / per_block), heads), 256, 0, stream>>>(
+        (const uint4*)x_re, x_stride_h, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out, out_stride_h,
+        out_stride_s);
+  } else {
+    scatter_rows_kernel<<<dim3((unsigned)((total + 255) / 256), heads), 256, 0, stream>>>(
+        (const uint4*)x_re, x_stride_h, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out,
+        out_stride_h, out_stride_s);
+  }
   PRISM_CHECK_LAUNCH("prism_scatter_rows");
   return PRISM_OK;
 }
