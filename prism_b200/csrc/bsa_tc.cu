@@ -377,6 +377,11 @@ __device__ __forceinline__ void add_key_bias(float (&s)[64], const float* __rest
 
 // Forward one-pass limit on a key tile's exponential sum (see the softmax loop).
 constexpr float kFwdSumLimit = 65536.0f;
+// Forward: every kFwdFmaEvery-th pair of score columns takes its exp2 on the FMA pipe.
+#ifndef PRISM_FWD_FMA_EVERY
+#define PRISM_FWD_FMA_EVERY 0
+#endif
+constexpr int kFwdFmaEvery = PRISM_FWD_FMA_EVERY;
 
 // Scores of keys outside the valid mask (bit c of vb clear) -> -inf.
 __device__ __forceinline__ void mask_keys(float (&s)[64], uint64_t vb) {
@@ -397,17 +402,55 @@ __device__ __forceinline__ float tile_max(const float (&s)[64]) {
   return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
 }
 
+// 2^x for a pair of arguments on the FMA pipe instead of the MUFU unit, from the
+// range reduction 2^x = 2^j * 2^f (j = x rounded to the nearest integer by the
+// 1.5 * 2^23 addition, f = x - j in [-1/2, 1/2]) and the Taylor series of
+// e^t = 2^f at t = f ln 2 through degree 4 (truncation below 4.3e-5 relative at
+// |t| <= ln2 / 2; P is rounded to bf16, 2^-9, after this).  2^j is added to the
+// exponent field.  Arguments are clamped at -126 (any x < -126 gives a value
+// below 2^-125 where exp2 gives 0 or a denormal: invisible next to the row sum,
+// which is >= 1).  Written from the series; checked against ex2.approx on the GPU.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  constexpr float kC1 = 0.693147180559945f, kC2 = 0.240226506959101f, kC3 = 0.0555041086648216f,
+                  kC4 = 0.00961812910762848f, kRound = 12582912.0f;  // ln2^k / k!, 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));            // j in the low mantissa bits
+  const float2 j = __fadd2_rn(t, make_float2(-kRound, -kRound));           // exact
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);            // x - j, exact
+  float2 p = __ffma2_rn(f, make_float2(kC4, kC4), make_float2(kC3, kC3));
+  p = __ffma2_rn(p, f, make_float2(kC2, kC2));
+  p = __ffma2_rn(p, f, make_float2(kC1, kC1));
+  p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+  // (bits(t) << 23) == j << 23 (mod 2^32): the constant part of bits(t) shifts out
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 // p = exp2(s * scale - m) for 64 scores as 32 bf16 pairs; returns the sum of the
 // fp32 p (even and odd columns summed separately, then added).  The exponent
 // arguments are packed f32x2 FFMAs (each lane rounds as fmaf does); the sums
 // stay scalar (a packed accumulator costs registers the softmax does not have).
+// kFmaEvery > 0: every kFmaEvery-th pair of columns takes exp2_fma2 instead of
+// the MUFU ex2 -- the forward issues one ex2 per score against two MMAs per key
+// tile, so the MUFU unit alone takes as long as the tensor core; moving a share
+// of the exponentials to the FMA pipe leaves it headroom.
+template <int kFmaEvery>
 __device__ __forceinline__ float exp_tile(const float (&s)[64], float scale, float m, uint32_t (&pk)[32]) {
   const float2 sc = make_float2(scale, scale), nm = make_float2(-m, -m);
   float su0 = 0.f, su1 = 0.f;
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
     const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sc, nm);
-    const float p0 = ex2(x.x), p1 = ex2(x.y);
+    float p0, p1;
+    if (kFmaEvery > 0 && c % kFmaEvery == kFmaEvery - 1) {
+      const float2 e = exp2_fma2(x);
+      p0 = e.x;
+      p1 = e.y;
+    } else {
+      p0 = ex2(x.x);
+      p1 = ex2(x.y);
+    }
     su0 += p0;
     su1 += p1;
     pk[c] = pack_bf16(p0, p1);
@@ -692,7 +735,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tmem_load<2>(t_lane + L::T_S, sv);
           add_key_bias<kKeyBias>(sv, key_bias, t0);
           if (vb0 != ~0ull) mask_keys(sv, vb0);
-          sum0 = exp_tile(sv, qk_scale, m, pk0);
+          sum0 = exp_tile<kFwdFmaEvery>(sv, qk_scale, m, pk0);
         }
         two_pass = __any_sync(0xffffffffu, !(sum0 <= kFwdSumLimit));
       }
@@ -735,7 +778,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tmem_load<2>(t_lane + L::T_S + u * 64, s);
             add_key_bias<kKeyBias>(s, key_bias, u ? t1 : t0);
             if (vb != ~0ull) mask_keys(s, vb);
-            const float t = exp_tile(s, qk_scale, mb, pk);
+            const float t = exp_tile<kFwdFmaEvery>(s, qk_scale, mb, pk);
             if (u) sum1 = t; else sum0 = t;
           }
           // P columns [32 u, 32 u + 32) overlap S columns [0, 64), which pass 2
@@ -754,7 +797,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tmem_load<2>(t_lane + L::T_S + 64, sv);
           add_key_bias<kKeyBias>(sv, key_bias, t1);
           if (vb1 != ~0ull) mask_keys(sv, vb1);
-          sum1 = exp_tile(sv, qk_scale, m, pk1);
+          sum1 = exp_tile<kFwdFmaEvery>(sv, qk_scale, m, pk1);
         }
         const bool need = !(sum1 <= kFwdSumLimit);
         if (__any_sync(0xffffffffu, need)) {
@@ -781,7 +824,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             l = (l + sum0) * alpha;
             sum0 = 0.f;
             m = m_new;
-            sum1 = exp_tile(sv, qk_scale, m, pk1);
+            sum1 = exp_tile<kFwdFmaEvery>(sv, qk_scale, m, pk1);
           }
         }
         // P columns [32, 64) overlap S columns [32, 64) of the first key tile (read)
@@ -839,6 +882,130 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (warp == kFwdMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------ dK / dV softmax (both kernels)
+// The transposed softmax reads the 16x256b TMEM layout.  A softmax warp covers
+// its 32 key lanes x the 64 query columns of one tile.  With 16x256b loads a
+// thread holds, in each 16-lane half, key lanes a and a + 8 (a = lane / 4) at
+// the column pairs 8 j + 2 (lane % 4) + {0, 1}, j = 0..7: 16 query columns
+// rather than a whole row's 64, so it reads 16 lse and 16 delta values per tile
+// (one 8-byte load per column pair; a warp's load touches 4 addresses: one
+// shared-memory wavefront).  A thread owning a whole key row would need all 64
+// values of both, broadcast by 16-byte loads at 4 wavefronts each -- half of
+// the shared-memory port at the tensor core's rate, which the MMA operand reads
+// and TMA fills need.  The bf16 pairs go back with 16x128b stores, whose
+// layout puts packed column 4 j + lane % 4 of lanes a, a + 8 in the registers
+// that hold them.
+__device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_16x128b_x8(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x128b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+// Key validity of this thread's four lanes: bit 2 hl + kk <=> key lane
+// 32 q + 16 hl + 8 kk + lane / 4 of the CTA is valid (q = lane quarter of the warp).
+__device__ __forceinline__ uint32_t dkdv_lane_valid(uint64_t tile_valid_bits, int quarter, int lane) {
+  uint32_t v = 0;
+#pragma unroll
+  for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const int row = 32 * quarter + 16 * hl + 8 * kk + (lane >> 2);
+      v |= (uint32_t)((tile_valid_bits >> (row & 63)) & 1ull) << (2 * hl + kk);
+    }
+  return v;
+}
+
+// P^T of one query tile for this warp: p[32 hl + 4 j + 2 kk + e] = exp2(s * scale -
+// lse[col] / ln 2) (0 for an invalid key lane or an unselected tile), written as bf16
+// pairs over the first 32 of the tile's 64 S^T columns.  t_tile = TMEM address of
+// the warp's lane quarter at the tile's first S^T column.
+__device__ __forceinline__ void dkdv_p_tile(uint32_t t_tile, const float* __restrict__ lse_t,
+                                            float qk_scale, bool tile_on, uint32_t lane_valid,
+                                            int lane, float (&p)[64]) {
+  const int c2 = 2 * (lane & 3);
+  const float2 sc = make_float2(qk_scale, qk_scale), nr = make_float2(-kRcpLn2, -kRcpLn2);
+#pragma unroll
+  for (int hl = 0; hl < 2; ++hl) {
+    uint32_t pk[16];
+    if (tile_on) {
+      uint32_t raw[32];
+      tmem_ld_16x256b_x8(t_tile + ((uint32_t)(16 * hl) << 16), raw);
+      tmem_wait_ld_dep(raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        // -(lse * c) == lse * (-c) exactly; each lane of the packed ops rounds as fmaf / fmul
+        const float2 nl = __fmul2_rn(*reinterpret_cast<const float2*>(lse_t + 8 * j + c2), nr);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const bool on = (lane_valid >> (2 * hl + kk)) & 1u;
+          const float2 x = __ffma2_rn(make_float2(u2f(raw[4 * j + 2 * kk]), u2f(raw[4 * j + 2 * kk + 1])), sc, nl);
+          const float e0 = on ? ex2(x.x) : 0.0f, e1 = on ? ex2(x.y) : 0.0f;
+          p[32 * hl + 4 * j + 2 * kk] = e0;
+          p[32 * hl + 4 * j + 2 * kk + 1] = e1;
+          pk[2 * j + kk] = pack_bf16(e0, e1);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p[32 * hl + i] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = 0u;
+    }
+    // bf16 columns [0, 32) of the tile over S^T columns this half has read
+    tmem_st_16x128b_x8(t_tile + ((uint32_t)(16 * hl) << 16), pk);
+  }
+}
+
+// dS^T = P^T (dP^T - delta[col]) of one query tile as bf16 pairs over the first 32
+// of the tile's 64 dP^T columns (t_tile: the warp's lane quarter at the tile's first
+// dP^T column).
+__device__ __forceinline__ void dkdv_ds_tile(uint32_t t_tile, const float* __restrict__ delta_t,
+                                             bool tile_on, int lane, const float (&p)[64]) {
+  const int c2 = 2 * (lane & 3);
+  const float2 neg1 = make_float2(-1.0f, -1.0f);
+#pragma unroll
+  for (int hl = 0; hl < 2; ++hl) {
+    uint32_t pk[16];
+    if (tile_on) {
+      uint32_t raw[32];
+      tmem_ld_16x256b_x8(t_tile + ((uint32_t)(16 * hl) << 16), raw);
+      tmem_wait_ld_dep(raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 d2 = *reinterpret_cast<const float2*>(delta_t + 8 * j + c2);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const int i = 32 * hl + 4 * j + 2 * kk;
+          // dp - delta as fma(delta, -1, dp): the same single rounding as the subtraction
+          const float2 ds = __fmul2_rn(make_float2(p[i], p[i + 1]),
+                                       __ffma2_rn(d2, neg1, make_float2(u2f(raw[4 * j + 2 * kk]),
+                                                                        u2f(raw[4 * j + 2 * kk + 1]))));
+          pk[2 * j + kk] = pack_bf16(ds.x, ds.y);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = 0u;
+    }
+    tmem_st_16x128b_x8(t_tile + ((uint32_t)(16 * hl) << 16), pk);
   }
 }
 
@@ -1044,70 +1211,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else {
     // softmax warpgroups: wg w takes query tile w of each step (64 columns)
     const int wg = warp >> 2;
-    const int r = (warp & 3) * 32 + lane;  // key row within the CTA == TMEM lane
-    const int half = r >> 6;
+    const int r = (warp & 3) * 32 + lane;  // key row of the epilogue == TMEM lane
+    const int half = (warp & 3) >> 1;      // this warp's key tile of the CTA
     const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const bool kvalid = (tile_bits[2 * pair + half] >> (r & 63)) & 1ull;
+    const uint32_t lane_valid = dkdv_lane_valid(tile_bits[2 * pair + half], warp & 3, lane);
     UnionPairIter it;
     it.init(row_a, row_b, wq);
     int n = 0, t0, s0, t1, s1;
     bool ok = true;
     const float* sM = reinterpret_cast<const float*>(sm + L::M);
     const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
-    const float2 neg1 = make_float2(-1.0f, -1.0f);
     while (it.next(t0, s0, t1, s1)) {
       const int st = n & 1, ph = n & 1;
       const int sel = wg ? s1 : s0;
       const bool tile_on = (wg == 0 || t1 >= 0) && ((sel >> half) & 1);  // warp-uniform
-      const bool on = tile_on && kvalid;
       if (!warp_wait(bar(L::B_QF + st), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax) ||
           !warp_wait(bar(L::B_SF), ph, abort_flag, kErrDkdvSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const float4* m_st = reinterpret_cast<const float4*>(sM + st * 128 + wg * 64);
-      const float4* d_st = reinterpret_cast<const float4*>(sDl + st * 128 + wg * 64);
       const uint32_t tcol = wg * 64;
       float p[64];
-      if (tile_on) {
-        tmem_load<2>(t_lane + L::T_S + tcol, p);
-        if (on) {
-          // p = exp2(s * scale - lse / ln 2) in packed pairs (each lane rounds as
-          // fmaf / fmul; -(lse * c) == lse * (-c) exactly)
-          const float2 sc = make_float2(qk_scale, qk_scale), nr = make_float2(-kRcpLn2, -kRcpLn2);
-#pragma unroll
-          for (int c4 = 0; c4 < 16; ++c4) {
-            const float4 mv = m_st[c4];
-            const float2 n0 = __fmul2_rn(make_float2(mv.x, mv.y), nr);
-            const float2 n1 = __fmul2_rn(make_float2(mv.z, mv.w), nr);
-            const float2 x0 = __ffma2_rn(make_float2(p[4 * c4], p[4 * c4 + 1]), sc, n0);
-            const float2 x1 = __ffma2_rn(make_float2(p[4 * c4 + 2], p[4 * c4 + 3]), sc, n1);
-            p[4 * c4] = ex2(x0.x);
-            p[4 * c4 + 1] = ex2(x0.y);
-            p[4 * c4 + 2] = ex2(x1.x);
-            p[4 * c4 + 3] = ex2(x1.y);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) p[c] = 0.0f;
-        }
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int c = 0; c < 32; c += 2) pk[c / 2] = pack_bf16(p[32 * hh + c], p[32 * hh + c + 1]);
-          tmem_st16(t_lane + L::T_S + tcol + 16 * hh, pk);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) p[c] = 0.0f;
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = 0u;
-        tmem_st16(t_lane + L::T_S + tcol, pk);
-        tmem_st16(t_lane + L::T_S + tcol + 16, pk);
-      }
+      dkdv_p_tile(t_lane + L::T_S + tcol, sM + st * 128 + wg * 64, qk_scale, tile_on, lane_valid, lane, p);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -1117,32 +1243,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       }
       tc_fence_after();
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t pk[16];
-        if (tile_on) {
-          float dp[32];
-          tmem_load<1>(t_lane + L::T_DP + tcol + 32 * hh, dp);
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 dv4 = d_st[8 * hh + c4];
-            const int c = 4 * c4, pc = 32 * hh + c;
-            // dp - delta as fma(delta, -1, dp): the same single rounding as the subtraction
-            const float2 a = __fmul2_rn(make_float2(p[pc], p[pc + 1]),
-                                        __ffma2_rn(make_float2(dv4.x, dv4.y), neg1, make_float2(dp[c], dp[c + 1])));
-            const float2 b = __fmul2_rn(make_float2(p[pc + 2], p[pc + 3]),
-                                        __ffma2_rn(make_float2(dv4.z, dv4.w), neg1, make_float2(dp[c + 2], dp[c + 3])));
-            pk[c / 2] = pack_bf16(a.x, a.y);
-            pk[c / 2 + 1] = pack_bf16(b.x, b.y);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = 0u;
-        }
-        // dS^T columns [64 w + 16 hh, +16) overlap dP^T columns [64 w, 64 w + 32),
-        // which the first half has read already (hh = 0 writes over columns it read)
-        tmem_st16(t_lane + L::T_DP + tcol + 16 * hh, pk);
-      }
+      dkdv_ds_tile(t_lane + L::T_DP + tcol, sDl + st * 128 + wg * 64, tile_on, lane, p);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -1453,10 +1554,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     // softmax warpgroups of both CTAs: wg w takes query tile w of each step (64
     // columns) for this CTA's 128 keys
     const int wg = warp >> 2;
-    const int r = (warp & 3) * 32 + lane;  // key row within the CTA == TMEM lane
-    const int half = r >> 6;               // this CTA's key tile of the row (warp-uniform)
+    const int r = (warp & 3) * 32 + lane;  // key row of the epilogue == TMEM lane
+    const int half = (warp & 3) >> 1;      // this warp's key tile of the CTA
     const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const bool kvalid = live && ((tile_bits[kt + half] >> (r & 63)) & 1ull);
+    const uint32_t lane_valid = live ? dkdv_lane_valid(tile_bits[kt + half], warp & 3, lane) : 0u;
     const int selbit = 2 * (int)cr + half;
     Union4Iter it;
     it.init(rows, wq);
@@ -1464,58 +1565,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     const float* sM = reinterpret_cast<const float*>(sm + L::M);
     const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
-    const float2 neg1 = make_float2(-1.0f, -1.0f);
     while (it.next_pair(t0, s0, t1, s1)) {
       const int st = n & 1, ph = n & 1;
       const int sel = wg ? s1 : s0;
       const bool tile_on = (sel >> selbit) & 1;  // warp-uniform
-      const bool on = tile_on && kvalid;
       if (!warp_wait(bar(L::B_QFL + st), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax) ||
           !warp_wait(bar(L::B_SF), ph, abort_flag, kErrDkdvSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const float4* m_st = reinterpret_cast<const float4*>(sM + st * 128 + wg * 64);
-      const float4* d_st = reinterpret_cast<const float4*>(sDl + st * 128 + wg * 64);
       const uint32_t tcol = wg * 64;
       float p[64];
-      if (tile_on) {
-        tmem_load<2>(t_lane + L::T_S + tcol, p);
-        if (on) {
-          const float2 sc = make_float2(qk_scale, qk_scale), nr = make_float2(-kRcpLn2, -kRcpLn2);
-#pragma unroll
-          for (int c4 = 0; c4 < 16; ++c4) {
-            const float4 mv = m_st[c4];
-            const float2 n0 = __fmul2_rn(make_float2(mv.x, mv.y), nr);
-            const float2 n1 = __fmul2_rn(make_float2(mv.z, mv.w), nr);
-            const float2 x0 = __ffma2_rn(make_float2(p[4 * c4], p[4 * c4 + 1]), sc, n0);
-            const float2 x1 = __ffma2_rn(make_float2(p[4 * c4 + 2], p[4 * c4 + 3]), sc, n1);
-            p[4 * c4] = ex2(x0.x);
-            p[4 * c4 + 1] = ex2(x0.y);
-            p[4 * c4 + 2] = ex2(x1.x);
-            p[4 * c4 + 3] = ex2(x1.y);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) p[c] = 0.0f;
-        }
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int c = 0; c < 32; c += 2) pk[c / 2] = pack_bf16(p[32 * hh + c], p[32 * hh + c + 1]);
-          tmem_st16(t_lane + L::T_S + tcol + 16 * hh, pk);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) p[c] = 0.0f;
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = 0u;
-        tmem_st16(t_lane + L::T_S + tcol, pk);
-        tmem_st16(t_lane + L::T_S + tcol + 16, pk);
-      }
+      dkdv_p_tile(t_lane + L::T_S + tcol, sM + st * 128 + wg * 64, qk_scale, tile_on, lane_valid, lane, p);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -1525,29 +1587,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
         break;
       }
       tc_fence_after();
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t pk[16];
-        if (tile_on) {
-          float dp[32];
-          tmem_load<1>(t_lane + L::T_DP + tcol + 32 * hh, dp);
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 dv4 = d_st[8 * hh + c4];
-            const int c = 4 * c4, pc = 32 * hh + c;
-            const float2 a = __fmul2_rn(make_float2(p[pc], p[pc + 1]),
-                                        __ffma2_rn(make_float2(dv4.x, dv4.y), neg1, make_float2(dp[c], dp[c + 1])));
-            const float2 b = __fmul2_rn(make_float2(p[pc + 2], p[pc + 3]),
-                                        __ffma2_rn(make_float2(dv4.z, dv4.w), neg1, make_float2(dp[c + 2], dp[c + 3])));
-            pk[c / 2] = pack_bf16(a.x, a.y);
-            pk[c / 2 + 1] = pack_bf16(b.x, b.y);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = 0u;
-        }
-        tmem_st16(t_lane + L::T_DP + tcol + 16 * hh, pk);
-      }
+      dkdv_ds_tile(t_lane + L::T_DP + tcol, sDl + st * 128 + wg * 64, tile_on, lane, p);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
