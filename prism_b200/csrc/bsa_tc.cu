@@ -42,7 +42,6 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
-#include <cstdlib>
 #include <mutex>
 
 #include "prism_common.cuh"
@@ -70,7 +69,6 @@ enum WaitCode : int {
   kErrFwdProducer = 101, kErrFwdMma = 102, kErrFwdSoftmax = 103,
   kErrDkdvProducer = 201, kErrDkdvMma = 202, kErrDkdvSoftmax = 203,
   kErrDqProducer = 301, kErrDqMma = 302, kErrDqSoftmax = 303,
-  kErrDkdvPairExit = 204,
 };
 
 // Union iterator over two bitmap rows (global memory, read through the
@@ -109,18 +107,6 @@ struct UnionIter {
 __device__ __forceinline__ int union_count(const uint32_t* ra, const uint32_t* rb, int wq) {
   int c = 0;
   for (int w = 0; w < wq; ++w) c += __popc(__ldg(ra + w) | __ldg(rb + w));
-  return c;
-}
-
-// Number of tiles in the union of up to four bitmap rows (nullptr = empty row).
-__device__ __forceinline__ int union4_count(const uint32_t* const (&r)[4], int wq) {
-  int c = 0;
-  for (int w = 0; w < wq; ++w) {
-    uint32_t x = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) x |= r[i] ? __ldg(r[i] + w) : 0u;
-    c += __popc(x);
-  }
   return c;
 }
 
@@ -377,11 +363,6 @@ __device__ __forceinline__ void add_key_bias(float (&s)[64], const float* __rest
 
 // Forward one-pass limit on a key tile's exponential sum (see the softmax loop).
 constexpr float kFwdSumLimit = 65536.0f;
-// Forward: every kFwdFmaEvery-th pair of score columns takes its exp2 on the FMA pipe.
-#ifndef PRISM_FWD_FMA_EVERY
-#define PRISM_FWD_FMA_EVERY 0
-#endif
-constexpr int kFwdFmaEvery = PRISM_FWD_FMA_EVERY;
 
 // Scores of keys outside the valid mask (bit c of vb clear) -> -inf.
 __device__ __forceinline__ void mask_keys(float (&s)[64], uint64_t vb) {
@@ -402,55 +383,17 @@ __device__ __forceinline__ float tile_max(const float (&s)[64]) {
   return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
 }
 
-// 2^x for a pair of arguments on the FMA pipe instead of the MUFU unit, from the
-// range reduction 2^x = 2^j * 2^f (j = x rounded to the nearest integer by the
-// 1.5 * 2^23 addition, f = x - j in [-1/2, 1/2]) and the Taylor series of
-// e^t = 2^f at t = f ln 2 through degree 4 (truncation below 4.3e-5 relative at
-// |t| <= ln2 / 2; P is rounded to bf16, 2^-9, after this).  2^j is added to the
-// exponent field.  Arguments are clamped at -126 (any x < -126 gives a value
-// below 2^-125 where exp2 gives 0 or a denormal: invisible next to the row sum,
-// which is >= 1).  Written from the series; checked against ex2.approx on the GPU.
-__device__ __forceinline__ float2 exp2_fma2(float2 x) {
-  constexpr float kC1 = 0.693147180559945f, kC2 = 0.240226506959101f, kC3 = 0.0555041086648216f,
-                  kC4 = 0.00961812910762848f, kRound = 12582912.0f;  // ln2^k / k!, 1.5 * 2^23
-  x.x = fmaxf(x.x, -126.0f);
-  x.y = fmaxf(x.y, -126.0f);
-  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));            // j in the low mantissa bits
-  const float2 j = __fadd2_rn(t, make_float2(-kRound, -kRound));           // exact
-  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);            // x - j, exact
-  float2 p = __ffma2_rn(f, make_float2(kC4, kC4), make_float2(kC3, kC3));
-  p = __ffma2_rn(p, f, make_float2(kC2, kC2));
-  p = __ffma2_rn(p, f, make_float2(kC1, kC1));
-  p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
-  // (bits(t) << 23) == j << 23 (mod 2^32): the constant part of bits(t) shifts out
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
-}
-
 // p = exp2(s * scale - m) for 64 scores as 32 bf16 pairs; returns the sum of the
 // fp32 p (even and odd columns summed separately, then added).  The exponent
 // arguments are packed f32x2 FFMAs (each lane rounds as fmaf does); the sums
 // stay scalar (a packed accumulator costs registers the softmax does not have).
-// kFmaEvery > 0: every kFmaEvery-th pair of columns takes exp2_fma2 instead of
-// the MUFU ex2 -- the forward issues one ex2 per score against two MMAs per key
-// tile, so the MUFU unit alone takes as long as the tensor core; moving a share
-// of the exponentials to the FMA pipe leaves it headroom.
-template <int kFmaEvery>
 __device__ __forceinline__ float exp_tile(const float (&s)[64], float scale, float m, uint32_t (&pk)[32]) {
   const float2 sc = make_float2(scale, scale), nm = make_float2(-m, -m);
   float su0 = 0.f, su1 = 0.f;
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
     const float2 x = __ffma2_rn(make_float2(s[2 * c], s[2 * c + 1]), sc, nm);
-    float p0, p1;
-    if (kFmaEvery > 0 && c % kFmaEvery == kFmaEvery - 1) {
-      const float2 e = exp2_fma2(x);
-      p0 = e.x;
-      p1 = e.y;
-    } else {
-      p0 = ex2(x.x);
-      p1 = ex2(x.y);
-    }
+    const float p0 = ex2(x.x), p1 = ex2(x.y);
     su0 += p0;
     su1 += p1;
     pk[c] = pack_bf16(p0, p1);
@@ -735,7 +678,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tmem_load<2>(t_lane + L::T_S, sv);
           add_key_bias<kKeyBias>(sv, key_bias, t0);
           if (vb0 != ~0ull) mask_keys(sv, vb0);
-          sum0 = exp_tile<kFwdFmaEvery>(sv, qk_scale, m, pk0);
+          sum0 = exp_tile(sv, qk_scale, m, pk0);
         }
         two_pass = __any_sync(0xffffffffu, !(sum0 <= kFwdSumLimit));
       }
@@ -778,7 +721,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tmem_load<2>(t_lane + L::T_S + u * 64, s);
             add_key_bias<kKeyBias>(s, key_bias, u ? t1 : t0);
             if (vb != ~0ull) mask_keys(s, vb);
-            const float t = exp_tile<kFwdFmaEvery>(s, qk_scale, mb, pk);
+            const float t = exp_tile(s, qk_scale, mb, pk);
             if (u) sum1 = t; else sum0 = t;
           }
           // P columns [32 u, 32 u + 32) overlap S columns [0, 64), which pass 2
@@ -797,7 +740,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tmem_load<2>(t_lane + L::T_S + 64, sv);
           add_key_bias<kKeyBias>(sv, key_bias, t1);
           if (vb1 != ~0ull) mask_keys(sv, vb1);
-          sum1 = exp_tile<kFwdFmaEvery>(sv, qk_scale, m, pk1);
+          sum1 = exp_tile(sv, qk_scale, m, pk1);
         }
         const bool need = !(sum1 <= kFwdSumLimit);
         if (__any_sync(0xffffffffu, need)) {
@@ -824,7 +767,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             l = (l + sum0) * alpha;
             sum0 = 0.f;
             m = m_new;
-            sum1 = exp_tile<kFwdFmaEvery>(sv, qk_scale, m, pk1);
+            sum1 = exp_tile(sv, qk_scale, m, pk1);
           }
         }
         // P columns [32, 64) overlap S columns [32, 64) of the first key tile (read)
@@ -1282,361 +1225,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// ======================================================= dK / dV on CTA pairs
-// A (2, 1, 1) cluster computes 256 keys (key tiles 4p..4p+3: the even CTA
-// holds tiles 4p, 4p+1, the odd one 4p+2, 4p+3) with cta_group::2 MMAs of
-// M = 256.  Per step two query tiles (t0, t1) of the union of the four key
-// tiles' transposed rows (N = 128 query columns).  The even CTA stores tile
-// t0's Q / dO rows (the N half of the B operand of S^T = K Q^T and
-// dP^T = V dO^T), the odd CTA tile t1's; each stores the D columns
-// [64 r, 64 r + 64) of both tiles (its N half of the B operand of dK += dS^T Q
-// and dV += P^T dO).  Each CTA therefore reads its own 128 key rows and only
-// half of every B operand from its shared memory: 128 KB of operand reads per
-// step instead of 192 KB on one CTA, for the same TMA bytes -- the one-CTA
-// kernel is bound on the shared-memory port (operand reads + fills ~ the tensor
-// time).  TMEM (each CTA, its 128 key rows): dK, dV, S^T, dP^T (128 columns
-// each).  Warp 9 of the even CTA issues every MMA and waits on barriers of the
-// even CTA that collect both CTAs' arrivals; MMA completions are committed to
-// both CTAs.  Each CTA's loads complete on its own barrier (so each CTA drains
-// its own copies), and a relay lane of its producer warp forwards each
-// completion to the even CTA.  The last step of an odd union repeats tile t0
-// as its second tile with no row selecting it (P = 0 there).  D = 128 only.
-template <int D>
-struct DkdvPairLayout {
-  static_assert(D == 128, "CTA-pair dK/dV: head dim 128");
-  static constexpr int kRing = 2;
-  static constexpr int K = 0;                         // 128 keys x D: 2 sub-buffers of 128 rows
-  static constexpr int V = K + 32768;
-  static constexpr int SLOT = V + 32768;              // kRing ring slots of kSlotBytes
-  // within a slot: QS / DOS = this CTA's query tile (2 sub-buffers of 64 rows);
-  // QK / DOK = D columns [64 r, 64 r + 64) of both tiles (1 sub-buffer of 128 rows)
-  static constexpr int QS = 0, DOS = 16384, QK = 32768, DOK = 49152, kSlotBytes = 65536;
-  static constexpr int M = SLOT + kRing * kSlotBytes;  // kRing x 128 f32 (lse of both tiles)
-  static constexpr int DL = M + kRing * 512;           // kRing x 128 f32 (delta)
-  static constexpr int BAR = DL + kRing * 512;
-  static constexpr int B_KVL = 0, B_KV = 1, B_QFL = 2, B_QF = B_QFL + kRing, B_QE = B_QF + kRing,
-                       B_SF = B_QE + kRing, B_DPF = B_SF + 1, B_PF = B_DPF + 1, B_DSF = B_PF + 1,
-                       B_FIN = B_DSF + 1, B_DRAIN = B_FIN + 1, B_EXIT = B_DRAIN + 1,
-                       NBAR = B_EXIT + 1;
-  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
-  static constexpr int ABORT = TMEM_SLOT + 4;
-  static constexpr size_t kBytes = 1024 + ABORT + 4;
-  static constexpr int T_DK = 0, T_DV = 128, T_S = 256, T_DP = 384;
-};
-
-// Union of up to four bitmap rows (nullptr = empty row), increasing tile order;
-// sel bit i: row i selected the tile.
-struct Union4Iter {
-  const uint32_t* r[4];
-  int wq, wi;
-  uint32_t w[4];
-  __device__ __forceinline__ uint32_t word(int i, int k) const { return r[i] ? __ldg(r[i] + k) : 0u; }
-  __device__ __forceinline__ void init(const uint32_t* const (&rows)[4], int n) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) r[i] = rows[i];
-    wq = n;
-    wi = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) w[i] = n > 0 ? word(i, 0) : 0u;
-  }
-  __device__ __forceinline__ int next(int& sel) {
-    while ((w[0] | w[1] | w[2] | w[3]) == 0u) {
-      if (++wi >= wq) return -1;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = word(i, wi);
-    }
-    const int bit = __ffs(w[0] | w[1] | w[2] | w[3]) - 1;
-    const uint32_t m = 1u << bit;
-    sel = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      sel |= (w[i] & m) ? (1 << i) : 0;
-      w[i] &= ~m;
-    }
-    return wi * 32 + bit;
-  }
-  // the next two tiles; an odd last tile is paired with itself, selected by no row
-  __device__ __forceinline__ bool next_pair(int& t0, int& s0, int& t1, int& s1) {
-    t0 = next(s0);
-    if (t0 < 0) return false;
-    t1 = next(s1);
-    if (t1 < 0) {
-      t1 = t0;
-      s1 = 0;
-    }
-    return true;
-  }
-};
-
-// A bounded wait that ignores the CTA's abort flag: the pair's exit handshake
-// must wait for the peer even after an abort (the peer leaves its loops within
-// one slow-wait check of the error word).
-__device__ __forceinline__ bool exit_wait(uint32_t bar) {
-  const uint64_t t0 = globaltimer();
-  for (;;) {
-    if (mbar_try_sleep_cl(bar, 0u, 20000u)) return true;
-    if (globaltimer() - t0 > 2ull * *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns))
-      return false;
-  }
-}
-
-template <int KSUB, int A_SUB, int B_SUB>
-__device__ __forceinline__ void mma2_kd(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc,
-                                        uint32_t accumulate) {
-  mma2_chain4<2, 4, 6, 2, 4, 6>(d_tmem, a0, b0, idesc, accumulate);
-  if (KSUB > 1) mma2_chain4<2, 4, 6, 2, 4, 6>(d_tmem, a0 + (A_SUB >> 4), b0 + (B_SUB >> 4), idesc, 1u);
-}
-
-template <int D>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
-    dkdv_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                     const float* __restrict__ lse, const float* __restrict__ delta, int64_t Sq,
-                     int64_t Sk, int wq, float qk_scale, float sm_scale,
-                     const uint32_t* __restrict__ bits_k, const uint64_t* __restrict__ tile_bits,
-                     __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv) {
-  using L = DkdvPairLayout<D>;
-  constexpr int R = L::kRing;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = align1024(smem_raw);
-  const uint32_t sb = smem_u32(sm);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t cr = cluster_ctarank();  // 0: the CTA that issues the MMAs
-  const int pair = blockIdx.x >> 1, h = blockIdx.y;
-  const int64_t n_ktiles = Sk / 64;
-  const int kt = 4 * pair + 2 * (int)cr;  // this CTA's first key tile
-  const bool live = kt < n_ktiles;         // n_ktiles is even: kt + 1 exists too
-  const int row_base = (int)((int64_t)h * Sk + (int64_t)kt * 64);
-  const int head_row = (int)((int64_t)h * Sq);
-  auto bar = [&](int i) { return sb + L::BAR + 8 * i; };
-  auto bar0 = [&](int i) { return mapa_shared(sb + L::BAR + 8 * i, 0u); };
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::ABORT);
-  const uint32_t* rows[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    rows[i] = 4 * (int64_t)pair + i < n_ktiles ? bits_k + ((int64_t)h * n_ktiles + 4 * pair + i) * wq : nullptr;
-
-  if (threadIdx.x == 0) {
-    mbar_init(bar(L::B_KVL), 1);
-    mbar_init(bar(L::B_KV), 2);
-    for (int i = 0; i < R; ++i) {
-      mbar_init(bar(L::B_QFL + i), 1);
-      mbar_init(bar(L::B_QF + i), 2);
-      mbar_init(bar(L::B_QE + i), 1);
-    }
-    mbar_init(bar(L::B_SF), 1);
-    mbar_init(bar(L::B_DPF), 1);
-    mbar_init(bar(L::B_PF), 16);
-    mbar_init(bar(L::B_DSF), 16);
-    mbar_init(bar(L::B_FIN), 1);
-    mbar_init(bar(L::B_DRAIN), 1);
-    mbar_init(bar(L::B_EXIT), 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == kBwdMmaWarp) {
-    tmem_alloc_pair(sb + L::TMEM_SLOT, 512);
-    tmem_relinquish_pair();
-    tc_fence_before();
-  }
-  __syncthreads();
-  cluster_sync_all();  // both CTAs' barriers are initialised before any arrival crosses
-  tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + L::TMEM_SLOT);
-
-  if (warp == kBwdProducerWarp) {
-    if (lane == 0) {
-      // ---------------------------------------------------------- loads
-      mbar_expect_tx(bar(L::B_KVL), 2 * 128 * D * 2);
-#pragma unroll
-      for (int s = 0; s < 2; ++s)
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          tma_load_2d(sb + L::K + s * 16384 + rr * 8192, &tm_k, s * 64, row_base + rr * 64, bar(L::B_KVL));
-          tma_load_2d(sb + L::V + s * 16384 + rr * 8192, &tm_v, s * 64, row_base + rr * 64, bar(L::B_KVL));
-        }
-      Union4Iter it;
-      it.init(rows, wq);
-      int n = 0, t0, s0, t1, s1;
-      while (it.next_pair(t0, s0, t1, s1)) {
-        const int st = n & 1;
-        if (n >= R && !mbar_wait(bar(L::B_QE + st), ((n >> 1) - 1) & 1, abort_flag, &g_tc_error,
-                                 kErrDkdvProducer))
-          break;
-        const uint32_t slot = sb + L::SLOT + st * L::kSlotBytes, fb = bar(L::B_QFL + st);
-        mbar_expect_tx(fb, 4 * 2 * 8192 + 2 * 512);
-        const int tm = cr ? t1 : t0;
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          tma_load_2d(slot + L::QS + s * 8192, &tm_q, s * 64, head_row + tm * 64, fb);
-          tma_load_2d(slot + L::DOS + s * 8192, &tm_do, s * 64, head_row + tm * 64, fb);
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int t = u ? t1 : t0;
-          tma_load_2d(slot + L::QK + u * 8192, &tm_q, (int)cr * 64, head_row + t * 64, fb);
-          tma_load_2d(slot + L::DOK + u * 8192, &tm_do, (int)cr * 64, head_row + t * 64, fb);
-          bulk_load(sb + L::M + st * 512 + u * 256, lse + head_row + (int64_t)t * 64, 256, fb);
-          bulk_load(sb + L::DL + st * 512 + u * 256, delta + head_row + (int64_t)t * 64, 256, fb);
-        }
-        ++n;
-      }
-      // drain: every issued copy has landed before the CTA may leave
-      for (int m = (n > R ? n - R : 0); m < n; ++m)
-        mbar_wait(bar(L::B_QFL + (m & 1)), (m >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
-      mbar_wait(bar(L::B_KVL), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
-    } else if (lane == 1) {
-      // ---------------------------------------------------------- relay
-      bool ok = mbar_wait(bar(L::B_KVL), 0, abort_flag, &g_tc_error, kErrDkdvProducer);
-      if (ok) mbar_arrive_cluster(bar0(L::B_KV));
-      const int steps = (union4_count(rows, wq) + 1) >> 1;
-      for (int n = 0; ok && n < steps; ++n) {
-        ok = mbar_wait(bar(L::B_QFL + (n & 1)), (n >> 1) & 1, abort_flag, &g_tc_error, kErrDkdvProducer);
-        if (ok) mbar_arrive_cluster(bar0(L::B_QF + (n & 1)));
-      }
-    }
-  } else if (warp == kBwdMmaWarp) {
-    // Even CTA only.  Issue order as in the one-CTA kernel: S^T(n) | dK(n-1) |
-    // dP^T(n) | dV(n), ..., dK(last).
-    if (cr == 0 && lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_bf16(256, 128, false, false);
-      constexpr uint32_t IDESC_G = idesc_bf16(256, D, false, true);
-      constexpr uint32_t kSlot = L::kSlotBytes >> 4;
-      const uint64_t dK = desc_k_sw128(sb + L::K), dV = desc_k_sw128(sb + L::V),
-                     dQS = desc_k_sw128(sb + L::SLOT + L::QS), dDOS = desc_k_sw128(sb + L::SLOT + L::DOS),
-                     dQK = desc_mn_sw128(sb + L::SLOT + L::QK, 16384),
-                     dDOK = desc_mn_sw128(sb + L::SLOT + L::DOK, 16384);
-      const int steps = (union4_count(rows, wq) + 1) >> 1;
-      auto dk_step = [&](int j) -> bool {
-        const uint32_t js = (uint32_t)j & 1u;
-        if (!mbar_wait_cl(bar(L::B_DSF), js, abort_flag, &g_tc_error, kErrDkdvMma)) return false;
-        tc_fence_after();
-        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP, dQK + js * kSlot, IDESC_G,
-                                                 j > 0 ? 1u : 0u);
-        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DK, tmem + L::T_DP + 64,
-                                                 dQK + js * kSlot + (8192 >> 4), IDESC_G, 1u);
-        mma_commit_pair(bar(L::B_QE + js));
-        return true;
-      };
-      bool ok = mbar_wait_cl(bar(L::B_KV), 0, abort_flag, &g_tc_error, kErrDkdvMma);
-      tc_fence_after();
-      for (int n = 0; ok && n < steps; ++n) {
-        const uint32_t st = (uint32_t)n & 1u;
-        if (!mbar_wait_cl(bar(L::B_QF + st), ((uint32_t)n >> 1) & 1u, abort_flag, &g_tc_error, kErrDkdvMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        mma2_kd<2, 16384, 8192>(tmem + L::T_S, dK, dQS + st * kSlot, IDESC_S, 0u);
-        mma_commit_pair(bar(L::B_SF));
-        if (n > 0 && !dk_step(n - 1)) {
-          ok = false;
-          break;
-        }
-        mma2_kd<2, 16384, 8192>(tmem + L::T_DP, dV, dDOS + st * kSlot, IDESC_S, 0u);
-        mma_commit_pair(bar(L::B_DPF));
-        if (!mbar_wait_cl(bar(L::B_PF), st, abort_flag, &g_tc_error, kErrDkdvMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S, dDOK + st * kSlot, IDESC_G,
-                                                 n > 0 ? 1u : 0u);
-        mma2_ts_chain4<8, 16, 24, 128, 256, 384>(tmem + L::T_DV, tmem + L::T_S + 64,
-                                                 dDOK + st * kSlot + (8192 >> 4), IDESC_G, 1u);
-      }
-      if (ok && steps > 0) dk_step(steps - 1);
-      mma_commit_pair(bar(L::B_FIN));
-      mma_commit_pair_local(bar(L::B_DRAIN));
-      mbar_wait(bar(L::B_DRAIN), 0, abort_flag, &g_tc_error, kErrDkdvMma);
-    }
-  } else {
-    // softmax warpgroups of both CTAs: wg w takes query tile w of each step (64
-    // columns) for this CTA's 128 keys
-    const int wg = warp >> 2;
-    const int r = (warp & 3) * 32 + lane;  // key row of the epilogue == TMEM lane
-    const int half = (warp & 3) >> 1;      // this warp's key tile of the CTA
-    const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const uint32_t lane_valid = live ? dkdv_lane_valid(tile_bits[kt + half], warp & 3, lane) : 0u;
-    const int selbit = 2 * (int)cr + half;
-    Union4Iter it;
-    it.init(rows, wq);
-    int n = 0, t0, s0, t1, s1;
-    bool ok = true;
-    const float* sM = reinterpret_cast<const float*>(sm + L::M);
-    const float* sDl = reinterpret_cast<const float*>(sm + L::DL);
-    while (it.next_pair(t0, s0, t1, s1)) {
-      const int st = n & 1, ph = n & 1;
-      const int sel = wg ? s1 : s0;
-      const bool tile_on = (sel >> selbit) & 1;  // warp-uniform
-      if (!warp_wait(bar(L::B_QFL + st), (n >> 1) & 1, abort_flag, kErrDkdvSoftmax) ||
-          !warp_wait(bar(L::B_SF), ph, abort_flag, kErrDkdvSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t tcol = wg * 64;
-      float p[64];
-      dkdv_p_tile(t_lane + L::T_S + tcol, sM + st * 128 + wg * 64, qk_scale, tile_on, lane_valid, lane, p);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(bar0(L::B_PF));
-      if (!warp_wait(bar(L::B_DPF), ph, abort_flag, kErrDkdvSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      dkdv_ds_tile(t_lane + L::T_DP + tcol, sDl + st * 128 + wg * 64, tile_on, lane, p);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(bar0(L::B_DSF));
-      ++n;
-    }
-    // epilogue: wg 0 writes dK (scaled by sm_scale), wg 1 writes dV
-    if (live) {
-      const int64_t grow = (int64_t)row_base + r;
-      __nv_bfloat16* out = (wg == 0 ? dk : dv) + grow * D;
-      const float scale = wg == 0 ? sm_scale : 1.0f;
-      const int tcolo = wg == 0 ? L::T_DK : L::T_DV;
-      if (ok && n > 0 && warp_wait(bar(L::B_FIN), 0, abort_flag, kErrDkdvSoftmax)) {
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t raw[32], pk2[16];
-          tmem_ld32(t_lane + tcolo + c * 32, raw);
-          tmem_wait_ld_dep(raw);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk2[i] = pack_bf16(u2f(raw[2 * i]) * scale, u2f(raw[2 * i + 1]) * scale);
-          uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk2[4 * i], pk2[4 * i + 1], pk2[4 * i + 2], pk2[4 * i + 3]);
-        }
-      } else if (ok && n == 0) {
-        uint4* a = reinterpret_cast<uint4*>(out);
-#pragma unroll
-        for (int i = 0; i < D / 8; ++i) a[i] = make_uint4(0, 0, 0, 0);
-      }
-    }
-  }
-  tc_fence_before();
-  asm volatile("fence.acq_rel.cluster;" ::: "memory");  // this thread's arrivals at the peer are performed
-  __syncthreads();
-  // Neither CTA frees its TMEM or leaves while the other may still use it: the
-  // even CTA's MMAs have drained (B_DRAIN) before its thread 0 gets here, and
-  // each CTA's softmax and relay arrivals to the even CTA are done.
-  if (threadIdx.x == 0) {
-    mbar_arrive_cluster(mapa_shared(bar(L::B_EXIT), cr ^ 1u));
-    if (!exit_wait(bar(L::B_EXIT))) atomicCAS(&g_tc_error, 0, kErrDkdvPairExit);
-  }
-  __syncthreads();
-  if (warp == kBwdMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, 512);
-  }
-}
-
 // ======================================================================= dQ
 // CTA = 128 queries (tiles 2p, 2p+1); per step a PAIR of key tiles (N = 128):
 // S = Q [K_a; K_b]^T and dP = dO [V_a; V_b]^T in TMEM; the softmax warpgroups
@@ -2071,29 +1659,6 @@ prism_status_t launch_dkdv2(const void* q, const void* k, const void* v, const v
 }
 
 template <int D>
-prism_status_t launch_dkdv_pair(const void* q, const void* k, const void* v, const void* dout,
-                                const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
-                                float sm_scale, const uint32_t* bits_k, const uint64_t* tile_bits,
-                                void* dk, void* dv, cudaStream_t stream) {
-  const int64_t n_ktiles = Sk / 64;
-  const int wq = (int)((Sq / 64 + 31) / 32);  // words per bits_k row (query tiles)
-  const size_t sm = DkdvPairLayout<D>::kBytes > kMinSmem ? DkdvPairLayout<D>::kBytes : kMinSmem;
-  PRISM_CHECK_ARG(sm <= 227 * 1024, "prism_bsa_bwd: shared memory layout exceeds 227 KB");
-  CUtensorMap mq, mk, mv, mdo;
-  PRISM_TRY(make_map(&mq, q, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mk, k, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mv, v, (int64_t)heads * Sk, D, "prism_bsa_bwd_dkdv"));
-  PRISM_TRY(make_map(&mdo, dout, (int64_t)heads * Sq, D, "prism_bsa_bwd_dkdv"));
-  PRISM_CHECK_CUDA(cudaFuncSetAttribute(dkdv_pair_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
-                   "prism_bsa_bwd: smem attribute");
-  dkdv_pair_kernel<D><<<dim3((unsigned)(2 * ((n_ktiles + 3) / 4)), heads), kBwdThreads, sm, stream>>>(
-      mq, mk, mv, mdo, lse, delta, Sq, Sk, wq, sm_scale * kRcpLn2, sm_scale, bits_k, tile_bits,
-      (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
-  PRISM_CHECK_LAUNCH("prism_bsa_bwd_dkdv");
-  return PRISM_OK;
-}
-
-template <int D>
 prism_status_t launch_dq(const void* q, const void* k, const void* v, const void* dout,
                          const float* lse, const float* delta, int heads, int64_t Sq, int64_t Sk,
                          float sm_scale, const uint32_t* bits_q, const uint64_t* tile_bits,
@@ -2233,16 +1798,8 @@ static prism_status_t bwd_dkdv_qk(const void* q, const void* k, const void* v, c
   PRISM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dout) && aligned16(dk) &&
                       aligned16(dv) && aligned16(lse) && aligned16(delta),
                   "prism_bsa_bwd_dkdv: tensors must be 16-byte aligned");
-  if (D == 128) {
-    static const bool pair = [] {
-      const char* e = getenv("PRISM_DKDV_PAIR");
-      return e != nullptr && e[0] == '1';
-    }();
-    if (pair)
-      return tc::launch_dkdv_pair<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
-    return tc::launch_dkdv2<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
-  }
-  return tc::launch_dkdv2<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
+  return D == 128 ? tc::launch_dkdv2<128>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream)
+                  : tc::launch_dkdv2<64>(q, k, v, dout, lse, delta, heads, Sq, Sk, sm_scale, bits_k, tile_bits, dk, dv, stream);
 }
 
 static prism_status_t bwd_dq_qk(const void* q, const void* k, const void* v, const void* dout,

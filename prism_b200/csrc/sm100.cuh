@@ -285,134 +285,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
-// ------------------------------------------------------------ CTA pairs
-// Two CTAs of a (2, 1, 1) cluster sharing tcgen05 MMAs (cta_group::2): the MMA
-// is M = 256 with rows 0-127 in the even CTA's TMEM / shared memory and rows
-// 128-255 in the odd CTA's; a B operand of N columns is stored as N/2 columns
-// in each CTA's shared memory at the same offset.  One thread of the even CTA
-// issues every MMA.  No multicast loads: each CTA loads its own operands.
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
-  return r;
-}
-// arrive on an mbarrier of any CTA of the cluster (release at cluster scope)
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// try_wait with acquire at cluster scope (the barrier receives arrivals from the peer CTA)
-__device__ __forceinline__ bool mbar_try_sleep_cl(uint32_t bar, uint32_t parity, uint32_t ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(ns)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_try_cl(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                             int* err, int code) {
-  if (mbar_try_cl(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i)
-      if (mbar_try_sleep_cl(bar, parity, 20000u)) return true;
-    if (*abort_flag) return false;
-    if (*reinterpret_cast<volatile int*>(err) != 0) {
-      *abort_flag = 1;
-      return false;
-    }
-    if (globaltimer() - t0 > *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns)) {
-      *abort_flag = 1;
-      atomicCAS(err, 0, code);
-      return false;
-    }
-  }
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-// arrive once on the mbarrier at this offset in both CTAs of the pair when all
-// previously issued MMAs of this thread have completed
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
-  asm volatile(
-      "{\n .reg .b16 m;\n mov.b16 m, 3;\n"
-      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n}\n" ::"r"(
-          bar)
-      : "memory");
-}
-// the same, arriving only on this CTA's barrier
-__device__ __forceinline__ void mma_commit_pair_local(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-// cta_group::2 forms of mma_chain4 / mma_ts_chain4 (see there)
-template <int A1, int A2, int A3, int B1, int B2, int B3>
-__device__ __forceinline__ void mma2_chain4(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p0, p1;\n .reg .b64 a1, a2, a3, b1, b2, b3;\n"
-      " setp.ne.b32 p0, %4, 0;\n setp.eq.b32 p1, %4, %4;\n"
-      " add.s64 a1, %1, %5;\n add.s64 a2, %1, %6;\n add.s64 a3, %1, %7;\n"
-      " add.s64 b1, %2, %8;\n add.s64 b2, %2, %9;\n add.s64 b3, %2, %10;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], a1, b1, %3, p1;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], a2, b2, %3, p1;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], a3, b3, %3, p1;\n}\n" ::"r"(d_tmem),
-      "l"(a0), "l"(b0), "r"(idesc), "r"(accumulate), "n"(A1), "n"(A2), "n"(A3), "n"(B1), "n"(B2),
-      "n"(B3)
-      : "memory");
-}
-template <int A1, int A2, int A3, int B1, int B2, int B3>
-__device__ __forceinline__ void mma2_ts_chain4(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0,
-                                               uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p0, p1;\n .reg .b32 a1, a2, a3;\n .reg .b64 b1, b2, b3;\n"
-      " setp.ne.b32 p0, %4, 0;\n setp.eq.b32 p1, %4, %4;\n"
-      " add.s32 a1, %1, %5;\n add.s32 a2, %1, %6;\n add.s32 a3, %1, %7;\n"
-      " add.s64 b1, %2, %8;\n add.s64 b2, %2, %9;\n add.s64 b3, %2, %10;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], b1, %3, p1;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], [a2], b2, %3, p1;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], [a3], b3, %3, p1;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate), "n"(A1), "n"(A2), "n"(A3), "n"(B1),
-      "n"(B2), "n"(B3)
-      : "memory");
-}
-
 // ------------------------------------------------------- UMMA descriptors
 // Shared-memory matrix descriptor (sm_100 format): start address >> 4 in
 // bits [0,14), leading byte offset >> 4 in [16,30), stride byte offset >> 4
