@@ -331,6 +331,11 @@ prism_status_t prism_bsa_fwd_keybias(const void* q, const void* k, const void* v
  * bias_rectification_triton.py:270-292); other rows out = O_spa.  O given as bf16
  * plus an optional bf16 residual (o_lo of the forward).  Rows [heads, S, D].
  *
+ * prism_rectified_contract: o_ncri [heads, nq, D] fp32 = a_rect [heads, nq, nk] x
+ * v_cmp [heads, nk, D] fp32 (the pooled values of the key chunks), one fmaf per term
+ * in increasing key chunk order (deterministic): the A_rect V_cmp product of
+ * _rectified_correction_fwd_kernel (bias_rectification_triton.py:9-95).
+ *
  * prism_rectified_apply: rows r < seq_q: out = R[h][a] O_spa + o_ncri[h][a][:]
  * (o_ncri [heads, nq, D] fp32 = a_rect V_cmp); other rows out = O_spa
  * (_rectified_correction_fwd_kernel, bias_rectification_triton.py:9-95). */
@@ -349,9 +354,25 @@ prism_status_t prism_taylor_merge(const void* o_spa, const void* o_spa_lo, const
                                   const void* o_t, const void* o_t_lo, const float* lse_t,
                                   const float* M, const float* tau, int heads, int64_t S, int64_t seq_q,
                                   int chunk_q, int D, void* out, cudaStream_t stream);
+prism_status_t prism_rectified_contract(const float* a_rect, const float* v_cmp, int heads, int nq, int nk,
+                                        int D, float* o_ncri, cudaStream_t stream);
 prism_status_t prism_rectified_apply(const void* o_spa, const void* o_spa_lo, const float* R,
                                      const float* o_ncri, int heads, int64_t S, int64_t seq_q, int chunk_q,
                                      int D, void* out, cudaStream_t stream);
+
+/* Dense GEMM on the tensor cores for the layer's projections (self.q / k / v / o,
+ * wan_video_dit.py:699-701, 841) and their gradients; replaces F.linear / cuBLAS:
+ *   C[M, N] (bf16, row stride ldc) = sum_k A(m, k) B(n, k) (+ bias[n] fp32; with
+ *   accumulate != 0 the old C is added), fp32 accumulation.
+ * A is K-major (A(m, k) = a[m * lda + k]) or, with a_mn_major, MN-major
+ * (a[k * lda + m]); B likewise.  Forward y = x W^T: both K-major; dx = dy W: A
+ * K-major, B MN-major; dW = dy^T x: both MN-major.  N, lda, ldb, ldc multiples of 8;
+ * 16-byte aligned tensors.  Persistent kernel: 128 x 256 tiles, 4-stage TMA ring,
+ * double-buffered TMEM accumulators.  Bounded waits report through
+ * prism_device_status (codes 401-403). */
+prism_status_t prism_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
+                               int b_mn_major, int M, int N, int K, const float* bias, void* c,
+                               int64_t ldc, int accumulate, cudaStream_t stream);
 
 /* Producer side of the self-attention (SelfAttention.forward,
  * wan_video_dit.py:699-705, 764-787), one pass per token row after the q / k / v

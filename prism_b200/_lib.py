@@ -25,6 +25,7 @@ SIGNATURES = {
     "prism_device_status": (_I, []),
     "prism_test_fwd_withheld_load": (_I, [_P, _P, _P, _I64, _I, _F, _P, _P, _P, _P, ctypes.c_uint64, _P]),
     "prism_token_norms": (_I, [_P, _I64, _I, _P, _P]),
+    "prism_gemm_bf16": (_I, [_P, _I64, _I, _P, _I64, _I, _I, _I, _I, _P, _P, _I64, _I, _P]),
     "prism_zone_stats_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "prism_zone_stats": (_I, [_P, _I, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "prism_shape_select": (_I, [_P, _P, _P, _I, _I, _I, _I, _F, _F, _F, _P, _P, _P, _P]),
@@ -50,6 +51,7 @@ SIGNATURES = {
     "prism_key_log_bias": (_I, [_P, _I, _I, _I, _F, _P, _P]),
     "prism_rows_to_bf16": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "prism_taylor_merge": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _I, _P, _P]),
+    "prism_rectified_contract": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "prism_rectified_apply": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I, _I, _P, _P]),
     "prism_norm_rope_pack": (_I, [_P, _I64, _I64, _I64, _I, _I, _I, _I, _P, _F, _P, _I, _P, _P, _P]),
     "prism_norm_rope_pack_bwd_workspace_bytes": (_SZ, [_I64, _I, _I]),
@@ -78,7 +80,8 @@ KERNELS = {
     "prism_guidance_scale": 1, "prism_pool_chunks": 1, "prism_chunk_scores": 1,
     "prism_bsa_fwd_keybias": 1, "prism_correction_stats": 1, "prism_taylor_prep": 1,
     "prism_key_log_bias": 1, "prism_rows_to_bf16": 1, "prism_taylor_merge": 1,
-    "prism_rectified_apply": 1, "prism_norm_rope_pack": 1, "prism_norm_rope_pack_bwd": 4,
+    "prism_rectified_apply": 1, "prism_rectified_contract": 1, "prism_norm_rope_pack": 1,
+    "prism_gemm_bf16": 1, "prism_norm_rope_pack_bwd": 4,
 }
 launch_count = 0
 

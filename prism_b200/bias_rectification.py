@@ -19,9 +19,9 @@ them, as the reference's reshape(-1) does).
 
 Everything runs in libprism_bsa.so: the selection and sparse forward of the
 uniform path, the chunk statistics (prism_correction_stats), the pooled-key pass
-as the forward kernel's key-bias form (prism_bsa_fwd_keybias) and the merges;
-the unselected mass times V_cmp of the rectified form is a batched fp32 GEMM
-(torch.bmm, cuBLAS).  Like the reference's fused kernels this path is for
+as the forward kernel's key-bias form (prism_bsa_fwd_keybias), the unselected
+mass times V_cmp of the rectified form (prism_rectified_contract, fp32 in a fixed
+order) and the merges.  Like the reference's fused kernels this path is for
 inference: it raises when gradients are required.
 """
 from __future__ import annotations
@@ -73,7 +73,7 @@ def corrected_forward(plan: SparsePlan, q_re, k_re, v_re, kind: str, alpha_f: fl
                                                 want_a_rect=kind == "rectified")
     v_cmp = ops.pool_chunks(v_re, seq_k, ck, bits=plan.tile_bits)  # _pool_v, masked mean
     if kind == "rectified":
-        o_ncri = torch.bmm(a_rect, v_cmp)  # [heads, nq, D] fp32
+        o_ncri = ops.rectified_contract(a_rect, v_cmp)  # [heads, nq, D] fp32
         return ops.rectified_apply(o, o_lo, R, o_ncri, seq_q, cq)
     tau = global_quantile_across_sp(M, alpha_f)
     nk = seq_k // ck

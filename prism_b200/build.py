@@ -27,6 +27,7 @@ SOURCES = {
     "correction_kernels.cu": ["-fmad=false"],
     "producer_kernels.cu": ["-fmad=false"],
     "bsa_tc.cu": [],
+    "gemm_tc.cu": [],
 }
 
 

@@ -1686,6 +1686,8 @@ prism_status_t launch_dq(const void* q, const void* k, const void* v, const void
 
 using namespace prism;
 
+int prism_gemm_device_status_internal(void);
+
 extern "C" {
 
 int prism_device_status(void) {
@@ -1695,7 +1697,9 @@ int prism_device_status(void) {
     const int zero = 0;
     cudaMemcpyToSymbol(tc::g_tc_error, &zero, sizeof(int));
   }
-  return v;
+  const int g = prism_gemm_device_status_internal();  // the GEMM kernels' word (gemm_tc.cu)
+  if (g < 0) return -1;
+  return v != 0 ? v : g;
 }
 
 // Row indices of the [heads * S, D] views are 32-bit TMA coordinates.

@@ -234,6 +234,62 @@ __global__ void taylor_merge_kernel(const __nv_bfloat16* __restrict__ o_spa,
   }
 }
 
+// o_ncri[h][a][d] = sum over key chunks j (in order) of a_rect[h][a][j] * v_cmp[h][j][d]:
+// the unselected chunks' pooled-softmax mass times their pooled values (the A_rect
+// V_cmp of _rectified_correction_fwd_kernel, bias_rectification_triton.py:9-95).
+// CTA = 64 q chunks x 64 channels of one head, 256 threads with 4 x 4 outputs each;
+// the reduction runs over kRectK key chunks at a time staged in shared memory, one
+// fmaf per (output, j) in increasing j, so the result is deterministic.
+constexpr int kRectTile = 64, kRectK = 32;
+__global__ void __launch_bounds__(256) rect_contract_kernel(const float* __restrict__ a_rect,
+                                                            const float* __restrict__ v_cmp, int nq,
+                                                            int nk, int D, float* __restrict__ out) {
+  __shared__ float As[kRectK][kRectTile + 4];  // [j][a]
+  __shared__ float Vs[kRectK][kRectTile + 4];  // [j][d]
+  const int a0 = blockIdx.y * kRectTile, d0 = blockIdx.x * kRectTile, h = blockIdx.z;
+  const float* ah = a_rect + (int64_t)h * nq * nk;
+  const float* vh = v_cmp + (int64_t)h * nk * D;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  for (int j0 = 0; j0 < nk; j0 += kRectK) {
+    for (int i = threadIdx.x; i < kRectK * kRectTile; i += blockDim.x) {
+      const int r = i / kRectK, j = i % kRectK;  // A: row r (q chunk), column j (coalesced in j)
+      As[j][r] = (a0 + r < nq && j0 + j < nk) ? ah[(int64_t)(a0 + r) * nk + j0 + j] : 0.0f;
+      const int jj = i / kRectTile, c = i % kRectTile;  // V: row jj (key chunk), channel c
+      Vs[jj][c] = (j0 + jj < nk && d0 + c < D) ? vh[(int64_t)(j0 + jj) * D + d0 + c] : 0.0f;
+    }
+    __syncthreads();
+    const int jn = min(kRectK, nk - j0);
+    for (int j = 0; j < jn; ++j) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[j][ty * 4 + i];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) bv[k] = Vs[j][tx * 4 + k];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[i][k] = __fmaf_rn(av[i], bv[k], acc[i][k]);
+    }
+    __syncthreads();
+  }
+  float* oh = out + (int64_t)h * nq * D;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int a = a0 + ty * 4 + i;
+    if (a >= nq) continue;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = d0 + tx * 4 + k;
+      if (d < D) oh[(int64_t)a * D + d] = acc[i][k];
+    }
+  }
+}
+
 // out = R(h, a) O_spa + O_ncri(h, a) (_rectified_correction_fwd_kernel,
 // bias_rectification_triton.py:9-95); rows in chunk order past seq_q copy O_spa.
 __global__ void rectified_apply_kernel(const __nv_bfloat16* __restrict__ o_spa,
@@ -345,6 +401,18 @@ prism_status_t prism_rectified_apply(const void* o_spa, const void* o_spa_lo, co
       (const __nv_bfloat16*)o_spa, (const __nv_bfloat16*)o_spa_lo, R, o_ncri, heads, S, seq_q, chunk_q,
       (int)(seq_q / chunk_q), D, (__nv_bfloat16*)out);
   PRISM_CHECK_LAUNCH("prism_rectified_apply");
+  return PRISM_OK;
+}
+
+prism_status_t prism_rectified_contract(const float* a_rect, const float* v_cmp, int heads, int nq, int nk,
+                                        int D, float* o_ncri, cudaStream_t stream) {
+  PRISM_CHECK_ARG(a_rect && v_cmp && o_ncri, "prism_rectified_contract: null pointer");
+  PRISM_CHECK_ARG(heads >= 1 && heads <= 65535 && nq >= 1 && nk >= 1 && D >= 1,
+                  "prism_rectified_contract: bad sizes");
+  rect_contract_kernel<<<dim3((unsigned)((D + kRectTile - 1) / kRectTile),
+                              (unsigned)((nq + kRectTile - 1) / kRectTile), heads),
+                         256, 0, stream>>>(a_rect, v_cmp, nq, nk, D, o_ncri);
+  PRISM_CHECK_LAUNCH("prism_rectified_contract");
   return PRISM_OK;
 }
 

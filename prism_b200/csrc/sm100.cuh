@@ -61,10 +61,10 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 // wait, so one failure does not cost every CTA of the grid the full limit.
 // The word stays set until the host reads it (prism_device_status).  The
 // limit is 2 s; only the test entry prism_test_fwd_withheld_load shortens it,
-// for its own launch (stream-ordered writes before and after it).  This
-// header is compiled into one translation unit (bsa_tc.cu).
+// for its own launch (stream-ordered writes before and after it).  Each
+// translation unit that includes this header has its own copy.
 constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;  // 2 s
-__device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
+static __device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 // try_wait with a suspend-time hint: the thread sleeps until the phase
 // completes or about `ns` nanoseconds pass, instead of polling the barrier

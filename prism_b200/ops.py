@@ -325,6 +325,19 @@ def taylor_merge(o_spa, o_spa_lo, lse_spa, o_t, o_t_lo, lse_t, M, tau, seq_q: in
     return out
 
 
+def rectified_contract(a_rect: torch.Tensor, v_cmp: torch.Tensor) -> torch.Tensor:
+    """a_rect [heads, nq, nk] fp32 x v_cmp [heads, nk, D] fp32 -> [heads, nq, D] fp32
+    (fixed summation order over the key chunks)."""
+    _check_cuda(a_rect, v_cmp)
+    heads, nq, nk = a_rect.shape
+    D = v_cmp.shape[-1]
+    a = a_rect.contiguous()
+    v = v_cmp.contiguous()
+    out = torch.empty(heads, nq, D, dtype=torch.float32, device=a_rect.device)
+    _lib.call("prism_rectified_contract", _p(a), _p(v), heads, nq, nk, D, _p(out), _stream(a_rect))
+    return out
+
+
 def rectified_apply(o_spa, o_spa_lo, R, o_ncri, seq_q: int, chunk_q: int, out=None):
     _check_cuda(o_spa, R, o_ncri)
     heads, S, D = o_spa.shape
@@ -332,6 +345,31 @@ def rectified_apply(o_spa, o_spa_lo, R, o_ncri, seq_q: int, chunk_q: int, out=No
     oc = o_ncri.contiguous()
     _lib.call("prism_rectified_apply", _p(o_spa), _p(o_spa_lo), _p(R), _p(oc), heads, S, seq_q,
               chunk_q, D, _p(out), _stream(o_spa))
+    return out
+
+
+# ------------------------------------------------------------- projections
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False,
+         M: Optional[int] = None, N: Optional[int] = None, K: Optional[int] = None,
+         bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+         accumulate: bool = False) -> torch.Tensor:
+    """prism_gemm_bf16: C[M, N] (+)= sum_k A(m, k) B(n, k) (+ bias).  a, b: 2D bf16
+    tensors with unit column stride; K-major A is [M, K] (a_mn: [K, M]), K-major B is
+    [N, K] (b_mn: [K, N]).  M / N / K default to the shapes those layouts imply.
+    out: a bf16 [M, N] tensor with unit column stride (allocated when None)."""
+    _check_cuda(a, b, bias, out)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("gemm expects bf16 operands")
+    if a.stride(1) != 1 or b.stride(1) != 1:
+        raise ValueError("gemm operands need unit column stride")
+    M = (a.shape[1] if a_mn else a.shape[0]) if M is None else M
+    K = (a.shape[0] if a_mn else a.shape[1]) if K is None else K
+    N = (b.shape[1] if b_mn else b.shape[0]) if N is None else N
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    bf = None if bias is None else bias.to(torch.float32).contiguous()
+    _lib.call("prism_gemm_bf16", _p(a), a.stride(0), int(a_mn), _p(b), b.stride(0), int(b_mn), M, N, K,
+              _p(bf), _p(out), out.stride(0), int(accumulate), _stream(a))
     return out
 
 

@@ -10,7 +10,8 @@ Reference sequence (per layer, per rank):
   all_to_all_4D back -> drop padded heads -> flatten -> self.o(x)         (:824-841)
 
 Here:
-* the projections are cuBLAS GEMMs (plain library GEMMs);
+* the projections run on the repository's tensor-core GEMM (prism_b200.linear,
+  prism_gemm_bf16), forward and backward;
 * RMSNorm + RoPE + the all-to-all pack are one pass per token row
   (``prism_norm_rope_pack``), writing each head straight into the send layout
   [P, S/P, H/P, D], and the backward is the mirror pass (``prism_norm_rope_pack_bwd``):
@@ -21,7 +22,7 @@ Here:
   the attention reads the received buffer in place;
 * the output projection reads the inverse all-to-all's receive buffer in place:
   out = sum over source ranks p of recv[p] W_o[:, heads of p]^T, P accumulating
-  GEMMs instead of an unpack copy plus one GEMM.
+  GEMMs instead of an unpack copy plus one GEMM (prism_b200.linear.o_proj_packed).
 
 ``rope_table`` restates ``precompute_freqs_cis_3d`` (:125-139) and the per-token
 assembly of :1183-1187 as a (cos, sin) float64 table; the kernels take it split into
@@ -37,6 +38,7 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
+from .linear import linear, o_proj_packed
 from .communications import (HeadsToWire, WireToHeads, live_ranks, sp_chunk_sizes,
                              sp_num_local_real_heads, sp_pad_num_heads)
 from .parallel_states import get_sequence_parallel_state, nccl_info
@@ -117,26 +119,6 @@ def norm_rope_pack(q_lin, k_lin, v_lin, gamma_q, gamma_k, eps: float, rope_cs, h
                                hp, S_pack)
 
 
-def o_proj_packed(recv: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], heads: int,
-                  S_local: int) -> torch.Tensor:
-    """self.o of the rows held in the inverse all-to-all's receive buffer
-    recv [P, S_pack, hp, D] (source rank p holds heads [p*hp, p*hp + hp), padded
-    heads h >= heads dropped): sum over p of recv[p] W[:, heads of p]^T + bias."""
-    P, S_pack, hp, D = recv.shape
-    out = None
-    for p in range(P):
-        h0, h1 = p * hp, min(p * hp + hp, heads)
-        if h1 <= h0:
-            continue
-        a = recv[p, :S_local, : h1 - h0].reshape(S_local, (h1 - h0) * D)
-        w = weight[:, h0 * D:h1 * D]
-        if out is None:
-            out = F.linear(a, w, bias)
-        else:
-            out = out.addmm(a, w.t())
-    return out
-
-
 def fused_self_attention(x: torch.Tensor, rope_cs: torch.Tensor, params: dict, num_heads: int,
                          grid_size: Tuple[int, int, int], *, attention: str = "dynamic",
                          full_seq_len: Optional[int] = None,
@@ -157,9 +139,9 @@ def fused_self_attention(x: torch.Tensor, rope_cs: torch.Tensor, params: dict, n
     assert b == 1, "batch 1"
     D = dim // num_heads
     xs = x[0]
-    q_lin = F.linear(xs, params["q_weight"], params.get("q_bias"))
-    k_lin = F.linear(xs, params["k_weight"], params.get("k_bias"))
-    v_lin = F.linear(xs, params["v_weight"], params.get("v_bias"))
+    q_lin = linear(xs, params["q_weight"], params.get("q_bias"))
+    k_lin = linear(xs, params["k_weight"], params.get("k_bias"))
+    v_lin = linear(xs, params["v_weight"], params.get("v_bias"))
     sp = get_sequence_parallel_state() and nccl_info.sp_size > 1
     P = nccl_info.sp_size if sp else 1
     padded = sp_pad_num_heads(num_heads, P)

@@ -150,3 +150,17 @@ def test_correction_refuses_grad(cuda):
     q = torch.zeros(1, 2, 512, 64, dtype=torch.bfloat16, device=cuda, requires_grad=True)
     with pytest.raises(NotImplementedError):
         bsa_taylor_sparse_attn(q, q, q, 64, 64, 0.5, None, 0.125)
+
+
+def test_rectified_contraction_fixed_order(cuda):
+    """prism_rectified_contract (the Rectified form's A_rect V_cmp) against a float64
+    product, on sizes that leave partial tiles in every dimension, and run-to-run
+    bit-identical."""
+    g = torch.Generator().manual_seed(21)
+    heads, nq, nk, D = 3, 97, 150, 128
+    a = (torch.rand(heads, nq, nk, generator=g) * (torch.rand(heads, nq, nk, generator=g) < 0.4)).to(cuda)
+    v = torch.randn(heads, nk, D, generator=g).to(cuda)
+    got = ops.rectified_contract(a, v)
+    ref = torch.bmm(a.double(), v.double())
+    assert float((got.double() - ref).abs().max()) <= 1e-5 * max(1.0, float(ref.abs().max()))
+    assert torch.equal(got, ops.rectified_contract(a, v))

@@ -20,6 +20,7 @@ from helpers import bits, load_fixture, rel_l2
 from inputs import PRODUCER_CASES, make_producer_inputs
 from oracle import oracle as O
 from prism_b200 import ops, run_bsa_uniform
+from prism_b200.linear import linear
 from prism_b200.producer import (fused_self_attention, norm_rope_pack, o_proj_packed, rope_table,
                                  rope_table_ff)
 
@@ -142,19 +143,31 @@ def test_fused_layer_equals_unfused_p1(cuda):
             p.grad = None
     # unfused composition with the same kernels: projections, norm_rope_pack at P = 1,
     # attention, output projection as one GEMM
-    xb = x.clone().requires_grad_(True)
-    ql, kl, vl = (F.linear(xb[0], params[n + "_weight"], params[n + "_bias"]) for n in "qkv")
-    q, k, v = norm_rope_pack(ql, kl, vl, params["norm_q_weight"], params["norm_k_weight"], 1e-6, cs,
-                             heads)
-    xo = run_bsa_uniform(q.view(1, S, heads, D), k.view(1, S, heads, D), v.view(1, S, heads, D), grid,
-                         layout="bshd", **ATTN)
-    ref = F.linear(xo.reshape(S, dim), params["o_weight"], params["o_bias"]).unsqueeze(0)
-    ref.backward(gout)
+    def unfused(proj):
+        xb = x.clone().requires_grad_(True)
+        ql, kl, vl = (proj(xb[0], params[n + "_weight"], params[n + "_bias"]) for n in "qkv")
+        q, k, v = norm_rope_pack(ql, kl, vl, params["norm_q_weight"], params["norm_k_weight"], 1e-6,
+                                 cs, heads)
+        xo = run_bsa_uniform(q.view(1, S, heads, D), k.view(1, S, heads, D), v.view(1, S, heads, D),
+                             grid, layout="bshd", **ATTN)
+        ref = proj(xo.reshape(S, dim), params["o_weight"], params["o_bias"]).unsqueeze(0)
+        ref.backward(gout)
+        grads = {n: p.grad.clone() for n, p in params.items() if torch.is_tensor(p)}
+        for p in params.values():
+            if torch.is_tensor(p):
+                p.grad = None
+        return ref, xb.grad, grads
+
+    ref, gxb, gb = unfused(linear)
     assert torch.equal(out, ref)
-    assert torch.equal(gx, xb.grad)
-    for n, p in params.items():
-        if torch.is_tensor(p):
-            assert torch.equal(ga[n], p.grad), n
+    assert torch.equal(gx, gxb)
+    for n in ga:
+        assert torch.equal(ga[n], gb[n]), n
+    # the repository's GEMM against cuBLAS (F.linear) through the whole layer: bf16 rounding
+    ref2, gx2, g2 = unfused(F.linear)
+    for name, a, b in [("out", out, ref2), ("dx", gx, gx2)] + [(n, ga[n], g2[n]) for n in ga]:
+        a, b = a.float(), b.float()
+        assert float((a - b).norm() / b.norm()) <= 1e-2, name
 
 
 def test_fused_layer_two_rank_emulation(cuda):
@@ -179,7 +192,7 @@ def test_fused_layer_two_rank_emulation(cuda):
             send = []
             for r in range(P):
                 xr = x[0, rows[r]]
-                ql, kl, vl = (F.linear(xr, params[n + "_weight"], params[n + "_bias"]) for n in "qkv")
+                ql, kl, vl = (linear(xr, params[n + "_weight"], params[n + "_bias"]) for n in "qkv")
                 send.append(norm_rope_pack(ql, kl, vl, params["norm_q_weight"], params["norm_k_weight"],
                                            1e-6, cs[rows[r]].contiguous(), heads, P, hp, S_pack))
             recv = [[torch.stack([send[p][t][r] for p in range(P)]) for t in range(3)] for r in range(P)]

@@ -12,13 +12,24 @@ import torch
 from test_sp_gloo import _init, _run
 
 
+def _k_split_projection(recv, W, b, heads, S_local):
+    """The K-split form prism_b200.linear.o_proj_packed computes on the GPU: the sum
+    over source ranks p of recv[p] W[:, heads of p]^T (padded heads skipped), + b."""
+    P, S_pack, hp, D = recv.shape
+    out = b.expand(S_local, W.shape[0]).clone()
+    for p in range(P):
+        h0, h1 = p * hp, min(p * hp + hp, heads)
+        if h1 > h0:
+            out = out + recv[p, :S_local, : h1 - h0].reshape(S_local, -1) @ W[:, h0 * D:h1 * D].t()
+    return out
+
+
 def _worker(rank, world, port, q):
     try:
         _init(rank, world, port)
         from prism_b200 import parallel_states as ps
         from prism_b200.communications import sp_chunk_sizes, sp_pad_num_heads
         from prism_b200.communications import HeadsToWire, WireToHeads
-        from prism_b200.producer import o_proj_packed
         ps.initialize_sequence_parallel()
         group = ps.nccl_info.sp_group
         g = torch.Generator().manual_seed(0)
@@ -48,7 +59,7 @@ def _worker(rank, world, port, q):
             assert torch.equal(seq[:, hh], want), (rank, hh)
         # inverse exchange of the (identity) attention output, then the K-split projection
         recv2 = HeadsToWire.apply(seq4, group, S).squeeze(1)    # [P, S_pack, hp, D]
-        out = o_proj_packed(recv2, W, b, H, sizes[rank])
+        out = _k_split_projection(recv2, W, b, H, sizes[rank])
         ref = mine.reshape(sizes[rank], H * D) @ W.t() + b
         assert torch.allclose(out, ref, rtol=1e-12, atol=1e-12)
         # adjoint: the gradient of sum(out * w) reaches the send buffer's real entries as
