@@ -461,6 +461,78 @@ def run_producer(args):
     print(json.dumps(line), flush=True)
 
 
+def run_gemm(args):
+    """--path gemm: the self-attention layer's projection GEMMs on the repository's
+    tensor-core GEMM (prism_gemm_bf16) at the 720p shape -- x [75,600, 5,120] times
+    W [5,120, 5,120]: forward y = x W^T + b, dgrad dx = dy W, wgrad dW = dy^T x --
+    against torch.matmul (cuBLAS) on the same operands; effective TFLOPS =
+    2 M N K per GEMM / CUDA-event time, fraction of the measured burst bf16 peak."""
+    import torch
+    from prism_b200 import _lib, ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.load(build_if_missing=False)
+    grid, H, D = CONFIG["grid"], CONFIG["heads"], CONFIG["head_dim"]
+    M, C = grid[0] * grid[1] * grid[2], H * D
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(M, C, generator=gen, device=dev).to(torch.bfloat16)
+    W = (torch.randn(C, C, generator=gen, device=dev) / C ** 0.5).to(torch.bfloat16)
+    b = torch.randn(C, generator=gen, device=dev)
+    dy = torch.randn(M, C, generator=gen, device=dev).to(torch.bfloat16)
+    y, dx, dW = (torch.empty(M, C, dtype=torch.bfloat16, device=dev),
+                 torch.empty(M, C, dtype=torch.bfloat16, device=dev),
+                 torch.empty(C, C, dtype=torch.bfloat16, device=dev))
+    ours = {"forward": lambda: ops.gemm(x, W, bias=b, out=y),
+            "dgrad": lambda: ops.gemm(dy, W, b_mn=True, out=dx),
+            "wgrad": lambda: ops.gemm(dy, x, a_mn=True, b_mn=True, out=dW)}
+    bf = b.to(torch.bfloat16)
+    cublas = {"forward": lambda: torch.addmm(bf, x, W.t(), out=y),
+              "dgrad": lambda: torch.mm(dy, W, out=dx),
+              "wgrad": lambda: torch.mm(dy.t(), x, out=dW)}
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    burst = peaks.get("bf16_tflops") or 1590.0
+    flops = 2.0 * M * C * C
+    clk = ClockSampler(0)
+    clk.start()
+    l0 = _lib.launch_count
+    res = {n: timed(fn) for n, fn in ours.items()}
+    launches = (_lib.launch_count - l0) // (len(ours) * (args.steps + args.warmup))
+    clocks = clk.stop()
+    ref = {n: timed(fn) for n, fn in cublas.items()}
+    ms = sum(res.values())
+    tf = {n: flops / (t * 1e-3) / 1e12 for n, t in res.items()}
+    line = {"metric": "projection_gemm_tflops", "value": 3 * flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1)",
+            "config": {"workload": "720p layer projection GEMMs (x W^T, dy W, dy^T x), one of q/k/v/o",
+                       "M": M, "N": C, "K": C},
+            "ms": res, "tflops": tf, "frac_of_burst": {n: v / burst for n, v in tf.items()},
+            "cublas_ms": ref, "cublas_tflops": {n: flops / (t * 1e-3) / 1e12 for n, t in ref.items()},
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel", "achieved": max(tf.values()),
+                         "peak": burst, "unit": "TFLOP/s", "frac": max(tf.values()) / burst, "traffic": None,
+                         "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback"},
+            "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def run_cross(args):
     """--path cross: the v2a / a2v bridge's cross-modal BSA at 720p (flash_attn_bsa_cross,
     bsa_interface.py:1276-1392): audio queries (1D, the config's audio tokens) over the
@@ -518,7 +590,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", default="720p", choices=sorted(CONFIGS),
                     help="benchmark config: 720p (config 1, default), 1080p (config 2), 2k (config 3)")
-    ap.add_argument("--path", default="dynamic", choices=["dynamic", "uniform", "producer", "cross"],
+    ap.add_argument("--path", default="dynamic", choices=["dynamic", "uniform", "producer", "cross", "gemm"],
                     help="dynamic block shapes (flash_attn_bsa_3d_dynamic, the metric's path) or "
                          "the uniform fixed-shape path (flash_attn_bsa_3d, 4x4x4 chunks, "
                          "sparsity 0.75, cdf 0.2)")
@@ -534,9 +606,9 @@ def main():
                          "for profiler captures)")
     args = ap.parse_args()
     CONFIG.update(CONFIGS[args.config])
-    if args.path in ("producer", "cross"):
+    if args.path in ("producer", "cross", "gemm"):
         CONFIG["heads"] = args.heads
-        (run_producer if args.path == "producer" else run_cross)(args)
+        {"producer": run_producer, "cross": run_cross, "gemm": run_gemm}[args.path](args)
         return
     CONFIG["heads"] = args.heads
     CONFIG["path"] = args.path

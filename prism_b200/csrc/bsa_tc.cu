@@ -1451,47 +1451,51 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       }
       tc_fence_after();
-      float p[64];
-      if (vb != 0ull) {
-        tmem_load<2>(t_lane + L::T_S + wg * 64, p);
-        if (vb != ~0ull) mask_keys(p, vb);  // masked keys: exp2(-inf) = 0
-        exp_rows(p, qk_scale, -mrow);
-      }
+      // S(n) and dP(n) are both read into registers before the exponentials and
+      // released at once (B_DPE), so the tensor core computes S(n+1) and dP(n+1)
+      // while this step's exp2 (1,024 MUFU clocks per step for the SM) and dS run.
+      // dS(n) overwrites dS(n-1): its stores wait until dQ(n-1) has read it
+      // (B_DSE); it is written in two halves of 16 columns to bound registers.
+      float p[64], dp[64];
+      if (vb != 0ull) tmem_load<2>(t_lane + L::T_S + wg * 64, p);
       if (!warp_wait(bar(L::B_DPF), n & 1, abort_flag, kErrDqSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t pk[32];
-      if (vb != 0ull) {
-        float dp[64];
-        tmem_load<2>(t_lane + L::T_DP + wg * 64, dp);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(L::B_DPE));
-        const float2 nd = make_float2(-drow, -drow);
+      if (vb != 0ull) tmem_load<2>(t_lane + L::T_DP + wg * 64, dp);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_DPE));
+      if (vb != 0ull && vb != ~0ull) mask_keys(p, vb);  // masked keys: exp2(-inf) = 0
+      const float2 sc = make_float2(qk_scale, qk_scale), nm = make_float2(-mrow, -mrow),
+                   nd = make_float2(-drow, -drow);
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
-          const float2 ds = __fmul2_rn(make_float2(p[c], p[c + 1]),
-                                       __fadd2_rn(make_float2(dp[c], dp[c + 1]), nd));
-          pk[c / 2] = pack_bf16(ds.x, ds.y);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t pk[16];
+        if (vb != 0ull) {
+#pragma unroll
+          for (int c = 32 * hh; c < 32 * hh + 32; c += 2) {
+            const float2 x = __ffma2_rn(make_float2(p[c], p[c + 1]), sc, nm);
+            const float2 ds = __fmul2_rn(make_float2(ex2(x.x), ex2(x.y)),
+                                         __fadd2_rn(make_float2(dp[c], dp[c + 1]), nd));
+            pk[(c - 32 * hh) / 2] = pack_bf16(ds.x, ds.y);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = 0u;
         }
-      } else {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(L::B_DPE));
-#pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = 0u;
+        if (hh == 0) {
+          if (n > 0 && !warp_wait(bar(L::B_DSE), (n - 1) & 1, abort_flag, kErrDqSoftmax)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        if (live) tmem_st16(t_lane + L::T_DS + wg * 32 + 16 * hh, pk);
       }
-      // dS(n) overwrites dS(n-1): wait until dQ(n-1) has read it
-      if (n > 0 && !warp_wait(bar(L::B_DSE), (n - 1) & 1, abort_flag, kErrDqSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (live) {
-        tmem_st32(t_lane + L::T_DS + wg * 32, pk);
-        tmem_wait_st();
-      }
+      if (!ok) break;
+      if (live) tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(L::B_DSF));

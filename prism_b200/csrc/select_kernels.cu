@@ -86,31 +86,35 @@ __global__ void zone_partial_kernel(const uint16_t* __restrict__ v, int heads, i
   float fr0 = 0.0f, fr1 = 0.0f;
   for (int lh = 0; lh < 8; ++lh) {
     float rh0 = 0.0f, rh1 = 0.0f;
+    // the eight tokens of the row are independent until their ordered sums below:
+    // their head sums run side by side (eight loads in flight per head step)
+    const uint16_t* base[8];
+    bool ok[8];
 #pragma unroll
     for (int lw = 0; lw < 8; ++lw) {
-      int64_t s;
-      if (!token_valid(t, zh * 8 + lh, zw * 8 + lw, T, H, W, Hp, Wp, valid, s)) continue;
-      const uint16_t* base = v + s * ss + c0;
-      float a0 = 0.0f, a1 = 0.0f;
-      int hh = 0;
-      // eight heads' loads in flight, then their sums in head order
-      for (; hh + 8 <= heads; hh += 8) {
-        uint32_t u[8];
+      int64_t s = 0;
+      ok[lw] = token_valid(t, zh * 8 + lh, zw * 8 + lw, T, H, W, Hp, Wp, valid, s);
+      base[lw] = v + (ok[lw] ? s : 0) * ss + c0;
+    }
+    float a0[8], a1[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) u[i] = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)(hh + i) * sh));
+    for (int lw = 0; lw < 8; ++lw) a0[lw] = a1[lw] = 0.0f;
+    for (int hh = 0; hh < heads; ++hh) {
+      uint32_t u[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          a0 = __fadd_rn(a0, __uint_as_float(u[i] << 16));
-          a1 = __fadd_rn(a1, __uint_as_float(u[i] & 0xffff0000u));
-        }
+      for (int lw = 0; lw < 8; ++lw)
+        u[lw] = ok[lw] ? __ldg(reinterpret_cast<const uint32_t*>(base[lw] + (int64_t)hh * sh)) : 0u;
+#pragma unroll
+      for (int lw = 0; lw < 8; ++lw) {
+        a0[lw] = __fadd_rn(a0[lw], __uint_as_float(u[lw] << 16));
+        a1[lw] = __fadd_rn(a1[lw], __uint_as_float(u[lw] & 0xffff0000u));
       }
-      for (; hh < heads; ++hh) {
-        uint32_t u0 = __ldg(reinterpret_cast<const uint32_t*>(base + (int64_t)hh * sh));
-        a0 = __fadd_rn(a0, __uint_as_float(u0 << 16));
-        a1 = __fadd_rn(a1, __uint_as_float(u0 & 0xffff0000u));
-      }
-      const float x0 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a0, fheads)));
-      const float x1 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a1, fheads)));
+    }
+#pragma unroll
+    for (int lw = 0; lw < 8; ++lw) {
+      if (!ok[lw]) continue;
+      const float x0 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a0[lw], fheads)));
+      const float x1 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a1[lw], fheads)));
       rh0 = __fadd_rn(rh0, x0);
       rh1 = __fadd_rn(rh1, x1);
       cw0[lw] = __fadd_rn(cw0[lw], x0);
