@@ -42,8 +42,11 @@ CONFIGS = {
     "720p": dict(CONFIG),
     "1080p": dict(CONFIG, workload="1080p dynamic BSA layer fwd+bwd (benchmark config 2)",
                   grid=(21, 68, 120)),
+    # config 3's zone-statistics inputs: V ~ N(0, 1) (the video hidden states) and the a2v
+    # residual N(0, 1) scaled per zone by U(0.2, 2)
     "2k": dict(CONFIG, workload="2K dynamic BSA layer fwd+bwd (benchmark config 3)",
-               grid=(31, 90, 160), audio_tokens=189, sparsity=0.95),
+               grid=(31, 90, 160), audio_tokens=189, sparsity=0.95, v_values="normal",
+               a2v_zone_scale=(0.2, 2.0)),
 }
 # DRAM bytes (read + write) per head of one launch of each attention kernel on the 720p
 # layer: ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-head capture / 4.  Heads
@@ -71,8 +74,9 @@ def padded_grid():
 
 # ------------------------------------------------------------------ inputs
 def make_layer_inputs(device, rank=0, world=1, seed=0):
-    """Config-1 synthetic layer, generated on the device from a seeded CPU generator
-    per zone (zone mean + 0.3 noise, both N(0, 0.5^2))."""
+    """Synthetic layer inputs, generated on the device from a seeded generator: q, k (and
+    v, except for config 3) per zone = zone mean + 0.3 noise, both N(0, 0.5^2); config 3's
+    v is N(0, 1) and its a2v residual N(0, 1) scaled per zone by U(0.2, 2)."""
     import torch
     T, H, W = CONFIG["grid"]
     h, D = CONFIG["heads"], CONFIG["head_dim"]
@@ -86,9 +90,19 @@ def make_layer_inputs(device, rank=0, world=1, seed=0):
         return x[:, :T, :H, :W].reshape(h, T * H * W, D).transpose(0, 1).to(torch.bfloat16)
 
     S = T * H * W
-    q, k, v = zoned(), zoned(), zoned()          # [S, h, D]  (sequence-major, like the projections)
+    q, k = zoned(), zoned()                      # [S, h, D]  (sequence-major, like the projections)
+    if CONFIG.get("v_values") == "normal":
+        v = torch.randn(S, h, D, generator=g, device=device).to(torch.bfloat16)
+    else:
+        v = zoned()
     do = torch.randn(S, h, D, generator=g, device=device).to(torch.bfloat16)
-    a2v = torch.randn(S, CONFIG["hidden"], generator=g, device=device).to(torch.bfloat16)
+    a2v = torch.randn(S, CONFIG["hidden"], generator=g, device=device)
+    if CONFIG.get("a2v_zone_scale"):
+        lo, hi = CONFIG["a2v_zone_scale"]
+        zs = lo + (hi - lo) * torch.rand(Tp // 8, Hp // 8, Wp // 8, generator=g, device=device)
+        zs = zs.repeat_interleave(8, 0).repeat_interleave(8, 1).repeat_interleave(8, 2)
+        a2v = a2v * zs[:T, :H, :W].reshape(S, 1)
+    a2v = a2v.to(torch.bfloat16)
     C = -(-S // world)  # ceil(S / P) rows per shard, the last one shorter
     sl = slice(min(rank * C, S), min(rank * C + C, S))
     sizes = [sl.stop - sl.start if r == rank else 0 for r in range(world)]

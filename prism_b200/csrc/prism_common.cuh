@@ -42,6 +42,7 @@ void set_error(const char* fmt, ...);
   } while (0)
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // ------------------------------------------------------------------ shapes
 // Candidate block shapes (bt, bh, bw): 7 of 64 tokens then 6 of 128 tokens

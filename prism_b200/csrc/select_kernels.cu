@@ -153,6 +153,140 @@ __global__ void zone_partial_kernel(const uint16_t* __restrict__ v, int heads, i
   }
 }
 
+// The same partial sums with the eight rows of the frame in parallel (D <= 128): a
+// CTA of 8 x D/2 threads (two CTAs per SM), thread (lh, channel pair) makes row lh's
+// head means (kZoneHeads heads' loads in flight per step) and its row sums; the
+// column sums over the rows and the frame sum are then taken from shared memory in
+// row order lh = 0..7, so every sum has the summation order of zone_partial_kernel
+// and the result is the same bit for bit.
+constexpr int kZoneHeads = 2;
+__global__ void __launch_bounds__(512, 2) zone_partial_rows_kernel(
+    const uint16_t* __restrict__ v, int heads, int64_t sh, int64_t ss, int T, int H, int W, int Hp,
+    int Wp, int D, const uint8_t* __restrict__ valid, const uint16_t* __restrict__ norms,
+    float* __restrict__ part, float* __restrict__ apart) {
+  extern __shared__ float zsm[];
+  float* xs = zsm;           // [8 lh][8 lw][D] head means of the frame's tokens
+  float* rs = zsm + 64 * D;  // [8 lh][D] row sums
+  __shared__ float an[64];
+  __shared__ unsigned long long okm;
+  const int ZH = Hp / 8, ZW = Wp / 8;
+  const int z = blockIdx.x >> 3, lt = blockIdx.x & 7;
+  const int zt = z / (ZH * ZW), zh = (z / ZW) % ZH, zw = z % ZW;
+  const int t = zt * 8 + lt;
+  const int half = D / 2;
+  const int lh = threadIdx.x / half;
+  const int c0 = 2 * (threadIdx.x - lh * half);
+  float* P = part + (int64_t)blockIdx.x * kPart * D;
+  const float fheads = (float)heads;
+  if (threadIdx.x == 0) okm = 0ull;
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    int64_t s = 0;
+    const bool ok = token_valid(t, zh * 8 + threadIdx.x / 8, zw * 8 + threadIdx.x % 8, T, H, W, Hp, Wp,
+                                valid, s);
+    an[threadIdx.x] = ok && norms != nullptr ? bfbits2f(__ldg(norms + s)) : 0.0f;
+    if (ok) atomicOr(&okm, 1ull << threadIdx.x);
+  }
+  // the row's eight tokens are consecutive source tokens (w = 8 zw + lw); only the
+  // valid ones are loaded
+  unsigned okb = 0;
+#pragma unroll
+  for (int lw = 0; lw < 8; ++lw) {
+    int64_t s = 0;
+    if (token_valid(t, zh * 8 + lh, zw * 8 + lw, T, H, W, Hp, Wp, valid, s)) okb |= 1u << lw;
+  }
+  const uint16_t* vb = v + (okb ? (((int64_t)t * H + zh * 8 + lh) * W + zw * 8) * ss + c0 : 0);
+  float a0[8], a1[8];
+#pragma unroll
+  for (int lw = 0; lw < 8; ++lw) a0[lw] = a1[lw] = 0.0f;
+  int hh = 0;
+  // kZoneHeads heads' loads in flight per step, summed in head order
+  for (; hh + kZoneHeads <= heads; hh += kZoneHeads) {
+    uint32_t u[kZoneHeads][8];
+#pragma unroll
+    for (int e = 0; e < kZoneHeads; ++e)
+#pragma unroll
+      for (int lw = 0; lw < 8; ++lw)
+        u[e][lw] = (okb >> lw) & 1u
+                       ? __ldg(reinterpret_cast<const uint32_t*>(vb + lw * ss + (int64_t)(hh + e) * sh))
+                       : 0u;
+#pragma unroll
+    for (int e = 0; e < kZoneHeads; ++e)
+#pragma unroll
+      for (int lw = 0; lw < 8; ++lw) {
+        a0[lw] = __fadd_rn(a0[lw], __uint_as_float(u[e][lw] << 16));
+        a1[lw] = __fadd_rn(a1[lw], __uint_as_float(u[e][lw] & 0xffff0000u));
+      }
+  }
+  for (; hh < heads; ++hh) {
+#pragma unroll
+    for (int lw = 0; lw < 8; ++lw) {
+      const uint32_t u =
+          (okb >> lw) & 1u ? __ldg(reinterpret_cast<const uint32_t*>(vb + lw * ss + (int64_t)hh * sh)) : 0u;
+      a0[lw] = __fadd_rn(a0[lw], __uint_as_float(u << 16));
+      a1[lw] = __fadd_rn(a1[lw], __uint_as_float(u & 0xffff0000u));
+    }
+  }
+  float rh0 = 0.0f, rh1 = 0.0f;
+#pragma unroll
+  for (int lw = 0; lw < 8; ++lw) {
+    if (!((okb >> lw) & 1u)) continue;
+    const float x0 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a0[lw], fheads)));
+    const float x1 = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a1[lw], fheads)));
+    rh0 = __fadd_rn(rh0, x0);
+    rh1 = __fadd_rn(rh1, x1);
+    xs[(lh * 8 + lw) * D + c0] = x0;
+    xs[(lh * 8 + lw) * D + c0 + 1] = x1;
+  }
+  P[(1 + lh) * D + c0] = rh0;
+  P[(1 + lh) * D + c0 + 1] = rh1;
+  rs[lh * D + c0] = rh0;
+  rs[lh * D + c0 + 1] = rh1;
+  __syncthreads();
+  const unsigned long long m = okm;
+  {
+    // column lw = lh of the frame, summed over its rows in order
+    const int lw = lh;
+    float cw0 = 0.0f, cw1 = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (!((m >> (r * 8 + lw)) & 1ull)) continue;
+      cw0 = __fadd_rn(cw0, xs[(r * 8 + lw) * D + c0]);
+      cw1 = __fadd_rn(cw1, xs[(r * 8 + lw) * D + c0 + 1]);
+    }
+    P[(9 + lw) * D + c0] = cw0;
+    P[(9 + lw) * D + c0 + 1] = cw1;
+  }
+  if (lh == 0) {
+    float fr0 = 0.0f, fr1 = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      fr0 = __fadd_rn(fr0, rs[r * D + c0]);
+      fr1 = __fadd_rn(fr1, rs[r * D + c0 + 1]);
+    }
+    P[c0] = fr0;
+    P[c0 + 1] = fr1;
+  }
+  if (threadIdx.x == 0) {
+    float* A = apart + (int64_t)blockIdx.x * kPart;
+    float cw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float fr = 0.0f;
+    for (int r = 0; r < 8; ++r) {
+      float rh = 0.0f;
+      for (int lw = 0; lw < 8; ++lw) {
+        if (!((m >> (r * 8 + lw)) & 1ull)) continue;
+        const float x = an[r * 8 + lw];
+        rh = __fadd_rn(rh, x);
+        cw[lw] = __fadd_rn(cw[lw], x);
+      }
+      A[1 + r] = rh;
+      fr = __fadd_rn(fr, rh);
+    }
+    A[0] = fr;
+    for (int lw = 0; lw < 8; ++lw) A[9 + lw] = cw[lw];
+  }
+}
+
 // Stage 2: one CTA per zone; combine the eight frames in order lt = 0..7.
 __global__ void zone_combine_kernel(const float* __restrict__ part, const float* __restrict__ apart,
                                     int T, int H, int W, int Hp, int Wp, int D,
@@ -619,6 +753,112 @@ __global__ void __launch_bounds__(256) scatter_rows4_kernel(
   }
 }
 
+// Token-major forms, used when a token's heads lie side by side (head stride == D,
+// the [S, H, D] layout of the model and of the Ulysses receive buffer): one CTA moves
+// kTokRows tokens with every head, so each token's source (gather) or destination
+// (scatter) is one contiguous heads*D*2-byte span instead of `heads` 256-byte pieces
+// kilobytes apart, and each head's side is kTokRows consecutive tile-order rows.
+// Consecutive threads take consecutive 16-byte chunks of that span; a thread issues
+// kTokUnroll loads before its stores.
+constexpr int kTokRows = 8;
+constexpr int kTokUnroll = 4;
+__global__ void __launch_bounds__(256) gather_rows_tok_kernel(
+    const uint4* __restrict__ x, int64_t xss, int heads, int chunks, int T, int H, int W, int Hp,
+    int Wp, int Sp, const int32_t* __restrict__ src_idx, uint4* __restrict__ out, int64_t osh) {
+  __shared__ int64_t s_off[kTokRows];  // 16-byte offset of the token's span, -1 for padding
+  const int r0 = blockIdx.x * kTokRows;
+  if (threadIdx.x < kTokRows) {
+    const int r = r0 + threadIdx.x;
+    int64_t off = -1;
+    if (r < Sp) {
+      const int g = __ldg(src_idx + r);
+      const int hw = Hp * Wp;
+      const int t = g / hw;
+      const int rem = g - t * hw;
+      const int hh = rem / Wp;
+      const int w = rem - hh * Wp;
+      if (t < T && hh < H && w < W) off = ((((int64_t)t * H + hh) * W + w) * xss) / 8;
+    }
+    s_off[threadIdx.x] = off;
+  }
+  __syncthreads();
+  const int per_row = heads * chunks;
+  const int total = kTokRows * per_row;
+  const int64_t osh16 = osh / 8;
+  for (int i0 = threadIdx.x; i0 < total; i0 += 256 * kTokUnroll) {
+    uint4 val[kTokUnroll];
+#pragma unroll
+    for (int u = 0; u < kTokUnroll; ++u) {
+      const int i = i0 + u * 256;
+      val[u] = make_uint4(0, 0, 0, 0);
+      if (i < total) {
+        const int row = i / per_row;
+        const int64_t off = s_off[row];
+        if (off >= 0) val[u] = __ldg(x + off + (i - row * per_row));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kTokUnroll; ++u) {
+      const int i = i0 + u * 256;
+      if (i < total) {
+        const int row = i / per_row;
+        const int rem = i - row * per_row;
+        const int h = rem / chunks;
+        const int r = r0 + row;
+        if (r < Sp) out[h * osh16 + (int64_t)r * chunks + (rem - h * chunks)] = val[u];
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) scatter_rows_tok_kernel(
+    const uint4* __restrict__ x, int64_t xsh, int heads, int chunks, int T, int H, int W, int Hp,
+    int Wp, const int32_t* __restrict__ inv_idx, uint4* __restrict__ out, int64_t oss) {
+  __shared__ int s_row[kTokRows];  // tile-order row of the token
+  const int S = T * H * W;
+  const int s0 = blockIdx.x * kTokRows;
+  if (threadIdx.x < kTokRows) {
+    const int s = s0 + threadIdx.x;
+    int r = 0;
+    if (s < S) {
+      const int hw = H * W;
+      const int t = s / hw;
+      const int rem = s - t * hw;
+      const int hh = rem / W;
+      const int w = rem - hh * W;
+      r = __ldg(inv_idx + ((int64_t)t * Hp + hh) * Wp + w);
+    }
+    s_row[threadIdx.x] = r;
+  }
+  __syncthreads();
+  const int per_row = heads * chunks;
+  const int total = kTokRows * per_row;
+  const int64_t xsh16 = xsh / 8, oss16 = oss / 8;
+  for (int i0 = threadIdx.x; i0 < total; i0 += 256 * kTokUnroll) {
+    uint4 val[kTokUnroll];
+#pragma unroll
+    for (int u = 0; u < kTokUnroll; ++u) {
+      const int i = i0 + u * 256;
+      if (i < total) {
+        const int row = i / per_row;
+        const int rem = i - row * per_row;
+        const int h = rem / chunks;
+        val[u] = make_uint4(0, 0, 0, 0);
+        if (s0 + row < S)
+          val[u] = __ldg(x + h * xsh16 + (int64_t)s_row[row] * chunks + (rem - h * chunks));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kTokUnroll; ++u) {
+      const int i = i0 + u * 256;
+      if (i < total) {
+        const int row = i / per_row;
+        if (s0 + row < S) out[(int64_t)(s0 + row) * oss16 + (i - row * per_row)] = val[u];
+      }
+    }
+  }
+}
+
 __global__ void scatter_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int chunks, int T, int H,
                                     int W, int Hp, int Wp, const int32_t* __restrict__ inv_idx,
                                     uint4* __restrict__ out, int64_t osh, int64_t oss) {
@@ -683,6 +923,60 @@ __global__ void pool_kernel(const uint16_t* __restrict__ q, const uint16_t* __re
   const float den = cnt < 1.0f ? 1.0f : cnt;
   qc[((int64_t)h * nb_max + b) * D + d] = __fdiv_rn(oq, den);
   kc[((int64_t)h * nb_max + b) * D + d] = __fdiv_rn(ok, den);
+  if (h == 0 && d == 0) bvalid[b] = cnt > 0.0f;
+}
+
+// The same pooling with two channels per thread (D/2 threads, 4-byte loads): each
+// thread keeps 16 rows x 2 tensors x 4 bytes in flight; per channel the masked sums
+// run in row order as above, so the means are the same bit for bit.
+__global__ void pool2_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, int64_t S,
+                             int D, const int32_t* __restrict__ block_tiles,
+                             const int32_t* __restrict__ n_blocks,
+                             const uint64_t* __restrict__ tile_bits, float* __restrict__ qc,
+                             float* __restrict__ kc, uint8_t* __restrict__ bvalid, int nb_max) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  if (b >= *n_blocks) return;
+  const int64_t n_tiles = S / 64;
+  const int d = 2 * threadIdx.x;
+  float oq0 = 0.0f, oq1 = 0.0f, ok0 = 0.0f, ok1 = 0.0f, cnt = 0.0f;
+  for (int p = 0; p < 2; ++p) {
+    const int j = block_tiles[2 * b + p];
+    if (j >= n_tiles) continue;
+    const uint64_t bits = tile_bits[j];
+    const int c = __popcll(bits);
+    const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + ((int64_t)h * S + (int64_t)j * 64) * D + d);
+    const uint32_t* kr = reinterpret_cast<const uint32_t*>(k + ((int64_t)h * S + (int64_t)j * 64) * D + d);
+    const int rs = D / 2;  // row stride in 4-byte words
+    float sq0 = 0.0f, sq1 = 0.0f, sk0 = 0.0f, sk1 = 0.0f;
+    for (int i0 = 0; i0 < 64; i0 += 16) {
+      uint32_t uq[16], uk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        uq[i] = __ldg(qr + (int64_t)(i0 + i) * rs);
+        uk[i] = __ldg(kr + (int64_t)(i0 + i) * rs);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (!((bits >> (i0 + i)) & 1ull)) continue;
+        sq0 = __fadd_rn(sq0, __uint_as_float(uq[i] << 16));
+        sq1 = __fadd_rn(sq1, __uint_as_float(uq[i] & 0xffff0000u));
+        sk0 = __fadd_rn(sk0, __uint_as_float(uk[i] << 16));
+        sk1 = __fadd_rn(sk1, __uint_as_float(uk[i] & 0xffff0000u));
+      }
+    }
+    const float fc = (float)c;
+    const float den = c > 0 ? fc : 1.0f;
+    oq0 = __fadd_rn(oq0, __fmul_rn(__fdiv_rn(sq0, den), fc));
+    oq1 = __fadd_rn(oq1, __fmul_rn(__fdiv_rn(sq1, den), fc));
+    ok0 = __fadd_rn(ok0, __fmul_rn(__fdiv_rn(sk0, den), fc));
+    ok1 = __fadd_rn(ok1, __fmul_rn(__fdiv_rn(sk1, den), fc));
+    cnt = __fadd_rn(cnt, fc);
+  }
+  const float den = cnt < 1.0f ? 1.0f : cnt;
+  float2* qo = reinterpret_cast<float2*>(qc + ((int64_t)h * nb_max + b) * D + d);
+  float2* ko = reinterpret_cast<float2*>(kc + ((int64_t)h * nb_max + b) * D + d);
+  *qo = make_float2(__fdiv_rn(oq0, den), __fdiv_rn(oq1, den));
+  *ko = make_float2(__fdiv_rn(ok0, den), __fdiv_rn(ok1, den));
   if (h == 0 && d == 0) bvalid[b] = cnt > 0.0f;
 }
 
@@ -1486,9 +1780,15 @@ prism_status_t prism_zone_stats(const void* v, int heads, int64_t v_stride_h, in
   const int Nz = (Tp / 8) * (Hp / 8) * (Wp / 8);
   float* part = (float*)workspace;
   float* apart = part + (size_t)Nz * 8 * kPart * D;
-  zone_partial_kernel<<<Nz * 8, D / 2, 0, stream>>>((const uint16_t*)v, heads, v_stride_h, v_stride_s,
-                                                    T, H, W, Hp, Wp, D, valid, (const uint16_t*)norms, part,
-                                                    apart);
+  if (D <= 128) {
+    zone_partial_rows_kernel<<<Nz * 8, 4 * D, (size_t)72 * D * sizeof(float), stream>>>(
+        (const uint16_t*)v, heads, v_stride_h, v_stride_s, T, H, W, Hp, Wp, D, valid,
+        (const uint16_t*)norms, part, apart);
+  } else {
+    zone_partial_kernel<<<Nz * 8, D / 2, 0, stream>>>((const uint16_t*)v, heads, v_stride_h, v_stride_s,
+                                                      T, H, W, Hp, Wp, D, valid, (const uint16_t*)norms,
+                                                      part, apart);
+  }
   PRISM_CHECK_LAUNCH("prism_zone_stats/partial");
   zone_combine_kernel<<<Nz, D < 1024 ? (D < 32 ? 32 : D) : 1024, 0, stream>>>(
       part, apart, T, H, W, Hp, Wp, D, valid, packed, axis_valid, audio);
@@ -1561,7 +1861,11 @@ prism_status_t prism_gather_rows(const void* x, int64_t x_stride_h, int64_t x_st
                   "prism_gather_rows: bad row count");
   const int64_t total = n_rows * chunks;
   if (total == 0 || heads == 0) return PRISM_OK;
-  if (256 % chunks == 0) {
+  if (x_stride_h == D && heads >= 2 && (int64_t)kTokRows * heads * chunks < (int64_t)1 << 31) {
+    gather_rows_tok_kernel<<<(unsigned)((n_rows + kTokRows - 1) / kTokRows), 256, 0, stream>>>(
+        (const uint4*)x, x_stride_s, heads, chunks, T, H, W, Hp, Wp, (int)n_rows, src_idx, (uint4*)out,
+        out_stride_h);
+  } else if (256 % chunks == 0) {
     const int64_t per_block = (256 / chunks) * kRowsPerThread;
     gather_rows4_kernel<<<dim3((unsigned)((n_rows + per_block - 1) / per_block), heads), 256, 0, stream>>>(
         (const uint4*)x, x_stride_h, x_stride_s, chunks, T, H, W, Hp, Wp, (int)n_rows, src_idx,
@@ -1588,7 +1892,10 @@ prism_status_t prism_scatter_rows(const void* x_re, int64_t x_stride_h, int head
   PRISM_CHECK_ARG(S * chunks < (int64_t)1 << 31 && heads <= 65535, "prism_scatter_rows: too many rows");
   const int64_t total = S * chunks;
   if (total == 0 || heads == 0) return PRISM_OK;
-  if (256 % chunks == 0) {
+  if (out_stride_h == D && heads >= 2 && (int64_t)kTokRows * heads * chunks < (int64_t)1 << 31) {
+    scatter_rows_tok_kernel<<<(unsigned)((S + kTokRows - 1) / kTokRows), 256, 0, stream>>>(
+        (const uint4*)x_re, x_stride_h, heads, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out, out_stride_s);
+  } else if (256 % chunks == 0) {
     const int64_t per_block = (256 / chunks) * kRowsPerThread;
     scatter_rows4_kernel<<<dim3((unsigned)((S + per_block - 1) / per_block), heads), 256, 0, stream>>>(
         (const uint4*)x_re, x_stride_h, chunks, T, H, W, Hp, Wp, inv_idx, (uint4*)out, out_stride_h,
@@ -1628,9 +1935,15 @@ prism_status_t prism_block_select(const void* q_re, const void* k_re, int heads,
   float* kc = qc + (size_t)heads * nb_max * D;
   float* sc = kc + (size_t)heads * nb_max * D;
   uint8_t* bvalid = (uint8_t*)(sc + (size_t)heads * nb_max * nb_max);
-  pool_kernel<<<dim3(nb_max, heads), D, 0, stream>>>((const uint16_t*)q_re, (const uint16_t*)k_re, S, D,
-                                                    block_tiles, n_blocks, tile_bits, qc, kc, bvalid,
-                                                    nb_max);
+  if (D % 2 == 0 && aligned_to(q_re, 4) && aligned_to(k_re, 4)) {
+    pool2_kernel<<<dim3(nb_max, heads), D / 2, 0, stream>>>((const uint16_t*)q_re, (const uint16_t*)k_re, S,
+                                                            D, block_tiles, n_blocks, tile_bits, qc, kc,
+                                                            bvalid, nb_max);
+  } else {
+    pool_kernel<<<dim3(nb_max, heads), D, 0, stream>>>((const uint16_t*)q_re, (const uint16_t*)k_re, S, D,
+                                                      block_tiles, n_blocks, tile_bits, qc, kc, bvalid,
+                                                      nb_max);
+  }
   PRISM_CHECK_LAUNCH("prism_block_select/pool");
   const size_t ssm = 2 * (size_t)D * (kScoreTile + 4) * sizeof(float);
   PRISM_CHECK_CUDA(cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm),

@@ -152,9 +152,11 @@ _DynBsaFunction = _BsaFunction
 
 
 def _check_head_dim(D: int):
+    """The reference's head-dim contract (bsa_interface.py:604-605).  16 and 32 run on the
+    D = 64 kernels with zero columns (ops.bsa_fwd / ops.bsa_bwd); 256 is not built."""
     assert D in {16, 32, 64, 128, 256}, "head dim must be one of 16, 32, 64, 128, 256"
-    if D not in (64, 128):
-        raise NotImplementedError(f"prism_b200 kernels support head_dim 64 and 128, got {D}")
+    if D == 256:
+        raise NotImplementedError("prism_b200 attention kernels take head_dim 16, 32, 64 or 128, got 256")
 
 
 def build_plan(q_hsd, k_hsd, v_hsd, grid, grid_padded, *, method, sparsity, cdf_threshold,

@@ -304,6 +304,12 @@ def bsa_fwd_keybias(q_re, k_re, v_re, bits_q, key_masks, key_bias, sm_scale: flo
     """Forward with per-(head, q tile, key tile) key masks and per-key score offsets
     -> (o, lse, o_lo)."""
     _check_cuda(q_re, k_re, v_re, bits_q, key_masks, key_bias)
+    D0 = q_re.shape[-1]
+    Dk = _kernel_head_dim(D0)
+    if Dk != D0:
+        o, lse, o_lo = bsa_fwd_keybias(_pad_cols(q_re, Dk), _pad_cols(k_re, Dk), _pad_cols(v_re, Dk),
+                                       bits_q, key_masks, key_bias, sm_scale)
+        return o[..., :D0].contiguous(), lse, o_lo[..., :D0].contiguous()
     heads, Sq, D = q_re.shape
     Sk = k_re.shape[1]
     o = torch.empty_like(q_re)
@@ -512,9 +518,37 @@ def _timed(name, device, fn):
     return r
 
 
+# The attention kernels are built for head dims 64 and 128.  Head dims 16 and 32 (which
+# the reference's contract also accepts, bsa_interface.py:604-605) run on the D = 64
+# kernels with zero columns appended: a zero column adds exact zeros to every score and
+# produces zero output / gradient columns, which are dropped.  The caller's sm_scale
+# (1/sqrt of the real head dim) is passed through unchanged.
+_KERNEL_D = {16: 64, 32: 64, 64: 64, 128: 128}
+
+
+def _pad_cols(x: torch.Tensor, Dk: int) -> torch.Tensor:
+    if x is None or x.shape[-1] == Dk:
+        return x
+    out = x.new_zeros(*x.shape[:-1], Dk)
+    out[..., :x.shape[-1]] = x
+    return out
+
+
+def _kernel_head_dim(D: int) -> int:
+    if D not in _KERNEL_D:
+        raise NotImplementedError(f"prism_b200 attention kernels take head_dim 16, 32, 64 or 128, got {D}")
+    return _KERNEL_D[D]
+
+
 def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float, want_lo: bool = False):
     """Returns (o, lse) or (o, lse, o_lo) with o_lo the bf16 rounding residual of o."""
     _check_cuda(q_re, k_re, v_re)
+    D0 = q_re.shape[-1]
+    Dk = _kernel_head_dim(D0)
+    if Dk != D0:
+        r = bsa_fwd(_pad_cols(q_re, Dk), _pad_cols(k_re, Dk), _pad_cols(v_re, Dk), bits_q, tile_bits,
+                    sm_scale, want_lo)
+        return tuple(t[..., :D0].contiguous() if t.dim() == 3 else t for t in r)
     heads, Sq, D = q_re.shape
     Sk = k_re.shape[1]
     o = torch.empty_like(q_re)
@@ -531,6 +565,12 @@ def bsa_fwd(q_re, k_re, v_re, bits_q, tile_bits, sm_scale: float, want_lo: bool 
 def bsa_bwd(q_re, k_re, v_re, o_re, do_re, lse, bits_q, bits_k, tile_bits, sm_scale: float,
             o_lo=None):
     _check_cuda(q_re, do_re)
+    D0 = q_re.shape[-1]
+    Dk = _kernel_head_dim(D0)
+    if Dk != D0:
+        g = bsa_bwd(*(_pad_cols(t, Dk) for t in (q_re, k_re, v_re, o_re, do_re)), lse, bits_q, bits_k,
+                    tile_bits, sm_scale, o_lo=_pad_cols(o_lo, Dk))
+        return tuple(t[..., :D0].contiguous() for t in g)
     heads, Sq, D = q_re.shape
     Sk = k_re.shape[1]
     dq = torch.empty_like(q_re)

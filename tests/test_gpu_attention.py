@@ -3,6 +3,7 @@
 Tolerance (from the task's north star): every bf16 output and gradient must
 match within max-abs error 2e-2 and relative L2 error 1e-2 of the float64
 oracle / the reference's fp32 outputs."""
+import dataclasses
 import math
 
 import numpy as np
@@ -54,7 +55,7 @@ def _random_problem(heads, n_tiles, D, density, seed, dev, masked_tiles=(), empt
     return dict(q=q, k=k, v=v, do=do, bq=bq, valid=valid.numpy(), dev=dev_t)
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [16, 32, 64, 128])
 @pytest.mark.parametrize("density", [0.3, 0.9])
 def test_sparse_kernels_vs_oracle(D, density, cuda):
     pr = _random_problem(2, 16, D, density, seed=D + int(density * 10), dev=cuda,
@@ -171,6 +172,39 @@ def test_dynamic_path_vs_reference_golden(name, cuda):
             q, k, v, case.grid_padded, method=case.method, sparsity=case.sparsity,
             cdf_threshold=case.cdf_threshold, valid_mask=inp["valid"].to(cuda), shape_ids=ids)
     assert torch.equal(out.detach(), out2)
+
+
+@pytest.mark.parametrize("D", [16, 32])
+def test_dynamic_path_small_head_dim(D, cuda):
+    """Head dims 16 and 32 (accepted by the reference, bsa_interface.py:604-605) through
+    flash_attn_bsa_3d_dynamic: shape ids bit-exact against the oracle; output and the
+    three gradients within the tolerance of the float64 oracle on the oracle's selection."""
+    case = dataclasses.replace(CASES["mixed_d64"], head_dim=D, name=f"mixed_d{D}")
+    inp = make_inputs(case)
+    q, k, v = (inp[n].to(cuda).requires_grad_(True) for n in ("q", "k", "v"))
+    out, ids = flash_attn_bsa_3d_dynamic(
+        q, k, v, case.grid_padded, method=case.method, sparsity=case.sparsity,
+        cdf_threshold=case.cdf_threshold, audio_token_norms=inp["norms"].to(cuda),
+        valid_mask=inp["valid"].to(cuda), lambda_a=case.lambda_a, tau_128=case.tau_128,
+        lambda_128=case.lambda_128, return_shape_ids=True)
+    out.backward(inp["do"].to(cuda))
+    b16 = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    r = O.dynamic_forward_selection(b16(inp["q"][0]), b16(inp["k"][0]), b16(inp["v"][0]),
+                                    case.grid_padded, method=case.method, sparsity=case.sparsity,
+                                    cdf_threshold=case.cdf_threshold, norms_bits=b16(inp["norms"]),
+                                    valid=inp["valid"].numpy().astype(np.uint8), lambda_a=case.lambda_a,
+                                    tau_128=case.tau_128, lambda_128=case.lambda_128)
+    assert np.array_equal(ids.cpu().numpy(), r["shape_ids"])
+    f = O.bf16_bits_to_f32
+    qr, kr, vr = f(r["q_re"]), f(r["k_re"]), f(r["v_re"])
+    o, _ = O.bsa_forward(qr, kr, vr, r["bits_q"], r["valid_re"])
+    do_re = inp["do"][0].float().numpy()[:, r["src_idx"]]
+    dq, dk, dv = O.bsa_backward(qr, kr, vr, o, do_re, r["bits_q"], r["valid_re"])
+    inv = r["inv_idx"]
+    for name, got, ref in (("O", out.detach()[0], o), ("dQ", q.grad[0], dq), ("dK", k.grad[0], dk),
+                           ("dV", v.grad[0], dv)):
+        _close(got.float().cpu().numpy(), ref[:, inv], f"{name} (D={D})")
+    assert _lib.load().prism_device_status() == 0, "a bounded wait inside a kernel gave up"
 
 
 @pytest.mark.parametrize("layout", ["bhsd", "bshd"])
