@@ -735,14 +735,21 @@ def main():
     # FLOPs actually computed (selected tile pairs, all ranks)
     pairs, plan, (q4, k4, v4, norms), executed = selected_pairs(q.detach(), k.detach(), v.detach(),
                                                                 a2v, S, world)
-    mine = torch.tensor([pairs, executed, ms_local], device=dev, dtype=torch.float64)
-    every = torch.empty(world, 3, device=dev, dtype=torch.float64)
+    # per-rank exchange time inside the timed steps (NCCL all-to-alls and the layout
+    # copies around them, CUDA events on the step's stream)
+    a2a_ms = (kt_step or {}).get("sp_all_to_all", 0.0) / args.steps
+    copy_ms = (kt_step or {}).get("sp_layout_copy", 0.0) / args.steps
+    mine = torch.tensor([pairs, executed, ms_local, a2a_ms, copy_ms], device=dev, dtype=torch.float64)
+    every = torch.empty(world, 5, device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_gather_into_tensor(every, mine)
     else:
         every.copy_(mine[None])
     per_rank = {"selected_tile_pairs": [int(x) for x in every[:, 0].tolist()],
                 "ms_per_step": [round(float(x), 3) for x in every[:, 2].tolist()]}
+    if world > 1:
+        per_rank["all_to_all_ms_per_step"] = [round(float(x), 3) for x in every[:, 3].tolist()]
+        per_rank["layout_copy_ms_per_step"] = [round(float(x), 3) for x in every[:, 4].tolist()]
     total_pairs = float(every[:, 0].sum().item())
     total_executed = float(every[:, 1].sum().item())
     D = CONFIG["head_dim"]

@@ -145,12 +145,21 @@ def _negotiate_length(local: int, P: int, group, device) -> int:
     return S
 
 
+def _timed_span(name: str, x: torch.Tensor, fn):
+    """fn() inside a CUDA-event span of the step timer (prism_b200.ops.KernelTimer)
+    when one is set (CUDA tensors only; measurement, not part of the exchange)."""
+    if x.is_cuda:
+        from . import ops
+        return ops._timed(name, x.device, fn)
+    return fn()
+
+
 def _exchange(send: torch.Tensor, group, P: int) -> torch.Tensor:
     """One all_to_all_single over dim 0 of a contiguous [P, ...] buffer."""
     if P == 1:
         return send
     recv = torch.empty_like(send)
-    dist.all_to_all_single(recv, send, group=group)
+    _timed_span("sp_all_to_all", send, lambda: dist.all_to_all_single(recv, send, group=group))
     return recv
 
 
@@ -218,7 +227,8 @@ def _seq_to_heads(x, group, S):
         raise ValueError(f"{Hp} heads do not split over {P} SP ranks; pad them first (sp_pad_heads)")
     if n != g.rows(r):
         raise ValueError(f"rank {r} holds {n} tokens, the split of {S} over {P} gives {g.rows(r)}")
-    recv = _exchange(_seq_to_wire(x, P, g.C, Hp // P), group, P)
+    wire = _timed_span("sp_layout_copy", x, lambda: _seq_to_wire(x, P, g.C, Hp // P))
+    recv = _exchange(wire, group, P)
     return _wire_to_heads(recv, S)
 
 
@@ -227,8 +237,9 @@ def _heads_to_seq(x, group, S):
     g = ShardGeometry(P, S)
     if x.shape[1] != S:
         raise ValueError(f"expected the full sequence of {S} tokens, got {x.shape[1]}")
-    recv = _exchange(_heads_to_wire(x, P, g.C).contiguous(), group, P)
-    return _wire_to_seq(recv, g.rows(r))
+    wire = _timed_span("sp_layout_copy", x, lambda: _heads_to_wire(x, P, g.C).contiguous())
+    recv = _exchange(wire, group, P)
+    return _timed_span("sp_layout_copy", recv, lambda: _wire_to_seq(recv, g.rows(r)))
 
 
 class SeqToHeads(torch.autograd.Function):
