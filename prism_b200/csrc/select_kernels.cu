@@ -358,27 +358,6 @@ __global__ void zone_combine_kernel(const float* __restrict__ part, const float*
 }
 
 // ================================================================ a4/a6/a7
-__device__ float axis_var_dev(const float* A, const uint8_t* valid, int D) {
-  float n = 0.0f;
-  for (int p = 0; p < 8; ++p) n = __fadd_rn(n, valid[p] ? 1.0f : 0.0f);
-  if (n < 1.0f) n = 1.0f;
-  float tot = 0.0f;
-  for (int d = 0; d < D; ++d) {
-    float s = 0.0f;
-    for (int p = 0; p < 8; ++p)
-      if (valid[p]) s = __fadd_rn(s, A[p * D + d]);
-    const float mean = __fdiv_rn(s, n);
-    float q = 0.0f;
-    for (int p = 0; p < 8; ++p)
-      if (valid[p]) {
-        const float t = __fsub_rn(A[p * D + d], mean);
-        q = __fadd_rn(q, __fmul_rn(t, t));
-      }
-    tot = __fadd_rn(tot, __fdiv_rn(q, n));
-  }
-  return __fdiv_rn(tot, (float)D);
-}
-
 __device__ float masked_var8_dev(const float* a, const uint8_t* valid) {
   float n = 0.0f;
   for (int p = 0; p < 8; ++p) n = __fadd_rn(n, valid[p] ? 1.0f : 0.0f);
@@ -413,8 +392,8 @@ __device__ float block_max_f(float v, float* red) {
   return v;
 }
 
-// One CTA; one thread per zone (strided).  Per-zone intermediates in shared
-// memory: rho_raw, aniso[3], abar, vhat[3].
+// One CTA.  Per-zone intermediates in shared memory: rho_raw, aniso[3], abar,
+// vhat[3]; then the per-warp channel-term rows of the statistics pass.
 __global__ void __launch_bounds__(512) shape_select_kernel(const float* __restrict__ packed,
                                     const uint8_t* __restrict__ axis_valid,
                                     const float* __restrict__ audio, int has_audio, int Nz, int D,
@@ -429,63 +408,110 @@ __global__ void __launch_bounds__(512) shape_select_kernel(const float* __restri
   __shared__ float red[32];
   const float EPS = 1e-6f;
   float lmax_r = -INFINITY, lmax_a = -INFINITY;
-  for (int z = threadIdx.x; z < Nz; z += blockDim.x) {
+  // One warp per zone.  The per-channel terms of every statistic are computed by the
+  // lanes in parallel (each term with the same operations as a one-thread pass) and
+  // staged in shared memory; each sum over the channels is then taken by one lane in
+  // channel order, so every result is the same bit for bit as a sequential pass.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  float* T = zsm + 8 * Nz + warp * 6 * D;  // [6][D]: channel means, temporal terms,
+                                           // 3 axis terms, spatial terms
+  for (int z = warp; z < Nz; z += nwarps) {
     const float* pk = packed + (int64_t)z * 25 * D;
     const uint8_t* av = axis_valid + (int64_t)z * 24;
-    float s = 0.0f;
-    for (int d = 0; d < D; ++d) s = __fadd_rn(s, pk[d]);
-    const float gcm = __fdiv_rn(s, (float)D);
-    float sv = 0.0f;
-    for (int d = 0; d < D; ++d) {
-      const float t = __fsub_rn(pk[d], gcm);
-      sv = __fadd_rn(sv, __fmul_rn(t, t));
-    }
-    const float spatial = __fdiv_rn(sv, (float)D);
     float npairs = 0.0f;
-    uint8_t both[7];
+    bool both[7];
+#pragma unroll
     for (int p = 0; p < 7; ++p) {
       both[p] = av[p + 1] && av[p];
       npairs = __fadd_rn(npairs, both[p] ? 1.0f : 0.0f);
     }
     if (npairs < 1.0f) npairs = 1.0f;
-    float tv = 0.0f;
-    for (int d = 0; d < D; ++d) {
+    float nax[3];
+#pragma unroll
+    for (int ax = 0; ax < 3; ++ax) {
+      float n = 0.0f;
+      for (int p = 0; p < 8; ++p) n = __fadd_rn(n, av[8 * ax + p] ? 1.0f : 0.0f);
+      nax[ax] = n < 1.0f ? 1.0f : n;
+    }
+    for (int d = lane; d < D; d += 32) {
+      T[d] = pk[d];
       float a = 0.0f;
       for (int p = 0; p < 7; ++p)
         if (both[p]) {
           const float t = __fsub_rn(pk[D + (p + 1) * D + d], pk[D + p * D + d]);
           a = __fadd_rn(a, __fmul_rn(t, t));
         }
-      tv = __fadd_rn(tv, __fdiv_rn(a, npairs));
+      T[D + d] = __fdiv_rn(a, npairs);
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        const float* A = pk + D + ax * 8 * D;
+        const uint8_t* valid = av + 8 * ax;
+        float sm = 0.0f;
+        for (int p = 0; p < 8; ++p)
+          if (valid[p]) sm = __fadd_rn(sm, A[p * D + d]);
+        const float mean = __fdiv_rn(sm, nax[ax]);
+        float q = 0.0f;
+        for (int p = 0; p < 8; ++p)
+          if (valid[p]) {
+            const float t = __fsub_rn(A[p * D + d], mean);
+            q = __fadd_rn(q, __fmul_rn(t, t));
+          }
+        T[(2 + ax) * D + d] = __fdiv_rn(q, nax[ax]);
+      }
     }
-    const float temporal = __fdiv_rn(tv, (float)D);
-    rho_raw[z] = __fadd_rn(spatial, temporal);
-    const float vT = axis_var_dev(pk + D, av, D);
-    const float vH = axis_var_dev(pk + D + 8 * D, av + 8, D);
-    const float vW = axis_var_dev(pk + D + 16 * D, av + 16, D);
-    float asum = __fadd_rn(__fadd_rn(vT, vH), vW);
-    if (asum < EPS) asum = EPS;
-    aniso[3 * z + 0] = __fdiv_rn(vT, asum);
-    aniso[3 * z + 1] = __fdiv_rn(vH, asum);
-    aniso[3 * z + 2] = __fdiv_rn(vW, asum);
-    if (has_audio) {
-      const float* au = audio + (int64_t)z * 25;
-      abar[z] = au[0];
-      const float aT = masked_var8_dev(au + 1, av);
-      const float aH = masked_var8_dev(au + 9, av + 8);
-      const float aW = masked_var8_dev(au + 17, av + 16);
-      float den = __fadd_rn(__fadd_rn(aT, aH), aW);
-      if (den < EPS) den = EPS;
-      vhat[3 * z + 0] = __fdiv_rn(aT, den);
-      vhat[3 * z + 1] = __fdiv_rn(aH, den);
-      vhat[3 * z + 2] = __fdiv_rn(aW, den);
-    } else {
-      abar[z] = 0.0f;
-      vhat[3 * z + 0] = vhat[3 * z + 1] = vhat[3 * z + 2] = 0.0f;
+    __syncwarp();
+    float gcm = 0.0f;
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int d = 0; d < D; ++d) sum = __fadd_rn(sum, T[d]);
+      gcm = __fdiv_rn(sum, (float)D);
     }
-    lmax_r = fmaxf(lmax_r, rho_raw[z]);
-    lmax_a = fmaxf(lmax_a, abar[z]);
+    gcm = __shfl_sync(0xffffffffu, gcm, 0);
+    for (int d = lane; d < D; d += 32) {
+      const float t = __fsub_rn(T[d], gcm);
+      T[5 * D + d] = __fmul_rn(t, t);
+    }
+    __syncwarp();
+    // lane 0: spatial (row 5), lane 1: temporal (row 1), lanes 2-4: axes (rows 2-4)
+    float chain = 0.0f;
+    if (lane < 5) {
+      const float* row = T + (lane == 0 ? 5 : lane) * D;
+      for (int d = 0; d < D; ++d) chain = __fadd_rn(chain, row[d]);
+      chain = __fdiv_rn(chain, (float)D);
+    }
+    const float temporal = __shfl_sync(0xffffffffu, chain, 1);
+    const float vT = __shfl_sync(0xffffffffu, chain, 2);
+    const float vH = __shfl_sync(0xffffffffu, chain, 3);
+    const float vW = __shfl_sync(0xffffffffu, chain, 4);
+    if (lane == 0) {
+      const float spatial = chain;
+      rho_raw[z] = __fadd_rn(spatial, temporal);
+      float asum = __fadd_rn(__fadd_rn(vT, vH), vW);
+      if (asum < EPS) asum = EPS;
+      aniso[3 * z + 0] = __fdiv_rn(vT, asum);
+      aniso[3 * z + 1] = __fdiv_rn(vH, asum);
+      aniso[3 * z + 2] = __fdiv_rn(vW, asum);
+      if (has_audio) {
+        const float* au = audio + (int64_t)z * 25;
+        abar[z] = au[0];
+        const float aT = masked_var8_dev(au + 1, av);
+        const float aH = masked_var8_dev(au + 9, av + 8);
+        const float aW = masked_var8_dev(au + 17, av + 16);
+        float den = __fadd_rn(__fadd_rn(aT, aH), aW);
+        if (den < EPS) den = EPS;
+        vhat[3 * z + 0] = __fdiv_rn(aT, den);
+        vhat[3 * z + 1] = __fdiv_rn(aH, den);
+        vhat[3 * z + 2] = __fdiv_rn(aW, den);
+      } else {
+        abar[z] = 0.0f;
+        vhat[3 * z + 0] = vhat[3 * z + 1] = vhat[3 * z + 2] = 0.0f;
+      }
+      lmax_r = fmaxf(lmax_r, rho_raw[z]);
+      lmax_a = fmaxf(lmax_a, abar[z]);
+    }
+    __syncwarp();
   }
+  __syncthreads();
   float rmax = block_max_f(lmax_r, red);
   float amax = block_max_f(lmax_a, red);
   if (rmax < EPS) rmax = EPS;
@@ -1804,11 +1830,16 @@ prism_status_t prism_shape_select(const float* packed, const uint8_t* axis_valid
   PRISM_CHECK_ARG(packed && axis_valid && shape_ids && (audio || !has_audio), "prism_shape_select: null pointer");
   PRISM_CHECK_ARG(method == 0 || method == 1, "prism_shape_select: unknown dynamic-block method %d", method);
   PRISM_CHECK_ARG(Nz >= 1 && Nz <= 6000, "prism_shape_select: Nz=%d outside [1, 6000]", Nz);
-  const size_t smem = (size_t)Nz * 8 * sizeof(float);
+  // per-zone values (8 floats) + one row block of 6 x D channel terms per warp
+  const size_t base = (size_t)Nz * 8 * sizeof(float), per_warp = (size_t)6 * D * sizeof(float);
+  int warps = 16;
+  while (warps > 1 && base + warps * per_warp > 227 * 1024) warps >>= 1;
+  const size_t smem = base + warps * per_warp;
+  PRISM_CHECK_ARG(smem <= 227 * 1024, "prism_shape_select: Nz=%d with D=%d exceeds shared memory", Nz, D);
   if (smem > 48 * 1024)
     PRISM_CHECK_CUDA(cudaFuncSetAttribute(shape_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                      "prism_shape_select: smem attribute");
-  shape_select_kernel<<<1, 512, smem, stream>>>(packed, axis_valid, audio, has_audio, Nz, D, method,
+  shape_select_kernel<<<1, warps * 32, smem, stream>>>(packed, axis_valid, audio, has_audio, Nz, D, method,
                                                  lambda_a, tau_128, lambda_128, shape_ids, g_out,
                                                  rho_out);
   PRISM_CHECK_LAUNCH("prism_shape_select");
