@@ -52,9 +52,9 @@ CONFIGS = {
 # layer: ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-head capture / 4.  Heads
 # are independent (one head's K/V tiles stay in L2), so a launch over h heads moves h times
 # this; roofline.traffic reports it for the dominant kernel.
-TRAFFIC_PER_HEAD_720P = {"bsa_fwd": (430.5e6 + 171.5e6) / 4,
-                         "bsa_bwd_dkdv": (598.1e6 + 174.6e6) / 4,
-                         "bsa_bwd_dq": (531.6e6 + 90.8e6) / 4}
+TRAFFIC_PER_HEAD_720P = {"bsa_fwd": (545.0e6 + 170.6e6) / 4,
+                         "bsa_bwd_dkdv": (584.3e6 + 174.3e6) / 4,
+                         "bsa_bwd_dq": (555.9e6 + 88.9e6) / 4}
 FWD_BWD_FACTOR = 3.5  # 1 (forward) + 2.5 (backward): the canonical FLOP count of one fwd+bwd
 # --path uniform: the uniform fixed-shape path (flash_attn_bsa_3d) with the training
 # configs' block-sparse settings (4x4x4 chunks, sparsity 0.75, cdf threshold 0.2)

@@ -418,42 +418,47 @@ __global__ void __launch_bounds__(512) shape_select_kernel(const float* __restri
   for (int z = warp; z < Nz; z += nwarps) {
     const float* pk = packed + (int64_t)z * 25 * D;
     const uint8_t* av = axis_valid + (int64_t)z * 24;
+    uint32_t vm = 0;  // bit i: av[i] (the same 24 bytes for every lane)
+    for (int i = 0; i < 24; ++i) vm |= (av[i] ? 1u : 0u) << i;
     float npairs = 0.0f;
-    bool both[7];
 #pragma unroll
-    for (int p = 0; p < 7; ++p) {
-      both[p] = av[p + 1] && av[p];
-      npairs = __fadd_rn(npairs, both[p] ? 1.0f : 0.0f);
-    }
+    for (int p = 0; p < 7; ++p) npairs = __fadd_rn(npairs, ((vm >> (p + 1)) & (vm >> p) & 1u) ? 1.0f : 0.0f);
     if (npairs < 1.0f) npairs = 1.0f;
     float nax[3];
 #pragma unroll
     for (int ax = 0; ax < 3; ++ax) {
       float n = 0.0f;
-      for (int p = 0; p < 8; ++p) n = __fadd_rn(n, av[8 * ax + p] ? 1.0f : 0.0f);
+#pragma unroll
+      for (int p = 0; p < 8; ++p) n = __fadd_rn(n, ((vm >> (8 * ax + p)) & 1u) ? 1.0f : 0.0f);
       nax[ax] = n < 1.0f ? 1.0f : n;
     }
     for (int d = lane; d < D; d += 32) {
-      T[d] = pk[d];
+      // the channel's 25 packed values (row 0: zone mean, rows 1 + 8 ax + p: axis-ax
+      // slice means) in registers, all loads in flight at once
+      float x[25];
+#pragma unroll
+      for (int r = 0; r < 25; ++r) x[r] = pk[r * D + d];
+      T[d] = x[0];
       float a = 0.0f;
+#pragma unroll
       for (int p = 0; p < 7; ++p)
-        if (both[p]) {
-          const float t = __fsub_rn(pk[D + (p + 1) * D + d], pk[D + p * D + d]);
+        if ((vm >> (p + 1)) & (vm >> p) & 1u) {
+          const float t = __fsub_rn(x[2 + p], x[1 + p]);
           a = __fadd_rn(a, __fmul_rn(t, t));
         }
       T[D + d] = __fdiv_rn(a, npairs);
 #pragma unroll
       for (int ax = 0; ax < 3; ++ax) {
-        const float* A = pk + D + ax * 8 * D;
-        const uint8_t* valid = av + 8 * ax;
         float sm = 0.0f;
+#pragma unroll
         for (int p = 0; p < 8; ++p)
-          if (valid[p]) sm = __fadd_rn(sm, A[p * D + d]);
+          if ((vm >> (8 * ax + p)) & 1u) sm = __fadd_rn(sm, x[1 + 8 * ax + p]);
         const float mean = __fdiv_rn(sm, nax[ax]);
         float q = 0.0f;
+#pragma unroll
         for (int p = 0; p < 8; ++p)
-          if (valid[p]) {
-            const float t = __fsub_rn(A[p * D + d], mean);
+          if ((vm >> (8 * ax + p)) & 1u) {
+            const float t = __fsub_rn(x[1 + 8 * ax + p], mean);
             q = __fadd_rn(q, __fmul_rn(t, t));
           }
         T[(2 + ax) * D + d] = __fdiv_rn(q, nax[ax]);
