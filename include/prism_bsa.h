@@ -145,6 +145,17 @@ prism_status_t prism_scatter_rows(const void* x_re, int64_t x_stride_h, int head
                                   void* out, int64_t out_stride_h, int64_t out_stride_s,
                                   cudaStream_t stream);
 
+/* Strided block copy (the Ulysses exchange's layout changes,
+ * communications.py:179-183, 195, 219-225, 235 of the reference): for block o <
+ * n_blocks and row r < n_rows, row_bytes bytes from
+ * src + o * src_stride_block + r * src_stride_row to
+ * dst + o * dst_stride_block + r * dst_stride_row (all byte offsets; pointers, strides
+ * and row_bytes multiples of 16; n_blocks <= 65535).  Source and destination must not
+ * overlap. */
+prism_status_t prism_copy_rows(const void* src, int64_t src_stride_block, int64_t src_stride_row,
+                               void* dst, int64_t dst_stride_block, int64_t dst_stride_row,
+                               int64_t n_blocks, int64_t n_rows, int64_t row_bytes, cudaStream_t stream);
+
 /* Pooled logical-block scores and hybrid selection, per head
  * (masked_mean_pooling_compression bsa_interface.py:177-201,
  * _logical_block_means dynamic_block_attention.py:173-188, cal_score

@@ -33,6 +33,7 @@ SIGNATURES = {
     "prism_tile_valid": (_I, [_P, _I64, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "prism_gather_rows": (_I, [_P, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I64, _P, _I64, _P]),
     "prism_scatter_rows": (_I, [_P, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _I64, _P]),
+    "prism_copy_rows": (_I, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "prism_block_select_workspace_bytes": (_SZ, [_I, _I64, _I]),
     "prism_block_select": (_I, [_P, _P, _I, _I64, _I, _P, _P, _P, _I, _D, _D, _P, _P, _P, _P]),
     "prism_uniform_layout": (_I, [_I, _I, _I, _I, _I, _I, _I64, _P, _P, _P]),
@@ -72,7 +73,7 @@ SIGNATURES = {
 KERNELS = {
     "prism_token_norms": 1, "prism_zone_stats": 2, "prism_shape_select": 1,
     "prism_build_layout": 2, "prism_tile_valid": 1, "prism_gather_rows": 1,
-    "prism_scatter_rows": 1, "prism_block_select": 4, "prism_bsa_fwd": 1, "prism_bsa_bwd": 3,
+    "prism_scatter_rows": 1, "prism_copy_rows": 1, "prism_block_select": 4, "prism_bsa_fwd": 1, "prism_bsa_bwd": 3,
     "prism_bsa_bwd_delta": 1, "prism_bsa_bwd_dkdv": 1, "prism_bsa_bwd_dq": 1,
     "prism_bsa_bwd_noalloc": 3, "prism_uniform_layout": 1, "prism_block_select_uniform": 4,
     "prism_bsa_fwd_qk": 1, "prism_bsa_bwd_qk": 3, "prism_gather_values": 1,

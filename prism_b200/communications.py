@@ -164,11 +164,24 @@ def _exchange(send: torch.Tensor, group, P: int) -> torch.Tensor:
 
 
 # ------------------------------------------------------ layout conversions
+def _row_copy_ok(*ts) -> bool:
+    """The row-copy kernel (prism_copy_rows) applies: CUDA tensors, 16-byte aligned
+    storage offsets and rows (a rank's hp heads of one token) of whole 16-byte chunks."""
+    return all(t.is_cuda and t.data_ptr() % 16 == 0 and t.stride(-1) == 1 for t in ts)
+
+
 def _seq_to_wire(x: torch.Tensor, P: int, C: int, hp: int) -> torch.Tensor:
     """[B, S_local, P*hp, D] (token-major) -> contiguous wire [P, B, C, hp, D]."""
     B, n, Hp, D = x.shape
     wire = x.new_empty(P, B, C, hp, D)
-    wire[:, :, :n].copy_(x.unflatten(2, (P, hp)).permute(2, 0, 1, 3, 4))
+    es = x.element_size()
+    if (B == 1 and x.stride(2) == D and (hp * D * es) % 16 == 0 and (x.stride(1) * es) % 16 == 0
+            and _row_copy_ok(x, wire)):
+        # block p = heads [p hp, p hp + hp) of every token: one contiguous hp*D row per token
+        from . import ops
+        ops.copy_rows(x, (hp * D, x.stride(1)), wire, (C * hp * D, hp * D), P, n, hp * D)
+    else:
+        wire[:, :, :n].copy_(x.unflatten(2, (P, hp)).permute(2, 0, 1, 3, 4))
     if n < C:
         wire[:, :, n:].zero_()
     return wire
@@ -178,7 +191,12 @@ def _wire_to_seq(wire: torch.Tensor, n: int) -> torch.Tensor:
     """Wire [P, B, C, hp, D] -> [B, n, P*hp, D] (this rank's first n rows)."""
     P, B, C, hp, D = wire.shape
     out = wire.new_empty(B, n, P, hp, D)
-    out.copy_(wire[:, :, :n].permute(1, 2, 0, 3, 4))
+    es = wire.element_size()
+    if B == 1 and wire.is_contiguous() and (hp * D * es) % 16 == 0 and _row_copy_ok(wire, out):
+        from . import ops
+        ops.copy_rows(wire, (C * hp * D, hp * D), out, (hp * D, P * hp * D), P, n, hp * D)
+    else:
+        out.copy_(wire[:, :, :n].permute(1, 2, 0, 3, 4))
     return out.view(B, n, P * hp, D)
 
 

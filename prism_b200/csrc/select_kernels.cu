@@ -890,6 +890,41 @@ __global__ void __launch_bounds__(256) scatter_rows_tok_kernel(
   }
 }
 
+// Strided block copy for the Ulysses exchange layouts: row r of block o, `chunks`
+// 16-byte chunks long, from src + o * so + r * sr to dst + o * dso + r * dsr (strides
+// in 16-byte units).  A CTA moves kCopyRows consecutive rows of one block; consecutive
+// threads take consecutive chunks, kTokUnroll loads in flight before their stores.
+constexpr int kCopyRows = 8;
+__global__ void __launch_bounds__(256) copy_rows_kernel(const uint4* __restrict__ src, int64_t so, int64_t sr,
+                                                        uint4* __restrict__ dst, int64_t dso, int64_t dsr,
+                                                        int64_t n_rows, int chunks) {
+  const int64_t o = blockIdx.y;
+  const int64_t r0 = (int64_t)blockIdx.x * kCopyRows;
+  const int rows = (int)min((int64_t)kCopyRows, n_rows - r0);
+  const int total = rows * chunks;
+  const uint4* s = src + o * so + r0 * sr;
+  uint4* d = dst + o * dso + r0 * dsr;
+  for (int i0 = threadIdx.x; i0 < total; i0 += 256 * kTokUnroll) {
+    uint4 val[kTokUnroll];
+#pragma unroll
+    for (int u = 0; u < kTokUnroll; ++u) {
+      const int i = i0 + u * 256;
+      if (i < total) {
+        const int row = i / chunks;
+        val[u] = __ldg(s + row * sr + (i - row * chunks));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kTokUnroll; ++u) {
+      const int i = i0 + u * 256;
+      if (i < total) {
+        const int row = i / chunks;
+        d[row * dsr + (i - row * chunks)] = val[u];
+      }
+    }
+  }
+}
+
 __global__ void scatter_rows_kernel(const uint4* __restrict__ x, int64_t xsh, int chunks, int T, int H,
                                     int W, int Hp, int Wp, const int32_t* __restrict__ inv_idx,
                                     uint4* __restrict__ out, int64_t osh, int64_t oss) {
@@ -1942,6 +1977,25 @@ prism_status_t prism_scatter_rows(const void* x_re, int64_t x_stride_h, int head
         out_stride_h, out_stride_s);
   }
   PRISM_CHECK_LAUNCH("prism_scatter_rows");
+  return PRISM_OK;
+}
+
+prism_status_t prism_copy_rows(const void* src, int64_t src_stride_block, int64_t src_stride_row,
+                               void* dst, int64_t dst_stride_block, int64_t dst_stride_row,
+                               int64_t n_blocks, int64_t n_rows, int64_t row_bytes, cudaStream_t stream) {
+  PRISM_CHECK_ARG(src && dst, "prism_copy_rows: null pointer");
+  PRISM_CHECK_ARG(aligned16(src) && aligned16(dst) && row_bytes % 16 == 0 && src_stride_block % 16 == 0 &&
+                      src_stride_row % 16 == 0 && dst_stride_block % 16 == 0 && dst_stride_row % 16 == 0,
+                  "prism_copy_rows: pointers, strides and row length must be multiples of 16 bytes");
+  PRISM_CHECK_ARG(n_blocks >= 0 && n_blocks <= 65535 && n_rows >= 0 && row_bytes >= 0 &&
+                      row_bytes / 16 * kCopyRows < ((int64_t)1 << 31) &&
+                      (n_rows + kCopyRows - 1) / kCopyRows < ((int64_t)1 << 31),
+                  "prism_copy_rows: bad sizes");
+  if (n_blocks == 0 || n_rows == 0 || row_bytes == 0) return PRISM_OK;
+  copy_rows_kernel<<<dim3((unsigned)((n_rows + kCopyRows - 1) / kCopyRows), (unsigned)n_blocks), 256, 0,
+                     stream>>>((const uint4*)src, src_stride_block / 16, src_stride_row / 16, (uint4*)dst,
+                               dst_stride_block / 16, dst_stride_row / 16, n_rows, (int)(row_bytes / 16));
+  PRISM_CHECK_LAUNCH("prism_copy_rows");
   return PRISM_OK;
 }
 

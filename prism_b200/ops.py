@@ -174,6 +174,18 @@ def scatter_rows(x_re: torch.Tensor, grid, grid_padded, inv_idx: torch.Tensor,
     return out
 
 
+def copy_rows(src: torch.Tensor, src_strides, dst: torch.Tensor, dst_strides, n_blocks: int,
+              n_rows: int, row_elems: int) -> None:
+    """dst rows <- src rows: for block o and row r, row_elems elements from
+    src.data_ptr() + o * src_strides[0] + r * src_strides[1] to the same position of dst
+    (strides in elements of src.dtype; every offset a multiple of 16 bytes)."""
+    _check_cuda(src, dst)
+    es = src.element_size()
+    _lib.call("prism_copy_rows", _p(src), src_strides[0] * es, src_strides[1] * es, _p(dst),
+              dst_strides[0] * es, dst_strides[1] * es, int(n_blocks), int(n_rows), int(row_elems) * es,
+              _stream(src))
+
+
 # -------------------------------------------------------------- a11-a14
 def block_select(q_re, k_re, layout, tile_bits, sparsity, cdf_threshold):
     _check_cuda(q_re, k_re)
