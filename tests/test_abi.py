@@ -45,6 +45,8 @@ def test_error_channel_without_gpu():
     rc = L.prism_shape_select(None, None, None, 0, 1, 64, 7, ctypes.c_float(0.5),
                               ctypes.c_float(0.15), ctypes.c_float(1.0), None, None, None, None)
     assert rc != 0
+    rc = L.prism_copy_rows(None, 0, 256, None, 0, 256, 1, 4, 256, None)
+    assert rc != 0 and b"null pointer" in L.prism_last_error()
 
 
 def test_library_is_sm100a():
