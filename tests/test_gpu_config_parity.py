@@ -1,8 +1,9 @@
-"""Parity at the benchmark configurations' grids (BASELINE configs 1 and 2).
+"""Parity at the benchmark configurations' grids (2 and 3).
 
-Config 1 (720p: 21x45x80 -> 24x48x80, 1,440 tiles) on 2 heads and config 2 (1080p:
-21x68x120 -> 24x72x120, 3,240 tiles) on 1 head, D = 128, zone-structured q/k/v,
-top-k 8 % + cumulative mass 0.9, audio token norms:
+Config 1 (720p: 21x45x80 -> 24x48x80, 1,440 tiles) on 2 heads, config 2 (1080p:
+21x68x120 -> 24x72x120, 3,240 tiles) on 1 head and config 3 (2K: 31x90x160 ->
+32x96x160, 7,680 tiles) on 1 head, D = 128, zone-structured q/k/v, top-k 8 % (5 % for
+config 3) + cumulative mass 0.9, audio token norms:
 
 * selection side against the C oracle (oracle/prism_oracle.c) on the same inputs:
   shape ids, the permutation and both tile bitmaps bit for bit.  A differing
@@ -35,6 +36,10 @@ CONFIG_CASES = {
                        cdf_threshold=0.9, audio_tokens=64, seed=0),
     "c2_1080p_h1": Case("c2_1080p_h1", (21, 68, 120), 1, 128, values="zoned", sparsity=0.92,
                         cdf_threshold=0.9, audio_tokens=64, seed=1),
+    # config 3's grid and selection rule (top-k 5 % + cumulative mass 0.9): 7,680 tiles,
+    # ~50 M selected tile pairs on one head (the C oracle takes ~25 s on the host)
+    "c3_2k_h1": Case("c3_2k_h1", (31, 90, 160), 1, 128, values="zoned", sparsity=0.95,
+                     cdf_threshold=0.9, audio_tokens=64, seed=2),
 }
 
 
