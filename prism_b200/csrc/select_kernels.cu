@@ -153,7 +153,7 @@ __global__ void zone_partial_kernel(const uint16_t* __restrict__ v, int heads, i
   }
 }
 
-// The same partial sums with the eight rows of the frame in parallel (D <= 128): a
+// The same partial sums with the eight rows of the frame in parallel (16 <= D <= 128): a
 // CTA of 8 x D/2 threads (two CTAs per SM), thread (lh, channel pair) makes row lh's
 // head means (kZoneHeads heads' loads in flight per step) and its row sums; the
 // column sums over the rows and the frame sum are then taken from shared memory in
@@ -1846,7 +1846,7 @@ prism_status_t prism_zone_stats(const void* v, int heads, int64_t v_stride_h, in
   const int Nz = (Tp / 8) * (Hp / 8) * (Wp / 8);
   float* part = (float*)workspace;
   float* apart = part + (size_t)Nz * 8 * kPart * D;
-  if (D <= 128) {
+  if (D >= 16 && D <= 128) {  // 4 D >= 64 threads: one per token of the frame for the audio sums
     zone_partial_rows_kernel<<<Nz * 8, 4 * D, (size_t)72 * D * sizeof(float), stream>>>(
         (const uint16_t*)v, heads, v_stride_h, v_stride_s, T, H, W, Hp, Wp, D, valid,
         (const uint16_t*)norms, part, apart);

@@ -149,3 +149,31 @@ def test_invalid_arguments_raise(cuda):
                          torch.zeros(1, 25, device=cuda), False, "bogus")
     with pytest.raises(Exception):
         ops.token_norms(x[:, :7])
+
+
+@pytest.mark.parametrize("D", [8, 16, 32, 256])
+def test_zone_stats_head_dims_bit_exact(D, cuda):
+    """Zone statistics and shape ids at head dims on both sides of the row-parallel
+    kernel's range (16 <= D <= 128; the one-thread-per-channel-pair kernel otherwise),
+    with 5 heads, padding on every axis and audio norms, against the C oracle."""
+    g = torch.Generator().manual_seed(D)
+    grid, gp, heads = (5, 11, 13), (8, 16, 16), 5
+    S = grid[0] * grid[1] * grid[2]
+    Sp = gp[0] * gp[1] * gp[2]
+    v_pad = torch.zeros(heads, gp[0], gp[1], gp[2], D)
+    v_pad[:, :grid[0], :grid[1], :grid[2]] = torch.randn(heads, *grid, D, generator=g)
+    v_pad = v_pad.reshape(heads, Sp, D).to(torch.bfloat16)
+    valid = torch.zeros(gp, dtype=torch.bool)
+    valid[:grid[0], :grid[1], :grid[2]] = True
+    valid = valid.reshape(Sp)
+    norms = (torch.rand(Sp, generator=g) * 3).to(torch.bfloat16) * valid
+    packed, av, audio = ops.zone_stats(v_pad.to(cuda), gp, gp, valid.to(cuda), norms.to(cuda))
+    o_packed, o_av, o_audio = O.zone_stats(bits(v_pad), gp, valid.numpy().astype(np.uint8),
+                                           bits(norms))
+    assert np.array_equal(packed.cpu().numpy().view(np.uint32), o_packed.view(np.uint32))
+    assert np.array_equal(av.cpu().numpy(), o_av)
+    assert np.array_equal(audio.cpu().numpy().view(np.uint32), o_audio.view(np.uint32))
+    ids = ops.shape_select(packed, av, audio, True, "ivpq")
+    o_ids, _, _ = O.shape_select(o_packed, o_av, o_audio, True, "ivpq", 0.5, 0.15, 1.0)
+    assert np.array_equal(ids.cpu().numpy(), o_ids)
+    assert S < Sp
