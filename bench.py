@@ -327,17 +327,30 @@ class CpuLayerSample:
     def run(self, seconds):
         np, O = self.np, self.O
         D = CONFIG["head_dim"]
+        uniform = CONFIG.get("path") == "uniform"
         t0 = time.perf_counter()
-        norms = self.pad(O.token_norms(self.a2v)[:, None])[:, 0]
-        packed, av, audio = O.zone_stats(self.v_all, self.gp, self.valid, norms)
-        ids, _, _ = O.shape_select(packed, av, audio, True, CONFIG["method"])
-        t_stats = time.perf_counter() - t0
-        t1 = time.perf_counter()
-        src, inv, bot, bt, nb = O.layout(ids, self.gp)
-        q_re, k_re = self.q0[:, src], self.k0[:, src]
-        valid_re = self.valid[src]
-        bq, _, _ = O.block_select(q_re, k_re, valid_re, bt, nb, CONFIG["sparsity"],
-                                  CONFIG["cdf_threshold"])
+        if uniform:
+            # the uniform path: 3D-chunk order, no zone statistics or shape choice
+            # (unguided chunk selection; --guidance / --correction are not restated here)
+            t_stats = 0.0
+            t1 = time.perf_counter()
+            src, inv = O.uniform_layout(self.gp, CONFIG["chunk"])
+            q_re, k_re = self.q0[:, src], self.k0[:, src]
+            valid_re = self.valid[src]
+            vol = int(np.prod(CONFIG["chunk"]))
+            bq, _, _ = O.block_select_uniform(q_re, k_re, src.size, src.size, vol, vol, valid_re,
+                                              valid_re, CONFIG["sparsity"], CONFIG["cdf_threshold"])
+        else:
+            norms = self.pad(O.token_norms(self.a2v)[:, None])[:, 0]
+            packed, av, audio = O.zone_stats(self.v_all, self.gp, self.valid, norms)
+            ids, _, _ = O.shape_select(packed, av, audio, True, CONFIG["method"])
+            t_stats = time.perf_counter() - t0
+            t1 = time.perf_counter()
+            src, inv, bot, bt, nb = O.layout(ids, self.gp)
+            q_re, k_re = self.q0[:, src], self.k0[:, src]
+            valid_re = self.valid[src]
+            bq, _, _ = O.block_select(q_re, k_re, valid_re, bt, nb, CONFIG["sparsity"],
+                                      CONFIG["cdf_threshold"])
         t_sel = time.perf_counter() - t1
         nt = src.size // 64
         dense = O.bits_to_dense(bq, nt)[0]
@@ -379,8 +392,10 @@ class CpuLayerSample:
         layer_ms = (t_stats + heads * (t_sel + t_attn / max(n_done, 1) * nt)) * 1e3
         return {"value": flops / t_attn / 1e12, "unit": "TFLOPS", "cores": os.cpu_count() or 1,
                 "kind": "port", "wall_ms": wall * 1e3,
-                "sample": f"the GPU arm's inputs: audio norms + zone statistics over {heads} heads + "
-                          f"shape choice ({t_stats:.1f} s, C oracle), head 0's full selection "
+                "sample": ("the GPU arm's inputs: uniform 3D-chunk order, " if uniform else
+                           f"the GPU arm's inputs: audio norms + zone statistics over {heads} heads + "
+                           f"shape choice ({t_stats:.1f} s, C oracle), ")
+                          + f"head 0's full selection "
                           f"({t_sel:.1f} s, C oracle, {int(dense.sum())} tile pairs, density "
                           f"{dense.sum() / nt / nt:.3f}"
                           + ("" if same is None else f", identical to the GPU arm's: {same}")
